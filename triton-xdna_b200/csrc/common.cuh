@@ -1,0 +1,130 @@
+// Shared helpers for the xb200 CUDA kernels (sm_100a).
+//
+// Error convention mirrors the reference's native C ABI
+// (amd_triton_npu/backend/include/HsaRuntime/HsaRuntime.cpp:740-794):
+// every entry point returns 0 on success or a negative status, and on error
+// writes a NUL-terminated message into the caller's (err, errlen) buffer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+#include <stdarg.h>
+
+#include "../../include/xb200.h"
+
+namespace xb {
+
+// Write a printf-style message into the caller's error buffer (may be NULL).
+inline void set_err(char* err, size_t errlen, const char* fmt, ...) {
+  if (!err || errlen == 0) return;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(err, errlen, fmt, ap);
+  va_end(ap);
+}
+
+// Report the first error from an asynchronous launch (launch-configuration
+// errors surface here; execution errors surface at the caller's next sync).
+inline int check_launch(const char* what, char* err, size_t errlen) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_err(err, errlen, "%s: kernel launch failed: %s", what, cudaGetErrorString(e));
+    return XB_ERR_CUDA;
+  }
+  return XB_OK;
+}
+
+inline int sm_count(int* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  static int cached[64] = {0};
+  if (dev >= 0 && dev < 64 && cached[dev] > 0) { *out = cached[dev]; return 0; }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  if (dev >= 0 && dev < 64) cached[dev] = n;
+  *out = n;
+  return 0;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int dtype_size(int dt) {
+  switch (dt) {
+    case XB_DT_BF16: return 2;
+    case XB_DT_F32: return 4;
+    case XB_DT_I8: return 1;
+    case XB_DT_I16: return 2;
+    case XB_DT_I32: return 4;
+    default: return 0;
+  }
+}
+
+// ---- element conversions (fp32 compute, round-to-nearest-even stores) ----
+template <typename T> struct Cvt;
+template <> struct Cvt<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <> struct Cvt<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+// Round an fp32 value to the storage type and back (models a store of an
+// intermediate in the storage dtype, as the reference's torch expressions do).
+template <typename T>
+__device__ __forceinline__ float round_to(float v) { return Cvt<T>::to_f(Cvt<T>::from_f(v)); }
+
+// 16-byte vector of T.
+template <typename T> struct Vec16 {
+  static constexpr int N = 16 / sizeof(T);
+  T v[N];
+};
+
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld16_stream(const T* p) {
+  Vec16<T> r;
+  int4 raw = __ldcs(reinterpret_cast<const int4*>(p));
+  memcpy(&r, &raw, 16);
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld16(const T* p) {
+  Vec16<T> r;
+  int4 raw = __ldg(reinterpret_cast<const int4*>(p));
+  memcpy(&r, &raw, 16);
+  return r;
+}
+template <typename T>
+__device__ __forceinline__ void st16_stream(T* p, const Vec16<T>& v) {
+  int4 raw;
+  memcpy(&raw, &v, 16);
+  __stcs(reinterpret_cast<int4*>(p), raw);
+}
+template <typename T>
+__device__ __forceinline__ void st16(T* p, const Vec16<T>& v) {
+  int4 raw;
+  memcpy(&raw, &v, 16);
+  *reinterpret_cast<int4*>(p) = raw;
+}
+
+}  // namespace xb
+
+// Dispatch on the runtime dtype code to a templated launcher.
+#define XB_DISPATCH_FLOAT(dt, T, what, err, errlen, ...)                       \
+  do {                                                                         \
+    if ((dt) == XB_DT_BF16) {                                                  \
+      using T = __nv_bfloat16;                                                 \
+      __VA_ARGS__;                                                             \
+    } else if ((dt) == XB_DT_F32) {                                            \
+      using T = float;                                                         \
+      __VA_ARGS__;                                                             \
+    } else {                                                                   \
+      ::xb::set_err(err, errlen, "%s: unsupported dtype code %d (want bf16=%d or f32=%d)", \
+                    what, (int)(dt), XB_DT_BF16, XB_DT_F32);                   \
+      return XB_ERR_UNSUPPORTED;                                               \
+    }                                                                          \
+  } while (0)

@@ -1,0 +1,253 @@
+// Flat elementwise / activation kernels (HBM-bound streaming).
+//
+// One templated grid-stride kernel family: each thread moves UNROLL 16-byte
+// vectors per iteration (all loads issued before any math, so every thread
+// keeps 64 B of reads in flight), math in fp32, streaming (evict-first)
+// loads/stores because every byte is touched exactly once.  The grid is a
+// multiple of the SM count (8 resident 256-thread CTAs per SM).  A scalar
+// instantiation handles buffers that are not 16-byte aligned and the ragged
+// tail.
+//
+// The functors restate the reference examples' torch CPU check expressions
+// (the parity oracle), including where those round an intermediate to the
+// storage dtype:
+//   vecadd      examples/vec-add/vec-add.py:49          torch.add(a, b)
+//   axpy        examples/axpy/axpy.py:40                alpha * x + y
+//   relu        examples/relu/relu.py:35                torch.relu(x)
+//   leaky_relu  examples/leaky_relu/leaky_relu.py:40    F.leaky_relu(x, 0.01)
+//   gelu        examples/gelu/gelu.py:40                x * sigmoid(1.702 x.float()).to(dtype)
+//   gelu_tanh   examples/gpt2/kernels/gelu.py:25-45     tanh-form GELU
+//   sigmoid     examples/sigmoid/sigmoid.py:39          torch.sigmoid(x)
+//   silu        examples/silu/silu.py:39                F.silu(x)
+//   swiglu      examples/swiglu/swiglu.py:43            F.silu(gate) * up
+#include "common.cuh"
+
+namespace xb {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kUnroll = 4;
+
+// Explicit _rn intrinsics keep the compiler from contracting a*b+c into an
+// FMA: the torch expressions evaluate each operator separately.
+__device__ __forceinline__ float sigmoid_f(float x) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+}
+
+template <typename T> struct OpAdd {
+  __device__ __forceinline__ float operator()(float a, float b) const { return __fadd_rn(a, b); }
+};
+template <typename T> struct OpAxpy {
+  float alpha;
+  __device__ __forceinline__ float operator()(float x, float y) const {
+    return __fadd_rn(round_to<T>(__fmul_rn(alpha, x)), y);
+  }
+};
+template <typename T> struct OpRelu {
+  // torch.relu is clamp_min(x, 0): -0.0 and NaN pass through unchanged.
+  __device__ __forceinline__ float operator()(float x) const { return x < 0.0f ? 0.0f : x; }
+};
+template <typename T> struct OpLeakyRelu {
+  float slope;
+  __device__ __forceinline__ float operator()(float x) const { return x > 0.0f ? x : __fmul_rn(x, slope); }
+};
+template <typename T> struct OpGeluSigmoid {
+  __device__ __forceinline__ float operator()(float x) const {
+    float s = round_to<T>(sigmoid_f(__fmul_rn(1.702f, x)));
+    return __fmul_rn(x, s);
+  }
+};
+template <typename T> struct OpGeluTanh {
+  __device__ __forceinline__ float operator()(float x) const {
+    const float kBeta = 0.7978845608028654f;  // sqrt(2/pi)
+    const float kKappa = 0.044715f;
+    float x3 = __fmul_rn(__fmul_rn(x, x), x);
+    float inner = __fmul_rn(kBeta, __fadd_rn(x, __fmul_rn(kKappa, x3)));
+    return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));
+  }
+};
+template <typename T> struct OpSigmoid {
+  __device__ __forceinline__ float operator()(float x) const { return sigmoid_f(x); }
+};
+template <typename T> struct OpSilu {
+  __device__ __forceinline__ float operator()(float x) const {
+    return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+  }
+};
+template <typename T> struct OpSwiglu {
+  __device__ __forceinline__ float operator()(float g, float u) const {
+    float s = round_to<T>(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))));
+    return __fmul_rn(s, u);
+  }
+};
+
+template <typename T, typename Op>
+__global__ void __launch_bounds__(kThreads) unary_vec_kernel(const T* __restrict__ x, T* __restrict__ y,
+                                                             int64_t nvec, Op op) {
+  using V = Vec16<T>;
+  const int64_t step = (int64_t)gridDim.x * kThreads * kUnroll;
+  for (int64_t base = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x; base < nvec; base += step) {
+    V v[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      int64_t i = base + (int64_t)u * kThreads;
+      if (i < nvec) v[u] = ld16_stream(x + i * V::N);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      int64_t i = base + (int64_t)u * kThreads;
+      if (i < nvec) {
+        V o;
+#pragma unroll
+        for (int e = 0; e < V::N; ++e) o.v[e] = Cvt<T>::from_f(op(Cvt<T>::to_f(v[u].v[e])));
+        st16_stream(y + i * V::N, o);
+      }
+    }
+  }
+}
+
+template <typename T, typename Op>
+__global__ void __launch_bounds__(kThreads) binary_vec_kernel(const T* __restrict__ a, const T* __restrict__ b,
+                                                              T* __restrict__ y, int64_t nvec, Op op) {
+  using V = Vec16<T>;
+  const int64_t step = (int64_t)gridDim.x * kThreads * kUnroll;
+  for (int64_t base = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x; base < nvec; base += step) {
+    V va[kUnroll], vb[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      int64_t i = base + (int64_t)u * kThreads;
+      if (i < nvec) {
+        va[u] = ld16_stream(a + i * V::N);
+        vb[u] = ld16_stream(b + i * V::N);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      int64_t i = base + (int64_t)u * kThreads;
+      if (i < nvec) {
+        V o;
+#pragma unroll
+        for (int e = 0; e < V::N; ++e)
+          o.v[e] = Cvt<T>::from_f(op(Cvt<T>::to_f(va[u].v[e]), Cvt<T>::to_f(vb[u].v[e])));
+        st16_stream(y + i * V::N, o);
+      }
+    }
+  }
+}
+
+// Scalar path: elements [begin, n).  Used for the tail after the vector body
+// and for whole buffers that are not 16-byte aligned.
+template <typename T, typename Op>
+__global__ void unary_scalar_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t begin, int64_t n, Op op) {
+  for (int64_t i = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = Cvt<T>::from_f(op(Cvt<T>::to_f(x[i])));
+}
+template <typename T, typename Op>
+__global__ void binary_scalar_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ y,
+                                     int64_t begin, int64_t n, Op op) {
+  for (int64_t i = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = Cvt<T>::from_f(op(Cvt<T>::to_f(a[i]), Cvt<T>::to_f(b[i])));
+}
+
+int grid_for(int64_t work_items, int per_block) {
+  int sms = 148;
+  sm_count(&sms);
+  int64_t want = (work_items + per_block - 1) / per_block;
+  int64_t cap = (int64_t)sms * 8;  // 8 x 256 threads = 2048 resident threads per SM
+  if (want > cap) want = cap;
+  if (want < 1) want = 1;
+  return (int)want;
+}
+
+template <typename T, typename Op>
+int launch_unary(const void* xv, void* yv, int64_t n, Op op, cudaStream_t s, const char* what, char* err,
+                 size_t errlen) {
+  if (n < 0) { set_err(err, errlen, "%s: negative element count %lld", what, (long long)n); return XB_ERR_INVALID; }
+  if (n == 0) return XB_OK;
+  if (!xv || !yv) { set_err(err, errlen, "%s: null pointer", what); return XB_ERR_INVALID; }
+  const T* x = static_cast<const T*>(xv);
+  T* y = static_cast<T*>(yv);
+  constexpr int VN = Vec16<T>::N;
+  int64_t nvec = (aligned16(x) && aligned16(y)) ? n / VN : 0;
+  if (nvec > 0)
+    unary_vec_kernel<T, Op><<<grid_for(nvec, kThreads * kUnroll), kThreads, 0, s>>>(x, y, nvec, op);
+  if (nvec * VN < n)
+    unary_scalar_kernel<T, Op><<<grid_for(n - nvec * VN, kThreads), kThreads, 0, s>>>(x, y, nvec * VN, n, op);
+  return check_launch(what, err, errlen);
+}
+
+template <typename T, typename Op>
+int launch_binary(const void* av, const void* bv, void* yv, int64_t n, Op op, cudaStream_t s, const char* what,
+                  char* err, size_t errlen) {
+  if (n < 0) { set_err(err, errlen, "%s: negative element count %lld", what, (long long)n); return XB_ERR_INVALID; }
+  if (n == 0) return XB_OK;
+  if (!av || !bv || !yv) { set_err(err, errlen, "%s: null pointer", what); return XB_ERR_INVALID; }
+  const T* a = static_cast<const T*>(av);
+  const T* b = static_cast<const T*>(bv);
+  T* y = static_cast<T*>(yv);
+  constexpr int VN = Vec16<T>::N;
+  int64_t nvec = (aligned16(a) && aligned16(b) && aligned16(y)) ? n / VN : 0;
+  if (nvec > 0)
+    binary_vec_kernel<T, Op><<<grid_for(nvec, kThreads * kUnroll), kThreads, 0, s>>>(a, b, y, nvec, op);
+  if (nvec * VN < n)
+    binary_scalar_kernel<T, Op><<<grid_for(n - nvec * VN, kThreads), kThreads, 0, s>>>(a, b, y, nvec * VN, n, op);
+  return check_launch(what, err, errlen);
+}
+
+}  // namespace
+}  // namespace xb
+
+using namespace xb;
+
+#define XB_S(stream) static_cast<cudaStream_t>(stream)
+
+extern "C" int xb_vecadd(const void* a, const void* b, void* c, int64_t n, int dtype, void* stream, char* err,
+                         size_t errlen) {
+  XB_DISPATCH_FLOAT(dtype, T, "xb_vecadd", err, errlen,
+                    return launch_binary<T>(a, b, c, n, OpAdd<T>{}, XB_S(stream), "xb_vecadd", err, errlen));
+}
+
+extern "C" int xb_axpy(const void* x, const void* y, void* out, float alpha, int64_t n, int dtype, void* stream,
+                       char* err, size_t errlen) {
+  XB_DISPATCH_FLOAT(dtype, T, "xb_axpy", err, errlen,
+                    return launch_binary<T>(x, y, out, n, OpAxpy<T>{alpha}, XB_S(stream), "xb_axpy", err, errlen));
+}
+
+extern "C" int xb_relu(const void* x, void* y, int64_t n, int dtype, void* stream, char* err, size_t errlen) {
+  XB_DISPATCH_FLOAT(dtype, T, "xb_relu", err, errlen,
+                    return launch_unary<T>(x, y, n, OpRelu<T>{}, XB_S(stream), "xb_relu", err, errlen));
+}
+
+extern "C" int xb_leaky_relu(const void* x, void* y, float slope, int64_t n, int dtype, void* stream, char* err,
+                             size_t errlen) {
+  XB_DISPATCH_FLOAT(dtype, T, "xb_leaky_relu", err, errlen,
+                    return launch_unary<T>(x, y, n, OpLeakyRelu<T>{slope}, XB_S(stream), "xb_leaky_relu", err,
+                                           errlen));
+}
+
+extern "C" int xb_gelu(const void* x, void* y, int64_t n, int dtype, void* stream, char* err, size_t errlen) {
+  XB_DISPATCH_FLOAT(dtype, T, "xb_gelu", err, errlen,
+                    return launch_unary<T>(x, y, n, OpGeluSigmoid<T>{}, XB_S(stream), "xb_gelu", err, errlen));
+}
+
+extern "C" int xb_gelu_tanh(const void* x, void* y, int64_t n, int dtype, void* stream, char* err, size_t errlen) {
+  XB_DISPATCH_FLOAT(dtype, T, "xb_gelu_tanh", err, errlen,
+                    return launch_unary<T>(x, y, n, OpGeluTanh<T>{}, XB_S(stream), "xb_gelu_tanh", err, errlen));
+}
+
+extern "C" int xb_sigmoid(const void* x, void* y, int64_t n, int dtype, void* stream, char* err, size_t errlen) {
+  XB_DISPATCH_FLOAT(dtype, T, "xb_sigmoid", err, errlen,
+                    return launch_unary<T>(x, y, n, OpSigmoid<T>{}, XB_S(stream), "xb_sigmoid", err, errlen));
+}
+
+extern "C" int xb_silu(const void* x, void* y, int64_t n, int dtype, void* stream, char* err, size_t errlen) {
+  XB_DISPATCH_FLOAT(dtype, T, "xb_silu", err, errlen,
+                    return launch_unary<T>(x, y, n, OpSilu<T>{}, XB_S(stream), "xb_silu", err, errlen));
+}
+
+extern "C" int xb_swiglu(const void* gate, const void* up, void* out, int64_t n, int dtype, void* stream, char* err,
+                         size_t errlen) {
+  XB_DISPATCH_FLOAT(dtype, T, "xb_swiglu", err, errlen,
+                    return launch_binary<T>(gate, up, out, n, OpSwiglu<T>{}, XB_S(stream), "xb_swiglu", err,
+                                            errlen));
+}

@@ -1,0 +1,248 @@
+"""Tensor-level operators over the C ABI (device tensors in, device tensors out).
+
+Each function takes CUDA tensors, validates dtype / device / layout on the
+host, and enqueues one library call on the current torch CUDA stream.  There
+is no PyTorch or CPU fallback: a missing library or an unsupported input
+raises.  For the reference's host-tensor launch semantics see
+``xb200.kernels``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+DT = {torch.bfloat16: 0, torch.float32: 1, torch.int8: 2, torch.int16: 3, torch.int32: 4}
+FLOAT_DTYPES = (torch.bfloat16, torch.float32)
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _cuda(*ts: torch.Tensor) -> None:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not isinstance(t, torch.Tensor) or t.device.type != "cuda":
+            raise ValueError("xb200.ops operates on CUDA tensors (use xb200.kernels for host tensors)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} and {t.device}")
+
+
+def _flat(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+def _float_dtype(*ts: torch.Tensor) -> int:
+    dt = ts[0].dtype
+    if dt not in FLOAT_DTYPES:
+        raise TypeError(f"unsupported dtype {dt}: bf16 or fp32 expected")
+    for t in ts[1:]:
+        if t is not None and t.dtype != dt:
+            raise TypeError(f"dtype mismatch: {dt} vs {t.dtype}")
+    return DT[dt]
+
+
+def _out_like(x: torch.Tensor, out: torch.Tensor | None) -> torch.Tensor:
+    if out is None:
+        return torch.empty_like(x, memory_format=torch.contiguous_format)
+    _cuda(out)
+    if out.dtype != x.dtype or out.numel() != x.numel():
+        raise ValueError("out has the wrong dtype or size")
+    return _flat(out, "out")
+
+
+# --------------------------------------------------------------------------- elementwise
+
+
+def _binary(fn: str, a: torch.Tensor, b: torch.Tensor, out, *scalar) -> torch.Tensor:
+    _cuda(a, b)
+    dt = _float_dtype(a, b)
+    if a.numel() != b.numel():
+        raise ValueError(f"size mismatch: {a.numel()} vs {b.numel()}")
+    out = _out_like(a, out)
+    _lib.call(fn, _flat(a, "a").data_ptr(), _flat(b, "b").data_ptr(), out.data_ptr(), *scalar[:1], a.numel(), dt,
+              _stream())
+    return out
+
+
+def _unary(fn: str, x: torch.Tensor, out, *scalar) -> torch.Tensor:
+    _cuda(x)
+    dt = _float_dtype(x)
+    out = _out_like(x, out)
+    if scalar:
+        _lib.call(fn, _flat(x, "x").data_ptr(), out.data_ptr(), scalar[0], x.numel(), dt, _stream())
+    else:
+        _lib.call(fn, _flat(x, "x").data_ptr(), out.data_ptr(), x.numel(), dt, _stream())
+    return out
+
+
+def vecadd(a, b, out=None):
+    """c = a + b (examples/vec-add/vec-add.py:16-35)."""
+    return _binary("xb_vecadd", a, b, out)
+
+
+def axpy(x, y, alpha: float, out=None):
+    """out = alpha * x + y (examples/axpy/axpy.py:13-29)."""
+    _cuda(x, y)
+    dt = _float_dtype(x, y)
+    if x.numel() != y.numel():
+        raise ValueError("size mismatch")
+    out = _out_like(x, out)
+    _lib.call("xb_axpy", _flat(x, "x").data_ptr(), _flat(y, "y").data_ptr(), out.data_ptr(), float(alpha),
+              x.numel(), dt, _stream())
+    return out
+
+
+def relu(x, out=None):
+    """max(x, 0) (examples/relu/relu.py:13-26)."""
+    return _unary("xb_relu", x, out)
+
+
+def leaky_relu(x, negative_slope: float = 0.01, out=None):
+    """x >= 0 ? x : slope * x (examples/leaky_relu/leaky_relu.py:15-31)."""
+    return _unary("xb_leaky_relu", x, out, float(negative_slope))
+
+
+def gelu(x, out=None):
+    """x * sigmoid(1.702 x) (examples/gelu/gelu.py:13-30)."""
+    return _unary("xb_gelu", x, out)
+
+
+def gelu_tanh(x, out=None):
+    """tanh-form GELU (examples/gpt2/kernels/gelu.py:25-45)."""
+    return _unary("xb_gelu_tanh", x, out)
+
+
+def sigmoid(x, out=None):
+    """1 / (1 + exp(-x)) (examples/sigmoid/sigmoid.py:13-34)."""
+    return _unary("xb_sigmoid", x, out)
+
+
+def silu(x, out=None):
+    """x * sigmoid(x) (examples/silu/silu.py:13-30)."""
+    return _unary("xb_silu", x, out)
+
+
+def swiglu(gate, up, out=None):
+    """silu(gate) * up (examples/swiglu/swiglu.py:13-33)."""
+    return _binary("xb_swiglu", gate, up, out)
+
+
+# --------------------------------------------------------------------------- row reductions
+
+
+def _rows(x: torch.Tensor, name: str) -> tuple[int, int, int]:
+    if x.dim() < 1:
+        raise ValueError(f"{name} needs at least one dimension")
+    cols = x.shape[-1]
+    if x.stride(-1) != 1 and cols > 1:
+        raise ValueError(f"{name}: last dimension must have unit stride")
+    if x.dim() == 1:
+        return 1, cols, cols
+    x2 = x.reshape(-1, cols) if x.dim() > 2 else x
+    if x.dim() > 2 and not x.is_contiguous():
+        raise ValueError(f"{name}: >2-D input must be contiguous")
+    return x2.shape[0], cols, x2.stride(0)
+
+
+def _row_out(x, out):
+    if out is None:
+        return torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    _cuda(out)
+    if out.shape != x.shape or out.dtype != x.dtype:
+        raise ValueError("out has the wrong shape or dtype")
+    return out
+
+
+def softmax(x, out=None):
+    """Row softmax over the last dim (examples/test_softmax/test_softmax.py:13-45)."""
+    _cuda(x)
+    dt = _float_dtype(x)
+    out = _row_out(x, out)
+    rows, cols, xs = _rows(x, "x")
+    _, _, ys = _rows(out, "out")
+    _lib.call("xb_softmax", x.data_ptr(), out.data_ptr(), rows, cols, xs, ys, dt, _stream())
+    return out
+
+
+def layernorm(x, weight=None, bias=None, eps: float = 1e-5, out=None):
+    """(x - mean) * rsqrt(var + eps) * weight + bias over the last dim
+    (examples/test_layernorm/test_layernorm.py:13-60)."""
+    _cuda(x, weight, bias)
+    dt = _float_dtype(x, weight, bias)
+    out = _row_out(x, out)
+    rows, cols, xs = _rows(x, "x")
+    _, _, ys = _rows(out, "out")
+    for p, n in ((weight, "weight"), (bias, "bias")):
+        if p is not None and (p.numel() != cols or not p.is_contiguous()):
+            raise ValueError(f"{n} must be a contiguous vector of {cols} elements")
+    _lib.call("xb_layernorm", x.data_ptr(), weight.data_ptr() if weight is not None else None,
+              bias.data_ptr() if bias is not None else None, out.data_ptr(), rows, cols, xs, ys, float(eps), dt,
+              _stream())
+    return out
+
+
+def rms_norm(x, weight=None, eps: float = 1e-5, out=None):
+    """x * rsqrt(mean(x^2) + eps) [* weight] (examples/rms_norm/rms_norm.py:23-55,
+    examples/weighted_rms_norm/weighted_rms_norm.py:21-58)."""
+    _cuda(x, weight)
+    dt = _float_dtype(x, weight)
+    out = _row_out(x, out)
+    rows, cols, xs = _rows(x, "x")
+    _, _, ys = _rows(out, "out")
+    if weight is not None and (weight.numel() != cols or not weight.is_contiguous()):
+        raise ValueError(f"weight must be a contiguous vector of {cols} elements")
+    _lib.call("xb_rms_norm", x.data_ptr(), weight.data_ptr() if weight is not None else None, out.data_ptr(), rows,
+              cols, xs, ys, float(eps), dt, _stream())
+    return out
+
+
+def weighted_rms_norm(x, weight, eps: float = 1e-5, out=None):
+    return rms_norm(x, weight, eps, out)
+
+
+def row_center(x, out=None):
+    """x - mean(x) over the last dim (examples/average_pool/average_pool.py:24-52)."""
+    _cuda(x)
+    dt = _float_dtype(x)
+    out = _row_out(x, out)
+    rows, cols, xs = _rows(x, "x")
+    _, _, ys = _rows(out, "out")
+    _lib.call("xb_row_center", x.data_ptr(), out.data_ptr(), rows, cols, xs, ys, dt, _stream())
+    return out
+
+
+def avg_pool2d_2x2(x, out=None):
+    """2x2 / stride-2 average pooling of a contiguous [..., H, W] tensor."""
+    _cuda(x)
+    dt = _float_dtype(x)
+    if x.dim() < 2 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous tensor with at least 2 dims")
+    h, w = x.shape[-2], x.shape[-1]
+    planes = x.numel() // (h * w) if h * w else 0
+    oshape = tuple(x.shape[:-2]) + (h // 2, w // 2)
+    if out is None:
+        out = torch.empty(oshape, dtype=x.dtype, device=x.device)
+    else:
+        _cuda(out)
+        if tuple(out.shape) != oshape or out.dtype != x.dtype or not out.is_contiguous():
+            raise ValueError("out has the wrong shape, dtype or layout")
+    _lib.call("xb_avg_pool2d_2x2", x.data_ptr(), out.data_ptr(), planes, h, w, dt, _stream())
+    return out
+
+
+def device_name(device: int = 0) -> tuple[str, int]:
+    buf = ctypes.create_string_buffer(256)
+    sms = ctypes.c_int(0)
+    _lib.call("xb_device_name", device, buf, 256, ctypes.byref(sms))
+    return buf.value.decode(), sms.value
