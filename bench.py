@@ -8,6 +8,10 @@ fp32 tensor.  One step = one pass of every operator over its inputs
 (17 kernel launches).  Every input is larger than L2 (126 MB), so no flush is
 needed between steps.
 
+Other workloads (``--workload``) measure the remaining operator rows with the
+same machinery: ``rowreduce`` (softmax, layernorm, rms_norm,
+weighted_rms_norm on [32768, 4096] bf16 and fp32).
+
 Metric: algorithmic HBM bytes (each input read once, each output written
 once) per second, aggregated over the step and over all ranks.
 
@@ -24,20 +28,18 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
-import threading
 import time
 
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "triton-xdna_b200"))
+sys.path.insert(0, ROOT)
 
 N28 = 1 << 28
-N27 = 1 << 27
 POOL_SHAPE = (64, 256, 224, 224)
+ROWS, COLS = 32768, 4096
 
 
 def _peaks() -> dict:
@@ -45,139 +47,199 @@ def _peaks() -> dict:
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
-# ----------------------------------------------------------------------------- workload
+def _tag(dt):
+    return "bf16" if dt == torch.bfloat16 else "f32"
 
 
-def suite_ops():
-    """(name, dtype, n_in_elems, n_out_elems, elem_bytes) for each launch of a step."""
+# ----------------------------------------------------------------------------- workloads
+#
+# A workload is a list of ops.  Each op has a name, its algorithmic bytes, a
+# device launch (closure over device-resident tensors) and, for the headline
+# workload, a launch through the public reference-signature API on pinned
+# host tensors (for the end-to-end number).
+
+
+class Op:
+    def __init__(self, name, nbytes, run, e2e=None, h2d=0, d2h=0):
+        self.name, self.nbytes, self.run, self.e2e = name, nbytes, run, e2e
+        self.h2d, self.d2h = h2d, d2h
+
+
+def elementwise_workload(dev, n: int, seed: int, host: bool):
+    from xb200 import kernels
+    from xb200 import ops as X
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    gh = torch.Generator().manual_seed(seed)
+    half = n // 2
     out = []
-    for dt, eb in ((torch.bfloat16, 2), (torch.float32, 4)):
-        tag = "bf16" if dt == torch.bfloat16 else "f32"
+    for dt in (torch.bfloat16, torch.float32):
+        eb = 2 if dt == torch.bfloat16 else 4
+        x = torch.randn(n, generator=g, device=dev, dtype=torch.float32).to(dt)
+        y = torch.randn(n, generator=g, device=dev, dtype=torch.float32).to(dt)
+        o = torch.empty_like(x)
+        hx = hy = ho = None
+        if host:
+            hx = torch.randn(n, generator=gh).to(dt).pin_memory()
+            hy = torch.randn(n, generator=gh).to(dt).pin_memory()
+            ho = torch.empty_like(hx).pin_memory()
+        t = _tag(dt)
+        B = {"BLOCK_SIZE": 1024}
+        grid = (max(1, n // 1024),)
+
+        def mk(name, nin, nout, dev_fn, host_fn, nptr):
+            # the launcher copies every pointer argument in and the last one back
+            return Op(f"{name}_{t}", (nin + nout) * eb, dev_fn, host_fn, h2d=nptr * nout * eb, d2h=nout * eb)
+
         out += [
-            (f"vecadd_{tag}", dt, 2 * N28, N28, eb),
-            (f"axpy_{tag}", dt, 2 * N28, N28, eb),
-            (f"relu_{tag}", dt, N28, N28, eb),
-            (f"leaky_relu_{tag}", dt, N28, N28, eb),
-            (f"gelu_tanh_{tag}", dt, N28, N28, eb),
-            (f"sigmoid_{tag}", dt, N28, N28, eb),
-            (f"silu_{tag}", dt, N28, N28, eb),
-            (f"swiglu_{tag}", dt, 2 * N27, N27, eb),
+            mk("vecadd", 2 * n, n, lambda x=x, y=y, o=o: X.vecadd(x, y, out=o),
+               lambda hx=hx, hy=hy, ho=ho: kernels.vecadd[grid](hx, hy, ho, n, BLOCK_SIZE_N=1024), 3),
+            mk("axpy", 2 * n, n, lambda x=x, y=y, o=o: X.axpy(x, y, 2.5, out=o),
+               lambda hx=hx, hy=hy, ho=ho: kernels.axpy_kernel[grid](hx, hy, ho, 2.5, n, **B), 3),
+            mk("relu", n, n, lambda x=x, o=o: X.relu(x, out=o),
+               lambda hx=hx, ho=ho: kernels.relu_kernel[grid](hx, ho, n, **B), 2),
+            mk("leaky_relu", n, n, lambda x=x, o=o: X.leaky_relu(x, 0.01, out=o),
+               lambda hx=hx, ho=ho: kernels.leaky_relu_kernel[grid](hx, ho, n, **B), 2),
+            mk("gelu_tanh", n, n, lambda x=x, o=o: X.gelu_tanh(x, out=o),
+               lambda hx=hx, ho=ho: kernels.gelu_kernel_gpu[grid](hx, ho, n, **B), 2),
+            mk("sigmoid", n, n, lambda x=x, o=o: X.sigmoid(x, out=o),
+               lambda hx=hx, ho=ho: kernels.sigmoid_kernel[grid](hx, ho, n, **B), 2),
+            mk("silu", n, n, lambda x=x, o=o: X.silu(x, out=o),
+               lambda hx=hx, ho=ho: kernels.silu_kernel[grid](hx, ho, n, **B), 2),
+            mk("swiglu", 2 * half, half, lambda x=x, y=y, o=o: X.swiglu(x[:half], y[:half], out=o[:half]),
+               lambda hx=hx, hy=hy, ho=ho: kernels.swiglu_kernel[(max(1, half // 1024),)](
+                   hx[:half], hy[:half], ho[:half], half, **B), 3),
         ]
-    n_in = 1
-    for s in POOL_SHAPE:
-        n_in *= s
-    out.append(("avg_pool2d_2x2_f32", torch.float32, n_in, n_in // 4, 4))
-    return out
+    planes = max(1, POOL_SHAPE[0] * n // N28) * POOL_SHAPE[1]
+    H, W = POOL_SHAPE[2], POOL_SHAPE[3]
+    pin = torch.randn((planes, H, W), generator=g, device=dev)
+    pout = torch.empty((planes, H // 2, W // 2), device=dev)
+    hpin = hpout = None
+    if host:
+        hpin = torch.randn((planes, H, W), generator=gh).pin_memory()
+        hpout = torch.empty((planes, H // 2, W // 2)).pin_memory()
+    nin, nout = planes * H * W, planes * (H // 2) * (W // 2)
+    out.append(Op("avg_pool2d_2x2_f32", (nin + nout) * 4, lambda: X.avg_pool2d_2x2(pin, out=pout),
+                  lambda: kernels.avg_pool2d_kernel[(planes,)](hpin, hpout, planes, H, W, BLOCK=1),
+                  h2d=(nin + nout) * 4, d2h=nout * 4))
+    config = {
+        "workload": f"elementwise/activation suite: 8 ops x {{bf16,f32}} on {n} elements "
+                    f"(swiglu {half}+{half}) + avg_pool2d 2x2/s2 on [{planes // 256},256,224,224] f32",
+        "n_elements": n,
+        "l2": "every input > 126 MB L2 (no flush needed)" if n * 2 > 126e6 else "inputs may fit in L2",
+    }
+    return out, config, "elementwise/activation suite algorithmic HBM throughput", "bf16+f32"
 
 
-def op_bytes(op) -> int:
-    _, _, nin, nout, eb = op
-    return (nin + nout) * eb
+def rowreduce_workload(dev, n: int, seed: int, host: bool):
+    from xb200 import ops as X
+
+    rows = max(1, ROWS * n // N28)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    out = []
+    for dt in (torch.bfloat16, torch.float32):
+        eb = 2 if dt == torch.bfloat16 else 4
+        x = (torch.randn(rows, COLS, generator=g, device=dev) * 3).to(dt)
+        gm = (1 + 0.1 * torch.randn(COLS, generator=g, device=dev)).to(dt)
+        bt = (0.1 * torch.randn(COLS, generator=g, device=dev)).to(dt)
+        y = torch.empty_like(x)
+        t = _tag(dt)
+        nb = 2 * rows * COLS * eb
+        out += [
+            Op(f"softmax_{t}", nb, lambda x=x, y=y: X.softmax(x, out=y)),
+            Op(f"layernorm_{t}", nb + 2 * COLS * eb, lambda x=x, y=y, gm=gm, bt=bt: X.layernorm(x, gm, bt, 1e-5, out=y)),
+            Op(f"rms_norm_{t}", nb, lambda x=x, y=y: X.rms_norm(x, None, 1e-6, out=y)),
+            Op(f"weighted_rms_norm_{t}", nb + COLS * eb, lambda x=x, y=y, gm=gm: X.rms_norm(x, gm, 1e-6, out=y)),
+        ]
+    config = {"workload": f"row reductions on [{rows} x {COLS}] bf16 and f32, x~N(0,1)*3", "rows": rows,
+              "cols": COLS, "l2": "every input > 126 MB L2 (no flush needed)"}
+    return out, config, "row-reduction suite algorithmic HBM throughput", "bf16+f32"
 
 
-class DeviceSuite:
-    """Device-resident inputs/outputs and the launch sequence of one step."""
-
-    def __init__(self, device, seed: int = 0):
-        from xb200 import ops
-
-        self.ops = ops
-        g = torch.Generator(device=device).manual_seed(seed)
-        self.t = {}
-        for dt in (torch.bfloat16, torch.float32):
-            x = torch.randn(N28, generator=g, device=device, dtype=torch.float32).to(dt)
-            y = torch.randn(N28, generator=g, device=device, dtype=torch.float32).to(dt)
-            self.t[dt] = (x, y, torch.empty_like(x))
-        self.pool_in = torch.randn(POOL_SHAPE, generator=g, device=device, dtype=torch.float32)
-        self.pool_out = torch.empty(POOL_SHAPE[:2] + (POOL_SHAPE[2] // 2, POOL_SHAPE[3] // 2), device=device)
-
-    def run(self, name):
-        o = self.ops
-        if name.startswith("avg_pool2d"):
-            o.avg_pool2d_2x2(self.pool_in, out=self.pool_out)
-            return
-        dt = torch.bfloat16 if name.endswith("bf16") else torch.float32
-        x, y, out = self.t[dt]
-        base = name.rsplit("_", 1)[0]
-        if base == "vecadd":
-            o.vecadd(x, y, out=out)
-        elif base == "axpy":
-            o.axpy(x, y, 2.5, out=out)
-        elif base == "relu":
-            o.relu(x, out=out)
-        elif base == "leaky_relu":
-            o.leaky_relu(x, 0.01, out=out)
-        elif base == "gelu_tanh":
-            o.gelu_tanh(x, out=out)
-        elif base == "sigmoid":
-            o.sigmoid(x, out=out)
-        elif base == "silu":
-            o.silu(x, out=out)
-        elif base == "swiglu":
-            o.swiglu(x[:N27], y[:N27], out=out[:N27])
-        else:
-            raise KeyError(name)
+WORKLOADS = {"elementwise": elementwise_workload, "rowreduce": rowreduce_workload}
 
 
 # ----------------------------------------------------------------------------- clocks
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
+    """SM clock and clock-event (throttle) reasons of the benchmark's GPU, read
+    through NVML every 5 ms by a background thread while the timed region
+    runs (read-only queries; nothing about the GPU is changed)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {
+        "hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+        "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+        "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+        "sw_power_cap": "nvmlClocksEventReasonSwPowerCap",
+        "hw_power_brake_slowdown": "nvmlClocksEventReasonHwPowerBrakeSlowdown",
+    }
 
-    def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = None
+    def __init__(self, cuda_index: int, period_s: float = 0.005):
+        self.cuda_index = cuda_index
+        self.period = period_s
+        self.samples = []
+        self.smax = None
+        self._stop = None
+        self._thr = None
+        self.nv = None
+
+    def _handle(self):
+        import pynvml as nv
+
+        nv.nvmlInit()
+        self.nv = nv
+        p = torch.cuda.get_device_properties(self.cuda_index)
+        try:
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.cuda_index)
 
     def __enter__(self):
+        import threading
+
         try:
-            fd, self.path = tempfile.mkstemp(suffix=".csv")
-            os.close(fd)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            h = self._handle()
+            nv = self.nv
+            self.smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons",
+                                  getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+        except Exception:
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), int(get_reasons(h))))
+                except Exception:
+                    pass
+                self._stop.wait(self.period)
+
+        self._thr = threading.Thread(target=loop, daemon=True)
+        self._thr.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        if self._thr is not None:
+            self._stop.set()
+            self._thr.join(timeout=2)
 
     def summary(self):
-        if self.proc is None or not self.path or not os.path.exists(self.path):
+        if not self.samples:
             return None
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(nm)
-        os.unlink(self.path)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = set()
+        for _, bits in self.samples:
+            for name, attr in self.REASONS.items():
+                if bits & getattr(self.nv, attr, 0):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(c for c, _ in self.samples), "sm_max_mhz": self.smax,
+                "reasons": sorted(reasons), "samples": len(self.samples), "source": "NVML, 5 ms"}
 
 
 # ----------------------------------------------------------------------------- distributed helpers
@@ -220,47 +282,54 @@ def _max_over_ranks(v: float, world: int) -> float:
 # ----------------------------------------------------------------------------- CPU baseline
 
 
-def cpu_suite(sample_elems: int, reps: int = 1):
-    """Time the oracle (examples' torch CPU expressions) on a bounded sample of
-    the suite; returns (GB/s, seconds, threads, description)."""
-    sys.path.insert(0, ROOT)
+def cpu_baseline(workload: str, sample: int, reps: int = 1):
+    """Time the oracle (the examples' torch CPU expressions) on a bounded sample
+    of the workload with every host thread; returns (GB/s, threads, description)."""
     from oracle import ops as O
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    frac = sample_elems / N28
     g = torch.Generator().manual_seed(0)
-    total_bytes = 0
-    total_s = 0.0
-    pool_planes = max(1, int(POOL_SHAPE[0] * POOL_SHAPE[1] * frac))
-    for op in suite_ops():
-        name, dt, nin, nout, eb = op
-        if name.startswith("avg_pool"):
-            x = torch.randn((pool_planes, POOL_SHAPE[2], POOL_SHAPE[3]), generator=g)
-            fn = lambda: O.avg_pool2d_2x2(x)  # noqa: E731
-            nbytes = x.numel() * 4 * 5 // 4
-        else:
-            n = max(1024, int(nout * frac))
-            x = torch.randn(n, generator=g).to(dt)
-            y = torch.randn(n, generator=g).to(dt)
-            base = name.rsplit("_", 1)[0]
-            fn = {
-                "vecadd": lambda: O.vecadd(x, y), "axpy": lambda: O.axpy(x, y, 2.5), "relu": lambda: O.relu(x),
-                "leaky_relu": lambda: O.leaky_relu(x, 0.01), "gelu_tanh": lambda: O.gelu_tanh(x),
-                "sigmoid": lambda: O.sigmoid(x), "silu": lambda: O.silu(x), "swiglu": lambda: O.swiglu(x, y),
-            }[base]
-            nbytes = (nin // nout + 1) * n * eb
-        fn()  # warm-up
-        best = None
-        for _ in range(reps):
-            t0 = time.perf_counter()
-            fn()
-            dt_s = time.perf_counter() - t0
-            best = dt_s if best is None else min(best, dt_s)
-        total_bytes += nbytes
+    cases = []
+    if workload == "elementwise":
+        for dt in (torch.bfloat16, torch.float32):
+            eb = 2 if dt == torch.bfloat16 else 4
+            x = torch.randn(sample, generator=g).to(dt)
+            y = torch.randn(sample, generator=g).to(dt)
+            h = sample // 2
+            cases += [
+                (lambda x=x, y=y: O.vecadd(x, y), 3 * sample * eb), (lambda x=x, y=y: O.axpy(x, y, 2.5), 3 * sample * eb),
+                (lambda x=x: O.relu(x), 2 * sample * eb), (lambda x=x: O.leaky_relu(x, 0.01), 2 * sample * eb),
+                (lambda x=x: O.gelu_tanh(x), 2 * sample * eb), (lambda x=x: O.sigmoid(x), 2 * sample * eb),
+                (lambda x=x: O.silu(x), 2 * sample * eb), (lambda x=x, y=y: O.swiglu(x[:h], y[:h]), 3 * h * eb),
+            ]
+        planes = max(1, sample // (224 * 224))
+        p = torch.randn((planes, 224, 224), generator=g)
+        cases.append((lambda: O.avg_pool2d_2x2(p), p.numel() * 4 * 5 // 4))
+        desc = f"every suite operator on {sample} elements ({sample / N28:.4f} of the workload), min of {reps}"
+    else:
+        rows = max(1, sample // COLS)
+        for dt in (torch.bfloat16, torch.float32):
+            eb = 2 if dt == torch.bfloat16 else 4
+            x = (torch.randn(rows, COLS, generator=g) * 3).to(dt)
+            w = (1 + 0.1 * torch.randn(COLS, generator=g)).to(dt)
+            nb = 2 * rows * COLS * eb
+            cases += [(lambda x=x: O.softmax(x), nb), (lambda x=x, w=w: O.layernorm(x, w, w, 1e-5), nb),
+                      (lambda x=x: O.rms_norm(x, 1e-6), nb), (lambda x=x, w=w: O.weighted_rms_norm(x, w, 1e-6), nb)]
+        desc = f"every row op on [{rows} x {COLS}] ({rows / ROWS:.4f} of the workload), min of {reps}"
+    total_b, total_s = 0, 0.0
+    for fn, nb in cases:
+        fn()
+        best = min(_timeit(fn) for _ in range(reps))
+        total_b += nb
         total_s += best
-    desc = f"every suite operator on {sample_elems} elements ({frac:.4f} of the workload), min of {reps}"
-    return total_bytes / total_s / 1e9, total_s, threads, desc
+    return total_b / total_s / 1e9, threads, desc
+
+
+def _timeit(fn):
+    t0 = time.perf_counter()
+    fn()
+    return time.perf_counter() - t0
 
 
 # ----------------------------------------------------------------------------- main
@@ -269,69 +338,56 @@ def cpu_suite(sample_elems: int, reps: int = 1):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="xb200", choices=["xb200", "reference"])
+    ap.add_argument("--workload", default="elementwise", choices=sorted(WORKLOADS))
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--elements", type=int, default=1 << 28,
+    ap.add_argument("--elements", type=int, default=N28,
                     help="flat tensor length (default 2^28, the workload); smaller values are for profiling only")
     args = ap.parse_args()
-    global N28, N27, POOL_SHAPE
-    if args.elements != N28:
-        N28 = args.elements
-        N27 = N28 // 2
-        POOL_SHAPE = (max(1, 64 * N28 // (1 << 28)),) + POOL_SHAPE[1:]
     warmup = max(3, args.warmup)
 
-    world, rank, local = _dist_init() if args.impl == "xb200" else (
-        int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)
-    ops_list = suite_ops()
-    step_bytes = sum(op_bytes(o) for o in ops_list)
-    config = {
-        "workload": "elementwise/activation suite: 8 ops x {bf16,f32} on 2^28 elements (swiglu 2^27+2^27) "
-                    "+ avg_pool2d 2x2/s2 on [64,256,224,224] f32",
-        "n_elements": N28,
-        "launches_per_step": len(ops_list),
-        "bytes_per_step": step_bytes,
-        "l2": "every input > 126 MB L2 (no flush needed)",
-        "parallelism": f"weak x{world} (independent replicas of the suite, no collective)",
-    }
-
     if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
         if rank != 0:
             return
         sample = 1 << 22
-        gbs, secs, threads, desc = cpu_suite(sample, reps=1)
-        for _ in range(warmup - 1):
-            pass
-        vals = []
-        for _ in range(args.steps):
-            v, _, _, _ = cpu_suite(sample, reps=1)
-            vals.append(v)
+        for _ in range(warmup):
+            cpu_baseline(args.workload, 1 << 16)
+        vals = [cpu_baseline(args.workload, sample)[0] for _ in range(args.steps)]
+        _, threads, desc = cpu_baseline(args.workload, sample)
         value = statistics.median(vals)
-        line = {
-            "impl": "reference", "metric": "elementwise/activation suite algorithmic HBM throughput",
+        print(json.dumps({
+            "impl": "reference", "metric": f"{args.workload} suite algorithmic HBM throughput",
             "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16+f32",
-            "data": "synthetic N(0,1), seed 0", "config": config,
+            "data": "synthetic N(0,1), seed 0",
+            "config": {"workload": f"{args.workload} suite, CPU sample", "sample": desc},
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": desc},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }
-        print(json.dumps(line))
+        }))
         return
 
-    from xb200 import _lib, kernels
+    world, rank, local = _dist_init()
+    from xb200 import _lib
 
     _lib.load()
     dev = torch.device("cuda", torch.cuda.current_device())
-    suite = DeviceSuite(dev, seed=rank)
+    want_e2e = rank == 0 and args.e2e_steps > 0 and args.workload == "elementwise"
+    ops_list, config, metric, dtype = WORKLOADS[args.workload](dev, args.elements, rank, want_e2e)
+    config["launches_per_step"] = len(ops_list)
+    config["parallelism"] = f"weak x{world} (independent replicas, no collective)"
+    step_bytes = sum(o.nbytes for o in ops_list)
+    config["bytes_per_step"] = step_bytes
     stream = torch.cuda.current_stream()
 
     for _ in range(warmup):
         for o in ops_list:
-            suite.run(o[0])
+            o.run()
     torch.cuda.synchronize()
 
     # ---- timed region: K steps, per-launch CUDA events on the launching stream
@@ -345,111 +401,61 @@ def main():
         for s in range(args.steps):
             for i, o in enumerate(ops_list):
                 evs[s][i][0].record(stream)
-                suite.run(o[0])
+                o.run()
                 evs[s][i][1].record(stream)
         stop.record(stream)
         torch.cuda.synchronize()
     _barrier(world)
-    total_ms = start.elapsed_time(stop)
-    total_ms = _max_over_ranks(total_ms, world)
+    total_ms = _max_over_ranks(start.elapsed_time(stop), world)
     clocks = clk.summary()
 
-    per_op_ms = {o[0]: statistics.mean(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(args.steps))
+    per_op_ms = {o.name: statistics.mean(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(args.steps))
                  for i, o in enumerate(ops_list)}
     ms_per_step = total_ms / args.steps
     value = step_bytes * world / (ms_per_step * 1e-3) / 1e9
     peaks = _peaks()
     hbm = peaks["hbm_gbs"]
-    dom = max(ops_list, key=lambda o: per_op_ms[o[0]])
-    dom_gbs = op_bytes(dom) / (per_op_ms[dom[0]] * 1e-3) / 1e9
-    suite_detail = {o[0]: {"ms": round(per_op_ms[o[0]], 4),
-                           "gbs": round(op_bytes(o) / (per_op_ms[o[0]] * 1e-3) / 1e9, 1),
-                           "frac": round(op_bytes(o) / (per_op_ms[o[0]] * 1e-3) / 1e9 / hbm, 3)} for o in ops_list}
+    dom = max(ops_list, key=lambda o: per_op_ms[o.name])
+    dom_gbs = dom.nbytes / (per_op_ms[dom.name] * 1e-3) / 1e9
+    detail = {o.name: {"ms": round(per_op_ms[o.name], 4), "gbs": round(o.nbytes / (per_op_ms[o.name] * 1e-3) / 1e9, 1),
+                       "frac": round(o.nbytes / (per_op_ms[o.name] * 1e-3) / 1e9 / hbm, 3)} for o in ops_list}
 
-    # ---- end to end through the public launch API with host (pinned) tensors
     e2e = None
-    if rank == 0 and args.e2e_steps > 0:
-        e2e = e2e_suite(kernels, dev, args.e2e_steps)
+    if want_e2e:
+        for o in ops_list:
+            o.e2e()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.e2e_steps):
+            for o in ops_list:
+                o.e2e()
+        torch.cuda.synchronize()
+        secs = (time.perf_counter() - t0) / args.e2e_steps
+        e2e = {"value": round(step_bytes / secs / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": sum(o.h2d for o in ops_list), "d2h_bytes_per_step": sum(o.d2h for o in ops_list),
+               "ms_per_step": round(secs * 1e3, 2),
+               "api": "xb200.kernels.<reference kernel>[grid](pinned host tensors...)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, secs, threads, desc = cpu_suite(1 << 24, reps=1)
+        gbs, threads, desc = cpu_baseline(args.workload, 1 << 24)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc}
 
     if rank == 0:
-        line = {
-            "metric": "elementwise/activation suite algorithmic HBM throughput",
-            "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": warmup,
-            "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16+f32", "data": "synthetic N(0,1), seed = rank", "config": config,
-            "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": round(dom_gbs, 1), "peak": hbm,
+        print(json.dumps({
+            "metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic N(0,1), seed = rank", "config": config,
+            "roofline": {"bound": "hbm", "kernel": dom.name, "achieved": round(dom_gbs, 1), "peak": hbm,
                          "peak_source": peaks["source"], "unit": "GB/s", "frac": round(dom_gbs / hbm, 4),
                          "traffic": None},
-            "suite": suite_detail,
-            "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks, "gpu_launches": len(ops_list) * args.steps,
-        }
-        print(json.dumps(line))
+            "ops": detail, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
+            "gpu_launches": len(ops_list) * args.steps,
+        }))
     if world > 1:
         import torch.distributed as dist
 
         dist.destroy_process_group()
-
-
-def e2e_suite(kernels, dev, steps: int):
-    """Each op through xb200.kernels (the reference-signature launcher) on pinned
-    host tensors: host->device copies of every pointer argument, the kernel,
-    and the copy of the output back, all inside the timed region."""
-    g = torch.Generator().manual_seed(0)
-    host = {}
-    for dt in (torch.bfloat16, torch.float32):
-        x = torch.randn(N28, generator=g).to(dt).pin_memory()
-        y = torch.randn(N28, generator=g).to(dt).pin_memory()
-        host[dt] = (x, y, torch.empty_like(x).pin_memory())
-    pin = torch.randn(POOL_SHAPE, generator=g).pin_memory()
-    pout = torch.empty(POOL_SHAPE[:2] + (POOL_SHAPE[2] // 2, POOL_SHAPE[3] // 2)).pin_memory()
-    pool_rows = POOL_SHAPE[0] * POOL_SHAPE[1]
-
-    def one_step():
-        h2d = d2h = 0
-        for name, dt, nin, nout, eb in suite_ops():
-            if name.startswith("avg_pool"):
-                kernels.avg_pool2d_kernel[(pool_rows,)](pin, pout, POOL_SHAPE[0] * POOL_SHAPE[1], POOL_SHAPE[2],
-                                                          POOL_SHAPE[3], BLOCK=1)
-                h2d += (pin.numel() + pout.numel()) * 4
-                d2h += pout.numel() * 4
-                continue
-            x, y, out = host[dt]
-            base = name.rsplit("_", 1)[0]
-            blk = {"BLOCK_SIZE": 1024}
-            if base == "vecadd":
-                kernels.vecadd[(N28 // 1024,)](x, y, out, N28, BLOCK_SIZE_N=1024)
-                h2d += 3 * N28 * eb
-            elif base == "axpy":
-                kernels.axpy_kernel[(N28 // 1024,)](x, y, out, 2.5, N28, **blk)
-                h2d += 3 * N28 * eb
-            elif base == "swiglu":
-                kernels.swiglu_kernel[(N27 // 1024,)](x[:N27], y[:N27], out[:N27], N27, **blk)
-                h2d += 3 * N27 * eb
-            else:
-                k = {"relu": kernels.relu_kernel, "leaky_relu": kernels.leaky_relu_kernel,
-                     "gelu_tanh": kernels.gelu_kernel_gpu, "sigmoid": kernels.sigmoid_kernel,
-                     "silu": kernels.silu_kernel}[base]
-                k[(N28 // 1024,)](x, out, N28, **blk)
-                h2d += 2 * N28 * eb
-            d2h += nout * eb
-        return h2d, d2h
-
-    one_step()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        h2d, d2h = one_step()
-    torch.cuda.synchronize()
-    secs = (time.perf_counter() - t0) / steps
-    step_bytes = sum(op_bytes(o) for o in suite_ops())
-    return {"value": round(step_bytes / secs / 1e9, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h, "ms_per_step": round(secs * 1e3, 2),
-            "api": "xb200.kernels.<reference kernel>[grid](host tensors...)"}
 
 
 if __name__ == "__main__":

@@ -68,9 +68,9 @@ int run_pool(const void* xv, void* yv, int64_t planes, int64_t h, int64_t w, cud
   const T* x = static_cast<const T*>(xv);
   T* y = static_cast<T*>(yv);
   constexpr int VN = Vec16<T>::N;
-  int sms = 148;
-  sm_count(&sms);
-  const int64_t cap = (int64_t)sms * 8;
+  // one-shot grid (one output vector per thread): the block scheduler balances
+  // the SMs better than a persistent grid-stride loop for a pure stream
+  const int64_t cap = 0x7fffffffLL;
   if (w % (2 * VN) == 0 && ow % VN == 0 && aligned16(x) && aligned16(y)) {
     int64_t total = planes * oh * (ow / VN);
     int64_t grid = (total + 255) / 256;
