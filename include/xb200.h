@@ -144,6 +144,61 @@ XB_API int xb_avg_pool2d_2x2(const void* x, void* y, int64_t planes, int64_t h,
                       int64_t w, int dtype, void* stream, char* err,
                       size_t errlen);
 
+/* ---------------------------------------------------------------------------
+ * Dense GEMMs on the tcgen05 tensor cores.  Row-major operands, leading
+ * dimensions in elements.  A and B (and W) must start on a 16-byte boundary
+ * with row pitches that are multiples of 16 bytes (TMA); C needs no alignment
+ * beyond its element size.  Ragged M / N / K are handled.
+ * ------------------------------------------------------------------------- */
+
+/* C[M,N] (int32) = A[M,K] (int8) @ B[K,N] (int8), exact.  Replaces
+ * `bare_matmul_i8` (examples/matmul_i8_m128_n64_k64/matmul_i8_m128_n64_k64.py:
+ * 22-52, examples/matmul_i8_m64_n64_k64/matmul_i8_m64_n64_k64.py:21-51). */
+XB_API int xb_matmul_i8(const void* A, const void* B, void* C, int64_t M,
+                        int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                        int64_t ldc, void* stream, char* err, size_t errlen);
+
+/* Bytes of device workspace xb_matmul_i16 needs for an M x N x K product.
+ * The reference has int16 GEMM only as a README claim (README.md:21) with an
+ * i32 accumulator (amd_triton_npu/backend/matmul_transform.py:62-64). */
+XB_API int xb_matmul_i16_workspace_size(int64_t M, int64_t N, int64_t K,
+                                        size_t* bytes, char* err,
+                                        size_t errlen);
+
+/* C[M,N] (int32) = A[M,K] (int16) @ B[K,N] (int16) with int32 wrap-around
+ * (mod 2^32), the semantics of an int32 accumulator.  `workspace` (256-byte
+ * aligned, >= xb_matmul_i16_workspace_size bytes) receives the int8 limb
+ * planes; it must stay untouched until the call's work on `stream` is done. */
+XB_API int xb_matmul_i16(const void* A, const void* B, void* C, int64_t M,
+                         int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                         int64_t ldc, void* workspace, size_t workspace_bytes,
+                         void* stream, char* err, size_t errlen);
+
+/* C[M,N] = A[M,K] (bf16) @ B[K,N] (bf16), fp32 accumulation, C in f32 or bf16
+ * (out_dtype XB_DT_F32 / XB_DT_BF16).  Replaces `bare_matmul`
+ * (examples/matmul_bf16_m64_n64_k64/matmul_bf16_m64_n64_k64.py:16-46,
+ * examples/autotune-matmul/matmul.py:22-53). */
+XB_API int xb_matmul_bf16(const void* A, const void* B, void* C, int64_t M,
+                          int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                          int64_t ldc, int out_dtype, void* stream, char* err,
+                          size_t errlen);
+
+/* Y[M,N] (bf16) = X[M,K] @ W[N,K]^T (+ bias[N]), W in nn.Linear layout, fp32
+ * accumulation; bias may be NULL.  Replaces `triton_linear`
+ * (examples/qwen2_5/kernels/matmul.py:172-296). */
+XB_API int xb_linear_bf16(const void* X, const void* W, const void* bias,
+                          void* Y, int64_t M, int64_t N, int64_t K,
+                          int64_t ldx, int64_t ldw, int64_t ldy, void* stream,
+                          char* err, size_t errlen);
+
+/* Read (synchronising `stream`) and clear the device status word that the
+ * tensor-core kernels set when a bounded wait runs out: 0 = fine,
+ * XB_ERR_TIMEOUT = a kernel gave up and returned early (its output is not
+ * valid).  Mirrors the reference runtime's watchdog
+ * (amd_triton_npu/backend/include/HsaRuntime/HsaRuntime.h:57-67). */
+XB_API int xb_device_status(void* stream, int* status, char* err,
+                            size_t errlen);
+
 #ifdef __cplusplus
 } /* extern "C" */
 #endif

@@ -54,5 +54,8 @@ def test_tight_against_oracle(case):
         torch.testing.assert_close(out.float(), ref.float(), atol=1e-6, rtol=2 ** -7)
         same = (out == ref).float().mean().item()
         assert same > 0.97, f"only {same:.3f} of elements bit-identical"
+    elif entry["kernel"] == "bare_matmul":
+        # fp32 accumulation in a different order than the CPU's
+        torch.testing.assert_close(out, ref, atol=1e-3, rtol=1e-4)
     else:
         torch.testing.assert_close(out, ref, atol=2e-5, rtol=2e-5)

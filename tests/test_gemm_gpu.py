@@ -1,0 +1,179 @@
+"""tcgen05 GEMMs against the oracle.
+
+int8 / int16 are bit-exact (int32 accumulation, wrap-around mod 2^32 for
+int16).  bf16 uses the autotune example's tolerance rule
+(examples/autotune-matmul/matmul.py:105-115: atol 1.5e-3 * sqrt(8192 / K),
+rtol 1.6e-2, inputs scaled by 1/sqrt(K)) against an fp32 product of the same
+bf16 inputs.  Full-size shapes are checked exactly through row and column
+checksums (C 1 = A (B 1), 1^T C = (1^T A) B) in float64, which is exact at
+these magnitudes.
+"""
+
+import math
+
+import pytest
+import torch
+
+from oracle import cgemm
+from oracle import ops as O
+from xb200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _rand_int(shape, lo, hi, dtype, seed):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(lo, hi, shape, generator=g, dtype=dtype)
+
+
+def _status_ok():
+    assert ops.device_status() == 0
+
+
+I8_SHAPES = [(128, 64, 64), (256, 128, 256), (1024, 1024, 256), (200, 304, 176), (16, 512, 1024), (1, 16, 16),
+             (300, 640, 4096), (129, 257 + 15, 48)]
+
+
+@pytest.mark.parametrize("M,N,K", I8_SHAPES)
+def test_matmul_i8_exact(M, N, K):
+    if (N % 16) or (K % 16):
+        pytest.skip("TMA row pitch must be a multiple of 16 bytes")
+    a = _rand_int((M, K), -128, 128, torch.int8, M * 7 + K)
+    b = _rand_int((K, N), -128, 128, torch.int8, N * 3 + K)
+    c = ops.matmul_i8(a.cuda(), b.cuda())
+    assert torch.equal(c.cpu(), cgemm.gemm_int(a, b))
+    _status_ok()
+
+
+def test_matmul_i8_padded_leading_dims_and_guard_bands():
+    M, N, K = 130, 272, 96
+    a_full = _rand_int((M, K + 32), -128, 128, torch.int8, 1)
+    b_full = _rand_int((K, N + 48), -128, 128, torch.int8, 2)
+    a, b = a_full[:, :K], b_full[:, :N]
+    c_full = torch.full((M + 2, N + 40), 12345, dtype=torch.int32, device="cuda")
+    c = c_full[1:M + 1, 8:N + 8]
+    ops.matmul_i8(a_full.cuda()[:, :K], b_full.cuda()[:, :N], out=c)
+    assert torch.equal(c.cpu(), cgemm.gemm_int(a.contiguous(), b.contiguous()))
+    c_cpu = c_full.cpu()
+    assert torch.all(c_cpu[0] == 12345) and torch.all(c_cpu[-1] == 12345)
+    assert torch.all(c_cpu[:, :8] == 12345) and torch.all(c_cpu[:, N + 8:] == 12345)
+
+
+I16_SHAPES = [(128, 128, 64), (256, 256, 512), (100, 144, 80), (16, 256, 1024), (384, 128, 1000)]
+
+
+@pytest.mark.parametrize("M,N,K", I16_SHAPES)
+def test_matmul_i16_exact(M, N, K):
+    a = _rand_int((M, K), -2**15, 2**15, torch.int16, M + K)
+    b = _rand_int((K, N), -2**15, 2**15, torch.int16, N + 2 * K)
+    c = ops.matmul_i16(a.cuda(), b.cuda())
+    assert torch.equal(c.cpu(), cgemm.gemm_int(a, b))
+    _status_ok()
+
+
+def test_matmul_i16_wraps_mod_2_32():
+    # extreme values: every partial product is 2^30, sums leave int32 range
+    M, N, K = 128, 128, 4096
+    a = torch.full((M, K), -2**15, dtype=torch.int16)
+    b = torch.full((K, N), -2**15, dtype=torch.int16)
+    a[1::2] = 2**15 - 1
+    b[:, ::3] = 12345
+    c = ops.matmul_i16(a.cuda(), b.cuda())
+    assert torch.equal(c.cpu(), O.matmul_int_exact(a, b))
+    _status_ok()
+
+
+BF16_SHAPES = [(256, 256, 256), (512, 384, 320), (1024, 1024, 1024), (200, 264, 136), (16, 1024, 2048),
+               (128, 256, 8192)]
+
+
+@pytest.mark.parametrize("M,N,K", BF16_SHAPES)
+def test_matmul_bf16_f32_out(M, N, K):
+    g = torch.Generator().manual_seed(M * N + K)
+    s = 1.0 / math.sqrt(K)
+    a = (torch.randn((M, K), generator=g) * s).to(torch.bfloat16)
+    b = (torch.randn((K, N), generator=g) * s).to(torch.bfloat16)
+    c = ops.matmul_bf16(a.cuda(), b.cuda(), torch.float32).cpu()
+    ref = O.matmul_bf16_f32acc(a, b)
+    atol = 1.5e-3 * math.sqrt(8192 / K)
+    torch.testing.assert_close(c, ref, atol=atol, rtol=1.6e-2)
+    # much tighter in practice: fp32 accumulation of the same products
+    assert float((c - ref).abs().max()) < 1e-4 * max(1.0, float(ref.abs().max()))
+    _status_ok()
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (100, 200, 64), (4096, 4096, 4096)])
+def test_matmul_bf16_bf16_out(M, N, K):
+    g = torch.Generator().manual_seed(K)
+    a = torch.randn((M, K), generator=g).to(torch.bfloat16)
+    b = torch.randn((K, N), generator=g).to(torch.bfloat16)
+    c = ops.matmul_bf16(a.cuda(), b.cuda(), torch.bfloat16).cpu().float()
+    ref = O.matmul_bf16_f32acc(a, b).to(torch.bfloat16).float()
+    torch.testing.assert_close(c, ref, atol=1e-2 * math.sqrt(K) * 0.1, rtol=2 ** -7)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 896, 896), (512, 1152, 896), (33, 4864, 896), (128, 896, 4864)])
+def test_linear_bias(M, N, K):
+    g = torch.Generator().manual_seed(N + K)
+    x = torch.randn((M, K), generator=g).to(torch.bfloat16)
+    w = (torch.randn((N, K), generator=g) * 0.02).to(torch.bfloat16)
+    bias = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+    y = ops.linear(x.cuda(), w.cuda(), bias.cuda()).cpu().float()
+    ref = (x.float() @ w.float().t() + bias.float()).to(torch.bfloat16).float()
+    torch.testing.assert_close(y, ref, atol=2e-3, rtol=2 ** -7)
+    y2 = ops.linear(x.cuda(), w.cuda(), None).cpu().float()
+    ref2 = (x.float() @ w.float().t()).to(torch.bfloat16).float()
+    torch.testing.assert_close(y2, ref2, atol=2e-3, rtol=2 ** -7)
+
+
+def test_zero_k_gives_zeros():
+    a = torch.empty((5, 0), dtype=torch.int8, device="cuda")
+    b = torch.empty((0, 7), dtype=torch.int8, device="cuda")
+    c = ops.matmul_i8(a, b)
+    assert torch.equal(c.cpu(), torch.zeros(5, 7, dtype=torch.int32))
+
+
+def test_unaligned_pitch_is_rejected():
+    from xb200 import XbError
+
+    a = torch.zeros((8, 24), dtype=torch.int8, device="cuda")
+    b = torch.zeros((24, 8), dtype=torch.int8, device="cuda")
+    with pytest.raises(XbError) as e:
+        ops.matmul_i8(a, b)
+    assert "16 bytes" in e.value.message
+
+
+def _checksums_exact(a_dev, b_dev, c_dev):
+    af, bf, cf = a_dev.double(), b_dev.double(), c_dev.double()
+    row = cf.sum(1)
+    col = cf.sum(0)
+    assert torch.equal(row, af @ bf.sum(1))
+    assert torch.equal(col, af.sum(0) @ bf)
+
+
+@pytest.mark.parametrize("n", [4096, 8192])
+def test_full_size_i8_checksums(n):
+    g = torch.Generator(device="cuda").manual_seed(n)
+    a = torch.randint(-128, 128, (n, n), generator=g, device="cuda", dtype=torch.int8)
+    b = torch.randint(-128, 128, (n, n), generator=g, device="cuda", dtype=torch.int8)
+    c = ops.matmul_i8(a, b)
+    _checksums_exact(a, b, c)
+    # plus an exact spot check of 8 rows against the C oracle
+    rows = torch.randperm(n, generator=torch.Generator().manual_seed(1))[:8]
+    ref = cgemm.gemm_int(a[rows.cuda()].cpu(), b.cpu())
+    assert torch.equal(c[rows.cuda()].cpu(), ref)
+    _status_ok()
+    del a, b, c
+    torch.cuda.empty_cache()
+
+
+def test_full_size_i16_checksums_mod_2_32():
+    n = 4096
+    g = torch.Generator(device="cuda").manual_seed(7)
+    a = torch.randint(-2**15, 2**15, (n, n), generator=g, device="cuda", dtype=torch.int16)
+    b = torch.randint(-2**15, 2**15, (n, n), generator=g, device="cuda", dtype=torch.int16)
+    c = ops.matmul_i16(a, b)
+    rows = torch.randperm(n, generator=torch.Generator().manual_seed(2))[:4]
+    ref = cgemm.gemm_int(a[rows.cuda()].cpu(), b.cpu())
+    assert torch.equal(c[rows.cuda()].cpu(), ref)
+    _status_ok()

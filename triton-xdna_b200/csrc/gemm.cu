@@ -1,0 +1,598 @@
+// Dense GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+//   C[M,N] = A[M,K] @ B[K,N]          (int8 -> int32, bf16 -> f32 / bf16)
+//   C[M,N] = A[M,K] @ W[N,K]^T (+bias) (bf16 linear layer, W in nn.Linear layout)
+//   C[M,N] = A[M,K] @ B[K,N]          (int16 -> int32 via int8 limb products)
+//
+// Reference: examples/matmul_i8_m128_n64_k64/matmul_i8_m128_n64_k64.py:22-52
+// (`bare_matmul_i8`, i8 x i8 -> i32), examples/matmul_bf16_m64_n64_k64/
+// matmul_bf16_m64_n64_k64.py:16-46 and examples/autotune-matmul/matmul.py:22-53
+// (`bare_matmul`, bf16 x bf16 -> f32), examples/qwen2_5/kernels/matmul.py:172-296
+// (`triton_linear`, x @ W^T + b).  The reference's i8/i16 accumulator is i32
+// (amd_triton_npu/backend/matmul_transform.py:62-64).
+//
+// Kernel design (one persistent CTA per SM, 6 warps, warp-specialised):
+//   warp 0     TMA producer: one elected thread streams 128-byte-wide K slices
+//              of A and B into a STAGES-deep shared-memory ring (128B swizzle);
+//   warp 1     MMA issuer: allocates TMEM, one thread issues tcgen05.mma for
+//              each 32-byte K step and commits each stage back to the producer;
+//   warps 2-5  epilogue: tcgen05.ld the accumulator (each warp owns its 32 TMEM
+//              lanes = 32 rows), convert, store C with 16-byte stores.
+// Tiles are 128 x 256 with two TMEM accumulator buffers (512 columns), so the
+// epilogue of one tile overlaps the main loop of the next.  B in row-major
+// [K, N] is consumed as an MN-major operand straight from its TMA tile (no
+// transpose pass); W in [N, K] is K-major.  Out-of-range rows / columns / K
+// are zero-filled by TMA and masked in the epilogue.
+//
+// int16: A = 256*Ah + Al with Ah = A >> 8 (s8) and Al = A & 255 (u8), likewise
+// B.  A@B = 2^16 AhBh + 2^8 (AhBl + AlBh) + AlBl: four kind::i8 MMAs per K step
+// into three s32 accumulators (the two cross terms share one), combined in the
+// epilogue modulo 2^32 -- exactly the wrap-around of an int32 accumulator.
+// The limb planes are produced by a small split kernel into a workspace.
+//
+// Every mbarrier wait is bounded; a timeout sets a device status word
+// (read with xb_device_status) and the kernel drains its in-flight copies and
+// MMAs, frees TMEM and returns.
+#include "common.cuh"
+#include "tc.cuh"
+
+namespace xb {
+namespace gemm {
+
+using namespace tc;
+
+__device__ int g_gemm_status = 0;
+constexpr uint64_t kWaitLimit = 2000000000ull;  // 2 s per wait: far above any legitimate wait
+
+enum Kind { kBf16 = 0, kInt8 = 1, kInt16Limbs = 2 };
+enum Out { kOutF32 = 0, kOutBf16 = 1, kOutI32 = 2 };
+
+template <int KIND, bool B_KMAJOR>
+struct Cfg {
+  static constexpr int BM = 128;
+  static constexpr int BN = KIND == kInt16Limbs ? 128 : 256;
+  static constexpr int ESZ = KIND == kBf16 ? 2 : 1;  // operand element bytes
+  static constexpr int BK = 128 / ESZ;              // K elements per stage (128 bytes)
+  static constexpr int PLANES = KIND == kInt16Limbs ? 2 : 1;
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = PLANES * (A_BYTES + B_BYTES);
+  static constexpr int STAGES = KIND == kInt16Limbs ? 3 : 4;
+  static constexpr int UMMA_K = 32 / ESZ;  // 32 bytes of K per MMA
+  static constexpr int KSTEPS = BK / UMMA_K;
+  static constexpr int ACCS = KIND == kInt16Limbs ? 3 : 1;
+  static constexpr int ACC_BUFS = KIND == kInt16Limbs ? 1 : 2;
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int B_BOX_N = 128 / ESZ;  // N elements in one MN-major B box
+  static constexpr int B_BOXES = B_KMAJOR ? 1 : BN / B_BOX_N;
+  static constexpr int B_BOX_BYTES = B_KMAJOR ? B_BYTES : BK * 128;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static_assert(ACCS * ACC_BUFS * BN <= TMEM_COLS, "TMEM budget");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+struct alignas(64) Maps {
+  CUtensorMap a[2];  // A plane(s): [M, K] K-major
+  CUtensorMap b[2];  // B plane(s): [K, N] MN-major, or W [N, K] K-major
+};
+
+struct Args {
+  void* c;
+  const void* bias;  // bf16 [N] or nullptr (linear layer only)
+  int64_t ldc;
+  int m, n, k;
+  int tiles_m, tiles_n, num_tiles, kblocks;
+};
+
+constexpr int kGroupM = 16;  // tile raster: groups of 16 M-tiles sweep N (L2 reuse)
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int group = kGroupM * tiles_n;
+  const int g = t / group;
+  const int first_m = g * kGroupM;
+  const int gm = min(kGroupM, tiles_m - first_m);
+  const int r = t - g * group;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+template <int KIND, bool B_KMAJOR, int OUT>
+__global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Maps maps, const Args args) {
+  using C = Cfg<KIND, B_KMAJOR>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar[C::ACC_BUFS];
+  __shared__ __align__(8) uint64_t tempty_bar[C::ACC_BUFS];
+  __shared__ __align__(8) uint64_t drain_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_u32 - smem_u32(smem_raw));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < C::ACC_BUFS; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 128);
+    }
+    mbar_init(&drain_bar, 1);
+    abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    for (int p = 0; p < C::PLANES; ++p) {
+      prefetch_tmap(&maps.a[p]);
+      prefetch_tmap(&maps.b[p]);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  auto fail = [&]() {
+    atomicExch(&g_gemm_status, XB_ERR_TIMEOUT);
+    abort_flag = 1;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t it = 0;  // global k-block counter (ring position)
+      uint32_t issued[C::STAGES];  // loads issued per stage (for the exit drain)
+#pragma unroll
+      for (int s = 0; s < C::STAGES; ++s) issued[s] = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+        for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, kWaitLimit, &abort_flag)) { fail(); ok = false; break; }
+          mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+          uint8_t* st = smem + s * C::STAGE_BYTES;
+          for (int p = 0; p < C::PLANES; ++p) {
+            tma_load_2d(st + p * C::A_BYTES, &maps.a[p], &full_bar[s], kb * C::BK, tm * C::BM);
+            uint8_t* sb = st + C::PLANES * C::A_BYTES + p * C::B_BYTES;
+            if (B_KMAJOR) {
+              tma_load_2d(sb, &maps.b[p], &full_bar[s], kb * C::BK, tn * C::BN);
+            } else {
+#pragma unroll
+              for (int j = 0; j < C::B_BOXES; ++j)
+                tma_load_2d(sb + j * C::B_BOX_BYTES, &maps.b[p], &full_bar[s], tn * C::BN + j * C::B_BOX_N,
+                            kb * C::BK);
+            }
+          }
+          issued[s] = it / C::STAGES + 1;
+        }
+      }
+      // Drain: every load issued into a stage must have landed before exit.
+      for (int s = 0; s < C::STAGES; ++s)
+        if (issued[s] && !mbar_wait(&full_bar[s], (issued[s] - 1) & 1, kWaitLimit, &abort_flag)) fail();
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      bool any = false;
+      for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x, ++local) {
+        const int buf = local % C::ACC_BUFS;
+        const uint32_t tph = (local / C::ACC_BUFS) & 1;
+        if (!mbar_wait(&tempty_bar[buf], tph ^ 1, kWaitLimit, &abort_flag)) { fail(); break; }
+        tc_fence_after();
+        const uint32_t d0 = tmem_base + buf * C::ACCS * C::BN;
+        for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (!mbar_wait(&full_bar[s], ph, kWaitLimit, &abort_flag)) { fail(); ok = false; break; }
+          tc_fence_after();
+          const uint32_t st = base_u32 + s * C::STAGE_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < C::KSTEPS; ++ks) {
+            const uint32_t acc = (kb > 0 || ks > 0) ? 1u : 0u;
+            uint64_t ad[2], bd[2];
+#pragma unroll
+            for (int p = 0; p < C::PLANES; ++p) {
+              ad[p] = umma_desc_sw128(st + p * C::A_BYTES + ks * 32, 16, 1024);
+              const uint32_t sb = st + C::PLANES * C::A_BYTES + p * C::B_BYTES;
+              bd[p] = B_KMAJOR ? umma_desc_sw128(sb + ks * 32, 16, 1024)
+                               : umma_desc_sw128(sb + ks * C::UMMA_K * 128, C::B_BOX_BYTES, 1024);
+            }
+            constexpr uint32_t bmn = B_KMAJOR ? 0 : 1;
+            if constexpr (KIND == kBf16) {
+              mma_f16(d0, ad[0], bd[0], umma_idesc(1, 1, 1, 0, bmn, C::BM, C::BN), acc);
+            } else if constexpr (KIND == kInt8) {
+              mma_i8(d0, ad[0], bd[0], umma_idesc(2, 1, 1, 0, bmn, C::BM, C::BN), acc);
+            } else {
+              // planes: 0 = high limb (s8), 1 = low limb (u8)
+              mma_i8(d0, ad[0], bd[0], umma_idesc(2, 1, 1, 0, bmn, C::BM, C::BN), acc);               // hi*hi
+              mma_i8(d0 + C::BN, ad[0], bd[1], umma_idesc(2, 1, 0, 0, bmn, C::BM, C::BN), acc);       // hi*lo
+              mma_i8(d0 + C::BN, ad[1], bd[0], umma_idesc(2, 0, 1, 0, bmn, C::BM, C::BN), 1u);        // lo*hi
+              mma_i8(d0 + 2 * C::BN, ad[1], bd[1], umma_idesc(2, 0, 0, 0, bmn, C::BM, C::BN), acc);   // lo*lo
+            }
+            any = true;
+          }
+          tc_commit(&empty_bar[s]);  // frees the stage once these MMAs have read it
+        }
+        if (!ok) break;
+        tc_commit(&tfull_bar[buf]);  // accumulator ready for the epilogue
+      }
+      if (any) {
+        tc_commit(&drain_bar);
+        if (!mbar_wait(&drain_bar, 0, kWaitLimit, &abort_flag)) fail();
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x, ++local) {
+      const int buf = local % C::ACC_BUFS;
+      const uint32_t tph = (local / C::ACC_BUFS) & 1;
+      if (!mbar_wait(&tfull_bar[buf], tph, kWaitLimit, &abort_flag)) { fail(); break; }
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+      const int row = tm * C::BM + q * 32 + lane;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * C::ACCS * C::BN;
+#pragma unroll 1
+      for (int cc = 0; cc < C::BN / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tbase + cc * 32, v);
+        if constexpr (KIND == kInt16Limbs) {
+          uint32_t mid[32], lo[32];
+          tmem_ld_32x32b_x32(tbase + C::BN + cc * 32, mid);
+          tmem_ld_32x32b_x32(tbase + 2 * C::BN + cc * 32, lo);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = (v[j] << 16) + (mid[j] << 8) + lo[j];
+        } else {
+          tmem_ld_wait();
+        }
+        const int col0 = tn * C::BN + cc * 32;
+        if (row >= args.m || col0 >= args.n) continue;
+        if constexpr (OUT == kOutBf16) {
+          float f[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+          if (args.bias) {
+            const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(args.bias) + col0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.n) f[j] += __bfloat162float(bp[j]);
+          }
+          __nv_bfloat16* cp = static_cast<__nv_bfloat16*>(args.c) + (int64_t)row * args.ldc + col0;
+          if (col0 + 32 <= args.n && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              __nv_bfloat162 h[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(f[j + 2 * e], f[j + 2 * e + 1]);
+              *reinterpret_cast<int4*>(cp + j) = *reinterpret_cast<int4*>(h);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.n) cp[j] = __float2bfloat16_rn(f[j]);
+          }
+        } else {
+          uint32_t* cp = static_cast<uint32_t*>(args.c) + (int64_t)row * args.ldc + col0;
+          if (col0 + 32 <= args.n && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<uint4*>(cp + j) = make_uint4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.n) cp[j] = v[j];
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[buf]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// int16 -> (high s8, low u8) limb planes, each [rows, cols] with leading dim ldp.
+__global__ void split_i16_kernel(const int16_t* __restrict__ src, int64_t rows, int64_t cols, int64_t lds,
+                                 int8_t* __restrict__ hi, uint8_t* __restrict__ lo, int64_t ldp) {
+  const int64_t total = rows * cols;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cols, c = i - r * cols;
+    const int16_t v = src[r * lds + c];
+    hi[r * ldp + c] = (int8_t)(v >> 8);
+    lo[r * ldp + c] = (uint8_t)(v & 0xFF);
+  }
+}
+
+// ------------------------------------------------------------------------- host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder(char* err, size_t errlen) {
+  static EncodeTiledFn fn = nullptr;
+  if (fn) return fn;
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p) {
+    set_err(err, errlen, "cuTensorMapEncodeTiled unavailable: %s", cudaGetErrorString(e));
+    return nullptr;
+  }
+  fn = reinterpret_cast<EncodeTiledFn>(p);
+  return fn;
+}
+
+// 2-D tiled map over a row-major matrix [outer, inner] with 128-byte swizzle.
+int make_map(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int esz, uint64_t inner, uint64_t outer,
+             uint64_t ld_elems, uint32_t box_inner, uint32_t box_outer, char* err, size_t errlen) {
+  EncodeTiledFn enc = encoder(err, errlen);
+  if (!enc) return XB_ERR_CUDA;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * (uint64_t)esz};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_err(err, errlen, "cuTensorMapEncodeTiled failed (%d) for a %llux%llu operand", (int)r,
+            (unsigned long long)outer, (unsigned long long)inner);
+    return XB_ERR_CUDA;
+  }
+  return XB_OK;
+}
+
+bool tma_ok(const void* p, int64_t ld, int esz) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (ld * esz) % 16 == 0;
+}
+
+struct Operands {
+  const void* a[2];
+  const void* b[2];
+  int64_t lda, ldb;
+};
+
+template <int KIND, bool B_KMAJOR, int OUT>
+int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
+           cudaStream_t s, const char* what, char* err, size_t errlen) {
+  using Cf = Cfg<KIND, B_KMAJOR>;
+  const CUtensorMapDataType dt = KIND == kBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  Maps maps;
+  memset(&maps, 0, sizeof(maps));
+  for (int p = 0; p < Cf::PLANES; ++p) {
+    int rc = make_map(&maps.a[p], op.a[p], dt, Cf::ESZ, K, M, op.lda, Cf::BK, Cf::BM, err, errlen);
+    if (rc) return rc;
+    rc = B_KMAJOR ? make_map(&maps.b[p], op.b[p], dt, Cf::ESZ, K, N, op.ldb, Cf::BK, Cf::BN, err, errlen)
+                  : make_map(&maps.b[p], op.b[p], dt, Cf::ESZ, N, K, op.ldb, Cf::B_BOX_N, Cf::BK, err, errlen);
+    if (rc) return rc;
+  }
+  Args args;
+  args.c = c;
+  args.bias = bias;
+  args.ldc = ldc;
+  args.m = (int)M;
+  args.n = (int)N;
+  args.k = (int)K;
+  args.tiles_m = (int)((M + Cf::BM - 1) / Cf::BM);
+  args.tiles_n = (int)((N + Cf::BN - 1) / Cf::BN);
+  args.num_tiles = args.tiles_m * args.tiles_n;
+  args.kblocks = (int)((K + Cf::BK - 1) / Cf::BK);
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<KIND, B_KMAJOR, OUT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+    if (e != cudaSuccess) {
+      set_err(err, errlen, "%s: cudaFuncSetAttribute: %s", what, cudaGetErrorString(e));
+      return XB_ERR_CUDA;
+    }
+    attr_set = true;
+  }
+  int sms = 148;
+  sm_count(&sms);
+  const int grid = args.num_tiles < sms ? args.num_tiles : sms;
+  gemm_kernel<KIND, B_KMAJOR, OUT><<<grid, 192, Cf::SMEM, s>>>(maps, args);
+  return check_launch(what, err, errlen);
+}
+
+int check_common(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+                 int64_t ldc, bool b_kmajor, const char* what, char* err, size_t errlen) {
+  if (M < 0 || N < 0 || K < 0) { set_err(err, errlen, "%s: negative shape", what); return XB_ERR_INVALID; }
+  if (M > 0x7fffff00LL || N > 0x7fffff00LL || K > 0x7fffff00LL) {
+    set_err(err, errlen, "%s: dimension too large", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  if (M == 0 || N == 0) return 1;  // nothing to do
+  if (!C || (K > 0 && (!A || !B))) { set_err(err, errlen, "%s: null pointer", what); return XB_ERR_INVALID; }
+  if (lda < K || ldc < N || ldb < (b_kmajor ? K : N)) {
+    set_err(err, errlen, "%s: leading dimension smaller than the row (lda=%lld ldb=%lld ldc=%lld)", what,
+            (long long)lda, (long long)ldb, (long long)ldc);
+    return XB_ERR_INVALID;
+  }
+  return 0;
+}
+
+int zero_fill(void* C, int64_t M, int64_t N, int64_t ldc, int esz, cudaStream_t s, const char* what, char* err,
+              size_t errlen) {
+  cudaError_t e = cudaMemset2DAsync(C, ldc * esz, 0, N * esz, M, s);
+  if (e != cudaSuccess) { set_err(err, errlen, "%s: %s", what, cudaGetErrorString(e)); return XB_ERR_CUDA; }
+  return XB_OK;
+}
+
+size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Workspace layout for the int16 limb planes (each plane 256-byte aligned,
+// rows padded to a multiple of 16 bytes for TMA).
+struct LimbLayout {
+  int64_t lda_p, ldb_p;
+  size_t a_plane, b_plane, total;
+};
+LimbLayout limb_layout(int64_t M, int64_t N, int64_t K) {
+  LimbLayout L;
+  L.lda_p = (int64_t)round_up((size_t)(K > 0 ? K : 1), 16);
+  L.ldb_p = (int64_t)round_up((size_t)(N > 0 ? N : 1), 16);
+  L.a_plane = round_up((size_t)(M > 0 ? M : 1) * L.lda_p, 256);
+  L.b_plane = round_up((size_t)(K > 0 ? K : 1) * L.ldb_p, 256);
+  L.total = 2 * L.a_plane + 2 * L.b_plane;
+  return L;
+}
+
+int split_launch(const int16_t* src, int64_t rows, int64_t cols, int64_t lds, int8_t* hi, uint8_t* lo, int64_t ldp,
+                 cudaStream_t s) {
+  const int64_t total = rows * cols;
+  int64_t grid = (total + 255) / 256;
+  if (grid > 148 * 32) grid = 148 * 32;
+  if (grid < 1) grid = 1;
+  split_i16_kernel<<<(unsigned)grid, 256, 0, s>>>(src, rows, cols, lds, hi, lo, ldp);
+  return 0;
+}
+
+int run_i16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
+            int64_t ldc, void* ws, size_t ws_bytes, cudaStream_t s, const char* what, char* err, size_t errlen) {
+  int rc = check_common(A, B, C, M, N, K, lda, ldb, ldc, false, what, err, errlen);
+  if (rc) return rc < 0 ? rc : XB_OK;
+  if (K == 0) return zero_fill(C, M, N, ldc, 4, s, what, err, errlen);
+  const LimbLayout L = limb_layout(M, N, K);
+  if (!ws || ws_bytes < L.total) {
+    set_err(err, errlen, "%s: workspace of %zu bytes given, %zu needed", what, ws_bytes, L.total);
+    return XB_ERR_INVALID;
+  }
+  if ((reinterpret_cast<uintptr_t>(ws) & 255) != 0) {
+    set_err(err, errlen, "%s: workspace must be 256-byte aligned", what);
+    return XB_ERR_INVALID;
+  }
+  if ((reinterpret_cast<uintptr_t>(C) & 3) != 0) {
+    set_err(err, errlen, "%s: C must be 4-byte aligned", what);
+    return XB_ERR_INVALID;
+  }
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  int8_t* ahi = reinterpret_cast<int8_t*>(w);
+  uint8_t* alo = w + L.a_plane;
+  int8_t* bhi = reinterpret_cast<int8_t*>(w + 2 * L.a_plane);
+  uint8_t* blo = w + 2 * L.a_plane + L.b_plane;
+  split_launch(static_cast<const int16_t*>(A), M, K, lda, ahi, alo, L.lda_p, s);
+  split_launch(static_cast<const int16_t*>(B), K, N, ldb, bhi, blo, L.ldb_p, s);
+  rc = check_launch(what, err, errlen);
+  if (rc) return rc;
+  Operands op{{ahi, alo}, {bhi, blo}, L.lda_p, L.ldb_p};
+  return launch<kInt16Limbs, false, kOutI32>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
+}
+
+}  // namespace gemm
+}  // namespace xb
+
+using namespace xb::gemm;
+using xb::set_err;
+
+extern "C" int xb_matmul_i8(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                            int64_t ldb, int64_t ldc, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_matmul_i8";
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc = check_common(A, B, C, M, N, K, lda, ldb, ldc, false, what, err, errlen);
+  if (rc) return rc < 0 ? rc : XB_OK;
+  if (K == 0) return zero_fill(C, M, N, ldc, 4, s, what, err, errlen);
+  if (!tma_ok(A, lda, 1) || !tma_ok(B, ldb, 1)) {
+    set_err(err, errlen, "%s: A/B must be 16-byte aligned with row pitches a multiple of 16 bytes", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  Operands op{{A, nullptr}, {B, nullptr}, lda, ldb};
+  return launch<kInt8, false, kOutI32>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
+}
+
+extern "C" int xb_matmul_i16_workspace_size(int64_t M, int64_t N, int64_t K, size_t* bytes, char* err,
+                                            size_t errlen) {
+  if (!bytes || M < 0 || N < 0 || K < 0) {
+    set_err(err, errlen, "xb_matmul_i16_workspace_size: bad arguments");
+    return XB_ERR_INVALID;
+  }
+  *bytes = limb_layout(M, N, K).total;
+  return XB_OK;
+}
+
+extern "C" int xb_matmul_i16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                             int64_t ldb, int64_t ldc, void* workspace, size_t workspace_bytes, void* stream,
+                             char* err, size_t errlen) {
+  return run_i16(A, B, C, M, N, K, lda, ldb, ldc, workspace, workspace_bytes, (cudaStream_t)stream, "xb_matmul_i16",
+                 err, errlen);
+}
+
+extern "C" int xb_matmul_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
+                              int64_t ldb, int64_t ldc, int out_dtype, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_matmul_bf16";
+  cudaStream_t s = (cudaStream_t)stream;
+  if (out_dtype != XB_DT_F32 && out_dtype != XB_DT_BF16) {
+    set_err(err, errlen, "%s: out_dtype must be f32 or bf16", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  int rc = check_common(A, B, C, M, N, K, lda, ldb, ldc, false, what, err, errlen);
+  if (rc) return rc < 0 ? rc : XB_OK;
+  const int osz = out_dtype == XB_DT_F32 ? 4 : 2;
+  if (K == 0) return zero_fill(C, M, N, ldc, osz, s, what, err, errlen);
+  if (!tma_ok(A, lda, 2) || !tma_ok(B, ldb, 2)) {
+    set_err(err, errlen, "%s: A/B must be 16-byte aligned with row pitches a multiple of 16 bytes", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  Operands op{{A, nullptr}, {B, nullptr}, lda, ldb};
+  if (out_dtype == XB_DT_F32) return launch<kBf16, false, kOutF32>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
+  return launch<kBf16, false, kOutBf16>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
+}
+
+extern "C" int xb_linear_bf16(const void* X, const void* W, const void* bias, void* Y, int64_t M, int64_t N,
+                              int64_t K, int64_t ldx, int64_t ldw, int64_t ldy, void* stream, char* err,
+                              size_t errlen) {
+  const char* what = "xb_linear_bf16";
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc = check_common(X, W, Y, M, N, K, ldx, ldw, ldy, true, what, err, errlen);
+  if (rc) return rc < 0 ? rc : XB_OK;
+  if (K == 0) {
+    set_err(err, errlen, "%s: K must be positive", what);
+    return XB_ERR_INVALID;
+  }
+  if (!tma_ok(X, ldx, 2) || !tma_ok(W, ldw, 2)) {
+    set_err(err, errlen, "%s: X/W must be 16-byte aligned with row pitches a multiple of 16 bytes", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
+  return launch<kBf16, true, kOutBf16>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
+}
+
+extern "C" int xb_device_status(void* stream, int* status, char* err, size_t errlen) {
+  if (!status) {
+    set_err(err, errlen, "xb_device_status: null output");
+    return XB_ERR_INVALID;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(status, g_gemm_status, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(g_gemm_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    set_err(err, errlen, "xb_device_status: %s", cudaGetErrorString(e));
+    return XB_ERR_CUDA;
+  }
+  return XB_OK;
+}

@@ -201,9 +201,57 @@ rms_norm_kernel = XbKernel("rms_norm_kernel", "xb_rms_norm", _rms)
 weighted_rms_norm_kernel = XbKernel("weighted_rms_norm_kernel", "xb_rms_norm", _wrms)
 
 
+# ----------------------------------------------------------------------------- GEMMs
+
+
+def _mat_view(t, rows, cols, stride_r, stride_c, name):
+    if stride_c != 1:
+        raise ValueError(f"{name}: xb200 GEMMs need row-major operands (unit column stride)")
+    need = (rows - 1) * stride_r + cols if rows else 0
+    if t.numel() < need:
+        raise ValueError(f"{name}: tensor too small for [{rows}, {cols}] with row stride {stride_r}")
+    return torch.as_strided(t, (rows, cols), (stride_r, 1), t.storage_offset())
+
+
+def _matmul(A, B, C, M, N, K, stride_am, stride_ak, stride_bk, stride_bn, stride_cm, stride_cn, BLOCK_SIZE_M,
+            BLOCK_SIZE_N, BLOCK_SIZE_K, grid):
+    a = _mat_view(A, M, K, stride_am, stride_ak, "A")
+    b = _mat_view(B, K, N, stride_bk, stride_bn, "B")
+    c = _mat_view(C, M, N, stride_cm, stride_cn, "C")
+    if A.dtype == torch.int8:
+        ops.matmul_i8(a, b, out=c)
+    elif A.dtype == torch.int16:
+        ops.matmul_i16(a, b, out=c)
+    else:
+        ops.matmul_bf16(a, b, out=c)
+
+
+class _Autotuned(XbKernel):
+    """An autotuned reference kernel: block sizes the caller leaves out come
+    from its first config (examples/autotune-matmul/matmul.py:16-19), the way
+    Triton's autotuner fills META before calling the grid."""
+
+    def __init__(self, name, entry, run, defaults):
+        super().__init__(name, entry, run)
+        self.defaults = defaults
+
+    def _bind(self, args, kwargs):
+        kw = dict(self.defaults)
+        kw.update(kwargs)
+        for k in list(self.defaults):
+            if k in self.params[: len(args)]:
+                kw.pop(k)
+        return super()._bind(args, kw)
+
+
+bare_matmul_i8 = XbKernel("bare_matmul_i8", "xb_matmul_i8", _matmul)
+bare_matmul = XbKernel("bare_matmul", "xb_matmul_bf16", _matmul)
+bare_matmul_autotuned = _Autotuned("bare_matmul", "xb_matmul_bf16", _matmul, {"BLOCK_SIZE_M": 256})
+
+
 REGISTRY = {
     k.name: k
     for k in (vecadd, axpy_kernel, relu_kernel, leaky_relu_kernel, gelu_kernel, gelu_kernel_gpu, sigmoid_kernel,
-              silu_kernel, swiglu_kernel, avg_pool_kernel, avg_pool2d_kernel, softmax_kernel, _layer_norm_fwd_fused, rms_norm_kernel,
-              weighted_rms_norm_kernel)
+              silu_kernel, swiglu_kernel, avg_pool_kernel, avg_pool2d_kernel, softmax_kernel, _layer_norm_fwd_fused,
+              rms_norm_kernel, weighted_rms_norm_kernel, bare_matmul_i8, bare_matmul)
 }

@@ -246,3 +246,111 @@ def device_name(device: int = 0) -> tuple[str, int]:
     sms = ctypes.c_int(0)
     _lib.call("xb_device_name", device, buf, 256, ctypes.byref(sms))
     return buf.value.decode(), sms.value
+
+
+# --------------------------------------------------------------------------- GEMMs
+
+
+def _mat(t: torch.Tensor, name: str) -> int:
+    if t.dim() != 2:
+        raise ValueError(f"{name} must be 2-D")
+    if t.stride(1) != 1 and t.shape[1] > 1:
+        raise ValueError(f"{name} must be row-major (unit column stride)")
+    return t.stride(0) if t.shape[0] > 1 else max(t.shape[1], 1)
+
+
+def _gemm_out(a, b_cols, dtype, out):
+    M = a.shape[0]
+    if out is None:
+        return torch.empty((M, b_cols), dtype=dtype, device=a.device)
+    _cuda(out)
+    if tuple(out.shape) != (M, b_cols) or out.dtype != dtype:
+        raise ValueError(f"out must be {(M, b_cols)} {dtype}")
+    return out
+
+
+def matmul_i8(a, b, out=None):
+    """int32 C = A (int8 [M,K]) @ B (int8 [K,N]), exact
+    (examples/matmul_i8_m128_n64_k64/matmul_i8_m128_n64_k64.py:22-52)."""
+    _cuda(a, b, out)
+    if a.dtype != torch.int8 or b.dtype != torch.int8:
+        raise TypeError("matmul_i8 takes int8 operands")
+    if a.shape[1] != b.shape[0]:
+        raise ValueError(f"shape mismatch {tuple(a.shape)} @ {tuple(b.shape)}")
+    out = _gemm_out(a, b.shape[1], torch.int32, out)
+    M, K = a.shape
+    N = b.shape[1]
+    _lib.call("xb_matmul_i8", a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _mat(a, "A"), _mat(b, "B"),
+              _mat(out, "C"), _stream())
+    return out
+
+
+def matmul_i16(a, b, out=None, workspace=None):
+    """int32 C = A (int16) @ B (int16) with int32 wrap-around."""
+    _cuda(a, b, out)
+    if a.dtype != torch.int16 or b.dtype != torch.int16:
+        raise TypeError("matmul_i16 takes int16 operands")
+    if a.shape[1] != b.shape[0]:
+        raise ValueError(f"shape mismatch {tuple(a.shape)} @ {tuple(b.shape)}")
+    out = _gemm_out(a, b.shape[1], torch.int32, out)
+    M, K = a.shape
+    N = b.shape[1]
+    need = ctypes.c_size_t(0)
+    _lib.call("xb_matmul_i16_workspace_size", M, N, K, ctypes.byref(need))
+    if workspace is None or workspace.numel() * workspace.element_size() < need.value:
+        # torch's caching allocator returns 512-byte aligned blocks
+        workspace = torch.empty(need.value, dtype=torch.uint8, device=a.device)
+    _lib.call("xb_matmul_i16", a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _mat(a, "A"), _mat(b, "B"),
+              _mat(out, "C"), workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream())
+    return out
+
+
+def matmul_bf16(a, b, out_dtype=torch.float32, out=None):
+    """C = A (bf16 [M,K]) @ B (bf16 [K,N]), fp32 accumulation, C in f32 or bf16
+    (examples/matmul_bf16_m64_n64_k64/matmul_bf16_m64_n64_k64.py:16-46)."""
+    _cuda(a, b, out)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise TypeError("matmul_bf16 takes bf16 operands")
+    if a.shape[1] != b.shape[0]:
+        raise ValueError(f"shape mismatch {tuple(a.shape)} @ {tuple(b.shape)}")
+    if out is not None:
+        out_dtype = out.dtype
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("out dtype must be float32 or bfloat16")
+    out = _gemm_out(a, b.shape[1], out_dtype, out)
+    M, K = a.shape
+    N = b.shape[1]
+    _lib.call("xb_matmul_bf16", a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _mat(a, "A"), _mat(b, "B"),
+              _mat(out, "C"), DT[out_dtype], _stream())
+    return out
+
+
+def linear(x, weight, bias=None, out=None):
+    """y = x @ weight^T + bias, weight [N, K] (nn.Linear layout), bf16
+    (examples/qwen2_5/kernels/matmul.py:172-296)."""
+    _cuda(x, weight, bias, out)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("linear takes bf16 x and weight")
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != weight.shape[0]
+                             or not bias.is_contiguous()):
+        raise ValueError("bias must be a contiguous bf16 vector of N elements")
+    K = x.shape[-1]
+    N = weight.shape[0]
+    if weight.shape[1] != K:
+        raise ValueError(f"shape mismatch x[..., {K}] vs weight {tuple(weight.shape)}")
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    if out is None:
+        y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    else:
+        y = out.reshape(M, N)
+    _lib.call("xb_linear_bf16", x2.data_ptr(), weight.data_ptr(), bias.data_ptr() if bias is not None else None,
+              y.data_ptr(), M, N, K, _mat(x2, "x"), _mat(weight, "weight"), _mat(y, "y"), _stream())
+    return y.reshape(*x.shape[:-1], N) if out is None else out
+
+
+def device_status() -> int:
+    """Read and clear the device status word (0 = fine, -4 = a kernel timed out)."""
+    st = ctypes.c_int(0)
+    _lib.call("xb_device_status", _stream(), ctypes.byref(st))
+    return st.value
