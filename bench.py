@@ -64,9 +64,10 @@ def _tag(dt):
 
 
 class Op:
-    def __init__(self, name, nbytes, run, e2e=None, h2d=0, d2h=0):
+    def __init__(self, name, nbytes, run, e2e=None, h2d=0, d2h=0, flops=0, peak_key=None):
         self.name, self.nbytes, self.run, self.e2e = name, nbytes, run, e2e
         self.h2d, self.d2h = h2d, d2h
+        self.flops, self.peak_key = flops, peak_key
 
 
 def elementwise_workload(dev, n: int, seed: int, host: bool):
@@ -160,7 +161,122 @@ def rowreduce_workload(dev, n: int, seed: int, host: bool):
     return out, config, "row-reduction suite algorithmic HBM throughput", "bf16+f32"
 
 
-WORKLOADS = {"elementwise": elementwise_workload, "rowreduce": rowreduce_workload}
+GEMM_SIZES = [(256, 256, 256), (1024, 1024, 1024), (4096, 4096, 4096), (8192, 8192, 8192), (16384, 16384, 16384),
+              (16, 8192, 8192)]
+
+
+def gemm_workload(dev, n: int, seed: int, host: bool):
+    """The GEMM sweep: int8 (int32 out), int16 (int32 out, wrap-around) and
+    bf16 (fp32 accumulate, bf16 out) at M=N=K in {256 .. 16384} and the
+    M=16 x 8192 x 8192 decode shape.  Operands are allocated per op and
+    freed after timing to bound device memory."""
+    from xb200 import ops as X
+
+    g = torch.Generator(device=dev).manual_seed(seed)
+    sizes = [s for s in GEMM_SIZES if max(s) <= max(n, 256)] if n != N28 else GEMM_SIZES
+    out = []
+    for dt in ("i8", "i16", "bf16"):
+        for (M, N, K) in sizes:
+            def make(M=M, N=N, K=K, dt=dt):
+                if dt == "i8":
+                    a = torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+                    b = torch.randint(-128, 128, (K, N), generator=g, device=dev, dtype=torch.int8)
+                    c = torch.empty((M, N), dtype=torch.int32, device=dev)
+                    return lambda: X.matmul_i8(a, b, out=c), (a, b, c)
+                if dt == "i16":
+                    a = torch.randint(-2**15, 2**15, (M, K), generator=g, device=dev, dtype=torch.int16)
+                    b = torch.randint(-2**15, 2**15, (K, N), generator=g, device=dev, dtype=torch.int16)
+                    c = torch.empty((M, N), dtype=torch.int32, device=dev)
+                    ws = torch.empty(2 * (M * K + K * N) + 4096, dtype=torch.uint8, device=dev)
+                    return lambda: X.matmul_i16(a, b, out=c, workspace=ws), (a, b, c, ws)
+                a = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+                b = torch.randn((K, N), generator=g, device=dev).to(torch.bfloat16)
+                c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
+                return lambda: X.matmul_bf16(a, b, torch.bfloat16, out=c), (a, b, c)
+
+            eb = {"i8": 1, "i16": 2, "bf16": 2}[dt]
+            ob = 2 if dt == "bf16" else 4
+            op = Op(f"gemm_{dt}_{M}x{N}x{K}", (M * K + K * N) * eb + M * N * ob, None, flops=2 * M * N * K,
+                    peak_key="bf16_tflops" if dt == "bf16" else "i8_tops")
+            op.make = make
+            out.append(op)
+    config = {"workload": "GEMM sweep M=N=K in {256,1024,4096,8192,16384} + 16x8192x8192, int8 / int16 / bf16",
+              "l2": "L2 flushed (256 MB write) before every timed launch"}
+    return out, config, "GEMM TOPS", "i8/i16/bf16"
+
+
+WORKLOADS = {"elementwise": elementwise_workload, "rowreduce": rowreduce_workload, "gemm": gemm_workload}
+
+
+def run_gemm_bench(args, ops_list, config, world, rank, local, dev):
+    """Per-GEMM timing: L2 flush, then CUDA events around each launch; the
+    cuBLAS bf16 / int8 GEMMs are timed the same way as reference lines."""
+    peaks = _peaks()
+    peaks["i8_tops"] = 4500.0  # nominal dense int8 (no measured value in MEASURED_PEAKS.json)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    res = {}
+    if args.only:
+        ops_list = [o for o in ops_list if args.only in o.name]
+    with ClockSampler(local) as clk:
+        for op in ops_list:
+            fn, keep = op.make()
+            for _ in range(max(3, args.warmup)):
+                fn()
+            times = []
+            for _ in range(max(3, args.steps // 3)):
+                flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                fn()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1))
+            ms = statistics.median(times)
+            tops = op.flops / (ms * 1e-3) / 1e12
+            res[op.name] = {"ms": round(ms, 4), "tops": round(tops, 1),
+                            "frac": round(tops / peaks[op.peak_key], 3), "peak_key": op.peak_key}
+            del fn, keep
+            torch.cuda.empty_cache()
+        # cuBLAS reference lines (library GEMMs, not the product)
+        ref = {}
+        for n in (() if args.no_library else (4096, 8192, 16384)):
+            a = torch.randn((n, n), device=dev).to(torch.bfloat16)
+            b = torch.randn((n, n), device=dev).to(torch.bfloat16)
+            ref[f"torch.matmul_bf16_{n}"] = a @ b
+            ai = torch.randint(-128, 128, (n, n), device=dev, dtype=torch.int8)
+            bi = torch.randint(-128, 128, (n, n), device=dev, dtype=torch.int8)
+            for name, fn, fl in ((f"cublas_bf16_{n}", lambda: a @ b, 2 * n ** 3),
+                                 (f"cublas_int8_{n}", lambda: torch._int_mm(ai, bi), 2 * n ** 3)):
+                for _ in range(3):
+                    fn()
+                times = []
+                for _ in range(5):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    fn()
+                    e1.record(stream)
+                    torch.cuda.synchronize()
+                    times.append(e0.elapsed_time(e1))
+                ms = statistics.median(times)
+                res[name] = {"ms": round(ms, 4), "tops": round(fl / (ms * 1e-3) / 1e12, 1), "library": True}
+            del a, b, ai, bi
+            ref.clear()
+            torch.cuda.empty_cache()
+    clocks = clk.summary()
+    big = "gemm_bf16_8192x8192x8192"
+    line = {
+        "metric": "GEMM TOPS", "value": res[big]["tops"] if big in res else None, "unit": "TOPS", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "i8/i16/bf16", "data": "synthetic, seed 0", "config": config,
+        "roofline": {"bound": "tensor", "kernel": big, "achieved": res.get(big, {}).get("tops"),
+                     "peak": peaks["bf16_tflops"], "peak_source": peaks["source"], "unit": "TFLOP/s",
+                     "frac": res.get(big, {}).get("frac"), "traffic": None},
+        "ops": res, "clocks": clocks, "gpu_launches": None,
+    }
+    if rank == 0:
+        print(json.dumps(line))
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -344,6 +460,8 @@ def main():
     ap.add_argument("--workload", default="elementwise", choices=sorted(WORKLOADS))
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", default=None, help="gemm workload: run only ops whose name contains this string")
+    ap.add_argument("--no-library", action="store_true", help="gemm workload: skip the cuBLAS reference lines")
     ap.add_argument("--elements", type=int, default=N28,
                     help="flat tensor length (default 2^28, the workload); smaller values are for profiling only")
     args = ap.parse_args()
@@ -379,6 +497,13 @@ def main():
     dev = torch.device("cuda", torch.cuda.current_device())
     want_e2e = rank == 0 and args.e2e_steps > 0 and args.workload == "elementwise"
     ops_list, config, metric, dtype = WORKLOADS[args.workload](dev, args.elements, rank, want_e2e)
+    if args.workload == "gemm":
+        run_gemm_bench(args, ops_list, config, world, rank, local, dev)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
     config["launches_per_step"] = len(ops_list)
     config["parallelism"] = f"weak x{world} (independent replicas, no collective)"
     step_bytes = sum(o.nbytes for o in ops_list)
