@@ -174,6 +174,24 @@ XB_API int xb_matmul_i16(const void* A, const void* B, void* C, int64_t M,
                          int64_t ldc, void* workspace, size_t workspace_bytes,
                          void* stream, char* err, size_t errlen);
 
+/* Size of the scratch array built into the library for xb_matmul_i16_noalloc
+ * (held on every GPU that loads the library until the process exits). */
+#define XB_I16_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
+
+/* xb_matmul_i16 for callers that cannot allocate device memory (a stream
+ * being captured into a CUDA graph, a host framework that owns every device
+ * allocation, a path where an allocation could stall).  No counterpart in the
+ * reference.  The int8 limb planes go to a fixed XB_I16_NOALLOC_SCRATCH_BYTES
+ * array inside the library instead of a caller workspace; a product needing
+ * more than that (xb_matmul_i16_workspace_size) is rejected with
+ * XB_ERR_UNSUPPORTED.  Nothing is allocated.  The first call on a device looks
+ * up the array's device address, so make it before any stream capture.  All
+ * calls share the array: calls whose GPU work overlaps race. */
+XB_API int xb_matmul_i16_noalloc(const void* A, const void* B, void* C,
+                                 int64_t M, int64_t N, int64_t K, int64_t lda,
+                                 int64_t ldb, int64_t ldc, void* stream,
+                                 char* err, size_t errlen);
+
 /* C[M,N] = A[M,K] (bf16) @ B[K,N] (bf16), fp32 accumulation, C in f32 or bf16
  * (out_dtype XB_DT_F32 / XB_DT_BF16).  Replaces `bare_matmul`
  * (examples/matmul_bf16_m64_n64_k64/matmul_bf16_m64_n64_k64.py:16-46,

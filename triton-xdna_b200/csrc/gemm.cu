@@ -36,6 +36,8 @@
 #include "common.cuh"
 #include "tc.cuh"
 
+#include <mutex>
+
 namespace xb {
 namespace gemm {
 
@@ -537,6 +539,73 @@ extern "C" int xb_matmul_i16(const void* A, const void* B, void* C, int64_t M, i
                              char* err, size_t errlen) {
   return run_i16(A, B, C, M, N, K, lda, ldb, ldc, workspace, workspace_bytes, (cudaStream_t)stream, "xb_matmul_i16",
                  err, errlen);
+}
+
+// ---------------------------------------------------------------------------
+// int16 GEMM for callers that cannot allocate device memory.
+//
+// Some callers cannot call cudaMalloc at all: code running while a CUDA graph
+// is being captured, plugins whose host framework owns every device
+// allocation through its own pool, or real-time paths where an allocation
+// could stall.  xb_matmul_i16 needs a caller-provided workspace for its int8
+// limb planes; this variant instead keeps them in a fixed-size array compiled
+// into the library (XB_I16_NOALLOC_SCRATCH_BYTES per GPU, resident on every
+// GPU that loads this module until the process exits).  The caller still
+// passes A, B and C.
+//
+// In host code the array's name is only a host-side stand-in, so its device
+// address is looked up once per device with cudaGetSymbolAddress, with that
+// device current, on the first call made on it.  That first call must
+// therefore come before any stream capture on the device.  All calls share the
+// one array: calls whose GPU work overlaps (two streams, or two host threads)
+// race on it.  The split kernel rewrites every limb byte the GEMM reads before
+// it reads them, so nothing has to start at zero, and stale contents from an
+// earlier call are never used.
+static __device__ __align__(256) uint8_t g_i16_noalloc_scratch[XB_I16_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+}  // namespace
+
+extern "C" int xb_matmul_i16_noalloc(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                                     int64_t lda, int64_t ldb, int64_t ldc, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_matmul_i16_noalloc";
+  if (M < 0 || N < 0 || K < 0) {
+    set_err(err, errlen, "%s: negative shape", what);
+    return XB_ERR_INVALID;
+  }
+  const size_t need = limb_layout(M, N, K).total;
+  if (need > (size_t)XB_I16_NOALLOC_SCRATCH_BYTES) {
+    set_err(err, errlen,
+            "%s: an %lldx%lldx%lld product needs %zu bytes of limb scratch, more than the built-in %zu bytes; "
+            "use xb_matmul_i16 with a workspace",
+            what, (long long)M, (long long)N, (long long)K, need, (size_t)XB_I16_NOALLOC_SCRATCH_BYTES);
+    return XB_ERR_UNSUPPORTED;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    set_err(err, errlen, "%s: no usable current device (%s)", what, cudaGetErrorString(e));
+    return XB_ERR_CUDA;
+  }
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_i16_noalloc_scratch);
+      if (e != cudaSuccess || !p) {
+        set_err(err, errlen, "%s: cudaGetSymbolAddress of the scratch array failed on device %d: %s", what, dev,
+                cudaGetErrorString(e));
+        return XB_ERR_CUDA;
+      }
+      g_noalloc_ptr[dev] = p;
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  return run_i16(A, B, C, M, N, K, lda, ldb, ldc, scratch, (size_t)XB_I16_NOALLOC_SCRATCH_BYTES,
+                 (cudaStream_t)stream, what, err, errlen);
 }
 
 extern "C" int xb_matmul_bf16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
