@@ -78,6 +78,20 @@ template <> struct Cvt<__nv_bfloat16> {
 template <typename T>
 __device__ __forceinline__ float round_to(float v) { return Cvt<T>::to_f(Cvt<T>::from_f(v)); }
 
+// Hardware approximations (one MUFU instruction each, relative error about
+// 2^-22, subnormal results flushed to zero).  Used only where the result is
+// stored as bf16, whose ulp (2^-8 relative) dwarfs that error.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
 // 16-byte vector of T.
 template <typename T> struct Vec16 {
   static constexpr int N = 16 / sizeof(T);

@@ -42,16 +42,6 @@ constexpr int kUnroll = 2;
 // that the bf16 activations stay HBM-bound instead of issue-bound.  Both
 // approximations flush subnormals, so a bf16 result below 2^-126 in
 // magnitude (sigmoid(x) for x < -87.3) becomes 0.
-__device__ __forceinline__ float ex2_approx(float x) {
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
-__device__ __forceinline__ float rcp_approx(float x) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
-}
 template <typename T>
 __device__ __forceinline__ float sigmoid_t(float x) {
   if constexpr (sizeof(T) == 2) return rcp_approx(1.0f + ex2_approx(x * -1.4426950408889634f));

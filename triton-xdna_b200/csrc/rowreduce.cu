@@ -35,6 +35,14 @@ struct RowArgs {
   float eps;
 };
 
+// exp(x - m): for bf16 rows the hardware exp2 (FFMA + one MUFU) keeps the
+// kernel HBM-bound; fp32 rows use expf.
+template <typename T>
+__device__ __forceinline__ float exp_shifted(float x, float m) {
+  if constexpr (sizeof(T) == 2) return ex2_approx((x - m) * 1.4426950408889634f);
+  else return expf(x - m);
+}
+
 template <int GROUP, bool MAX>
 __device__ __forceinline__ float group_reduce(float v, float* red) {
   constexpr int W = GROUP < 32 ? GROUP : 32;
@@ -100,7 +108,7 @@ __global__ void __launch_bounds__(GROUP > 32 ? GROUP : 256) row_vec_kernel(RowAr
       if ((int64_t)k * GROUP + t < nvec)
 #pragma unroll
         for (int e = 0; e < VN; ++e) {
-          v[k][e] = expf(v[k][e] - m);
+          v[k][e] = exp_shifted<T>(v[k][e], m);
           s += v[k][e];
         }
     s = group_reduce<GROUP, false>(s, red);
