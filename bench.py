@@ -51,6 +51,14 @@ def _peaks() -> dict:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
+# DRAM traffic per launch / algorithmic bytes, from one ncu capture of the
+# kernel on a smaller case of the same workload (traffic scales with the
+# units processed); see the named summary under profiles/.
+MEASURED_TRAFFIC_RATIO = {
+    "avg_pool2d_2x2_f32": (1000.5 / 1027.6, "profiles/avg_pool2d_f32_16x256x224x224.md"),
+}
+
+
 def _tag(dt):
     return "bf16" if dt == torch.bfloat16 else "f32"
 
@@ -205,7 +213,114 @@ def gemm_workload(dev, n: int, seed: int, host: bool):
     return out, config, "GEMM TOPS", "i8/i16/bf16"
 
 
-WORKLOADS = {"elementwise": elementwise_workload, "rowreduce": rowreduce_workload, "gemm": gemm_workload}
+def qwen_workload(dev, n: int, seed: int, host: bool):
+    return [], {"workload": "Qwen2.5-0.5B architecture, random-init bf16 weights (seed 0): batch 64 x 512-token "
+                            "random-id prefill + 128 greedy decode steps, batch-sharded over ranks"}, \
+        "LLM tokens/s", "bf16"
+
+
+WORKLOADS = {"elementwise": elementwise_workload, "rowreduce": rowreduce_workload, "gemm": gemm_workload,
+             "qwen": qwen_workload}
+
+
+def qwen_flops_bytes(cfg, B, S, ctx_end):
+    """Algorithmic work of the Qwen forward: prefill FLOPs (linears over all
+    tokens + causal attention + last-position LM head) and decode bytes per
+    step (every weight once + the KV cache read)."""
+    D, H, KVH, HD, I, V = cfg.n_embd, cfg.n_head, cfg.n_kv_head, cfg.head_dim, cfg.intermediate, cfg.vocab_size
+    per_tok = 2 * (D * (H + 2 * KVH) * HD + H * HD * D + 3 * D * I) * cfg.n_layer
+    attn = 2 * 2 * B * H * HD * (S * (S + 1) // 2) * cfg.n_layer
+    prefill = per_tok * B * S + attn + 2 * B * D * V
+    weights = (per_tok // 2 + D * V) * 2  # bf16 bytes of every weight (LM head tied to the embedding)
+    kv_mean = 2 * cfg.n_layer * B * KVH * HD * 2 * ((S + ctx_end) / 2)
+    return prefill, weights + kv_mean
+
+
+def run_qwen_bench(args, world, rank, local, dev):
+    from xb200.qwen import Qwen2Model, QwenConfig, random_weights
+
+    cfg = QwenConfig()
+    B_total, S, new = 64, 512, 128
+    if B_total % world:
+        raise SystemExit(f"batch {B_total} does not split over {world} ranks")
+    B = B_total // world
+    sd = random_weights(cfg, seed=0)
+    model = Qwen2Model(sd, cfg, device=dev, rope_len=1024)
+    del sd
+    g = torch.Generator().manual_seed(1000 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=g).to(dev)
+    cache = model.new_cache(B, S + new)
+
+    def step():
+        cache.length = 0
+        return model.generate(ids, new, cache)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    peaks = _peaks()
+    pre, dec = [], []
+    _barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            _, t = step()
+            pre.append(t["prefill_ms"])
+            dec.append(t["decode_ms"])
+    _barrier(world)
+    pre_ms = _max_over_ranks(statistics.mean(pre), world)
+    dec_ms = _max_over_ranks(statistics.mean(dec), world)
+    flops, dec_bytes = qwen_flops_bytes(cfg, B, S, S + new)
+    prefill_tps = B_total * S / (pre_ms * 1e-3)
+    decode_tps = B_total * (new - 1) / (dec_ms * 1e-3)
+    total_tps = B_total * (S + new) / ((pre_ms + dec_ms) * 1e-3)
+    tflops = flops / (pre_ms * 1e-3) / 1e12
+    dec_gbs = dec_bytes * (new - 1) / (dec_ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = qwen_cpu_baseline(cfg)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "LLM tokens/s (prefill + decode)", "value": round(total_tps, 1), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(pre_ms + dec_ms, 2), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic random ids, random-init weights (seed 0)",
+            "config": {"workload": "Qwen2.5-0.5B architecture (24 layers, hidden 896, 14/2 heads, MLP 4864, "
+                                   "vocab 151936): batch 64 x 512 prefill + 128 greedy decode",
+                       "global_batch": B_total, "seq_len": S, "new_tokens": new,
+                       "parallelism": f"batch-sharded x{world} (replicated weights, no collective)"},
+            "prefill_tokens_per_s": round(prefill_tps, 1), "decode_tokens_per_s": round(decode_tps, 1),
+            "prefill_ms": round(pre_ms, 2), "decode_ms": round(dec_ms, 2),
+            "roofline": {"bound": "tensor (prefill) / hbm (decode)",
+                         "prefill": {"achieved": round(tflops, 1), "unit": "TFLOP/s", "peak": peaks["bf16_tflops"],
+                                     "frac": round(tflops / peaks["bf16_tflops"], 4)},
+                         "decode": {"achieved": round(dec_gbs, 1), "unit": "GB/s", "peak": peaks["hbm_gbs"],
+                                    "frac": round(dec_gbs / peaks["hbm_gbs"], 4)},
+                         "peak_source": peaks["source"]},
+            "cpu_baseline": cpu, "clocks": clk.summary(),
+        }))
+
+
+def qwen_cpu_baseline(cfg):
+    """The oracle forward on the host cores: one 128-token prefill + 4 decode
+    steps of one sequence (a bounded sample of the workload)."""
+    from oracle.qwen import OracleQwen
+    from xb200.qwen import random_weights
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    sd = random_weights(cfg, seed=0)
+    orc = OracleQwen(sd, cfg)
+    ids = torch.randint(0, cfg.vocab_size, (1, 128), generator=torch.Generator().manual_seed(5))
+    cache = orc.new_cache(1, 132)
+    t0 = time.perf_counter()
+    logits = orc.forward(ids, cache)
+    tok = logits[:, -1].argmax(-1)
+    for _ in range(4):
+        logits = orc.forward(tok.view(1, 1), cache)
+        tok = logits[:, -1].argmax(-1)
+    secs = time.perf_counter() - t0
+    return {"value": round(132 / secs, 2), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": "1 sequence: 128-token prefill + 4 greedy decode steps through the oracle forward"}
 
 
 def run_gemm_bench(args, ops_list, config, world, rank, local, dev):
@@ -496,6 +611,13 @@ def main():
     _lib.load()
     dev = torch.device("cuda", torch.cuda.current_device())
     want_e2e = rank == 0 and args.e2e_steps > 0 and args.workload == "elementwise"
+    if args.workload == "qwen":
+        run_qwen_bench(args, world, rank, local, dev)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
     ops_list, config, metric, dtype = WORKLOADS[args.workload](dev, args.elements, rank, want_e2e)
     if args.workload == "gemm":
         run_gemm_bench(args, ops_list, config, world, rank, local, dev)
@@ -573,7 +695,10 @@ def main():
             "vs_baseline": None, "dtype": dtype, "data": "synthetic N(0,1), seed = rank", "config": config,
             "roofline": {"bound": "hbm", "kernel": dom.name, "achieved": round(dom_gbs, 1), "peak": hbm,
                          "peak_source": peaks["source"], "unit": "GB/s", "frac": round(dom_gbs / hbm, 4),
-                         "traffic": None},
+                         "traffic": (round(MEASURED_TRAFFIC_RATIO[dom.name][0] * dom.nbytes)
+                                     if dom.name in MEASURED_TRAFFIC_RATIO else None),
+                         "traffic_source": MEASURED_TRAFFIC_RATIO.get(dom.name, (None, None))[1],
+                         "algorithmic_bytes": dom.nbytes},
             "ops": detail, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
             "gpu_launches": len(ops_list) * args.steps,
         }))

@@ -104,6 +104,12 @@ XB_API int xb_silu(const void* x, void* y, int64_t n, int dtype, void* stream,
 XB_API int xb_swiglu(const void* gate, const void* up, void* out, int64_t n,
               int dtype, void* stream, char* err, size_t errlen);
 
+/* out = silu(gate) * up evaluated in fp32 with one rounding (the Qwen2.5
+ * MLP form).  Replaces `swiglu_kernel_gpu` (examples/qwen2_5/kernels/
+ * swiglu.py:29-50). */
+XB_API int xb_silu_mul(const void* gate, const void* up, void* out, int64_t n,
+                       int dtype, void* stream, char* err, size_t errlen);
+
 /* ---------------------------------------------------------------------------
  * Row reductions over a [rows, cols] matrix with row strides (elements) and
  * unit column stride.  fp32 accumulation.
@@ -201,13 +207,58 @@ XB_API int xb_matmul_bf16(const void* A, const void* B, void* C, int64_t M,
                           int64_t ldc, int out_dtype, void* stream, char* err,
                           size_t errlen);
 
-/* Y[M,N] (bf16) = X[M,K] @ W[N,K]^T (+ bias[N]), W in nn.Linear layout, fp32
- * accumulation; bias may be NULL.  Replaces `triton_linear`
- * (examples/qwen2_5/kernels/matmul.py:172-296). */
+/* Y[M,N] = X[M,K] (bf16) @ W[N,K]^T (bf16) (+ bias[N], bf16), W in
+ * nn.Linear layout, fp32 accumulation, Y in bf16 or f32 (out_dtype); bias
+ * may be NULL.  Replaces `triton_linear` (examples/qwen2_5/kernels/matmul.py:
+ * 172-296) and the fp32 LM head of examples/qwen2_5/model.py:1097-1106. */
 XB_API int xb_linear_bf16(const void* X, const void* W, const void* bias,
                           void* Y, int64_t M, int64_t N, int64_t K,
-                          int64_t ldx, int64_t ldw, int64_t ldy, void* stream,
-                          char* err, size_t errlen);
+                          int64_t ldx, int64_t ldw, int64_t ldy, int out_dtype,
+                          void* stream, char* err, size_t errlen);
+
+/* ---------------------------------------------------------------------------
+ * Qwen2.5 decoder pieces (examples/qwen2_5/model.py:824-1179).
+ * ------------------------------------------------------------------------- */
+
+/* out[m, :] = table[ids[m], :] (bf16 rows of `dim`, dim % 8 == 0).  Ids
+ * outside [0, vocab) produce zero rows.  Replaces model.py:911
+ * (`self.embed_tokens[input_ids]`). */
+XB_API int xb_embedding_bf16(const void* table, const int64_t* ids, void* out,
+                             int64_t rows, int64_t dim, int64_t vocab,
+                             void* stream, char* err, size_t errlen);
+
+/* Rotary embedding of the fused QKV projection plus the KV-cache write.
+ * qkv: [batch*seq, (n_head + 2*n_kv_head)*head_dim]; cos/sin: fp32 tables of
+ * at least pos_offset+seq rows of head_dim (rope.py:20-35); q_out:
+ * [batch, n_head, seq, head_dim]; k_cache / v_cache: [batch, n_kv_head,
+ * max_seq, head_dim], rows pos_offset .. pos_offset+seq-1 written.
+ * Replaces model.py:851-867 and kernels/rope.py:44-67. */
+XB_API int xb_rope_kv_bf16(const void* qkv, const float* cos_t,
+                           const float* sin_t, void* q_out, void* k_cache,
+                           void* v_cache, int64_t batch, int64_t seq,
+                           int64_t n_head, int64_t n_kv_head, int64_t head_dim,
+                           int64_t max_seq, int64_t pos_offset, void* stream,
+                           char* err, size_t errlen);
+
+/* Causal GQA attention over the KV cache: query row s (position
+ * pos_offset+s) attends keys 0 .. pos_offset+s.  q: [batch, n_head, seq,
+ * head_dim]; out: [batch, seq, n_head*head_dim]; head_dim 64.  Online
+ * softmax in fp32, P rounded to bf16 before P@V.  Replaces
+ * `fused_attention_kernel` (examples/qwen2_5/kernels/attention.py:27-122)
+ * and the GQA expansion of model.py:868-889 (done natively here). */
+XB_API int xb_attention_bf16(const void* q, const void* k_cache,
+                             const void* v_cache, void* out, int64_t batch,
+                             int64_t seq, int64_t n_head, int64_t n_kv_head,
+                             int64_t head_dim, int64_t max_seq,
+                             int64_t pos_offset, float scale, void* stream,
+                             char* err, size_t errlen);
+
+/* idx[r] = first index of the maximum of x[r, 0:cols] (row pitch ld);
+ * NaN counts as the maximum.  Replaces `torch.argmax(logits[..., -1, :])`
+ * of model.py:1155, 1171. */
+XB_API int xb_argmax_f32(const float* x, int64_t rows, int64_t cols,
+                         int64_t ld, int64_t* idx, void* stream, char* err,
+                         size_t errlen);
 
 /* Read (synchronising `stream`) and clear the device status word that the
  * tensor-core kernels set when a bounded wait runs out: 0 = fine,

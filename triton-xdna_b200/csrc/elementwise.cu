@@ -103,6 +103,13 @@ template <typename T> struct OpSwiglu {
   }
 };
 
+// silu(g) * u in fp32 with a single rounding: the Qwen2.5 MLP form
+// (examples/qwen2_5/kernels/swiglu.py:29-50, model.py:781-786), unlike the
+// swiglu example, which rounds silu(g) to the storage type first.
+template <typename T> struct OpSiluMul {
+  __device__ __forceinline__ float operator()(float g, float u) const { return __fmul_rn(OpSilu<T>{}(g), u); }
+};
+
 template <typename T, typename Op>
 __global__ void __launch_bounds__(kThreads) unary_vec_kernel(const T* __restrict__ x, T* __restrict__ y,
                                                              int64_t nvec, Op op) {
@@ -280,5 +287,12 @@ extern "C" int xb_swiglu(const void* gate, const void* up, void* out, int64_t n,
                          size_t errlen) {
   XB_DISPATCH_FLOAT(dtype, T, "xb_swiglu", err, errlen,
                     return launch_binary<T>(gate, up, out, n, OpSwiglu<T>{}, XB_S(stream), "xb_swiglu", err,
+                                            errlen));
+}
+
+extern "C" int xb_silu_mul(const void* gate, const void* up, void* out, int64_t n, int dtype, void* stream, char* err,
+                           size_t errlen) {
+  XB_DISPATCH_FLOAT(dtype, T, "xb_silu_mul", err, errlen,
+                    return launch_binary<T>(gate, up, out, n, OpSiluMul<T>{}, XB_S(stream), "xb_silu_mul", err,
                                             errlen));
 }

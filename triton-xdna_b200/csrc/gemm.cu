@@ -292,6 +292,14 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
               if (col0 + j < args.n) cp[j] = __float2bfloat16_rn(f[j]);
           }
         } else {
+          if constexpr (OUT == kOutF32) {
+            if (args.bias) {
+              const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(args.bias) + col0;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.n) v[j] = __float_as_uint(__uint_as_float(v[j]) + __bfloat162float(bp[j]));
+            }
+          }
           uint32_t* cp = static_cast<uint32_t*>(args.c) + (int64_t)row * args.ldc + col0;
           if (col0 + 32 <= args.n && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
 #pragma unroll
@@ -630,10 +638,14 @@ extern "C" int xb_matmul_bf16(const void* A, const void* B, void* C, int64_t M, 
 }
 
 extern "C" int xb_linear_bf16(const void* X, const void* W, const void* bias, void* Y, int64_t M, int64_t N,
-                              int64_t K, int64_t ldx, int64_t ldw, int64_t ldy, void* stream, char* err,
-                              size_t errlen) {
+                              int64_t K, int64_t ldx, int64_t ldw, int64_t ldy, int out_dtype, void* stream,
+                              char* err, size_t errlen) {
   const char* what = "xb_linear_bf16";
   cudaStream_t s = (cudaStream_t)stream;
+  if (out_dtype != XB_DT_F32 && out_dtype != XB_DT_BF16) {
+    set_err(err, errlen, "%s: out_dtype must be f32 or bf16", what);
+    return XB_ERR_UNSUPPORTED;
+  }
   int rc = check_common(X, W, Y, M, N, K, ldx, ldw, ldy, true, what, err, errlen);
   if (rc) return rc < 0 ? rc : XB_OK;
   if (K == 0) {
@@ -645,6 +657,7 @@ extern "C" int xb_linear_bf16(const void* X, const void* W, const void* bias, vo
     return XB_ERR_UNSUPPORTED;
   }
   Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
+  if (out_dtype == XB_DT_F32) return launch<kBf16, true, kOutF32>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
   return launch<kBf16, true, kOutBf16>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
 }
 

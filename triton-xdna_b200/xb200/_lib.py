@@ -44,9 +44,14 @@ _CTYPES = {
     "const void*": ctypes.c_void_p,
     "void* const*": ctypes.c_void_p,
     "int": ctypes.c_int,
+    # host out-parameters (passed with ctypes.byref)
     "int*": ctypes.POINTER(ctypes.c_int),
     "int64_t": ctypes.c_int64,
-    "int64_t*": ctypes.POINTER(ctypes.c_int64),
+    # device pointers travel as plain addresses
+    "int64_t*": ctypes.c_void_p,
+    "const int64_t*": ctypes.c_void_p,
+    "float*": ctypes.c_void_p,
+    "const float*": ctypes.c_void_p,
     "size_t": ctypes.c_size_t,
     "size_t*": ctypes.POINTER(ctypes.c_size_t),
     "float": ctypes.c_float,

@@ -138,6 +138,11 @@ def swiglu(gate, up, out=None):
     return _binary("xb_swiglu", gate, up, out)
 
 
+def silu_mul(gate, up, out=None):
+    """silu(gate) * up in fp32, one rounding (examples/qwen2_5/kernels/swiglu.py:29-50)."""
+    return _binary("xb_silu_mul", gate, up, out)
+
+
 # --------------------------------------------------------------------------- row reductions
 
 
@@ -325,9 +330,9 @@ def matmul_bf16(a, b, out_dtype=torch.float32, out=None):
     return out
 
 
-def linear(x, weight, bias=None, out=None):
-    """y = x @ weight^T + bias, weight [N, K] (nn.Linear layout), bf16
-    (examples/qwen2_5/kernels/matmul.py:172-296)."""
+def linear(x, weight, bias=None, out=None, out_dtype=torch.bfloat16):
+    """y = x @ weight^T + bias, weight [N, K] (nn.Linear layout), bf16 inputs,
+    fp32 accumulation, y in bf16 or fp32 (examples/qwen2_5/kernels/matmul.py:172-296)."""
     _cuda(x, weight, bias, out)
     if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
         raise TypeError("linear takes bf16 x and weight")
@@ -340,12 +345,18 @@ def linear(x, weight, bias=None, out=None):
         raise ValueError(f"shape mismatch x[..., {K}] vs weight {tuple(weight.shape)}")
     x2 = x.reshape(-1, K)
     M = x2.shape[0]
+    if out is not None:
+        out_dtype = out.dtype
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError("out dtype must be float32 or bfloat16")
     if out is None:
-        y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+        y = torch.empty((M, N), dtype=out_dtype, device=x.device)
     else:
+        if out.numel() != M * N:
+            raise ValueError("out has the wrong size")
         y = out.reshape(M, N)
     _lib.call("xb_linear_bf16", x2.data_ptr(), weight.data_ptr(), bias.data_ptr() if bias is not None else None,
-              y.data_ptr(), M, N, K, _mat(x2, "x"), _mat(weight, "weight"), _mat(y, "y"), _stream())
+              y.data_ptr(), M, N, K, _mat(x2, "x"), _mat(weight, "weight"), _mat(y, "y"), DT[out_dtype], _stream())
     return y.reshape(*x.shape[:-1], N) if out is None else out
 
 
@@ -354,3 +365,50 @@ def device_status() -> int:
     st = ctypes.c_int(0)
     _lib.call("xb_device_status", _stream(), ctypes.byref(st))
     return st.value
+
+
+# --------------------------------------------------------------------------- Qwen2.5 decoder pieces
+
+
+def embedding(table, ids, out=None):
+    """out[..., :] = table[ids] (bf16 rows), as model.py:911."""
+    _cuda(table, ids, out)
+    if table.dtype != torch.bfloat16 or ids.dtype != torch.int64:
+        raise TypeError("embedding takes a bf16 table and int64 ids")
+    ids_c = ids.contiguous()
+    rows = ids_c.numel()
+    dim = table.shape[1]
+    if out is None:
+        out = torch.empty(tuple(ids.shape) + (dim,), dtype=torch.bfloat16, device=table.device)
+    _lib.call("xb_embedding_bf16", table.data_ptr(), ids_c.data_ptr(), out.data_ptr(), rows, dim, table.shape[0],
+              _stream())
+    return out
+
+
+def rope_kv(qkv, cos_t, sin_t, q_out, k_cache, v_cache, batch, seq, n_head, n_kv_head, head_dim, pos_offset):
+    """RoPE on the fused QKV projection + KV-cache write (model.py:851-867)."""
+    _cuda(qkv, cos_t, sin_t, q_out, k_cache, v_cache)
+    if cos_t.shape[0] < pos_offset + seq:
+        raise ValueError("RoPE tables are shorter than the positions")
+    _lib.call("xb_rope_kv_bf16", qkv.data_ptr(), cos_t.data_ptr(), sin_t.data_ptr(), q_out.data_ptr(),
+              k_cache.data_ptr(), v_cache.data_ptr(), batch, seq, n_head, n_kv_head, head_dim, k_cache.shape[2],
+              pos_offset, _stream())
+
+
+def attention(q, k_cache, v_cache, out, batch, seq, n_head, n_kv_head, head_dim, pos_offset, scale):
+    """Causal GQA attention over the cache (kernels/attention.py:27-122)."""
+    _cuda(q, k_cache, v_cache, out)
+    _lib.call("xb_attention_bf16", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), batch, seq,
+              n_head, n_kv_head, head_dim, k_cache.shape[2], pos_offset, float(scale), _stream())
+    return out
+
+
+def argmax(x, out=None):
+    """First index of the row maximum of a 2-D fp32 tensor (torch.argmax(-1))."""
+    _cuda(x, out)
+    if x.dtype != torch.float32 or x.dim() != 2 or x.stride(1) != 1:
+        raise TypeError("argmax takes a row-major 2-D float32 tensor")
+    if out is None:
+        out = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
+    _lib.call("xb_argmax_f32", x.data_ptr(), x.shape[0], x.shape[1], x.stride(0), out.data_ptr(), _stream())
+    return out

@@ -1,0 +1,203 @@
+"""Qwen2.5 decoder forward and greedy generation on xb200 kernels.
+
+Mirrors `Qwen2Model` of the reference (examples/qwen2_5/model.py:571-1179) on
+its GPU path:
+
+  embedding gather                                   model.py:911
+  per layer: rmsnorm -> fused QKV linear (+bias)     model.py:750-765, 836-849
+             RoPE + KV-cache write                   model.py:851-867, kernels/rope.py:44-67
+             causal GQA attention                    model.py:868-889, kernels/attention.py:27-122
+             o_proj, residual add                    model.py:893, 1045-1046
+             rmsnorm, gate/up, silu*up, down, add    model.py:1047-1061
+  final rmsnorm, tied LM head in fp32                model.py:1087-1106
+  greedy argmax generation with a KV cache           model.py:1110-1179
+
+Every step is an xb200 kernel (ops.*); torch only owns device memory.
+Differences from the reference, all deliberate: GQA is handled natively by
+the attention kernel (no repeat_interleave of K/V); the QKV bias is added in
+fp32 inside the GEMM epilogue (the reference rounds the product to bf16 and
+adds in bf16); generation is batched (the reference's `generate` is batch 1)
+and may return last-position logits only (all a greedy step needs).
+"""
+
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+
+
+@dataclass
+class QwenConfig:
+    """Qwen2.5 dimensions (examples/qwen2_5/model.py:57-90)."""
+
+    n_layer: int = 24
+    n_head: int = 14
+    n_kv_head: int = 2
+    n_embd: int = 896
+    head_dim: int = 64
+    intermediate: int = 4864
+    vocab_size: int = 151936
+    rope_theta: float = 1000000.0
+    rms_eps: float = 1e-6
+    max_seq_len: int = 32768
+
+    @classmethod
+    def qwen2_5_0_5b(cls) -> "QwenConfig":
+        return cls()
+
+
+def random_weights(cfg: QwenConfig, seed: int = 0, std: float = 0.02) -> dict:
+    """Seeded random-init bf16 weights with the HF state-dict names the
+    reference loads (model.py:660-683): N(0, std) matrices and biases, RMSNorm
+    weights 1 + N(0, std).  Generated on the CPU so every process (and the
+    CPU oracle) gets identical weights from the same seed."""
+    g = torch.Generator().manual_seed(seed)
+
+    def w(*shape, base=0.0):
+        return (base + std * torch.randn(*shape, generator=g)).to(torch.bfloat16)
+
+    D, KV = cfg.n_embd, cfg.n_kv_head * cfg.head_dim
+    sd = {"model.embed_tokens.weight": w(cfg.vocab_size, D)}
+    for i in range(cfg.n_layer):
+        p = f"model.layers.{i}"
+        sd[f"{p}.input_layernorm.weight"] = w(D, base=1.0)
+        sd[f"{p}.post_attention_layernorm.weight"] = w(D, base=1.0)
+        sd[f"{p}.self_attn.q_proj.weight"] = w(cfg.n_head * cfg.head_dim, D)
+        sd[f"{p}.self_attn.q_proj.bias"] = w(cfg.n_head * cfg.head_dim)
+        sd[f"{p}.self_attn.k_proj.weight"] = w(KV, D)
+        sd[f"{p}.self_attn.k_proj.bias"] = w(KV)
+        sd[f"{p}.self_attn.v_proj.weight"] = w(KV, D)
+        sd[f"{p}.self_attn.v_proj.bias"] = w(KV)
+        sd[f"{p}.self_attn.o_proj.weight"] = w(D, cfg.n_head * cfg.head_dim)
+        sd[f"{p}.mlp.gate_proj.weight"] = w(cfg.intermediate, D)
+        sd[f"{p}.mlp.up_proj.weight"] = w(cfg.intermediate, D)
+        sd[f"{p}.mlp.down_proj.weight"] = w(D, cfg.intermediate)
+    sd["model.norm.weight"] = w(D, base=1.0)
+    return sd
+
+
+def rope_tables(head_dim: int, max_seq_len: int, base: float):
+    """cos / sin tables [max_seq_len, head_dim] in fp32, computed exactly as
+    examples/qwen2_5/kernels/rope.py:20-35 does."""
+    half = head_dim // 2
+    inv_freq = 1.0 / (base ** (torch.arange(0, half, dtype=torch.float32) / half))
+    t = torch.arange(max_seq_len, dtype=torch.float32)
+    freqs = torch.outer(t, inv_freq)
+    emb = torch.cat([freqs, freqs], dim=-1)
+    return emb.cos(), emb.sin()
+
+
+class KVCache:
+    """Per-layer K / V caches [B, n_kv_head, max_seq, head_dim] (model.py:1110-1132)."""
+
+    def __init__(self, cfg: QwenConfig, batch: int, max_seq: int, device):
+        shape = (batch, cfg.n_kv_head, max_seq, cfg.head_dim)
+        self.k = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(cfg.n_layer)]
+        self.v = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(cfg.n_layer)]
+        self.batch = batch
+        self.max_seq = max_seq
+        self.length = 0
+
+
+class Qwen2Model:
+    def __init__(self, state_dict: dict, cfg: QwenConfig | None = None, device="cuda", rope_len: int | None = None):
+        self.cfg = cfg or QwenConfig()
+        c = self.cfg
+        self.device = torch.device(device)
+        dev = self.device
+
+        def t(name):
+            return state_dict[name].to(device=dev, dtype=torch.bfloat16).contiguous()
+
+        self.embed = t("model.embed_tokens.weight")
+        self.layers = []
+        for i in range(c.n_layer):
+            p = f"model.layers.{i}"
+            self.layers.append({
+                "input_ln": t(f"{p}.input_layernorm.weight"),
+                "post_ln": t(f"{p}.post_attention_layernorm.weight"),
+                # fused QKV weight / bias, as model.py:840-846 builds them
+                "qkv_w": torch.cat([t(f"{p}.self_attn.q_proj.weight"), t(f"{p}.self_attn.k_proj.weight"),
+                                    t(f"{p}.self_attn.v_proj.weight")], 0).contiguous(),
+                "qkv_b": torch.cat([t(f"{p}.self_attn.q_proj.bias"), t(f"{p}.self_attn.k_proj.bias"),
+                                    t(f"{p}.self_attn.v_proj.bias")], 0).contiguous(),
+                "o_w": t(f"{p}.self_attn.o_proj.weight"),
+                "gate_w": t(f"{p}.mlp.gate_proj.weight"),
+                "up_w": t(f"{p}.mlp.up_proj.weight"),
+                "down_w": t(f"{p}.mlp.down_proj.weight"),
+            })
+        self.norm_w = t("model.norm.weight")
+        cos, sin = rope_tables(c.head_dim, rope_len or c.max_seq_len, c.rope_theta)
+        self.cos = cos.to(dev).contiguous()
+        self.sin = sin.to(dev).contiguous()
+        self.scale = 1.0 / math.sqrt(c.head_dim)
+
+    def new_cache(self, batch: int, max_seq: int) -> KVCache:
+        if max_seq > self.cos.shape[0]:
+            raise ValueError(f"cache length {max_seq} exceeds the RoPE table ({self.cos.shape[0]})")
+        return KVCache(self.cfg, batch, max_seq, self.device)
+
+    @torch.no_grad()
+    def forward(self, ids: torch.Tensor, cache: KVCache, last_only: bool = False) -> torch.Tensor:
+        """ids [B, S] int64 on the device; appends S positions to `cache`.
+        Returns fp32 logits [B, S, vocab], or [B, vocab] of the last position."""
+        c = self.cfg
+        B, S = ids.shape
+        if cache.batch != B:
+            raise ValueError("cache batch size differs from the input")
+        pos = cache.length
+        if pos + S > cache.max_seq:
+            raise ValueError("KV cache full")
+        M = B * S
+        D, H, KVH, HD = c.n_embd, c.n_head, c.n_kv_head, c.head_dim
+        x = ops.embedding(self.embed, ids.reshape(-1)).reshape(M, D)
+        q_buf = torch.empty((B, H, S, HD), dtype=torch.bfloat16, device=self.device)
+        attn = torch.empty((M, H * HD), dtype=torch.bfloat16, device=self.device)
+        for i, L in enumerate(self.layers):
+            xn = ops.rms_norm(x, L["input_ln"], c.rms_eps)
+            qkv = ops.linear(xn, L["qkv_w"], L["qkv_b"])
+            ops.rope_kv(qkv, self.cos, self.sin, q_buf, cache.k[i], cache.v[i], B, S, H, KVH, HD, pos)
+            ops.attention(q_buf, cache.k[i], cache.v[i], attn, B, S, H, KVH, HD, pos, self.scale)
+            proj = ops.linear(attn, L["o_w"])
+            x = ops.vecadd(x, proj)
+            xn = ops.rms_norm(x, L["post_ln"], c.rms_eps)
+            gate = ops.linear(xn, L["gate_w"])
+            up = ops.linear(xn, L["up_w"])
+            h = ops.silu_mul(gate, up)
+            down = ops.linear(h, L["down_w"])
+            x = ops.vecadd(x, down)
+        cache.length = pos + S
+        if last_only:
+            x = x.reshape(B, S, D)[:, -1, :]  # strided rows: the norm kernel gathers them
+        x = ops.rms_norm(x, self.norm_w, c.rms_eps, out=torch.empty((x.shape[0], D), dtype=torch.bfloat16,
+                                                                     device=self.device))
+        logits = ops.linear(x, self.embed, out_dtype=torch.float32)
+        return logits if last_only else logits.reshape(B, S, c.vocab_size)
+
+    @torch.no_grad()
+    def generate(self, ids: torch.Tensor, max_new_tokens: int, cache: KVCache | None = None):
+        """Greedy decoding (model.py:1134-1179), batched.  Returns
+        (tokens [B, max_new_tokens] int64 on the device, timing dict with
+        CUDA-event prefill / decode milliseconds)."""
+        B, S = ids.shape
+        if cache is None:
+            cache = self.new_cache(B, S + max_new_tokens)
+        # step-major token buffer: row `step` holds every sequence's token, so
+        # the argmax writes and the next step's embedding reads are contiguous
+        toks = torch.empty((max_new_tokens, B), dtype=torch.int64, device=self.device)
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        logits = self.forward(ids, cache, last_only=True)
+        ops.argmax(logits, out=toks[0])
+        e1.record()
+        for step in range(1, max_new_tokens):
+            logits = self.forward(toks[step - 1].view(B, 1), cache, last_only=True)
+            ops.argmax(logits, out=toks[step])
+        e2.record()
+        torch.cuda.synchronize()
+        return toks.t(), {"prefill_ms": e0.elapsed_time(e1), "decode_ms": e1.elapsed_time(e2)}
