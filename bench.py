@@ -240,7 +240,7 @@ def run_qwen_bench(args, world, rank, local, dev):
     from xb200.qwen import Qwen2Model, QwenConfig, random_weights
 
     cfg = QwenConfig()
-    B_total, S, new = 64, 512, 128
+    B_total, S, new = args.qwen_batch, args.qwen_prompt, args.qwen_new
     if B_total % world:
         raise SystemExit(f"batch {B_total} does not split over {world} ranks")
     B = B_total // world
@@ -249,11 +249,11 @@ def run_qwen_bench(args, world, rank, local, dev):
     del sd
     g = torch.Generator().manual_seed(1000 + rank)
     ids = torch.randint(0, cfg.vocab_size, (B, S), generator=g).to(dev)
-    cache = model.new_cache(B, S + new)
+    graphs = None if args.qwen_eager else model.decode_graphs(B, S, new)  # decode steps replay CUDA graphs
+    cache = model.new_cache(B, S + new) if graphs is None else None
 
     def step():
-        cache.length = 0
-        return model.generate(ids, new, cache)
+        return model.generate(ids, new, cache=cache, graphs=graphs)
 
     for _ in range(max(1, args.warmup)):
         step()
@@ -575,6 +575,10 @@ def main():
     ap.add_argument("--workload", default="elementwise", choices=sorted(WORKLOADS))
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--qwen-batch", type=int, default=64)
+    ap.add_argument("--qwen-prompt", type=int, default=512)
+    ap.add_argument("--qwen-new", type=int, default=128)
+    ap.add_argument("--qwen-eager", action="store_true", help="qwen: launch decode steps directly (no CUDA graphs)")
     ap.add_argument("--only", default=None, help="gemm workload: run only ops whose name contains this string")
     ap.add_argument("--no-library", action="store_true", help="gemm workload: skip the cuBLAS reference lines")
     ap.add_argument("--elements", type=int, default=N28,

@@ -216,6 +216,30 @@ XB_API int xb_linear_bf16(const void* X, const void* W, const void* bias,
                           int64_t ldx, int64_t ldw, int64_t ldy, int out_dtype,
                           void* stream, char* err, size_t errlen);
 
+/* Plan for xb_linear_small_bf16: the K-slice count it picks for an
+ * M x N x K product and the fp32 workspace it then needs (0 when it writes
+ * straight to Y). */
+XB_API int xb_linear_small_plan(int64_t M, int64_t N, int64_t K,
+                                int has_residual, int* splits,
+                                size_t* workspace_bytes, char* err,
+                                size_t errlen);
+
+/* Y = [residual +] (X[M,K] @ W[N,K]^T + bias), for few tokens (decode,
+ * M <= 64 is the target): the weight rows fill the 128-row MMA dimension and
+ * the tokens a 64-wide tile (swap-AB), K is split over `splits` slices (<= 0:
+ * automatic) so the weight streams from HBM on every SM, and a fixed-order
+ * reduction adds the slices, the bias and the residual (bf16 [M, N], row
+ * pitch ldr, may be NULL).  Needs the workspace xb_linear_small_plan
+ * reports.  Replaces `triton_linear` + `triton_add` in the decode step
+ * (examples/qwen2_5/model.py:1045-1061). */
+XB_API int xb_linear_small_bf16(const void* X, const void* W, const void* bias,
+                                const void* residual, void* Y, int64_t M,
+                                int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                                int64_t ldr, int64_t ldy, int out_dtype,
+                                int splits, void* workspace,
+                                size_t workspace_bytes, void* stream,
+                                char* err, size_t errlen);
+
 /* ---------------------------------------------------------------------------
  * Qwen2.5 decoder pieces (examples/qwen2_5/model.py:824-1179).
  * ------------------------------------------------------------------------- */

@@ -177,3 +177,34 @@ def test_full_size_i16_checksums_mod_2_32():
     ref = cgemm.gemm_int(a[rows.cuda()].cpu(), b.cpu())
     assert torch.equal(c[rows.cuda()].cpu(), ref)
     _status_ok()
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 896, 896), (7, 1152, 896), (16, 4864, 896), (64, 896, 4864), (64, 896, 896),
+                                   (33, 1000, 200), (64, 151936, 896)])
+def test_small_m_linear_matches_tiled_gemm(M, N, K):
+    g = torch.Generator().manual_seed(M + N + K)
+    x = torch.randn((M, K), generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn((N, K), generator=g) * 0.05).to(torch.bfloat16).cuda()
+    b = (torch.randn(N, generator=g) * 0.1).to(torch.bfloat16).cuda()
+    ref = (x.float() @ w.float().t() + b.float())
+    for dt in (torch.bfloat16, torch.float32):
+        y = ops.linear(x, w, b, out_dtype=dt)  # M <= 64: swap-AB split-K path
+        torch.testing.assert_close(y.float(), ref, atol=2e-3, rtol=2 ** -7 if dt == torch.bfloat16 else 1e-4)
+        y2 = ops.linear(x, w, b, out_dtype=dt)
+        assert torch.equal(y, y2)  # fixed-order reduction: bit-repeatable
+    _status_ok()
+
+
+def test_small_m_linear_fuses_residual_like_two_ops():
+    M, N, K = 64, 896, 4864
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn((M, K), generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn((N, K), generator=g) * 0.02).to(torch.bfloat16).cuda()
+    r = torch.randn((M, N), generator=g).to(torch.bfloat16).cuda()
+    fused = ops.linear(x, w, residual=r)
+    lin = ops.linear(x, w)
+    two = ops.vecadd(r, lin)  # the same rounding sequence, unfused
+    assert torch.equal(fused, two)
+    big = torch.randn((100, K), generator=g).to(torch.bfloat16).cuda()  # tiled path: linear then vecadd
+    rb = torch.randn((100, N), generator=g).to(torch.bfloat16).cuda()
+    assert torch.equal(ops.linear(big, w, residual=rb), ops.vecadd(rb, ops.linear(big, w)))

@@ -112,10 +112,24 @@ def test_batch_invariance_is_exact():
     cfg = QwenConfig(n_layer=4)
     sd = random_weights(cfg, seed=14)
     model = Qwen2Model(sd, cfg, rope_len=1024)
-    ids = _ids(8, 64, cfg.vocab_size, 8).cuda()
-    big = model.forward(ids, model.new_cache(8, 64), last_only=True)
-    one = model.forward(ids[3:4], model.new_cache(1, 64), last_only=True)
+    # 80 tokens: both runs take the tiled GEMM path (more than 64 rows)
+    ids = _ids(8, 80, cfg.vocab_size, 8).cuda()
+    big = model.forward(ids, model.new_cache(8, 80), last_only=True)
+    one = model.forward(ids[3:4], model.new_cache(1, 80), last_only=True)
     assert torch.equal(big[3:4], one)
+
+
+def test_decode_graphs_replay_equals_eager_generation():
+    cfg = QwenConfig(n_layer=4)
+    sd = random_weights(cfg, seed=15)
+    model = Qwen2Model(sd, cfg, rope_len=1024)
+    ids = _ids(4, 32, cfg.vocab_size, 10).cuda()
+    eager, _ = model.generate(ids, 6)
+    graphs = model.decode_graphs(4, 32, 6)
+    replayed, t1 = model.generate(ids, 6, graphs=graphs)
+    again, _ = model.generate(ids, 6, graphs=graphs)
+    assert torch.equal(eager, replayed) and torch.equal(replayed, again)
+    assert t1["decode_ms"] > 0
 
 
 def test_workload_shape_runs_finite():
@@ -126,6 +140,9 @@ def test_workload_shape_runs_finite():
     ids = _ids(64, 512, cfg.vocab_size, 9).cuda()
     toks, timing = model.generate(ids, 4)
     assert toks.shape == (64, 4)
+    graphs = model.decode_graphs(64, 512, 4)
+    toks2, _ = model.generate(ids, 4, graphs=graphs)
+    assert torch.equal(toks, toks2)
     assert int(toks.min()) >= 0 and int(toks.max()) < cfg.vocab_size
     assert ops.device_status() == 0
     del model

@@ -49,28 +49,34 @@ constexpr uint64_t kWaitLimit = 2000000000ull;  // 2 s per wait: far above any l
 enum Kind { kBf16 = 0, kInt8 = 1, kInt16Limbs = 2 };
 enum Out { kOutF32 = 0, kOutBf16 = 1, kOutI32 = 2 };
 
-template <int KIND, bool B_KMAJOR>
+constexpr int tmem_cols_for(int cols) { return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512; }
+
+// BN_: tile N (0 = the default for the kind).  The small-M path (swap-AB:
+// weight rows in the 128-row MMA dimension, up to 64 tokens in N) uses 64
+// with a deeper ring, since it streams weights from HBM in short K ranges.
+template <int KIND, bool B_KMAJOR, int BN_ = 0>
 struct Cfg {
   static constexpr int BM = 128;
-  static constexpr int BN = KIND == kInt16Limbs ? 128 : 256;
+  static constexpr int BN = BN_ ? BN_ : (KIND == kInt16Limbs ? 128 : 256);
   static constexpr int ESZ = KIND == kBf16 ? 2 : 1;  // operand element bytes
   static constexpr int BK = 128 / ESZ;              // K elements per stage (128 bytes)
   static constexpr int PLANES = KIND == kInt16Limbs ? 2 : 1;
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE_BYTES = PLANES * (A_BYTES + B_BYTES);
-  static constexpr int STAGES = KIND == kInt16Limbs ? 3 : 4;
+  static constexpr int STAGES = KIND == kInt16Limbs ? 3 : (BN <= 64 ? 8 : 4);
   static constexpr int UMMA_K = 32 / ESZ;  // 32 bytes of K per MMA
   static constexpr int KSTEPS = BK / UMMA_K;
   static constexpr int ACCS = KIND == kInt16Limbs ? 3 : 1;
   static constexpr int ACC_BUFS = KIND == kInt16Limbs ? 1 : 2;
-  static constexpr int TMEM_COLS = 512;
+  static constexpr int TMEM_COLS = tmem_cols_for(ACCS * ACC_BUFS * BN);
   static constexpr int B_BOX_N = 128 / ESZ;  // N elements in one MN-major B box
   static constexpr int B_BOXES = B_KMAJOR ? 1 : BN / B_BOX_N;
   static constexpr int B_BOX_BYTES = B_KMAJOR ? B_BYTES : BK * 128;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
   static_assert(ACCS * ACC_BUFS * BN <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(B_KMAJOR || BN % B_BOX_N == 0, "MN-major B needs whole boxes");
 };
 
 struct alignas(64) Maps {
@@ -82,8 +88,10 @@ struct Args {
   void* c;
   const void* bias;  // bf16 [N] or nullptr (linear layer only)
   int64_t ldc;
+  int64_t split_stride;  // elements between the split-K slices of c
   int m, n, k;
   int tiles_m, tiles_n, num_tiles, kblocks;
+  int splits, kps;  // split-K: `splits` slices of `kps` K blocks each
 };
 
 constexpr int kGroupM = 16;  // tile raster: groups of 16 M-tiles sweep N (L2 reuse)
@@ -98,9 +106,11 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   tn = r / gm;
 }
 
-template <int KIND, bool B_KMAJOR, int OUT>
+// TRANS: the epilogue stores C^T (element (r, c) of the tile product at
+// c * ldc + r); with A = W and B = X this computes Y = X W^T for few tokens.
+template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false>
 __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Maps maps, const Args args) {
-  using C = Cfg<KIND, B_KMAJOR>;
+  using C = Cfg<KIND, B_KMAJOR, BN_>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
@@ -158,8 +168,10 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       bool ok = true;
       for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x) {
         int tm, tn;
-        tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
-        for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
+        tile_coords(t / args.splits, args.tiles_m, args.tiles_n, tm, tn);
+        const int kb0 = (t % args.splits) * args.kps;
+        const int kb1 = min(kb0 + args.kps, args.kblocks);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           if (!mbar_wait(&empty_bar[s], ph ^ 1, kWaitLimit, &abort_flag)) { fail(); ok = false; break; }
@@ -197,7 +209,9 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
         if (!mbar_wait(&tempty_bar[buf], tph ^ 1, kWaitLimit, &abort_flag)) { fail(); break; }
         tc_fence_after();
         const uint32_t d0 = tmem_base + buf * C::ACCS * C::BN;
-        for (int kb = 0; kb < args.kblocks; ++kb, ++it) {
+        const int kb0 = (t % args.splits) * args.kps;
+        const int kb1 = min(kb0 + args.kps, args.kblocks);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           if (!mbar_wait(&full_bar[s], ph, kWaitLimit, &abort_flag)) { fail(); ok = false; break; }
@@ -205,7 +219,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
           const uint32_t st = base_u32 + s * C::STAGE_BYTES;
 #pragma unroll
           for (int ks = 0; ks < C::KSTEPS; ++ks) {
-            const uint32_t acc = (kb > 0 || ks > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > kb0 || ks > 0) ? 1u : 0u;
             uint64_t ad[2], bd[2];
 #pragma unroll
             for (int p = 0; p < C::PLANES; ++p) {
@@ -248,8 +262,9 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       if (!mbar_wait(&tfull_bar[buf], tph, kWaitLimit, &abort_flag)) { fail(); break; }
       tc_fence_after();
       int tm, tn;
-      tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+      tile_coords(t / args.splits, args.tiles_m, args.tiles_n, tm, tn);
       const int row = tm * C::BM + q * 32 + lane;
+      const int64_t slice = (int64_t)(t % args.splits) * args.split_stride;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * C::ACCS * C::BN;
 #pragma unroll 1
       for (int cc = 0; cc < C::BN / 32; ++cc) {
@@ -267,40 +282,51 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
         }
         const int col0 = tn * C::BN + cc * 32;
         if (row >= args.m || col0 >= args.n) continue;
-        if constexpr (OUT == kOutBf16) {
-          float f[32];
+        if constexpr (OUT != kOutI32) {
+          if (args.bias) {  // bias indexed by the output feature: the row of W
+            const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(args.bias);
+            if constexpr (TRANS) {
+              const float bv = __bfloat162float(bp[row]);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-          if (args.bias) {
-            const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(args.bias) + col0;
+              for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + bv);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.n) v[j] = __float_as_uint(__uint_as_float(v[j]) + __bfloat162float(bp[col0 + j]));
+            }
+          }
+        }
+        if constexpr (TRANS) {
+          // lanes hold consecutive rows: each j is one coalesced row segment of C
+          if constexpr (OUT == kOutBf16) {
+            __nv_bfloat16* cp = static_cast<__nv_bfloat16*>(args.c) + slice + row;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (col0 + j < args.n) f[j] += __bfloat162float(bp[j]);
+              if (col0 + j < args.n) cp[(int64_t)(col0 + j) * args.ldc] = __float2bfloat16_rn(__uint_as_float(v[j]));
+          } else {
+            uint32_t* cp = static_cast<uint32_t*>(args.c) + slice + row;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.n) cp[(int64_t)(col0 + j) * args.ldc] = v[j];
           }
-          __nv_bfloat16* cp = static_cast<__nv_bfloat16*>(args.c) + (int64_t)row * args.ldc + col0;
+        } else if constexpr (OUT == kOutBf16) {
+          __nv_bfloat16* cp = static_cast<__nv_bfloat16*>(args.c) + slice + (int64_t)row * args.ldc + col0;
           if (col0 + 32 <= args.n && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
 #pragma unroll
             for (int j = 0; j < 32; j += 8) {
               __nv_bfloat162 h[4];
 #pragma unroll
-              for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(f[j + 2 * e], f[j + 2 * e + 1]);
+              for (int e = 0; e < 4; ++e)
+                h[e] = __floats2bfloat162_rn(__uint_as_float(v[j + 2 * e]), __uint_as_float(v[j + 2 * e + 1]));
               *reinterpret_cast<int4*>(cp + j) = *reinterpret_cast<int4*>(h);
             }
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (col0 + j < args.n) cp[j] = __float2bfloat16_rn(f[j]);
+              if (col0 + j < args.n) cp[j] = __float2bfloat16_rn(__uint_as_float(v[j]));
           }
         } else {
-          if constexpr (OUT == kOutF32) {
-            if (args.bias) {
-              const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(args.bias) + col0;
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < args.n) v[j] = __float_as_uint(__uint_as_float(v[j]) + __bfloat162float(bp[j]));
-            }
-          }
-          uint32_t* cp = static_cast<uint32_t*>(args.c) + (int64_t)row * args.ldc + col0;
+          uint32_t* cp = static_cast<uint32_t*>(args.c) + slice + (int64_t)row * args.ldc + col0;
           if (col0 + 32 <= args.n && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
@@ -323,6 +349,48 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
+}
+
+// Y[m, n] = [residual[m, n] +] round(sum_s part[s, m, n] + bias[n]): the
+// split-K reduction of the small-M linear, in a fixed order (deterministic),
+// fused with the bias and the residual add that follow o_proj / down_proj.
+// With bf16 output the linear result is rounded to bf16 before the residual
+// add, as two separate bf16 operations would round it.
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t M,
+                                                            int64_t N, const __nv_bfloat16* __restrict__ bias,
+                                                            const __nv_bfloat16* __restrict__ residual, int64_t ldr,
+                                                            void* __restrict__ y, int64_t ldy) {
+  const int64_t total = M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / N, n = i - m * N;
+    float acc = 0.0f;
+    for (int s2 = 0; s2 < splits; ++s2) acc += part[(int64_t)s2 * total + i];
+    if (bias) acc += __bfloat162float(bias[n]);
+    if constexpr (OUT_BF16) {
+      float r = __bfloat162float(__float2bfloat16_rn(acc));
+      if (residual) r = __bfloat162float(residual[m * ldr + n]) + r;
+      static_cast<__nv_bfloat16*>(y)[m * ldy + n] = __float2bfloat16_rn(r);
+    } else {
+      if (residual) acc += __bfloat162float(residual[m * ldr + n]);
+      static_cast<float*>(y)[m * ldy + n] = acc;
+    }
+  }
+}
+
+// Split count for the small-M linear: enough (weight-row tile, K slice)
+// work units to cover the SMs, at least two K blocks per slice.
+int small_m_splits(int64_t N, int64_t K) {
+  const int64_t tiles = (N + 127) / 128;
+  const int64_t kblocks = (K + 63) / 64;
+  int sms = 148;
+  sm_count(&sms);
+  int64_t want = (sms + tiles - 1) / tiles;
+  const int64_t cap = kblocks / 2 > 0 ? kblocks / 2 : 1;
+  if (want > cap) want = cap;
+  if (want < 1) want = 1;
+  const int64_t kps = (kblocks + want - 1) / want;
+  return (int)((kblocks + kps - 1) / kps);
 }
 
 // int16 -> (high s8, low u8) limb planes, each [rows, cols] with leading dim ldp.
@@ -386,10 +454,10 @@ struct Operands {
   int64_t lda, ldb;
 };
 
-template <int KIND, bool B_KMAJOR, int OUT>
+template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false>
 int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
-           cudaStream_t s, const char* what, char* err, size_t errlen) {
-  using Cf = Cfg<KIND, B_KMAJOR>;
+           cudaStream_t s, const char* what, char* err, size_t errlen, int splits = 1, int64_t split_stride = 0) {
+  using Cf = Cfg<KIND, B_KMAJOR, BN_>;
   const CUtensorMapDataType dt = KIND == kBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   Maps maps;
   memset(&maps, 0, sizeof(maps));
@@ -409,11 +477,16 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   args.k = (int)K;
   args.tiles_m = (int)((M + Cf::BM - 1) / Cf::BM);
   args.tiles_n = (int)((N + Cf::BN - 1) / Cf::BN);
-  args.num_tiles = args.tiles_m * args.tiles_n;
   args.kblocks = (int)((K + Cf::BK - 1) / Cf::BK);
+  if (splits < 1) splits = 1;
+  if (splits > args.kblocks) splits = args.kblocks;
+  args.kps = (args.kblocks + splits - 1) / splits;
+  args.splits = (args.kblocks + args.kps - 1) / args.kps;  // every slice gets at least one K block
+  args.split_stride = split_stride;
+  args.num_tiles = args.tiles_m * args.tiles_n * args.splits;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<KIND, B_KMAJOR, OUT>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
     if (e != cudaSuccess) {
       set_err(err, errlen, "%s: cudaFuncSetAttribute: %s", what, cudaGetErrorString(e));
@@ -424,7 +497,7 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   int sms = 148;
   sm_count(&sms);
   const int grid = args.num_tiles < sms ? args.num_tiles : sms;
-  gemm_kernel<KIND, B_KMAJOR, OUT><<<grid, 192, Cf::SMEM, s>>>(maps, args);
+  gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS><<<grid, 192, Cf::SMEM, s>>>(maps, args);
   return check_launch(what, err, errlen);
 }
 
@@ -516,6 +589,7 @@ int run_i16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t
 
 using namespace xb::gemm;
 using xb::set_err;
+using xb::check_launch;
 
 extern "C" int xb_matmul_i8(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                             int64_t ldb, int64_t ldc, void* stream, char* err, size_t errlen) {
@@ -659,6 +733,78 @@ extern "C" int xb_linear_bf16(const void* X, const void* W, const void* bias, vo
   Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
   if (out_dtype == XB_DT_F32) return launch<kBf16, true, kOutF32>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
   return launch<kBf16, true, kOutBf16>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
+}
+
+extern "C" int xb_linear_small_plan(int64_t M, int64_t N, int64_t K, int has_residual, int* splits,
+                                    size_t* workspace_bytes, char* err, size_t errlen) {
+  if (M < 0 || N <= 0 || K <= 0 || !splits || !workspace_bytes) {
+    set_err(err, errlen, "xb_linear_small_plan: bad arguments");
+    return XB_ERR_INVALID;
+  }
+  *splits = small_m_splits(N, K);
+  *workspace_bytes = (*splits > 1 || has_residual) ? (size_t)(*splits) * (size_t)M * (size_t)N * sizeof(float) : 0;
+  return XB_OK;
+}
+
+extern "C" int xb_linear_small_bf16(const void* X, const void* W, const void* bias, const void* residual, void* Y,
+                                    int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw, int64_t ldr,
+                                    int64_t ldy, int out_dtype, int splits, void* workspace, size_t workspace_bytes,
+                                    void* stream, char* err, size_t errlen) {
+  const char* what = "xb_linear_small_bf16";
+  cudaStream_t s = (cudaStream_t)stream;
+  if (out_dtype != XB_DT_F32 && out_dtype != XB_DT_BF16) {
+    set_err(err, errlen, "%s: out_dtype must be f32 or bf16", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  int rc = check_common(X, W, Y, M, N, K, ldx, ldw, ldy, true, what, err, errlen);
+  if (rc) return rc < 0 ? rc : XB_OK;
+  if (K == 0) {
+    set_err(err, errlen, "%s: K must be positive", what);
+    return XB_ERR_INVALID;
+  }
+  if (residual && ldr < N) {
+    set_err(err, errlen, "%s: residual row pitch shorter than N", what);
+    return XB_ERR_INVALID;
+  }
+  if (!tma_ok(X, ldx, 2) || !tma_ok(W, ldw, 2)) {
+    set_err(err, errlen, "%s: X/W must be 16-byte aligned with row pitches a multiple of 16 bytes", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  if (splits <= 0) splits = small_m_splits(N, K);
+  const int kblocks = (int)((K + 63) / 64);
+  if (splits > kblocks) splits = kblocks;
+  const int kps = (kblocks + splits - 1) / splits;
+  splits = (kblocks + kps - 1) / kps;
+  // swap-AB: the weight is the 128-row MMA operand, the tokens the 64-wide one
+  Operands op{{W, nullptr}, {X, nullptr}, ldw, ldx};
+  if (splits == 1 && !residual) {
+    if (out_dtype == XB_DT_F32)
+      return launch<kBf16, true, kOutF32, 64, true>(op, Y, bias, N, M, K, ldy, s, what, err, errlen);
+    return launch<kBf16, true, kOutBf16, 64, true>(op, Y, bias, N, M, K, ldy, s, what, err, errlen);
+  }
+  const size_t need = (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
+  if (!workspace || workspace_bytes < need) {
+    set_err(err, errlen, "%s: workspace of %zu bytes given, %zu needed (%d K slices)", what, workspace_bytes, need,
+            splits);
+    return XB_ERR_INVALID;
+  }
+  float* part = static_cast<float*>(workspace);
+  rc = launch<kBf16, true, kOutF32, 64, true>(op, part, nullptr, N, M, K, N, s, what, err, errlen, splits, M * N);
+  if (rc) return rc;
+  const int64_t total = M * N;
+  int64_t grid = (total + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  if (out_dtype == XB_DT_BF16)
+    splitk_reduce_kernel<true><<<(unsigned)grid, 256, 0, s>>>(part, splits, M, N,
+                                                               static_cast<const __nv_bfloat16*>(bias),
+                                                               static_cast<const __nv_bfloat16*>(residual), ldr, Y,
+                                                               ldy);
+  else
+    splitk_reduce_kernel<false><<<(unsigned)grid, 256, 0, s>>>(part, splits, M, N,
+                                                                static_cast<const __nv_bfloat16*>(bias),
+                                                                static_cast<const __nv_bfloat16*>(residual), ldr, Y,
+                                                                ldy);
+  return check_launch(what, err, errlen);
 }
 
 extern "C" int xb_device_status(void* stream, int* status, char* err, size_t errlen) {

@@ -264,18 +264,25 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const bf16* __restric
 // ----------------------------------------------------------------------------- decode attention
 
 // One CTA per (batch, KV head) serves the H/KVH query heads that share it, so
-// each cached key / value row is read from memory once per step.  Scores live
-// in shared memory ([n_rep][total] fp32); P is rounded to bf16 before P@V as
-// in the prefill kernel.
+// each cached key / value row is read once per step.  Every phase is
+// parallel over keys (no serial chain over the context):
+//   1. scores: thread t takes keys t, t+256, ...; q (fp32) is broadcast from
+//      shared memory; scores go to smem [n_rep][total];
+//   2. softmax per head (one warp per head), P rounded to bf16 as the
+//      prefill kernel does;
+//   3. P@V: warp w takes keys w, w+8, ...; lane l owns dims 2l, 2l+1 of every
+//      head; the 8 warps' partial sums are added through shared memory.
 __global__ void __launch_bounds__(256) attn_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
                                                           const bf16* __restrict__ vc, bf16* __restrict__ out, int H,
                                                           int KVH, int smax, int total, float scale_log2) {
-  extern __shared__ float sc[];  // [n_rep][total]
+  extern __shared__ float dsm[];  // sc [n_rep][total], then red [8][n_rep][kHD]
   __shared__ float qs[16][kHD];
   __shared__ float lsum[16];
   const int b = blockIdx.x, kvh = blockIdx.y;
   const int n_rep = H / KVH;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* sc = dsm;
+  float* red = dsm + n_rep * total;
   for (int i = threadIdx.x; i < n_rep * kHD; i += 256) {
     const int r = i / kHD, d = i % kHD;
     qs[r][d] = __bfloat162float(q[((int64_t)b * H + kvh * n_rep + r) * kHD + d]);
@@ -283,15 +290,28 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const bf16* __restrict
   __syncthreads();
   const bf16* kp = kc + ((int64_t)(b * KVH + kvh) * smax) * kHD;
   const bf16* vp = vc + ((int64_t)(b * KVH + kvh) * smax) * kHD;
-  for (int key = warp; key < total; key += 8) {
-    const __nv_bfloat162 kv = reinterpret_cast<const __nv_bfloat162*>(kp + (int64_t)key * kHD)[lane];
-    const float kx = __low2float(kv), ky = __high2float(kv);
-    for (int r = 0; r < n_rep; ++r) {
-      float p = qs[r][2 * lane] * kx + qs[r][2 * lane + 1] * ky;
+
+  for (int key = threadIdx.x; key < total; key += 256) {
+    float acc[16];
 #pragma unroll
-      for (int o_ = 16; o_ > 0; o_ >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o_);
-      if (lane == 0) sc[r * total + key] = p * scale_log2;
+    for (int r = 0; r < 16; ++r) acc[r] = 0.0f;
+    const int4* krow = reinterpret_cast<const int4*>(kp + (int64_t)key * kHD);
+#pragma unroll
+    for (int c = 0; c < kHD / 8; ++c) {
+      const int4 raw = __ldg(krow + c);
+      const __nv_bfloat162* kv = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float kx = __low2float(kv[e]), ky = __high2float(kv[e]);
+        const int d = c * 8 + 2 * e;
+#pragma unroll
+        for (int r = 0; r < 16; ++r)
+          if (r < n_rep) acc[r] += qs[r][d] * kx + qs[r][d + 1] * ky;
+      }
     }
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+      if (r < n_rep) sc[r * total + key] = acc[r] * scale_log2;
   }
   __syncthreads();
   for (int r = warp; r < n_rep; r += 8) {
@@ -310,17 +330,34 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const bf16* __restrict
     if (lane == 0) lsum[r] = sum;
   }
   __syncthreads();
-  for (int r = warp; r < n_rep; r += 8) {
-    float ax = 0.0f, ay = 0.0f;
-    for (int k = 0; k < total; ++k) {
-      const float p = sc[r * total + k];
-      const __nv_bfloat162 vv = reinterpret_cast<const __nv_bfloat162*>(vp + (int64_t)k * kHD)[lane];
-      ax += p * __low2float(vv);
-      ay += p * __high2float(vv);
+  float ax[16], ay[16];
+#pragma unroll
+  for (int r = 0; r < 16; ++r) ax[r] = ay[r] = 0.0f;
+#pragma unroll 4
+  for (int k = warp; k < total; k += 8) {
+    const __nv_bfloat162 vv = reinterpret_cast<const __nv_bfloat162*>(vp + (int64_t)k * kHD)[lane];
+    const float vx = __low2float(vv), vy = __high2float(vv);
+#pragma unroll
+    for (int r = 0; r < 16; ++r)
+      if (r < n_rep) {
+        const float p = sc[r * total + k];
+        ax[r] += p * vx;
+        ay[r] += p * vy;
+      }
+  }
+#pragma unroll
+  for (int r = 0; r < 16; ++r)
+    if (r < n_rep) {
+      red[(warp * n_rep + r) * kHD + 2 * lane] = ax[r];
+      red[(warp * n_rep + r) * kHD + 2 * lane + 1] = ay[r];
     }
-    const float inv = 1.0f / lsum[r];
-    reinterpret_cast<__nv_bfloat162*>(out + ((int64_t)b * H + kvh * n_rep + r) * kHD)[lane] =
-        __floats2bfloat162_rn(ax * inv, ay * inv);
+  __syncthreads();
+  for (int i = threadIdx.x; i < n_rep * kHD; i += 256) {
+    const int r = i / kHD, d = i % kHD;
+    float acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) acc += red[(w * n_rep + r) * kHD + d];
+    out[((int64_t)b * H + kvh * n_rep + r) * kHD + d] = __float2bfloat16_rn(acc / lsum[r]);
   }
 }
 
@@ -481,12 +518,16 @@ extern "C" int xb_attention_bf16(const void* q, const void* k_cache, const void*
       set_err(err, errlen, "%s: more than 16 query heads per KV head", what);
       return XB_ERR_UNSUPPORTED;
     }
-    const size_t smem = (size_t)n_rep * total * sizeof(float);
+    const size_t smem = ((size_t)n_rep * total + 8 * (size_t)n_rep * kHD) * sizeof(float);
     if (smem > 200 * 1024) {
       set_err(err, errlen, "%s: decode context %d too long for the score buffer", what, total);
       return XB_ERR_UNSUPPORTED;
     }
-    if (smem > 48 * 1024) cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    static size_t smem_set = 48 * 1024;
+    if (smem > smem_set) {
+      cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      smem_set = 200 * 1024;
+    }
     attn_decode_kernel<<<dim3((unsigned)batch, (unsigned)n_kv_head), 256, smem, s>>>(
         static_cast<const bf16*>(q), static_cast<const bf16*>(k_cache), static_cast<const bf16*>(v_cache),
         static_cast<bf16*>(out), (int)n_head, (int)n_kv_head, (int)max_seq, total, scale_log2);

@@ -330,10 +330,27 @@ def matmul_bf16(a, b, out_dtype=torch.float32, out=None):
     return out
 
 
-def linear(x, weight, bias=None, out=None, out_dtype=torch.bfloat16):
-    """y = x @ weight^T + bias, weight [N, K] (nn.Linear layout), bf16 inputs,
-    fp32 accumulation, y in bf16 or fp32 (examples/qwen2_5/kernels/matmul.py:172-296)."""
-    _cuda(x, weight, bias, out)
+SMALL_M = 64  # token counts at or below this take the swap-AB split-K path
+_workspaces: dict = {}
+
+
+def _workspace(device, nbytes: int) -> torch.Tensor:
+    """A per-device fp32 scratch buffer that only grows (kept alive so its
+    address is stable, e.g. across CUDA-graph replays)."""
+    ws = _workspaces.get(device)
+    if ws is None or ws.numel() * 4 < nbytes:
+        ws = torch.empty(max(nbytes // 4, 1 << 20), dtype=torch.float32, device=device)
+        _workspaces[device] = ws
+    return ws
+
+
+def linear(x, weight, bias=None, out=None, out_dtype=torch.bfloat16, residual=None):
+    """y = [residual +] x @ weight^T + bias, weight [N, K] (nn.Linear layout),
+    bf16 inputs, fp32 accumulation, y in bf16 or fp32
+    (examples/qwen2_5/kernels/matmul.py:172-296).  Up to SMALL_M rows use the
+    small-M kernel with the residual add fused; larger inputs use the tiled
+    GEMM followed by vecadd."""
+    _cuda(x, weight, bias, out, residual)
     if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
         raise TypeError("linear takes bf16 x and weight")
     if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != weight.shape[0]
@@ -355,8 +372,28 @@ def linear(x, weight, bias=None, out=None, out_dtype=torch.bfloat16):
         if out.numel() != M * N:
             raise ValueError("out has the wrong size")
         y = out.reshape(M, N)
-    _lib.call("xb_linear_bf16", x2.data_ptr(), weight.data_ptr(), bias.data_ptr() if bias is not None else None,
-              y.data_ptr(), M, N, K, _mat(x2, "x"), _mat(weight, "weight"), _mat(y, "y"), DT[out_dtype], _stream())
+    bptr = bias.data_ptr() if bias is not None else None
+    if residual is not None:
+        if residual.dtype != torch.bfloat16 or residual.numel() != M * N:
+            raise ValueError("residual must be bf16 with M x N elements")
+        r2 = residual.reshape(M, N)
+    if 0 < M <= SMALL_M:
+        splits = ctypes.c_int(0)
+        need = ctypes.c_size_t(0)
+        _lib.call("xb_linear_small_plan", M, N, K, int(residual is not None), ctypes.byref(splits), ctypes.byref(need))
+        ws = _workspace(x.device, need.value) if need.value else None
+        _lib.call("xb_linear_small_bf16", x2.data_ptr(), weight.data_ptr(), bptr,
+                  r2.data_ptr() if residual is not None else None, y.data_ptr(), M, N, K, _mat(x2, "x"),
+                  _mat(weight, "weight"), _mat(r2, "residual") if residual is not None else N, _mat(y, "y"),
+                  DT[out_dtype], splits.value, ws.data_ptr() if ws is not None else None,
+                  ws.numel() * 4 if ws is not None else 0, _stream())
+    else:
+        _lib.call("xb_linear_bf16", x2.data_ptr(), weight.data_ptr(), bptr, y.data_ptr(), M, N, K, _mat(x2, "x"),
+                  _mat(weight, "weight"), _mat(y, "y"), DT[out_dtype], _stream())
+        if residual is not None:
+            if out_dtype != torch.bfloat16:
+                raise TypeError("a fused residual needs bf16 output")
+            vecadd(r2, y, out=y)
     return y.reshape(*x.shape[:-1], N) if out is None else out
 
 

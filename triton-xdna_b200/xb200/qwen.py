@@ -163,14 +163,12 @@ class Qwen2Model:
             qkv = ops.linear(xn, L["qkv_w"], L["qkv_b"])
             ops.rope_kv(qkv, self.cos, self.sin, q_buf, cache.k[i], cache.v[i], B, S, H, KVH, HD, pos)
             ops.attention(q_buf, cache.k[i], cache.v[i], attn, B, S, H, KVH, HD, pos, self.scale)
-            proj = ops.linear(attn, L["o_w"])
-            x = ops.vecadd(x, proj)
+            x = ops.linear(attn, L["o_w"], residual=x)  # o_proj + residual add
             xn = ops.rms_norm(x, L["post_ln"], c.rms_eps)
             gate = ops.linear(xn, L["gate_w"])
             up = ops.linear(xn, L["up_w"])
             h = ops.silu_mul(gate, up)
-            down = ops.linear(h, L["down_w"])
-            x = ops.vecadd(x, down)
+            x = ops.linear(h, L["down_w"], residual=x)  # down_proj + residual add
         cache.length = pos + S
         if last_only:
             x = x.reshape(B, S, D)[:, -1, :]  # strided rows: the norm kernel gathers them
@@ -180,24 +178,71 @@ class Qwen2Model:
         return logits if last_only else logits.reshape(B, S, c.vocab_size)
 
     @torch.no_grad()
-    def generate(self, ids: torch.Tensor, max_new_tokens: int, cache: KVCache | None = None):
+    def generate(self, ids: torch.Tensor, max_new_tokens: int, cache: KVCache | None = None,
+                 graphs: "DecodeGraphs | None" = None):
         """Greedy decoding (model.py:1134-1179), batched.  Returns
         (tokens [B, max_new_tokens] int64 on the device, timing dict with
-        CUDA-event prefill / decode milliseconds)."""
+        CUDA-event prefill / decode milliseconds).  With `graphs` (built by
+        `decode_graphs` for this cache and shape) every decode step replays a
+        captured CUDA graph instead of launching its ~300 kernels from Python."""
         B, S = ids.shape
-        if cache is None:
-            cache = self.new_cache(B, S + max_new_tokens)
-        # step-major token buffer: row `step` holds every sequence's token, so
-        # the argmax writes and the next step's embedding reads are contiguous
-        toks = torch.empty((max_new_tokens, B), dtype=torch.int64, device=self.device)
+        if graphs is not None:
+            cache, toks = graphs.cache, graphs.toks
+            if (graphs.batch, graphs.prompt, graphs.new) != (B, S, max_new_tokens):
+                raise ValueError("decode graphs were captured for another shape")
+        else:
+            if cache is None:
+                cache = self.new_cache(B, S + max_new_tokens)
+            # step-major token buffer: row `step` holds every sequence's token,
+            # so the argmax writes and the next embedding reads are contiguous
+            toks = torch.empty((max_new_tokens, B), dtype=torch.int64, device=self.device)
+        cache.length = 0
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
         logits = self.forward(ids, cache, last_only=True)
         ops.argmax(logits, out=toks[0])
         e1.record()
-        for step in range(1, max_new_tokens):
-            logits = self.forward(toks[step - 1].view(B, 1), cache, last_only=True)
-            ops.argmax(logits, out=toks[step])
+        if graphs is not None:
+            graphs.replay()
+        else:
+            for step in range(1, max_new_tokens):
+                logits = self.forward(toks[step - 1].view(B, 1), cache, last_only=True)
+                ops.argmax(logits, out=toks[step])
         e2.record()
         torch.cuda.synchronize()
         return toks.t(), {"prefill_ms": e0.elapsed_time(e1), "decode_ms": e1.elapsed_time(e2)}
+
+    @torch.no_grad()
+    def decode_graphs(self, batch: int, prompt: int, new: int) -> "DecodeGraphs":
+        return DecodeGraphs(self, batch, prompt, new)
+
+
+class DecodeGraphs:
+    """One captured CUDA graph per decode step (positions are baked into the
+    kernel arguments), sharing one memory pool and replayed in capture order.
+    Owns the KV cache and the token buffer the graphs read and write."""
+
+    def __init__(self, model: Qwen2Model, batch: int, prompt: int, new: int):
+        self.batch, self.prompt, self.new = batch, prompt, new
+        self.cache = model.new_cache(batch, prompt + new)
+        self.toks = torch.zeros((new, batch), dtype=torch.int64, device=model.device)
+        # one eager step first: per-kernel attributes and the small-M
+        # workspace are set up outside any capture
+        self.cache.length = prompt
+        model.forward(self.toks[0].view(batch, 1), self.cache, last_only=True)
+        torch.cuda.synchronize()
+        pool = torch.cuda.graph_pool_handle()
+        self.graphs = []
+        for step in range(1, new):
+            self.cache.length = prompt + step - 1
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                logits = model.forward(self.toks[step - 1].view(batch, 1), self.cache, last_only=True)
+                ops.argmax(logits, out=self.toks[step])
+            self.graphs.append(g)
+        self.cache.length = 0
+
+    def replay(self):
+        for g in self.graphs:
+            g.replay()
+        self.cache.length = self.prompt + self.new - 1
