@@ -240,6 +240,18 @@ XB_API int xb_linear_small_bf16(const void* X, const void* W, const void* bias,
                                 size_t workspace_bytes, void* stream,
                                 char* err, size_t errlen);
 
+/* The decode MLP front half: Y[M, n_out] = silu(X @ Wg^T) * (X @ Wu^T) with
+ * W = [Wg; Wu] ([2*n_out, K], gate rows first), one GEMM over the stacked
+ * weight (the small-M kernel) and the silu*up in its split-K reduction, with
+ * the roundings of the unfused sequence (two bf16 linears, then
+ * xb_silu_mul).  Workspace: the xb_linear_small_plan size for N = 2*n_out.
+ * Replaces model.py:1049-1059 (gate / up linears + `triton_swiglu`). */
+XB_API int xb_linear_small_swiglu_bf16(const void* X, const void* W, void* Y,
+                                       int64_t M, int64_t n_out, int64_t K,
+                                       int64_t ldx, int64_t ldw, int64_t ldy,
+                                       void* workspace, size_t workspace_bytes,
+                                       void* stream, char* err, size_t errlen);
+
 /* ---------------------------------------------------------------------------
  * Qwen2.5 decoder pieces (examples/qwen2_5/model.py:824-1179).
  * ------------------------------------------------------------------------- */
@@ -274,8 +286,17 @@ XB_API int xb_attention_bf16(const void* q, const void* k_cache,
                              const void* v_cache, void* out, int64_t batch,
                              int64_t seq, int64_t n_head, int64_t n_kv_head,
                              int64_t head_dim, int64_t max_seq,
-                             int64_t pos_offset, float scale, void* stream,
-                             char* err, size_t errlen);
+                             int64_t pos_offset, float scale, void* workspace,
+                             size_t workspace_bytes, void* stream, char* err,
+                             size_t errlen);
+
+/* Workspace xb_attention_bf16 needs: the per-chunk partial results of
+ * single-token (seq == 1) attention, split over 128-key chunks of the
+ * context; 0 for seq > 1. */
+XB_API int xb_attention_workspace_size(int64_t batch, int64_t seq,
+                                       int64_t n_head, int64_t n_kv_head,
+                                       int64_t pos_offset, size_t* bytes,
+                                       char* err, size_t errlen);
 
 /* idx[r] = first index of the maximum of x[r, 0:cols] (row pitch ld);
  * NaN counts as the maximum.  Replaces `torch.argmax(logits[..., -1, :])`

@@ -12,6 +12,7 @@
 #include <stdio.h>
 #include <string.h>
 #include <stdarg.h>
+#include <stdlib.h>
 
 #include "../../include/xb200.h"
 
@@ -90,6 +91,51 @@ __device__ __forceinline__ float rcp_approx(float x) {
   float r;
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
+}
+
+// silu(x) = x * sigmoid(x) on the MUFU approximations, for values stored as
+// bf16 (shared by the elementwise kernels and the fused MLP reduction so both
+// round identically).
+__device__ __forceinline__ float silu_bf16path(float x) {
+  return __fmul_rn(x, rcp_approx(1.0f + ex2_approx(x * -1.4426950408889634f)));
+}
+
+// ---- programmatic dependent launch ----------------------------------------
+// Every kernel waits for its predecessor on the stream with pdl_wait() before
+// touching global memory, then lets its own successor begin launching
+// (pdl_trigger).  When a kernel is launched with programmatic stream
+// serialisation (launch_k below), its launch and any prologue placed before
+// pdl_wait() overlap the tail of the previous kernel; correctness is
+// unchanged because griddepcontrol.wait returns only once the prerequisite
+// grid has completed and its memory is visible.  Without the attribute both
+// instructions are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// XB_PDL=0 in the environment turns the overlap off (plain launches).
+inline bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("XB_PDL");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
 // 16-byte vector of T.

@@ -92,7 +92,7 @@ template <typename T> struct OpSigmoid {
 };
 template <typename T> struct OpSilu {
   __device__ __forceinline__ float operator()(float x) const {
-    if constexpr (sizeof(T) == 2) return __fmul_rn(x, sigmoid_t<T>(x));
+    if constexpr (sizeof(T) == 2) return silu_bf16path(x);
     else return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
   }
 };
@@ -113,6 +113,8 @@ template <typename T> struct OpSiluMul {
 template <typename T, typename Op>
 __global__ void __launch_bounds__(kThreads) unary_vec_kernel(const T* __restrict__ x, T* __restrict__ y,
                                                              int64_t nvec, Op op) {
+  pdl_wait();
+  pdl_trigger();
   using V = Vec16<T>;
   const int64_t step = (int64_t)gridDim.x * kThreads * kUnroll;
   for (int64_t base = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x; base < nvec; base += step) {
@@ -138,6 +140,8 @@ __global__ void __launch_bounds__(kThreads) unary_vec_kernel(const T* __restrict
 template <typename T, typename Op>
 __global__ void __launch_bounds__(kThreads) binary_vec_kernel(const T* __restrict__ a, const T* __restrict__ b,
                                                               T* __restrict__ y, int64_t nvec, Op op) {
+  pdl_wait();
+  pdl_trigger();
   using V = Vec16<T>;
   const int64_t step = (int64_t)gridDim.x * kThreads * kUnroll;
   for (int64_t base = (int64_t)blockIdx.x * kThreads * kUnroll + threadIdx.x; base < nvec; base += step) {
@@ -168,12 +172,16 @@ __global__ void __launch_bounds__(kThreads) binary_vec_kernel(const T* __restric
 // and for whole buffers that are not 16-byte aligned.
 template <typename T, typename Op>
 __global__ void unary_scalar_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t begin, int64_t n, Op op) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     y[i] = Cvt<T>::from_f(op(Cvt<T>::to_f(x[i])));
 }
 template <typename T, typename Op>
 __global__ void binary_scalar_kernel(const T* __restrict__ a, const T* __restrict__ b, T* __restrict__ y,
                                      int64_t begin, int64_t n, Op op) {
+  pdl_wait();
+  pdl_trigger();
   for (int64_t i = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     y[i] = Cvt<T>::from_f(op(Cvt<T>::to_f(a[i]), Cvt<T>::to_f(b[i])));
 }
@@ -208,9 +216,9 @@ int launch_unary(const void* xv, void* yv, int64_t n, Op op, cudaStream_t s, con
   constexpr int VN = Vec16<T>::N;
   int64_t nvec = (aligned16(x) && aligned16(y)) ? n / VN : 0;
   if (nvec > 0)
-    unary_vec_kernel<T, Op><<<oneshot_grid(nvec, kThreads * kUnroll), kThreads, 0, s>>>(x, y, nvec, op);
+    launch_k(unary_vec_kernel<T, Op>, oneshot_grid(nvec, kThreads * kUnroll), kThreads, 0, s, x, y, nvec, op);
   if (nvec * VN < n)
-    unary_scalar_kernel<T, Op><<<grid_for(n - nvec * VN, kThreads), kThreads, 0, s>>>(x, y, nvec * VN, n, op);
+    launch_k(unary_scalar_kernel<T, Op>, grid_for(n - nvec * VN, kThreads), kThreads, 0, s, x, y, nvec * VN, n, op);
   return check_launch(what, err, errlen);
 }
 
@@ -226,9 +234,10 @@ int launch_binary(const void* av, const void* bv, void* yv, int64_t n, Op op, cu
   constexpr int VN = Vec16<T>::N;
   int64_t nvec = (aligned16(a) && aligned16(b) && aligned16(y)) ? n / VN : 0;
   if (nvec > 0)
-    binary_vec_kernel<T, Op><<<oneshot_grid(nvec, kThreads * kUnroll), kThreads, 0, s>>>(a, b, y, nvec, op);
+    launch_k(binary_vec_kernel<T, Op>, oneshot_grid(nvec, kThreads * kUnroll), kThreads, 0, s, a, b, y, nvec, op);
   if (nvec * VN < n)
-    binary_scalar_kernel<T, Op><<<grid_for(n - nvec * VN, kThreads), kThreads, 0, s>>>(a, b, y, nvec * VN, n, op);
+    launch_k(binary_scalar_kernel<T, Op>, grid_for(n - nvec * VN, kThreads), kThreads, 0, s, a, b, y, nvec * VN, n,
+             op);
   return check_launch(what, err, errlen);
 }
 

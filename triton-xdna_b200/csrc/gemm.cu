@@ -152,6 +152,10 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
+  // Everything above touched only shared memory, TMEM and the tensor maps in
+  // the kernel parameters: it overlaps the previous kernel on the stream.
+  pdl_wait();
+  pdl_trigger();
 
   auto fail = [&]() {
     atomicExch(&g_gemm_status, XB_ERR_TIMEOUT);
@@ -361,6 +365,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
                                                             int64_t N, const __nv_bfloat16* __restrict__ bias,
                                                             const __nv_bfloat16* __restrict__ residual, int64_t ldr,
                                                             void* __restrict__ y, int64_t ldy) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = M * N;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t m = i / N, n = i - m * N;
@@ -378,15 +384,39 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
   }
 }
 
+// The decode MLP: W stacks the gate rows [0, n_out) over the up rows
+// [n_out, 2 n_out); y[m, f] = bf16(silu(bf16(g)) * bf16(u)) with g, u the
+// split-K sums of gate row f and up row f -- the same roundings as a gate
+// linear, an up linear and the silu*up kernel run one after another.
+__global__ void __launch_bounds__(256) splitk_swiglu_kernel(const float* __restrict__ part, int splits, int64_t M,
+                                                            int64_t n_out, __nv_bfloat16* __restrict__ y,
+                                                            int64_t ldy) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t total = M * n_out;
+  const int64_t slice = M * 2 * n_out;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = i / n_out, f = i - m * n_out;
+    float g = 0.0f, u = 0.0f;
+    for (int s2 = 0; s2 < splits; ++s2) {
+      g += part[(int64_t)s2 * slice + m * 2 * n_out + f];
+      u += part[(int64_t)s2 * slice + m * 2 * n_out + n_out + f];
+    }
+    g = __bfloat162float(__float2bfloat16_rn(g));
+    u = __bfloat162float(__float2bfloat16_rn(u));
+    y[m * ldy + f] = __float2bfloat16_rn(__fmul_rn(silu_bf16path(g), u));
+  }
+}
+
 // Split count for the small-M linear: enough (weight-row tile, K slice)
-// work units to cover the SMs, at least two K blocks per slice.
+// work units to cover the SMs (a slice may be a single 64-wide K block).
 int small_m_splits(int64_t N, int64_t K) {
   const int64_t tiles = (N + 127) / 128;
   const int64_t kblocks = (K + 63) / 64;
   int sms = 148;
   sm_count(&sms);
   int64_t want = (sms + tiles - 1) / tiles;
-  const int64_t cap = kblocks / 2 > 0 ? kblocks / 2 : 1;
+  const int64_t cap = kblocks;
   if (want > cap) want = cap;
   if (want < 1) want = 1;
   const int64_t kps = (kblocks + want - 1) / want;
@@ -396,6 +426,8 @@ int small_m_splits(int64_t N, int64_t K) {
 // int16 -> (high s8, low u8) limb planes, each [rows, cols] with leading dim ldp.
 __global__ void split_i16_kernel(const int16_t* __restrict__ src, int64_t rows, int64_t cols, int64_t lds,
                                  int8_t* __restrict__ hi, uint8_t* __restrict__ lo, int64_t ldp) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = rows * cols;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / cols, c = i - r * cols;
@@ -497,7 +529,7 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   int sms = 148;
   sm_count(&sms);
   const int grid = args.num_tiles < sms ? args.num_tiles : sms;
-  gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS><<<grid, 192, Cf::SMEM, s>>>(maps, args);
+  launch_k(gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS>, grid, 192, Cf::SMEM, s, maps, args);
   return check_launch(what, err, errlen);
 }
 
@@ -549,7 +581,7 @@ int split_launch(const int16_t* src, int64_t rows, int64_t cols, int64_t lds, in
   int64_t grid = (total + 255) / 256;
   if (grid > 148 * 32) grid = 148 * 32;
   if (grid < 1) grid = 1;
-  split_i16_kernel<<<(unsigned)grid, 256, 0, s>>>(src, rows, cols, lds, hi, lo, ldp);
+  launch_k(split_i16_kernel, (unsigned)grid, 256, 0, s, src, rows, cols, lds, hi, lo, ldp);
   return 0;
 }
 
@@ -590,6 +622,7 @@ int run_i16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t
 using namespace xb::gemm;
 using xb::set_err;
 using xb::check_launch;
+using xb::launch_k;
 
 extern "C" int xb_matmul_i8(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda,
                             int64_t ldb, int64_t ldc, void* stream, char* err, size_t errlen) {
@@ -795,15 +828,52 @@ extern "C" int xb_linear_small_bf16(const void* X, const void* W, const void* bi
   int64_t grid = (total + 255) / 256;
   if (grid > 148 * 16) grid = 148 * 16;
   if (out_dtype == XB_DT_BF16)
-    splitk_reduce_kernel<true><<<(unsigned)grid, 256, 0, s>>>(part, splits, M, N,
+    launch_k(splitk_reduce_kernel<true>, (unsigned)grid, 256, 0, s, part, splits, M, N,
                                                                static_cast<const __nv_bfloat16*>(bias),
                                                                static_cast<const __nv_bfloat16*>(residual), ldr, Y,
                                                                ldy);
   else
-    splitk_reduce_kernel<false><<<(unsigned)grid, 256, 0, s>>>(part, splits, M, N,
+    launch_k(splitk_reduce_kernel<false>, (unsigned)grid, 256, 0, s, part, splits, M, N,
                                                                 static_cast<const __nv_bfloat16*>(bias),
                                                                 static_cast<const __nv_bfloat16*>(residual), ldr, Y,
                                                                 ldy);
+  return check_launch(what, err, errlen);
+}
+
+extern "C" int xb_linear_small_swiglu_bf16(const void* X, const void* W, void* Y, int64_t M, int64_t n_out, int64_t K,
+                                           int64_t ldx, int64_t ldw, int64_t ldy, void* workspace,
+                                           size_t workspace_bytes, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_linear_small_swiglu_bf16";
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t N = 2 * n_out;
+  int rc = check_common(X, W, Y, M, N, K, ldx, ldw, ldy + n_out, true, what, err, errlen);
+  if (rc) return rc < 0 ? rc : XB_OK;
+  if (K == 0 || ldy < n_out) {
+    set_err(err, errlen, "%s: bad K or output pitch", what);
+    return XB_ERR_INVALID;
+  }
+  if (!tma_ok(X, ldx, 2) || !tma_ok(W, ldw, 2)) {
+    set_err(err, errlen, "%s: X/W must be 16-byte aligned with row pitches a multiple of 16 bytes", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  int splits = small_m_splits(N, K);
+  const size_t need = (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
+  if (!workspace || workspace_bytes < need) {
+    set_err(err, errlen, "%s: workspace of %zu bytes given, %zu needed", what, workspace_bytes, need);
+    return XB_ERR_INVALID;
+  }
+  Operands op{{W, nullptr}, {X, nullptr}, ldw, ldx};
+  float* part = static_cast<float*>(workspace);
+  rc = launch<kBf16, true, kOutF32, 64, true>(op, part, nullptr, N, M, K, N, s, what, err, errlen, splits, M * N);
+  if (rc) return rc;
+  const int kblocks = (int)((K + 63) / 64);
+  const int kps = (kblocks + splits - 1) / splits;
+  splits = (kblocks + kps - 1) / kps;  // the count launch() used
+  const int64_t total = M * n_out;
+  int64_t grid = (total + 255) / 256;
+  if (grid > 148 * 16) grid = 148 * 16;
+  launch_k(splitk_swiglu_kernel, (unsigned)grid, 256, 0, s, (const float*)part, splits, M, n_out,
+           static_cast<__nv_bfloat16*>(Y), ldy);
   return check_launch(what, err, errlen);
 }
 

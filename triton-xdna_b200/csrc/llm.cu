@@ -29,6 +29,8 @@ typedef __nv_bfloat16 bf16;
 __global__ void __launch_bounds__(256) embedding_kernel(const bf16* __restrict__ table, const int64_t* __restrict__ ids,
                                                         bf16* __restrict__ out, int64_t rows, int64_t dim,
                                                         int64_t vocab, int* __restrict__ bad) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -45,48 +47,42 @@ __global__ void __launch_bounds__(256) embedding_kernel(const bf16* __restrict__
 
 // ----------------------------------------------------------------------------- RoPE + KV write
 
-// One thread per (token, head slot, pair i < D/2).  Head slots [0, H) are
-// queries, [H, H+KVH) keys, [H+KVH, H+2KVH) values (copied unrotated).
+// One CTA per token; thread j of the CTA handles head slot j / (D/2) and pair
+// i = j % (D/2).  Head slots [0, H) are queries, [H, H+KVH) keys,
+// [H+KVH, H+2KVH) values (copied unrotated).
 // x_out[i] = x[i]*cos - x[i+D/2]*sin, x_out[i+D/2] = x[i+D/2]*cos + x[i]*sin,
 // each product and sum rounded separately in fp32 as rope.py:63-66 does.
-__global__ void __launch_bounds__(256) rope_kv_kernel(const bf16* __restrict__ qkv, const float* __restrict__ cos_t,
-                                                      const float* __restrict__ sin_t, bf16* __restrict__ q_out,
-                                                      bf16* __restrict__ k_cache, bf16* __restrict__ v_cache, int B,
-                                                      int S, int H, int KVH, int D, int smax, int pos_offset) {
+__global__ void __launch_bounds__(1024) rope_kv_kernel(const bf16* __restrict__ qkv, const float* __restrict__ cos_t,
+                                                       const float* __restrict__ sin_t, bf16* __restrict__ q_out,
+                                                       bf16* __restrict__ k_cache, bf16* __restrict__ v_cache, int S,
+                                                       int H, int KVH, int D, int smax, int pos_offset) {
+  pdl_wait();
+  pdl_trigger();
   const int half = D / 2;
   const int slots = H + 2 * KVH;
-  const int64_t total = (int64_t)B * S * slots * half;
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
-       idx += (int64_t)gridDim.x * blockDim.x) {
-    const int i = (int)(idx % half);
-    const int64_t r = idx / half;
-    const int slot = (int)(r % slots);
-    const int64_t m = r / slots;  // token row b*S + s
-    const int s = (int)(m % S);
-    const int b = (int)(m / S);
-    const bf16* x = qkv + m * (int64_t)(slots * D) + (int64_t)slot * D;
-    const int pos = pos_offset + s;
+  const int64_t m = blockIdx.x;  // token row b*S + s
+  const int s = (int)(m % S);
+  const int b = (int)(m / S);
+  const int pos = pos_offset + s;
+  const bf16* xrow = qkv + m * (int64_t)(slots * D);
+  const float* cr = cos_t + (int64_t)pos * D;
+  const float* sr = sin_t + (int64_t)pos * D;
+  for (int j = threadIdx.x; j < slots * half; j += blockDim.x) {
+    const int slot = j / half;
+    const int i = j - slot * half;
+    const bf16* x = xrow + slot * D;
     if (slot >= H + KVH) {  // value head: copy
-      const int kh = slot - H - KVH;
-      bf16* dst = v_cache + (((int64_t)b * KVH + kh) * smax + pos) * D;
+      bf16* dst = v_cache + (((int64_t)b * KVH + (slot - H - KVH)) * smax + pos) * D;
       dst[i] = x[i];
       dst[i + half] = x[i + half];
       continue;
     }
     const float x0 = __bfloat162float(x[i]);
     const float x1 = __bfloat162float(x[i + half]);
-    const float c = cos_t[(int64_t)pos * D + i];
-    const float sn = sin_t[(int64_t)pos * D + i];
-    const float c2 = cos_t[(int64_t)pos * D + i + half];
-    const float s2 = sin_t[(int64_t)pos * D + i + half];
-    const float y0 = __fadd_rn(__fmul_rn(x0, c), __fmul_rn(-x1, sn));
-    const float y1 = __fadd_rn(__fmul_rn(x1, c2), __fmul_rn(x0, s2));
-    bf16* dst;
-    if (slot < H) {
-      dst = q_out + (((int64_t)b * H + slot) * S + s) * D;
-    } else {
-      dst = k_cache + (((int64_t)b * KVH + (slot - H)) * smax + pos) * D;
-    }
+    const float y0 = __fadd_rn(__fmul_rn(x0, cr[i]), __fmul_rn(-x1, sr[i]));
+    const float y1 = __fadd_rn(__fmul_rn(x1, cr[i + half]), __fmul_rn(x0, sr[i + half]));
+    bf16* dst = slot < H ? q_out + (((int64_t)b * H + slot) * S + s) * D
+                         : k_cache + (((int64_t)b * KVH + (slot - H)) * smax + pos) * D;
     dst[i] = __float2bfloat16_rn(y0);
     dst[i + half] = __float2bfloat16_rn(y1);
   }
@@ -128,6 +124,8 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const bf16* __restric
                                                            const bf16* __restrict__ vc, bf16* __restrict__ out, int H,
                                                            int KVH, int S, int smax, int pos_offset,
                                                            float scale_log2) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ __align__(16) bf16 sK[kBK][kPad];
   __shared__ __align__(16) bf16 sV[kBK][kPad];
   const int bh = blockIdx.y;
@@ -263,39 +261,45 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const bf16* __restric
 
 // ----------------------------------------------------------------------------- decode attention
 
-// One CTA per (batch, KV head) serves the H/KVH query heads that share it, so
-// each cached key / value row is read once per step.  Every phase is
-// parallel over keys (no serial chain over the context):
-//   1. scores: thread t takes keys t, t+256, ...; q (fp32) is broadcast from
-//      shared memory; scores go to smem [n_rep][total];
-//   2. softmax per head (one warp per head), P rounded to bf16 as the
-//      prefill kernel does;
-//   3. P@V: warp w takes keys w, w+8, ...; lane l owns dims 2l, 2l+1 of every
-//      head; the 8 warps' partial sums are added through shared memory.
-__global__ void __launch_bounds__(256) attn_decode_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
-                                                          const bf16* __restrict__ vc, bf16* __restrict__ out, int H,
-                                                          int KVH, int smax, int total, float scale_log2) {
-  extern __shared__ float dsm[];  // sc [n_rep][total], then red [8][n_rep][kHD]
-  __shared__ float qs[16][kHD];
-  __shared__ float lsum[16];
-  const int b = blockIdx.x, kvh = blockIdx.y;
-  const int n_rep = H / KVH;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* sc = dsm;
-  float* red = dsm + n_rep * total;
-  for (int i = threadIdx.x; i < n_rep * kHD; i += 256) {
-    const int r = i / kHD, d = i % kHD;
-    qs[r][d] = __bfloat162float(q[((int64_t)b * H + kvh * n_rep + r) * kHD + d]);
-  }
-  __syncthreads();
-  const bf16* kp = kc + ((int64_t)(b * KVH + kvh) * smax) * kHD;
-  const bf16* vp = vc + ((int64_t)(b * KVH + kvh) * smax) * kHD;
+// Single-token (decode) attention, split over the context: a CTA handles one
+// (batch, KV head, chunk of 128 keys) for the NREP query heads sharing that
+// KV head, so each cached key / value row is read once per step and a
+// 640-token context at batch 64 spreads over 640 CTAs.
+//   1. scores: thread t takes key t of the chunk (NREP dot products, q
+//      broadcast from shared memory);
+//   2. per head: chunk max m, P = exp2(s - m) rounded to bf16 for P@V (as
+//      the prefill kernel does), l = sum of the unrounded P;
+//   3. P@V: warp w takes keys 32w .. 32w+31, lane l dims 2l, 2l+1;
+// the partial (o, m, l) of each chunk goes to the workspace, and
+// attn_decode_combine_kernel merges the chunks (max-rescaled sums).
+constexpr int kDecChunk = 128;
 
-  for (int key = threadIdx.x; key < total; key += 256) {
-    float acc[16];
+template <int NREP>
+__global__ void __launch_bounds__(128) attn_decode_split_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
+                                                                const bf16* __restrict__ vc, float* __restrict__ ws,
+                                                                int H, int KVH, int smax, int total, int nchunks,
+                                                                float scale_log2) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float qs[NREP][kHD];
+  __shared__ float ps[NREP][kDecChunk];
+  __shared__ float red[4][NREP][kHD];
+  __shared__ float stat[NREP][2];
+  const int b = blockIdx.x, kvh = blockIdx.y, chunk = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int k0 = chunk * kDecChunk;
+  const int nk = min(kDecChunk, total - k0);
+  for (int i = tid; i < NREP * kHD; i += 128)
+    qs[i / kHD][i % kHD] = __bfloat162float(q[((int64_t)b * H + kvh * NREP + i / kHD) * kHD + i % kHD]);
+  __syncthreads();
+  const bf16* kp = kc + ((int64_t)(b * KVH + kvh) * smax + k0) * kHD;
+  const bf16* vp = vc + ((int64_t)(b * KVH + kvh) * smax + k0) * kHD;
+
+  if (tid < nk) {
+    float acc[NREP];
 #pragma unroll
-    for (int r = 0; r < 16; ++r) acc[r] = 0.0f;
-    const int4* krow = reinterpret_cast<const int4*>(kp + (int64_t)key * kHD);
+    for (int r = 0; r < NREP; ++r) acc[r] = 0.0f;
+    const int4* krow = reinterpret_cast<const int4*>(kp + (int64_t)tid * kHD);
 #pragma unroll
     for (int c = 0; c < kHD / 8; ++c) {
       const int4 raw = __ldg(krow + c);
@@ -303,62 +307,93 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const bf16* __restrict
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float kx = __low2float(kv[e]), ky = __high2float(kv[e]);
-        const int d = c * 8 + 2 * e;
 #pragma unroll
-        for (int r = 0; r < 16; ++r)
-          if (r < n_rep) acc[r] += qs[r][d] * kx + qs[r][d + 1] * ky;
+        for (int r = 0; r < NREP; ++r) {
+          const float2 qq = *reinterpret_cast<const float2*>(&qs[r][c * 8 + 2 * e]);
+          acc[r] += qq.x * kx + qq.y * ky;
+        }
       }
     }
 #pragma unroll
-    for (int r = 0; r < 16; ++r)
-      if (r < n_rep) sc[r * total + key] = acc[r] * scale_log2;
+    for (int r = 0; r < NREP; ++r) ps[r][tid] = acc[r] * scale_log2;
+  } else {
+#pragma unroll
+    for (int r = 0; r < NREP; ++r) ps[r][tid] = -INFINITY;
   }
   __syncthreads();
-  for (int r = warp; r < n_rep; r += 8) {
+  for (int r = warp; r < NREP; r += 4) {
     float mx = -INFINITY;
-    for (int k = lane; k < total; k += 32) mx = fmaxf(mx, sc[r * total + k]);
+#pragma unroll
+    for (int j = 0; j < kDecChunk / 32; ++j) mx = fmaxf(mx, ps[r][lane + 32 * j]);
 #pragma unroll
     for (int o_ = 16; o_ > 0; o_ >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o_));
     float sum = 0.0f;
-    for (int k = lane; k < total; k += 32) {
-      const float p = ex2_approx(sc[r * total + k] - mx);
+#pragma unroll
+    for (int j = 0; j < kDecChunk / 32; ++j) {
+      const int k = lane + 32 * j;
+      const float p = k < nk ? ex2_approx(ps[r][k] - mx) : 0.0f;
       sum += p;
-      sc[r * total + k] = __bfloat162float(__float2bfloat16_rn(p));
+      ps[r][k] = __bfloat162float(__float2bfloat16_rn(p));
     }
 #pragma unroll
     for (int o_ = 16; o_ > 0; o_ >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o_);
-    if (lane == 0) lsum[r] = sum;
+    if (lane == 0) {
+      stat[r][0] = mx;
+      stat[r][1] = sum;
+    }
   }
   __syncthreads();
-  float ax[16], ay[16];
+  float ax[NREP], ay[NREP];
 #pragma unroll
-  for (int r = 0; r < 16; ++r) ax[r] = ay[r] = 0.0f;
+  for (int r = 0; r < NREP; ++r) ax[r] = ay[r] = 0.0f;
+  const int kend = min(32 * warp + 32, nk);
 #pragma unroll 4
-  for (int k = warp; k < total; k += 8) {
+  for (int k = 32 * warp; k < kend; ++k) {
     const __nv_bfloat162 vv = reinterpret_cast<const __nv_bfloat162*>(vp + (int64_t)k * kHD)[lane];
     const float vx = __low2float(vv), vy = __high2float(vv);
 #pragma unroll
-    for (int r = 0; r < 16; ++r)
-      if (r < n_rep) {
-        const float p = sc[r * total + k];
-        ax[r] += p * vx;
-        ay[r] += p * vy;
-      }
-  }
-#pragma unroll
-  for (int r = 0; r < 16; ++r)
-    if (r < n_rep) {
-      red[(warp * n_rep + r) * kHD + 2 * lane] = ax[r];
-      red[(warp * n_rep + r) * kHD + 2 * lane + 1] = ay[r];
+    for (int r = 0; r < NREP; ++r) {
+      const float p = ps[r][k];
+      ax[r] += p * vx;
+      ay[r] += p * vy;
     }
-  __syncthreads();
-  for (int i = threadIdx.x; i < n_rep * kHD; i += 256) {
-    const int r = i / kHD, d = i % kHD;
-    float acc = 0.0f;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) acc += red[(w * n_rep + r) * kHD + d];
-    out[((int64_t)b * H + kvh * n_rep + r) * kHD + d] = __float2bfloat16_rn(acc / lsum[r]);
   }
+#pragma unroll
+  for (int r = 0; r < NREP; ++r) {
+    red[warp][r][2 * lane] = ax[r];
+    red[warp][r][2 * lane + 1] = ay[r];
+  }
+  __syncthreads();
+  float* part = ws + ((int64_t)(b * KVH + kvh) * nchunks + chunk) * NREP * (kHD + 2);
+  for (int i = tid; i < NREP * kHD; i += 128) {
+    const int r = i / kHD, d = i % kHD;
+    part[r * (kHD + 2) + d] = red[0][r][d] + red[1][r][d] + red[2][r][d] + red[3][r][d];
+  }
+  if (tid < NREP) {
+    part[tid * (kHD + 2) + kHD] = stat[tid][0];
+    part[tid * (kHD + 2) + kHD + 1] = stat[tid][1];
+  }
+}
+
+// out[b, h, :] = sum_c o_c 2^(m_c - M) / sum_c l_c 2^(m_c - M), M = max_c m_c.
+__global__ void __launch_bounds__(kHD) attn_decode_combine_kernel(const float* __restrict__ ws, bf16* __restrict__ out,
+                                                                  int H, int KVH, int nchunks) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int n_rep = H / KVH;
+  const int kvh = h / n_rep, r = h % n_rep;
+  const float* base = ws + ((int64_t)(b * KVH + kvh) * nchunks) * n_rep * (kHD + 2) + r * (kHD + 2);
+  const int64_t cstride = (int64_t)n_rep * (kHD + 2);
+  float mx = -INFINITY;
+  for (int c = 0; c < nchunks; ++c) mx = fmaxf(mx, base[c * cstride + kHD]);
+  float l = 0.0f, o = 0.0f;
+  for (int c = 0; c < nchunks; ++c) {
+    const float w = ex2_approx(base[c * cstride + kHD] - mx);
+    l += base[c * cstride + kHD + 1] * w;
+    o += base[c * cstride + d] * w;
+  }
+  out[((int64_t)b * H + h) * kHD + d] = __float2bfloat16_rn(o / l);
 }
 
 // ----------------------------------------------------------------------------- argmax
@@ -377,12 +412,44 @@ __device__ __forceinline__ bool better(float v1, int64_t i1, float v2, int64_t i
 // idx[r] = first index of the maximum of logits[r, :].
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ x, int64_t cols, int64_t ld,
                                                       int64_t* __restrict__ idx) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float sv[32];
   __shared__ int64_t si[32];
   const float* row = x + (int64_t)blockIdx.x * ld;
   float best = 0.0f;
   int64_t bi = cols;
-  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+  // 16-byte loads, four in flight per thread, when the row allows it; each
+  // thread still visits its indices in increasing order, so ties keep the
+  // first index.
+  int64_t vec_end = 0;
+  if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    vec_end = cols / 4 * 4;
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    const int64_t n4 = vec_end / 4;
+    for (int64_t base = threadIdx.x; base < n4; base += 4 * (int64_t)blockDim.x) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t i = base + (int64_t)u * blockDim.x;
+        v[u] = i < n4 ? __ldcs(r4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t i = base + (int64_t)u * blockDim.x;
+        if (i < n4) {
+          const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (better(best, bi, e[j], 4 * i + j, cols)) {
+              best = e[j];
+              bi = 4 * i + j;
+            }
+        }
+      }
+    }
+  }
+  for (int64_t c = vec_end + threadIdx.x; c < cols; c += blockDim.x) {
     const float v = row[c];
     if (better(best, bi, v, c, cols)) {
       best = v;
@@ -429,6 +496,7 @@ __device__ int g_bad_token = 0;
 using namespace xb::llm;
 using xb::set_err;
 using xb::check_launch;
+using xb::launch_k;
 
 extern "C" int xb_embedding_bf16(const void* table, const int64_t* ids, void* out, int64_t rows, int64_t dim,
                                  int64_t vocab, void* stream, char* err, size_t errlen) {
@@ -450,8 +518,8 @@ extern "C" int xb_embedding_bf16(const void* table, const int64_t* ids, void* ou
     set_err(err, errlen, "xb_embedding_bf16: status word unavailable");
     return XB_ERR_CUDA;
   }
-  embedding_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream>>>(
-      static_cast<const bf16*>(table), ids, static_cast<bf16*>(out), rows, dim, vocab, bad);
+  launch_k(embedding_kernel, (unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream, static_cast<const bf16*>(table),
+           ids, static_cast<bf16*>(out), rows, dim, vocab, bad);
   return check_launch("xb_embedding_bf16", err, errlen);
 }
 
@@ -474,19 +542,37 @@ extern "C" int xb_rope_kv_bf16(const void* qkv, const float* cos_t, const float*
     set_err(err, errlen, "xb_rope_kv_bf16: null pointer");
     return XB_ERR_INVALID;
   }
-  const int64_t total = batch * seq * (n_head + 2 * n_kv_head) * (head_dim / 2);
-  int64_t grid = (total + 255) / 256;
-  if (grid > 148 * 64) grid = 148 * 64;
-  rope_kv_kernel<<<(unsigned)grid, 256, 0, (cudaStream_t)stream>>>(
-      static_cast<const bf16*>(qkv), cos_t, sin_t, static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache),
-      static_cast<bf16*>(v_cache), (int)batch, (int)seq, (int)n_head, (int)n_kv_head, (int)head_dim, (int)max_seq,
-      (int)pos_offset);
+  const int64_t per_token = (n_head + 2 * n_kv_head) * (head_dim / 2);
+  const int threads = per_token >= 1024 ? 1024 : (int)((per_token + 31) / 32 * 32);
+  if (batch * seq > 0x7fffffffLL) {
+    set_err(err, errlen, "xb_rope_kv_bf16: too many tokens");
+    return XB_ERR_UNSUPPORTED;
+  }
+  launch_k(rope_kv_kernel, (unsigned)(batch * seq), threads, 0, (cudaStream_t)stream, static_cast<const bf16*>(qkv),
+           cos_t, sin_t, static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache), (int)seq,
+           (int)n_head, (int)n_kv_head, (int)head_dim, (int)max_seq, (int)pos_offset);
   return check_launch("xb_rope_kv_bf16", err, errlen);
+}
+
+extern "C" int xb_attention_workspace_size(int64_t batch, int64_t seq, int64_t n_head, int64_t n_kv_head,
+                                           int64_t pos_offset, size_t* bytes, char* err, size_t errlen) {
+  if (!bytes || batch < 0 || seq < 0 || n_head <= 0 || n_kv_head <= 0 || pos_offset < 0) {
+    set_err(err, errlen, "xb_attention_workspace_size: bad arguments");
+    return XB_ERR_INVALID;
+  }
+  if (seq != 1) {
+    *bytes = 0;
+    return XB_OK;
+  }
+  const int64_t nchunks = (pos_offset + 1 + kDecChunk - 1) / kDecChunk;
+  *bytes = (size_t)(batch * n_kv_head * nchunks * (n_head / n_kv_head) * (kHD + 2)) * sizeof(float);
+  return XB_OK;
 }
 
 extern "C" int xb_attention_bf16(const void* q, const void* k_cache, const void* v_cache, void* out, int64_t batch,
                                  int64_t seq, int64_t n_head, int64_t n_kv_head, int64_t head_dim, int64_t max_seq,
-                                 int64_t pos_offset, float scale, void* stream, char* err, size_t errlen) {
+                                 int64_t pos_offset, float scale, void* workspace, size_t workspace_bytes,
+                                 void* stream, char* err, size_t errlen) {
   const char* what = "xb_attention_bf16";
   if (batch < 0 || seq < 0 || n_head <= 0 || n_kv_head <= 0 || n_head % n_kv_head || pos_offset < 0) {
     set_err(err, errlen, "%s: bad shape", what);
@@ -514,26 +600,32 @@ extern "C" int xb_attention_bf16(const void* q, const void* k_cache, const void*
   if (seq == 1) {
     const int total = (int)(pos_offset + 1);
     const int n_rep = (int)(n_head / n_kv_head);
-    if (n_rep > 16) {
-      set_err(err, errlen, "%s: more than 16 query heads per KV head", what);
-      return XB_ERR_UNSUPPORTED;
+    const int nchunks = (total + kDecChunk - 1) / kDecChunk;
+    const size_t need = (size_t)batch * n_kv_head * nchunks * n_rep * (kHD + 2) * sizeof(float);
+    if (!workspace || workspace_bytes < need) {
+      set_err(err, errlen, "%s: decode needs a workspace of %zu bytes (%zu given)", what, need, workspace_bytes);
+      return XB_ERR_INVALID;
     }
-    const size_t smem = ((size_t)n_rep * total + 8 * (size_t)n_rep * kHD) * sizeof(float);
-    if (smem > 200 * 1024) {
-      set_err(err, errlen, "%s: decode context %d too long for the score buffer", what, total);
-      return XB_ERR_UNSUPPORTED;
+    float* ws = static_cast<float*>(workspace);
+    dim3 grid((unsigned)batch, (unsigned)n_kv_head, (unsigned)nchunks);
+    const bf16* qq = static_cast<const bf16*>(q);
+    const bf16* kk = static_cast<const bf16*>(k_cache);
+    const bf16* vv = static_cast<const bf16*>(v_cache);
+    const int Hh = (int)n_head, KV = (int)n_kv_head, SM = (int)max_seq;
+    switch (n_rep) {
+#define XB_DEC(R) \
+  case R: launch_k(attn_decode_split_kernel<R>, grid, 128, 0, s, qq, kk, vv, ws, Hh, KV, SM, total, nchunks, scale_log2); break;
+      XB_DEC(1) XB_DEC(2) XB_DEC(3) XB_DEC(4) XB_DEC(5) XB_DEC(6) XB_DEC(7) XB_DEC(8)
+#undef XB_DEC
+      default:
+        set_err(err, errlen, "%s: %d query heads per KV head not supported (1..8)", what, n_rep);
+        return XB_ERR_UNSUPPORTED;
     }
-    static size_t smem_set = 48 * 1024;
-    if (smem > smem_set) {
-      cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      smem_set = 200 * 1024;
-    }
-    attn_decode_kernel<<<dim3((unsigned)batch, (unsigned)n_kv_head), 256, smem, s>>>(
-        static_cast<const bf16*>(q), static_cast<const bf16*>(k_cache), static_cast<const bf16*>(v_cache),
-        static_cast<bf16*>(out), (int)n_head, (int)n_kv_head, (int)max_seq, total, scale_log2);
+    launch_k(attn_decode_combine_kernel, dim3((unsigned)batch, (unsigned)n_head), kHD, 0, s, (const float*)ws,
+             static_cast<bf16*>(out), Hh, KV, nchunks);
   } else {
     dim3 grid((unsigned)((seq + kBQ - 1) / kBQ), (unsigned)(batch * n_head));
-    attn_prefill_kernel<<<grid, 128, 0, s>>>(static_cast<const bf16*>(q), static_cast<const bf16*>(k_cache),
+    launch_k(attn_prefill_kernel, grid, 128, 0, s, static_cast<const bf16*>(q), static_cast<const bf16*>(k_cache),
                                              static_cast<const bf16*>(v_cache), static_cast<bf16*>(out),
                                              (int)n_head, (int)n_kv_head, (int)seq, (int)max_seq, (int)pos_offset,
                                              scale_log2);
@@ -552,6 +644,6 @@ extern "C" int xb_argmax_f32(const float* x, int64_t rows, int64_t cols, int64_t
     set_err(err, errlen, "xb_argmax_f32: null pointer");
     return XB_ERR_INVALID;
   }
-  argmax_kernel<<<(unsigned)rows, 1024, 0, (cudaStream_t)stream>>>(x, cols, ld, idx);
+  launch_k(argmax_kernel, (unsigned)rows, 1024, 0, (cudaStream_t)stream, x, cols, ld, idx);
   return check_launch("xb_argmax_f32", err, errlen);
 }

@@ -14,6 +14,8 @@ namespace {
 template <typename T>
 __global__ void __launch_bounds__(256) pool_vec_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t planes,
                                                        int64_t h, int64_t w, int64_t oh, int64_t ow) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int VN = Vec16<T>::N;
   const int64_t ovr = ow / VN;  // output vectors per output row
   const int64_t total = planes * oh * ovr;
@@ -46,6 +48,8 @@ __global__ void __launch_bounds__(256) pool_vec_kernel(const T* __restrict__ x, 
 template <typename T>
 __global__ void __launch_bounds__(256) pool_scalar_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t planes,
                                                           int64_t h, int64_t w, int64_t oh, int64_t ow) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t total = planes * oh * ow;
   for (int64_t o = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < total; o += (int64_t)gridDim.x * blockDim.x) {
     const int64_t oj = o % ow;
@@ -74,11 +78,11 @@ int run_pool(const void* xv, void* yv, int64_t planes, int64_t h, int64_t w, cud
   if (w % (2 * VN) == 0 && ow % VN == 0 && aligned16(x) && aligned16(y)) {
     int64_t total = planes * oh * (ow / VN);
     int64_t grid = (total + 255) / 256;
-    pool_vec_kernel<T><<<(unsigned)(grid < cap ? grid : cap), 256, 0, s>>>(x, y, planes, h, w, oh, ow);
+    launch_k(pool_vec_kernel<T>, (unsigned)(grid < cap ? grid : cap), 256, 0, s, x, y, planes, h, w, oh, ow);
   } else {
     int64_t total = planes * oh * ow;
     int64_t grid = (total + 255) / 256;
-    pool_scalar_kernel<T><<<(unsigned)(grid < cap ? grid : cap), 256, 0, s>>>(x, y, planes, h, w, oh, ow);
+    launch_k(pool_scalar_kernel<T>, (unsigned)(grid < cap ? grid : cap), 256, 0, s, x, y, planes, h, w, oh, ow);
   }
   return check_launch("xb_avg_pool2d_2x2", err, errlen);
 }

@@ -66,6 +66,8 @@ __device__ __forceinline__ float group_reduce(float v, float* red) {
 
 template <typename T, int GROUP, int VPT, int OP>
 __global__ void __launch_bounds__(GROUP > 32 ? GROUP : 256) row_vec_kernel(RowArgs a) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int VN = Vec16<T>::N;
   constexpr int CTA = GROUP > 32 ? GROUP : 256;
   constexpr int RPC = CTA / GROUP;
@@ -200,6 +202,8 @@ __global__ void __launch_bounds__(GROUP > 32 ? GROUP : 256) row_vec_kernel(RowAr
 // strided walk of the row, then a second walk writes the output.
 template <typename T, int OP>
 __global__ void __launch_bounds__(256) row_generic_kernel(RowArgs a) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float red[8];
   const int64_t row = blockIdx.x;
   const T* xr = static_cast<const T*>(a.x) + row * a.xs;
@@ -258,7 +262,7 @@ void launch_vec(const RowArgs& a, cudaStream_t s) {
   constexpr int CTA = GROUP > 32 ? GROUP : 256;
   constexpr int RPC = CTA / GROUP;
   const int64_t grid = (a.rows + RPC - 1) / RPC;
-  row_vec_kernel<T, GROUP, VPT, OP><<<(unsigned)grid, CTA, 0, s>>>(a);
+  launch_k(row_vec_kernel<T, GROUP, VPT, OP>, (unsigned)grid, CTA, 0, s, a);
 }
 
 // Pick (GROUP, VPT) for a row of nvec vectors; returns false if the row does
@@ -266,6 +270,17 @@ void launch_vec(const RowArgs& a, cudaStream_t s) {
 template <typename T, int OP>
 bool dispatch_vec(const RowArgs& a, int64_t nvec, cudaStream_t s) {
   constexpr int MAXV = sizeof(T) == 2 ? 4 : 8;  // at most 32 fp32 values per thread
+  // The configuration depends on the row length only, never on the row
+  // count, so a row is reduced in the same order whatever the batch (batch
+  // invariance).  Rows of 33..256 vectors (e.g. the 896-wide hidden state of
+  // Qwen2.5-0.5B) get one row per CTA, which also spreads the few rows of a
+  // decode step over the SMs.
+  if (nvec > 32 && nvec <= 256) {
+    if (nvec <= 64) { launch_vec<T, 64, 1, OP>(a, s); return true; }
+    if (nvec <= 128) { launch_vec<T, 128, 1, OP>(a, s); return true; }
+    launch_vec<T, 128, 2, OP>(a, s);
+    return true;
+  }
   if (nvec <= 32 * MAXV) {
     int g = 4;
     while (g * MAXV < nvec) g *= 2;
@@ -312,7 +327,7 @@ int run_row(const RowArgs& a, cudaStream_t s, const char* what, char* err, size_
   const bool vec_ok = a.cols % VN == 0 && a.xs % VN == 0 && a.ys % VN == 0 && aligned16(a.x) && aligned16(a.y) &&
                       (!a.w || aligned16(a.w)) && (!a.b || aligned16(a.b));
   if (!(vec_ok && dispatch_vec<T, OP>(a, a.cols / VN, s)))
-    row_generic_kernel<T, OP><<<(unsigned)a.rows, 256, 0, s>>>(a);
+    launch_k(row_generic_kernel<T, OP>, (unsigned)a.rows, 256, 0, s, a);
   return check_launch(what, err, errlen);
 }
 

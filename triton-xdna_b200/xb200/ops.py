@@ -397,6 +397,26 @@ def linear(x, weight, bias=None, out=None, out_dtype=torch.bfloat16, residual=No
     return y.reshape(*x.shape[:-1], N) if out is None else out
 
 
+def linear_swiglu(x, w_gate_up):
+    """silu(x @ Wg^T) * (x @ Wu^T) for few tokens, W = [Wg; Wu] stacked
+    ([2*n_out, K]); the same roundings as two linears then silu_mul."""
+    _cuda(x, w_gate_up)
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    N = w_gate_up.shape[0]
+    if N % 2 or w_gate_up.shape[1] != K:
+        raise ValueError("w_gate_up must be [2*n_out, K]")
+    splits = ctypes.c_int(0)
+    need = ctypes.c_size_t(0)
+    _lib.call("xb_linear_small_plan", M, N, K, 1, ctypes.byref(splits), ctypes.byref(need))
+    ws = _workspace(x.device, need.value)
+    y = torch.empty((M, N // 2), dtype=torch.bfloat16, device=x.device)
+    _lib.call("xb_linear_small_swiglu_bf16", x2.data_ptr(), w_gate_up.data_ptr(), y.data_ptr(), M, N // 2, K,
+              _mat(x2, "x"), _mat(w_gate_up, "w"), N // 2, ws.data_ptr(), ws.numel() * 4, _stream())
+    return y.reshape(*x.shape[:-1], N // 2)
+
+
 def device_status() -> int:
     """Read and clear the device status word (0 = fine, -4 = a kernel timed out)."""
     st = ctypes.c_int(0)
@@ -435,8 +455,12 @@ def rope_kv(qkv, cos_t, sin_t, q_out, k_cache, v_cache, batch, seq, n_head, n_kv
 def attention(q, k_cache, v_cache, out, batch, seq, n_head, n_kv_head, head_dim, pos_offset, scale):
     """Causal GQA attention over the cache (kernels/attention.py:27-122)."""
     _cuda(q, k_cache, v_cache, out)
+    need = ctypes.c_size_t(0)
+    _lib.call("xb_attention_workspace_size", batch, seq, n_head, n_kv_head, pos_offset, ctypes.byref(need))
+    ws = _workspace(q.device, need.value) if need.value else None
     _lib.call("xb_attention_bf16", q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), batch, seq,
-              n_head, n_kv_head, head_dim, k_cache.shape[2], pos_offset, float(scale), _stream())
+              n_head, n_kv_head, head_dim, k_cache.shape[2], pos_offset, float(scale),
+              ws.data_ptr() if ws is not None else None, ws.numel() * 4 if ws is not None else 0, _stream())
     return out
 
 

@@ -127,10 +127,15 @@ class Qwen2Model:
                 "qkv_b": torch.cat([t(f"{p}.self_attn.q_proj.bias"), t(f"{p}.self_attn.k_proj.bias"),
                                     t(f"{p}.self_attn.v_proj.bias")], 0).contiguous(),
                 "o_w": t(f"{p}.self_attn.o_proj.weight"),
-                "gate_w": t(f"{p}.mlp.gate_proj.weight"),
-                "up_w": t(f"{p}.mlp.up_proj.weight"),
+                # gate rows stacked over up rows: one GEMM in the decode step;
+                # prefill uses the two halves (views, no copy) as separate linears
+                "gate_up_w": torch.cat([t(f"{p}.mlp.gate_proj.weight"), t(f"{p}.mlp.up_proj.weight")],
+                                       0).contiguous(),
                 "down_w": t(f"{p}.mlp.down_proj.weight"),
             })
+            L = self.layers[-1]
+            L["gate_w"] = L["gate_up_w"][: c.intermediate]
+            L["up_w"] = L["gate_up_w"][c.intermediate:]
         self.norm_w = t("model.norm.weight")
         cos, sin = rope_tables(c.head_dim, rope_len or c.max_seq_len, c.rope_theta)
         self.cos = cos.to(dev).contiguous()
@@ -165,9 +170,10 @@ class Qwen2Model:
             ops.attention(q_buf, cache.k[i], cache.v[i], attn, B, S, H, KVH, HD, pos, self.scale)
             x = ops.linear(attn, L["o_w"], residual=x)  # o_proj + residual add
             xn = ops.rms_norm(x, L["post_ln"], c.rms_eps)
-            gate = ops.linear(xn, L["gate_w"])
-            up = ops.linear(xn, L["up_w"])
-            h = ops.silu_mul(gate, up)
+            if M <= ops.SMALL_M:
+                h = ops.linear_swiglu(xn, L["gate_up_w"])  # gate + up + silu*up, one GEMM
+            else:
+                h = ops.silu_mul(ops.linear(xn, L["gate_w"]), ops.linear(xn, L["up_w"]))
             x = ops.linear(h, L["down_w"], residual=x)  # down_proj + residual add
         cache.length = pos + S
         if last_only:
