@@ -323,6 +323,73 @@ def qwen_cpu_baseline(cfg):
             "sample": "1 sequence: 128-token prefill + 4 greedy decode steps through the oracle forward"}
 
 
+def run_gemm_sharded_bench(args, world, rank, local, dev):
+    """N-sharded GEMMs over `world` GPUs: the fused kernel (GEMM epilogue
+    stores into every rank's C over NVLink) and the NCCL all-gather baseline,
+    each timed with CUDA events on every rank (max over ranks); TOPS counts
+    the whole M x N x K product."""
+    from xb200.dist import ShardedMatmul, nccl_sharded_matmul, shard_columns
+
+    peaks = _peaks()
+    peaks["i8_tops"] = 4500.0
+    stream = torch.cuda.current_stream()
+    sizes = [(4096, 4096, 4096), (8192, 8192, 8192), (16384, 16384, 16384), (16, 8192, 8192)]
+    res = {}
+    with ClockSampler(local) as clk:
+        for dt in (torch.int8, torch.bfloat16):
+            for (M, N, K) in sizes:
+                if args.only and args.only not in f"{M}":
+                    continue
+                g = torch.Generator(device=dev).manual_seed(0)
+                if dt == torch.int8:
+                    a = torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=dt)
+                    b = torch.randint(-128, 128, (K, N), generator=g, device=dev, dtype=dt)
+                else:
+                    a = torch.randn((M, K), generator=g, device=dev).to(dt)
+                    b = torch.randn((K, N), generator=g, device=dev).to(dt)
+                s0, ns = shard_columns(N, world)[rank]
+                bs = b[:, s0:s0 + ns].contiguous()
+                del b
+                sm = ShardedMatmul(M, N, K, dt)
+                tag = "i8" if dt == torch.int8 else "bf16"
+                for name, fn in ((f"sharded_fused_{tag}_{M}x{N}x{K}", lambda: sm.run(a, bs)),
+                                 (f"sharded_nccl_{tag}_{M}x{N}x{K}", lambda: nccl_sharded_matmul(a, bs))):
+                    for _ in range(max(3, args.warmup)):
+                        fn()
+                    times = []
+                    for _ in range(max(3, args.steps // 3)):
+                        _barrier(world)
+                        torch.cuda.synchronize()
+                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                        e0.record(stream)
+                        fn()
+                        e1.record(stream)
+                        torch.cuda.synchronize()
+                        times.append(_max_over_ranks(e0.elapsed_time(e1), world))
+                    ms = statistics.median(times)
+                    tops = 2 * M * N * K / (ms * 1e-3) / 1e12
+                    pk = peaks["i8_tops"] if tag == "i8" else peaks["bf16_tflops"]
+                    res[name] = {"ms": round(ms, 4), "tops": round(tops, 1), "frac_of_world_peak":
+                                 round(tops / (pk * world), 3)}
+                st = sm.status()
+                if st != 0:
+                    raise RuntimeError(f"peer wait timed out (status {st})")
+                sm.close()
+                del a, bs
+                torch.cuda.empty_cache()
+    big = "sharded_fused_bf16_16384x16384x16384"
+    if rank == 0:
+        print(json.dumps({
+            "metric": "GEMM TOPS (N-sharded, all-gather of C fused into the epilogue)",
+            "value": res.get(big, {}).get("tops"), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "i8/bf16", "data": "synthetic, seed 0",
+            "config": {"workload": "GEMM M=N=K in {4096, 8192, 16384} + 16x8192x8192, N-sharded, full C on every rank",
+                       "parallelism": f"N-shard x{world}, peer-store all-gather over NVLink (NCCL path timed beside)"},
+            "ops": res, "clocks": clk.summary(),
+        }))
+
+
 def run_gemm_bench(args, ops_list, config, world, rank, local, dev):
     """Per-GEMM timing: L2 flush, then CUDA events around each launch; the
     cuBLAS bf16 / int8 GEMMs are timed the same way as reference lines."""
@@ -624,7 +691,10 @@ def main():
         return
     ops_list, config, metric, dtype = WORKLOADS[args.workload](dev, args.elements, rank, want_e2e)
     if args.workload == "gemm":
-        run_gemm_bench(args, ops_list, config, world, rank, local, dev)
+        if world > 1:
+            run_gemm_sharded_bench(args, world, rank, local, dev)
+        else:
+            run_gemm_bench(args, ops_list, config, world, rank, local, dev)
         if world > 1:
             import torch.distributed as dist
 

@@ -253,6 +253,47 @@ XB_API int xb_linear_small_swiglu_bf16(const void* X, const void* W, void* Y,
                                        void* stream, char* err, size_t errlen);
 
 /* ---------------------------------------------------------------------------
+ * N-sharded GEMM across the GPUs of one node (one process per GPU).  The
+ * reference runs on one device; this is the multi-GPU form of its GEMM
+ * (examples/matmul_*), with the all-gather of C fused into the epilogue.
+ * ------------------------------------------------------------------------- */
+
+/* cudaMalloc `bytes` (zeroed) and export a 64-byte CUDA IPC handle for it. */
+XB_API int xb_peer_alloc(size_t bytes, void** ptr, void* ipc_handle,
+                         char* err, size_t errlen);
+/* Map a peer's allocation from its IPC handle (NVLink peer access). */
+XB_API int xb_peer_open(const void* ipc_handle, void** ptr, char* err,
+                        size_t errlen);
+XB_API int xb_peer_close(void* ptr, char* err, size_t errlen);
+XB_API int xb_peer_free(void* ptr, char* err, size_t errlen);
+
+/* This rank computes C[:, rank*N_shard : (rank+1)*N_shard] = A[M,K] @
+ * B_shard[K,N_shard] (int8 -> int32, or bf16 -> bf16 with fp32
+ * accumulation) and stores every output tile into the C of EVERY rank
+ * (C_ranks[r]: rank r's C [M, ldc] as mapped in this process) with plain
+ * stores over NVLink; when its grid is done it adds 1 to slot `rank` of every
+ * peer's signal buffer (signal_ranks[r]: uint64 [world + 1], zero-initialised
+ * peer memory).  Wait for the peers with xb_peer_wait.  The caller must make
+ * sure no rank still reads the previous contents of C.  world <= 8. */
+XB_API int xb_matmul_sharded(const void* A, const void* B_shard,
+                             void* const* C_ranks, void* const* signal_ranks,
+                             int world, int rank, int64_t M, int64_t N_shard,
+                             int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
+                             int dtype, void* stream, char* err,
+                             size_t errlen);
+
+/* Enqueue a wait until every other rank's slot in this rank's signal buffer
+ * reaches `epoch` (the number of sharded GEMMs issued so far); gives up
+ * after timeout_ns and records XB_ERR_TIMEOUT (read with xb_peer_status). */
+XB_API int xb_peer_wait(const uint64_t* signal, int world, int rank,
+                        uint64_t epoch, uint64_t timeout_ns, void* stream,
+                        char* err, size_t errlen);
+
+/* Read (synchronising `stream`) and clear the peer-wait status word. */
+XB_API int xb_peer_status(void* stream, int* status, char* err,
+                          size_t errlen);
+
+/* ---------------------------------------------------------------------------
  * Qwen2.5 decoder pieces (examples/qwen2_5/model.py:824-1179).
  * ------------------------------------------------------------------------- */
 

@@ -92,6 +92,12 @@ struct Args {
   int m, n, k;
   int tiles_m, tiles_n, num_tiles, kblocks;
   int splits, kps;  // split-K: `splits` slices of `kps` K blocks each
+  // N-sharded GEMM over the GPUs of a node: the epilogue stores every tile
+  // into each rank's C (peer pointers, this rank's column block), and the
+  // grid's last CTA signals every peer.
+  int world, rank;
+  void* peers[8];
+  uint64_t* signals[8];  // each rank's signal buffer (uint64 [world + 1])
 };
 
 constexpr int kGroupM = 16;  // tile raster: groups of 16 M-tiles sweep N (L2 reuse)
@@ -108,7 +114,11 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 
 // TRANS: the epilogue stores C^T (element (r, c) of the tile product at
 // c * ldc + r); with A = W and B = X this computes Y = X W^T for few tokens.
-template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false>
+__device__ __forceinline__ void red_release_sys_add(uint64_t* p, uint64_t v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false>
 __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Maps maps, const Args args) {
   using C = Cfg<KIND, B_KMAJOR, BN_>;
   extern __shared__ uint8_t smem_raw[];
@@ -313,8 +323,12 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
             for (int j = 0; j < 32; ++j)
               if (col0 + j < args.n) cp[(int64_t)(col0 + j) * args.ldc] = v[j];
           }
-        } else if constexpr (OUT == kOutBf16) {
-          __nv_bfloat16* cp = static_cast<__nv_bfloat16*>(args.c) + slice + (int64_t)row * args.ldc + col0;
+        } else {
+#pragma unroll 1
+         for (int pe = 0; pe < (PEERS ? args.world : 1); ++pe) {
+          void* cbase = PEERS ? args.peers[pe] : args.c;
+          if constexpr (OUT == kOutBf16) {
+          __nv_bfloat16* cp = static_cast<__nv_bfloat16*>(cbase) + slice + (int64_t)row * args.ldc + col0;
           if (col0 + 32 <= args.n && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
 #pragma unroll
             for (int j = 0; j < 32; j += 8) {
@@ -329,8 +343,8 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
             for (int j = 0; j < 32; ++j)
               if (col0 + j < args.n) cp[j] = __float2bfloat16_rn(__uint_as_float(v[j]));
           }
-        } else {
-          uint32_t* cp = static_cast<uint32_t*>(args.c) + slice + (int64_t)row * args.ldc + col0;
+          } else {
+          uint32_t* cp = static_cast<uint32_t*>(cbase) + slice + (int64_t)row * args.ldc + col0;
           if (col0 + 32 <= args.n && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4)
@@ -340,6 +354,8 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
             for (int j = 0; j < 32; ++j)
               if (col0 + j < args.n) cp[j] = v[j];
           }
+          }
+         }
         }
       }
       tc_fence_before();
@@ -347,7 +363,20 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
     }
   }
 
+  if constexpr (PEERS) __threadfence_system();  // this thread's peer stores, before the CTA is counted done
   __syncthreads();
+  if constexpr (PEERS) {
+    if (threadIdx.x == 0 && !abort_flag) {
+      uint64_t* done = args.signals[args.rank] + args.world;
+      const unsigned long long prev = atomicAdd(reinterpret_cast<unsigned long long*>(done), 1ull);
+      if (prev == gridDim.x - 1) {  // last CTA of the grid: every tile of this rank has landed everywhere
+        __threadfence_system();
+        for (int pe = 0; pe < args.world; ++pe)
+          if (pe != args.rank) red_release_sys_add(args.signals[pe] + args.rank, 1ull);
+        *done = 0;  // no CTA of this grid touches it again; ready for the next call
+      }
+    }
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -486,9 +515,16 @@ struct Operands {
   int64_t lda, ldb;
 };
 
-template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false>
+struct PeerArgs {
+  int world = 1, rank = 0;
+  void* peers[8] = {nullptr};
+  uint64_t* signals[8] = {nullptr};
+};
+
+template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false>
 int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
-           cudaStream_t s, const char* what, char* err, size_t errlen, int splits = 1, int64_t split_stride = 0) {
+           cudaStream_t s, const char* what, char* err, size_t errlen, int splits = 1, int64_t split_stride = 0,
+           const PeerArgs* pa = nullptr) {
   using Cf = Cfg<KIND, B_KMAJOR, BN_>;
   const CUtensorMapDataType dt = KIND == kBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   Maps maps;
@@ -516,9 +552,15 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   args.splits = (args.kblocks + args.kps - 1) / args.kps;  // every slice gets at least one K block
   args.split_stride = split_stride;
   args.num_tiles = args.tiles_m * args.tiles_n * args.splits;
+  args.world = pa ? pa->world : 1;
+  args.rank = pa ? pa->rank : 0;
+  for (int i = 0; i < 8; ++i) {
+    args.peers[i] = pa ? pa->peers[i] : nullptr;
+    args.signals[i] = pa ? pa->signals[i] : nullptr;
+  }
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS, PEERS>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
     if (e != cudaSuccess) {
       set_err(err, errlen, "%s: cudaFuncSetAttribute: %s", what, cudaGetErrorString(e));
@@ -529,7 +571,7 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   int sms = 148;
   sm_count(&sms);
   const int grid = args.num_tiles < sms ? args.num_tiles : sms;
-  launch_k(gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS>, grid, 192, Cf::SMEM, s, maps, args);
+  launch_k(gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS, PEERS>, grid, 192, Cf::SMEM, s, maps, args);
   return check_launch(what, err, errlen);
 }
 
@@ -875,6 +917,56 @@ extern "C" int xb_linear_small_swiglu_bf16(const void* X, const void* W, void* Y
   launch_k(splitk_swiglu_kernel, (unsigned)grid, 256, 0, s, (const float*)part, splits, M, n_out,
            static_cast<__nv_bfloat16*>(Y), ldy);
   return check_launch(what, err, errlen);
+}
+
+extern "C" int xb_matmul_sharded(const void* A, const void* B_shard, void* const* C_ranks, void* const* signal_ranks,
+                                 int world, int rank, int64_t M, int64_t N_shard, int64_t K, int64_t lda, int64_t ldb,
+                                 int64_t ldc, int dtype, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_matmul_sharded";
+  cudaStream_t s = (cudaStream_t)stream;
+  if (world < 1 || world > 8 || rank < 0 || rank >= world || !C_ranks || !signal_ranks) {
+    set_err(err, errlen, "%s: world must be 1..8 with a C and a signal pointer per rank", what);
+    return XB_ERR_INVALID;
+  }
+  if (ldc < (int64_t)world * N_shard) {
+    set_err(err, errlen, "%s: ldc %lld shorter than world * N_shard", what, (long long)ldc);
+    return XB_ERR_INVALID;
+  }
+  if (dtype != XB_DT_I8 && dtype != XB_DT_BF16) {
+    set_err(err, errlen, "%s: dtype must be int8 or bf16", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  if (M <= 0 || N_shard <= 0 || K <= 0) {
+    set_err(err, errlen, "%s: M, N_shard and K must be positive", what);
+    return XB_ERR_INVALID;
+  }
+  const int esz = dtype == XB_DT_I8 ? 1 : 2;
+  const int osz = dtype == XB_DT_I8 ? 4 : 2;
+  int rc = check_common(A, B_shard, C_ranks[rank], M, N_shard, K, lda, ldb, ldc, false, what, err, errlen);
+  if (rc) return rc < 0 ? rc : XB_OK;
+  if (!tma_ok(A, lda, esz) || !tma_ok(B_shard, ldb, esz)) {
+    set_err(err, errlen, "%s: A/B must be 16-byte aligned with row pitches a multiple of 16 bytes", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  PeerArgs pa;
+  pa.world = world;
+  pa.rank = rank;
+  for (int r = 0; r < world; ++r) {
+    if (!C_ranks[r] || !signal_ranks[r]) {
+      set_err(err, errlen, "%s: null peer pointer for rank %d", what, r);
+      return XB_ERR_INVALID;
+    }
+    // this rank's column block inside rank r's C
+    pa.peers[r] = static_cast<char*>(C_ranks[r]) + (size_t)rank * N_shard * osz;
+    pa.signals[r] = static_cast<uint64_t*>(signal_ranks[r]);
+  }
+  Operands op{{A, nullptr}, {B_shard, nullptr}, lda, ldb};
+  void* local = pa.peers[rank];
+  if (dtype == XB_DT_I8)
+    return launch<kInt8, false, kOutI32, 0, false, true>(op, local, nullptr, M, N_shard, K, ldc, s, what, err, errlen,
+                                                          1, 0, &pa);
+  return launch<kBf16, false, kOutBf16, 0, false, true>(op, local, nullptr, M, N_shard, K, ldc, s, what, err, errlen,
+                                                         1, 0, &pa);
 }
 
 extern "C" int xb_device_status(void* stream, int* status, char* err, size_t errlen) {

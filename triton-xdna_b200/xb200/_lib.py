@@ -43,6 +43,8 @@ _CTYPES = {
     "void*": ctypes.c_void_p,
     "const void*": ctypes.c_void_p,
     "void* const*": ctypes.c_void_p,
+    "void**": ctypes.POINTER(ctypes.c_void_p),
+    "const uint64_t*": ctypes.c_void_p,
     "int": ctypes.c_int,
     # host out-parameters (passed with ctypes.byref)
     "int*": ctypes.POINTER(ctypes.c_int),
