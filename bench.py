@@ -183,9 +183,14 @@ def gemm_workload(dev, n: int, seed: int, host: bool):
     g = torch.Generator(device=dev).manual_seed(seed)
     sizes = [s for s in GEMM_SIZES if max(s) <= max(n, 256)] if n != N28 else GEMM_SIZES
     out = []
-    for dt in ("i8", "i16", "bf16"):
+    for dt in ("i8", "i8nt", "i16", "bf16"):
         for (M, N, K) in sizes:
             def make(M=M, N=N, K=K, dt=dt):
+                if dt == "i8nt":  # int8 linear: W [N, K] (K-major B)
+                    a = torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+                    w = torch.randint(-128, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+                    c = torch.empty((M, N), dtype=torch.int32, device=dev)
+                    return lambda: X.linear_i8(a, w, out=c), (a, w, c)
                 if dt == "i8":
                     a = torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
                     b = torch.randint(-128, 128, (K, N), generator=g, device=dev, dtype=torch.int8)
@@ -202,7 +207,7 @@ def gemm_workload(dev, n: int, seed: int, host: bool):
                 c = torch.empty((M, N), dtype=torch.bfloat16, device=dev)
                 return lambda: X.matmul_bf16(a, b, torch.bfloat16, out=c), (a, b, c)
 
-            eb = {"i8": 1, "i16": 2, "bf16": 2}[dt]
+            eb = {"i8": 1, "i8nt": 1, "i16": 2, "bf16": 2}[dt]
             ob = 2 if dt == "bf16" else 4
             op = Op(f"gemm_{dt}_{M}x{N}x{K}", (M * K + K * N) * eb + M * N * ob, None, flops=2 * M * N * K,
                     peak_key="bf16_tflops" if dt == "bf16" else "i8_tops")

@@ -164,6 +164,13 @@ XB_API int xb_matmul_i8(const void* A, const void* B, void* C, int64_t M,
                         int64_t N, int64_t K, int64_t lda, int64_t ldb,
                         int64_t ldc, void* stream, char* err, size_t errlen);
 
+/* Y[M,N] (int32) = X[M,K] (int8) @ W[N,K]^T (int8), W in nn.Linear layout
+ * (K-major): the int8 linear layer; exact.  The reference's int8 GEMM with
+ * its B operand given transposed (examples/matmul_i8_m128_n64_k64). */
+XB_API int xb_linear_i8(const void* X, const void* W, void* Y, int64_t M,
+                        int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                        int64_t ldy, void* stream, char* err, size_t errlen);
+
 /* Bytes of device workspace xb_matmul_i16 needs for an M x N x K product.
  * The reference has int16 GEMM only as a README claim (README.md:21) with an
  * i32 accumulator (amd_triton_npu/backend/matmul_transform.py:62-64). */

@@ -222,3 +222,11 @@ def test_small_m_swiglu_equals_unfused(M):
     # differ in the last bits: compare at bf16 level, and exactly where they agree
     torch.testing.assert_close(fused.float(), unfused.float(), atol=1e-3, rtol=2 ** -7)
     assert (fused == unfused).float().mean().item() > 0.95
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 128), (300, 640, 4096), (16, 8192, 512)])
+def test_linear_i8_exact(M, N, K):
+    x = _rand_int((M, K), -128, 128, torch.int8, M)
+    w = _rand_int((N, K), -128, 128, torch.int8, N)
+    y = ops.linear_i8(x.cuda(), w.cuda())
+    assert torch.equal(y.cpu(), cgemm.gemm_int(x, w.t().contiguous()))

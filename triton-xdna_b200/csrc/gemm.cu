@@ -681,6 +681,21 @@ extern "C" int xb_matmul_i8(const void* A, const void* B, void* C, int64_t M, in
   return launch<kInt8, false, kOutI32>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
 }
 
+extern "C" int xb_linear_i8(const void* X, const void* W, void* Y, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                            int64_t ldw, int64_t ldy, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_linear_i8";
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc = check_common(X, W, Y, M, N, K, ldx, ldw, ldy, true, what, err, errlen);
+  if (rc) return rc < 0 ? rc : XB_OK;
+  if (K == 0) return zero_fill(Y, M, N, ldy, 4, s, what, err, errlen);
+  if (!tma_ok(X, ldx, 1) || !tma_ok(W, ldw, 1)) {
+    set_err(err, errlen, "%s: X/W must be 16-byte aligned with row pitches a multiple of 16 bytes", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
+  return launch<kInt8, true, kOutI32>(op, Y, nullptr, M, N, K, ldy, s, what, err, errlen);
+}
+
 extern "C" int xb_matmul_i16_workspace_size(int64_t M, int64_t N, int64_t K, size_t* bytes, char* err,
                                             size_t errlen) {
   if (!bytes || M < 0 || N < 0 || K < 0) {

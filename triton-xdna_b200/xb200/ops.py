@@ -290,6 +290,21 @@ def matmul_i8(a, b, out=None):
     return out
 
 
+def linear_i8(x, w, out=None):
+    """int32 y = x (int8 [M,K]) @ w^T (int8 [N,K]), exact."""
+    _cuda(x, w, out)
+    if x.dtype != torch.int8 or w.dtype != torch.int8:
+        raise TypeError("linear_i8 takes int8 operands")
+    if x.shape[1] != w.shape[1]:
+        raise ValueError("shape mismatch")
+    out = _gemm_out(x, w.shape[0], torch.int32, out)
+    M, K = x.shape
+    N = w.shape[0]
+    _lib.call("xb_linear_i8", x.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, K, _mat(x, "x"), _mat(w, "w"),
+              _mat(out, "y"), _stream())
+    return out
+
+
 def matmul_i16(a, b, out=None, workspace=None):
     """int32 C = A (int16) @ B (int16) with int32 wrap-around."""
     _cuda(a, b, out)
