@@ -230,3 +230,23 @@ def test_linear_i8_exact(M, N, K):
     w = _rand_int((N, K), -128, 128, torch.int8, N)
     y = ops.linear_i8(x.cuda(), w.cuda())
     assert torch.equal(y.cpu(), cgemm.gemm_int(x, w.t().contiguous()))
+
+
+@pytest.mark.parametrize("M,N,K", [(300, 272, 96), (64, 16, 32)])
+def test_four_byte_output_with_unaligned_pitch(M, N, K):
+    """C rows whose pitch is not a multiple of 16 bytes cannot be TMA-stored:
+    the epilogue falls back to per-thread stores with the same results."""
+    a = _rand_int((M, K), -128, 128, torch.int8, 11)
+    b = _rand_int((K, N), -128, 128, torch.int8, 12)
+    c_full = torch.full((M, N + 1), 777, dtype=torch.int32, device="cuda")
+    ops.matmul_i8(a.cuda(), b.cuda(), out=c_full[:, :N])
+    assert torch.equal(c_full[:, :N].cpu(), cgemm.gemm_int(a, b))
+    assert torch.all(c_full[:, N].cpu() == 777)
+    g = torch.Generator().manual_seed(13)
+    x = (torch.randn((M, K), generator=g) / 8).to(torch.bfloat16)
+    y = (torch.randn((K, N), generator=g) / 8).to(torch.bfloat16)
+    f_full = torch.full((M, N + 1), 5.0, dtype=torch.float32, device="cuda")
+    ops.matmul_bf16(x.cuda(), y.cuda(), torch.float32, out=f_full[:, :N])
+    torch.testing.assert_close(f_full[:, :N].cpu(), O.matmul_bf16_f32acc(x, y), atol=1e-4, rtol=1e-4)
+    assert torch.all(f_full[:, N].cpu() == 5.0)
+    _status_ok()

@@ -54,35 +54,48 @@ constexpr int tmem_cols_for(int cols) { return cols <= 32 ? 32 : cols <= 64 ? 64
 // BN_: tile N (0 = the default for the kind).  The small-M path (swap-AB:
 // weight rows in the 128-row MMA dimension, up to 64 tokens in N) uses 64
 // with a deeper ring, since it streams weights from HBM in short K ranges.
-template <int KIND, bool B_KMAJOR, int BN_ = 0>
+// PAIR: a cluster of two CTAs computes one 256 x BN tile with cta_group::2
+// MMAs; each CTA stages its own 128 rows of A and half of the B columns, so
+// a CTA moves 2/3 of the operand bytes of a 128 x 256 single-CTA tile for
+// the same MMA work (the L2 -> shared-memory stream is what bounds the
+// single-CTA kernel at large shapes).
+template <int KIND, bool B_KMAJOR, int BN_ = 0, bool PAIR = false>
 struct Cfg {
-  static constexpr int BM = 128;
+  static constexpr int BM = 128;                    // rows per CTA (TMEM lanes)
+  static constexpr int TILE_M = PAIR ? 256 : 128;   // rows per tile
   static constexpr int BN = BN_ ? BN_ : (KIND == kInt16Limbs ? 128 : 256);
+  static constexpr int BN_CTA = PAIR ? BN / 2 : BN;  // B columns staged per CTA
   static constexpr int ESZ = KIND == kBf16 ? 2 : 1;  // operand element bytes
   static constexpr int BK = 128 / ESZ;              // K elements per stage (128 bytes)
   static constexpr int PLANES = KIND == kInt16Limbs ? 2 : 1;
   static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int B_BYTES = BN_CTA * 128;
   static constexpr int STAGE_BYTES = PLANES * (A_BYTES + B_BYTES);
-  static constexpr int STAGES = KIND == kInt16Limbs ? 3 : (BN <= 64 ? 8 : 4);
+  static constexpr int STAGES = PAIR ? 6 : KIND == kInt16Limbs ? 3 : (BN <= 64 ? 8 : 4);
   static constexpr int UMMA_K = 32 / ESZ;  // 32 bytes of K per MMA
   static constexpr int KSTEPS = BK / UMMA_K;
   static constexpr int ACCS = KIND == kInt16Limbs ? 3 : 1;
   static constexpr int ACC_BUFS = KIND == kInt16Limbs ? 1 : 2;
   static constexpr int TMEM_COLS = tmem_cols_for(ACCS * ACC_BUFS * BN);
   static constexpr int B_BOX_N = 128 / ESZ;  // N elements in one MN-major B box
-  static constexpr int B_BOXES = B_KMAJOR ? 1 : BN / B_BOX_N;
+  static constexpr int B_BOXES = B_KMAJOR ? 1 : BN_CTA / B_BOX_N;
   static constexpr int B_BOX_BYTES = B_KMAJOR ? B_BYTES : BK * 128;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
   static_assert(ACCS * ACC_BUFS * BN <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
-  static_assert(B_KMAJOR || BN % B_BOX_N == 0, "MN-major B needs whole boxes");
+  static_assert(B_KMAJOR || BN_CTA % B_BOX_N == 0, "MN-major B needs whole boxes");
+  static_assert(!PAIR || KIND != kInt16Limbs, "pairs run the single-accumulator kinds");
 };
 
 struct alignas(64) Maps {
   CUtensorMap a[2];  // A plane(s): [M, K] K-major
   CUtensorMap b[2];  // B plane(s): [K, N] MN-major, or W [N, K] K-major
+  CUtensorMap c;     // C [M, N] for the TMA-store epilogue (4-byte outputs), 32 x 32 boxes
 };
+
+// Epilogue staging for TMA stores: per epilogue warp two 32 x 32 4-byte
+// tiles (128-byte rows, 128-byte swizzle), after the operand ring.
+constexpr int kEpiStageBytes = 4 * 2 * 32 * 128;
 
 struct Args {
   void* c;
@@ -95,6 +108,7 @@ struct Args {
   // N-sharded GEMM over the GPUs of a node: the epilogue stores every tile
   // into each rank's C (peer pointers, this rank's column block), and the
   // grid's last CTA signals every peer.
+  int c_tma;  // 1: C is written through maps.c (TMA stores from shared memory)
   int world, rank;
   void* peers[8];
   uint64_t* signals[8];  // each rank's signal buffer (uint64 [world + 1])
@@ -102,11 +116,12 @@ struct Args {
 
 constexpr int kGroupM = 16;  // tile raster: groups of 16 M-tiles sweep N (L2 reuse)
 
+template <int GROUP_M = kGroupM>
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
-  const int group = kGroupM * tiles_n;
+  const int group = GROUP_M * tiles_n;
   const int g = t / group;
-  const int first_m = g * kGroupM;
-  const int gm = min(kGroupM, tiles_m - first_m);
+  const int first_m = g * GROUP_M;
+  const int gm = min(GROUP_M, tiles_m - first_m);
   const int r = t - g * group;
   tm = first_m + r % gm;
   tn = r / gm;
@@ -118,9 +133,10 @@ __device__ __forceinline__ void red_release_sys_add(uint64_t* p, uint64_t v) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false>
+template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false>
 __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Maps maps, const Args args) {
-  using C = Cfg<KIND, B_KMAJOR, BN_>;
+  using C = Cfg<KIND, B_KMAJOR, BN_, PAIR>;
+  constexpr int GM = PAIR ? 8 : kGroupM;  // raster group (in tiles)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
@@ -134,6 +150,12 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
   const int lane = threadIdx.x & 31;
   const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base_u32 - smem_u32(smem_raw));
+  // Pair roles: CTA 0 of the cluster issues the MMAs and owns the barriers
+  // that gate them; both CTAs load operands and run an epilogue.
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = crank == 0;
+  const int tile0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tstep = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -142,7 +164,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
     }
     for (int b = 0; b < C::ACC_BUFS; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], 128);
+      mbar_init(&tempty_bar[b], PAIR ? 256 : 128);
     }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
@@ -155,11 +177,17 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
     }
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc2(&tmem_base_sh, C::TMEM_COLS);
+      tmem_relinquish2();
+    } else {
+      tmem_alloc(&tmem_base_sh, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // barrier init and TMEM allocation visible to the peer CTA
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
   // Everything above touched only shared memory, TMEM and the tensor maps in
@@ -180,47 +208,74 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
 #pragma unroll
       for (int s = 0; s < C::STAGES; ++s) issued[s] = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x) {
+      for (int t = tile0; t < args.num_tiles && ok; t += tstep) {
         int tm, tn;
-        tile_coords(t / args.splits, args.tiles_m, args.tiles_n, tm, tn);
+        tile_coords<GM>(t / args.splits, args.tiles_m, args.tiles_n, tm, tn);
         const int kb0 = (t % args.splits) * args.kps;
         const int kb1 = min(kb0 + args.kps, args.kblocks);
+        const int arow = tm * C::TILE_M + (int)crank * C::BM;    // this CTA's rows of A
+        const int bcol = tn * C::BN + (int)crank * C::BN_CTA;    // this CTA's columns of B
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
-          if (!mbar_wait(&empty_bar[s], ph ^ 1, kWaitLimit, &abort_flag)) { fail(); ok = false; break; }
-          mbar_arrive_expect_tx(&full_bar[s], C::STAGE_BYTES);
+          const bool got = PAIR ? mbar_wait_cl(&empty_bar[s], ph ^ 1, kWaitLimit, &abort_flag)
+                                : mbar_wait(&empty_bar[s], ph ^ 1, kWaitLimit, &abort_flag);
+          if (!got) { fail(); ok = false; break; }
+          // the leader's full barrier counts the bytes of both CTAs of a pair
+          if (leader) mbar_arrive_expect_tx(&full_bar[s], (PAIR ? 2 : 1) * C::STAGE_BYTES);
+          const uint32_t fb = PAIR ? mapa_u32(smem_u32(&full_bar[s]), 0) : 0u;
+          auto load = [&](void* dst, const CUtensorMap* map, int32_t c0, int32_t c1) {
+            if constexpr (PAIR) tma_load_2d_pair(dst, map, fb, c0, c1);
+            else tma_load_2d(dst, map, &full_bar[s], c0, c1);
+          };
           uint8_t* st = smem + s * C::STAGE_BYTES;
           for (int p = 0; p < C::PLANES; ++p) {
-            tma_load_2d(st + p * C::A_BYTES, &maps.a[p], &full_bar[s], kb * C::BK, tm * C::BM);
+            load(st + p * C::A_BYTES, &maps.a[p], kb * C::BK, arow);
             uint8_t* sb = st + C::PLANES * C::A_BYTES + p * C::B_BYTES;
             if (B_KMAJOR) {
-              tma_load_2d(sb, &maps.b[p], &full_bar[s], kb * C::BK, tn * C::BN);
+              load(sb, &maps.b[p], kb * C::BK, bcol);
             } else {
 #pragma unroll
-              for (int j = 0; j < C::B_BOXES; ++j)
-                tma_load_2d(sb + j * C::B_BOX_BYTES, &maps.b[p], &full_bar[s], tn * C::BN + j * C::B_BOX_N,
-                            kb * C::BK);
+              for (int j = 0; j < C::B_BOXES; ++j) load(sb + j * C::B_BOX_BYTES, &maps.b[p], bcol + j * C::B_BOX_N, kb * C::BK);
             }
           }
           issued[s] = it / C::STAGES + 1;
         }
       }
-      // Drain: every load issued into a stage must have landed before exit.
-      for (int s = 0; s < C::STAGES; ++s)
-        if (issued[s] && !mbar_wait(&full_bar[s], (issued[s] - 1) & 1, kWaitLimit, &abort_flag)) fail();
+      if (leader) {
+        // Drain: every load issued into a stage must have landed before exit.
+        for (int s = 0; s < C::STAGES; ++s)
+          if (issued[s] && !mbar_wait(&full_bar[s], (issued[s] - 1) & 1, kWaitLimit, &abort_flag)) fail();
+      } else if (!ok) {
+        // The odd CTA's loads complete on the leader's barriers: after a
+        // failure give any load still in flight time to land (loads take
+        // microseconds) before the cluster barrier lets the CTA exit.
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 1000000ull) __nanosleep(1000);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       uint32_t it = 0;
       int local = 0;
       bool ok = true;
       bool any = false;
-      for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x, ++local) {
+      // commit to a barrier of this CTA and, for a pair, to the same barrier of the odd CTA
+      auto commit = [&](uint64_t* bar) {
+        if constexpr (PAIR) {
+          tc_commit2(smem_u32(bar));
+          tc_commit2(mapa_u32(smem_u32(bar), 1));
+        } else {
+          tc_commit(bar);
+        }
+      };
+      for (int t = tile0; t < args.num_tiles && ok; t += tstep, ++local) {
         const int buf = local % C::ACC_BUFS;
         const uint32_t tph = (local / C::ACC_BUFS) & 1;
-        if (!mbar_wait(&tempty_bar[buf], tph ^ 1, kWaitLimit, &abort_flag)) { fail(); break; }
+        const bool got = PAIR ? mbar_wait_cl(&tempty_bar[buf], tph ^ 1, kWaitLimit, &abort_flag)
+                              : mbar_wait(&tempty_bar[buf], tph ^ 1, kWaitLimit, &abort_flag);
+        if (!got) { fail(); break; }
         tc_fence_after();
         const uint32_t d0 = tmem_base + buf * C::ACCS * C::BN;
         const int kb0 = (t % args.splits) * args.kps;
@@ -243,7 +298,11 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
                                : umma_desc_sw128(sb + ks * C::UMMA_K * 128, C::B_BOX_BYTES, 1024);
             }
             constexpr uint32_t bmn = B_KMAJOR ? 0 : 1;
-            if constexpr (KIND == kBf16) {
+            if constexpr (PAIR && KIND == kBf16) {
+              mma2_f16(d0, ad[0], bd[0], umma_idesc(1, 1, 1, 0, bmn, C::TILE_M, C::BN), acc);
+            } else if constexpr (PAIR) {
+              mma2_i8(d0, ad[0], bd[0], umma_idesc(2, 1, 1, 0, bmn, C::TILE_M, C::BN), acc);
+            } else if constexpr (KIND == kBf16) {
               mma_f16(d0, ad[0], bd[0], umma_idesc(1, 1, 1, 0, bmn, C::BM, C::BN), acc);
             } else if constexpr (KIND == kInt8) {
               mma_i8(d0, ad[0], bd[0], umma_idesc(2, 1, 1, 0, bmn, C::BM, C::BN), acc);
@@ -256,13 +315,14 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
             }
             any = true;
           }
-          tc_commit(&empty_bar[s]);  // frees the stage once these MMAs have read it
+          commit(&empty_bar[s]);  // frees the stage once these MMAs have read it
         }
         if (!ok) break;
-        tc_commit(&tfull_bar[buf]);  // accumulator ready for the epilogue
+        commit(&tfull_bar[buf]);  // accumulator ready for the epilogue
       }
       if (any) {
-        tc_commit(&drain_bar);
+        if constexpr (PAIR) tc_commit2(smem_u32(&drain_bar));
+        else tc_commit(&drain_bar);
         if (!mbar_wait(&drain_bar, 0, kWaitLimit, &abort_flag)) fail();
       }
     }
@@ -270,14 +330,16 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int local = 0;
-    for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x, ++local) {
+    for (int t = tile0; t < args.num_tiles; t += tstep, ++local) {
       const int buf = local % C::ACC_BUFS;
       const uint32_t tph = (local / C::ACC_BUFS) & 1;
-      if (!mbar_wait(&tfull_bar[buf], tph, kWaitLimit, &abort_flag)) { fail(); break; }
+      const bool got = PAIR ? mbar_wait_cl(&tfull_bar[buf], tph, kWaitLimit, &abort_flag)
+                            : mbar_wait(&tfull_bar[buf], tph, kWaitLimit, &abort_flag);
+      if (!got) { fail(); break; }
       tc_fence_after();
       int tm, tn;
-      tile_coords(t / args.splits, args.tiles_m, args.tiles_n, tm, tn);
-      const int row = tm * C::BM + q * 32 + lane;
+      tile_coords<GM>(t / args.splits, args.tiles_m, args.tiles_n, tm, tn);
+      const int row = tm * C::TILE_M + (int)crank * C::BM + q * 32 + lane;
       const int64_t slice = (int64_t)(t % args.splits) * args.split_stride;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * C::ACCS * C::BN;
 #pragma unroll 1
@@ -295,6 +357,42 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
           tmem_ld_wait();
         }
         const int col0 = tn * C::BN + cc * 32;
+        if constexpr (OUT != kOutBf16 && !TRANS && !PEERS) {
+          if (args.c_tma) {
+            // Coalesced store: each thread writes its row's 128 bytes into a
+            // swizzled 32 x 32 staging tile, one lane stores the tile with TMA
+            // (the unit clips rows / columns outside C).  Chunks wholly outside
+            // C (warp-uniform test) touch no staging buffer and commit nothing.
+            if (col0 >= args.n || row - lane >= args.m) continue;
+            if constexpr (OUT == kOutF32) {
+              if (args.bias) {
+                const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(args.bias);
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (col0 + j < args.n) v[j] = __float_as_uint(__uint_as_float(v[j]) + __bfloat162float(bp[col0 + j]));
+              }
+            }
+            uint8_t* stg = smem + C::STAGES * C::STAGE_BYTES + (q * 2 + (cc & 1)) * (32 * 128);
+            // the store that last used this buffer has read it (a tile's first
+            // chunk waits for all: chunks past the edges of C commit nothing)
+            if (lane == 0) {
+              if (cc == 0) bulk_wait_read<0>();
+              else bulk_wait_read<1>();
+            }
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<uint4*>(stg + lane * 128 + ((j ^ (lane & 7)) * 16)) =
+                  make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&maps.c, stg, col0, row);
+              bulk_commit();
+            }
+            continue;
+          }
+        }
         if (row >= args.m || col0 >= args.n) continue;
         if constexpr (OUT != kOutI32) {
           if (args.bias) {  // bias indexed by the output feature: the row of W
@@ -359,7 +457,12 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty_bar[buf]);
+      if constexpr (PAIR) mbar_arrive_cluster(mapa_u32(smem_u32(&tempty_bar[buf]), 0));
+      else mbar_arrive(&tempty_bar[buf]);
+    }
+    if constexpr (OUT != kOutBf16 && !TRANS && !PEERS) {
+      if (args.c_tma && lane == 0) bulk_wait_all();  // every TMA store of C has completed
+      __syncwarp();
     }
   }
 
@@ -377,10 +480,17 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       }
     }
   }
+  if constexpr (PAIR) {
+    // Neither CTA leaves while the other may still read its shared memory
+    // (MMA operands), signal its barriers or write its TMEM.
+    tc_fence_before();
+    cluster_sync();
+  }
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, C::TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc2(tmem_base, C::TMEM_COLS);
+    else tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
 
@@ -521,18 +631,39 @@ struct PeerArgs {
   uint64_t* signals[8] = {nullptr};
 };
 
-template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false>
+// Launch with clusters of two CTAs (and programmatic dependent launch when enabled).
+template <typename... KArgs, typename... Args2>
+cudaError_t launch_pairs(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t s,
+                         Args2... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false>
 int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
            cudaStream_t s, const char* what, char* err, size_t errlen, int splits = 1, int64_t split_stride = 0,
            const PeerArgs* pa = nullptr) {
-  using Cf = Cfg<KIND, B_KMAJOR, BN_>;
+  using Cf = Cfg<KIND, B_KMAJOR, BN_, PAIR>;
   const CUtensorMapDataType dt = KIND == kBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   Maps maps;
   memset(&maps, 0, sizeof(maps));
   for (int p = 0; p < Cf::PLANES; ++p) {
     int rc = make_map(&maps.a[p], op.a[p], dt, Cf::ESZ, K, M, op.lda, Cf::BK, Cf::BM, err, errlen);
     if (rc) return rc;
-    rc = B_KMAJOR ? make_map(&maps.b[p], op.b[p], dt, Cf::ESZ, K, N, op.ldb, Cf::BK, Cf::BN, err, errlen)
+    rc = B_KMAJOR ? make_map(&maps.b[p], op.b[p], dt, Cf::ESZ, K, N, op.ldb, Cf::BK, Cf::BN_CTA, err, errlen)
                   : make_map(&maps.b[p], op.b[p], dt, Cf::ESZ, N, K, op.ldb, Cf::B_BOX_N, Cf::BK, err, errlen);
     if (rc) return rc;
   }
@@ -543,7 +674,7 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   args.m = (int)M;
   args.n = (int)N;
   args.k = (int)K;
-  args.tiles_m = (int)((M + Cf::BM - 1) / Cf::BM);
+  args.tiles_m = (int)((M + Cf::TILE_M - 1) / Cf::TILE_M);
   args.tiles_n = (int)((N + Cf::BN - 1) / Cf::BN);
   args.kblocks = (int)((K + Cf::BK - 1) / Cf::BK);
   if (splits < 1) splits = 1;
@@ -558,21 +689,70 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
     args.peers[i] = pa ? pa->peers[i] : nullptr;
     args.signals[i] = pa ? pa->signals[i] : nullptr;
   }
+  // 4-byte outputs of whole-tile GEMMs leave through the TMA-store epilogue
+  // when C meets the TMA alignment rules.
+  constexpr bool kStaged = OUT != kOutBf16 && !TRANS && !PEERS;
+  constexpr int kSmem = Cf::SMEM + (kStaged ? kEpiStageBytes : 0);
+  static_assert(kSmem <= 227 * 1024, "shared memory budget");
+  args.c_tma = 0;
+  if (kStaged && args.splits == 1 && tma_ok(c, ldc, 4)) {
+    int rc = make_map(&maps.c, c, OUT == kOutI32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
+                      N, M, ldc, 32, 32, err, errlen);
+    if (rc) return rc;
+    args.c_tma = 1;
+  }
+  auto kernel = gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS, PEERS, PAIR>;
   static bool attr_set = false;
+  static int max_clusters = 0;
   if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS, PEERS>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Cf::SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e == cudaSuccess && PAIR) {
+      // resident pairs: the persistent grid is sized to what runs at once
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2);
+      cfg.blockDim = dim3(192);
+      cfg.dynamicSmemBytes = kSmem;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = 2;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      e = cudaOccupancyMaxActiveClusters(&max_clusters, kernel, &cfg);
+      if (e == cudaSuccess && max_clusters < 1) e = cudaErrorInvalidConfiguration;
+    }
     if (e != cudaSuccess) {
-      set_err(err, errlen, "%s: cudaFuncSetAttribute: %s", what, cudaGetErrorString(e));
+      set_err(err, errlen, "%s: kernel setup: %s", what, cudaGetErrorString(e));
       return XB_ERR_CUDA;
     }
     attr_set = true;
   }
   int sms = 148;
   sm_count(&sms);
-  const int grid = args.num_tiles < sms ? args.num_tiles : sms;
-  launch_k(gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS, PEERS>, grid, 192, Cf::SMEM, s, maps, args);
+  if constexpr (PAIR) {
+    const int clusters = args.num_tiles < max_clusters ? args.num_tiles : max_clusters;
+    cudaError_t e = launch_pairs(kernel, 2 * clusters, 192, kSmem, s, maps, args);
+    if (e != cudaSuccess) {
+      set_err(err, errlen, "%s: %s", what, cudaGetErrorString(e));
+      return XB_ERR_CUDA;
+    }
+  } else {
+    const int grid = args.num_tiles < sms ? args.num_tiles : sms;
+    launch_k(kernel, grid, 192, kSmem, s, maps, args);
+  }
   return check_launch(what, err, errlen);
+}
+
+// CTA pairs for products with at least two 128-row blocks; XB_GEMM_PAIRS=0
+// in the environment selects the single-CTA kernel everywhere.
+bool use_pairs(int64_t M) {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("XB_GEMM_PAIRS");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1 && M >= 256;
 }
 
 int check_common(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb,
@@ -678,6 +858,7 @@ extern "C" int xb_matmul_i8(const void* A, const void* B, void* C, int64_t M, in
     return XB_ERR_UNSUPPORTED;
   }
   Operands op{{A, nullptr}, {B, nullptr}, lda, ldb};
+  if (use_pairs(M)) return launch<kInt8, false, kOutI32, 0, false, false, true>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
   return launch<kInt8, false, kOutI32>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
 }
 
@@ -693,6 +874,7 @@ extern "C" int xb_linear_i8(const void* X, const void* W, void* Y, int64_t M, in
     return XB_ERR_UNSUPPORTED;
   }
   Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
+  if (use_pairs(M)) return launch<kInt8, true, kOutI32, 0, false, false, true>(op, Y, nullptr, M, N, K, ldy, s, what, err, errlen);
   return launch<kInt8, true, kOutI32>(op, Y, nullptr, M, N, K, ldy, s, what, err, errlen);
 }
 
@@ -797,6 +979,11 @@ extern "C" int xb_matmul_bf16(const void* A, const void* B, void* C, int64_t M, 
     return XB_ERR_UNSUPPORTED;
   }
   Operands op{{A, nullptr}, {B, nullptr}, lda, ldb};
+  if (use_pairs(M)) {
+    if (out_dtype == XB_DT_F32)
+      return launch<kBf16, false, kOutF32, 0, false, false, true>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
+    return launch<kBf16, false, kOutBf16, 0, false, false, true>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
+  }
   if (out_dtype == XB_DT_F32) return launch<kBf16, false, kOutF32>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
   return launch<kBf16, false, kOutBf16>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
 }
@@ -821,6 +1008,11 @@ extern "C" int xb_linear_bf16(const void* X, const void* W, const void* bias, vo
     return XB_ERR_UNSUPPORTED;
   }
   Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
+  if (use_pairs(M)) {
+    if (out_dtype == XB_DT_F32)
+      return launch<kBf16, true, kOutF32, 0, false, false, true>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
+    return launch<kBf16, true, kOutBf16, 0, false, false, true>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
+  }
   if (out_dtype == XB_DT_F32) return launch<kBf16, true, kOutF32>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
   return launch<kBf16, true, kOutBf16>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
 }
