@@ -10,7 +10,11 @@ needed between steps.
 
 Other workloads (``--workload``) measure the remaining operator rows with the
 same machinery: ``rowreduce`` (softmax, layernorm, rms_norm,
-weighted_rms_norm on [32768, 4096] bf16 and fp32).
+weighted_rms_norm on [32768, 4096] bf16 and fp32), ``gemm`` (the int8 /
+int16 / bf16 GEMM sweep; N-sharded over the ranks when N > 1), ``qwen`` and
+``gpt2`` (batch 64 x 512-token prefill + 128 greedy decode steps of the
+Qwen2.5-0.5B and GPT-2 124M architectures with random-init weights,
+batch-sharded over the ranks; metric tokens/s).
 
 Metric: algorithmic HBM bytes (each input read once, each output written
 once) per second, aggregated over the step and over all ranks.
@@ -225,35 +229,58 @@ def qwen_workload(dev, n: int, seed: int, host: bool):
 
 
 WORKLOADS = {"elementwise": elementwise_workload, "rowreduce": rowreduce_workload, "gemm": gemm_workload,
-             "qwen": qwen_workload}
+             "qwen": qwen_workload, "gpt2": qwen_workload}
 
 
-def qwen_flops_bytes(cfg, B, S, ctx_end):
-    """Algorithmic work of the Qwen forward: prefill FLOPs (linears over all
+def llm_flops_bytes(kind, cfg, B, S, ctx_end):
+    """Algorithmic work of an LLM forward: prefill FLOPs (linears over all
     tokens + causal attention + last-position LM head) and decode bytes per
     step (every weight once + the KV cache read)."""
-    D, H, KVH, HD, I, V = cfg.n_embd, cfg.n_head, cfg.n_kv_head, cfg.head_dim, cfg.intermediate, cfg.vocab_size
-    per_tok = 2 * (D * (H + 2 * KVH) * HD + H * HD * D + 3 * D * I) * cfg.n_layer
-    attn = 2 * 2 * B * H * HD * (S * (S + 1) // 2) * cfg.n_layer
+    D, H, KVH, HD, V, L = cfg.n_embd, cfg.n_head, cfg.n_kv_head, cfg.head_dim, cfg.vocab_size, cfg.n_layer
+    if kind == "qwen":
+        per_tok = 2 * (D * (H + 2 * KVH) * HD + H * HD * D + 3 * D * cfg.intermediate) * L
+    else:  # gpt2: QKV, attention projection, fc and mlp projection
+        per_tok = 2 * (3 * D * D + D * D + 2 * D * 4 * D) * L
+    attn = 2 * 2 * B * H * HD * (S * (S + 1) // 2) * L
     prefill = per_tok * B * S + attn + 2 * B * D * V
     weights = (per_tok // 2 + D * V) * 2  # bf16 bytes of every weight (LM head tied to the embedding)
-    kv_mean = 2 * cfg.n_layer * B * KVH * HD * 2 * ((S + ctx_end) / 2)
+    kv_mean = 2 * L * B * KVH * HD * 2 * ((S + ctx_end) / 2)
     return prefill, weights + kv_mean
 
 
-def run_qwen_bench(args, world, rank, local, dev):
-    from xb200.qwen import Qwen2Model, QwenConfig, random_weights
+LLM_WORKLOADS = {
+    "qwen": "Qwen2.5-0.5B architecture (24 layers, hidden 896, 14/2 heads, MLP 4864, vocab 151936)",
+    "gpt2": "GPT-2 124M architecture (12 layers, hidden 768, 12 heads, MLP 3072, vocab 50257, learned positions)",
+}
 
-    cfg = QwenConfig()
+
+def _llm_model(kind, dev):
+    if kind == "qwen":
+        from xb200.qwen import Qwen2Model, QwenConfig, random_weights
+        cfg = QwenConfig()
+        return cfg, Qwen2Model(random_weights(cfg, seed=0), cfg, device=dev, rope_len=1024)
+    from xb200.gpt2 import GPT2Config, GPT2Model, random_weights
+    cfg = GPT2Config.variant("gpt2")
+    return cfg, GPT2Model(random_weights(cfg, seed=0), cfg, device=dev)
+
+
+def run_llm_bench(args, world, rank, local, dev, kind):
+    from xb200 import ops as X
+
     B_total, S, new = args.qwen_batch, args.qwen_prompt, args.qwen_new
     if B_total % world:
         raise SystemExit(f"batch {B_total} does not split over {world} ranks")
     B = B_total // world
-    sd = random_weights(cfg, seed=0)
-    model = Qwen2Model(sd, cfg, device=dev, rope_len=1024)
-    del sd
+    cfg, model = _llm_model(kind, dev)
     g = torch.Generator().manual_seed(1000 + rank)
-    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=g).to(dev)
+    ids_host = torch.randint(0, cfg.vocab_size, (B, S), generator=g).pin_memory()
+    ids = ids_host.to(dev)
+    toks_host = torch.empty((B, new), dtype=torch.int64).pin_memory()
+    # kernels one step launches: count an eager step (graph replays re-run the
+    # kernels recorded at capture, which the counter saw once)
+    n0 = X.launch_count()
+    model.generate(ids, new)
+    launches_per_step = X.launch_count() - n0
     graphs = None if args.qwen_eager else model.decode_graphs(B, S, new)  # decode steps replay CUDA graphs
     cache = model.new_cache(B, S + new) if graphs is None else None
 
@@ -274,7 +301,21 @@ def run_qwen_bench(args, world, rank, local, dev):
     _barrier(world)
     pre_ms = _max_over_ranks(statistics.mean(pre), world)
     dec_ms = _max_over_ranks(statistics.mean(dec), world)
-    flops, dec_bytes = qwen_flops_bytes(cfg, B, S, S + new)
+    # end to end through the public API: prompt ids from pinned host memory,
+    # generation, generated ids back to the host, every step
+    e2e = []
+    for _ in range(max(1, args.e2e_steps)):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record()
+        ids.copy_(ids_host, non_blocking=True)
+        toks, _ = model.generate(ids, new, cache=cache, graphs=graphs)
+        toks_host.copy_(toks, non_blocking=True)
+        ev1.record()
+        torch.cuda.synchronize()
+        e2e.append(ev0.elapsed_time(ev1))
+    e2e_ms = _max_over_ranks(statistics.mean(e2e), world)
+    flops, dec_bytes = llm_flops_bytes(kind, cfg, B, S, S + new)
     prefill_tps = B_total * S / (pre_ms * 1e-3)
     decode_tps = B_total * (new - 1) / (dec_ms * 1e-3)
     total_tps = B_total * (S + new) / ((pre_ms + dec_ms) * 1e-3)
@@ -282,17 +323,17 @@ def run_qwen_bench(args, world, rank, local, dev):
     dec_gbs = dec_bytes * (new - 1) / (dec_ms * 1e-3) / 1e9
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = qwen_cpu_baseline(cfg)
+        cpu = llm_cpu_baseline(kind, cfg)
     if rank == 0:
         print(json.dumps({
             "metric": "LLM tokens/s (prefill + decode)", "value": round(total_tps, 1), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(pre_ms + dec_ms, 2), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic random ids, random-init weights (seed 0)",
-            "config": {"workload": "Qwen2.5-0.5B architecture (24 layers, hidden 896, 14/2 heads, MLP 4864, "
-                                   "vocab 151936): batch 64 x 512 prefill + 128 greedy decode",
+            "config": {"workload": f"{LLM_WORKLOADS[kind]}: batch {B_total} x {S} prefill + {new} greedy decode",
                        "global_batch": B_total, "seq_len": S, "new_tokens": new,
-                       "parallelism": f"batch-sharded x{world} (replicated weights, no collective)"},
+                       "parallelism": f"batch-sharded x{world} (replicated weights, no collective)",
+                       "l2": "weights re-read every step; decode steps replay CUDA graphs"},
             "prefill_tokens_per_s": round(prefill_tps, 1), "decode_tokens_per_s": round(decode_tps, 1),
             "prefill_ms": round(pre_ms, 2), "decode_ms": round(dec_ms, 2),
             "roofline": {"bound": "tensor (prefill) / hbm (decode)",
@@ -301,20 +342,27 @@ def run_qwen_bench(args, world, rank, local, dev):
                          "decode": {"achieved": round(dec_gbs, 1), "unit": "GB/s", "peak": peaks["hbm_gbs"],
                                     "frac": round(dec_gbs / peaks["hbm_gbs"], 4)},
                          "peak_source": peaks["source"]},
+            "e2e": {"value": round(B_total * (S + new) / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": ids_host.numel() * 8 * world,
+                    "d2h_bytes_per_step": toks_host.numel() * 8 * world, "ms_per_step": round(e2e_ms, 2),
+                    "api": f"{type(model).__name__}.generate(ids copied from pinned host memory) -> tokens to host"},
+            "gpu_launches": launches_per_step * args.steps,
             "cpu_baseline": cpu, "clocks": clk.summary(),
         }))
 
 
-def qwen_cpu_baseline(cfg):
+def llm_cpu_baseline(kind, cfg):
     """The oracle forward on the host cores: one 128-token prefill + 4 decode
     steps of one sequence (a bounded sample of the workload)."""
-    from oracle.qwen import OracleQwen
-    from xb200.qwen import random_weights
-
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    sd = random_weights(cfg, seed=0)
-    orc = OracleQwen(sd, cfg)
+    if kind == "qwen":
+        from oracle.qwen import OracleQwen as Oracle
+        from xb200.qwen import random_weights
+    else:
+        from oracle.gpt2 import OracleGPT2 as Oracle
+        from xb200.gpt2 import random_weights
+    orc = Oracle(random_weights(cfg, seed=0), cfg)
     ids = torch.randint(0, cfg.vocab_size, (1, 128), generator=torch.Generator().manual_seed(5))
     cache = orc.new_cache(1, 132)
     t0 = time.perf_counter()
@@ -405,12 +453,16 @@ def run_gemm_bench(args, ops_list, config, world, rank, local, dev):
     res = {}
     if args.only:
         ops_list = [o for o in ops_list if args.only in o.name]
+    from xb200 import ops as X
+
+    launches = 0
     with ClockSampler(local) as clk:
         for op in ops_list:
             fn, keep = op.make()
             for _ in range(max(3, args.warmup)):
                 fn()
             times = []
+            n0 = X.launch_count()
             for _ in range(max(3, args.steps // 3)):
                 flush.zero_()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -419,6 +471,7 @@ def run_gemm_bench(args, ops_list, config, world, rank, local, dev):
                 e1.record(stream)
                 torch.cuda.synchronize()
                 times.append(e0.elapsed_time(e1))
+            launches += X.launch_count() - n0
             ms = statistics.median(times)
             tops = op.flops / (ms * 1e-3) / 1e12
             res[op.name] = {"ms": round(ms, 4), "tops": round(tops, 1),
@@ -453,6 +506,11 @@ def run_gemm_bench(args, ops_list, config, world, rank, local, dev):
             torch.cuda.empty_cache()
     clocks = clk.summary()
     big = "gemm_bf16_8192x8192x8192"
+    e2e = gemm_e2e(dev, args.e2e_steps) if (big in res and args.e2e_steps > 0) else None
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, threads, desc = gemm_cpu_baseline()
+        cpu = {"value": round(v, 4), "unit": "TOPS", "cores": threads, "kind": "port", "sample": desc}
     line = {
         "metric": "GEMM TOPS", "value": res[big]["tops"] if big in res else None, "unit": "TOPS", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
@@ -460,10 +518,58 @@ def run_gemm_bench(args, ops_list, config, world, rank, local, dev):
         "roofline": {"bound": "tensor", "kernel": big, "achieved": res.get(big, {}).get("tops"),
                      "peak": peaks["bf16_tflops"], "peak_source": peaks["source"], "unit": "TFLOP/s",
                      "frac": res.get(big, {}).get("frac"), "traffic": None},
-        "ops": res, "clocks": clocks, "gpu_launches": None,
+        "ops": res, "clocks": clocks, "gpu_launches": launches, "e2e": e2e, "cpu_baseline": cpu,
     }
     if rank == 0:
         print(json.dumps(line))
+
+
+def gemm_e2e(dev, steps):
+    """bf16 8192^3 through the public tensor API with host operands: A and B
+    copied from pinned host memory, the GEMM, C copied back, every step."""
+    from xb200 import ops as X
+
+    n = 8192
+    g = torch.Generator().manual_seed(0)
+    ha = torch.randn((n, n), generator=g).to(torch.bfloat16).pin_memory()
+    hb = torch.randn((n, n), generator=g).to(torch.bfloat16).pin_memory()
+    hc = torch.empty((n, n), dtype=torch.bfloat16).pin_memory()
+    da, db = torch.empty_like(ha, device=dev), torch.empty_like(hb, device=dev)
+    dc = torch.empty((n, n), dtype=torch.bfloat16, device=dev)
+    times = []
+    for i in range(steps + 1):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        da.copy_(ha, non_blocking=True)
+        db.copy_(hb, non_blocking=True)
+        X.matmul_bf16(da, db, torch.bfloat16, out=dc)
+        hc.copy_(dc, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        if i:
+            times.append(e0.elapsed_time(e1))
+    ms = statistics.mean(times)
+    return {"value": round(2 * n ** 3 / (ms * 1e-3) / 1e12, 1), "unit": "TOPS", "ms_per_step": round(ms, 3),
+            "h2d_bytes_per_step": 2 * n * n * 2, "d2h_bytes_per_step": n * n * 2,
+            "api": "xb200.ops.matmul_bf16 on operands copied from pinned host memory (bf16 8192^3)"}
+
+
+def gemm_cpu_baseline():
+    """The int8 GEMM of the oracle (plain-C int32 accumulation, OpenMP over
+    every host thread) on a 2048^3 sample; TOPS = 2 M N K / time."""
+    from oracle import cgemm
+
+    threads = os.cpu_count() or 1
+    n = 2048
+    g = torch.Generator().manual_seed(0)
+    a = torch.randint(-128, 128, (n, n), generator=g, dtype=torch.int8)
+    b = torch.randint(-128, 128, (n, n), generator=g, dtype=torch.int8)
+    cgemm.gemm_int(a[:256], b)  # warm-up (and build check)
+    t0 = time.perf_counter()
+    cgemm.gemm_int(a, b)
+    secs = time.perf_counter() - t0
+    return 2 * n ** 3 / secs / 1e12, threads, f"int8 {n}x{n}x{n} through the oracle's C GEMM ({threads} threads)"
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -629,6 +735,42 @@ def cpu_baseline(workload: str, sample: int, reps: int = 1):
     return total_b / total_s / 1e9, threads, desc
 
 
+def reference_arm_other(args, world, warmup):
+    """--impl reference for the GEMM and LLM workloads: the oracle's CPU path
+    (the examples' torch expressions / the C int GEMM) on bounded samples."""
+    vals = []
+    if args.workload == "gemm":
+        for i in range(warmup + args.steps):
+            v, threads, desc = gemm_cpu_baseline()
+            if i >= warmup:
+                vals.append(v)
+        metric, unit, dtype = "GEMM TOPS", "TOPS", "i8"
+        cfg = {"workload": "GEMM sweep (CPU sample)", "sample": desc}
+    else:
+        if args.workload == "qwen":
+            from xb200.qwen import QwenConfig
+            cfg_m = QwenConfig()
+        else:
+            from xb200.gpt2 import GPT2Config
+            cfg_m = GPT2Config.variant("gpt2")
+        steps = max(1, min(args.steps, 5))
+        for i in range(1 + steps):
+            r = llm_cpu_baseline(args.workload, cfg_m)
+            if i:
+                vals.append(r["value"])
+        threads, desc = r["cores"], r["sample"]
+        metric, unit, dtype = "LLM tokens/s (prefill + decode)", "tokens/s", "bf16"
+        cfg = {"workload": f"{LLM_WORKLOADS[args.workload]} (CPU sample)", "sample": desc}
+    value = statistics.median(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": world,
+        "steps": len(vals), "warmup": warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": dtype, "data": "synthetic, seed 0", "config": cfg,
+        "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
 def _timeit(fn):
     t0 = time.perf_counter()
     fn()
@@ -663,6 +805,9 @@ def main():
         world = int(os.environ.get("WORLD_SIZE", "1"))
         if rank != 0:
             return
+        if args.workload in LLM_WORKLOADS or args.workload == "gemm":
+            reference_arm_other(args, world, warmup)
+            return
         sample = 1 << 22
         for _ in range(warmup):
             cpu_baseline(args.workload, 1 << 16)
@@ -687,8 +832,8 @@ def main():
     _lib.load()
     dev = torch.device("cuda", torch.cuda.current_device())
     want_e2e = rank == 0 and args.e2e_steps > 0 and args.workload == "elementwise"
-    if args.workload == "qwen":
-        run_qwen_bench(args, world, rank, local, dev)
+    if args.workload in LLM_WORKLOADS:
+        run_llm_bench(args, world, rank, local, dev, args.workload)
         if world > 1:
             import torch.distributed as dist
 

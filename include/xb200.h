@@ -305,17 +305,37 @@ XB_API int xb_peer_status(void* stream, int* status, char* err,
  * ------------------------------------------------------------------------- */
 
 /* out[m, :] = table[ids[m], :] (bf16 rows of `dim`, dim % 8 == 0).  Ids
- * outside [0, vocab) produce zero rows.  Replaces model.py:911
- * (`self.embed_tokens[input_ids]`). */
+ * outside [0, vocab) produce zero rows and set the flag xb_token_status
+ * reports.  Replaces model.py:911 (`self.embed_tokens[input_ids]`). */
 XB_API int xb_embedding_bf16(const void* table, const int64_t* ids, void* out,
                              int64_t rows, int64_t dim, int64_t vocab,
                              void* stream, char* err, size_t errlen);
+
+/* *status = 1 if an embedding kernel met a token id outside its vocabulary
+ * since the previous call (then clears the flag), else 0.  Synchronises
+ * `stream`.  The reference raises an IndexError on such ids. */
+XB_API int xb_token_status(void* stream, int* status, char* err,
+                           size_t errlen);
+
+/* out[m, :] = bf16(table[ids[m], :] + pos_table[pos_offset + m % seq, :]):
+ * token plus learned position embeddings of `rows` = batch*seq tokens (rows
+ * of `seq` consecutive positions).  Ids outside [0, vocab) produce zero rows
+ * and set the flag xb_token_status reports.  Replaces
+ * examples/gpt2/model.py:866-876 (`self.wte[input_ids] + self.wpe[positions]`). */
+XB_API int xb_embedding_pos_bf16(const void* table, const void* pos_table,
+                                 const int64_t* ids, void* out, int64_t rows,
+                                 int64_t seq, int64_t dim, int64_t vocab,
+                                 int64_t n_pos, int64_t pos_offset,
+                                 void* stream, char* err, size_t errlen);
 
 /* Rotary embedding of the fused QKV projection plus the KV-cache write.
  * qkv: [batch*seq, (n_head + 2*n_kv_head)*head_dim]; cos/sin: fp32 tables of
  * at least pos_offset+seq rows of head_dim (rope.py:20-35); q_out:
  * [batch, n_head, seq, head_dim]; k_cache / v_cache: [batch, n_kv_head,
  * max_seq, head_dim], rows pos_offset .. pos_offset+seq-1 written.
+ * cos_t and sin_t may both be NULL: the query and key heads are then copied
+ * unrotated (models with learned positions: the head split, transpose and
+ * cache write of examples/gpt2/model.py:757-775).
  * Replaces model.py:851-867 and kernels/rope.py:44-67. */
 XB_API int xb_rope_kv_bf16(const void* qkv, const float* cos_t,
                            const float* sin_t, void* q_out, void* k_cache,
@@ -360,6 +380,12 @@ XB_API int xb_argmax_f32(const float* x, int64_t rows, int64_t cols,
  * (amd_triton_npu/backend/include/HsaRuntime/HsaRuntime.h:57-67). */
 XB_API int xb_device_status(void* stream, int* status, char* err,
                             size_t errlen);
+
+/* Number of kernels this library has launched since it was loaded (launch
+ * calls made on the host, including those recorded into a CUDA graph during
+ * stream capture; graph replays are not counted).  No reference counterpart:
+ * the benchmark uses it to report how many of its own kernels a step runs. */
+XB_API int xb_launch_count(uint64_t* count, char* err, size_t errlen);
 
 #ifdef __cplusplus
 } /* extern "C" */

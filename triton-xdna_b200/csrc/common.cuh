@@ -6,6 +6,8 @@
 // writes a NUL-terminated message into the caller's (err, errlen) buffer.
 #pragma once
 
+#include <atomic>
+
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -122,6 +124,13 @@ inline bool pdl_enabled() {
   return on == 1;
 }
 
+// Kernels launched by this library since it was loaded (host-side count of
+// launch calls, stream capture included; read with xb_launch_count).
+inline std::atomic<unsigned long long>& launch_counter() {
+  static std::atomic<unsigned long long> n{0};
+  return n;
+}
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                             Args... args) {
@@ -135,6 +144,7 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  launch_counter().fetch_add(1, std::memory_order_relaxed);
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 

@@ -29,3 +29,12 @@ extern "C" int xb_device_name(int device, char* buf, size_t buf_len, int* sm_cou
   if (sm_count) *sm_count = p.multiProcessorCount;
   return XB_OK;
 }
+
+extern "C" int xb_launch_count(uint64_t* count, char* err, size_t errlen) {
+  if (!count) {
+    xb::set_err(err, errlen, "xb_launch_count: null output");
+    return XB_ERR_INVALID;
+  }
+  *count = xb::launch_counter().load(std::memory_order_relaxed);
+  return XB_OK;
+}

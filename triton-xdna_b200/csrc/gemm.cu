@@ -649,6 +649,7 @@ cudaError_t launch_pairs(void (*kernel)(KArgs...), unsigned grid, unsigned block
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  launch_counter().fetch_add(1, std::memory_order_relaxed);
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 

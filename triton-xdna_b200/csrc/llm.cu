@@ -45,6 +45,40 @@ __global__ void __launch_bounds__(256) embedding_kernel(const bf16* __restrict__
   for (int64_t v = lane; v < dim / 8; v += 32) dst[v] = __ldg(src + v);
 }
 
+// out[m, :] = bf16(table[ids[m], :] + pos_table[pos_offset + m % seq, :]):
+// token plus learned position embedding, one rounding of the fp32 sum (the
+// bf16 + bf16 add of examples/gpt2/model.py:872-876).
+__global__ void __launch_bounds__(256) embedding_pos_kernel(const bf16* __restrict__ table,
+                                                            const bf16* __restrict__ pos_table,
+                                                            const int64_t* __restrict__ ids, bf16* __restrict__ out,
+                                                            int64_t rows, int64_t dim, int64_t vocab, int seq,
+                                                            int pos_offset, int* __restrict__ bad) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int64_t id = ids[row];
+  int4* dst = reinterpret_cast<int4*>(out + row * dim);
+  if (id < 0 || id >= vocab) {  // out-of-range token: flag it, write zeros
+    if (lane == 0) atomicExch(bad, 1);
+    for (int64_t v = lane; v < dim / 8; v += 32) dst[v] = make_int4(0, 0, 0, 0);
+    return;
+  }
+  const int4* a = reinterpret_cast<const int4*>(table + id * dim);
+  const int4* p = reinterpret_cast<const int4*>(pos_table + (int64_t)(pos_offset + (int)(row % seq)) * dim);
+  for (int64_t v = lane; v < dim / 8; v += 32) {
+    int4 x = __ldg(a + v), y = __ldg(p + v);
+    const bf16* xe = reinterpret_cast<const bf16*>(&x);
+    const bf16* ye = reinterpret_cast<const bf16*>(&y);
+    int4 o;
+    bf16* oe = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) oe[e] = __float2bfloat16_rn(__bfloat162float(xe[e]) + __bfloat162float(ye[e]));
+    dst[v] = o;
+  }
+}
+
 // ----------------------------------------------------------------------------- RoPE + KV write
 
 // One CTA per token; thread j of the CTA handles head slot j / (D/2) and pair
@@ -65,8 +99,9 @@ __global__ void __launch_bounds__(1024) rope_kv_kernel(const bf16* __restrict__ 
   const int b = (int)(m / S);
   const int pos = pos_offset + s;
   const bf16* xrow = qkv + m * (int64_t)(slots * D);
-  const float* cr = cos_t + (int64_t)pos * D;
-  const float* sr = sin_t + (int64_t)pos * D;
+  const bool rotate = cos_t != nullptr;  // no tables: heads are copied (learned positions)
+  const float* cr = rotate ? cos_t + (int64_t)pos * D : nullptr;
+  const float* sr = rotate ? sin_t + (int64_t)pos * D : nullptr;
   for (int j = threadIdx.x; j < slots * half; j += blockDim.x) {
     const int slot = j / half;
     const int i = j - slot * half;
@@ -77,12 +112,17 @@ __global__ void __launch_bounds__(1024) rope_kv_kernel(const bf16* __restrict__ 
       dst[i + half] = x[i + half];
       continue;
     }
+    bf16* dst = slot < H ? q_out + (((int64_t)b * H + slot) * S + s) * D
+                         : k_cache + (((int64_t)b * KVH + (slot - H)) * smax + pos) * D;
+    if (!rotate) {
+      dst[i] = x[i];
+      dst[i + half] = x[i + half];
+      continue;
+    }
     const float x0 = __bfloat162float(x[i]);
     const float x1 = __bfloat162float(x[i + half]);
     const float y0 = __fadd_rn(__fmul_rn(x0, cr[i]), __fmul_rn(-x1, sr[i]));
     const float y1 = __fadd_rn(__fmul_rn(x1, cr[i + half]), __fmul_rn(x0, sr[i + half]));
-    bf16* dst = slot < H ? q_out + (((int64_t)b * H + slot) * S + s) * D
-                         : k_cache + (((int64_t)b * KVH + (slot - H)) * smax + pos) * D;
     dst[i] = __float2bfloat16_rn(y0);
     dst[i + half] = __float2bfloat16_rn(y1);
   }
@@ -523,6 +563,57 @@ extern "C" int xb_embedding_bf16(const void* table, const int64_t* ids, void* ou
   return check_launch("xb_embedding_bf16", err, errlen);
 }
 
+extern "C" int xb_token_status(void* stream, int* status, char* err, size_t errlen) {
+  if (!status) {
+    set_err(err, errlen, "xb_token_status: null output");
+    return XB_ERR_INVALID;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(status, g_bad_token, sizeof(int), 0, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(g_bad_token, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    set_err(err, errlen, "xb_token_status: %s", cudaGetErrorString(e));
+    return XB_ERR_CUDA;
+  }
+  return XB_OK;
+}
+
+extern "C" int xb_embedding_pos_bf16(const void* table, const void* pos_table, const int64_t* ids, void* out,
+                                     int64_t rows, int64_t seq, int64_t dim, int64_t vocab, int64_t n_pos,
+                                     int64_t pos_offset, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_embedding_pos_bf16";
+  if (rows < 0 || seq <= 0 || dim <= 0 || vocab <= 0 || n_pos <= 0 || pos_offset < 0 || (rows % seq) != 0) {
+    set_err(err, errlen, "%s: bad shape", what);
+    return XB_ERR_INVALID;
+  }
+  if (pos_offset + seq > n_pos) {
+    set_err(err, errlen, "%s: positions %lld..%lld exceed the position table (%lld)", what, (long long)pos_offset,
+            (long long)(pos_offset + seq - 1), (long long)n_pos);
+    return XB_ERR_INVALID;
+  }
+  if (rows == 0) return XB_OK;
+  if (!table || !pos_table || !ids || !out) {
+    set_err(err, errlen, "%s: null pointer", what);
+    return XB_ERR_INVALID;
+  }
+  if (dim % 8 || !xb::aligned16(table) || !xb::aligned16(pos_table) || !xb::aligned16(out)) {
+    set_err(err, errlen, "%s: rows must be whole 16-byte vectors (dim %% 8 == 0, aligned)", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  int* bad = nullptr;
+  if (cudaGetSymbolAddress((void**)&bad, g_bad_token) != cudaSuccess) {
+    set_err(err, errlen, "%s: status word unavailable", what);
+    return XB_ERR_CUDA;
+  }
+  launch_k(embedding_pos_kernel, (unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream,
+           static_cast<const bf16*>(table), static_cast<const bf16*>(pos_table), ids, static_cast<bf16*>(out), rows,
+           dim, vocab, (int)seq, (int)pos_offset, bad);
+  return check_launch(what, err, errlen);
+}
+
 extern "C" int xb_rope_kv_bf16(const void* qkv, const float* cos_t, const float* sin_t, void* q_out, void* k_cache,
                                void* v_cache, int64_t batch, int64_t seq, int64_t n_head, int64_t n_kv_head,
                                int64_t head_dim, int64_t max_seq, int64_t pos_offset, void* stream, char* err,
@@ -538,7 +629,7 @@ extern "C" int xb_rope_kv_bf16(const void* qkv, const float* cos_t, const float*
     return XB_ERR_INVALID;
   }
   if (batch == 0 || seq == 0) return XB_OK;
-  if (!qkv || !cos_t || !sin_t || !q_out || !k_cache || !v_cache) {
+  if (!qkv || !q_out || !k_cache || !v_cache || (!cos_t) != (!sin_t)) {
     set_err(err, errlen, "xb_rope_kv_bf16: null pointer");
     return XB_ERR_INVALID;
   }

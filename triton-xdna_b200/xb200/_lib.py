@@ -45,6 +45,7 @@ _CTYPES = {
     "void* const*": ctypes.c_void_p,
     "void**": ctypes.POINTER(ctypes.c_void_p),
     "const uint64_t*": ctypes.c_void_p,
+    "uint64_t*": ctypes.POINTER(ctypes.c_uint64),  # host out-parameter (xb_launch_count)
     "int": ctypes.c_int,
     # host out-parameters (passed with ctypes.byref)
     "int*": ctypes.POINTER(ctypes.c_int),

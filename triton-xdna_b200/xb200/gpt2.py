@@ -1,0 +1,224 @@
+"""GPT-2 forward and greedy generation on xb200 kernels.
+
+Mirrors `GPT2Model` of the reference (examples/gpt2/model.py:431-1206) on its
+GPU path ("gpu" backend):
+
+  token + learned position embedding (bf16 add)      model.py:866-876
+  per layer: layernorm -> fused QKV linear (+bias)   model.py:1026-1031, 757-760
+             head split + KV-cache write             model.py:762-775
+             causal multi-head attention             model.py:777-800, kernels/attention.py:27-179
+             output projection (+bias), residual add model.py:829-836, 1032-1033
+             layernorm, fc (+bias), tanh GELU,       model.py:1034-1059
+             proj (+bias), residual add
+  final layernorm, tied LM head in fp32              model.py:1082-1112
+  greedy argmax generation with a KV cache           model.py:1119-1206
+
+All four sizes (gpt2, -medium, -large, -xl) share the kernels: head_dim is 64
+everywhere, hidden sizes are multiples of 8.  Hugging Face stores the
+projections as Conv1D weights [in, out]; they are transposed once at load
+into the [out, in] layout of the linear kernel (the reference passes
+`weight.t()` to `triton_linear`, model.py:640-654).
+
+Deliberate differences from the reference: biases are added in fp32 inside
+the GEMM epilogue (the reference rounds the product to bf16 and then adds the
+bias in bf16, kernels/matmul.py:276-277), the attention residual of small
+batches is added inside the projection's split-K reduction, and generation is
+batched (the reference's `generate` is batch 1 and stops at EOS; here every
+sequence runs the requested number of steps).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+from .qwen import DecodeGraphs
+
+# (n_layer, n_head, n_embd) of the four published sizes (model.py:90-108)
+GPT2_SIZES = {
+    "gpt2": (12, 12, 768),
+    "gpt2-medium": (24, 16, 1024),
+    "gpt2-large": (36, 20, 1280),
+    "gpt2-xl": (48, 25, 1600),
+}
+
+
+@dataclass
+class GPT2Config:
+    """GPT-2 dimensions (model.py:86-112): vocab 50257, 1024 positions, LN eps 1e-5."""
+
+    n_layer: int = 12
+    n_head: int = 12
+    n_embd: int = 768
+    vocab_size: int = 50257
+    n_positions: int = 1024
+    ln_eps: float = 1e-5
+
+    @classmethod
+    def variant(cls, name: str = "gpt2") -> "GPT2Config":
+        n_layer, n_head, n_embd = GPT2_SIZES[name]
+        return cls(n_layer=n_layer, n_head=n_head, n_embd=n_embd)
+
+    @property
+    def head_dim(self) -> int:
+        return self.n_embd // self.n_head
+
+    @property
+    def n_kv_head(self) -> int:
+        return self.n_head
+
+    @property
+    def mlp(self) -> int:
+        return 4 * self.n_embd
+
+
+def random_weights(cfg: GPT2Config, seed: int = 0, std: float = 0.02) -> dict:
+    """Seeded random-init bf16 weights under the Hugging Face GPT-2 state-dict
+    names the reference loads (model.py:519-563): Conv1D weights [in, out]
+    and biases N(0, std), layernorm weights 1 + N(0, std), biases N(0, std),
+    token embeddings N(0, std), position embeddings N(0, std / 2)."""
+    g = torch.Generator().manual_seed(seed)
+    D, V, P, F = cfg.n_embd, cfg.vocab_size, cfg.n_positions, cfg.mlp
+
+    def w(*shape, base=0.0, s=std):
+        return (base + s * torch.randn(shape, generator=g)).to(torch.bfloat16)
+
+    sd = {"transformer.wte.weight": w(V, D), "transformer.wpe.weight": w(P, D, s=std / 2)}
+    for i in range(cfg.n_layer):
+        p = f"transformer.h.{i}"
+        sd[f"{p}.ln_1.weight"] = w(D, base=1.0)
+        sd[f"{p}.ln_1.bias"] = w(D)
+        sd[f"{p}.attn.c_attn.weight"] = w(D, 3 * D)
+        sd[f"{p}.attn.c_attn.bias"] = w(3 * D)
+        sd[f"{p}.attn.c_proj.weight"] = w(D, D)
+        sd[f"{p}.attn.c_proj.bias"] = w(D)
+        sd[f"{p}.ln_2.weight"] = w(D, base=1.0)
+        sd[f"{p}.ln_2.bias"] = w(D)
+        sd[f"{p}.mlp.c_fc.weight"] = w(D, F)
+        sd[f"{p}.mlp.c_fc.bias"] = w(F)
+        sd[f"{p}.mlp.c_proj.weight"] = w(F, D)
+        sd[f"{p}.mlp.c_proj.bias"] = w(D)
+    sd["transformer.ln_f.weight"] = w(D, base=1.0)
+    sd["transformer.ln_f.bias"] = w(D)
+    return sd
+
+
+class KVCache:
+    """Per-layer K / V caches [B, n_head, max_seq, 64] (model.py:1119-1142)."""
+
+    def __init__(self, cfg: GPT2Config, batch: int, max_seq: int, device):
+        shape = (batch, cfg.n_head, max_seq, cfg.head_dim)
+        self.k = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(cfg.n_layer)]
+        self.v = [torch.zeros(shape, dtype=torch.bfloat16, device=device) for _ in range(cfg.n_layer)]
+        self.batch = batch
+        self.max_seq = max_seq
+        self.length = 0
+
+
+class GPT2Model:
+    def __init__(self, state_dict: dict, cfg: GPT2Config | None = None, device="cuda"):
+        self.cfg = cfg or GPT2Config()
+        c = self.cfg
+        if c.head_dim != 64 or c.n_embd % 8:
+            raise ValueError("the attention kernels take head_dim 64 and rows of whole 16-byte vectors")
+        self.device = torch.device(device)
+        dev = self.device
+
+        def t(name):
+            return state_dict[name].to(device=dev, dtype=torch.bfloat16).contiguous()
+
+        def conv1d(name):  # Conv1D [in, out] -> linear weight [out, in]
+            return state_dict[name].to(device=dev, dtype=torch.bfloat16).t().contiguous()
+
+        self.wte = t("transformer.wte.weight")
+        self.wpe = t("transformer.wpe.weight")
+        self.layers = []
+        for i in range(c.n_layer):
+            p = f"transformer.h.{i}"
+            self.layers.append({
+                "ln1_w": t(f"{p}.ln_1.weight"), "ln1_b": t(f"{p}.ln_1.bias"),
+                "qkv_w": conv1d(f"{p}.attn.c_attn.weight"), "qkv_b": t(f"{p}.attn.c_attn.bias"),
+                "proj_w": conv1d(f"{p}.attn.c_proj.weight"), "proj_b": t(f"{p}.attn.c_proj.bias"),
+                "ln2_w": t(f"{p}.ln_2.weight"), "ln2_b": t(f"{p}.ln_2.bias"),
+                "fc_w": conv1d(f"{p}.mlp.c_fc.weight"), "fc_b": t(f"{p}.mlp.c_fc.bias"),
+                "mproj_w": conv1d(f"{p}.mlp.c_proj.weight"), "mproj_b": t(f"{p}.mlp.c_proj.bias"),
+            })
+        self.lnf_w = t("transformer.ln_f.weight")
+        self.lnf_b = t("transformer.ln_f.bias")
+        self.scale = 1.0 / math.sqrt(c.head_dim)
+
+    def new_cache(self, batch: int, max_seq: int) -> KVCache:
+        if max_seq > self.cfg.n_positions:
+            raise ValueError(f"cache length {max_seq} exceeds the position table ({self.cfg.n_positions})")
+        return KVCache(self.cfg, batch, max_seq, self.device)
+
+    @torch.no_grad()
+    def forward(self, ids: torch.Tensor, cache: KVCache, last_only: bool = False) -> torch.Tensor:
+        """ids [B, S] int64 on the device; appends S positions to `cache`.
+        Returns fp32 logits [B, S, vocab], or [B, vocab] of the last position."""
+        c = self.cfg
+        B, S = ids.shape
+        if cache.batch != B:
+            raise ValueError("cache batch size differs from the input")
+        pos = cache.length
+        if pos + S > cache.max_seq:
+            raise ValueError("KV cache full")
+        M = B * S
+        D, H, HD = c.n_embd, c.n_head, c.head_dim
+        x = ops.embedding_pos(self.wte, self.wpe, ids, pos).reshape(M, D)
+        q_buf = torch.empty((B, H, S, HD), dtype=torch.bfloat16, device=self.device)
+        attn = torch.empty((M, D), dtype=torch.bfloat16, device=self.device)
+        for i, L in enumerate(self.layers):
+            xn = ops.layernorm(x, L["ln1_w"], L["ln1_b"], c.ln_eps)
+            qkv = ops.linear(xn, L["qkv_w"], L["qkv_b"])
+            ops.rope_kv(qkv, None, None, q_buf, cache.k[i], cache.v[i], B, S, H, H, HD, pos)
+            ops.attention(q_buf, cache.k[i], cache.v[i], attn, B, S, H, H, HD, pos, self.scale)
+            x = ops.linear(attn, L["proj_w"], L["proj_b"], residual=x)  # c_proj + residual add
+            xn = ops.layernorm(x, L["ln2_w"], L["ln2_b"], c.ln_eps)
+            h = ops.gelu_tanh(ops.linear(xn, L["fc_w"], L["fc_b"]))
+            x = ops.linear(h, L["mproj_w"], L["mproj_b"], residual=x)  # mlp c_proj + residual add
+        cache.length = pos + S
+        if last_only:
+            x = x.reshape(B, S, D)[:, -1, :]  # strided rows: the norm kernel gathers them
+        x = ops.layernorm(x, self.lnf_w, self.lnf_b, c.ln_eps,
+                          out=torch.empty((x.shape[0], D), dtype=torch.bfloat16, device=self.device))
+        logits = ops.linear(x, self.wte, out_dtype=torch.float32)
+        return logits if last_only else logits.reshape(B, S, c.vocab_size)
+
+    @torch.no_grad()
+    def generate(self, ids: torch.Tensor, max_new_tokens: int, cache: KVCache | None = None,
+                 graphs: DecodeGraphs | None = None):
+        """Greedy decoding (model.py:1144-1206), batched.  Returns (tokens
+        [B, max_new_tokens] int64 on the device, timing dict with CUDA-event
+        prefill / decode milliseconds)."""
+        B, S = ids.shape
+        if graphs is not None:
+            cache, toks = graphs.cache, graphs.toks
+            if (graphs.batch, graphs.prompt, graphs.new) != (B, S, max_new_tokens):
+                raise ValueError("decode graphs were captured for another shape")
+        else:
+            if cache is None:
+                cache = self.new_cache(B, S + max_new_tokens)
+            toks = torch.empty((max_new_tokens, B), dtype=torch.int64, device=self.device)
+        cache.length = 0
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        logits = self.forward(ids, cache, last_only=True)
+        ops.argmax(logits, out=toks[0])
+        e1.record()
+        if graphs is not None:
+            graphs.replay()
+        else:
+            for step in range(1, max_new_tokens):
+                logits = self.forward(toks[step - 1].view(B, 1), cache, last_only=True)
+                ops.argmax(logits, out=toks[step])
+        e2.record()
+        torch.cuda.synchronize()
+        return toks.t(), {"prefill_ms": e0.elapsed_time(e1), "decode_ms": e1.elapsed_time(e2)}
+
+    @torch.no_grad()
+    def decode_graphs(self, batch: int, prompt: int, new: int) -> DecodeGraphs:
+        return DecodeGraphs(self, batch, prompt, new)

@@ -457,12 +457,48 @@ def embedding(table, ids, out=None):
     return out
 
 
+def embedding_pos(table, pos_table, ids, pos_offset=0, out=None):
+    """out[b, s, :] = bf16(table[ids[b, s]] + pos_table[pos_offset + s]): token
+    plus learned position embedding (examples/gpt2/model.py:866-876)."""
+    _cuda(table, pos_table, ids, out)
+    if table.dtype != torch.bfloat16 or pos_table.dtype != torch.bfloat16 or ids.dtype != torch.int64:
+        raise TypeError("embedding_pos takes bf16 tables and int64 ids")
+    if ids.dim() != 2:
+        raise ValueError("ids must be [batch, seq]")
+    ids_c = ids.contiguous()
+    B, S = ids_c.shape
+    dim = table.shape[1]
+    if out is None:
+        out = torch.empty((B, S, dim), dtype=torch.bfloat16, device=table.device)
+    _lib.call("xb_embedding_pos_bf16", table.data_ptr(), pos_table.data_ptr(), ids_c.data_ptr(), out.data_ptr(),
+              B * S, S, dim, table.shape[0], pos_table.shape[0], pos_offset, _stream())
+    return out
+
+
+def launch_count() -> int:
+    """Kernels launched by the library so far (graph replays not counted)."""
+    n = ctypes.c_uint64(0)
+    _lib.call("xb_launch_count", ctypes.byref(n))
+    return n.value
+
+
+def token_status() -> int:
+    """1 if an embedding met an out-of-vocabulary id since the last call, else 0."""
+    st = ctypes.c_int(0)
+    _lib.call("xb_token_status", _stream(), ctypes.byref(st))
+    return st.value
+
+
 def rope_kv(qkv, cos_t, sin_t, q_out, k_cache, v_cache, batch, seq, n_head, n_kv_head, head_dim, pos_offset):
-    """RoPE on the fused QKV projection + KV-cache write (model.py:851-867)."""
+    """RoPE on the fused QKV projection + KV-cache write (model.py:851-867).
+    cos_t = sin_t = None: heads are split and written unrotated (GPT-2)."""
     _cuda(qkv, cos_t, sin_t, q_out, k_cache, v_cache)
-    if cos_t.shape[0] < pos_offset + seq:
+    if (cos_t is None) != (sin_t is None):
+        raise ValueError("give both RoPE tables or neither")
+    if cos_t is not None and cos_t.shape[0] < pos_offset + seq:
         raise ValueError("RoPE tables are shorter than the positions")
-    _lib.call("xb_rope_kv_bf16", qkv.data_ptr(), cos_t.data_ptr(), sin_t.data_ptr(), q_out.data_ptr(),
+    _lib.call("xb_rope_kv_bf16", qkv.data_ptr(), cos_t.data_ptr() if cos_t is not None else None,
+              sin_t.data_ptr() if sin_t is not None else None, q_out.data_ptr(),
               k_cache.data_ptr(), v_cache.data_ptr(), batch, seq, n_head, n_kv_head, head_dim, k_cache.shape[2],
               pos_offset, _stream())
 
