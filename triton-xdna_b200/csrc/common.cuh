@@ -7,6 +7,8 @@
 #pragma once
 
 #include <atomic>
+#include <mutex>
+#include <vector>
 
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -131,7 +133,22 @@ inline std::atomic<unsigned long long>& launch_counter() {
   return n;
 }
 
-template <typename... KArgs, typename... Args>
+// Every kernel of the library prefers the largest shared-memory carveout, so
+// consecutive kernels never force an SM to drain and reconfigure its L1 /
+// shared split (which would serialise them despite programmatic launch).
+inline void prefer_max_smem(const void* fn) {
+  static std::mutex mu;
+  static std::vector<const void*> done;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const void* f : done)
+    if (f == fn) return;
+  cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+  done.push_back(fn);
+}
+
+// kMaxSmem = false keeps the default carveout: the streaming elementwise and
+// pooling kernels lose bandwidth with the smallest L1.
+template <bool kMaxSmem = true, typename... KArgs, typename... Args>
 inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                             Args... args) {
   cudaLaunchConfig_t cfg = {};
@@ -144,6 +161,7 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  if (kMaxSmem) prefer_max_smem(reinterpret_cast<const void*>(kernel));
   launch_counter().fetch_add(1, std::memory_order_relaxed);
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }

@@ -216,9 +216,9 @@ int launch_unary(const void* xv, void* yv, int64_t n, Op op, cudaStream_t s, con
   constexpr int VN = Vec16<T>::N;
   int64_t nvec = (aligned16(x) && aligned16(y)) ? n / VN : 0;
   if (nvec > 0)
-    launch_k(unary_vec_kernel<T, Op>, oneshot_grid(nvec, kThreads * kUnroll), kThreads, 0, s, x, y, nvec, op);
+    launch_k<false>(unary_vec_kernel<T, Op>, oneshot_grid(nvec, kThreads * kUnroll), kThreads, 0, s, x, y, nvec, op);
   if (nvec * VN < n)
-    launch_k(unary_scalar_kernel<T, Op>, grid_for(n - nvec * VN, kThreads), kThreads, 0, s, x, y, nvec * VN, n, op);
+    launch_k<false>(unary_scalar_kernel<T, Op>, grid_for(n - nvec * VN, kThreads), kThreads, 0, s, x, y, nvec * VN, n, op);
   return check_launch(what, err, errlen);
 }
 
@@ -234,9 +234,9 @@ int launch_binary(const void* av, const void* bv, void* yv, int64_t n, Op op, cu
   constexpr int VN = Vec16<T>::N;
   int64_t nvec = (aligned16(a) && aligned16(b) && aligned16(y)) ? n / VN : 0;
   if (nvec > 0)
-    launch_k(binary_vec_kernel<T, Op>, oneshot_grid(nvec, kThreads * kUnroll), kThreads, 0, s, a, b, y, nvec, op);
+    launch_k<false>(binary_vec_kernel<T, Op>, oneshot_grid(nvec, kThreads * kUnroll), kThreads, 0, s, a, b, y, nvec, op);
   if (nvec * VN < n)
-    launch_k(binary_scalar_kernel<T, Op>, grid_for(n - nvec * VN, kThreads), kThreads, 0, s, a, b, y, nvec * VN, n,
+    launch_k<false>(binary_scalar_kernel<T, Op>, grid_for(n - nvec * VN, kThreads), kThreads, 0, s, a, b, y, nvec * VN, n,
              op);
   return check_launch(what, err, errlen);
 }

@@ -71,7 +71,9 @@ struct Cfg {
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN_CTA * 128;
   static constexpr int STAGE_BYTES = PLANES * (A_BYTES + B_BYTES);
-  static constexpr int STAGES = PAIR ? 6 : KIND == kInt16Limbs ? 3 : (BN <= 64 ? 8 : 4);
+  // BN <= 64 (small-M, swap-AB): 6 slots leave room on the SM for the small
+  // kernel before it, so the weight prefetch can overlap that kernel
+  static constexpr int STAGES = PAIR ? 6 : KIND == kInt16Limbs ? 3 : (BN <= 64 ? 6 : 4);
   static constexpr int UMMA_K = 32 / ESZ;  // 32 bytes of K per MMA
   static constexpr int KSTEPS = BK / UMMA_K;
   static constexpr int ACCS = KIND == kInt16Limbs ? 3 : 1;
@@ -192,8 +194,13 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
   const uint32_t tmem_base = tmem_base_sh;
   // Everything above touched only shared memory, TMEM and the tensor maps in
   // the kernel parameters: it overlaps the previous kernel on the stream.
-  pdl_wait();
-  pdl_trigger();
+  // The small-M producer first issues the weight loads of its first ring
+  // slots (weights are never written by an earlier kernel), then waits.
+  constexpr bool kPrefetchW = TRANS && !PAIR;
+  if (!(kPrefetchW && threadIdx.x == 0)) {
+    pdl_wait();
+    pdl_trigger();
+  }
 
   auto fail = [&]() {
     atomicExch(&g_gemm_status, XB_ERR_TIMEOUT);
@@ -208,6 +215,21 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
 #pragma unroll
       for (int s = 0; s < C::STAGES; ++s) issued[s] = 0;
       bool ok = true;
+      int npre = 0;  // ring slots whose weight (A) tile was issued before the wait
+      if constexpr (kPrefetchW) {
+        if (tile0 < args.num_tiles) {
+          int tm, tn;
+          tile_coords<GM>(tile0 / args.splits, args.tiles_m, args.tiles_n, tm, tn);
+          const int kb0 = (tile0 % args.splits) * args.kps;
+          npre = min(C::STAGES, min(kb0 + args.kps, args.kblocks) - kb0);
+          for (int i = 0; i < npre; ++i) {
+            mbar_arrive_expect_tx(&full_bar[i], C::STAGE_BYTES);
+            tma_load_2d(smem + i * C::STAGE_BYTES, &maps.a[0], &full_bar[i], (kb0 + i) * C::BK, tm * C::BM);
+          }
+        }
+        pdl_wait();
+        pdl_trigger();
+      }
       for (int t = tile0; t < args.num_tiles && ok; t += tstep) {
         int tm, tn;
         tile_coords<GM>(t / args.splits, args.tiles_m, args.tiles_n, tm, tn);
@@ -218,11 +240,12 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
-          const bool got = PAIR ? mbar_wait_cl(&empty_bar[s], ph ^ 1, kWaitLimit, &abort_flag)
-                                : mbar_wait(&empty_bar[s], ph ^ 1, kWaitLimit, &abort_flag);
+          const bool pre = (int)it < npre;  // slot armed and its A tile issued before the wait
+          const bool got = pre || (PAIR ? mbar_wait_cl(&empty_bar[s], ph ^ 1, kWaitLimit, &abort_flag)
+                                        : mbar_wait(&empty_bar[s], ph ^ 1, kWaitLimit, &abort_flag));
           if (!got) { fail(); ok = false; break; }
           // the leader's full barrier counts the bytes of both CTAs of a pair
-          if (leader) mbar_arrive_expect_tx(&full_bar[s], (PAIR ? 2 : 1) * C::STAGE_BYTES);
+          if (leader && !pre) mbar_arrive_expect_tx(&full_bar[s], (PAIR ? 2 : 1) * C::STAGE_BYTES);
           const uint32_t fb = PAIR ? mapa_u32(smem_u32(&full_bar[s]), 0) : 0u;
           auto load = [&](void* dst, const CUtensorMap* map, int32_t c0, int32_t c1) {
             if constexpr (PAIR) tma_load_2d_pair(dst, map, fb, c0, c1);
@@ -230,7 +253,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
           };
           uint8_t* st = smem + s * C::STAGE_BYTES;
           for (int p = 0; p < C::PLANES; ++p) {
-            load(st + p * C::A_BYTES, &maps.a[p], kb * C::BK, arow);
+            if (!pre) load(st + p * C::A_BYTES, &maps.a[p], kb * C::BK, arow);
             uint8_t* sb = st + C::PLANES * C::A_BYTES + p * C::B_BYTES;
             if (B_KMAJOR) {
               load(sb, &maps.b[p], kb * C::BK, bcol);
@@ -393,6 +416,44 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
             continue;
           }
         }
+        if constexpr (TRANS && !PEERS) {
+          if (args.c_tma) {
+            // C^T through shared memory: thread `lane` (one output feature)
+            // writes its 32 token values down a column of a [32 tokens][32
+            // features] staging tile -- consecutive lanes, consecutive
+            // addresses -- and one lane stores the tile with TMA (3-D map:
+            // features, tokens, K slice; the unit clips the edges).
+            const int frow0 = row - lane;
+            if (col0 >= args.n || frow0 >= args.m) continue;  // warp-uniform
+            if (args.bias && row < args.m) {
+              const float bv = __bfloat162float(static_cast<const __nv_bfloat16*>(args.bias)[row]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + bv);
+            }
+            uint8_t* stg = smem + C::STAGES * C::STAGE_BYTES + (q * 2 + (cc & 1)) * (32 * 128);
+            if (lane == 0) {
+              if (cc == 0) bulk_wait_read<0>();
+              else bulk_wait_read<1>();
+            }
+            __syncwarp();
+            if constexpr (OUT == kOutBf16) {
+              __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stg);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) st[j * 32 + lane] = __float2bfloat16_rn(__uint_as_float(v[j]));
+            } else {
+              uint32_t* st = reinterpret_cast<uint32_t*>(stg);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) st[j * 32 + lane] = v[j];
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&maps.c, stg, frow0, col0, t % args.splits);
+              bulk_commit();
+            }
+            continue;
+          }
+        }
         if (row >= args.m || col0 >= args.n) continue;
         if constexpr (OUT != kOutI32) {
           if (args.bias) {  // bias indexed by the output feature: the row of W
@@ -460,7 +521,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       if constexpr (PAIR) mbar_arrive_cluster(mapa_u32(smem_u32(&tempty_bar[buf]), 0));
       else mbar_arrive(&tempty_bar[buf]);
     }
-    if constexpr (OUT != kOutBf16 && !TRANS && !PEERS) {
+    if constexpr (!PEERS && (TRANS || OUT != kOutBf16)) {
       if (args.c_tma && lane == 0) bulk_wait_all();  // every TMA store of C has completed
       __syncwarp();
     }
@@ -521,6 +582,74 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restr
       static_cast<float*>(y)[m * ldy + n] = acc;
     }
   }
+}
+
+// Vectorised forms of the two reductions below (4 consecutive outputs per
+// thread, one CTA row per token, no 64-bit division); the summation order is
+// the same, so results are identical.  Used when every pointer and pitch is
+// aligned for 16-byte partial loads and 8-byte bf16 accesses.
+__device__ __forceinline__ void add4(float4& a, const float4 b) {
+  a.x += b.x;
+  a.y += b.y;
+  a.z += b.z;
+  a.w += b.w;
+}
+__device__ __forceinline__ float4 ld_bf16x4(const __nv_bfloat16* p) {
+  const uint2 raw = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  return make_float4(__low2float(h[0]), __high2float(h[0]), __low2float(h[1]), __high2float(h[1]));
+}
+__device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float a, float b, float c, float d) {
+  __nv_bfloat162 h[2] = {__floats2bfloat162_rn(a, b), __floats2bfloat162_rn(c, d)};
+  *reinterpret_cast<uint2*>(p) = *reinterpret_cast<uint2*>(h);
+}
+
+template <bool OUT_BF16>
+__global__ void __launch_bounds__(256) splitk_reduce4_kernel(const float* __restrict__ part, int splits, int M, int N,
+                                                             const __nv_bfloat16* __restrict__ bias,
+                                                             const __nv_bfloat16* __restrict__ residual, int64_t ldr,
+                                                             void* __restrict__ y, int64_t ldy) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.y;
+  const int n = (blockIdx.x * 256 + threadIdx.x) * 4;
+  if (n >= N) return;
+  const int64_t slice = (int64_t)M * N;
+  const float* p = part + (int64_t)m * N + n;
+  float4 acc = __ldcg(reinterpret_cast<const float4*>(p));
+  for (int s2 = 1; s2 < splits; ++s2) add4(acc, __ldcg(reinterpret_cast<const float4*>(p + s2 * slice)));
+  if (bias) add4(acc, ld_bf16x4(bias + n));
+  if constexpr (OUT_BF16) {
+    float4 r = make_float4(rbf(acc.x), rbf(acc.y), rbf(acc.z), rbf(acc.w));
+    if (residual) {
+      const float4 q = ld_bf16x4(residual + m * ldr + n);
+      r = make_float4(q.x + r.x, q.y + r.y, q.z + r.z, q.w + r.w);
+    }
+    st_bf16x4(static_cast<__nv_bfloat16*>(y) + m * ldy + n, r.x, r.y, r.z, r.w);
+  } else {
+    if (residual) add4(acc, ld_bf16x4(residual + m * ldr + n));
+    *reinterpret_cast<float4*>(static_cast<float*>(y) + m * ldy + n) = acc;
+  }
+}
+
+__global__ void __launch_bounds__(256) splitk_swiglu4_kernel(const float* __restrict__ part, int splits, int M,
+                                                             int n_out, __nv_bfloat16* __restrict__ y, int64_t ldy) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.y;
+  const int f = (blockIdx.x * 256 + threadIdx.x) * 4;
+  if (f >= n_out) return;
+  const int64_t slice = (int64_t)M * 2 * n_out;
+  const float* pg = part + (int64_t)m * 2 * n_out + f;
+  float4 g = __ldcg(reinterpret_cast<const float4*>(pg));
+  float4 u = __ldcg(reinterpret_cast<const float4*>(pg + n_out));
+  for (int s2 = 1; s2 < splits; ++s2) {
+    add4(g, __ldcg(reinterpret_cast<const float4*>(pg + s2 * slice)));
+    add4(u, __ldcg(reinterpret_cast<const float4*>(pg + s2 * slice + n_out)));
+  }
+  auto sw = [](float gg, float uu) { return __fmul_rn(silu_bf16path(rbf(gg)), rbf(uu)); };
+  st_bf16x4(y + m * ldy + f, sw(g.x, u.x), sw(g.y, u.y), sw(g.z, u.z), sw(g.w, u.w));
 }
 
 // The decode MLP: W stacks the gate rows [0, n_out) over the up rows
@@ -615,6 +744,27 @@ int make_map(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int esz,
   return XB_OK;
 }
 
+// 3-D map [outer2][outer1][inner] (strides in elements), box {bi, bo, 1},
+// no swizzle: plain row-major staging tiles.
+int make_map_3d(CUtensorMap* map, const void* ptr, CUtensorMapDataType dt, int esz, uint64_t inner, uint64_t outer1,
+                uint64_t outer2, uint64_t ld1, uint64_t ld2, uint32_t box_inner, uint32_t box_outer, char* err,
+                size_t errlen) {
+  EncodeTiledFn enc = encoder(err, errlen);
+  if (!enc) return XB_ERR_CUDA;
+  cuuint64_t dims[3] = {inner, outer1, outer2};
+  cuuint64_t strides[2] = {ld1 * (uint64_t)esz, ld2 * (uint64_t)esz};
+  cuuint32_t box[3] = {box_inner, box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_err(err, errlen, "cuTensorMapEncodeTiled failed (%d) for a %llux%llux%llu output", (int)r,
+            (unsigned long long)outer2, (unsigned long long)outer1, (unsigned long long)inner);
+    return XB_ERR_CUDA;
+  }
+  return XB_OK;
+}
+
 bool tma_ok(const void* p, int64_t ld, int esz) {
   return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && (ld * esz) % 16 == 0;
 }
@@ -649,6 +799,7 @@ cudaError_t launch_pairs(void (*kernel)(KArgs...), unsigned grid, unsigned block
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  prefer_max_smem(reinterpret_cast<const void*>(kernel));
   launch_counter().fetch_add(1, std::memory_order_relaxed);
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
@@ -692,15 +843,28 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   }
   // 4-byte outputs of whole-tile GEMMs leave through the TMA-store epilogue
   // when C meets the TMA alignment rules.
-  constexpr bool kStaged = OUT != kOutBf16 && !TRANS && !PEERS;
+  // Transposed (small-M) outputs too, through [tokens][features] staging tiles.
+  constexpr bool kStaged = !PEERS && (TRANS || OUT != kOutBf16);
   constexpr int kSmem = Cf::SMEM + (kStaged ? kEpiStageBytes : 0);
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
   args.c_tma = 0;
-  if (kStaged && args.splits == 1 && tma_ok(c, ldc, 4)) {
-    int rc = make_map(&maps.c, c, OUT == kOutI32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4,
-                      N, M, ldc, 32, 32, err, errlen);
-    if (rc) return rc;
-    args.c_tma = 1;
+  if constexpr (kStaged && !TRANS) {
+    if (args.splits == 1 && tma_ok(c, ldc, 4)) {
+      int rc = make_map(&maps.c, c, OUT == kOutI32 ? CU_TENSOR_MAP_DATA_TYPE_INT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                        4, N, M, ldc, 32, 32, err, errlen);
+      if (rc) return rc;
+      args.c_tma = 1;
+    }
+  }
+  if constexpr (kStaged && TRANS) {
+    const int esz = OUT == kOutBf16 ? 2 : 4;
+    if (tma_ok(c, ldc, esz) && (args.splits == 1 || (split_stride * esz) % 16 == 0)) {
+      int rc = make_map_3d(&maps.c, c, OUT == kOutBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                           esz, (uint64_t)M, (uint64_t)N, (uint64_t)args.splits, (uint64_t)ldc,
+                           (uint64_t)(args.splits == 1 ? ldc * N : split_stride), 32, 32, err, errlen);
+      if (rc) return rc;
+      args.c_tma = 1;
+    }
   }
   auto kernel = gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS, PEERS, PAIR>;
   static bool attr_set = false;
@@ -1075,6 +1239,21 @@ extern "C" int xb_linear_small_bf16(const void* X, const void* W, const void* bi
   rc = launch<kBf16, true, kOutF32, 64, true>(op, part, nullptr, N, M, K, N, s, what, err, errlen, splits, M * N);
   if (rc) return rc;
   const int64_t total = M * N;
+  const bool vec = N % 4 == 0 && M <= 65535 && (!bias || (reinterpret_cast<uintptr_t>(bias) & 7) == 0) &&
+                   (!residual || ((reinterpret_cast<uintptr_t>(residual) & 7) == 0 && ldr % 4 == 0)) &&
+                   (reinterpret_cast<uintptr_t>(Y) & 15) == 0 && ldy % 4 == 0;
+  if (vec) {
+    const dim3 g4((unsigned)((N / 4 + 255) / 256), (unsigned)M);
+    const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(bias);
+    const __nv_bfloat16* rp = static_cast<const __nv_bfloat16*>(residual);
+    if (out_dtype == XB_DT_BF16)
+      launch_k(splitk_reduce4_kernel<true>, g4, 256, 0, s, (const float*)part, splits, (int)M, (int)N, bp, rp, ldr, Y,
+               ldy);
+    else
+      launch_k(splitk_reduce4_kernel<false>, g4, 256, 0, s, (const float*)part, splits, (int)M, (int)N, bp, rp, ldr,
+               Y, ldy);
+    return check_launch(what, err, errlen);
+  }
   int64_t grid = (total + 255) / 256;
   if (grid > 148 * 16) grid = 148 * 16;
   if (out_dtype == XB_DT_BF16)
@@ -1120,6 +1299,12 @@ extern "C" int xb_linear_small_swiglu_bf16(const void* X, const void* W, void* Y
   const int kps = (kblocks + splits - 1) / splits;
   splits = (kblocks + kps - 1) / kps;  // the count launch() used
   const int64_t total = M * n_out;
+  if (n_out % 4 == 0 && M <= 65535 && (reinterpret_cast<uintptr_t>(Y) & 7) == 0 && ldy % 4 == 0) {
+    const dim3 g4((unsigned)((n_out / 4 + 255) / 256), (unsigned)M);
+    launch_k(splitk_swiglu4_kernel, g4, 256, 0, s, (const float*)part, splits, (int)M, (int)n_out,
+             static_cast<__nv_bfloat16*>(Y), ldy);
+    return check_launch(what, err, errlen);
+  }
   int64_t grid = (total + 255) / 256;
   if (grid > 148 * 16) grid = 148 * 16;
   launch_k(splitk_swiglu_kernel, (unsigned)grid, 256, 0, s, (const float*)part, splits, M, n_out,

@@ -319,31 +319,66 @@ __global__ void __launch_bounds__(128) attn_decode_split_kernel(const bf16* __re
                                                                 const bf16* __restrict__ vc, float* __restrict__ ws,
                                                                 int H, int KVH, int smax, int total, int nchunks,
                                                                 float scale_log2) {
-  pdl_wait();
-  pdl_trigger();
+  // K rows are padded to 72 elements (144 bytes) so thread t reading row t
+  // with 16-byte loads is bank-conflict free; the P@V partial sums reuse the
+  // K buffer once the scores are done.
+  constexpr int kKPad = kHD + 8;
+  __shared__ __align__(16) bf16 vs[kDecChunk][kHD];
+  __shared__ __align__(16) bf16 ks[kDecChunk * kKPad];
   __shared__ float qs[NREP][kHD];
   __shared__ float ps[NREP][kDecChunk];
-  __shared__ float red[4][NREP][kHD];
   __shared__ float stat[NREP][2];
+  static_assert(4 * NREP * kHD * sizeof(float) <= sizeof(ks), "partial sums fit the K buffer");
+  float(*red)[NREP][kHD] = reinterpret_cast<float(*)[NREP][kHD]>(ks);
   const int b = blockIdx.x, kvh = blockIdx.y, chunk = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int k0 = chunk * kDecChunk;
   const int nk = min(kDecChunk, total - k0);
-  for (int i = tid; i < NREP * kHD; i += 128)
-    qs[i / kHD][i % kHD] = __bfloat162float(q[((int64_t)b * H + kvh * NREP + i / kHD) * kHD + i % kHD]);
-  __syncthreads();
   const bf16* kp = kc + ((int64_t)(b * KVH + kvh) * smax + k0) * kHD;
   const bf16* vp = vc + ((int64_t)(b * KVH + kvh) * smax + k0) * kHD;
+  pdl_wait();
+  pdl_trigger();
+  // Every global load of the CTA is issued up front with coalesced 16-byte
+  // cp.async copies (consecutive threads, consecutive addresses): the K chunk
+  // (group 0), the V chunk (group 1), then q.
+#pragma unroll
+  for (int j = 0; j < kDecChunk * kHD / 8 / 128; ++j) {
+    const int i = tid + 128 * j;
+    const int r = i >> 3, c8 = (i & 7) * 8;
+    if (r < nk)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                       (uint32_t)__cvta_generic_to_shared(&ks[r * kKPad + c8])),
+                   "l"(kp + (int64_t)r * kHD + c8)
+                   : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+#pragma unroll
+  for (int j = 0; j < kDecChunk * kHD / 8 / 128; ++j) {
+    const int i = tid + 128 * j;
+    const int r = i >> 3, c8 = (i & 7) * 8;
+    if (r < nk)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(&vs[r][c8])),
+                   "l"(vp + (int64_t)r * kHD + c8)
+                   : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  for (int i = tid; i < NREP * kHD; i += 128)
+    qs[i / kHD][i % kHD] = __bfloat162float(q[((int64_t)b * H + kvh * NREP + i / kHD) * kHD + i % kHD]);
+  asm volatile("cp.async.wait_group 1;" ::: "memory");  // this thread's K copies have landed
+  __syncthreads();
+  int4 kr[kHD / 8];
+  if (tid < nk) {
+#pragma unroll
+    for (int c = 0; c < kHD / 8; ++c) kr[c] = *reinterpret_cast<const int4*>(&ks[tid * kKPad + c * 8]);
+  }
 
   if (tid < nk) {
     float acc[NREP];
 #pragma unroll
     for (int r = 0; r < NREP; ++r) acc[r] = 0.0f;
-    const int4* krow = reinterpret_cast<const int4*>(kp + (int64_t)tid * kHD);
 #pragma unroll
     for (int c = 0; c < kHD / 8; ++c) {
-      const int4 raw = __ldg(krow + c);
-      const __nv_bfloat162* kv = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const __nv_bfloat162* kv = reinterpret_cast<const __nv_bfloat162*>(&kr[c]);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float kx = __low2float(kv[e]), ky = __high2float(kv[e]);
@@ -382,14 +417,15 @@ __global__ void __launch_bounds__(128) attn_decode_split_kernel(const bf16* __re
       stat[r][1] = sum;
     }
   }
-  __syncthreads();
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();  // V landed; every thread is past its K reads (red reuses ks)
   float ax[NREP], ay[NREP];
 #pragma unroll
   for (int r = 0; r < NREP; ++r) ax[r] = ay[r] = 0.0f;
   const int kend = min(32 * warp + 32, nk);
-#pragma unroll 4
+#pragma unroll 8
   for (int k = 32 * warp; k < kend; ++k) {
-    const __nv_bfloat162 vv = reinterpret_cast<const __nv_bfloat162*>(vp + (int64_t)k * kHD)[lane];
+    const __nv_bfloat162 vv = *reinterpret_cast<const __nv_bfloat162*>(&vs[k][2 * lane]);
     const float vx = __low2float(vv), vy = __high2float(vv);
 #pragma unroll
     for (int r = 0; r < NREP; ++r) {
@@ -558,7 +594,7 @@ extern "C" int xb_embedding_bf16(const void* table, const int64_t* ids, void* ou
     set_err(err, errlen, "xb_embedding_bf16: status word unavailable");
     return XB_ERR_CUDA;
   }
-  launch_k(embedding_kernel, (unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream, static_cast<const bf16*>(table),
+  launch_k<false>(embedding_kernel, (unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream, static_cast<const bf16*>(table),
            ids, static_cast<bf16*>(out), rows, dim, vocab, bad);
   return check_launch("xb_embedding_bf16", err, errlen);
 }
@@ -608,7 +644,7 @@ extern "C" int xb_embedding_pos_bf16(const void* table, const void* pos_table, c
     set_err(err, errlen, "%s: status word unavailable", what);
     return XB_ERR_CUDA;
   }
-  launch_k(embedding_pos_kernel, (unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream,
+  launch_k<false>(embedding_pos_kernel, (unsigned)((rows + 7) / 8), 256, 0, (cudaStream_t)stream,
            static_cast<const bf16*>(table), static_cast<const bf16*>(pos_table), ids, static_cast<bf16*>(out), rows,
            dim, vocab, (int)seq, (int)pos_offset, bad);
   return check_launch(what, err, errlen);
@@ -639,7 +675,7 @@ extern "C" int xb_rope_kv_bf16(const void* qkv, const float* cos_t, const float*
     set_err(err, errlen, "xb_rope_kv_bf16: too many tokens");
     return XB_ERR_UNSUPPORTED;
   }
-  launch_k(rope_kv_kernel, (unsigned)(batch * seq), threads, 0, (cudaStream_t)stream, static_cast<const bf16*>(qkv),
+  launch_k<false>(rope_kv_kernel, (unsigned)(batch * seq), threads, 0, (cudaStream_t)stream, static_cast<const bf16*>(qkv),
            cos_t, sin_t, static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache), (int)seq,
            (int)n_head, (int)n_kv_head, (int)head_dim, (int)max_seq, (int)pos_offset);
   return check_launch("xb_rope_kv_bf16", err, errlen);
@@ -735,6 +771,6 @@ extern "C" int xb_argmax_f32(const float* x, int64_t rows, int64_t cols, int64_t
     set_err(err, errlen, "xb_argmax_f32: null pointer");
     return XB_ERR_INVALID;
   }
-  launch_k(argmax_kernel, (unsigned)rows, 1024, 0, (cudaStream_t)stream, x, cols, ld, idx);
+  launch_k<false>(argmax_kernel, (unsigned)rows, 1024, 0, (cudaStream_t)stream, x, cols, ld, idx);
   return check_launch("xb_argmax_f32", err, errlen);
 }

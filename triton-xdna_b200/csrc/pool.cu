@@ -78,11 +78,11 @@ int run_pool(const void* xv, void* yv, int64_t planes, int64_t h, int64_t w, cud
   if (w % (2 * VN) == 0 && ow % VN == 0 && aligned16(x) && aligned16(y)) {
     int64_t total = planes * oh * (ow / VN);
     int64_t grid = (total + 255) / 256;
-    launch_k(pool_vec_kernel<T>, (unsigned)(grid < cap ? grid : cap), 256, 0, s, x, y, planes, h, w, oh, ow);
+    launch_k<false>(pool_vec_kernel<T>, (unsigned)(grid < cap ? grid : cap), 256, 0, s, x, y, planes, h, w, oh, ow);
   } else {
     int64_t total = planes * oh * ow;
     int64_t grid = (total + 255) / 256;
-    launch_k(pool_scalar_kernel<T>, (unsigned)(grid < cap ? grid : cap), 256, 0, s, x, y, planes, h, w, oh, ow);
+    launch_k<false>(pool_scalar_kernel<T>, (unsigned)(grid < cap ? grid : cap), 256, 0, s, x, y, planes, h, w, oh, ow);
   }
   return check_launch("xb_avg_pool2d_2x2", err, errlen);
 }

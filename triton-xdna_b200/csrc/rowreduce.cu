@@ -64,7 +64,11 @@ __device__ __forceinline__ float group_reduce(float v, float* red) {
   return v;
 }
 
-template <typename T, int GROUP, int VPT, int OP>
+// DECODE (no effect on the arithmetic) makes a separate copy of the kernel
+// for launches of at most 256 rows, which prefers the largest shared-memory
+// carveout: a decode step's norm then shares the SMs with the weight
+// prefetch of the GEMM after it, while large batches keep the L1 they need.
+template <typename T, int GROUP, int VPT, int OP, int DECODE = 0>
 __global__ void __launch_bounds__(GROUP > 32 ? GROUP : 256) row_vec_kernel(RowArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -262,7 +266,13 @@ void launch_vec(const RowArgs& a, cudaStream_t s) {
   constexpr int CTA = GROUP > 32 ? GROUP : 256;
   constexpr int RPC = CTA / GROUP;
   const int64_t grid = (a.rows + RPC - 1) / RPC;
-  launch_k(row_vec_kernel<T, GROUP, VPT, OP>, (unsigned)grid, CTA, 0, s, a);
+  if constexpr (GROUP > 32 && GROUP <= 128) {
+    if (a.rows <= 256) {
+      launch_k<true>(row_vec_kernel<T, GROUP, VPT, OP, 1>, (unsigned)grid, CTA, 0, s, a);
+      return;
+    }
+  }
+  launch_k<false>(row_vec_kernel<T, GROUP, VPT, OP>, (unsigned)grid, CTA, 0, s, a);
 }
 
 // Pick (GROUP, VPT) for a row of nvec vectors; returns false if the row does
@@ -327,7 +337,7 @@ int run_row(const RowArgs& a, cudaStream_t s, const char* what, char* err, size_
   const bool vec_ok = a.cols % VN == 0 && a.xs % VN == 0 && a.ys % VN == 0 && aligned16(a.x) && aligned16(a.y) &&
                       (!a.w || aligned16(a.w)) && (!a.b || aligned16(a.b));
   if (!(vec_ok && dispatch_vec<T, OP>(a, a.cols / VN, s)))
-    launch_k(row_generic_kernel<T, OP>, (unsigned)a.rows, 256, 0, s, a);
+    launch_k<false>(row_generic_kernel<T, OP>, (unsigned)a.rows, 256, 0, s, a);
   return check_launch(what, err, errlen);
 }
 
