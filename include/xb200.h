@@ -259,6 +259,42 @@ XB_API int xb_linear_small_swiglu_bf16(const void* X, const void* W, void* Y,
                                        void* workspace, size_t workspace_bytes,
                                        void* stream, char* err, size_t errlen);
 
+/* Decode-step fusions of the small-M linear (one token per sequence, M =
+ * batch <= 65535 rows), each a split-K GEMM into `workspace` (the bytes
+ * xb_linear_small_plan reports for M, N, K) plus one finishing kernel.
+ *
+ * xb_linear_small_rope_kv_bf16: the fused QKV projection of a decode token
+ * finished into attention inputs: qkv = X @ W^T + bias (W [(H + 2 KVH) * D,
+ * K]), rounded to bf16, then RoPE of the query and key heads at position
+ * pos_offset (cos/sin fp32 tables [>= pos_offset + 1, D]; both NULL: no
+ * rotation, for learned positions) written to q [batch, H, 1, D] and the K /
+ * V caches [batch, KVH, max_seq, D] at row pos_offset.  Replaces
+ * xb_linear_small_bf16 + xb_rope_kv_bf16 on the decode path
+ * (examples/qwen2_5/model.py:836-867; examples/gpt2/model.py:757-775).
+ *
+ * xb_linear_small_residual_norm_bf16: Y = residual + bf16(X @ W^T + bias)
+ * (bf16, the residual stream) and Yn = norm(Y) (bf16): norm_kind 0 is
+ * RMSNorm (Y * rsqrt(mean(Y^2) + eps) * norm_w), 1 is LayerNorm ((Y - mean) *
+ * rsqrt(var + eps) * norm_w + norm_b).  N % 4 == 0, N <= 4096.  Replaces the
+ * o_proj / down_proj linear, the residual add and the following norm
+ * (examples/qwen2_5/model.py:1045-1061; examples/gpt2/model.py:1032-1059). */
+XB_API int xb_linear_small_rope_kv_bf16(const void* X, const void* W,
+                                        const void* bias, const float* cos_t,
+                                        const float* sin_t, void* q_out,
+                                        void* k_cache, void* v_cache,
+                                        int64_t batch, int64_t n_head,
+                                        int64_t n_kv_head, int64_t head_dim,
+                                        int64_t max_seq, int64_t pos_offset,
+                                        int64_t K, int64_t ldx, int64_t ldw,
+                                        void* workspace, size_t workspace_bytes,
+                                        void* stream, char* err, size_t errlen);
+XB_API int xb_linear_small_residual_norm_bf16(
+    const void* X, const void* W, const void* bias, const void* residual,
+    void* Y, void* Yn, const void* norm_w, const void* norm_b, float eps,
+    int norm_kind, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+    int64_t ldr, int64_t ldy, int64_t ldn, void* workspace,
+    size_t workspace_bytes, void* stream, char* err, size_t errlen);
+
 /* ---------------------------------------------------------------------------
  * N-sharded GEMM across the GPUs of one node (one process per GPU).  The
  * reference runs on one device; this is the multi-GPU form of its GEMM

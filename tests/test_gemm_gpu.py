@@ -250,3 +250,49 @@ def test_four_byte_output_with_unaligned_pitch(M, N, K):
     torch.testing.assert_close(f_full[:, :N].cpu(), O.matmul_bf16_f32acc(x, y), atol=1e-4, rtol=1e-4)
     assert torch.all(f_full[:, N].cpu() == 5.0)
     _status_ok()
+
+
+@pytest.mark.parametrize("rope", [True, False])
+def test_fused_decode_qkv_rope_equals_unfused(rope):
+    """linear_rope_kv = linear (fp32 bias, bf16 round) then rope_kv, bit for bit."""
+    from oracle.qwen import rope_tables
+    B, H, KVH, D, smax, pos, K = 5, 14, 2, 64, 48, 17, 896
+    g = torch.Generator().manual_seed(31)
+    x = (torch.randn(B, K, generator=g) / 4).to(torch.bfloat16).cuda()
+    w = (torch.randn((H + 2 * KVH) * D, K, generator=g) / 16).to(torch.bfloat16).cuda()
+    b = (torch.randn((H + 2 * KVH) * D, generator=g) / 4).to(torch.bfloat16).cuda()
+    cos, sin = (t.cuda() for t in rope_tables(D, 64, 1e6)) if rope else (None, None)
+    outs = []
+    for fused in (True, False):
+        q = torch.empty((B, H, 1, D), dtype=torch.bfloat16, device="cuda")
+        kc = torch.zeros((B, KVH, smax, D), dtype=torch.bfloat16, device="cuda")
+        vc = torch.zeros_like(kc)
+        if fused:
+            ops.linear_rope_kv(x, w, b, cos, sin, q, kc, vc, H, KVH, D, pos)
+        else:
+            ops.rope_kv(ops.linear(x, w, b), cos, sin, q, kc, vc, B, 1, H, KVH, D, pos)
+        outs.append((q.cpu(), kc.cpu(), vc.cpu()))
+    for a, c in zip(*outs):
+        assert torch.equal(a, c)
+    _status_ok()
+
+
+@pytest.mark.parametrize("kind,N,K,bias", [("rms", 896, 896, False), ("rms", 896, 4864, False),
+                                           ("layer", 768, 3072, True), ("layer", 1600, 1600, True)])
+def test_fused_decode_residual_norm_equals_unfused(kind, N, K, bias):
+    """linear_residual_norm: y bit-identical to linear(residual=...), the norm
+    within one bf16 rounding of the row-norm kernel (reduction order)."""
+    M = 7
+    g = torch.Generator().manual_seed(32)
+    x = (torch.randn(M, K, generator=g) / 4).to(torch.bfloat16).cuda()
+    w = (torch.randn(N, K, generator=g) / 16).to(torch.bfloat16).cuda()
+    bv = (torch.randn(N, generator=g) / 4).to(torch.bfloat16).cuda() if bias else None
+    r = torch.randn(M, N, generator=g).to(torch.bfloat16).cuda()
+    nw = (1 + 0.1 * torch.randn(N, generator=g)).to(torch.bfloat16).cuda()
+    nb = (0.1 * torch.randn(N, generator=g)).to(torch.bfloat16).cuda() if kind == "layer" else None
+    y, yn = ops.linear_residual_norm(x, w, bv, r, nw, nb, eps=1e-5, kind=kind)
+    y_ref = ops.linear(x, w, bv, residual=r)
+    assert torch.equal(y.cpu(), y_ref.cpu())
+    yn_ref = ops.rms_norm(y_ref, nw, 1e-5) if kind == "rms" else ops.layernorm(y_ref, nw, nb, 1e-5)
+    torch.testing.assert_close(yn.float().cpu(), yn_ref.float().cpu(), atol=2e-2, rtol=8e-3)
+    _status_ok()

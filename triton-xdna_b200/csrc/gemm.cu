@@ -652,6 +652,148 @@ __global__ void __launch_bounds__(256) splitk_swiglu4_kernel(const float* __rest
   st_bf16x4(y + m * ldy + f, sw(g.x, u.x), sw(g.y, u.y), sw(g.z, u.z), sw(g.w, u.w));
 }
 
+// ---- decode-step fusions of the split-K reduction -------------------------
+//
+// reduce_rope_kv_kernel: the fused QKV projection of one decode token per CTA
+// (M = batch rows, one position), finished in place of the reduce + RoPE/KV
+// kernels: v = bf16(sum_s part + bias) exactly as the reduction rounds it,
+// then the rotate-half RoPE of the query and key heads (skipped without
+// tables) with the same fp32 products and sums as the stand-alone RoPE
+// kernel, written to q [B, H, 1, D] and the K / V caches at `pos`.
+__global__ void __launch_bounds__(1024) reduce_rope_kv_kernel(const float* __restrict__ part, int splits, int M,
+                                                              int N, const __nv_bfloat16* __restrict__ bias,
+                                                              const float* __restrict__ cos_t,
+                                                              const float* __restrict__ sin_t,
+                                                              __nv_bfloat16* __restrict__ q_out,
+                                                              __nv_bfloat16* __restrict__ k_cache,
+                                                              __nv_bfloat16* __restrict__ v_cache, int H, int KVH,
+                                                              int D, int smax, int pos) {
+  pdl_wait();
+  pdl_trigger();
+  const int m = blockIdx.x;
+  const int half = D / 2;
+  const int slots = H + 2 * KVH;
+  const int64_t slice = (int64_t)M * N;
+  const float* pr = part + (int64_t)m * N;
+  for (int j = threadIdx.x; j < slots * half; j += blockDim.x) {
+    const int slot = j / half;
+    const int i = j - slot * half;
+    const int f0 = slot * D + i, f1 = f0 + half;
+    float a0 = __ldcg(pr + f0), a1 = __ldcg(pr + f1);
+    for (int s2 = 1; s2 < splits; ++s2) {
+      a0 += __ldcg(pr + s2 * slice + f0);
+      a1 += __ldcg(pr + s2 * slice + f1);
+    }
+    if (bias) {
+      a0 += __bfloat162float(bias[f0]);
+      a1 += __bfloat162float(bias[f1]);
+    }
+    const __nv_bfloat16 x0b = __float2bfloat16_rn(a0), x1b = __float2bfloat16_rn(a1);
+    if (slot >= H + KVH) {
+      __nv_bfloat16* dst = v_cache + (((int64_t)m * KVH + (slot - H - KVH)) * smax + pos) * D;
+      dst[i] = x0b;
+      dst[i + half] = x1b;
+      continue;
+    }
+    __nv_bfloat16* dst = slot < H ? q_out + ((int64_t)m * H + slot) * D
+                                  : k_cache + (((int64_t)m * KVH + (slot - H)) * smax + pos) * D;
+    if (!cos_t) {
+      dst[i] = x0b;
+      dst[i + half] = x1b;
+      continue;
+    }
+    const float x0 = __bfloat162float(x0b), x1 = __bfloat162float(x1b);
+    const float* cr = cos_t + (int64_t)pos * D;
+    const float* sr = sin_t + (int64_t)pos * D;
+    dst[i] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(x0, cr[i]), __fmul_rn(-x1, sr[i])));
+    dst[i + half] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(x1, cr[i + half]), __fmul_rn(x0, sr[i + half])));
+  }
+}
+
+// reduce_residual_norm_kernel: one CTA per row m of a decode step.
+//   y  = bf16(residual + bf16(sum_s part + bias))      (the residual stream)
+//   yn = bf16(norm(y))                                  (input of the next linear)
+// NORM 0: y * rsqrt(mean(y^2) + eps) * w (RMSNorm); NORM 1: (y - mean) *
+// rsqrt(var + eps) * w + b (LayerNorm), both in fp32 over the bf16 y.  Each
+// thread keeps its 4-column groups in registers (N <= 4096).
+template <int NORM>
+__global__ void __launch_bounds__(256) reduce_residual_norm_kernel(
+    const float* __restrict__ part, int splits, int M, int N, const __nv_bfloat16* __restrict__ bias,
+    const __nv_bfloat16* __restrict__ residual, int64_t ldr, __nv_bfloat16* __restrict__ y, int64_t ldy,
+    __nv_bfloat16* __restrict__ yn, int64_t ldn, const __nv_bfloat16* __restrict__ nw,
+    const __nv_bfloat16* __restrict__ nb, float eps) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[8];
+  __shared__ float bcast;
+  const int m = blockIdx.x, tid = threadIdx.x;
+  const int64_t slice = (int64_t)M * N;
+  float4 v[4];
+  float s1 = 0.0f;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int n = (tid + 256 * g) * 4;
+    v[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (n >= N) continue;
+    const float* p = part + (int64_t)m * N + n;
+    float4 acc = __ldcg(reinterpret_cast<const float4*>(p));
+    for (int s2 = 1; s2 < splits; ++s2) add4(acc, __ldcg(reinterpret_cast<const float4*>(p + s2 * slice)));
+    if (bias) add4(acc, ld_bf16x4(bias + n));
+    const float4 r = ld_bf16x4(residual + m * ldr + n);
+    const float4 o = make_float4(rbf(r.x + rbf(acc.x)), rbf(r.y + rbf(acc.y)), rbf(r.z + rbf(acc.z)),
+                                 rbf(r.w + rbf(acc.w)));
+    st_bf16x4(y + m * ldy + n, o.x, o.y, o.z, o.w);
+    v[g] = o;
+    s1 += NORM == 0 ? (o.x * o.x + o.y * o.y) + (o.z * o.z + o.w * o.w) : (o.x + o.y) + (o.z + o.w);
+  }
+  auto block_sum = [&](float x) {
+#pragma unroll
+    for (int o_ = 16; o_ > 0; o_ >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o_);
+    if ((tid & 31) == 0) red[tid >> 5] = x;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.0f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) t += red[w];
+      bcast = t;
+    }
+    __syncthreads();
+    const float r = bcast;
+    __syncthreads();
+    return r;
+  };
+  const float inv_n = 1.0f / (float)N;
+  float mean = 0.0f, rstd;
+  if constexpr (NORM == 0) {
+    rstd = __frsqrt_rn(block_sum(s1) * inv_n + eps);
+  } else {
+    mean = block_sum(s1) * inv_n;
+    float s2 = 0.0f;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int n = (tid + 256 * g) * 4;
+      if (n >= N) continue;
+      const float a = v[g].x - mean, b = v[g].y - mean, c = v[g].z - mean, d = v[g].w - mean;
+      s2 += (a * a + b * b) + (c * c + d * d);
+    }
+    rstd = __frsqrt_rn(block_sum(s2) * inv_n + eps);
+  }
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int n = (tid + 256 * g) * 4;
+    if (n >= N) continue;
+    const float4 w4 = ld_bf16x4(nw + n);
+    if constexpr (NORM == 0) {
+      st_bf16x4(yn + m * ldn + n, __fmul_rn(__fmul_rn(v[g].x, rstd), w4.x), __fmul_rn(__fmul_rn(v[g].y, rstd), w4.y),
+                __fmul_rn(__fmul_rn(v[g].z, rstd), w4.z), __fmul_rn(__fmul_rn(v[g].w, rstd), w4.w));
+    } else {
+      const float4 b4 = nb ? ld_bf16x4(nb + n) : make_float4(0.f, 0.f, 0.f, 0.f);
+      st_bf16x4(yn + m * ldn + n, (v[g].x - mean) * rstd * w4.x + b4.x, (v[g].y - mean) * rstd * w4.y + b4.y,
+                (v[g].z - mean) * rstd * w4.z + b4.z, (v[g].w - mean) * rstd * w4.w + b4.w);
+    }
+  }
+}
+
 // The decode MLP: W stacks the gate rows [0, n_out) over the up rows
 // [n_out, 2 n_out); y[m, f] = bf16(silu(bf16(g)) * bf16(u)) with g, u the
 // split-K sums of gate row f and up row f -- the same roundings as a gate
@@ -1309,6 +1451,110 @@ extern "C" int xb_linear_small_swiglu_bf16(const void* X, const void* W, void* Y
   if (grid > 148 * 16) grid = 148 * 16;
   launch_k(splitk_swiglu_kernel, (unsigned)grid, 256, 0, s, (const float*)part, splits, M, n_out,
            static_cast<__nv_bfloat16*>(Y), ldy);
+  return check_launch(what, err, errlen);
+}
+
+// Shared front half of the fused decode entries: the split-K partials of
+// X @ W^T (swap-AB small-M GEMM) into the workspace; returns the K slices used.
+static int small_partials(const void* X, const void* W, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                          void* workspace, size_t workspace_bytes, cudaStream_t s, const char* what, int* splits_out,
+                          char* err, size_t errlen) {
+  if (M <= 0 || M > 65535 || N <= 0 || K <= 0 || ldx < K || ldw < K) {
+    set_err(err, errlen, "%s: bad shape", what);
+    return XB_ERR_INVALID;
+  }
+  if (!X || !W) {
+    set_err(err, errlen, "%s: null pointer", what);
+    return XB_ERR_INVALID;
+  }
+  if (!tma_ok(X, ldx, 2) || !tma_ok(W, ldw, 2)) {
+    set_err(err, errlen, "%s: X/W must be 16-byte aligned with row pitches a multiple of 16 bytes", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  int splits = small_m_splits(N, K);
+  const size_t need = (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15) != 0) {
+    set_err(err, errlen, "%s: 16-byte aligned workspace of %zu bytes needed (%zu given)", what, need,
+            workspace_bytes);
+    return XB_ERR_INVALID;
+  }
+  Operands op{{W, nullptr}, {X, nullptr}, ldw, ldx};
+  int rc = launch<kBf16, true, kOutF32, 64, true>(op, workspace, nullptr, N, M, K, N, s, what, err, errlen, splits,
+                                                  M * N);
+  if (rc) return rc;
+  const int kblocks = (int)((K + 63) / 64);
+  const int kps = (kblocks + splits - 1) / splits;
+  *splits_out = (kblocks + kps - 1) / kps;  // the count launch() used
+  return XB_OK;
+}
+
+extern "C" int xb_linear_small_rope_kv_bf16(const void* X, const void* W, const void* bias, const float* cos_t,
+                                            const float* sin_t, void* q_out, void* k_cache, void* v_cache,
+                                            int64_t batch, int64_t n_head, int64_t n_kv_head, int64_t head_dim,
+                                            int64_t max_seq, int64_t pos_offset, int64_t K, int64_t ldx, int64_t ldw,
+                                            void* workspace, size_t workspace_bytes, void* stream, char* err,
+                                            size_t errlen) {
+  const char* what = "xb_linear_small_rope_kv_bf16";
+  cudaStream_t s = (cudaStream_t)stream;
+  if (n_head <= 0 || n_kv_head <= 0 || n_head % n_kv_head || head_dim <= 0 || head_dim % 2 || pos_offset < 0 ||
+      pos_offset >= max_seq) {
+    set_err(err, errlen, "%s: bad head layout or position", what);
+    return XB_ERR_INVALID;
+  }
+  if (!q_out || !k_cache || !v_cache || (!cos_t) != (!sin_t)) {
+    set_err(err, errlen, "%s: null pointer", what);
+    return XB_ERR_INVALID;
+  }
+  const int64_t N = (n_head + 2 * n_kv_head) * head_dim;
+  int splits = 1;
+  int rc = small_partials(X, W, batch, N, K, ldx, ldw, workspace, workspace_bytes, s, what, &splits, err, errlen);
+  if (rc) return rc;
+  const int64_t per_token = (n_head + 2 * n_kv_head) * (head_dim / 2);
+  const int threads = per_token >= 1024 ? 1024 : (int)((per_token + 31) / 32 * 32);
+  launch_k(reduce_rope_kv_kernel, (unsigned)batch, threads, 0, s, (const float*)workspace, splits, (int)batch, (int)N,
+           static_cast<const __nv_bfloat16*>(bias), cos_t, sin_t, static_cast<__nv_bfloat16*>(q_out),
+           static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), (int)n_head, (int)n_kv_head,
+           (int)head_dim, (int)max_seq, (int)pos_offset);
+  return check_launch(what, err, errlen);
+}
+
+extern "C" int xb_linear_small_residual_norm_bf16(const void* X, const void* W, const void* bias, const void* residual,
+                                                  void* Y, void* Yn, const void* norm_w, const void* norm_b, float eps,
+                                                  int norm_kind, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                                                  int64_t ldw, int64_t ldr, int64_t ldy, int64_t ldn, void* workspace,
+                                                  size_t workspace_bytes, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_linear_small_residual_norm_bf16";
+  cudaStream_t s = (cudaStream_t)stream;
+  if (norm_kind != 0 && norm_kind != 1) {
+    set_err(err, errlen, "%s: norm_kind must be 0 (RMSNorm) or 1 (LayerNorm)", what);
+    return XB_ERR_INVALID;
+  }
+  if (N % 4 || N > 4096 || ldr < N || ldy < N || ldn < N || ldr % 4 || ldy % 4 || ldn % 4) {
+    set_err(err, errlen, "%s: rows must be whole 4-element groups of at most 4096 (N = %lld)", what, (long long)N);
+    return XB_ERR_UNSUPPORTED;
+  }
+  if (!residual || !Y || !Yn || !norm_w) {
+    set_err(err, errlen, "%s: null pointer", what);
+    return XB_ERR_INVALID;
+  }
+  const void* ptrs[6] = {bias, residual, Y, Yn, norm_w, norm_b};
+  for (const void* p : ptrs)
+    if (p && (reinterpret_cast<uintptr_t>(p) & 7)) {
+      set_err(err, errlen, "%s: bf16 vectors must be 8-byte aligned", what);
+      return XB_ERR_UNSUPPORTED;
+    }
+  int splits = 1;
+  int rc = small_partials(X, W, M, N, K, ldx, ldw, workspace, workspace_bytes, s, what, &splits, err, errlen);
+  if (rc) return rc;
+  typedef __nv_bfloat16 bf;
+  if (norm_kind == 0)
+    launch_k(reduce_residual_norm_kernel<0>, (unsigned)M, 256, 0, s, (const float*)workspace, splits, (int)M, (int)N,
+             static_cast<const bf*>(bias), static_cast<const bf*>(residual), ldr, static_cast<bf*>(Y), ldy,
+             static_cast<bf*>(Yn), ldn, static_cast<const bf*>(norm_w), static_cast<const bf*>(norm_b), eps);
+  else
+    launch_k(reduce_residual_norm_kernel<1>, (unsigned)M, 256, 0, s, (const float*)workspace, splits, (int)M, (int)N,
+             static_cast<const bf*>(bias), static_cast<const bf*>(residual), ldr, static_cast<bf*>(Y), ldy,
+             static_cast<bf*>(Yn), ldn, static_cast<const bf*>(norm_w), static_cast<const bf*>(norm_b), eps);
   return check_launch(what, err, errlen);
 }
 

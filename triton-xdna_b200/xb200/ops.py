@@ -432,6 +432,54 @@ def linear_swiglu(x, w_gate_up):
     return y.reshape(*x.shape[:-1], N // 2)
 
 
+def _small_ws(x, M, N, K):
+    splits = ctypes.c_int(0)
+    need = ctypes.c_size_t(0)
+    _lib.call("xb_linear_small_plan", M, N, K, 1, ctypes.byref(splits), ctypes.byref(need))
+    return _workspace(x.device, need.value)
+
+
+def linear_rope_kv(x, w_qkv, b_qkv, cos_t, sin_t, q_out, k_cache, v_cache, n_head, n_kv_head, head_dim, pos_offset):
+    """Decode step (x [B, K], one token per sequence): qkv = x @ w_qkv^T + b,
+    rounded to bf16, RoPE (cos_t = sin_t = None: none) and the KV-cache
+    write at pos_offset, in one GEMM + one finishing kernel."""
+    _cuda(x, w_qkv, b_qkv, cos_t, sin_t, q_out, k_cache, v_cache)
+    B, K = x.shape
+    N = w_qkv.shape[0]
+    if N != (n_head + 2 * n_kv_head) * head_dim or w_qkv.shape[1] != K:
+        raise ValueError("w_qkv must be [(H + 2 KVH) * D, K]")
+    if cos_t is not None and cos_t.shape[0] <= pos_offset:
+        raise ValueError("RoPE tables are shorter than the position")
+    ws = _small_ws(x, B, N, K)
+    _lib.call("xb_linear_small_rope_kv_bf16", x.data_ptr(), w_qkv.data_ptr(),
+              b_qkv.data_ptr() if b_qkv is not None else None,
+              cos_t.data_ptr() if cos_t is not None else None, sin_t.data_ptr() if sin_t is not None else None,
+              q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), B, n_head, n_kv_head, head_dim,
+              k_cache.shape[2], pos_offset, K, _mat(x, "x"), _mat(w_qkv, "w"), ws.data_ptr(), ws.numel() * 4,
+              _stream())
+
+
+def linear_residual_norm(x, weight, bias, residual, norm_w, norm_b=None, eps=1e-6, kind="rms"):
+    """Decode step: y = residual + bf16(x @ weight^T + bias) and
+    yn = rmsnorm(y) * norm_w (kind "rms") or layernorm(y) * norm_w + norm_b
+    (kind "layer"), in one GEMM + one finishing kernel.  Returns (y, yn)."""
+    _cuda(x, weight, bias, residual, norm_w, norm_b)
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    N = weight.shape[0]
+    r2 = residual.reshape(M, N)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    yn = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    ws = _small_ws(x, M, N, K)
+    _lib.call("xb_linear_small_residual_norm_bf16", x2.data_ptr(), weight.data_ptr(),
+              bias.data_ptr() if bias is not None else None, r2.data_ptr(), y.data_ptr(), yn.data_ptr(),
+              norm_w.data_ptr(), norm_b.data_ptr() if norm_b is not None else None, float(eps),
+              0 if kind == "rms" else 1, M, N, K, _mat(x2, "x"), _mat(weight, "weight"), _mat(r2, "residual"), N, N,
+              ws.data_ptr(), ws.numel() * 4, _stream())
+    return y, yn
+
+
 def device_status() -> int:
     """Read and clear the device status word (0 = fine, -4 = a kernel timed out)."""
     st = ctypes.c_int(0)

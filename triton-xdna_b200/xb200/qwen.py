@@ -163,11 +163,26 @@ class Qwen2Model:
         x = ops.embedding(self.embed, ids.reshape(-1)).reshape(M, D)
         q_buf = torch.empty((B, H, S, HD), dtype=torch.bfloat16, device=self.device)
         attn = torch.empty((M, H * HD), dtype=torch.bfloat16, device=self.device)
+        # decode step: each linear is finished by one kernel that also does
+        # what follows it (RoPE + KV write; residual add + the next norm)
+        decode = S == 1 and M <= ops.SMALL_M
+        if decode:
+            xn = ops.rms_norm(x, self.layers[0]["input_ln"], c.rms_eps)
         for i, L in enumerate(self.layers):
-            xn = ops.rms_norm(x, L["input_ln"], c.rms_eps)
-            qkv = ops.linear(xn, L["qkv_w"], L["qkv_b"])
-            ops.rope_kv(qkv, self.cos, self.sin, q_buf, cache.k[i], cache.v[i], B, S, H, KVH, HD, pos)
+            if decode:
+                ops.linear_rope_kv(xn, L["qkv_w"], L["qkv_b"], self.cos, self.sin, q_buf, cache.k[i], cache.v[i],
+                                   H, KVH, HD, pos)
+            else:
+                xn = ops.rms_norm(x, L["input_ln"], c.rms_eps)
+                qkv = ops.linear(xn, L["qkv_w"], L["qkv_b"])
+                ops.rope_kv(qkv, self.cos, self.sin, q_buf, cache.k[i], cache.v[i], B, S, H, KVH, HD, pos)
             ops.attention(q_buf, cache.k[i], cache.v[i], attn, B, S, H, KVH, HD, pos, self.scale)
+            if decode:
+                x, xn = ops.linear_residual_norm(attn, L["o_w"], None, x, L["post_ln"], eps=c.rms_eps)
+                h = ops.linear_swiglu(xn, L["gate_up_w"])  # gate + up + silu*up, one GEMM
+                nxt = self.layers[i + 1]["input_ln"] if i + 1 < len(self.layers) else self.norm_w
+                x, xn = ops.linear_residual_norm(h, L["down_w"], None, x, nxt, eps=c.rms_eps)
+                continue
             x = ops.linear(attn, L["o_w"], residual=x)  # o_proj + residual add
             xn = ops.rms_norm(x, L["post_ln"], c.rms_eps)
             if M <= ops.SMALL_M:
@@ -176,10 +191,13 @@ class Qwen2Model:
                 h = ops.silu_mul(ops.linear(xn, L["gate_w"]), ops.linear(xn, L["up_w"]))
             x = ops.linear(h, L["down_w"], residual=x)  # down_proj + residual add
         cache.length = pos + S
-        if last_only:
-            x = x.reshape(B, S, D)[:, -1, :]  # strided rows: the norm kernel gathers them
-        x = ops.rms_norm(x, self.norm_w, c.rms_eps, out=torch.empty((x.shape[0], D), dtype=torch.bfloat16,
-                                                                     device=self.device))
+        if decode:
+            x = xn  # the last down projection already applied the final norm
+        else:
+            if last_only:
+                x = x.reshape(B, S, D)[:, -1, :]  # strided rows: the norm kernel gathers them
+            x = ops.rms_norm(x, self.norm_w, c.rms_eps, out=torch.empty((x.shape[0], D), dtype=torch.bfloat16,
+                                                                         device=self.device))
         logits = ops.linear(x, self.embed, out_dtype=torch.float32)
         return logits if last_only else logits.reshape(B, S, c.vocab_size)
 
