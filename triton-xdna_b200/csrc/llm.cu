@@ -303,19 +303,180 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const bf16* __restric
 
 // Single-token (decode) attention, split over the context: a CTA handles one
 // (batch, KV head, chunk of 128 keys) for the NREP query heads sharing that
-// KV head, so each cached key / value row is read once per step and a
-// 640-token context at batch 64 spreads over 640 CTAs.
-//   1. scores: thread t takes key t of the chunk (NREP dot products, q
-//      broadcast from shared memory);
-//   2. per head: chunk max m, P = exp2(s - m) rounded to bf16 for P@V (as
-//      the prefill kernel does), l = sum of the unrounded P;
-//   3. P@V: warp w takes keys 32w .. 32w+31, lane l dims 2l, 2l+1;
-// the partial (o, m, l) of each chunk goes to the workspace, and
-// attn_decode_combine_kernel merges the chunks (max-rescaled sums).
+// KV head (the NREP heads are the 16 rows of an mma.sync tile, rows past
+// NREP are zero), so each cached key / value row is read once per step and a
+// 640-token context at batch 64 spreads over 640 CTAs.  The chunk's K and V
+// rows stream into shared memory with coalesced cp.async copies (rows past
+// the context zero-filled); warp w then takes keys 32w .. 32w+31:
+//   S = Q K^T (mma.sync m16n8k16, fp32), the warp's row max m, P = exp2(S -
+//   m) rounded to bf16 for P V (as the prefill kernel and the reference's
+//   fused kernel do), l = sum of the unrounded P, O = P V (mma.sync);
+// the 4 warps' partials merge in shared memory, the chunk's (O, m, l) goes to
+// the workspace and attn_decode_combine_kernel merges the chunks of a head.
 constexpr int kDecChunk = 128;
 
 template <int NREP>
 __global__ void __launch_bounds__(128) attn_decode_split_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
+                                                                const bf16* __restrict__ vc, float* __restrict__ ws,
+                                                                int H, int KVH, int smax, int total, int nchunks,
+                                                                float scale_log2) {
+  static_assert(NREP >= 1 && NREP <= 16, "query heads per KV head fill one 16-row tile");
+  __shared__ __align__(16) bf16 sK[kDecChunk][kPad];
+  __shared__ __align__(16) bf16 sV[kDecChunk][kPad];
+  const int b = blockIdx.x, kvh = blockIdx.y, chunk = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int k0 = chunk * kDecChunk;
+  const int nk = min(kDecChunk, total - k0);
+  const bf16* kp = kc + ((int64_t)(b * KVH + kvh) * smax + k0) * kHD;
+  const bf16* vp = vc + ((int64_t)(b * KVH + kvh) * smax + k0) * kHD;
+  const bf16* qp = q + ((int64_t)b * H + kvh * NREP) * kHD;
+  pdl_wait();
+  pdl_trigger();
+#pragma unroll
+  for (int j = 0; j < kDecChunk * kHD / 8 / 128; ++j) {
+    const int i = tid + 128 * j;
+    const int r = i >> 3, c8 = (i & 7) * 8;
+    const int src_row = r < nk ? r : 0;     // rows past the context: zero-fill, nothing read
+    const uint32_t bytes = r < nk ? 16u : 0u;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     (uint32_t)__cvta_generic_to_shared(&sK[r][c8])),
+                 "l"(kp + (int64_t)src_row * kHD + c8), "r"(bytes)
+                 : "memory");
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     (uint32_t)__cvta_generic_to_shared(&sV[r][c8])),
+                 "l"(vp + (int64_t)src_row * kHD + c8), "r"(bytes)
+                 : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  uint32_t qa[4][4];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const int c = kk * 16 + 2 * t;
+    qa[kk][0] = g < NREP ? *reinterpret_cast<const uint32_t*>(qp + g * kHD + c) : 0u;
+    qa[kk][1] = g + 8 < NREP ? *reinterpret_cast<const uint32_t*>(qp + (g + 8) * kHD + c) : 0u;
+    qa[kk][2] = g < NREP ? *reinterpret_cast<const uint32_t*>(qp + g * kHD + c + 8) : 0u;
+    qa[kk][3] = g + 8 < NREP ? *reinterpret_cast<const uint32_t*>(qp + (g + 8) * kHD + c + 8) : 0u;
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();
+
+  const int kw = warp * 32;  // this warp's first key of the chunk
+  float sc[4][4];
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&sK[kw + nt * 8 + g][kk * 16 + 2 * t]);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&sK[kw + nt * 8 + g][kk * 16 + 8 + 2 * t]);
+      mma_bf16_16816(sc[nt], qa[kk], b0, b1);
+    }
+  }
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const bool ok = kw + nt * 8 + 2 * t + (e & 1) < nk;
+      sc[nt][e] = ok ? sc[nt][e] * scale_log2 : -INFINITY;
+      if (e < 2) mx0 = fmaxf(mx0, sc[nt][e]);
+      else mx1 = fmaxf(mx1, sc[nt][e]);
+    }
+#pragma unroll
+  for (int o_ = 1; o_ <= 2; o_ <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o_));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o_));
+  }
+  const float base0 = mx0 == -INFINITY ? 0.0f : mx0, base1 = mx1 == -INFINITY ? 0.0f : mx1;
+  float l0 = 0.0f, l1 = 0.0f;
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt) {
+    sc[nt][0] = ex2_approx(sc[nt][0] - base0);
+    sc[nt][1] = ex2_approx(sc[nt][1] - base0);
+    sc[nt][2] = ex2_approx(sc[nt][2] - base1);
+    sc[nt][3] = ex2_approx(sc[nt][3] - base1);
+    l0 += sc[nt][0] + sc[nt][1];
+    l1 += sc[nt][2] + sc[nt][3];
+  }
+#pragma unroll
+  for (int o_ = 1; o_ <= 2; o_ <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o_);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o_);
+  }
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {  // keys kw + kk*16 .. kw + kk*16 + 15
+    uint32_t pa[4];
+    pa[0] = pack_bf16(sc[2 * kk][0], sc[2 * kk][1]);
+    pa[1] = pack_bf16(sc[2 * kk][2], sc[2 * kk][3]);
+    pa[2] = pack_bf16(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+    pa[3] = pack_bf16(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+#pragma unroll
+    for (int dt = 0; dt < 8; dt += 2) {
+      const int mi = lane >> 3, r = lane & 7;
+      uint32_t vb[4];
+      ldmatrix_x4_trans(vb, &sV[kw + kk * 16 + (mi & 1) * 8 + r][dt * 8 + (mi >> 1) * 8]);
+      mma_bf16_16816(o[dt], pa, vb[0], vb[1]);
+      mma_bf16_16816(o[dt + 1], pa, vb[2], vb[3]);
+    }
+  }
+  // Merge the 4 warps' partials of the chunk (max-rescaled sums, warps in
+  // order) so the chunk leaves one (O, m, l) per head; the K buffer is free
+  // once every warp is past its P V products.
+  __shared__ float wm[4][16], wl[4][16];
+  if (t == 0) {
+    wm[warp][g] = mx0;
+    wm[warp][g + 8] = mx1;
+    wl[warp][g] = l0;
+    wl[warp][g + 8] = l1;
+  }
+  __syncthreads();
+  float* red = reinterpret_cast<float*>(&sK[0][0]);  // [4][16][64] fp32
+  static_assert(4 * 16 * kHD * sizeof(float) <= sizeof(sK), "merge buffer fits the K tile");
+  auto row_max = [&](int r) {
+    return fmaxf(fmaxf(wm[0][r], wm[1][r]), fmaxf(wm[2][r], wm[3][r]));
+  };
+  {
+    const float M0 = row_max(g), M1 = row_max(g + 8);
+    const float f0 = ex2_approx(mx0 - (M0 == -INFINITY ? 0.0f : M0));
+    const float f1 = ex2_approx(mx1 - (M1 == -INFINITY ? 0.0f : M1));
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) {
+      const int d = dt * 8 + 2 * t;
+      red[(warp * 16 + g) * kHD + d] = o[dt][0] * f0;
+      red[(warp * 16 + g) * kHD + d + 1] = o[dt][1] * f0;
+      red[(warp * 16 + g + 8) * kHD + d] = o[dt][2] * f1;
+      red[(warp * 16 + g + 8) * kHD + d + 1] = o[dt][3] * f1;
+    }
+  }
+  __syncthreads();
+  float* part = ws + ((int64_t)(b * KVH + kvh) * nchunks + chunk) * NREP * (kHD + 2);
+  for (int i = tid; i < NREP * kHD; i += 128) {
+    const int r = i / kHD, d = i % kHD;
+    part[r * (kHD + 2) + d] = ((red[r * kHD + d] + red[(16 + r) * kHD + d]) + red[(32 + r) * kHD + d]) +
+                              red[(48 + r) * kHD + d];
+  }
+  if (tid < NREP) {
+    const float M = row_max(tid);
+    const float base = M == -INFINITY ? 0.0f : M;
+    float l = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) l += wl[w][tid] * ex2_approx(wm[w][tid] - base);
+    part[tid * (kHD + 2) + kHD] = M;
+    part[tid * (kHD + 2) + kHD + 1] = l;
+  }
+}
+
+// The same partials computed on the CUDA cores, for one or two query heads
+// per KV head (GPT-2's multi-head attention), where a 16-row mma tile would
+// be mostly padding: thread t scores key t of the chunk (K rows staged in
+// shared memory, padded for conflict-free 16-byte reads), warps reduce the
+// chunk max and sum, warp w accumulates P V over keys 32w .. 32w+31.
+template <int NREP>
+__global__ void __launch_bounds__(128) attn_decode_scalar_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
                                                                 const bf16* __restrict__ vc, float* __restrict__ ws,
                                                                 int H, int KVH, int smax, int total, int nchunks,
                                                                 float scale_log2) {
@@ -742,8 +903,11 @@ extern "C" int xb_attention_bf16(const void* q, const void* k_cache, const void*
     switch (n_rep) {
 #define XB_DEC(R) \
   case R: launch_k(attn_decode_split_kernel<R>, grid, 128, 0, s, qq, kk, vv, ws, Hh, KV, SM, total, nchunks, scale_log2); break;
-      XB_DEC(1) XB_DEC(2) XB_DEC(3) XB_DEC(4) XB_DEC(5) XB_DEC(6) XB_DEC(7) XB_DEC(8)
+#define XB_DEC_SCALAR(R) \
+  case R: launch_k(attn_decode_scalar_kernel<R>, grid, 128, 0, s, qq, kk, vv, ws, Hh, KV, SM, total, nchunks, scale_log2); break;
+      XB_DEC_SCALAR(1) XB_DEC_SCALAR(2) XB_DEC(3) XB_DEC(4) XB_DEC(5) XB_DEC(6) XB_DEC(7) XB_DEC(8)
 #undef XB_DEC
+#undef XB_DEC_SCALAR
       default:
         set_err(err, errlen, "%s: %d query heads per KV head not supported (1..8)", what, n_rep);
         return XB_ERR_UNSUPPORTED;
