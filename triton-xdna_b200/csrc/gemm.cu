@@ -600,6 +600,36 @@ __device__ __forceinline__ float4 ld_bf16x4(const __nv_bfloat16* p) {
   return make_float4(__low2float(h[0]), __high2float(h[0]), __low2float(h[1]), __high2float(h[1]));
 }
 __device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// acc += p[s * slice] for s = 1 .. splits-1, in that order, four loads in
+// flight at a time (the order of the additions is the plain loop's).
+__device__ __forceinline__ void sum_splits4(float4& acc, const float* p, int splits, int64_t slice) {
+  int s2 = 1;
+  for (; s2 + 4 <= splits; s2 += 4) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(p + s2 * slice));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(p + (s2 + 1) * slice));
+    const float4 c = __ldcg(reinterpret_cast<const float4*>(p + (s2 + 2) * slice));
+    const float4 d = __ldcg(reinterpret_cast<const float4*>(p + (s2 + 3) * slice));
+    add4(acc, a);
+    add4(acc, b);
+    add4(acc, c);
+    add4(acc, d);
+  }
+  for (; s2 < splits; ++s2) add4(acc, __ldcg(reinterpret_cast<const float4*>(p + s2 * slice)));
+}
+__device__ __forceinline__ float sum_splits1(const float* p, int splits, int64_t slice) {
+  float acc = __ldcg(p);
+  int s2 = 1;
+  for (; s2 + 4 <= splits; s2 += 4) {
+    const float a = __ldcg(p + s2 * slice), b = __ldcg(p + (s2 + 1) * slice);
+    const float c = __ldcg(p + (s2 + 2) * slice), d = __ldcg(p + (s2 + 3) * slice);
+    acc += a;
+    acc += b;
+    acc += c;
+    acc += d;
+  }
+  for (; s2 < splits; ++s2) acc += __ldcg(p + s2 * slice);
+  return acc;
+}
 __device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float a, float b, float c, float d) {
   __nv_bfloat162 h[2] = {__floats2bfloat162_rn(a, b), __floats2bfloat162_rn(c, d)};
   *reinterpret_cast<uint2*>(p) = *reinterpret_cast<uint2*>(h);
@@ -618,7 +648,7 @@ __global__ void __launch_bounds__(256) splitk_reduce4_kernel(const float* __rest
   const int64_t slice = (int64_t)M * N;
   const float* p = part + (int64_t)m * N + n;
   float4 acc = __ldcg(reinterpret_cast<const float4*>(p));
-  for (int s2 = 1; s2 < splits; ++s2) add4(acc, __ldcg(reinterpret_cast<const float4*>(p + s2 * slice)));
+  sum_splits4(acc, p, splits, slice);
   if (bias) add4(acc, ld_bf16x4(bias + n));
   if constexpr (OUT_BF16) {
     float4 r = make_float4(rbf(acc.x), rbf(acc.y), rbf(acc.z), rbf(acc.w));
@@ -644,10 +674,8 @@ __global__ void __launch_bounds__(256) splitk_swiglu4_kernel(const float* __rest
   const float* pg = part + (int64_t)m * 2 * n_out + f;
   float4 g = __ldcg(reinterpret_cast<const float4*>(pg));
   float4 u = __ldcg(reinterpret_cast<const float4*>(pg + n_out));
-  for (int s2 = 1; s2 < splits; ++s2) {
-    add4(g, __ldcg(reinterpret_cast<const float4*>(pg + s2 * slice)));
-    add4(u, __ldcg(reinterpret_cast<const float4*>(pg + s2 * slice + n_out)));
-  }
+  sum_splits4(g, pg, splits, slice);
+  sum_splits4(u, pg + n_out, splits, slice);
   auto sw = [](float gg, float uu) { return __fmul_rn(silu_bf16path(rbf(gg)), rbf(uu)); };
   st_bf16x4(y + m * ldy + f, sw(g.x, u.x), sw(g.y, u.y), sw(g.z, u.z), sw(g.w, u.w));
 }
@@ -679,11 +707,7 @@ __global__ void __launch_bounds__(1024) reduce_rope_kv_kernel(const float* __res
     const int slot = j / half;
     const int i = j - slot * half;
     const int f0 = slot * D + i, f1 = f0 + half;
-    float a0 = __ldcg(pr + f0), a1 = __ldcg(pr + f1);
-    for (int s2 = 1; s2 < splits; ++s2) {
-      a0 += __ldcg(pr + s2 * slice + f0);
-      a1 += __ldcg(pr + s2 * slice + f1);
-    }
+    float a0 = sum_splits1(pr + f0, splits, slice), a1 = sum_splits1(pr + f1, splits, slice);
     if (bias) {
       a0 += __bfloat162float(bias[f0]);
       a1 += __bfloat162float(bias[f1]);
@@ -737,7 +761,7 @@ __global__ void __launch_bounds__(256) reduce_residual_norm_kernel(
     if (n >= N) continue;
     const float* p = part + (int64_t)m * N + n;
     float4 acc = __ldcg(reinterpret_cast<const float4*>(p));
-    for (int s2 = 1; s2 < splits; ++s2) add4(acc, __ldcg(reinterpret_cast<const float4*>(p + s2 * slice)));
+    sum_splits4(acc, p, splits, slice);
     if (bias) add4(acc, ld_bf16x4(bias + n));
     const float4 r = ld_bf16x4(residual + m * ldr + n);
     const float4 o = make_float4(rbf(r.x + rbf(acc.x)), rbf(r.y + rbf(acc.y)), rbf(r.z + rbf(acc.z)),

@@ -17,6 +17,7 @@
 //   attn out [B, S, H*D]                  input of o_proj
 //   cos/sin  [max_pos, D] fp32            tables of rope.py:20-35
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace xb {
 namespace llm {
@@ -924,6 +925,108 @@ extern "C" int xb_attention_bf16(const void* q, const void* k_cache, const void*
   return check_launch(what, err, errlen);
 }
 
+// Long rows (the vocabulary logits of a decode step): a cluster of 8 CTAs
+// splits each row into 8 column ranges (multiples of 4 columns, 16-byte loads
+// when the row is aligned), reduces each range in its CTA, and CTA 0 merges
+// the 8 candidates through distributed shared memory.  `better` is a total
+// order (value, then smaller index; NaN largest), so the merge order does not
+// change the result.
+constexpr int kArgmaxSplit = 8;
+__global__ void __launch_bounds__(256) argmax_cluster_kernel(const float* __restrict__ x, int64_t cols, int64_t ld,
+                                                             int64_t* __restrict__ idx) {
+  __shared__ float sv[8];
+  __shared__ int64_t si[8];
+  __shared__ float cand_v[kArgmaxSplit];
+  __shared__ int64_t cand_i[kArgmaxSplit];
+  const uint32_t rank = xb::tc::cluster_ctarank();
+  xb::pdl_wait();
+  xb::pdl_trigger();
+  const float* row = x + (int64_t)blockIdx.x * ld;
+  const int64_t chunk = ((cols + kArgmaxSplit - 1) / kArgmaxSplit + 3) / 4 * 4;
+  const int64_t c0 = min(cols, (int64_t)rank * chunk), c1 = min(cols, c0 + chunk);
+  float best = 0.0f;
+  int64_t bi = cols;
+  int64_t vec_end = c0;
+  if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    vec_end = c0 + (c1 - c0) / 4 * 4;
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    const int64_t a4 = c0 / 4, n4 = vec_end / 4;
+    for (int64_t base = a4 + threadIdx.x; base < n4; base += 4 * (int64_t)blockDim.x) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t i = base + (int64_t)u * blockDim.x;
+        v[u] = i < n4 ? __ldcs(r4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t i = base + (int64_t)u * blockDim.x;
+        if (i < n4) {
+          const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (better(best, bi, e[j], 4 * i + j, cols)) {
+              best = e[j];
+              bi = 4 * i + j;
+            }
+        }
+      }
+    }
+  }
+  for (int64_t c = vec_end + threadIdx.x; c < c1; c += blockDim.x) {
+    const float v = row[c];
+    if (better(best, bi, v, c, cols)) {
+      best = v;
+      bi = c;
+    }
+  }
+#pragma unroll
+  for (int o_ = 16; o_ > 0; o_ >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o_);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o_);
+    if (better(best, bi, ov, oi, cols)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    best = lane < 8 ? sv[lane] : 0.0f;
+    bi = lane < 8 ? si[lane] : cols;
+#pragma unroll
+    for (int o_ = 16; o_ > 0; o_ >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o_);
+      const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o_);
+      if (better(best, bi, ov, oi, cols)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {  // this range's candidate into CTA 0's shared memory
+      const uint32_t dv = xb::tc::mapa_u32(xb::tc::smem_u32(&cand_v[rank]), 0);
+      const uint32_t di = xb::tc::mapa_u32(xb::tc::smem_u32(&cand_i[rank]), 0);
+      asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dv), "f"(best) : "memory");
+      asm volatile("st.shared::cluster.s64 [%0], %1;" ::"r"(di), "l"(bi) : "memory");
+    }
+  }
+  xb::tc::cluster_sync();  // candidates visible in CTA 0; no CTA touches another's memory afterwards
+  if (rank == 0 && threadIdx.x == 0) {
+    float b = cand_v[0];
+    int64_t i0 = cand_i[0];
+    for (int r = 1; r < kArgmaxSplit; ++r)
+      if (better(b, i0, cand_v[r], cand_i[r], cols)) {
+        b = cand_v[r];
+        i0 = cand_i[r];
+      }
+    idx[blockIdx.x] = i0 < cols ? i0 : 0;
+  }
+}
+
 extern "C" int xb_argmax_f32(const float* x, int64_t rows, int64_t cols, int64_t ld, int64_t* idx, void* stream,
                              char* err, size_t errlen) {
   if (rows < 0 || cols <= 0 || ld < cols) {
@@ -934,6 +1037,28 @@ extern "C" int xb_argmax_f32(const float* x, int64_t rows, int64_t cols, int64_t
   if (!x || !idx) {
     set_err(err, errlen, "xb_argmax_f32: null pointer");
     return XB_ERR_INVALID;
+  }
+  if (cols >= 8192 && rows <= 0x7fffffffLL) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)rows, kArgmaxSplit, 1);
+    cfg.blockDim = dim3(256);
+    cfg.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = kArgmaxSplit;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = xb::pdl_enabled() ? 2 : 1;
+    xb::launch_counter().fetch_add(1, std::memory_order_relaxed);
+    cudaError_t e = cudaLaunchKernelEx(&cfg, argmax_cluster_kernel, x, cols, ld, idx);
+    if (e != cudaSuccess) {
+      set_err(err, errlen, "xb_argmax_f32: %s", cudaGetErrorString(e));
+      return XB_ERR_CUDA;
+    }
+    return check_launch("xb_argmax_f32", err, errlen);
   }
   launch_k<false>(argmax_kernel, (unsigned)rows, 1024, 0, (cudaStream_t)stream, x, cols, ld, idx);
   return check_launch("xb_argmax_f32", err, errlen);
