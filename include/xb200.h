@@ -104,6 +104,19 @@ XB_API int xb_silu(const void* x, void* y, int64_t n, int dtype, void* stream,
 XB_API int xb_swiglu(const void* gate, const void* up, void* out, int64_t n,
               int dtype, void* stream, char* err, size_t errlen);
 
+/* c = a * b elementwise (flat, n elements). */
+XB_API int xb_mul(const void* a, const void* b, void* c, int64_t n, int dtype,
+                  void* stream, char* err, size_t errlen);
+
+/* z[r, c] = x[r, c] * y[r, c] over rows x cols with row pitches ldx, ldy,
+ * ldz (elements): the tiled block-pointer product of
+ * examples/load_2d_block/test_load_2d_tensor_block.py:27-82 (a 4-D block
+ * pointer view of a 2-D tensor; every element of each program's block is
+ * loaded, multiplied and stored once). */
+XB_API int xb_mul_2d(const void* x, const void* y, void* z, int64_t rows,
+                     int64_t cols, int64_t ldx, int64_t ldy, int64_t ldz,
+                     int dtype, void* stream, char* err, size_t errlen);
+
 /* out = silu(gate) * up evaluated in fp32 with one rounding (the Qwen2.5
  * MLP form).  Replaces `swiglu_kernel_gpu` (examples/qwen2_5/kernels/
  * swiglu.py:29-50). */
@@ -163,6 +176,24 @@ XB_API int xb_avg_pool2d_2x2(const void* x, void* y, int64_t planes, int64_t h,
 XB_API int xb_matmul_i8(const void* A, const void* B, void* C, int64_t M,
                         int64_t N, int64_t K, int64_t lda, int64_t ldb,
                         int64_t ldc, void* stream, char* err, size_t errlen);
+
+/* f32 GEMM with bf16 emulation: C[M,N] (f32) = bf16(A) @ bf16(B) with f32
+ * accumulation, the operands rounded to bf16 (nearest even).  a_layout 0: A
+ * is [M, K] (row pitch lda); 1: A is stored transposed, [K, M] (row pitch
+ * lda).  B is [K, N].  M and N need not be multiples of any tile.  Needs
+ * the workspace xb_matmul_f32_bf16emu_workspace_size reports (256-byte
+ * aligned).  Replaces `padded_matmul_kernel` of
+ * examples/matmul_f32_m64_n32_k16_padded_atransposed/
+ * matmul_f32_m64_n32_k16_padded_atransposed.py:53-82 (A transposed, ragged
+ * M/N, bf16 emulation, golden L140-161). */
+XB_API int xb_matmul_f32_bf16emu_workspace_size(int64_t M, int64_t N,
+                                                int64_t K, size_t* bytes,
+                                                char* err, size_t errlen);
+XB_API int xb_matmul_f32_bf16emu(const float* A, const float* B, float* C,
+                                 int64_t M, int64_t N, int64_t K, int64_t lda,
+                                 int64_t ldb, int64_t ldc, int a_layout,
+                                 void* workspace, size_t workspace_bytes,
+                                 void* stream, char* err, size_t errlen);
 
 /* Y[M,N] (int32) = X[M,K] (int8) @ W[N,K]^T (int8), W in nn.Linear layout
  * (K-major): the int8 linear layer; exact.  The reference's int8 GEMM with

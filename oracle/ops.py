@@ -143,3 +143,19 @@ EXAMPLE_TOL = {
     "matmul_i8": (0, 0),  # matmul_i8_m128_n64_k64.py:89
     "matmul_bf16": (1e1, 1e-1),  # matmul_bf16_m64_n64_k64.py:85
 }
+
+
+def matmul_f32_bf16emu(a_km, b):
+    """bf16-emulated f32 GEMM with A stored transposed (K x M):
+    examples/matmul_f32_m64_n32_k16_padded_atransposed/
+    matmul_f32_m64_n32_k16_padded_atransposed.py:140-161 -- the f32 inputs
+    rounded to bf16 (ml_dtypes astype, nearest even), products and sums in
+    f32.  Returns C [M, N] f32."""
+    a = a_km.to(torch.bfloat16).float()
+    bb = b.to(torch.bfloat16).float()
+    return a.t() @ bb
+
+
+def mul(x, y):
+    """examples/load_2d_block/test_load_2d_tensor_block.py:118 -- expected = x * y."""
+    return x * y

@@ -139,6 +139,12 @@ FILLS = {
         O.weighted_rms_norm(_rows(b["X"], g[0] * b["BLOCK_M"], b["BLOCK_N"], b["N"]), b["W"], b["eps"])),
     "bare_matmul_i8": lambda b, g: b["C"].copy_(O.matmul_int(b["A"], b["B"])),
     "bare_matmul": lambda b, g: b["C"].copy_(O.matmul_bf16_f32acc(b["A"], b["B"]).to(b["C"].dtype)),
+    # A is stored K x M (stride_am == 1, row pitch stride_ak); only the
+    # M x N corner of the padded C is defined
+    "padded_matmul_kernel": lambda b, g: b["C"][:b["M"], :b["N"]].copy_(O.matmul_f32_bf16emu(
+        torch.as_strided(b["A"], (b["K"], b["M"]), (b["stride_ak"], 1)),
+        torch.as_strided(b["B"], (b["K"], b["N"]), (b["stride_bk"], 1)))),
+    "kernel": lambda b, g: b["z_ptr"].copy_(O.mul(b["x_ptr"], b["y_ptr"])),
 }
 
 # (case name, example file, kernel attribute, bench function, args, seed)
@@ -172,6 +178,12 @@ CASES = [
     ("matmul_bf16_256", "matmul_bf16_m64_n64_k64/matmul_bf16_m64_n64_k64.py", "bare_matmul", "bench_matmul",
      (256, 256, 256), 21),
     ("autotune_matmul_256", "autotune-matmul/matmul.py", "bare_matmul", "bench_matmul", (256, 256, 256), 0),
+    # examples that run their own test function without arguments (None):
+    # the f32 GEMM checks sampled elements itself and exits on a mismatch, so
+    # its pin is that check passing on the oracle's output
+    ("padded_matmul_f32_500x500x1024", "matmul_f32_m64_n32_k16_padded_atransposed/"
+     "matmul_f32_m64_n32_k16_padded_atransposed.py", "padded_matmul_kernel", "run_padded_matmul", None, 42),
+    ("load_2d_block_128x64", "load_2d_block/test_load_2d_tensor_block.py", "kernel", "test", None, 0),
 ]
 
 
@@ -200,7 +212,10 @@ def make(ref: str) -> dict:
                 torch.testing.assert_close = capture
                 try:
                     torch.manual_seed(seed)
-                    getattr(mod, fname)(*args, "test")
+                    if args is None:
+                        getattr(mod, fname)()
+                    else:
+                        getattr(mod, fname)(*args, "test")
                 finally:
                     torch.testing.assert_close = real_assert
                 assert len(rec.calls) == 1, f"{case}: expected one launch, got {len(rec.calls)}"
@@ -208,12 +223,22 @@ def make(ref: str) -> dict:
                 entry = {
                     "example": f"examples/{rel}",
                     "kernel": kname,
-                    "call": f"{fname}{args + ('test',)}",
+                    "call": f"{fname}{args + ('test',)}" if args is not None else f"{fname}()",
                     "seed": seed,
                     "grid": call["__grid__"],
-                    "pinned": bool(captured),
+                    "pinned": bool(captured) or args is None,
                 }
+                if args is None and not captured:
+                    entry["pinned_by"] = "the example's own sampled check passed on the oracle's output"
                 blob = {"args": {k: v for k, v in call.items() if k != "__grid__"}, "grid": call["__grid__"]}
+                if case.startswith("padded_matmul"):
+                    # 4 MB of f32 inputs regenerate exactly from the example's
+                    # numpy seed (L88-95): store their shapes only
+                    for k in ("A", "B"):
+                        t = blob["args"][k]
+                        blob["args"][k] = {"numpy_seed_42": list(t.shape), "dtype": "float32"}
+                    blob["regenerate"] = ("np.random.seed(42); A[:, :M] = rand(K, M) * 4; "
+                                          "B[:, :N] = rand(K, N) * 4 (zero padding beyond)")
                 if captured:
                     exp, kw = captured[0]
                     blob["expected"] = exp

@@ -31,7 +31,7 @@ def _launch(case):
     return entry, blob, args[output_name(blob)]
 
 
-@pytest.mark.parametrize("case", [c for c in CASES if INDEX[c]["pinned"]])
+@pytest.mark.parametrize("case", [c for c in CASES if INDEX[c]["pinned"] and "pinned_by" not in INDEX[c]])
 def test_example_assertion_holds(case):
     entry, blob, out = _launch(case)
     assert out.device.type == "cpu"  # copied back into the caller's host tensor
@@ -57,5 +57,21 @@ def test_tight_against_oracle(case):
     elif entry["kernel"] == "bare_matmul":
         # fp32 accumulation in a different order than the CPU's
         torch.testing.assert_close(out, ref, atol=1e-3, rtol=1e-4)
+    elif entry["kernel"] == "padded_matmul_kernel":
+        a = blob["args"]
+        torch.testing.assert_close(out[:a["M"], :a["N"]], ref, atol=1e-3, rtol=2e-5)
     else:
         torch.testing.assert_close(out, ref, atol=2e-5, rtol=2e-5)
+
+
+def test_f32_gemm_example_check_on_gpu_output():
+    """The f32 GEMM example's own sampled check, on the GPU result of its call."""
+    from test_oracle_golden import sampled_f32_gemm_check
+
+    case = "padded_matmul_f32_500x500x1024"
+    entry, blob, out = _launch(case)
+    args = materialize_args(blob)
+    a_km = torch.as_strided(args["A"], (args["K"], args["M"]), (args["stride_ak"], 1))
+    b = torch.as_strided(args["B"], (args["K"], args["N"]), (args["stride_bk"], 1))
+    assert out.device.type == "cpu"
+    assert sampled_f32_gemm_check(out, a_km, b, args["M"], args["N"]) == 0

@@ -49,13 +49,58 @@ def oracle_for(entry: dict, blob: dict) -> torch.Tensor:
         return O.matmul_int(a["A"], a["B"])
     if k == "bare_matmul":
         return O.matmul_bf16_f32acc(a["A"], a["B"])
+    if k == "padded_matmul_kernel":  # only the M x N corner of C is defined
+        return O.matmul_f32_bf16emu(torch.as_strided(a["A"], (a["K"], a["M"]), (a["stride_ak"], 1)),
+                                    torch.as_strided(a["B"], (a["K"], a["N"]), (a["stride_bk"], 1)))
+    if k == "kernel":  # examples/load_2d_block
+        return O.mul(a["x_ptr"], a["y_ptr"])
     if k == "_layer_norm_fwd_fused":
         return O.layernorm(_rows(a["input_ptr"], g[0] * a["BLOCK_SIZE"], a["n_cols"], a["input_stride_row"]),
                            eps=a["eps"])
     raise KeyError(k)
 
 
-PINNED = sorted(c for c, e in INDEX.items() if e["pinned"])
+PINNED = sorted(c for c, e in INDEX.items() if e["pinned"] and "pinned_by" not in e)
+
+
+def sampled_f32_gemm_check(c, a_km, b, M, N, seed_state=None):
+    """The f32 GEMM example's own check (matmul_f32_..._atransposed.py:140-186):
+    100 random elements plus the boundary tiles, each against an f32 numpy
+    dot product of the bf16-rounded inputs, np.isclose(rtol=0.1, atol=10).
+    Returns the number of mismatches."""
+    import numpy as np
+    from ml_dtypes import bfloat16
+
+    a16 = a_km.numpy().astype(bfloat16)
+    b16 = b.numpy().astype(bfloat16)
+    # the example's own sample positions: the global numpy stream after its
+    # seed-42 inputs (L88-95, L149-151)
+    rng = np.random.RandomState(42)
+    rng.rand(a_km.shape[0], M)
+    rng.rand(b.shape[0], N)
+    sm = list(rng.randint(0, M, 100))
+    sn = list(rng.randint(0, N, 100))
+    for bm in sorted({min(M - 1, m) for m in (M - 1, M - 64 + 1, 0) if m >= 0}):
+        for bn in sorted({min(N - 1, n) for n in (N - 1, N - 32 + 1, 0) if n >= 0}):
+            sm.append(bm)
+            sn.append(bn)
+    bad = 0
+    for m, n in zip(sm, sn):
+        exp = np.sum(a16[:, m].astype(np.float32) * b16[:, n].astype(np.float32), dtype=np.float32)
+        bad += not np.isclose(float(c[m, n]), exp, rtol=0.1, atol=10.0)
+    return bad
+
+
+def test_f32_gemm_oracle_passes_the_examples_check_and_float64():
+    case = "padded_matmul_f32_500x500x1024"
+    blob = load_golden(case)
+    a = materialize_args(blob)
+    got = oracle_for(INDEX[case], blob)
+    a_km = torch.as_strided(a["A"], (a["K"], a["M"]), (a["stride_ak"], 1))
+    b = torch.as_strided(a["B"], (a["K"], a["N"]), (a["stride_bk"], 1))
+    assert sampled_f32_gemm_check(got, a_km, b, a["M"], a["N"]) == 0
+    exact = a_km.to(torch.bfloat16).double().t() @ b.to(torch.bfloat16).double()
+    torch.testing.assert_close(got.double(), exact, atol=0.0, rtol=2e-5)
 
 
 @pytest.mark.parametrize("case", PINNED)
@@ -73,7 +118,7 @@ def test_oracle_matches_reference_expected(case):
 
 def test_every_example_operator_has_a_fixture():
     kernels = {e["kernel"] for e in INDEX.values()}
-    assert kernels >= {"vecadd", "axpy_kernel", "relu_kernel", "leaky_relu_kernel", "gelu_kernel", "sigmoid_kernel",
+    assert kernels >= {"padded_matmul_kernel", "kernel", "vecadd", "axpy_kernel", "relu_kernel", "leaky_relu_kernel", "gelu_kernel", "sigmoid_kernel",
                        "silu_kernel", "swiglu_kernel", "avg_pool_kernel", "softmax_kernel", "rms_norm_kernel",
                        "weighted_rms_norm_kernel", "bare_matmul_i8", "bare_matmul", "_layer_norm_fwd_fused"}
 

@@ -106,6 +106,10 @@ template <typename T> struct OpSwiglu {
 // silu(g) * u in fp32 with a single rounding: the Qwen2.5 MLP form
 // (examples/qwen2_5/kernels/swiglu.py:29-50, model.py:781-786), unlike the
 // swiglu example, which rounds silu(g) to the storage type first.
+template <typename T> struct OpMul {
+  __device__ __forceinline__ float operator()(float a, float b) const { return __fmul_rn(a, b); }
+};
+
 template <typename T> struct OpSiluMul {
   __device__ __forceinline__ float operator()(float g, float u) const { return __fmul_rn(OpSilu<T>{}(g), u); }
 };
@@ -297,6 +301,45 @@ extern "C" int xb_swiglu(const void* gate, const void* up, void* out, int64_t n,
   XB_DISPATCH_FLOAT(dtype, T, "xb_swiglu", err, errlen,
                     return launch_binary<T>(gate, up, out, n, OpSwiglu<T>{}, XB_S(stream), "xb_swiglu", err,
                                             errlen));
+}
+
+extern "C" int xb_mul(const void* a, const void* b, void* c, int64_t n, int dtype, void* stream, char* err,
+                      size_t errlen) {
+  XB_DISPATCH_FLOAT(dtype, T, "xb_mul", err, errlen,
+                    return launch_binary<T>(a, b, c, n, OpMul<T>{}, XB_S(stream), "xb_mul", err, errlen));
+}
+
+// z[r, c] = x[r, c] * y[r, c] over a strided 2-D region (rows of `cols`
+// elements, pitches in elements): the tiled block-pointer product of
+// examples/load_2d_block/test_load_2d_tensor_block.py:27-82.
+template <typename T>
+__global__ void __launch_bounds__(256) mul2d_kernel(const T* __restrict__ x, const T* __restrict__ y, T* __restrict__ z,
+                                                    int64_t rows, int64_t cols, int64_t ldx, int64_t ldy, int64_t ldz) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t c = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (c >= cols) return;
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y)
+    z[r * ldz + c] = Cvt<T>::from_f(__fmul_rn(Cvt<T>::to_f(x[r * ldx + c]), Cvt<T>::to_f(y[r * ldy + c])));
+}
+
+extern "C" int xb_mul_2d(const void* x, const void* y, void* z, int64_t rows, int64_t cols, int64_t ldx, int64_t ldy,
+                         int64_t ldz, int dtype, void* stream, char* err, size_t errlen) {
+  if (rows < 0 || cols < 0 || ldx < cols || ldy < cols || ldz < cols) {
+    set_err(err, errlen, "xb_mul_2d: bad shape or pitch");
+    return XB_ERR_INVALID;
+  }
+  if (rows == 0 || cols == 0) return XB_OK;
+  if (!x || !y || !z) {
+    set_err(err, errlen, "xb_mul_2d: null pointer");
+    return XB_ERR_INVALID;
+  }
+  const dim3 grid((unsigned)((cols + 255) / 256), (unsigned)(rows < 65535 ? rows : 65535));
+  XB_DISPATCH_FLOAT(dtype, T, "xb_mul_2d", err, errlen, {
+    launch_k<false>(mul2d_kernel<T>, grid, 256, 0, XB_S(stream), static_cast<const T*>(x), static_cast<const T*>(y),
+                    static_cast<T*>(z), rows, cols, ldx, ldy, ldz);
+    return check_launch("xb_mul_2d", err, errlen);
+  });
 }
 
 extern "C" int xb_silu_mul(const void* gate, const void* up, void* out, int64_t n, int dtype, void* stream, char* err,

@@ -35,6 +35,15 @@ def select_b200_backend(device: int | None = None) -> str:
 select_npu_backend = select_b200_backend
 
 
+def select_cpu_backend():
+    """The reference switches a process between its NPU driver and a CPU
+    driver (examples/multi_drivers/matmul.py:88-92, triton-cpu compiling the
+    same kernel for the host).  xb200 has no host execution path by design --
+    its operators run only as sm_100a kernels -- so selecting a CPU driver is
+    an error rather than a silent fallback."""
+    raise NotImplementedError("xb200 runs its operators on the GPU only; there is no CPU driver to select")
+
+
 def measure(repeats: int = 20, percentiles=(), timers=None):
     """Decorator timing a function (same output format as examples/benchmark.py:26-89).
 

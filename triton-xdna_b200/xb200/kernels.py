@@ -244,7 +244,37 @@ class _Autotuned(XbKernel):
         return super()._bind(args, kw)
 
 
+def _padded_matmul(A, B, C, M, N, K, stride_am, stride_ak, stride_bk, stride_bn, stride_cm, stride_cn, BLOCK_SIZE_M,
+                   BLOCK_SIZE_N, BLOCK_SIZE_K, grid):
+    # examples/matmul_f32_m64_n32_k16_padded_atransposed: stride_am == 1 means
+    # A is stored transposed (K x M, row pitch stride_ak); f32 operands run
+    # with bf16 emulation
+    if stride_am == 1 and M > 1:
+        a, trans = _mat_view(A, K, M, stride_ak, 1, "A"), True
+    else:
+        a, trans = _mat_view(A, M, K, stride_am, stride_ak, "A"), False
+    b = _mat_view(B, K, N, stride_bk, stride_bn, "B")
+    c = _mat_view(C, M, N, stride_cm, stride_cn, "C")
+    ops.matmul_f32_bf16emu(a, b, a_transposed=trans, out=c)
+
+
+def _load_2d(x_ptr, y_ptr, z_ptr, n_rows, n_cols, stride_0, stride_1, VEC_REG_SIZE_ROW, VEC_REG_SIZE_COL,
+             BLOCK_SIZE_ROW, BLOCK_SIZE_COL, grid):
+    # examples/load_2d_block/test_load_2d_tensor_block.py:27-82: program
+    # (p0, p1) loads the BLOCK_SIZE_ROW x BLOCK_SIZE_COL block at (p0 * BR,
+    # p1 * BC) of x and y through 4-D block pointers of VEC_REG sub-tiles and
+    # stores x * y at the same places of z: the grid covers these rows / cols
+    rows = min(n_rows, grid[0] * BLOCK_SIZE_ROW)
+    cols = min(n_cols, grid[1] * BLOCK_SIZE_COL)
+    if BLOCK_SIZE_ROW % VEC_REG_SIZE_ROW or BLOCK_SIZE_COL % VEC_REG_SIZE_COL:
+        raise ValueError("block sizes must be whole vector-register tiles")
+    views = [_mat_view(t, rows, cols, stride_0, stride_1, n) for t, n in ((x_ptr, "x"), (y_ptr, "y"), (z_ptr, "z"))]
+    ops.mul_2d(views[0], views[1], views[2])
+
+
 bare_matmul_i8 = XbKernel("bare_matmul_i8", "xb_matmul_i8", _matmul)
+padded_matmul_kernel = XbKernel("padded_matmul_kernel", "xb_matmul_f32_bf16emu", _padded_matmul)
+load_2d_block_kernel = XbKernel("kernel", "xb_mul_2d", _load_2d)
 bare_matmul = XbKernel("bare_matmul", "xb_matmul_bf16", _matmul)
 bare_matmul_autotuned = _Autotuned("bare_matmul", "xb_matmul_bf16", _matmul, {"BLOCK_SIZE_M": 256})
 
@@ -253,5 +283,6 @@ REGISTRY = {
     k.name: k
     for k in (vecadd, axpy_kernel, relu_kernel, leaky_relu_kernel, gelu_kernel, gelu_kernel_gpu, sigmoid_kernel,
               silu_kernel, swiglu_kernel, avg_pool_kernel, avg_pool2d_kernel, softmax_kernel, _layer_norm_fwd_fused,
-              rms_norm_kernel, weighted_rms_norm_kernel, bare_matmul_i8, bare_matmul)
+              rms_norm_kernel, weighted_rms_norm_kernel, bare_matmul_i8, bare_matmul, padded_matmul_kernel)
 }
+REGISTRY["load_2d_block_kernel"] = load_2d_block_kernel  # the example names its kernel plain `kernel`

@@ -138,6 +138,24 @@ def swiglu(gate, up, out=None):
     return _binary("xb_swiglu", gate, up, out)
 
 
+def mul(a, b, out=None):
+    """c = a * b elementwise."""
+    return _binary("xb_mul", a, b, out)
+
+
+def mul_2d(x, y, out):
+    """out[r, c] = x[r, c] * y[r, c] over 2-D views with unit column stride
+    (the block-pointer product of examples/load_2d_block)."""
+    _cuda(x, y, out)
+    dt = _float_dtype(x, y)
+    if out.dtype != x.dtype or x.shape != y.shape or out.shape != x.shape or x.dim() != 2:
+        raise ValueError("mul_2d takes three 2-D tensors of one shape and dtype")
+    rows, cols = x.shape
+    _lib.call("xb_mul_2d", x.data_ptr(), y.data_ptr(), out.data_ptr(), rows, cols, _mat(x, "x"), _mat(y, "y"),
+              _mat(out, "out"), dt, _stream())
+    return out
+
+
 def silu_mul(gate, up, out=None):
     """silu(gate) * up in fp32, one rounding (examples/qwen2_5/kernels/swiglu.py:29-50)."""
     return _binary("xb_silu_mul", gate, up, out)
@@ -302,6 +320,30 @@ def linear_i8(x, w, out=None):
     N = w.shape[0]
     _lib.call("xb_linear_i8", x.data_ptr(), w.data_ptr(), out.data_ptr(), M, N, K, _mat(x, "x"), _mat(w, "w"),
               _mat(out, "y"), _stream())
+    return out
+
+
+def matmul_f32_bf16emu(a, b, a_transposed=False, out=None):
+    """C (f32 [M, N]) = bf16(A) @ bf16(B) with f32 accumulation: f32 operands
+    rounded to bf16 as the reference's bf16 emulation does
+    (examples/matmul_f32_m64_n32_k16_padded_atransposed).  With
+    a_transposed, `a` is the [K, M] storage of A."""
+    _cuda(a, b, out)
+    if a.dtype != torch.float32 or b.dtype != torch.float32:
+        raise TypeError("matmul_f32_bf16emu takes f32 operands")
+    K, M = (a.shape[0], a.shape[1]) if a_transposed else (a.shape[1], a.shape[0])
+    if b.shape[0] != K:
+        raise ValueError(f"shape mismatch: K={K} vs B {tuple(b.shape)}")
+    N = b.shape[1]
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32, device=a.device)
+    elif out.dtype != torch.float32 or tuple(out.shape) != (M, N):
+        raise ValueError("out must be f32 [M, N]")
+    need = ctypes.c_size_t(0)
+    _lib.call("xb_matmul_f32_bf16emu_workspace_size", M, N, K, ctypes.byref(need))
+    ws = _workspace(a.device, need.value)
+    _lib.call("xb_matmul_f32_bf16emu", a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, _mat(a, "a"),
+              _mat(b, "b"), _mat(out, "out"), int(a_transposed), ws.data_ptr(), ws.numel() * 4, _stream())
     return out
 
 
