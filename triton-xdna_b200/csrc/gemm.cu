@@ -604,6 +604,13 @@ __device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2
 // flight at a time (the order of the additions is the plain loop's).
 __device__ __forceinline__ void sum_splits4(float4& acc, const float* p, int splits, int64_t slice) {
   int s2 = 1;
+  for (; s2 + 8 <= splits; s2 += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = __ldcg(reinterpret_cast<const float4*>(p + (s2 + u) * slice));
+#pragma unroll
+    for (int u = 0; u < 8; ++u) add4(acc, v[u]);
+  }
   for (; s2 + 4 <= splits; s2 += 4) {
     const float4 a = __ldcg(reinterpret_cast<const float4*>(p + s2 * slice));
     const float4 b = __ldcg(reinterpret_cast<const float4*>(p + (s2 + 1) * slice));
@@ -619,6 +626,13 @@ __device__ __forceinline__ void sum_splits4(float4& acc, const float* p, int spl
 __device__ __forceinline__ float sum_splits1(const float* p, int splits, int64_t slice) {
   float acc = __ldcg(p);
   int s2 = 1;
+  for (; s2 + 8 <= splits; s2 += 8) {
+    float v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = __ldcg(p + (s2 + u) * slice);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc += v[u];
+  }
   for (; s2 + 4 <= splits; s2 += 4) {
     const float a = __ldcg(p + s2 * slice), b = __ldcg(p + (s2 + 1) * slice);
     const float c = __ldcg(p + (s2 + 2) * slice), d = __ldcg(p + (s2 + 3) * slice);
@@ -703,7 +717,10 @@ __global__ void __launch_bounds__(1024) reduce_rope_kv_kernel(const float* __res
   const int slots = H + 2 * KVH;
   const int64_t slice = (int64_t)M * N;
   const float* pr = part + (int64_t)m * N;
-  for (int j = threadIdx.x; j < slots * half; j += blockDim.x) {
+  // blockIdx.y splits the token's (head slot, pair) items over gridDim.y CTAs
+  const int per = (slots * half + gridDim.y - 1) / gridDim.y;
+  const int j0 = blockIdx.y * per, j1 = min(slots * half, j0 + per);
+  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
     const int slot = j / half;
     const int i = j - slot * half;
     const int f0 = slot * D + i, f1 = f0 + half;
@@ -1534,8 +1551,10 @@ extern "C" int xb_linear_small_rope_kv_bf16(const void* X, const void* W, const 
   int rc = small_partials(X, W, batch, N, K, ldx, ldw, workspace, workspace_bytes, s, what, &splits, err, errlen);
   if (rc) return rc;
   const int64_t per_token = (n_head + 2 * n_kv_head) * (head_dim / 2);
-  const int threads = per_token >= 1024 ? 1024 : (int)((per_token + 31) / 32 * 32);
-  launch_k(reduce_rope_kv_kernel, (unsigned)batch, threads, 0, s, (const float*)workspace, splits, (int)batch, (int)N,
+  constexpr int kSplitY = 4;  // CTAs per token
+  const int64_t per_cta = (per_token + kSplitY - 1) / kSplitY;
+  const int threads = per_cta >= 1024 ? 1024 : (int)((per_cta + 31) / 32 * 32);
+  launch_k(reduce_rope_kv_kernel, dim3((unsigned)batch, kSplitY), threads, 0, s, (const float*)workspace, splits, (int)batch, (int)N,
            static_cast<const __nv_bfloat16*>(bias), cos_t, sin_t, static_cast<__nv_bfloat16*>(q_out),
            static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), (int)n_head, (int)n_kv_head,
            (int)head_dim, (int)max_seq, (int)pos_offset);

@@ -316,11 +316,14 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const bf16* __restric
 // the workspace and attn_decode_combine_kernel merges the chunks of a head.
 constexpr int kDecChunk = 128;
 
-template <int NREP>
+// CLUSTER: the nchunks (<= 8) CTAs of one (batch, KV head) form a cluster;
+// each sends its chunk partial into CTA 0's shared memory and CTA 0 merges
+// them (the combine kernel's arithmetic, chunks in order) straight into `out`.
+template <int NREP, bool CLUSTER = false>
 __global__ void __launch_bounds__(128) attn_decode_split_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
                                                                 const bf16* __restrict__ vc, float* __restrict__ ws,
                                                                 int H, int KVH, int smax, int total, int nchunks,
-                                                                float scale_log2) {
+                                                                float scale_log2, bf16* __restrict__ out) {
   static_assert(NREP >= 1 && NREP <= 16, "query heads per KV head fill one 16-row tile");
   __shared__ __align__(16) bf16 sK[kDecChunk][kPad];
   __shared__ __align__(16) bf16 sV[kDecChunk][kPad];
@@ -454,20 +457,67 @@ __global__ void __launch_bounds__(128) attn_decode_split_kernel(const bf16* __re
     }
   }
   __syncthreads();
-  float* part = ws + ((int64_t)(b * KVH + kvh) * nchunks + chunk) * NREP * (kHD + 2);
-  for (int i = tid; i < NREP * kHD; i += 128) {
-    const int r = i / kHD, d = i % kHD;
-    part[r * (kHD + 2) + d] = ((red[r * kHD + d] + red[(16 + r) * kHD + d]) + red[(32 + r) * kHD + d]) +
-                              red[(48 + r) * kHD + d];
-  }
-  if (tid < NREP) {
-    const float M = row_max(tid);
-    const float base = M == -INFINITY ? 0.0f : M;
-    float l = 0.0f;
+  float pv[(NREP * kHD + 127) / 128];
 #pragma unroll
-    for (int w = 0; w < 4; ++w) l += wl[w][tid] * ex2_approx(wm[w][tid] - base);
-    part[tid * (kHD + 2) + kHD] = M;
-    part[tid * (kHD + 2) + kHD + 1] = l;
+  for (int j = 0; j < (NREP * kHD + 127) / 128; ++j) {
+    const int i = tid + 128 * j, r = i / kHD, d = i % kHD;
+    pv[j] = i < NREP * kHD ? ((red[r * kHD + d] + red[(16 + r) * kHD + d]) + red[(32 + r) * kHD + d]) +
+                                 red[(48 + r) * kHD + d]
+                           : 0.0f;
+  }
+  float pm = 0.0f, pl = 0.0f;
+  if (tid < NREP) {
+    pm = row_max(tid);
+    const float base = pm == -INFINITY ? 0.0f : pm;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) pl += wl[w][tid] * ex2_approx(wm[w][tid] - base);
+  }
+  if constexpr (!CLUSTER) {
+    float* part = ws + ((int64_t)(b * KVH + kvh) * nchunks + chunk) * NREP * (kHD + 2);
+#pragma unroll
+    for (int j = 0; j < (NREP * kHD + 127) / 128; ++j) {
+      const int i = tid + 128 * j;
+      if (i < NREP * kHD) part[(i / kHD) * (kHD + 2) + i % kHD] = pv[j];
+    }
+    if (tid < NREP) {
+      part[tid * (kHD + 2) + kHD] = pm;
+      part[tid * (kHD + 2) + kHD + 1] = pl;
+    }
+  } else {
+    static_assert(8 * NREP * (kHD + 2) * sizeof(float) <= sizeof(sK), "8 chunk partials fit CTA 0's K tile");
+    float* slots = reinterpret_cast<float*>(&sK[0][0]);  // [nchunks][NREP][kHD + 2] in CTA 0
+    xb::tc::cluster_sync();  // every CTA is past its own K tile: CTA 0's may be overwritten
+    const uint32_t base = xb::tc::mapa_u32(xb::tc::smem_u32(slots), 0) +
+                          (uint32_t)(chunk * NREP * (kHD + 2)) * (uint32_t)sizeof(float);
+#pragma unroll
+    for (int j = 0; j < (NREP * kHD + 127) / 128; ++j) {
+      const int i = tid + 128 * j;
+      if (i < NREP * kHD) {
+        const uint32_t a = base + (uint32_t)((i / kHD) * (kHD + 2) + i % kHD) * 4u;
+        asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(pv[j]) : "memory");
+      }
+    }
+    if (tid < NREP) {
+      const uint32_t a = base + (uint32_t)(tid * (kHD + 2) + kHD) * 4u;
+      asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a), "f"(pm) : "memory");
+      asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(a + 4u), "f"(pl) : "memory");
+    }
+    xb::tc::cluster_sync();  // all partials landed in CTA 0; nobody touches a peer afterwards
+    if (chunk == 0) {
+      for (int i = tid; i < NREP * kHD; i += 128) {
+        const int r = i / kHD, d = i % kHD;
+        float mx = -INFINITY;
+        for (int c = 0; c < nchunks; ++c) mx = fmaxf(mx, slots[(c * NREP + r) * (kHD + 2) + kHD]);
+        float l = 0.0f, o = 0.0f;
+        for (int c = 0; c < nchunks; ++c) {
+          const float* sl = slots + (c * NREP + r) * (kHD + 2);
+          const float w = ex2_approx(sl[kHD] - mx);
+          l += sl[kHD + 1] * w;
+          o += sl[d] * w;
+        }
+        out[((int64_t)b * H + kvh * NREP + r) * kHD + d] = __float2bfloat16_rn(o / l);
+      }
+    }
   }
 }
 
@@ -901,9 +951,35 @@ extern "C" int xb_attention_bf16(const void* q, const void* k_cache, const void*
     const bf16* kk = static_cast<const bf16*>(k_cache);
     const bf16* vv = static_cast<const bf16*>(v_cache);
     const int Hh = (int)n_head, KV = (int)n_kv_head, SM = (int)max_seq;
+    bf16* ob = static_cast<bf16*>(out);
+    // contexts of up to 8 chunks merge inside a cluster (no combine launch)
+    const bool clustered = n_rep >= 3 && nchunks <= 8;
+    auto launch_cluster = [&](auto kernel) -> cudaError_t {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = grid;
+      cfg.blockDim = dim3(128);
+      cfg.stream = s;
+      cudaLaunchAttribute attr[2];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 1;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = (unsigned)nchunks;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = xb::pdl_enabled() ? 2 : 1;
+      xb::prefer_max_smem(reinterpret_cast<const void*>(kernel));
+      xb::launch_counter().fetch_add(1, std::memory_order_relaxed);
+      return cudaLaunchKernelEx(&cfg, kernel, qq, kk, vv, ws, Hh, KV, SM, total, nchunks, scale_log2, ob);
+    };
+    cudaError_t ce = cudaSuccess;
     switch (n_rep) {
-#define XB_DEC(R) \
-  case R: launch_k(attn_decode_split_kernel<R>, grid, 128, 0, s, qq, kk, vv, ws, Hh, KV, SM, total, nchunks, scale_log2); break;
+#define XB_DEC(R)                                                                                              \
+  case R:                                                                                                      \
+    if (clustered) ce = launch_cluster(attn_decode_split_kernel<R, true>);                                    \
+    else launch_k(attn_decode_split_kernel<R>, grid, 128, 0, s, qq, kk, vv, ws, Hh, KV, SM, total, nchunks,    \
+                  scale_log2, ob);                                                                             \
+    break;
 #define XB_DEC_SCALAR(R) \
   case R: launch_k(attn_decode_scalar_kernel<R>, grid, 128, 0, s, qq, kk, vv, ws, Hh, KV, SM, total, nchunks, scale_log2); break;
       XB_DEC_SCALAR(1) XB_DEC_SCALAR(2) XB_DEC(3) XB_DEC(4) XB_DEC(5) XB_DEC(6) XB_DEC(7) XB_DEC(8)
@@ -913,8 +989,13 @@ extern "C" int xb_attention_bf16(const void* q, const void* k_cache, const void*
         set_err(err, errlen, "%s: %d query heads per KV head not supported (1..8)", what, n_rep);
         return XB_ERR_UNSUPPORTED;
     }
-    launch_k(attn_decode_combine_kernel, dim3((unsigned)batch, (unsigned)n_head), kHD, 0, s, (const float*)ws,
-             static_cast<bf16*>(out), Hh, KV, nchunks);
+    if (ce != cudaSuccess) {
+      set_err(err, errlen, "%s: %s", what, cudaGetErrorString(ce));
+      return XB_ERR_CUDA;
+    }
+    if (!clustered)
+      launch_k(attn_decode_combine_kernel, dim3((unsigned)batch, (unsigned)n_head), kHD, 0, s, (const float*)ws,
+               static_cast<bf16*>(out), Hh, KV, nchunks);
   } else {
     dim3 grid((unsigned)((seq + kBQ - 1) / kBQ), (unsigned)(batch * n_head));
     launch_k(attn_prefill_kernel, grid, 128, 0, s, static_cast<const bf16*>(q), static_cast<const bf16*>(k_cache),
