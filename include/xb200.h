@@ -290,6 +290,29 @@ XB_API int xb_linear_small_swiglu_bf16(const void* X, const void* W, void* Y,
                                        void* workspace, size_t workspace_bytes,
                                        void* stream, char* err, size_t errlen);
 
+/* Y = residual + bf16(X @ W^T + bias) (bf16, any M): the linear with the
+ * residual add fused into the GEMM epilogue (o_proj / down_proj of a
+ * prefill; examples/qwen2_5/model.py:1045-1046, 1060-1061). */
+XB_API int xb_linear_residual_bf16(const void* X, const void* W, const void* bias,
+                                   const void* residual, void* Y, int64_t M,
+                                   int64_t N, int64_t K, int64_t ldx,
+                                   int64_t ldw, int64_t ldr, int64_t ldy,
+                                   void* stream, char* err, size_t errlen);
+
+/* Y [M, n_out] = bf16(silu(bf16(X Wg^T)) * bf16(X Wu^T)) with W [2 n_out, K]
+ * interleaving 128-row blocks of gate and up rows (block 2b = gate rows
+ * 128b..128b+127, block 2b+1 = the up rows of the same features); n_out %
+ * 128 == 0.  One GEMM whose epilogue applies the SwiGLU (M > 64), or the
+ * split-K small-M GEMM and its SwiGLU finisher (M <= 64; workspace as
+ * xb_linear_small_plan reports for N = 2 n_out).  The roundings are those of
+ * two linears and the silu*up kernel (examples/qwen2_5/model.py:1047-1059,
+ * kernels/swiglu.py:94-160). */
+XB_API int xb_linear_swiglu_bf16(const void* X, const void* W, void* Y,
+                                 int64_t M, int64_t n_out, int64_t K,
+                                 int64_t ldx, int64_t ldw, int64_t ldy,
+                                 void* workspace, size_t workspace_bytes,
+                                 void* stream, char* err, size_t errlen);
+
 /* Decode-step fusions of the small-M linear (one token per sequence, M =
  * batch <= 65535 rows), each a split-K GEMM into `workspace` (the bytes
  * xb_linear_small_plan reports for M, N, K) plus one finishing kernel.

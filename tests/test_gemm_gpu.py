@@ -296,3 +296,36 @@ def test_fused_decode_residual_norm_equals_unfused(kind, N, K, bias):
     yn_ref = ops.rms_norm(y_ref, nw, 1e-5) if kind == "rms" else ops.layernorm(y_ref, nw, nb, 1e-5)
     torch.testing.assert_close(yn.float().cpu(), yn_ref.float().cpu(), atol=2e-2, rtol=8e-3)
     _status_ok()
+
+
+@pytest.mark.parametrize("M", [100, 300, 1000])
+def test_linear_residual_epilogue_equals_linear_then_add(M):
+    g = torch.Generator().manual_seed(41)
+    x = (torch.randn(M, 896, generator=g) / 4).to(torch.bfloat16).cuda()
+    w = (torch.randn(896, 896, generator=g) / 16).to(torch.bfloat16).cuda()
+    b = (torch.randn(896, generator=g) / 4).to(torch.bfloat16).cuda()
+    r = torch.randn(M, 896, generator=g).to(torch.bfloat16).cuda()
+    fused = ops.linear(x, w, b, residual=r)
+    unfused = ops.vecadd(ops.linear(x, w, b), r)
+    assert torch.equal(fused.cpu(), unfused.cpu())
+    _status_ok()
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 100, 300, 700])
+def test_interleaved_swiglu_linear_equals_unfused(M):
+    """One GEMM with the SwiGLU in its epilogue (or the small-M split-K form)
+    = two linears + silu_mul, bit for bit."""
+    g = torch.Generator().manual_seed(42)
+    K, F = 896, 4864
+    x = (torch.randn(M, K, generator=g) / 4).to(torch.bfloat16).cuda()
+    wg = (torch.randn(F, K, generator=g) / 16).to(torch.bfloat16).cuda()
+    wu = (torch.randn(F, K, generator=g) / 16).to(torch.bfloat16).cuda()
+    w = ops.interleave_gate_up(wg, wu)
+    fused = ops.linear_swiglu(x, w, interleaved=True)
+    unfused = ops.silu_mul(ops.linear(x, wg), ops.linear(x, wu))
+    if M > ops.SMALL_M:  # both run the tiled GEMM: identical accumulation order
+        assert torch.equal(fused.cpu(), unfused.cpu())
+    else:  # split-K counts differ (N = 2 n_out vs n_out): fp32 sums in another order
+        torch.testing.assert_close(fused.float().cpu(), unfused.float().cpu(), atol=1e-3, rtol=2 ** -7)
+        assert (fused == unfused).float().mean().item() > 0.95
+    _status_ok()

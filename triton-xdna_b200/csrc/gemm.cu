@@ -47,7 +47,12 @@ __device__ int g_gemm_status = 0;
 constexpr uint64_t kWaitLimit = 2000000000ull;  // 2 s per wait: far above any legitimate wait
 
 enum Kind { kBf16 = 0, kInt8 = 1, kInt16Limbs = 2 };
-enum Out { kOutF32 = 0, kOutBf16 = 1, kOutI32 = 2 };
+// kOutSwiglu: W interleaves 128-row blocks of gate and up rows (block 2b =
+// gate rows 128b.., block 2b+1 = up rows 128b..), so a 256-column tile holds
+// the gate and up values of 128 output features; the epilogue writes
+// bf16(silu(bf16(g)) * bf16(u)) into C [M, N/2] -- the roundings of two bf16
+// linears followed by the silu*up kernel.
+enum Out { kOutF32 = 0, kOutBf16 = 1, kOutI32 = 2, kOutSwiglu = 3 };
 
 constexpr int tmem_cols_for(int cols) { return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512; }
 
@@ -102,6 +107,8 @@ constexpr int kEpiStageBytes = 4 * 2 * 32 * 128;
 struct Args {
   void* c;
   const void* bias;  // bf16 [N] or nullptr (linear layer only)
+  const void* residual;  // bf16 [M, N] added after the bf16 rounding (bf16 output), or nullptr
+  int64_t ldr;
   int64_t ldc;
   int64_t split_stride;  // elements between the split-K slices of c
   int m, n, k;
@@ -367,6 +374,38 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * C::ACCS * C::BN;
 #pragma unroll 1
       for (int cc = 0; cc < C::BN / 32; ++cc) {
+        if constexpr (OUT == kOutSwiglu) {
+          if (cc >= C::BN / 64) continue;
+          uint32_t gv[32], uv[32];
+          tmem_ld_32x32b_x32(tbase + cc * 32, gv);               // gate features
+          tmem_ld_32x32b_x32(tbase + C::BN / 2 + cc * 32, uv);   // up features
+          tmem_ld_wait();
+          const int f0 = tn * (C::BN / 2) + cc * 32;  // output feature of column 0
+          const int nout = args.n / 2;
+          if (row >= args.m || f0 >= nout) continue;
+          __nv_bfloat16* cp = static_cast<__nv_bfloat16*>(args.c) + (int64_t)row * args.ldc + f0;
+          float o[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float g = __bfloat162float(__float2bfloat16_rn(__uint_as_float(gv[j])));
+            const float u = __bfloat162float(__float2bfloat16_rn(__uint_as_float(uv[j])));
+            o[j] = __fmul_rn(silu_bf16path(g), u);
+          }
+          if (f0 + 32 <= nout && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              __nv_bfloat162 h[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(o[j + 2 * e], o[j + 2 * e + 1]);
+              *reinterpret_cast<int4*>(cp + j) = *reinterpret_cast<int4*>(h);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (f0 + j < nout) cp[j] = __float2bfloat16_rn(o[j]);
+          }
+          continue;
+        }
         uint32_t v[32];
         tmem_ld_32x32b_x32(tbase + cc * 32, v);
         if constexpr (KIND == kInt16Limbs) {
@@ -483,6 +522,28 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
               if (col0 + j < args.n) cp[(int64_t)(col0 + j) * args.ldc] = v[j];
           }
         } else {
+        if constexpr (OUT == kOutBf16 && !TRANS && !PEERS) {
+          if (args.residual && row < args.m) {  // y = residual + bf16(x W^T + b), as a linear then an add round
+            const __nv_bfloat16* rp = static_cast<const __nv_bfloat16*>(args.residual) + (int64_t)row * args.ldr + col0;
+            if (col0 + 32 <= args.n && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 8) {
+                const int4 raw = __ldg(reinterpret_cast<const int4*>(rp + j));
+                const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                  v[j + e] = __float_as_uint(__bfloat162float(re[e]) +
+                                             __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[j + e]))));
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < args.n)
+                  v[j] = __float_as_uint(__bfloat162float(rp[j]) +
+                                         __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[j]))));
+            }
+          }
+        }
 #pragma unroll 1
          for (int pe = 0; pe < (PEERS ? args.world : 1); ++pe) {
           void* cbase = PEERS ? args.peers[pe] : args.c;
@@ -521,7 +582,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       if constexpr (PAIR) mbar_arrive_cluster(mapa_u32(smem_u32(&tempty_bar[buf]), 0));
       else mbar_arrive(&tempty_bar[buf]);
     }
-    if constexpr (!PEERS && (TRANS || OUT != kOutBf16)) {
+    if constexpr (!PEERS && OUT != kOutSwiglu && (TRANS || OUT != kOutBf16)) {
       if (args.c_tma && lane == 0) bulk_wait_all();  // every TMA store of C has completed
       __syncwarp();
     }
@@ -677,6 +738,9 @@ __global__ void __launch_bounds__(256) splitk_reduce4_kernel(const float* __rest
   }
 }
 
+// IL: W interleaves 128-row blocks of gate and up rows (the kOutSwiglu layout);
+// otherwise gate rows [0, n_out) are stacked over up rows [n_out, 2 n_out).
+template <bool IL>
 __global__ void __launch_bounds__(256) splitk_swiglu4_kernel(const float* __restrict__ part, int splits, int M,
                                                              int n_out, __nv_bfloat16* __restrict__ y, int64_t ldy) {
   pdl_wait();
@@ -685,11 +749,14 @@ __global__ void __launch_bounds__(256) splitk_swiglu4_kernel(const float* __rest
   const int f = (blockIdx.x * 256 + threadIdx.x) * 4;
   if (f >= n_out) return;
   const int64_t slice = (int64_t)M * 2 * n_out;
-  const float* pg = part + (int64_t)m * 2 * n_out + f;
+  const int gcol = IL ? ((f >> 7) << 8) + (f & 127) : f;
+  const int ucol = gcol + (IL ? 128 : n_out);
+  const float* pg = part + (int64_t)m * 2 * n_out + gcol;
+  const float* pu = part + (int64_t)m * 2 * n_out + ucol;
   float4 g = __ldcg(reinterpret_cast<const float4*>(pg));
-  float4 u = __ldcg(reinterpret_cast<const float4*>(pg + n_out));
+  float4 u = __ldcg(reinterpret_cast<const float4*>(pu));
   sum_splits4(g, pg, splits, slice);
-  sum_splits4(u, pg + n_out, splits, slice);
+  sum_splits4(u, pu, splits, slice);
   auto sw = [](float gg, float uu) { return __fmul_rn(silu_bf16path(rbf(gg)), rbf(uu)); };
   st_bf16x4(y + m * ldy + f, sw(g.x, u.x), sw(g.y, u.y), sw(g.z, u.z), sw(g.w, u.w));
 }
@@ -990,7 +1057,7 @@ cudaError_t launch_pairs(void (*kernel)(KArgs...), unsigned grid, unsigned block
 template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false>
 int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
            cudaStream_t s, const char* what, char* err, size_t errlen, int splits = 1, int64_t split_stride = 0,
-           const PeerArgs* pa = nullptr) {
+           const PeerArgs* pa = nullptr, const void* residual = nullptr, int64_t ldr = 0) {
   using Cf = Cfg<KIND, B_KMAJOR, BN_, PAIR>;
   const CUtensorMapDataType dt = KIND == kBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   Maps maps;
@@ -1005,6 +1072,8 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   Args args;
   args.c = c;
   args.bias = bias;
+  args.residual = residual;
+  args.ldr = ldr;
   args.ldc = ldc;
   args.m = (int)M;
   args.n = (int)N;
@@ -1027,7 +1096,7 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   // 4-byte outputs of whole-tile GEMMs leave through the TMA-store epilogue
   // when C meets the TMA alignment rules.
   // Transposed (small-M) outputs too, through [tokens][features] staging tiles.
-  constexpr bool kStaged = !PEERS && (TRANS || OUT != kOutBf16);
+  constexpr bool kStaged = !PEERS && OUT != kOutSwiglu && (TRANS || OUT != kOutBf16);
   constexpr int kSmem = Cf::SMEM + (kStaged ? kEpiStageBytes : 0);
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
   args.c_tma = 0;
@@ -1484,7 +1553,7 @@ extern "C" int xb_linear_small_swiglu_bf16(const void* X, const void* W, void* Y
   const int64_t total = M * n_out;
   if (n_out % 4 == 0 && M <= 65535 && (reinterpret_cast<uintptr_t>(Y) & 7) == 0 && ldy % 4 == 0) {
     const dim3 g4((unsigned)((n_out / 4 + 255) / 256), (unsigned)M);
-    launch_k(splitk_swiglu4_kernel, g4, 256, 0, s, (const float*)part, splits, (int)M, (int)n_out,
+    launch_k(splitk_swiglu4_kernel<false>, g4, 256, 0, s, (const float*)part, splits, (int)M, (int)n_out,
              static_cast<__nv_bfloat16*>(Y), ldy);
     return check_launch(what, err, errlen);
   }
@@ -1598,6 +1667,74 @@ extern "C" int xb_linear_small_residual_norm_bf16(const void* X, const void* W, 
     launch_k(reduce_residual_norm_kernel<1>, (unsigned)M, 256, 0, s, (const float*)workspace, splits, (int)M, (int)N,
              static_cast<const bf*>(bias), static_cast<const bf*>(residual), ldr, static_cast<bf*>(Y), ldy,
              static_cast<bf*>(Yn), ldn, static_cast<const bf*>(norm_w), static_cast<const bf*>(norm_b), eps);
+  return check_launch(what, err, errlen);
+}
+
+extern "C" int xb_linear_residual_bf16(const void* X, const void* W, const void* bias, const void* residual, void* Y,
+                                       int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw, int64_t ldr,
+                                       int64_t ldy, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_linear_residual_bf16";
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc = check_common(X, W, Y, M, N, K, ldx, ldw, ldy, true, what, err, errlen);
+  if (rc) return rc < 0 ? rc : XB_OK;
+  if (!residual || ldr < N) {
+    set_err(err, errlen, "%s: residual missing or its pitch shorter than N", what);
+    return XB_ERR_INVALID;
+  }
+  if (K == 0 || !tma_ok(X, ldx, 2) || !tma_ok(W, ldw, 2)) {
+    set_err(err, errlen, "%s: K must be positive and X/W 16-byte aligned with 16-byte row pitches", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
+  if (use_pairs(M))
+    return launch<kBf16, true, kOutBf16, 0, false, false, true>(op, Y, bias, M, N, K, ldy, s, what, err, errlen, 1, 0,
+                                                                nullptr, residual, ldr);
+  return launch<kBf16, true, kOutBf16>(op, Y, bias, M, N, K, ldy, s, what, err, errlen, 1, 0, nullptr, residual,
+                                      ldr);
+}
+
+extern "C" int xb_linear_swiglu_bf16(const void* X, const void* W, void* Y, int64_t M, int64_t n_out, int64_t K,
+                                     int64_t ldx, int64_t ldw, int64_t ldy, void* workspace, size_t workspace_bytes,
+                                     void* stream, char* err, size_t errlen) {
+  const char* what = "xb_linear_swiglu_bf16";
+  cudaStream_t s = (cudaStream_t)stream;
+  if (n_out <= 0 || n_out % 128) {
+    set_err(err, errlen, "%s: n_out must be a positive multiple of 128 (interleaved 128-row blocks)", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  const int64_t N = 2 * n_out;
+  int rc = check_common(X, W, Y, M, N, K, ldx, ldw, ldy + n_out, true, what, err, errlen);
+  if (rc) return rc < 0 ? rc : XB_OK;
+  if (K == 0 || ldy < n_out || !tma_ok(X, ldx, 2) || !tma_ok(W, ldw, 2)) {
+    set_err(err, errlen, "%s: bad K / output pitch, or X/W not 16-byte aligned with 16-byte row pitches", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
+  if (M > 64) {
+    if (use_pairs(M))
+      return launch<kBf16, true, kOutSwiglu, 0, false, false, true>(op, Y, nullptr, M, N, K, ldy, s, what, err,
+                                                                    errlen);
+    return launch<kBf16, true, kOutSwiglu>(op, Y, nullptr, M, N, K, ldy, s, what, err, errlen);
+  }
+  // few tokens: swap-AB split-K partials, then the interleaved SwiGLU finisher
+  int splits = small_m_splits(N, K);
+  const size_t need = (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15) ||
+      (reinterpret_cast<uintptr_t>(Y) & 7) || ldy % 4) {
+    set_err(err, errlen, "%s: 16-byte aligned workspace of %zu bytes and an 8-byte aligned output needed", what,
+            need);
+    return XB_ERR_INVALID;
+  }
+  Operands sop{{W, nullptr}, {X, nullptr}, ldw, ldx};
+  rc = launch<kBf16, true, kOutF32, 64, true>(sop, workspace, nullptr, N, M, K, N, s, what, err, errlen, splits,
+                                             M * N);
+  if (rc) return rc;
+  const int kblocks = (int)((K + 63) / 64);
+  const int kps = (kblocks + splits - 1) / splits;
+  splits = (kblocks + kps - 1) / kps;
+  const dim3 g4((unsigned)((n_out / 4 + 255) / 256), (unsigned)M);
+  launch_k(splitk_swiglu4_kernel<true>, g4, 256, 0, s, (const float*)workspace, splits, (int)M, (int)n_out,
+           static_cast<__nv_bfloat16*>(Y), ldy);
   return check_launch(what, err, errlen);
 }
 

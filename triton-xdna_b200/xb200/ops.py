@@ -434,6 +434,11 @@ def linear(x, weight, bias=None, out=None, out_dtype=torch.bfloat16, residual=No
         if residual.dtype != torch.bfloat16 or residual.numel() != M * N:
             raise ValueError("residual must be bf16 with M x N elements")
         r2 = residual.reshape(M, N)
+    if residual is not None and M > SMALL_M and out_dtype == torch.bfloat16:
+        # the residual add happens in the GEMM epilogue
+        _lib.call("xb_linear_residual_bf16", x2.data_ptr(), weight.data_ptr(), bptr, r2.data_ptr(), y.data_ptr(), M,
+                  N, K, _mat(x2, "x"), _mat(weight, "weight"), _mat(r2, "residual"), _mat(y, "y"), _stream())
+        return y.reshape(*x.shape[:-1], N) if out is None else out
     if 0 < M <= SMALL_M:
         splits = ctypes.c_int(0)
         need = ctypes.c_size_t(0)
@@ -454,9 +459,22 @@ def linear(x, weight, bias=None, out=None, out_dtype=torch.bfloat16, residual=No
     return y.reshape(*x.shape[:-1], N) if out is None else out
 
 
-def linear_swiglu(x, w_gate_up):
-    """silu(x @ Wg^T) * (x @ Wu^T) for few tokens, W = [Wg; Wu] stacked
-    ([2*n_out, K]); the same roundings as two linears then silu_mul."""
+def interleave_gate_up(w_gate, w_up, block: int = 128) -> torch.Tensor:
+    """[2 n_out, K] weight interleaving 128-row blocks of gate and up rows, the
+    layout of the fused SwiGLU linear (xb_linear_swiglu_bf16)."""
+    n_out, K = w_gate.shape
+    if w_up.shape != w_gate.shape or n_out % block:
+        raise ValueError("gate and up weights must share a shape with n_out a multiple of 128")
+    g = w_gate.reshape(n_out // block, block, K)
+    u = w_up.reshape(n_out // block, block, K)
+    return torch.stack([g, u], 1).reshape(2 * n_out, K).contiguous()
+
+
+def linear_swiglu(x, w_gate_up, interleaved: bool = False):
+    """silu(x @ Wg^T) * (x @ Wu^T) with the roundings of two linears then
+    silu_mul.  interleaved=False: W = [Wg; Wu] stacked (few tokens only);
+    interleaved=True: W from interleave_gate_up (any number of tokens: one GEMM
+    whose epilogue applies the SwiGLU)."""
     _cuda(x, w_gate_up)
     K = x.shape[-1]
     x2 = x.reshape(-1, K)
@@ -464,6 +482,20 @@ def linear_swiglu(x, w_gate_up):
     N = w_gate_up.shape[0]
     if N % 2 or w_gate_up.shape[1] != K:
         raise ValueError("w_gate_up must be [2*n_out, K]")
+    if interleaved:
+        y = torch.empty((M, N // 2), dtype=torch.bfloat16, device=x.device)
+        ws = None
+        if M <= SMALL_M:
+            splits = ctypes.c_int(0)
+            need = ctypes.c_size_t(0)
+            _lib.call("xb_linear_small_plan", M, N, K, 1, ctypes.byref(splits), ctypes.byref(need))
+            ws = _workspace(x.device, need.value)
+        _lib.call("xb_linear_swiglu_bf16", x2.data_ptr(), w_gate_up.data_ptr(), y.data_ptr(), M, N // 2, K,
+                  _mat(x2, "x"), _mat(w_gate_up, "w"), N // 2, ws.data_ptr() if ws is not None else None,
+                  ws.numel() * 4 if ws is not None else 0, _stream())
+        return y.reshape(*x.shape[:-1], N // 2)
+    if M > SMALL_M:
+        raise ValueError("stacked gate/up weights take at most SMALL_M tokens; use interleave_gate_up")
     splits = ctypes.c_int(0)
     need = ctypes.c_size_t(0)
     _lib.call("xb_linear_small_plan", M, N, K, 1, ctypes.byref(splits), ctypes.byref(need))

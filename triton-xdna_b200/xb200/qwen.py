@@ -127,15 +127,12 @@ class Qwen2Model:
                 "qkv_b": torch.cat([t(f"{p}.self_attn.q_proj.bias"), t(f"{p}.self_attn.k_proj.bias"),
                                     t(f"{p}.self_attn.v_proj.bias")], 0).contiguous(),
                 "o_w": t(f"{p}.self_attn.o_proj.weight"),
-                # gate rows stacked over up rows: one GEMM in the decode step;
-                # prefill uses the two halves (views, no copy) as separate linears
-                "gate_up_w": torch.cat([t(f"{p}.mlp.gate_proj.weight"), t(f"{p}.mlp.up_proj.weight")],
-                                       0).contiguous(),
+                # gate and up rows interleaved in 128-row blocks: one GEMM (or one
+                # split-K GEMM at decode) whose epilogue applies silu(gate) * up
+                "gate_up_w": ops.interleave_gate_up(t(f"{p}.mlp.gate_proj.weight"),
+                                                    t(f"{p}.mlp.up_proj.weight")),
                 "down_w": t(f"{p}.mlp.down_proj.weight"),
             })
-            L = self.layers[-1]
-            L["gate_w"] = L["gate_up_w"][: c.intermediate]
-            L["up_w"] = L["gate_up_w"][c.intermediate:]
         self.norm_w = t("model.norm.weight")
         cos, sin = rope_tables(c.head_dim, rope_len or c.max_seq_len, c.rope_theta)
         self.cos = cos.to(dev).contiguous()
@@ -179,17 +176,14 @@ class Qwen2Model:
             ops.attention(q_buf, cache.k[i], cache.v[i], attn, B, S, H, KVH, HD, pos, self.scale)
             if decode:
                 x, xn = ops.linear_residual_norm(attn, L["o_w"], None, x, L["post_ln"], eps=c.rms_eps)
-                h = ops.linear_swiglu(xn, L["gate_up_w"])  # gate + up + silu*up, one GEMM
+                h = ops.linear_swiglu(xn, L["gate_up_w"], interleaved=True)  # gate + up + silu*up
                 nxt = self.layers[i + 1]["input_ln"] if i + 1 < len(self.layers) else self.norm_w
                 x, xn = ops.linear_residual_norm(h, L["down_w"], None, x, nxt, eps=c.rms_eps)
                 continue
-            x = ops.linear(attn, L["o_w"], residual=x)  # o_proj + residual add
+            x = ops.linear(attn, L["o_w"], residual=x)  # o_proj + residual add (in the epilogue)
             xn = ops.rms_norm(x, L["post_ln"], c.rms_eps)
-            if M <= ops.SMALL_M:
-                h = ops.linear_swiglu(xn, L["gate_up_w"])  # gate + up + silu*up, one GEMM
-            else:
-                h = ops.silu_mul(ops.linear(xn, L["gate_w"]), ops.linear(xn, L["up_w"]))
-            x = ops.linear(h, L["down_w"], residual=x)  # down_proj + residual add
+            h = ops.linear_swiglu(xn, L["gate_up_w"], interleaved=True)  # gate + up + silu*up, one GEMM
+            x = ops.linear(h, L["down_w"], residual=x)  # down_proj + residual add (in the epilogue)
         cache.length = pos + S
         if decode:
             x = xn  # the last down projection already applied the final norm
