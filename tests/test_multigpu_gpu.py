@@ -58,7 +58,10 @@ def _rank_main(rank, world, port):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
+        # ragged rows (300), ragged shard columns (176, 200: partial 32-column
+        # chunks take the per-thread store path), pairs (M >= 256) and single CTAs
         for dtype, (m, n, k) in ((torch.bfloat16, (512, 1024, 768)), (torch.int8, (300, 512, 256)),
+                                 (torch.int8, (300, 352, 128)), (torch.bfloat16, (200, 400, 64)),
                                  (torch.bfloat16, (4096, 4096, 4096))):
             g = torch.Generator(device="cuda").manual_seed(1)
             if dtype == torch.int8:

@@ -493,6 +493,54 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
             continue;
           }
         }
+        if constexpr (PEERS && !TRANS) {
+          if (args.c_tma) {
+            // Peer stores of whole lines: the warp's 32 x 32 chunk goes through
+            // a swizzled staging tile, then each store instruction writes
+            // complete 128-byte (int32) or 64-byte (bf16) row segments of 4 or
+            // 8 rows, to this rank's C and over NVLink to every peer's.
+            const int row0 = row - lane;
+            if (col0 >= args.n || row0 >= args.m) continue;  // warp-uniform
+            if (col0 + 32 <= args.n) {
+              uint8_t* stg = smem + C::STAGES * C::STAGE_BYTES + q * 2 * (32 * 128);
+              if constexpr (OUT == kOutBf16) {
+#pragma unroll
+                for (int p = 0; p < 4; ++p) {
+                  __nv_bfloat162 h[4];
+#pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    h[e] = __floats2bfloat162_rn(__uint_as_float(v[8 * p + 2 * e]),
+                                                 __uint_as_float(v[8 * p + 2 * e + 1]));
+                  *reinterpret_cast<int4*>(stg + lane * 64 + ((p ^ ((lane >> 1) & 3)) * 16)) =
+                      *reinterpret_cast<int4*>(h);
+                }
+              } else {
+#pragma unroll
+                for (int p = 0; p < 8; ++p)
+                  *reinterpret_cast<uint4*>(stg + lane * 128 + ((p ^ (lane & 7)) * 16)) =
+                      make_uint4(v[4 * p], v[4 * p + 1], v[4 * p + 2], v[4 * p + 3]);
+              }
+              __syncwarp();
+              constexpr int kRowsPer = OUT == kOutBf16 ? 8 : 4;      // rows per store instruction
+              constexpr int kPieces = OUT == kOutBf16 ? 4 : 8;       // 16-byte pieces per row
+              constexpr int kEsz = OUT == kOutBf16 ? 2 : 4;
+#pragma unroll 1
+              for (int pe = 0; pe < args.world; ++pe) {
+                uint8_t* cb = static_cast<uint8_t*>(args.peers[pe]) + (slice + (int64_t)row0 * args.ldc + col0) * kEsz;
+#pragma unroll
+                for (int k = 0; k < 32 / kRowsPer; ++k) {
+                  const int r = k * kRowsPer + lane / kPieces, p = lane % kPieces;
+                  const int phys = OUT == kOutBf16 ? (p ^ ((r >> 1) & 3)) : (p ^ (r & 7));
+                  const int4 val = *reinterpret_cast<const int4*>(stg + r * (kPieces * 16) + phys * 16);
+                  if (row0 + r < args.m)
+                    *reinterpret_cast<int4*>(cb + ((int64_t)r * args.ldc) * kEsz + p * 16) = val;
+                }
+              }
+              __syncwarp();  // staging free for the next chunk
+              continue;
+            }
+          }
+        }
         if (row >= args.m || col0 >= args.n) continue;
         if constexpr (OUT != kOutI32) {
           if (args.bias) {  // bias indexed by the output feature: the row of W
@@ -1097,7 +1145,7 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   // when C meets the TMA alignment rules.
   // Transposed (small-M) outputs too, through [tokens][features] staging tiles.
   constexpr bool kStaged = !PEERS && OUT != kOutSwiglu && (TRANS || OUT != kOutBf16);
-  constexpr int kSmem = Cf::SMEM + (kStaged ? kEpiStageBytes : 0);
+  constexpr int kSmem = Cf::SMEM + ((kStaged || PEERS) ? kEpiStageBytes : 0);
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
   args.c_tma = 0;
   if constexpr (kStaged && !TRANS) {
@@ -1117,6 +1165,12 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
       if (rc) return rc;
       args.c_tma = 1;
     }
+  }
+  if constexpr (PEERS && !TRANS) {  // whole-line peer stores need 16-byte aligned rows everywhere
+    const int esz = OUT == kOutBf16 ? 2 : 4;
+    bool ok = (ldc * esz) % 16 == 0;
+    for (int i = 0; i < args.world; ++i) ok = ok && (reinterpret_cast<uintptr_t>(args.peers[i]) & 15) == 0;
+    args.c_tma = ok ? 1 : 0;
   }
   auto kernel = gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS, PEERS, PAIR>;
   static bool attr_set = false;
@@ -1782,10 +1836,14 @@ extern "C" int xb_matmul_sharded(const void* A, const void* B_shard, void* const
   Operands op{{A, nullptr}, {B_shard, nullptr}, lda, ldb};
   void* local = pa.peers[rank];
   if (dtype == XB_DT_I8)
-    return launch<kInt8, false, kOutI32, 0, false, true>(op, local, nullptr, M, N_shard, K, ldc, s, what, err, errlen,
-                                                          1, 0, &pa);
-  return launch<kBf16, false, kOutBf16, 0, false, true>(op, local, nullptr, M, N_shard, K, ldc, s, what, err, errlen,
-                                                         1, 0, &pa);
+    return use_pairs(M) ? launch<kInt8, false, kOutI32, 0, false, true, true>(op, local, nullptr, M, N_shard, K, ldc,
+                                                                              s, what, err, errlen, 1, 0, &pa)
+                        : launch<kInt8, false, kOutI32, 0, false, true>(op, local, nullptr, M, N_shard, K, ldc, s,
+                                                                        what, err, errlen, 1, 0, &pa);
+  return use_pairs(M) ? launch<kBf16, false, kOutBf16, 0, false, true, true>(op, local, nullptr, M, N_shard, K, ldc, s,
+                                                                             what, err, errlen, 1, 0, &pa)
+                      : launch<kBf16, false, kOutBf16, 0, false, true>(op, local, nullptr, M, N_shard, K, ldc, s, what,
+                                                                       err, errlen, 1, 0, &pa);
 }
 
 extern "C" int xb_device_status(void* stream, int* status, char* err, size_t errlen) {
