@@ -493,15 +493,37 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
             continue;
           }
         }
-        if constexpr (PEERS && !TRANS) {
+        if constexpr ((PEERS || OUT == kOutBf16) && !TRANS) {
           if (args.c_tma) {
-            // Peer stores of whole lines: the warp's 32 x 32 chunk goes through
-            // a swizzled staging tile, then each store instruction writes
+            // Stores of whole lines: the warp's 32 x 32 chunk goes through a
+            // swizzled staging tile, then each store instruction writes
             // complete 128-byte (int32) or 64-byte (bf16) row segments of 4 or
-            // 8 rows, to this rank's C and over NVLink to every peer's.
+            // 8 rows -- to C, or with peers to this rank's C and over NVLink to
+            // every peer's.
             const int row0 = row - lane;
             if (col0 >= args.n || row0 >= args.m) continue;  // warp-uniform
             if (col0 + 32 <= args.n) {
+              if constexpr (OUT == kOutBf16 && !PEERS) {
+                if (args.bias) {
+                  const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(args.bias);
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    v[j] = __float_as_uint(__uint_as_float(v[j]) + __bfloat162float(bp[col0 + j]));
+                }
+                if (args.residual && row < args.m) {  // residual + bf16(x W^T + b)
+                  const __nv_bfloat16* rp =
+                      static_cast<const __nv_bfloat16*>(args.residual) + (int64_t)row * args.ldr + col0;
+#pragma unroll
+                  for (int j = 0; j < 32; j += 8) {
+                    const int4 raw = __ldg(reinterpret_cast<const int4*>(rp + j));
+                    const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e)
+                      v[j + e] = __float_as_uint(__bfloat162float(re[e]) +
+                                                 __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[j + e]))));
+                  }
+                }
+              }
               uint8_t* stg = smem + C::STAGES * C::STAGE_BYTES + q * 2 * (32 * 128);
               if constexpr (OUT == kOutBf16) {
 #pragma unroll
@@ -525,8 +547,9 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
               constexpr int kPieces = OUT == kOutBf16 ? 4 : 8;       // 16-byte pieces per row
               constexpr int kEsz = OUT == kOutBf16 ? 2 : 4;
 #pragma unroll 1
-              for (int pe = 0; pe < args.world; ++pe) {
-                uint8_t* cb = static_cast<uint8_t*>(args.peers[pe]) + (slice + (int64_t)row0 * args.ldc + col0) * kEsz;
+              for (int pe = 0; pe < (PEERS ? args.world : 1); ++pe) {
+                uint8_t* cb = static_cast<uint8_t*>(PEERS ? args.peers[pe] : args.c) +
+                              (slice + (int64_t)row0 * args.ldc + col0) * kEsz;
 #pragma unroll
                 for (int k = 0; k < 32 / kRowsPer; ++k) {
                   const int r = k * kRowsPer + lane / kPieces, p = lane % kPieces;
@@ -1102,6 +1125,8 @@ cudaError_t launch_pairs(void (*kernel)(KArgs...), unsigned grid, unsigned block
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+bool lines_enabled();
+
 template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false>
 int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
            cudaStream_t s, const char* what, char* err, size_t errlen, int splits = 1, int64_t split_stride = 0,
@@ -1145,7 +1170,8 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   // when C meets the TMA alignment rules.
   // Transposed (small-M) outputs too, through [tokens][features] staging tiles.
   constexpr bool kStaged = !PEERS && OUT != kOutSwiglu && (TRANS || OUT != kOutBf16);
-  constexpr int kSmem = Cf::SMEM + ((kStaged || PEERS) ? kEpiStageBytes : 0);
+  constexpr bool kLines = !TRANS && (PEERS || OUT == kOutBf16);  // whole-line staged stores
+  constexpr int kSmem = Cf::SMEM + ((kStaged || kLines) ? kEpiStageBytes : 0);
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
   args.c_tma = 0;
   if constexpr (kStaged && !TRANS) {
@@ -1166,10 +1192,14 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
       args.c_tma = 1;
     }
   }
-  if constexpr (PEERS && !TRANS) {  // whole-line peer stores need 16-byte aligned rows everywhere
+  if constexpr (kLines) {  // whole-line stores need 16-byte aligned rows everywhere
     const int esz = OUT == kOutBf16 ? 2 : 4;
-    bool ok = (ldc * esz) % 16 == 0;
-    for (int i = 0; i < args.world; ++i) ok = ok && (reinterpret_cast<uintptr_t>(args.peers[i]) & 15) == 0;
+    bool ok = (ldc * esz) % 16 == 0 && args.splits == 1 && (PEERS || lines_enabled());
+    if (PEERS) {
+      for (int i = 0; i < args.world; ++i) ok = ok && (reinterpret_cast<uintptr_t>(args.peers[i]) & 15) == 0;
+    } else {
+      ok = ok && (reinterpret_cast<uintptr_t>(c) & 15) == 0;
+    }
     args.c_tma = ok ? 1 : 0;
   }
   auto kernel = gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS, PEERS, PAIR>;
@@ -1217,6 +1247,16 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
 
 // CTA pairs for products with at least two 128-row blocks; XB_GEMM_PAIRS=0
 // in the environment selects the single-CTA kernel everywhere.
+// XB_GEMM_LINES=0 in the environment keeps per-thread row stores (A/B timing).
+bool lines_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("XB_GEMM_LINES");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 bool use_pairs(int64_t M) {
   static int on = -1;
   if (on < 0) {
