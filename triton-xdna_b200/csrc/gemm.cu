@@ -78,7 +78,7 @@ struct Cfg {
   static constexpr int STAGE_BYTES = PLANES * (A_BYTES + B_BYTES);
   // BN <= 64 (small-M, swap-AB): 6 slots leave room on the SM for the small
   // kernel before it, so the weight prefetch can overlap that kernel
-  static constexpr int STAGES = PAIR ? 6 : KIND == kInt16Limbs ? 3 : (BN <= 64 ? 6 : 4);
+  static constexpr int STAGES = PAIR ? (KIND == kInt16Limbs ? 4 : 6) : KIND == kInt16Limbs ? 3 : (BN <= 64 ? 6 : 4);
   static constexpr int UMMA_K = 32 / ESZ;  // 32 bytes of K per MMA
   static constexpr int KSTEPS = BK / UMMA_K;
   static constexpr int ACCS = KIND == kInt16Limbs ? 3 : 1;
@@ -91,7 +91,6 @@ struct Cfg {
   static_assert(ACCS * ACC_BUFS * BN <= TMEM_COLS, "TMEM budget");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
   static_assert(B_KMAJOR || BN_CTA % B_BOX_N == 0, "MN-major B needs whole boxes");
-  static_assert(!PAIR || KIND != kInt16Limbs, "pairs run the single-accumulator kinds");
 };
 
 struct alignas(64) Maps {
@@ -330,8 +329,13 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
             constexpr uint32_t bmn = B_KMAJOR ? 0 : 1;
             if constexpr (PAIR && KIND == kBf16) {
               mma2_f16(d0, ad[0], bd[0], umma_idesc(1, 1, 1, 0, bmn, C::TILE_M, C::BN), acc);
-            } else if constexpr (PAIR) {
+            } else if constexpr (PAIR && KIND == kInt8) {
               mma2_i8(d0, ad[0], bd[0], umma_idesc(2, 1, 1, 0, bmn, C::TILE_M, C::BN), acc);
+            } else if constexpr (PAIR) {  // int16 limbs, as below, on the 256-row pair tile
+              mma2_i8(d0, ad[0], bd[0], umma_idesc(2, 1, 1, 0, bmn, C::TILE_M, C::BN), acc);
+              mma2_i8(d0 + C::BN, ad[0], bd[1], umma_idesc(2, 1, 0, 0, bmn, C::TILE_M, C::BN), acc);
+              mma2_i8(d0 + C::BN, ad[1], bd[0], umma_idesc(2, 0, 1, 0, bmn, C::TILE_M, C::BN), 1u);
+              mma2_i8(d0 + 2 * C::BN, ad[1], bd[1], umma_idesc(2, 0, 0, 0, bmn, C::TILE_M, C::BN), acc);
             } else if constexpr (KIND == kBf16) {
               mma_f16(d0, ad[0], bd[0], umma_idesc(1, 1, 1, 0, bmn, C::BM, C::BN), acc);
             } else if constexpr (KIND == kInt8) {
@@ -1026,6 +1030,34 @@ __global__ void split_i16_kernel(const int16_t* __restrict__ src, int64_t rows, 
   }
 }
 
+// int16 [K, N] (pitch lds) -> (high s8, low u8) limb planes stored transposed,
+// [N, ldp] (K-major, the B operand layout of the limb GEMM); K <= k < ldp is
+// zero.  32 x 32 tiles through shared memory, 32 x 8 threads.
+__global__ void __launch_bounds__(256) split_i16_t_kernel(const int16_t* __restrict__ src, int64_t K, int64_t N,
+                                                          int64_t lds, int8_t* __restrict__ hi,
+                                                          uint8_t* __restrict__ lo, int64_t ldp) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ int16_t tile[32][33];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int64_t n0 = (int64_t)blockIdx.x * 32, k0 = (int64_t)blockIdx.y * 32;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t k = k0 + ty + 8 * i, n = n0 + tx;
+    tile[ty + 8 * i][tx] = (k < K && n < N) ? src[k * lds + n] : (int16_t)0;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t n = n0 + ty + 8 * i, k = k0 + tx;
+    if (n < N && k < ldp) {
+      const int16_t v = tile[tx][ty + 8 * i];
+      hi[n * ldp + k] = (int8_t)(v >> 8);
+      lo[n * ldp + k] = (uint8_t)(v & 0xFF);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------- host side
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -1300,10 +1332,11 @@ struct LimbLayout {
 };
 LimbLayout limb_layout(int64_t M, int64_t N, int64_t K) {
   LimbLayout L;
+  // both limb operands K-major: A planes [M, lda_p], B planes transposed [N, ldb_p]
   L.lda_p = (int64_t)round_up((size_t)(K > 0 ? K : 1), 16);
-  L.ldb_p = (int64_t)round_up((size_t)(N > 0 ? N : 1), 16);
+  L.ldb_p = L.lda_p;
   L.a_plane = round_up((size_t)(M > 0 ? M : 1) * L.lda_p, 256);
-  L.b_plane = round_up((size_t)(K > 0 ? K : 1) * L.ldb_p, 256);
+  L.b_plane = round_up((size_t)(N > 0 ? N : 1) * L.ldb_p, 256);
   L.total = 2 * L.a_plane + 2 * L.b_plane;
   return L;
 }
@@ -1342,11 +1375,20 @@ int run_i16(const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t
   int8_t* bhi = reinterpret_cast<int8_t*>(w + 2 * L.a_plane);
   uint8_t* blo = w + 2 * L.a_plane + L.b_plane;
   split_launch(static_cast<const int16_t*>(A), M, K, lda, ahi, alo, L.lda_p, s);
-  split_launch(static_cast<const int16_t*>(B), K, N, ldb, bhi, blo, L.ldb_p, s);
+  {
+    const dim3 grid((unsigned)((N + 31) / 32), (unsigned)((L.ldb_p + 31) / 32));
+    if (grid.y > 65535) {
+      set_err(err, errlen, "%s: K too large for the limb transpose grid", what);
+      return XB_ERR_UNSUPPORTED;
+    }
+    launch_k(split_i16_t_kernel, grid, 256, 0, s, static_cast<const int16_t*>(B), K, N, ldb, bhi, blo, L.ldb_p);
+  }
   rc = check_launch(what, err, errlen);
   if (rc) return rc;
   Operands op{{ahi, alo}, {bhi, blo}, L.lda_p, L.ldb_p};
-  return launch<kInt16Limbs, false, kOutI32>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
+  if (use_pairs(M)) return launch<kInt16Limbs, true, kOutI32, 0, false, false, true>(op, C, nullptr, M, N, K, ldc, s,
+                                                                                       what, err, errlen);
+  return launch<kInt16Limbs, true, kOutI32>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
 }
 
 }  // namespace gemm
