@@ -93,3 +93,25 @@ def test_embedding_and_argmax():
     x[4, 500] = float("nan")  # NaN counts as the maximum
     got = ops.argmax(x.cuda()).cpu()
     assert torch.equal(got, torch.argmax(x, -1))
+
+
+@pytest.mark.parametrize("rope", [True, False])
+def test_rope_kv_many_tokens_matches_oracle(rope):
+    """The grid-stride RoPE / KV-write kernel (prefill sizes) is bit-exact too."""
+    B, S, H, KVH, pos, smax = 4, 100, 14, 2, 3, 128
+    cos, sin = OQ.rope_tables(64, 128, 1e6)
+    qkv = _rand((B * S, (H + 2 * KVH) * 64), 11)
+    q = torch.empty((B, H, S, 64), dtype=torch.bfloat16, device="cuda")
+    kc = torch.zeros((B, KVH, smax, 64), dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros((B, KVH, smax, 64), dtype=torch.bfloat16, device="cuda")
+    ops.rope_kv(qkv.cuda(), cos.cuda() if rope else None, sin.cuda() if rope else None, q, kc, vc, B, S, H, KVH, 64,
+                pos)
+    qq, kk, vv = qkv.view(B, S, -1).split([H * 64, KVH * 64, KVH * 64], -1)
+    heads_q = qq.reshape(B, S, H, 64).transpose(1, 2)
+    heads_k = kk.reshape(B, S, KVH, 64).transpose(1, 2)
+    rq = OQ.apply_rope(heads_q, cos, sin, pos) if rope else heads_q
+    rk = OQ.apply_rope(heads_k, cos, sin, pos) if rope else heads_k
+    assert torch.equal(q.cpu(), rq)
+    assert torch.equal(kc.cpu()[:, :, pos:pos + S], rk)
+    assert torch.equal(vc.cpu()[:, :, pos:pos + S], vv.reshape(B, S, KVH, 64).transpose(1, 2))
+    assert torch.all(kc.cpu()[:, :, :pos] == 0) and torch.all(kc.cpu()[:, :, pos + S:] == 0)

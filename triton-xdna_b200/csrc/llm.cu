@@ -129,6 +129,60 @@ __global__ void __launch_bounds__(1024) rope_kv_kernel(const bf16* __restrict__ 
   }
 }
 
+// The same RoPE + KV write for many tokens: a grid-stride loop over (token,
+// head slot, pair of adjacent dims) items, 4-byte bf16x2 and 8-byte float2
+// accesses, several tokens per CTA (one CTA per token left the block
+// scheduler as the bottleneck of a 32768-token prefill).  Identical
+// arithmetic: products and sums rounded separately in fp32.
+__global__ void __launch_bounds__(256) rope_kv_flat_kernel(const bf16* __restrict__ qkv, const float* __restrict__ cos_t,
+                                                           const float* __restrict__ sin_t, bf16* __restrict__ q_out,
+                                                           bf16* __restrict__ k_cache, bf16* __restrict__ v_cache,
+                                                           int64_t tokens, int S, int H, int KVH, int D, int smax,
+                                                           int pos_offset) {
+  pdl_wait();
+  pdl_trigger();
+  const int half = D / 2, hp = half / 2;  // pairs of dims per head slot
+  const int slots = H + 2 * KVH;
+  const int64_t per_tok = (int64_t)slots * hp;
+  const int64_t total = tokens * per_tok;
+  for (int64_t it = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; it < total; it += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = it / per_tok;
+    const int rem = (int)(it - m * per_tok);
+    const int slot = rem / hp;
+    const int i = (rem - slot * hp) * 2;
+    const int s = (int)(m % S);
+    const int b = (int)(m / S);
+    const int pos = pos_offset + s;
+    const bf16* x = qkv + m * (int64_t)(slots * D) + slot * D;
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(x + i);
+    const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(x + i + half);
+    if (slot >= H + KVH) {
+      bf16* dst = v_cache + (((int64_t)b * KVH + (slot - H - KVH)) * smax + pos) * D;
+      *reinterpret_cast<__nv_bfloat162*>(dst + i) = a;
+      *reinterpret_cast<__nv_bfloat162*>(dst + i + half) = c;
+      continue;
+    }
+    bf16* dst = slot < H ? q_out + (((int64_t)b * H + slot) * S + s) * D
+                         : k_cache + (((int64_t)b * KVH + (slot - H)) * smax + pos) * D;
+    if (!cos_t) {
+      *reinterpret_cast<__nv_bfloat162*>(dst + i) = a;
+      *reinterpret_cast<__nv_bfloat162*>(dst + i + half) = c;
+      continue;
+    }
+    const float2 c0 = *reinterpret_cast<const float2*>(cos_t + (int64_t)pos * D + i);
+    const float2 c1 = *reinterpret_cast<const float2*>(cos_t + (int64_t)pos * D + i + half);
+    const float2 s0 = *reinterpret_cast<const float2*>(sin_t + (int64_t)pos * D + i);
+    const float2 s1 = *reinterpret_cast<const float2*>(sin_t + (int64_t)pos * D + i + half);
+    const float x0a = __low2float(a), x0b = __high2float(a), x1a = __low2float(c), x1b = __high2float(c);
+    const float y0a = __fadd_rn(__fmul_rn(x0a, c0.x), __fmul_rn(-x1a, s0.x));
+    const float y0b = __fadd_rn(__fmul_rn(x0b, c0.y), __fmul_rn(-x1b, s0.y));
+    const float y1a = __fadd_rn(__fmul_rn(x1a, c1.x), __fmul_rn(x0a, s1.x));
+    const float y1b = __fadd_rn(__fmul_rn(x1b, c1.y), __fmul_rn(x0b, s1.y));
+    *reinterpret_cast<__nv_bfloat162*>(dst + i) = __floats2bfloat162_rn(y0a, y0b);
+    *reinterpret_cast<__nv_bfloat162*>(dst + i + half) = __floats2bfloat162_rn(y1a, y1b);
+  }
+}
+
 // ----------------------------------------------------------------------------- prefill attention
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -886,6 +940,21 @@ extern "C" int xb_rope_kv_bf16(const void* qkv, const float* cos_t, const float*
   if (batch * seq > 0x7fffffffLL) {
     set_err(err, errlen, "xb_rope_kv_bf16: too many tokens");
     return XB_ERR_UNSUPPORTED;
+  }
+  const bool vec = head_dim % 4 == 0 && (reinterpret_cast<uintptr_t>(qkv) & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(q_out) & 3) == 0 && (reinterpret_cast<uintptr_t>(k_cache) & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(v_cache) & 3) == 0 &&
+                   (!cos_t || ((reinterpret_cast<uintptr_t>(cos_t) & 7) == 0 && (reinterpret_cast<uintptr_t>(sin_t) & 7) == 0));
+  if (vec && batch * seq >= 256) {
+    const int64_t items = batch * seq * (n_head + 2 * n_kv_head) * (head_dim / 4);
+    int64_t grid = (items + 255) / 256;
+    int sms = 148;
+    xb::sm_count(&sms);
+    if (grid > (int64_t)sms * 16) grid = (int64_t)sms * 16;
+    launch_k<false>(rope_kv_flat_kernel, (unsigned)grid, 256, 0, (cudaStream_t)stream, static_cast<const bf16*>(qkv),
+                    cos_t, sin_t, static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache),
+                    batch * seq, (int)seq, (int)n_head, (int)n_kv_head, (int)head_dim, (int)max_seq, (int)pos_offset);
+    return check_launch("xb_rope_kv_bf16", err, errlen);
   }
   launch_k<false>(rope_kv_kernel, (unsigned)(batch * seq), threads, 0, (cudaStream_t)stream, static_cast<const bf16*>(qkv),
            cos_t, sin_t, static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache), static_cast<bf16*>(v_cache), (int)seq,
