@@ -299,6 +299,16 @@ XB_API int xb_linear_residual_bf16(const void* X, const void* W, const void* bia
                                    int64_t ldw, int64_t ldr, int64_t ldy,
                                    void* stream, char* err, size_t errlen);
 
+/* Y = bf16(gelu_tanh(bf16(X @ W^T + bias))) (bf16, any M): the linear with
+ * the tanh GELU fused (GPT-2 c_fc + gelu, examples/gpt2/model.py:1046-1051),
+ * rounded as a linear followed by the GELU kernel.  M <= 64 uses the split-K
+ * form (workspace as xb_linear_small_plan reports; N % 4 == 0). */
+XB_API int xb_linear_gelu_bf16(const void* X, const void* W, const void* bias,
+                               void* Y, int64_t M, int64_t N, int64_t K,
+                               int64_t ldx, int64_t ldw, int64_t ldy,
+                               void* workspace, size_t workspace_bytes,
+                               void* stream, char* err, size_t errlen);
+
 /* Y [M, n_out] = bf16(silu(bf16(X Wg^T)) * bf16(X Wu^T)) with W [2 n_out, K]
  * interleaving 128-row blocks of gate and up rows (block 2b = gate rows
  * 128b..128b+127, block 2b+1 = the up rows of the same features); n_out %

@@ -329,3 +329,15 @@ def test_interleaved_swiglu_linear_equals_unfused(M):
         torch.testing.assert_close(fused.float().cpu(), unfused.float().cpu(), atol=1e-3, rtol=2 ** -7)
         assert (fused == unfused).float().mean().item() > 0.95
     _status_ok()
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 100, 300])
+def test_linear_gelu_epilogue_equals_linear_then_gelu(M):
+    g = torch.Generator().manual_seed(43)
+    x = (torch.randn(M, 768, generator=g) / 4).to(torch.bfloat16).cuda()
+    w = (torch.randn(3072, 768, generator=g) / 8).to(torch.bfloat16).cuda()
+    b = (torch.randn(3072, generator=g) / 4).to(torch.bfloat16).cuda()
+    fused = ops.linear(x, w, b, act="gelu_tanh")
+    unfused = ops.gelu_tanh(ops.linear(x, w, b))
+    assert torch.equal(fused.cpu(), unfused.cpu())
+    _status_ok()

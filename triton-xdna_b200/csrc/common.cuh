@@ -104,6 +104,18 @@ __device__ __forceinline__ float silu_bf16path(float x) {
   return __fmul_rn(x, rcp_approx(1.0f + ex2_approx(x * -1.4426950408889634f)));
 }
 
+// tanh-form GELU for bf16 outputs: 0.5 x (1 + tanh(z)) == x * sigmoid(2 z),
+// z = sqrt(2/pi) (x + 0.044715 x^3) (examples/gpt2/kernels/gelu.py:9-12),
+// shared by the elementwise kernel and the GEMM epilogues so both round
+// identically.
+__device__ __forceinline__ float gelu_tanh_bf16path(float x) {
+  const float kBeta = 0.7978845608028654f;  // sqrt(2/pi)
+  const float kKappa = 0.044715f;
+  const float x3 = __fmul_rn(__fmul_rn(x, x), x);
+  const float inner = __fmul_rn(kBeta, __fadd_rn(x, __fmul_rn(kKappa, x3)));
+  return __fmul_rn(x, rcp_approx(1.0f + ex2_approx(__fmul_rn(2.0f, inner) * -1.4426950408889634f)));
+}
+
 // ---- programmatic dependent launch ----------------------------------------
 // Every kernel waits for its predecessor on the stream with pdl_wait() before
 // touching global memory, then lets its own successor begin launching

@@ -73,14 +73,13 @@ template <typename T> struct OpGeluSigmoid {
 };
 template <typename T> struct OpGeluTanh {
   __device__ __forceinline__ float operator()(float x) const {
-    const float kBeta = 0.7978845608028654f;  // sqrt(2/pi)
-    const float kKappa = 0.044715f;
-    float x3 = __fmul_rn(__fmul_rn(x, x), x);
-    float inner = __fmul_rn(kBeta, __fadd_rn(x, __fmul_rn(kKappa, x3)));
     if constexpr (sizeof(T) == 2) {
-      // 0.5 x (1 + tanh(z)) == x * sigmoid(2 z) (examples/gpt2/kernels/gelu.py:9-12)
-      return __fmul_rn(x, sigmoid_t<T>(__fmul_rn(2.0f, inner)));
+      return gelu_tanh_bf16path(x);
     } else {
+      const float kBeta = 0.7978845608028654f;  // sqrt(2/pi)
+      const float kKappa = 0.044715f;
+      float x3 = __fmul_rn(__fmul_rn(x, x), x);
+      float inner = __fmul_rn(kBeta, __fadd_rn(x, __fmul_rn(kKappa, x3)));
       // fp32: the same formula as torch's tanh GELU, so the cancellation in
       // 1 + tanh(z) for negative x rounds the same way.
       return __fmul_rn(__fmul_rn(0.5f, x), __fadd_rn(1.0f, tanhf(inner)));

@@ -108,6 +108,7 @@ struct Args {
   const void* bias;  // bf16 [N] or nullptr (linear layer only)
   const void* residual;  // bf16 [M, N] added after the bf16 rounding (bf16 output), or nullptr
   int64_t ldr;
+  int act;  // bf16 output: 1 = tanh GELU of the bf16-rounded linear output (GPT-2 c_fc)
   int64_t ldc;
   int64_t split_stride;  // elements between the split-K slices of c
   int m, n, k;
@@ -473,6 +474,11 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + bv);
             }
+            if (OUT == kOutBf16 && args.act == 1) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                v[j] = __float_as_uint(gelu_tanh_bf16path(__bfloat162float(__float2bfloat16_rn(__uint_as_float(v[j])))));
+            }
             uint8_t* stg = smem + C::STAGES * C::STAGE_BYTES + (q * 2 + (cc & 1)) * (32 * 128);
             if (lane == 0) {
               if (cc == 0) bulk_wait_read<0>();
@@ -513,6 +519,12 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
 #pragma unroll
                   for (int j = 0; j < 32; ++j)
                     v[j] = __float_as_uint(__uint_as_float(v[j]) + __bfloat162float(bp[col0 + j]));
+                }
+                if (args.act == 1) {
+#pragma unroll
+                  for (int j = 0; j < 32; ++j)
+                    v[j] = __float_as_uint(gelu_tanh_bf16path(
+                        __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[j])))));
                 }
                 if (args.residual && row < args.m) {  // residual + bf16(x W^T + b)
                   const __nv_bfloat16* rp =
@@ -597,6 +609,13 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
               if (col0 + j < args.n) cp[(int64_t)(col0 + j) * args.ldc] = v[j];
           }
         } else {
+        if constexpr (OUT == kOutBf16) {
+          if (args.act == 1) {
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj)
+              v[jj] = __float_as_uint(gelu_tanh_bf16path(__bfloat162float(__float2bfloat16_rn(__uint_as_float(v[jj])))));
+          }
+        }
         if constexpr (OUT == kOutBf16 && !TRANS && !PEERS) {
           if (args.residual && row < args.m) {  // y = residual + bf16(x W^T + b), as a linear then an add round
             const __nv_bfloat16* rp = static_cast<const __nv_bfloat16*>(args.residual) + (int64_t)row * args.ldr + col0;
@@ -785,7 +804,7 @@ __device__ __forceinline__ void st_bf16x4(__nv_bfloat16* p, float a, float b, fl
   *reinterpret_cast<uint2*>(p) = *reinterpret_cast<uint2*>(h);
 }
 
-template <bool OUT_BF16>
+template <bool OUT_BF16, bool GELU = false>
 __global__ void __launch_bounds__(256) splitk_reduce4_kernel(const float* __restrict__ part, int splits, int M, int N,
                                                              const __nv_bfloat16* __restrict__ bias,
                                                              const __nv_bfloat16* __restrict__ residual, int64_t ldr,
@@ -802,6 +821,9 @@ __global__ void __launch_bounds__(256) splitk_reduce4_kernel(const float* __rest
   if (bias) add4(acc, ld_bf16x4(bias + n));
   if constexpr (OUT_BF16) {
     float4 r = make_float4(rbf(acc.x), rbf(acc.y), rbf(acc.z), rbf(acc.w));
+    if constexpr (GELU)
+      r = make_float4(gelu_tanh_bf16path(r.x), gelu_tanh_bf16path(r.y), gelu_tanh_bf16path(r.z),
+                      gelu_tanh_bf16path(r.w));
     if (residual) {
       const float4 q = ld_bf16x4(residual + m * ldr + n);
       r = make_float4(q.x + r.x, q.y + r.y, q.z + r.z, q.w + r.w);
@@ -1162,7 +1184,7 @@ bool lines_enabled();
 template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false>
 int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
            cudaStream_t s, const char* what, char* err, size_t errlen, int splits = 1, int64_t split_stride = 0,
-           const PeerArgs* pa = nullptr, const void* residual = nullptr, int64_t ldr = 0) {
+           const PeerArgs* pa = nullptr, const void* residual = nullptr, int64_t ldr = 0, int act = 0) {
   using Cf = Cfg<KIND, B_KMAJOR, BN_, PAIR>;
   const CUtensorMapDataType dt = KIND == kBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   Maps maps;
@@ -1179,6 +1201,7 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   args.bias = bias;
   args.residual = residual;
   args.ldr = ldr;
+  args.act = act;
   args.ldc = ldc;
   args.m = (int)M;
   args.n = (int)N;
@@ -1827,6 +1850,39 @@ extern "C" int xb_linear_residual_bf16(const void* X, const void* W, const void*
                                                                 nullptr, residual, ldr);
   return launch<kBf16, true, kOutBf16>(op, Y, bias, M, N, K, ldy, s, what, err, errlen, 1, 0, nullptr, residual,
                                       ldr);
+}
+
+extern "C" int xb_linear_gelu_bf16(const void* X, const void* W, const void* bias, void* Y, int64_t M, int64_t N,
+                                   int64_t K, int64_t ldx, int64_t ldw, int64_t ldy, void* workspace,
+                                   size_t workspace_bytes, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_linear_gelu_bf16";
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc = check_common(X, W, Y, M, N, K, ldx, ldw, ldy, true, what, err, errlen);
+  if (rc) return rc < 0 ? rc : XB_OK;
+  if (K == 0 || !tma_ok(X, ldx, 2) || !tma_ok(W, ldw, 2)) {
+    set_err(err, errlen, "%s: K must be positive and X/W 16-byte aligned with 16-byte row pitches", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  if (M > 64) {
+    Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
+    if (use_pairs(M))
+      return launch<kBf16, true, kOutBf16, 0, false, false, true>(op, Y, bias, M, N, K, ldy, s, what, err, errlen, 1,
+                                                                  0, nullptr, nullptr, 0, 1);
+    return launch<kBf16, true, kOutBf16>(op, Y, bias, M, N, K, ldy, s, what, err, errlen, 1, 0, nullptr, nullptr, 0,
+                                        1);
+  }
+  // few tokens: split-K partials, then the reduction applies bias and GELU
+  int splits = 1;
+  if (N % 4 || (reinterpret_cast<uintptr_t>(Y) & 15) || ldy % 4 || (bias && (reinterpret_cast<uintptr_t>(bias) & 7))) {
+    set_err(err, errlen, "%s: few-token form needs N %% 4 == 0 and aligned bias / output", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  rc = small_partials(X, W, M, N, K, ldx, ldw, workspace, workspace_bytes, s, what, &splits, err, errlen);
+  if (rc) return rc;
+  const dim3 g4((unsigned)((N / 4 + 255) / 256), (unsigned)M);
+  launch_k(splitk_reduce4_kernel<true, true>, g4, 256, 0, s, (const float*)workspace, splits, (int)M, (int)N,
+           static_cast<const __nv_bfloat16*>(bias), (const __nv_bfloat16*)nullptr, (int64_t)0, Y, ldy);
+  return check_launch(what, err, errlen);
 }
 
 extern "C" int xb_linear_swiglu_bf16(const void* X, const void* W, void* Y, int64_t M, int64_t n_out, int64_t K,

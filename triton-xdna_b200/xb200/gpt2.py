@@ -188,7 +188,7 @@ class GPT2Model:
             if decode:
                 x, xn = ops.linear_residual_norm(attn, L["proj_w"], L["proj_b"], x, L["ln2_w"], L["ln2_b"],
                                                  eps=c.ln_eps, kind="layer")
-                h = ops.gelu_tanh(ops.linear(xn, L["fc_w"], L["fc_b"]))
+                h = ops.linear(xn, L["fc_w"], L["fc_b"], act="gelu_tanh")  # c_fc + tanh GELU, one launch
                 nw, nb = ((self.layers[i + 1]["ln1_w"], self.layers[i + 1]["ln1_b"]) if i + 1 < len(self.layers)
                           else (self.lnf_w, self.lnf_b))
                 x, xn = ops.linear_residual_norm(h, L["mproj_w"], L["mproj_b"], x, nw, nb, eps=c.ln_eps,
@@ -196,7 +196,7 @@ class GPT2Model:
                 continue
             x = ops.linear(attn, L["proj_w"], L["proj_b"], residual=x)  # c_proj + residual add
             xn = ops.layernorm(x, L["ln2_w"], L["ln2_b"], c.ln_eps)
-            h = ops.gelu_tanh(ops.linear(xn, L["fc_w"], L["fc_b"]))
+            h = ops.linear(xn, L["fc_w"], L["fc_b"], act="gelu_tanh")  # c_fc + tanh GELU, one launch
             x = ops.linear(h, L["mproj_w"], L["mproj_b"], residual=x)  # mlp c_proj + residual add
         cache.length = pos + S
         if decode:

@@ -401,13 +401,28 @@ def _workspace(device, nbytes: int) -> torch.Tensor:
     return ws
 
 
-def linear(x, weight, bias=None, out=None, out_dtype=torch.bfloat16, residual=None):
+def linear(x, weight, bias=None, out=None, out_dtype=torch.bfloat16, residual=None, act=None):
     """y = [residual +] x @ weight^T + bias, weight [N, K] (nn.Linear layout),
     bf16 inputs, fp32 accumulation, y in bf16 or fp32
     (examples/qwen2_5/kernels/matmul.py:172-296).  Up to SMALL_M rows use the
-    small-M kernel with the residual add fused; larger inputs use the tiled
-    GEMM followed by vecadd."""
+    small-M kernel with the residual add fused; larger inputs the tiled GEMM
+    with the residual add in its epilogue.  act="gelu_tanh" applies the tanh
+    GELU to the bf16 output inside the same launch (GPT-2 c_fc)."""
     _cuda(x, weight, bias, out, residual)
+    if act is not None:
+        if act != "gelu_tanh" or residual is not None or out_dtype != torch.bfloat16:
+            raise ValueError("act='gelu_tanh' takes bf16 output and no residual")
+        K = x.shape[-1]
+        N = weight.shape[0]
+        x2 = x.reshape(-1, K)
+        M = x2.shape[0]
+        y = out.reshape(M, N) if out is not None else torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+        ws = _small_ws(x, M, N, K) if M <= SMALL_M else None
+        _lib.call("xb_linear_gelu_bf16", x2.data_ptr(), weight.data_ptr(),
+                  bias.data_ptr() if bias is not None else None, y.data_ptr(), M, N, K, _mat(x2, "x"),
+                  _mat(weight, "weight"), _mat(y, "y"), ws.data_ptr() if ws is not None else None,
+                  ws.numel() * 4 if ws is not None else 0, _stream())
+        return y.reshape(*x.shape[:-1], N) if out is None else out
     if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
         raise TypeError("linear takes bf16 x and weight")
     if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != weight.shape[0]
