@@ -391,9 +391,24 @@ SMALL_M = 64  # token counts at or below this take the swap-AB split-K path
 _workspaces: dict = {}
 
 
+def reserve_workspace(device, nbytes: int) -> None:
+    """Grow the shared scratch buffer to at least `nbytes` now.  A captured
+    CUDA graph records the buffer's address, so everything a set of graphs
+    will need must be reserved before the first capture (a later growth would
+    leave earlier graphs pointing at freed memory)."""
+    _workspace(torch.device(device), nbytes)
+
+
+def attention_workspace_bytes(batch, seq, n_head, n_kv_head, pos_offset) -> int:
+    need = ctypes.c_size_t(0)
+    _lib.call("xb_attention_workspace_size", batch, seq, n_head, n_kv_head, pos_offset, ctypes.byref(need))
+    return need.value
+
+
 def _workspace(device, nbytes: int) -> torch.Tensor:
     """A per-device fp32 scratch buffer that only grows (kept alive so its
-    address is stable, e.g. across CUDA-graph replays)."""
+    address is stable, e.g. across CUDA-graph replays).  One buffer per
+    device: operators that use it must not run concurrently on two streams."""
     ws = _workspaces.get(device)
     if ws is None or ws.numel() * 4 < nbytes:
         ws = torch.empty(max(nbytes // 4, 1 << 20), dtype=torch.float32, device=device)

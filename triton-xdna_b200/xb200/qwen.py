@@ -244,8 +244,12 @@ class DecodeGraphs:
         self.batch, self.prompt, self.new = batch, prompt, new
         self.cache = model.new_cache(batch, prompt + new)
         self.toks = torch.zeros((new, batch), dtype=torch.int64, device=model.device)
-        # one eager step first: per-kernel attributes and the small-M
-        # workspace are set up outside any capture
+        # the scratch buffer the last step's attention needs is reserved
+        # before any capture (graphs record its address), then one eager step
+        # sets up per-kernel attributes and the small-M workspace
+        c = model.cfg
+        ops.reserve_workspace(model.device, ops.attention_workspace_bytes(batch, 1, c.n_head, c.n_kv_head,
+                                                                          prompt + new - 1))
         self.cache.length = prompt
         model.forward(self.toks[0].view(batch, 1), self.cache, last_only=True)
         torch.cuda.synchronize()
