@@ -268,7 +268,11 @@ XB_API int xb_linear_small_plan(int64_t M, int64_t N, int64_t K,
  * automatic) so the weight streams from HBM on every SM, and a fixed-order
  * reduction adds the slices, the bias and the residual (bf16 [M, N], row
  * pitch ldr, may be NULL).  Needs the workspace xb_linear_small_plan
- * reports.  Replaces `triton_linear` + `triton_add` in the decode step
+ * reports.  With bf16 output, M <= 64, N % 4 == 0 and 8-byte aligned bf16
+ * vectors the whole linear is one launch of the cluster split-K decode
+ * kernel (xb_decode_linear_bf16 / xb_decode_linear_residual_bf16; `splits`
+ * and the workspace are then unused).  Replaces
+ * `triton_linear` + `triton_add` in the decode step
  * (examples/qwen2_5/model.py:1045-1061). */
 XB_API int xb_linear_small_bf16(const void* X, const void* W, const void* bias,
                                 const void* residual, void* Y, int64_t M,
@@ -301,8 +305,9 @@ XB_API int xb_linear_residual_bf16(const void* X, const void* W, const void* bia
 
 /* Y = bf16(gelu_tanh(bf16(X @ W^T + bias))) (bf16, any M): the linear with
  * the tanh GELU fused (GPT-2 c_fc + gelu, examples/gpt2/model.py:1046-1051),
- * rounded as a linear followed by the GELU kernel.  M <= 64 uses the split-K
- * form (workspace as xb_linear_small_plan reports; N % 4 == 0). */
+ * rounded as a linear followed by the GELU kernel.  M <= 64 uses the cluster
+ * split-K decode kernel (N % 4 == 0; the workspace, as xb_linear_small_plan
+ * reports, only when pointers or pitches rule that kernel out). */
 XB_API int xb_linear_gelu_bf16(const void* X, const void* W, const void* bias,
                                void* Y, int64_t M, int64_t N, int64_t K,
                                int64_t ldx, int64_t ldw, int64_t ldy,
@@ -310,11 +315,12 @@ XB_API int xb_linear_gelu_bf16(const void* X, const void* W, const void* bias,
                                void* stream, char* err, size_t errlen);
 
 /* Y [M, n_out] = bf16(silu(bf16(X Wg^T)) * bf16(X Wu^T)) with W [2 n_out, K]
- * interleaving 128-row blocks of gate and up rows (block 2b = gate rows
- * 128b..128b+127, block 2b+1 = the up rows of the same features); n_out %
- * 128 == 0.  One GEMM whose epilogue applies the SwiGLU (M > 64), or the
- * split-K small-M GEMM and its SwiGLU finisher (M <= 64; workspace as
- * xb_linear_small_plan reports for N = 2 n_out).  The roundings are those of
+ * interleaving 64-row blocks of gate and up rows (block 2b = gate rows
+ * 64b..64b+63, block 2b+1 = the up rows of the same features); n_out %
+ * 64 == 0.  One GEMM whose epilogue applies the SwiGLU (M > 64), or the
+ * cluster split-K decode kernel with the SwiGLU in the same launch (M <= 64;
+ * the workspace, as xb_linear_small_plan reports for N = 2 n_out, is used
+ * only when pointers or pitches rule that kernel out).  The roundings are those of
  * two linears and the silu*up kernel (examples/qwen2_5/model.py:1047-1059,
  * kernels/swiglu.py:94-160). */
 XB_API int xb_linear_swiglu_bf16(const void* X, const void* W, void* Y,
@@ -324,8 +330,11 @@ XB_API int xb_linear_swiglu_bf16(const void* X, const void* W, void* Y,
                                  void* stream, char* err, size_t errlen);
 
 /* Decode-step fusions of the small-M linear (one token per sequence, M =
- * batch <= 65535 rows), each a split-K GEMM into `workspace` (the bytes
- * xb_linear_small_plan reports for M, N, K) plus one finishing kernel.
+ * batch <= 65535 rows).  Up to 64 rows xb_linear_small_rope_kv_bf16 is ONE
+ * launch of the cluster split-K decode kernel (below) and
+ * xb_linear_small_residual_norm_bf16 that kernel plus the row-norm kernel;
+ * otherwise a split-K GEMM into `workspace` (the bytes xb_linear_small_plan
+ * reports for M, N, K) plus one finishing kernel.
  *
  * xb_linear_small_rope_kv_bf16: the fused QKV projection of a decode token
  * finished into attention inputs: qkv = X @ W^T + bias (W [(H + 2 KVH) * D,
@@ -358,6 +367,67 @@ XB_API int xb_linear_small_residual_norm_bf16(
     int norm_kind, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
     int64_t ldr, int64_t ldy, int64_t ldn, void* workspace,
     size_t workspace_bytes, void* stream, char* err, size_t errlen);
+
+/* Decode-step linears, one launch each, M <= 64 tokens (one per sequence):
+ * the cluster split-K kernel (a cluster of <= 8 CTAs per 128-row block of W
+ * [N, K]; the K slices are summed over distributed shared memory in rank
+ * order) with the work that follows the linear in the same kernel.
+ *
+ * Input X [M, K] bf16 (row pitch ldx) is used as is when x_stats is NULL.
+ * Otherwise X carries a pending norm, applied as X is loaded:
+ *   x_norm_kind 0  xn = bf16(x * rsqrt(mean(x^2) + eps) * x_norm_w)      (RMSNorm)
+ *   x_norm_kind 1  xn = bf16((x - mean) * rsqrt(var + eps) * x_norm_w
+ *                            + x_norm_b)                                  (LayerNorm)
+ * with the row statistics combined from x_stats, the block statistics that
+ * xb_decode_linear_residual_bf16 wrote with the same kind when it produced X
+ * (K % 8 == 0; x_norm_w / x_norm_b 16-byte aligned).  This is how a residual
+ * add, the norm after it and the next linear take two launches (the
+ * residual stream and the norm of examples/qwen2_5/model.py:1045-1061 and
+ * examples/gpt2/model.py:1032-1059).
+ *
+ * xb_decode_linear_bf16: Y = bf16(xn W^T + bias), act 1 = tanh GELU on that
+ *   value (GPT-2 c_fc + gelu, examples/gpt2/model.py:1046-1051).
+ * xb_decode_linear_rope_kv_bf16: the QKV projection finished into attention
+ *   inputs, as xb_linear_small_rope_kv_bf16 (head_dim % 8 == 0, dividing 128).
+ * xb_decode_linear_swiglu_bf16: Y [M, n_out] = bf16(silu(bf16(xn Wg^T)) *
+ *   bf16(xn Wu^T)), W interleaving 64-row blocks of gate and up rows (the
+ *   layout of xb_linear_swiglu_bf16), n_out % 64 == 0.
+ * xb_decode_linear_residual_bf16: Y = residual + bf16(xn W^T + bias) and,
+ *   when stats_out is not NULL, the statistics of each Y row per 128-column
+ *   block for the norm that follows: stats_out holds ceil(N / 128) * 64 float
+ *   pairs ([block][token]); stats_kind 0 stores (sum of squares, 0), 1 stores
+ *   (block mean, sum of squared deviations from it).
+ * The statistics are summed in block order, so every result is bit-
+ * repeatable.  Pitches are in elements; outputs and bf16 vectors 8-byte
+ * aligned with pitches % 4 == 0; N % 4 == 0. */
+XB_API int xb_decode_linear_bf16(const void* X, int64_t M, int64_t ldx,
+                                 const float* x_stats, const void* x_norm_w,
+                                 const void* x_norm_b, float x_eps,
+                                 int x_norm_kind, const void* W,
+                                 const void* bias, void* Y, int64_t N,
+                                 int64_t K, int64_t ldw, int64_t ldy, int act,
+                                 void* stream, char* err, size_t errlen);
+XB_API int xb_decode_linear_rope_kv_bf16(
+    const void* X, int64_t M, int64_t ldx, const float* x_stats,
+    const void* x_norm_w, const void* x_norm_b, float x_eps, int x_norm_kind,
+    const void* W, const void* bias, const float* cos_t, const float* sin_t,
+    void* q_out, void* k_cache, void* v_cache, int64_t n_head,
+    int64_t n_kv_head, int64_t head_dim, int64_t max_seq, int64_t pos_offset,
+    int64_t K, int64_t ldw, void* stream, char* err, size_t errlen);
+XB_API int xb_decode_linear_swiglu_bf16(const void* X, int64_t M, int64_t ldx,
+                                        const float* x_stats,
+                                        const void* x_norm_w,
+                                        const void* x_norm_b, float x_eps,
+                                        int x_norm_kind, const void* W, void* Y,
+                                        int64_t n_out, int64_t K, int64_t ldw,
+                                        int64_t ldy, void* stream, char* err,
+                                        size_t errlen);
+XB_API int xb_decode_linear_residual_bf16(
+    const void* X, int64_t M, int64_t ldx, const float* x_stats,
+    const void* x_norm_w, const void* x_norm_b, float x_eps, int x_norm_kind,
+    const void* W, const void* bias, const void* residual, void* Y,
+    float* stats_out, int stats_kind, int64_t N, int64_t K, int64_t ldw,
+    int64_t ldr, int64_t ldy, void* stream, char* err, size_t errlen);
 
 /* ---------------------------------------------------------------------------
  * N-sharded GEMM across the GPUs of one node (one process per GPU).  The

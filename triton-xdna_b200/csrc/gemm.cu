@@ -47,9 +47,10 @@ __device__ int g_gemm_status = 0;
 constexpr uint64_t kWaitLimit = 2000000000ull;  // 2 s per wait: far above any legitimate wait
 
 enum Kind { kBf16 = 0, kInt8 = 1, kInt16Limbs = 2 };
-// kOutSwiglu: W interleaves 128-row blocks of gate and up rows (block 2b =
-// gate rows 128b.., block 2b+1 = up rows 128b..), so a 256-column tile holds
-// the gate and up values of 128 output features; the epilogue writes
+// kOutSwiglu: W interleaves 64-row blocks of gate and up rows (block 2b =
+// gate rows 64b.., block 2b+1 = up rows 64b..), so a 256-column tile holds
+// the gate and up values of 128 output features (and a 128-row block of W,
+// the decode kernel's unit, those of 64); the epilogue writes
 // bf16(silu(bf16(g)) * bf16(u)) into C [M, N/2] -- the roundings of two bf16
 // linears followed by the silu*up kernel.
 enum Out { kOutF32 = 0, kOutBf16 = 1, kOutI32 = 2, kOutSwiglu = 3 };
@@ -382,8 +383,9 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
         if constexpr (OUT == kOutSwiglu) {
           if (cc >= C::BN / 64) continue;
           uint32_t gv[32], uv[32];
-          tmem_ld_32x32b_x32(tbase + cc * 32, gv);               // gate features
-          tmem_ld_32x32b_x32(tbase + C::BN / 2 + cc * 32, uv);   // up features
+          const int gc = (cc >> 1) * 128 + (cc & 1) * 32;  // 64 gate columns, then their 64 up columns
+          tmem_ld_32x32b_x32(tbase + gc, gv);        // gate features
+          tmem_ld_32x32b_x32(tbase + gc + 64, uv);   // up features
           tmem_ld_wait();
           const int f0 = tn * (C::BN / 2) + cc * 32;  // output feature of column 0
           const int nout = args.n / 2;
@@ -835,7 +837,7 @@ __global__ void __launch_bounds__(256) splitk_reduce4_kernel(const float* __rest
   }
 }
 
-// IL: W interleaves 128-row blocks of gate and up rows (the kOutSwiglu layout);
+// IL: W interleaves 64-row blocks of gate and up rows (the kOutSwiglu layout);
 // otherwise gate rows [0, n_out) are stacked over up rows [n_out, 2 n_out).
 template <bool IL>
 __global__ void __launch_bounds__(256) splitk_swiglu4_kernel(const float* __restrict__ part, int splits, int M,
@@ -846,8 +848,8 @@ __global__ void __launch_bounds__(256) splitk_swiglu4_kernel(const float* __rest
   const int f = (blockIdx.x * 256 + threadIdx.x) * 4;
   if (f >= n_out) return;
   const int64_t slice = (int64_t)M * 2 * n_out;
-  const int gcol = IL ? ((f >> 7) << 8) + (f & 127) : f;
-  const int ucol = gcol + (IL ? 128 : n_out);
+  const int gcol = IL ? ((f >> 6) << 7) + (f & 63) : f;
+  const int ucol = gcol + (IL ? 64 : n_out);
   const float* pg = part + (int64_t)m * 2 * n_out + gcol;
   const float* pu = part + (int64_t)m * 2 * n_out + ucol;
   float4 g = __ldcg(reinterpret_cast<const float4*>(pg));
@@ -1593,6 +1595,635 @@ extern "C" int xb_linear_bf16(const void* X, const void* W, const void* bias, vo
   return launch<kBf16, true, kOutBf16>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
 }
 
+namespace xb {
+namespace gemm {
+
+// ---- decode linears: split-K over a thread-block cluster, finished in place ----
+//
+// Y = X W^T for the few tokens of a decode step (M <= 64), with the work that
+// follows the linear in the same launch.  A cluster of S CTAs owns one
+// 128-row block of W (128 output features x all tokens); CTA r of the
+// cluster multiplies K blocks [r kps, (r+1) kps) into a 128 x 64 fp32 TMEM
+// accumulator (tcgen05, swap-AB: weight rows are the MMA's M, tokens its N).
+// CTA q of the cluster owns tokens [q pt, (q+1) pt), pt = ceil(64 / S): every
+// CTA pushes the rows of its partial that belong to CTA q into q's receive
+// buffer over distributed shared memory (16-byte stores), one cluster
+// barrier publishes them, and each CTA sums the S partials of its tokens from
+// its own shared memory in rank order (deterministic), then applies the
+// finisher:
+//   kFinStore     y = bf16(acc + bias), optionally the tanh GELU on that value
+//   kFinRopeKv    qkv = bf16(acc + bias), rotate-half RoPE of the query / key
+//                 heads, written to q [B, H, D] and the K / V caches at `pos`
+//   kFinSwiglu    W interleaves 64-row blocks of gate and up rows; y =
+//                 bf16(silu(bf16(g)) * bf16(u)) for the block's 64 features
+//   kFinResidual  y = bf16(residual + bf16(acc + bias)), plus per (128-row
+//                 block, token) statistics of y for the norm that follows:
+//                 the sum of squares (RMSNorm) or the block mean and sum of
+//                 squared deviations (LayerNorm, combined later with Chan's
+//                 parallel formula)
+// The partial sums never leave the chip (no split-K workspace, no second
+// kernel), and no CTA touches another's shared memory after the barrier, so
+// none waits for its peers before it exits.  A pending norm of X (XNORM) is
+// applied as X is loaded: the consumer combines the producer's block
+// statistics per token (fixed order) and, while the weight tiles stream, the
+// epilogue warps rewrite each X tile in shared memory as bf16(norm(x)) before
+// the MMA reads it -- so a residual add, the norm after it and the next
+// linear take two launches, not four.  Everything that does not depend on the
+// previous kernel (weight tiles of the first ring slots, norm weights, bias)
+// is requested before the programmatic-launch wait.
+enum Fin { kFinStore = 0, kFinRopeKv = 1, kFinSwiglu = 2, kFinResidual = 3 };
+
+constexpr int kDecBM = 128;                   // weight rows per cluster (TMEM lanes)
+constexpr int kDecBN = 64;                    // tokens (MMA N)
+constexpr int kDecBK = 64;                    // K elements per ring slot (128 bytes of bf16)
+constexpr int kDecA = kDecBM * 128;           // weight tile bytes per slot
+constexpr int kDecStage = kDecA + kDecBN * 128;
+constexpr int kDecRedBytes = kDecBN * kDecBM * 4;  // this CTA's fp32 partial [token][row], over the ring
+constexpr int kDecMaxCluster = 8;             // CTAs per cluster (the portable cluster size)
+// receive buffer [source rank][owned token][row] fp32: S * ceil(64 / S) <= 72 token rows
+constexpr int kDecRecvBytes = 72 * kDecBM * 4;
+
+struct DecMaps {
+  CUtensorMap w;  // W [N, K] K-major, 64 x 128 boxes
+  CUtensorMap x;  // X [M, K] K-major, 64 x 64 boxes (rows past M read as zero)
+};
+
+struct DecArgs {
+  int m, n, k;                 // tokens, weight rows, K
+  int kblocks, kps, splits;    // K blocks of 64, per CTA, CTAs per cluster
+  // pending norm of X (XNORM): block statistics [ceil(K / 128)][64] of its rows
+  const float2* xstats;
+  const __nv_bfloat16* xnw;
+  const __nv_bfloat16* xnb;    // LayerNorm bias or null
+  float xeps;
+  int xkind;                   // 0 RMSNorm, 1 LayerNorm
+  const __nv_bfloat16* bias;   // [n] or null
+  __nv_bfloat16* y;            // Store / Swiglu / Residual output
+  int64_t ldy;
+  int act;                     // Store: 1 = tanh GELU
+  const __nv_bfloat16* residual;
+  int64_t ldr;
+  float2* stats;               // Residual: statistics of y [ceil(n / 128)][64], or null
+  int stats_kind;              // 0 RMSNorm (sum of squares), 1 LayerNorm (mean, M2)
+  const float* cos_t;          // RopeKv: [positions, D] tables or null (no rotation)
+  const float* sin_t;
+  __nv_bfloat16* q_out;        // [B, H, D]
+  __nv_bfloat16* k_cache;      // [B, KVH, smax, D]
+  __nv_bfloat16* v_cache;
+  int H, KVH, D, smax, pos;
+};
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o_ = 16; o_ > 0; o_ >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o_);
+  return x;
+}
+
+__device__ __forceinline__ void st_dsmem_f4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w)
+               : "memory");
+}
+
+template <int FIN, int STAGES, bool XNORM>
+__global__ void __launch_bounds__(192, 1) decode_linear_kernel(const __grid_constant__ DecMaps maps,
+                                                               const DecArgs args) {
+  static_assert(STAGES * kDecStage >= kDecRedBytes, "the partial fits over the ring");
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t xready_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+  __shared__ float s_mean[kDecBN], s_rstd[kDecBN];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_u32 - smem_u32(smem_raw));
+  float* recv = reinterpret_cast<float*>(smem + STAGES * kDecStage);  // not the ring: peers write it any time
+  const int S = args.splits;
+  const int rank = (int)cluster_ctarank();
+  const int blk = (int)blockIdx.x / S;  // 128-row block of W
+  const int kb0 = rank * args.kps;
+  const int nkb = min(kb0 + args.kps, args.kblocks) - kb0;  // >= 1 (host picks S so)
+  const int pt = (kDecBN + S - 1) / S;                       // tokens owned per CTA
+  const int tok0 = rank * pt, ntok = max(0, min(args.m, tok0 + pt) - tok0);
+  const int row0 = blk * kDecBM;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&xready_bar[s], 128);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&tfull_bar, 1);
+    abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&maps.w);
+    prefetch_tmap(&maps.x);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, kDecBN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+  if (warp == 1) {
+    pdl_wait();
+    pdl_trigger();
+  }
+  auto fail = [&]() {
+    atomicExch(&g_gemm_status, XB_ERR_TIMEOUT);
+    abort_flag = 1;
+  };
+
+  // Residual finisher: warp w of the epilogue takes owned tokens w, w + 4, ...;
+  // their residual rows are requested while the MMAs run.
+  constexpr int kPre = 4;
+  float4 rpre[kPre];
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const int npre = min(STAGES, nkb);
+      for (int i = 0; i < npre; ++i) {
+        mbar_arrive_expect_tx(&full_bar[i], kDecStage);
+        tma_load_2d(smem + i * kDecStage, &maps.w, &full_bar[i], (kb0 + i) * kDecBK, row0);
+      }
+      pdl_wait();  // X is written by the previous kernel
+      pdl_trigger();
+      for (int i = 0; i < npre; ++i)
+        tma_load_2d(smem + i * kDecStage + kDecA, &maps.x, &full_bar[i], (kb0 + i) * kDecBK, 0);
+      int issued = npre;
+      for (int i = npre; i < nkb; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait(&empty_bar[s], ((i / STAGES) & 1) ^ 1, kWaitLimit, &abort_flag)) {
+          fail();
+          break;
+        }
+        mbar_arrive_expect_tx(&full_bar[s], kDecStage);
+        tma_load_2d(smem + s * kDecStage, &maps.w, &full_bar[s], (kb0 + i) * kDecBK, row0);
+        tma_load_2d(smem + s * kDecStage + kDecA, &maps.x, &full_bar[s], (kb0 + i) * kDecBK, 0);
+        issued = i + 1;
+      }
+      // every load issued must have landed before the ring is reused or the CTA exits
+      for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i)
+        if (!mbar_wait(&full_bar[i % STAGES], (i / STAGES) & 1, kWaitLimit, &abort_flag)) fail();
+    } else {
+      pdl_wait();
+      pdl_trigger();
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int done = 0;
+      for (int i = 0; i < nkb; ++i, ++done) {
+        const int s = i % STAGES;
+        uint64_t* ready = XNORM ? &xready_bar[s] : &full_bar[s];
+        if (!mbar_wait(ready, (i / STAGES) & 1, kWaitLimit, &abort_flag)) {
+          fail();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = base_u32 + s * kDecStage;
+#pragma unroll
+        for (int ks = 0; ks < kDecBK / 16; ++ks)
+          mma_f16(tmem_base, umma_desc_sw128(st + ks * 32, 16, 1024), umma_desc_sw128(st + kDecA + ks * 32, 16, 1024),
+                  umma_idesc(1, 1, 1, 0, 0, kDecBM, kDecBN), (i > 0 || ks > 0) ? 1u : 0u);
+        tc_commit(&empty_bar[s]);
+      }
+      if (done > 0) {
+        tc_commit(&tfull_bar);  // the accumulator is final once these MMAs complete
+        // The issuing thread itself sees them complete (whatever the abort
+        // flag says) before the TMEM can be released after the cluster barrier.
+        volatile int never = 0;
+        if (!mbar_wait(&tfull_bar, 0, kWaitLimit, &never)) fail();
+      }
+    }
+    __syncwarp();
+  } else {
+    const int e = threadIdx.x - 64;  // 0 .. 127
+    if constexpr (XNORM) {
+      // ---------------------------------------------------------- X tiles -> bf16(norm(X))
+      // Thread e rewrites the 16-byte chunks (token (e >> 3) + 16 jj, K
+      // elements 8 (e & 7) .. + 7) of every slot: one norm-weight vector per
+      // slot, the first requested before the wait (the weights are constant).
+      const int j = e & 7;
+      auto ld_w = [&](int i, uint4& w, uint4& b) {
+        const int k0 = (kb0 + i) * kDecBK + j * 8;
+        w = make_uint4(0u, 0u, 0u, 0u);
+        b = make_uint4(0u, 0u, 0u, 0u);
+        if (i < nkb && k0 < args.k) {
+          w = __ldg(reinterpret_cast<const uint4*>(args.xnw + k0));
+          if (args.xkind == 1 && args.xnb) b = __ldg(reinterpret_cast<const uint4*>(args.xnb + k0));
+        }
+      };
+      uint4 wn, bn;
+      ld_w(0, wn, bn);
+      pdl_wait();
+      pdl_trigger();
+      if (e < kDecBN) {  // per-token mean / rstd from the producer's block statistics, in block order
+        const int t = e;
+        float mean = 0.0f, rstd = 0.0f;
+        if (t < args.m) {
+          const int nb = (args.k + kDecBM - 1) / kDecBM;
+          float na = 0.0f, ma = 0.0f, acc = 0.0f;
+          for (int b0 = 0; b0 < nb; b0 += 8) {  // eight loads in flight, then the fixed-order combine
+            float2 st[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+              st[u] = b0 + u < nb ? __ldcg(&args.xstats[(b0 + u) * kDecBN + t]) : make_float2(0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+              if (b0 + u >= nb) break;
+              if (args.xkind == 0) {
+                acc += st[u].x;
+              } else {  // Chan et al.: merge (n_b, mean_b, M2_b) into the running (n, mean, M2)
+                const float nbk = (float)min(kDecBM, args.k - (b0 + u) * kDecBM);
+                const float n = na + nbk, delta = st[u].x - ma;
+                ma += delta * (nbk / n);
+                acc += st[u].y + delta * delta * (na * nbk / n);
+                na = n;
+              }
+            }
+          }
+          mean = args.xkind == 0 ? 0.0f : ma;
+          rstd = __frsqrt_rn(acc / (float)args.k + args.xeps);
+        }
+        s_mean[t] = mean;
+        s_rstd[t] = rstd;
+      }
+      epi_bar();
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % STAGES;
+        const uint4 wraw = wn, braw = bn;
+        ld_w(i + 1, wn, bn);  // the next slot's weights, while this one is rewritten
+        if (!mbar_wait(&full_bar[s], (i / STAGES) & 1, kWaitLimit, &abort_flag)) {
+          fail();
+          break;
+        }
+        uint8_t* xs = smem + s * kDecStage + kDecA;  // [64 tokens][128 bytes], 128-byte swizzle
+        const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wraw);
+        const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&braw);
+        if ((kb0 + i) * kDecBK + j * 8 < args.k) {  // past K: zero-filled, stays zero
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const int r = (e >> 3) + 16 * jj;
+            uint4* p = reinterpret_cast<uint4*>(xs + r * 128 + ((j ^ (r & 7)) << 4));
+            uint4 raw = *p;
+            __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+            const float mean = s_mean[r], rstd = s_rstd[r];
+            if (args.xkind == 0) {
+#pragma unroll
+              for (int q2 = 0; q2 < 4; ++q2)
+                h[q2] = __floats2bfloat162_rn(__fmul_rn(__fmul_rn(__low2float(h[q2]), rstd), __low2float(wh[q2])),
+                                              __fmul_rn(__fmul_rn(__high2float(h[q2]), rstd), __high2float(wh[q2])));
+            } else {
+#pragma unroll
+              for (int q2 = 0; q2 < 4; ++q2)
+                h[q2] = __floats2bfloat162_rn(
+                    (__low2float(h[q2]) - mean) * rstd * __low2float(wh[q2]) + __low2float(bh[q2]),
+                    (__high2float(h[q2]) - mean) * rstd * __high2float(wh[q2]) + __high2float(bh[q2]));
+            }
+            *p = raw;
+          }
+        }
+        fence_proxy_async_smem();  // these writes, before the MMA's (async-proxy) reads
+        mbar_arrive(&xready_bar[s]);
+      }
+    } else {
+      pdl_wait();
+      pdl_trigger();
+    }
+    if constexpr (FIN == kFinResidual) {
+#pragma unroll
+      for (int u = 0; u < kPre; ++u) {
+        const int tl = (warp - 2) + 4 * u, n = row0 + lane * 4;
+        rpre[u] = tl < ntok && n < args.n ? ld_bf16x4(args.residual + (tok0 + tl) * args.ldr + n)
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    // ------------------------------------------------------------ accumulator -> owners
+    const int q = warp & 3;  // TMEM lane quarter this warp may read
+    const bool got = mbar_wait(&tfull_bar, 0, kWaitLimit, &abort_flag);
+    if (!got) fail();
+    float* red = reinterpret_cast<float*>(smem);  // [token][row], over the ring (this CTA's MMAs are done)
+    if (got) {
+      tc_fence_after();
+      fence_proxy_async_smem();
+      const int row = q * 32 + lane;
+#pragma unroll
+      for (int h = 0; h < kDecBN / 32; ++h) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + h * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) red[(h * 32 + jj) * kDecBM + row] = __uint_as_float(v[jj]);
+      }
+    }
+    tc_fence_before();
+    epi_bar();
+    if (got) {
+      // token t's row of the partial -> slot `rank` of its owner's receive buffer
+      const uint32_t recv0 = smem_u32(recv);
+      for (int c = e; c < args.m * (kDecBM / 4); c += 128) {
+        const int t = c >> 5, owner = t / pt;
+        const uint32_t dst = mapa_u32(recv0, (uint32_t)owner) +
+                             (uint32_t)(((rank * pt + (t - owner * pt)) * kDecBM + (c & 31) * 4) * 4);
+        st_dsmem_f4(dst, reinterpret_cast<const float4*>(red)[c]);
+      }
+    }
+  }
+  __syncwarp();
+  cluster_sync();  // every partial row is in its owner's receive buffer
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kDecBN);
+  }
+  if (warp < 2) return;
+
+  // ------------------------------------------------------------ finisher (own shared memory only)
+  const int e = threadIdx.x - 64;  // 0 .. 127
+  // sum of the S partials of (owned token tl, rows c..c+3), rank order
+  auto gather = [&](int tl, int c) {
+    const float4* p = reinterpret_cast<const float4*>(recv + tl * kDecBM + c);
+    constexpr int kSlot = kDecBM / 4;  // float4 per token row
+    float4 acc = p[0];
+    for (int jr = 1; jr < S; ++jr) add4(acc, p[jr * pt * kSlot]);
+    return acc;
+  };
+  if constexpr (FIN == kFinStore) {
+    for (int u = e; u < ntok * 32; u += 128) {
+      const int tl = u >> 5, c = (u & 31) * 4;
+      const int n = row0 + c;
+      if (n >= args.n) continue;
+      float4 acc = gather(tl, c);
+      if (args.bias) add4(acc, ld_bf16x4(args.bias + n));
+      float4 o = make_float4(rbf(acc.x), rbf(acc.y), rbf(acc.z), rbf(acc.w));
+      if (args.act == 1)
+        o = make_float4(gelu_tanh_bf16path(o.x), gelu_tanh_bf16path(o.y), gelu_tanh_bf16path(o.z),
+                        gelu_tanh_bf16path(o.w));
+      st_bf16x4(args.y + (tok0 + tl) * args.ldy + n, o.x, o.y, o.z, o.w);
+    }
+  } else if constexpr (FIN == kFinResidual) {
+    // warp per owned token, lane = 4-row group: the block statistics of a
+    // token row reduce within the warp
+    const int c = lane * 4, n = row0 + c;
+    const bool valid = n < args.n;
+    const float cnt = (float)min(kDecBM, args.n - row0);
+    const float4 bias4 = valid && args.bias ? ld_bf16x4(args.bias + n) : make_float4(0.f, 0.f, 0.f, 0.f);
+    auto token = [&](int u, float4 r) {
+      const int tl = (warp - 2) + 4 * u, t = tok0 + tl;
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (valid) {
+        float4 acc = gather(tl, c);
+        add4(acc, bias4);
+        o = make_float4(rbf(r.x + rbf(acc.x)), rbf(r.y + rbf(acc.y)), rbf(r.z + rbf(acc.z)), rbf(r.w + rbf(acc.w)));
+        st_bf16x4(args.y + t * args.ldy + n, o.x, o.y, o.z, o.w);
+      }
+      if (args.stats) {
+        float2 st;
+        if (args.stats_kind == 0) {
+          st = make_float2(warp_sum((o.x * o.x + o.y * o.y) + (o.z * o.z + o.w * o.w)), 0.0f);
+        } else {
+          // shifted sums (shift: the block's first value) give the block mean and
+          // the sum of squared deviations in one pass of two interleaved reductions
+          const float sh = __shfl_sync(0xffffffffu, o.x, 0);
+          const float a = o.x - sh, b = o.y - sh, cc = o.z - sh, d = o.w - sh;
+          float s1 = valid ? (a + b) + (cc + d) : 0.0f;
+          float s2 = valid ? (a * a + b * b) + (cc * cc + d * d) : 0.0f;
+#pragma unroll
+          for (int o_ = 16; o_ > 0; o_ >>= 1) {
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o_);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, o_);
+          }
+          st = make_float2(sh + s1 / cnt, fmaxf(s2 - s1 * s1 / cnt, 0.0f));
+        }
+        if (lane == 0) args.stats[blk * kDecBN + t] = st;
+      }
+    };
+#pragma unroll
+    for (int u = 0; u < kPre; ++u)  // residual rows already in registers
+      if ((warp - 2) + 4 * u < ntok) token(u, rpre[u]);
+    for (int u = kPre; (warp - 2) + 4 * u < ntok; ++u)
+      token(u, valid ? ld_bf16x4(args.residual + (tok0 + (warp - 2) + 4 * u) * args.ldr + n)
+                     : make_float4(0.f, 0.f, 0.f, 0.f));
+  } else if constexpr (FIN == kFinSwiglu) {
+    // rows [0, 64) gate and [64, 128) up of features blk*64 .. blk*64+63
+    for (int u = e; u < ntok * 16; u += 128) {
+      const int tl = u >> 4, c = (u & 15) * 4;
+      const float4 g = gather(tl, c), up = gather(tl, 64 + c);
+      auto sw = [](float gg, float uu) { return __fmul_rn(silu_bf16path(rbf(gg)), rbf(uu)); };
+      st_bf16x4(args.y + (tok0 + tl) * args.ldy + blk * 64 + c, sw(g.x, up.x), sw(g.y, up.y), sw(g.z, up.z),
+                sw(g.w, up.w));
+    }
+  } else {
+    // kFinRopeKv: units (owned token, 4 consecutive rotation pairs of one head)
+    const int D = args.D, half = D >> 1;
+    const int slots = args.H + 2 * args.KVH;
+    for (int u = e; u < ntok * 16; u += 128) {
+      const int tl = u >> 4, p = (u & 15) * 4;  // first pair index within the block
+      const int hd = p / half, i = p - hd * half;
+      const int c0 = hd * D + i;               // row of the first element, within the block
+      const int slot = (row0 + hd * D) / D;
+      if (slot >= slots) continue;
+      const int t = tok0 + tl;
+      float4 a0 = gather(tl, c0), a1 = gather(tl, c0 + half);
+      const int f0 = row0 + c0;
+      if (args.bias) {
+        add4(a0, ld_bf16x4(args.bias + f0));
+        add4(a1, ld_bf16x4(args.bias + f0 + half));
+      }
+      const float x0[4] = {rbf(a0.x), rbf(a0.y), rbf(a0.z), rbf(a0.w)};
+      const float x1[4] = {rbf(a1.x), rbf(a1.y), rbf(a1.z), rbf(a1.w)};
+      __nv_bfloat16* dst;
+      if (slot < args.H)
+        dst = args.q_out + ((int64_t)t * args.H + slot) * D;
+      else if (slot < args.H + args.KVH)
+        dst = args.k_cache + (((int64_t)t * args.KVH + (slot - args.H)) * args.smax + args.pos) * D;
+      else
+        dst = args.v_cache + (((int64_t)t * args.KVH + (slot - args.H - args.KVH)) * args.smax + args.pos) * D;
+      float o0[4], o1[4];
+      if (slot >= args.H + args.KVH || !args.cos_t) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          o0[jj] = x0[jj];
+          o1[jj] = x1[jj];
+        }
+      } else {
+        const float* cr = args.cos_t + (int64_t)args.pos * D;
+        const float* sr = args.sin_t + (int64_t)args.pos * D;
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          o0[jj] = __fadd_rn(__fmul_rn(x0[jj], cr[i + jj]), __fmul_rn(-x1[jj], sr[i + jj]));
+          o1[jj] = __fadd_rn(__fmul_rn(x1[jj], cr[i + jj + half]), __fmul_rn(x0[jj], sr[i + jj + half]));
+        }
+      }
+      st_bf16x4(dst + i, o0[0], o0[1], o0[2], o0[3]);
+      st_bf16x4(dst + i + half, o1[0], o1[1], o1[2], o1[3]);
+    }
+  }
+}
+
+// Launch with clusters of `cx` CTAs along x (and programmatic dependent launch when enabled).
+template <typename... KArgs, typename... Args2>
+cudaError_t launch_clusters(void (*kernel)(KArgs...), unsigned grid, unsigned cx, unsigned block, size_t smem,
+                            cudaStream_t s, Args2... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cx;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  prefer_max_smem(reinterpret_cast<const void*>(kernel));
+  launch_counter().fetch_add(1, std::memory_order_relaxed);
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// XB_DECODE_CLUSTER=0 in the environment keeps the older decode entry points
+// on the split-K workspace path (partials in global memory + a finishing kernel).
+bool decode_cluster_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("XB_DECODE_CLUSTER");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+// Cluster size for a decode linear of `blocks` 128-row weight blocks and
+// `kblocks` 64-wide K blocks: about two CTAs per SM, at most 8 (portable
+// cluster size), every CTA with at least one K block.
+void decode_split(int blocks, int kblocks, int* splits, int* kps) {
+  int sms = 148;
+  sm_count(&sms);
+  int s = (2 * sms) / blocks;
+  if (s > kDecMaxCluster) s = kDecMaxCluster;
+  if (s > kblocks) s = kblocks;
+  if (s < 1) s = 1;
+  *kps = (kblocks + s - 1) / s;
+  *splits = (kblocks + *kps - 1) / *kps;
+}
+
+bool al8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Shapes and pointers the decode kernel takes (false: the older entry points
+// use the split-K workspace path instead).
+bool decode_fits(const void* X, const void* W, int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw) {
+  return M >= 1 && M <= kDecBN && N >= 1 && N % 4 == 0 && K >= 1 && ldx >= K && ldw >= K &&
+         N <= (int64_t)kDecBM * 65535 && X && W && tma_ok(X, ldx, 2) && tma_ok(W, ldw, 2);
+}
+
+// A pending norm of X: the statistics of its rows (as the residual form of
+// this kernel writes them) and the norm's parameters.
+struct DecInput {
+  const void* x;
+  int64_t m, ldx;
+  const float* stats;  // null: X is used as is
+  const void* nw;
+  const void* nb;
+  float eps;
+  int kind;
+};
+
+template <int FIN>
+int launch_decode(const DecInput& in, const void* W, int64_t N, int64_t K, int64_t ldw, DecArgs args,
+                  cudaStream_t s, const char* what, char* err, size_t errlen) {
+  DecMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  int rc = make_map(&maps.w, W, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, N, ldw, kDecBK, kDecBM, err, errlen);
+  if (rc) return rc;
+  rc = make_map(&maps.x, in.x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, in.m, in.ldx, kDecBK, kDecBN, err, errlen);
+  if (rc) return rc;
+  const int blocks = (int)((N + kDecBM - 1) / kDecBM);
+  args.m = (int)in.m;
+  args.n = (int)N;
+  args.k = (int)K;
+  args.kblocks = (int)((K + kDecBK - 1) / kDecBK);
+  args.xstats = reinterpret_cast<const float2*>(in.stats);
+  args.xnw = static_cast<const __nv_bfloat16*>(in.nw);
+  args.xnb = static_cast<const __nv_bfloat16*>(in.nb);
+  args.xeps = in.eps;
+  args.xkind = in.kind;
+  decode_split(blocks, args.kblocks, &args.splits, &args.kps);
+  int sms = 148;
+  sm_count(&sms);
+  // one CTA per SM with a deep ring when the grid is small, two with a short one
+  const bool deep = blocks * args.splits <= sms;
+  const bool xn = in.stats != nullptr;
+  void (*kernel)(DecMaps, DecArgs) =
+      xn ? (deep ? decode_linear_kernel<FIN, 7, true> : decode_linear_kernel<FIN, 3, true>)
+         : (deep ? decode_linear_kernel<FIN, 7, false> : decode_linear_kernel<FIN, 3, false>);
+  const int smem = (deep ? 7 : 3) * kDecStage + kDecRecvBytes + 1024;
+  static bool attr_set[2][2] = {{false, false}, {false, false}};
+  if (!attr_set[xn][deep]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) {
+      set_err(err, errlen, "%s: kernel setup: %s", what, cudaGetErrorString(e));
+      return XB_ERR_CUDA;
+    }
+    attr_set[xn][deep] = true;
+  }
+  cudaError_t e = launch_clusters(kernel, (unsigned)(blocks * args.splits), (unsigned)args.splits, 192, smem, s, maps,
+                                  args);
+  if (e != cudaSuccess) {
+    set_err(err, errlen, "%s: %s", what, cudaGetErrorString(e));
+    return XB_ERR_CUDA;
+  }
+  return check_launch(what, err, errlen);
+}
+
+// Validation shared by the xb_decode_* entry points: X (and its pending norm)
+// and W.  Returns XB_OK or an error code with the message set.
+int decode_check(const DecInput& in, const void* W, int64_t N, int64_t K, int64_t ldw, const char* what, char* err,
+                 size_t errlen) {
+  if (!in.x || !W) {
+    set_err(err, errlen, "%s: null pointer", what);
+    return XB_ERR_INVALID;
+  }
+  if (in.m < 1 || in.m > kDecBN || N < 1 || K < 1 || in.ldx < K || ldw < K) {
+    set_err(err, errlen, "%s: needs 1 <= M <= %d tokens, N, K >= 1 and pitches >= K", what, kDecBN);
+    return XB_ERR_INVALID;
+  }
+  if (N % 4 || N > (int64_t)kDecBM * 65535 || !tma_ok(in.x, in.ldx, 2) || !tma_ok(W, ldw, 2)) {
+    set_err(err, errlen, "%s: N %% 4 == 0 and 16-byte aligned X / W rows needed", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  if (in.stats) {
+    if (in.kind != 0 && in.kind != 1) {
+      set_err(err, errlen, "%s: x_norm_kind must be 0 (RMSNorm) or 1 (LayerNorm)", what);
+      return XB_ERR_INVALID;
+    }
+    if (!in.nw || K % 8 || !al16(in.nw) || (in.nb && !al16(in.nb)) || !al8(in.stats)) {
+      set_err(err, errlen, "%s: a pending norm needs K %% 8 == 0, 16-byte aligned norm vectors and statistics",
+              what);
+      return XB_ERR_UNSUPPORTED;
+    }
+  }
+  return XB_OK;
+}
+
+}  // namespace gemm
+}  // namespace xb
+
 extern "C" int xb_linear_small_plan(int64_t M, int64_t N, int64_t K, int has_residual, int* splits,
                                     size_t* workspace_bytes, char* err, size_t errlen) {
   if (M < 0 || N <= 0 || K <= 0 || !splits || !workspace_bytes) {
@@ -1627,6 +2258,19 @@ extern "C" int xb_linear_small_bf16(const void* X, const void* W, const void* bi
   if (!tma_ok(X, ldx, 2) || !tma_ok(W, ldw, 2)) {
     set_err(err, errlen, "%s: X/W must be 16-byte aligned with row pitches a multiple of 16 bytes", what);
     return XB_ERR_UNSUPPORTED;
+  }
+  if (out_dtype == XB_DT_BF16 && decode_cluster_enabled() && decode_fits(X, W, M, N, K, ldx, ldw) && al8(Y) &&
+      ldy % 4 == 0 && (!bias || al8(bias)) && (!residual || (al8(residual) && ldr % 4 == 0))) {
+    DecArgs a;
+    memset(&a, 0, sizeof(a));
+    a.bias = static_cast<const __nv_bfloat16*>(bias);
+    a.y = static_cast<__nv_bfloat16*>(Y);
+    a.ldy = ldy;
+    a.residual = static_cast<const __nv_bfloat16*>(residual);
+    a.ldr = ldr;
+    const DecInput in{X, M, ldx, nullptr, nullptr, nullptr, 0.0f, 0};
+    if (residual) return launch_decode<kFinResidual>(in, W, N, K, ldw, a, s, what, err, errlen);
+    return launch_decode<kFinStore>(in, W, N, K, ldw, a, s, what, err, errlen);
   }
   if (splits <= 0) splits = small_m_splits(N, K);
   const int kblocks = (int)((K + 63) / 64);
@@ -1775,6 +2419,24 @@ extern "C" int xb_linear_small_rope_kv_bf16(const void* X, const void* W, const 
     return XB_ERR_INVALID;
   }
   const int64_t N = (n_head + 2 * n_kv_head) * head_dim;
+  if (decode_cluster_enabled() && decode_fits(X, W, batch, N, K, ldx, ldw) && head_dim % 8 == 0 &&
+      kDecBM % head_dim == 0 && al8(q_out) && al8(k_cache) && al8(v_cache) && (!bias || al8(bias))) {
+    DecArgs a;
+    memset(&a, 0, sizeof(a));
+    a.bias = static_cast<const __nv_bfloat16*>(bias);
+    a.cos_t = cos_t;
+    a.sin_t = sin_t;
+    a.q_out = static_cast<__nv_bfloat16*>(q_out);
+    a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+    a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+    a.H = (int)n_head;
+    a.KVH = (int)n_kv_head;
+    a.D = (int)head_dim;
+    a.smax = (int)max_seq;
+    a.pos = (int)pos_offset;
+    const DecInput in{X, batch, ldx, nullptr, nullptr, nullptr, 0.0f, 0};
+    return launch_decode<kFinRopeKv>(in, W, N, K, ldw, a, s, what, err, errlen);
+  }
   int splits = 1;
   int rc = small_partials(X, W, batch, N, K, ldx, ldw, workspace, workspace_bytes, s, what, &splits, err, errlen);
   if (rc) return rc;
@@ -1814,10 +2476,25 @@ extern "C" int xb_linear_small_residual_norm_bf16(const void* X, const void* W, 
       set_err(err, errlen, "%s: bf16 vectors must be 8-byte aligned", what);
       return XB_ERR_UNSUPPORTED;
     }
+  typedef __nv_bfloat16 bf;
+  if (decode_cluster_enabled() && decode_fits(X, W, M, N, K, ldx, ldw)) {
+    // the residual linear in one launch, then the row norm of its output
+    DecArgs a;
+    memset(&a, 0, sizeof(a));
+    a.bias = static_cast<const bf*>(bias);
+    a.y = static_cast<bf*>(Y);
+    a.ldy = ldy;
+    a.residual = static_cast<const bf*>(residual);
+    a.ldr = ldr;
+    const DecInput in{X, M, ldx, nullptr, nullptr, nullptr, 0.0f, 0};
+    int rc = launch_decode<kFinResidual>(in, W, N, K, ldw, a, s, what, err, errlen);
+    if (rc) return rc;
+    return norm_kind == 0 ? xb_rms_norm(Y, norm_w, Yn, M, N, ldy, ldn, eps, XB_DT_BF16, stream, err, errlen)
+                          : xb_layernorm(Y, norm_w, norm_b, Yn, M, N, ldy, ldn, eps, XB_DT_BF16, stream, err, errlen);
+  }
   int splits = 1;
   int rc = small_partials(X, W, M, N, K, ldx, ldw, workspace, workspace_bytes, s, what, &splits, err, errlen);
   if (rc) return rc;
-  typedef __nv_bfloat16 bf;
   if (norm_kind == 0)
     launch_k(reduce_residual_norm_kernel<0>, (unsigned)M, 256, 0, s, (const float*)workspace, splits, (int)M, (int)N,
              static_cast<const bf*>(bias), static_cast<const bf*>(residual), ldr, static_cast<bf*>(Y), ldy,
@@ -1877,6 +2554,16 @@ extern "C" int xb_linear_gelu_bf16(const void* X, const void* W, const void* bia
     set_err(err, errlen, "%s: few-token form needs N %% 4 == 0 and aligned bias / output", what);
     return XB_ERR_UNSUPPORTED;
   }
+  if (decode_cluster_enabled() && decode_fits(X, W, M, N, K, ldx, ldw) && (!bias || al8(bias))) {
+    DecArgs a;
+    memset(&a, 0, sizeof(a));
+    a.bias = static_cast<const __nv_bfloat16*>(bias);
+    a.y = static_cast<__nv_bfloat16*>(Y);
+    a.ldy = ldy;
+    a.act = 1;
+    const DecInput in{X, M, ldx, nullptr, nullptr, nullptr, 0.0f, 0};
+    return launch_decode<kFinStore>(in, W, N, K, ldw, a, s, what, err, errlen);
+  }
   rc = small_partials(X, W, M, N, K, ldx, ldw, workspace, workspace_bytes, s, what, &splits, err, errlen);
   if (rc) return rc;
   const dim3 g4((unsigned)((N / 4 + 255) / 256), (unsigned)M);
@@ -1890,8 +2577,8 @@ extern "C" int xb_linear_swiglu_bf16(const void* X, const void* W, void* Y, int6
                                      void* stream, char* err, size_t errlen) {
   const char* what = "xb_linear_swiglu_bf16";
   cudaStream_t s = (cudaStream_t)stream;
-  if (n_out <= 0 || n_out % 128) {
-    set_err(err, errlen, "%s: n_out must be a positive multiple of 128 (interleaved 128-row blocks)", what);
+  if (n_out <= 0 || n_out % 64) {
+    set_err(err, errlen, "%s: n_out must be a positive multiple of 64 (interleaved 64-row blocks)", what);
     return XB_ERR_UNSUPPORTED;
   }
   const int64_t N = 2 * n_out;
@@ -1908,7 +2595,16 @@ extern "C" int xb_linear_swiglu_bf16(const void* X, const void* W, void* Y, int6
                                                                     errlen);
     return launch<kBf16, true, kOutSwiglu>(op, Y, nullptr, M, N, K, ldy, s, what, err, errlen);
   }
-  // few tokens: swap-AB split-K partials, then the interleaved SwiGLU finisher
+  // few tokens: one cluster split-K launch with the SwiGLU finisher
+  if (decode_cluster_enabled() && decode_fits(X, W, M, N, K, ldx, ldw) && al8(Y) && ldy % 4 == 0) {
+    DecArgs a;
+    memset(&a, 0, sizeof(a));
+    a.y = static_cast<__nv_bfloat16*>(Y);
+    a.ldy = ldy;
+    const DecInput in{X, M, ldx, nullptr, nullptr, nullptr, 0.0f, 0};
+    return launch_decode<kFinSwiglu>(in, W, N, K, ldw, a, s, what, err, errlen);
+  }
+  // otherwise swap-AB split-K partials, then the interleaved SwiGLU finisher
   int splits = small_m_splits(N, K);
   const size_t need = (size_t)splits * (size_t)M * (size_t)N * sizeof(float);
   if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15) ||
@@ -1929,6 +2625,118 @@ extern "C" int xb_linear_swiglu_bf16(const void* X, const void* W, void* Y, int6
            static_cast<__nv_bfloat16*>(Y), ldy);
   return check_launch(what, err, errlen);
 }
+
+// ---- decode-step linears with a pending input norm (one launch each) --------
+
+#define XB_DECODE_INPUT                                                                         \
+  const DecInput in{X, M, ldx, x_stats, x_norm_w, x_norm_b, x_eps, x_norm_kind};               \
+  {                                                                                             \
+    const int rc_ = decode_check(in, W, N, K, ldw, what, err, errlen);                          \
+    if (rc_) return rc_;                                                                        \
+  }
+
+extern "C" int xb_decode_linear_bf16(const void* X, int64_t M, int64_t ldx, const float* x_stats,
+                                     const void* x_norm_w, const void* x_norm_b, float x_eps, int x_norm_kind,
+                                     const void* W, const void* bias, void* Y, int64_t N, int64_t K, int64_t ldw,
+                                     int64_t ldy, int act, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_decode_linear_bf16";
+  XB_DECODE_INPUT
+  if (!Y || ldy < N || ldy % 4 || !al8(Y) || (bias && !al8(bias)) || (act != 0 && act != 1)) {
+    set_err(err, errlen, "%s: bad output / bias (8-byte aligned, pitch %% 4 == 0) or act", what);
+    return XB_ERR_INVALID;
+  }
+  DecArgs a;
+  memset(&a, 0, sizeof(a));
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.y = static_cast<__nv_bfloat16*>(Y);
+  a.ldy = ldy;
+  a.act = act;
+  return launch_decode<kFinStore>(in, W, N, K, ldw, a, (cudaStream_t)stream, what, err, errlen);
+}
+
+extern "C" int xb_decode_linear_rope_kv_bf16(const void* X, int64_t M, int64_t ldx, const float* x_stats,
+                                             const void* x_norm_w, const void* x_norm_b, float x_eps,
+                                             int x_norm_kind, const void* W, const void* bias, const float* cos_t,
+                                             const float* sin_t, void* q_out, void* k_cache, void* v_cache,
+                                             int64_t n_head, int64_t n_kv_head, int64_t head_dim, int64_t max_seq,
+                                             int64_t pos_offset, int64_t K, int64_t ldw, void* stream, char* err,
+                                             size_t errlen) {
+  const char* what = "xb_decode_linear_rope_kv_bf16";
+  if (n_head <= 0 || n_kv_head <= 0 || n_head % n_kv_head || head_dim <= 0 || head_dim % 8 ||
+      kDecBM % head_dim || pos_offset < 0 || pos_offset >= max_seq) {
+    set_err(err, errlen, "%s: bad head layout (head_dim %% 8 == 0 dividing 128) or position", what);
+    return XB_ERR_INVALID;
+  }
+  const int64_t N = (n_head + 2 * n_kv_head) * head_dim;
+  XB_DECODE_INPUT
+  if (!q_out || !k_cache || !v_cache || (!cos_t) != (!sin_t) || !al8(q_out) || !al8(k_cache) || !al8(v_cache) ||
+      (bias && !al8(bias))) {
+    set_err(err, errlen, "%s: null or unaligned (8-byte) output / bias", what);
+    return XB_ERR_INVALID;
+  }
+  DecArgs a;
+  memset(&a, 0, sizeof(a));
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.cos_t = cos_t;
+  a.sin_t = sin_t;
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  a.H = (int)n_head;
+  a.KVH = (int)n_kv_head;
+  a.D = (int)head_dim;
+  a.smax = (int)max_seq;
+  a.pos = (int)pos_offset;
+  return launch_decode<kFinRopeKv>(in, W, N, K, ldw, a, (cudaStream_t)stream, what, err, errlen);
+}
+
+extern "C" int xb_decode_linear_swiglu_bf16(const void* X, int64_t M, int64_t ldx, const float* x_stats,
+                                            const void* x_norm_w, const void* x_norm_b, float x_eps,
+                                            int x_norm_kind, const void* W, void* Y, int64_t n_out, int64_t K,
+                                            int64_t ldw, int64_t ldy, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_decode_linear_swiglu_bf16";
+  if (n_out <= 0 || n_out % 64) {
+    set_err(err, errlen, "%s: n_out must be a positive multiple of 64 (interleaved 64-row blocks)", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  const int64_t N = 2 * n_out;
+  XB_DECODE_INPUT
+  if (!Y || ldy < n_out || ldy % 4 || !al8(Y)) {
+    set_err(err, errlen, "%s: bad output (8-byte aligned, pitch %% 4 == 0)", what);
+    return XB_ERR_INVALID;
+  }
+  DecArgs a;
+  memset(&a, 0, sizeof(a));
+  a.y = static_cast<__nv_bfloat16*>(Y);
+  a.ldy = ldy;
+  return launch_decode<kFinSwiglu>(in, W, N, K, ldw, a, (cudaStream_t)stream, what, err, errlen);
+}
+
+extern "C" int xb_decode_linear_residual_bf16(const void* X, int64_t M, int64_t ldx, const float* x_stats,
+                                              const void* x_norm_w, const void* x_norm_b, float x_eps,
+                                              int x_norm_kind, const void* W, const void* bias,
+                                              const void* residual, void* Y, float* stats_out, int stats_kind,
+                                              int64_t N, int64_t K, int64_t ldw, int64_t ldr, int64_t ldy,
+                                              void* stream, char* err, size_t errlen) {
+  const char* what = "xb_decode_linear_residual_bf16";
+  XB_DECODE_INPUT
+  if (!Y || !residual || ldy < N || ldr < N || ldy % 4 || ldr % 4 || !al8(Y) || !al8(residual) ||
+      (bias && !al8(bias)) || (stats_out && (!al8(stats_out) || (stats_kind != 0 && stats_kind != 1)))) {
+    set_err(err, errlen, "%s: bad output / residual / bias (8-byte aligned, pitches %% 4 == 0) or statistics", what);
+    return XB_ERR_INVALID;
+  }
+  DecArgs a;
+  memset(&a, 0, sizeof(a));
+  a.bias = static_cast<const __nv_bfloat16*>(bias);
+  a.y = static_cast<__nv_bfloat16*>(Y);
+  a.ldy = ldy;
+  a.residual = static_cast<const __nv_bfloat16*>(residual);
+  a.ldr = ldr;
+  a.stats = reinterpret_cast<float2*>(stats_out);
+  a.stats_kind = stats_kind;
+  return launch_decode<kFinResidual>(in, W, N, K, ldw, a, (cudaStream_t)stream, what, err, errlen);
+}
+#undef XB_DECODE_INPUT
 
 extern "C" int xb_matmul_sharded(const void* A, const void* B_shard, void* const* C_ranks, void* const* signal_ranks,
                                  int world, int rank, int64_t M, int64_t N_shard, int64_t K, int64_t lda, int64_t ldb,

@@ -171,41 +171,41 @@ class GPT2Model:
         x = ops.embedding_pos(self.wte, self.wpe, ids, pos).reshape(M, D)
         q_buf = torch.empty((B, H, S, HD), dtype=torch.bfloat16, device=self.device)
         attn = torch.empty((M, D), dtype=torch.bfloat16, device=self.device)
-        # decode step: each linear is finished by one kernel that also does
-        # what follows it (head split + KV write; residual add + the next norm)
+        # decode step: each linear is one launch that also does what follows it
+        # (head split + KV write; residual add + the row statistics of the next
+        # layernorm, which the next linear applies as it loads its input)
         decode = S == 1 and M <= ops.SMALL_M
         if decode:
-            xn = ops.layernorm(x, self.layers[0]["ln1_w"], self.layers[0]["ln1_b"], c.ln_eps)
+            xin, xnorm = ops.layernorm(x, self.layers[0]["ln1_w"], self.layers[0]["ln1_b"], c.ln_eps), None
         for i, L in enumerate(self.layers):
             if decode:
-                ops.linear_rope_kv(xn, L["qkv_w"], L["qkv_b"], None, None, q_buf, cache.k[i], cache.v[i], H, H, HD,
-                                   pos)
+                ops.decode_linear_rope_kv(xin, L["qkv_w"], L["qkv_b"], None, None, q_buf, cache.k[i], cache.v[i],
+                                          H, H, HD, pos, xnorm=xnorm)
             else:
                 xn = ops.layernorm(x, L["ln1_w"], L["ln1_b"], c.ln_eps)
                 qkv = ops.linear(xn, L["qkv_w"], L["qkv_b"])
                 ops.rope_kv(qkv, None, None, q_buf, cache.k[i], cache.v[i], B, S, H, H, HD, pos)
             ops.attention(q_buf, cache.k[i], cache.v[i], attn, B, S, H, H, HD, pos, self.scale)
             if decode:
-                x, xn = ops.linear_residual_norm(attn, L["proj_w"], L["proj_b"], x, L["ln2_w"], L["ln2_b"],
-                                                 eps=c.ln_eps, kind="layer")
-                h = ops.linear(xn, L["fc_w"], L["fc_b"], act="gelu_tanh")  # c_fc + tanh GELU, one launch
-                nw, nb = ((self.layers[i + 1]["ln1_w"], self.layers[i + 1]["ln1_b"]) if i + 1 < len(self.layers)
-                          else (self.lnf_w, self.lnf_b))
-                x, xn = ops.linear_residual_norm(h, L["mproj_w"], L["mproj_b"], x, nw, nb, eps=c.ln_eps,
-                                                 kind="layer")
+                y, st = ops.decode_linear_residual(attn, L["proj_w"], L["proj_b"], x, stats_kind="layer")
+                h = ops.decode_linear(y, L["fc_w"], L["fc_b"], act="gelu_tanh",
+                                      xnorm=(st, L["ln2_w"], L["ln2_b"], c.ln_eps, "layer"))  # ln_2 + c_fc + GELU
+                last = i + 1 == len(self.layers)
+                x, st = ops.decode_linear_residual(h, L["mproj_w"], L["mproj_b"], y,
+                                                   stats_kind=None if last else "layer")
+                if not last:
+                    nxt = self.layers[i + 1]
+                    xin, xnorm = x, (st, nxt["ln1_w"], nxt["ln1_b"], c.ln_eps, "layer")
                 continue
             x = ops.linear(attn, L["proj_w"], L["proj_b"], residual=x)  # c_proj + residual add
             xn = ops.layernorm(x, L["ln2_w"], L["ln2_b"], c.ln_eps)
             h = ops.linear(xn, L["fc_w"], L["fc_b"], act="gelu_tanh")  # c_fc + tanh GELU, one launch
             x = ops.linear(h, L["mproj_w"], L["mproj_b"], residual=x)  # mlp c_proj + residual add
         cache.length = pos + S
-        if decode:
-            x = xn  # the last projection already applied the final layernorm
-        else:
-            if last_only:
-                x = x.reshape(B, S, D)[:, -1, :]  # strided rows: the norm kernel gathers them
-            x = ops.layernorm(x, self.lnf_w, self.lnf_b, c.ln_eps,
-                              out=torch.empty((x.shape[0], D), dtype=torch.bfloat16, device=self.device))
+        if last_only and not decode:
+            x = x.reshape(B, S, D)[:, -1, :]  # strided rows: the norm kernel gathers them
+        x = ops.layernorm(x, self.lnf_w, self.lnf_b, c.ln_eps,
+                          out=torch.empty((x.shape[0], D), dtype=torch.bfloat16, device=self.device))
         logits = ops.linear(x, self.wte, out_dtype=torch.float32)
         return logits if last_only else logits.reshape(B, S, c.vocab_size)
 

@@ -489,12 +489,12 @@ def linear(x, weight, bias=None, out=None, out_dtype=torch.bfloat16, residual=No
     return y.reshape(*x.shape[:-1], N) if out is None else out
 
 
-def interleave_gate_up(w_gate, w_up, block: int = 128) -> torch.Tensor:
-    """[2 n_out, K] weight interleaving 128-row blocks of gate and up rows, the
+def interleave_gate_up(w_gate, w_up, block: int = 64) -> torch.Tensor:
+    """[2 n_out, K] weight interleaving 64-row blocks of gate and up rows, the
     layout of the fused SwiGLU linear (xb_linear_swiglu_bf16)."""
     n_out, K = w_gate.shape
     if w_up.shape != w_gate.shape or n_out % block:
-        raise ValueError("gate and up weights must share a shape with n_out a multiple of 128")
+        raise ValueError(f"gate and up weights must share a shape with n_out a multiple of {block}")
     g = w_gate.reshape(n_out // block, block, K)
     u = w_up.reshape(n_out // block, block, K)
     return torch.stack([g, u], 1).reshape(2 * n_out, K).contiguous()
@@ -582,6 +582,96 @@ def linear_residual_norm(x, weight, bias, residual, norm_w, norm_b=None, eps=1e-
               0 if kind == "rms" else 1, M, N, K, _mat(x2, "x"), _mat(weight, "weight"), _mat(r2, "residual"), N, N,
               ws.data_ptr(), ws.numel() * 4, _stream())
     return y, yn
+
+
+# --------------------------------------------------------------------------- decode-step linears
+#
+# One launch each (the cluster split-K kernel, M <= SMALL_M tokens).  `xnorm`
+# = (stats, norm_w, norm_b, eps, kind) marks x as carrying a pending norm:
+# the statistics come from the decode_linear_residual call that produced x
+# with the same kind, and the kernel normalises x as it loads it.
+
+_NORM_KIND = {"rms": 0, "layer": 1}
+
+
+def decode_stats(n_features: int, device) -> torch.Tensor:
+    """Buffer for the per-block row statistics of decode_linear_residual:
+    ceil(N / 128) blocks x 64 tokens x 2 floats."""
+    return torch.empty(((n_features + 127) // 128) * 128, dtype=torch.float32, device=device)
+
+
+def _xin(x, xnorm):
+    if x.dtype != torch.bfloat16:
+        raise TypeError("decode linears take bf16 x")
+    M = x.shape[0]
+    if not 0 < M <= SMALL_M:
+        raise ValueError(f"decode linears take 1..{SMALL_M} tokens, got {M}")
+    if xnorm is None:
+        return (x.data_ptr(), M, _mat(x, "x"), None, None, None, 0.0, 0)
+    stats, w, b, eps, kind = xnorm
+    _cuda(stats, w, b)
+    if stats.dtype != torch.float32 or stats.numel() < ((x.shape[1] + 127) // 128) * 128:
+        raise ValueError("xnorm statistics must be a float32 decode_stats buffer for x's width")
+    return (x.data_ptr(), M, _mat(x, "x"), stats.data_ptr(), w.data_ptr(), b.data_ptr() if b is not None else None,
+            float(eps), _NORM_KIND[kind])
+
+
+def decode_linear(x, weight, bias=None, act=None, xnorm=None, out=None):
+    """y = bf16(norm?(x) @ weight^T + bias) [GELU] for a decode step, one launch
+    (examples/qwen2_5/kernels/matmul.py:172-296; GPT-2 c_fc + gelu)."""
+    _cuda(x, weight, bias, out)
+    N, K = weight.shape
+    if x.shape[-1] != K:
+        raise ValueError("shape mismatch")
+    if act not in (None, "gelu_tanh"):
+        raise ValueError("act must be None or 'gelu_tanh'")
+    y = out if out is not None else torch.empty((x.shape[0], N), dtype=torch.bfloat16, device=x.device)
+    _lib.call("xb_decode_linear_bf16", *_xin(x, xnorm), weight.data_ptr(),
+              bias.data_ptr() if bias is not None else None, y.data_ptr(), N, K, _mat(weight, "weight"),
+              _mat(y, "y"), 1 if act else 0, _stream())
+    return y
+
+
+def decode_linear_rope_kv(x, w_qkv, b_qkv, cos_t, sin_t, q_out, k_cache, v_cache, n_head, n_kv_head, head_dim,
+                          pos_offset, xnorm=None):
+    """Decode QKV projection + RoPE (none when the tables are None) + KV-cache
+    write at pos_offset, one launch (examples/qwen2_5/model.py:836-867)."""
+    _cuda(x, w_qkv, b_qkv, cos_t, sin_t, q_out, k_cache, v_cache)
+    if cos_t is not None and cos_t.shape[0] <= pos_offset:
+        raise ValueError("RoPE tables are shorter than the position")
+    K = w_qkv.shape[1]
+    _lib.call("xb_decode_linear_rope_kv_bf16", *_xin(x, xnorm), w_qkv.data_ptr(),
+              b_qkv.data_ptr() if b_qkv is not None else None,
+              cos_t.data_ptr() if cos_t is not None else None, sin_t.data_ptr() if sin_t is not None else None,
+              q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), n_head, n_kv_head, head_dim,
+              k_cache.shape[2], pos_offset, K, _mat(w_qkv, "w"), _stream())
+
+
+def decode_linear_swiglu(x, w_gate_up, xnorm=None):
+    """silu(norm?(x) Wg^T) * (norm?(x) Wu^T) with W from interleave_gate_up, one launch."""
+    _cuda(x, w_gate_up)
+    N, K = w_gate_up.shape
+    y = torch.empty((x.shape[0], N // 2), dtype=torch.bfloat16, device=x.device)
+    _lib.call("xb_decode_linear_swiglu_bf16", *_xin(x, xnorm), w_gate_up.data_ptr(), y.data_ptr(), N // 2, K,
+              _mat(w_gate_up, "w"), N // 2, _stream())
+    return y
+
+
+def decode_linear_residual(x, weight, bias, residual, stats_kind=None, xnorm=None):
+    """y = residual + bf16(norm?(x) @ weight^T + bias), one launch; with
+    stats_kind ("rms" / "layer") also the row statistics of y that the next
+    decode linear's xnorm takes.  Returns (y, stats or None)."""
+    _cuda(x, weight, bias, residual)
+    N, K = weight.shape
+    M = x.shape[0]
+    r2 = residual.reshape(M, N)
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    st = decode_stats(N, x.device) if stats_kind is not None else None
+    _lib.call("xb_decode_linear_residual_bf16", *_xin(x, xnorm), weight.data_ptr(),
+              bias.data_ptr() if bias is not None else None, r2.data_ptr(), y.data_ptr(),
+              st.data_ptr() if st is not None else None, _NORM_KIND[stats_kind] if stats_kind else 0, N, K,
+              _mat(weight, "weight"), _mat(r2, "residual"), N, _stream())
+    return y, st
 
 
 def device_status() -> int:

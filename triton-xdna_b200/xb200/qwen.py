@@ -127,8 +127,8 @@ class Qwen2Model:
                 "qkv_b": torch.cat([t(f"{p}.self_attn.q_proj.bias"), t(f"{p}.self_attn.k_proj.bias"),
                                     t(f"{p}.self_attn.v_proj.bias")], 0).contiguous(),
                 "o_w": t(f"{p}.self_attn.o_proj.weight"),
-                # gate and up rows interleaved in 128-row blocks: one GEMM (or one
-                # split-K GEMM at decode) whose epilogue applies silu(gate) * up
+                # gate and up rows interleaved in 64-row blocks: one GEMM (or one
+                # cluster split-K launch at decode) that applies silu(gate) * up
                 "gate_up_w": ops.interleave_gate_up(t(f"{p}.mlp.gate_proj.weight"),
                                                     t(f"{p}.mlp.up_proj.weight")),
                 "down_w": t(f"{p}.mlp.down_proj.weight"),
@@ -160,38 +160,38 @@ class Qwen2Model:
         x = ops.embedding(self.embed, ids.reshape(-1)).reshape(M, D)
         q_buf = torch.empty((B, H, S, HD), dtype=torch.bfloat16, device=self.device)
         attn = torch.empty((M, H * HD), dtype=torch.bfloat16, device=self.device)
-        # decode step: each linear is finished by one kernel that also does
-        # what follows it (RoPE + KV write; residual add + the next norm)
+        # decode step: each linear is one launch that also does what follows it
+        # (RoPE + KV write; residual add + the row statistics of the next norm,
+        # which the next linear applies as it loads its input)
         decode = S == 1 and M <= ops.SMALL_M
         if decode:
-            xn = ops.rms_norm(x, self.layers[0]["input_ln"], c.rms_eps)
+            xin, xnorm = ops.rms_norm(x, self.layers[0]["input_ln"], c.rms_eps), None
         for i, L in enumerate(self.layers):
             if decode:
-                ops.linear_rope_kv(xn, L["qkv_w"], L["qkv_b"], self.cos, self.sin, q_buf, cache.k[i], cache.v[i],
-                                   H, KVH, HD, pos)
+                ops.decode_linear_rope_kv(xin, L["qkv_w"], L["qkv_b"], self.cos, self.sin, q_buf, cache.k[i],
+                                          cache.v[i], H, KVH, HD, pos, xnorm=xnorm)
             else:
                 xn = ops.rms_norm(x, L["input_ln"], c.rms_eps)
                 qkv = ops.linear(xn, L["qkv_w"], L["qkv_b"])
                 ops.rope_kv(qkv, self.cos, self.sin, q_buf, cache.k[i], cache.v[i], B, S, H, KVH, HD, pos)
             ops.attention(q_buf, cache.k[i], cache.v[i], attn, B, S, H, KVH, HD, pos, self.scale)
             if decode:
-                x, xn = ops.linear_residual_norm(attn, L["o_w"], None, x, L["post_ln"], eps=c.rms_eps)
-                h = ops.linear_swiglu(xn, L["gate_up_w"], interleaved=True)  # gate + up + silu*up
-                nxt = self.layers[i + 1]["input_ln"] if i + 1 < len(self.layers) else self.norm_w
-                x, xn = ops.linear_residual_norm(h, L["down_w"], None, x, nxt, eps=c.rms_eps)
+                y, st = ops.decode_linear_residual(attn, L["o_w"], None, x, stats_kind="rms")
+                h = ops.decode_linear_swiglu(y, L["gate_up_w"], xnorm=(st, L["post_ln"], None, c.rms_eps, "rms"))
+                last = i + 1 == len(self.layers)
+                x, st = ops.decode_linear_residual(h, L["down_w"], None, y, stats_kind=None if last else "rms")
+                if not last:
+                    xin, xnorm = x, (st, self.layers[i + 1]["input_ln"], None, c.rms_eps, "rms")
                 continue
             x = ops.linear(attn, L["o_w"], residual=x)  # o_proj + residual add (in the epilogue)
             xn = ops.rms_norm(x, L["post_ln"], c.rms_eps)
             h = ops.linear_swiglu(xn, L["gate_up_w"], interleaved=True)  # gate + up + silu*up, one GEMM
             x = ops.linear(h, L["down_w"], residual=x)  # down_proj + residual add (in the epilogue)
         cache.length = pos + S
-        if decode:
-            x = xn  # the last down projection already applied the final norm
-        else:
-            if last_only:
-                x = x.reshape(B, S, D)[:, -1, :]  # strided rows: the norm kernel gathers them
-            x = ops.rms_norm(x, self.norm_w, c.rms_eps, out=torch.empty((x.shape[0], D), dtype=torch.bfloat16,
-                                                                         device=self.device))
+        if last_only and not decode:
+            x = x.reshape(B, S, D)[:, -1, :]  # strided rows: the norm kernel gathers them
+        x = ops.rms_norm(x, self.norm_w, c.rms_eps, out=torch.empty((x.shape[0], D), dtype=torch.bfloat16,
+                                                                     device=self.device))
         logits = ops.linear(x, self.embed, out_dtype=torch.float32)
         return logits if last_only else logits.reshape(B, S, c.vocab_size)
 
