@@ -1749,6 +1749,34 @@ __global__ void __launch_bounds__(192, 1) decode_linear_kernel(const __grid_cons
   // their residual rows are requested while the MMAs run.
   constexpr int kPre = 4;
   float4 rpre[kPre];
+  // Finisher constants (bias, RoPE table rows), requested before the
+  // programmatic-launch wait: every finisher unit of a thread uses the same rows.
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 pb0 = z4, pb1 = z4, pc0 = z4, pc1 = z4, ps0 = z4, ps1 = z4;
+  if (warp >= 2) {
+    const int e = threadIdx.x - 64;
+    if constexpr (FIN == kFinStore || FIN == kFinResidual) {
+      const int n = row0 + (FIN == kFinStore ? (e & 31) : lane) * 4;
+      if (args.bias && n < args.n) pb0 = ld_bf16x4(args.bias + n);
+    } else if constexpr (FIN == kFinRopeKv) {
+      const int half = args.D >> 1, p = (e & 15) * 4, hd = p / half, i = p - hd * half;
+      const int f0 = row0 + hd * args.D + i, slot = (row0 + hd * args.D) / args.D;
+      if (slot < args.H + 2 * args.KVH) {
+        if (args.bias) {
+          pb0 = ld_bf16x4(args.bias + f0);
+          pb1 = ld_bf16x4(args.bias + f0 + half);
+        }
+        if (args.cos_t && slot < args.H + args.KVH) {
+          const float* cr = args.cos_t + (int64_t)args.pos * args.D;
+          const float* sr = args.sin_t + (int64_t)args.pos * args.D;
+          pc0 = __ldg(reinterpret_cast<const float4*>(cr + i));
+          pc1 = __ldg(reinterpret_cast<const float4*>(cr + i + half));
+          ps0 = __ldg(reinterpret_cast<const float4*>(sr + i));
+          ps1 = __ldg(reinterpret_cast<const float4*>(sr + i + half));
+        }
+      }
+    }
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -1933,13 +1961,20 @@ __global__ void __launch_bounds__(192, 1) decode_linear_kernel(const __grid_cons
     tc_fence_before();
     epi_bar();
     if (got) {
-      // token t's row of the partial -> slot `rank` of its owner's receive buffer
+      // token t's row of the partial -> slot `rank` of its owner's receive
+      // buffer; thread e sends rows (e & 31) * 4 .. + 3 of tokens e / 32 + 4 k
+      // (t grows by 4 < pt per step, so the owner advances at most by one)
       const uint32_t recv0 = smem_u32(recv);
-      for (int c = e; c < args.m * (kDecBM / 4); c += 128) {
-        const int t = c >> 5, owner = t / pt;
-        const uint32_t dst = mapa_u32(recv0, (uint32_t)owner) +
-                             (uint32_t)(((rank * pt + (t - owner * pt)) * kDecBM + (c & 31) * 4) * 4);
-        st_dsmem_f4(dst, reinterpret_cast<const float4*>(red)[c]);
+      int t = e >> 5, owner = t / pt, tl = t - owner * pt;
+      uint32_t peer = mapa_u32(recv0, (uint32_t)owner);
+      for (; t < args.m; t += 4, tl += 4) {
+        if (tl >= pt) {
+          tl -= pt;
+          ++owner;
+          peer = mapa_u32(recv0, (uint32_t)owner);
+        }
+        st_dsmem_f4(peer + (uint32_t)(((rank * pt + tl) * kDecBM + (e & 31) * 4) * 4),
+                    reinterpret_cast<const float4*>(red)[t * (kDecBM / 4) + (e & 31)]);
       }
     }
   }
@@ -1953,123 +1988,198 @@ __global__ void __launch_bounds__(192, 1) decode_linear_kernel(const __grid_cons
 
   // ------------------------------------------------------------ finisher (own shared memory only)
   const int e = threadIdx.x - 64;  // 0 .. 127
-  // sum of the S partials of (owned token tl, rows c..c+3), rank order
-  auto gather = [&](int tl, int c) {
-    const float4* p = reinterpret_cast<const float4*>(recv + tl * kDecBM + c);
-    constexpr int kSlot = kDecBM / 4;  // float4 per token row
-    float4 acc = p[0];
-    for (int jr = 1; jr < S; ++jr) add4(acc, p[jr * pt * kSlot]);
-    return acc;
+  constexpr int kSlot = kDecBM / 4;  // float4 per token row of the receive buffer
+  const float4* rv = reinterpret_cast<const float4*>(recv);
+  // acc[u] = sum of the S partials of (owned token tl[u], rows c[u]..c[u]+3), rank
+  // order; the loads of up to four units are issued together
+  auto gather4 = [&](const int (&tl)[4], const int (&c)[4], const bool (&ok)[4], float4 (&acc)[4]) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) acc[u] = ok[u] ? rv[tl[u] * kSlot + (c[u] >> 2)] : z4;
+#pragma unroll
+    for (int jr = 1; jr < kDecMaxCluster; ++jr) {
+      if (jr < S) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = ok[u] ? rv[(jr * pt + tl[u]) * kSlot + (c[u] >> 2)] : z4;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (ok[u]) add4(acc[u], v[u]);
+      }
+    }
   };
   if constexpr (FIN == kFinStore) {
-    for (int u = e; u < ntok * 32; u += 128) {
-      const int tl = u >> 5, c = (u & 31) * 4;
-      const int n = row0 + c;
-      if (n >= args.n) continue;
-      float4 acc = gather(tl, c);
-      if (args.bias) add4(acc, ld_bf16x4(args.bias + n));
-      float4 o = make_float4(rbf(acc.x), rbf(acc.y), rbf(acc.z), rbf(acc.w));
-      if (args.act == 1)
-        o = make_float4(gelu_tanh_bf16path(o.x), gelu_tanh_bf16path(o.y), gelu_tanh_bf16path(o.z),
-                        gelu_tanh_bf16path(o.w));
-      st_bf16x4(args.y + (tok0 + tl) * args.ldy + n, o.x, o.y, o.z, o.w);
+    // units (owned token, 4-row group): thread e takes units e + 128 k, all with rows c
+    const int c = (e & 31) * 4, n = row0 + c;
+    for (int u0 = e; u0 < ntok * 32; u0 += 4 * 128) {
+      int tl[4], cc[4];
+      bool ok[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        tl[u] = (u0 + 128 * u) >> 5;
+        cc[u] = c;
+        ok[u] = u0 + 128 * u < ntok * 32 && n < args.n;
+      }
+      float4 acc[4];
+      gather4(tl, cc, ok, acc);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (!ok[u]) continue;
+        add4(acc[u], pb0);
+        float4 o = make_float4(rbf(acc[u].x), rbf(acc[u].y), rbf(acc[u].z), rbf(acc[u].w));
+        if (args.act == 1)
+          o = make_float4(gelu_tanh_bf16path(o.x), gelu_tanh_bf16path(o.y), gelu_tanh_bf16path(o.z),
+                          gelu_tanh_bf16path(o.w));
+        st_bf16x4(args.y + (tok0 + tl[u]) * args.ldy + n, o.x, o.y, o.z, o.w);
+      }
     }
   } else if constexpr (FIN == kFinResidual) {
-    // warp per owned token, lane = 4-row group: the block statistics of a
-    // token row reduce within the warp
+    // warp per owned token (tokens w, w + 4, ... of the epilogue warp w), lane =
+    // 4-row group: the block statistics of a token row reduce within the warp;
+    // four tokens at a time, their loads and reductions interleaved
     const int c = lane * 4, n = row0 + c;
     const bool valid = n < args.n;
     const float cnt = (float)min(kDecBM, args.n - row0);
-    const float4 bias4 = valid && args.bias ? ld_bf16x4(args.bias + n) : make_float4(0.f, 0.f, 0.f, 0.f);
-    auto token = [&](int u, float4 r) {
-      const int tl = (warp - 2) + 4 * u, t = tok0 + tl;
-      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (valid) {
-        float4 acc = gather(tl, c);
-        add4(acc, bias4);
-        o = make_float4(rbf(r.x + rbf(acc.x)), rbf(r.y + rbf(acc.y)), rbf(r.z + rbf(acc.z)), rbf(r.w + rbf(acc.w)));
-        st_bf16x4(args.y + t * args.ldy + n, o.x, o.y, o.z, o.w);
+    for (int ub = 0; (warp - 2) + 16 * ub < ntok; ++ub) {
+      int tl[4], cc[4];
+      bool ok[4], live[4];
+      float4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        tl[u] = (warp - 2) + 4 * (4 * ub + u);
+        cc[u] = c;
+        live[u] = tl[u] < ntok;  // warp-uniform
+        ok[u] = live[u] && valid;
+        r[u] = ub == 0 ? rpre[u]
+                       : (ok[u] ? ld_bf16x4(args.residual + (tok0 + tl[u]) * args.ldr + n) : z4);
+      }
+      float4 acc[4], o[4];
+      gather4(tl, cc, ok, acc);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        o[u] = z4;
+        if (!ok[u]) continue;
+        add4(acc[u], pb0);
+        o[u] = make_float4(rbf(r[u].x + rbf(acc[u].x)), rbf(r[u].y + rbf(acc[u].y)), rbf(r[u].z + rbf(acc[u].z)),
+                           rbf(r[u].w + rbf(acc[u].w)));
+        st_bf16x4(args.y + (tok0 + tl[u]) * args.ldy + n, o[u].x, o[u].y, o[u].z, o[u].w);
       }
       if (args.stats) {
-        float2 st;
-        if (args.stats_kind == 0) {
-          st = make_float2(warp_sum((o.x * o.x + o.y * o.y) + (o.z * o.z + o.w * o.w)), 0.0f);
-        } else {
-          // shifted sums (shift: the block's first value) give the block mean and
-          // the sum of squared deviations in one pass of two interleaved reductions
-          const float sh = __shfl_sync(0xffffffffu, o.x, 0);
-          const float a = o.x - sh, b = o.y - sh, cc = o.z - sh, d = o.w - sh;
-          float s1 = valid ? (a + b) + (cc + d) : 0.0f;
-          float s2 = valid ? (a * a + b * b) + (cc * cc + d * d) : 0.0f;
+        float s1[4], s2[4], sh[4];
 #pragma unroll
-          for (int o_ = 16; o_ > 0; o_ >>= 1) {
-            s1 += __shfl_xor_sync(0xffffffffu, s1, o_);
-            s2 += __shfl_xor_sync(0xffffffffu, s2, o_);
+        for (int u = 0; u < 4; ++u) {
+          const float4 v = o[u];
+          if (args.stats_kind == 0) {
+            sh[u] = 0.0f;
+            s1[u] = (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+            s2[u] = 0.0f;
+          } else {
+            // shifted sums (shift: the block's first value) give the block mean
+            // and the sum of squared deviations in one pass
+            sh[u] = __shfl_sync(0xffffffffu, v.x, 0);
+            const float a = v.x - sh[u], b = v.y - sh[u], cz = v.z - sh[u], d = v.w - sh[u];
+            s1[u] = valid ? (a + b) + (cz + d) : 0.0f;
+            s2[u] = valid ? (a * a + b * b) + (cz * cz + d * d) : 0.0f;
           }
-          st = make_float2(sh + s1 / cnt, fmaxf(s2 - s1 * s1 / cnt, 0.0f));
         }
-        if (lane == 0) args.stats[blk * kDecBN + t] = st;
-      }
-    };
 #pragma unroll
-    for (int u = 0; u < kPre; ++u)  // residual rows already in registers
-      if ((warp - 2) + 4 * u < ntok) token(u, rpre[u]);
-    for (int u = kPre; (warp - 2) + 4 * u < ntok; ++u)
-      token(u, valid ? ld_bf16x4(args.residual + (tok0 + (warp - 2) + 4 * u) * args.ldr + n)
-                     : make_float4(0.f, 0.f, 0.f, 0.f));
+        for (int o_ = 16; o_ > 0; o_ >>= 1) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            s1[u] += __shfl_xor_sync(0xffffffffu, s1[u], o_);
+            s2[u] += __shfl_xor_sync(0xffffffffu, s2[u], o_);
+          }
+        }
+        if (lane == 0) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (!live[u]) continue;
+            args.stats[blk * kDecBN + tok0 + tl[u]] =
+                args.stats_kind == 0 ? make_float2(s1[u], 0.0f)
+                                     : make_float2(sh[u] + s1[u] / cnt, fmaxf(s2[u] - s1[u] * s1[u] / cnt, 0.0f));
+          }
+        }
+      }
+    }
   } else if constexpr (FIN == kFinSwiglu) {
-    // rows [0, 64) gate and [64, 128) up of features blk*64 .. blk*64+63
-    for (int u = e; u < ntok * 16; u += 128) {
-      const int tl = u >> 4, c = (u & 15) * 4;
-      const float4 g = gather(tl, c), up = gather(tl, 64 + c);
+    // rows [0, 64) gate and [64, 128) up of features blk*64 .. blk*64+63;
+    // units (owned token, 4 features): thread e takes units e + 128 k
+    const int c = (e & 15) * 4;
+    for (int u0 = e; u0 < ntok * 16; u0 += 2 * 128) {
+      int tl[4], cc[4];
+      bool ok[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {  // (gate, up) of two units
+        tl[u] = (u0 + 128 * (u >> 1)) >> 4;
+        cc[u] = c + 64 * (u & 1);
+        ok[u] = u0 + 128 * (u >> 1) < ntok * 16;
+      }
+      float4 acc[4];
+      gather4(tl, cc, ok, acc);
       auto sw = [](float gg, float uu) { return __fmul_rn(silu_bf16path(rbf(gg)), rbf(uu)); };
-      st_bf16x4(args.y + (tok0 + tl) * args.ldy + blk * 64 + c, sw(g.x, up.x), sw(g.y, up.y), sw(g.z, up.z),
-                sw(g.w, up.w));
+#pragma unroll
+      for (int u = 0; u < 4; u += 2) {
+        if (!ok[u]) continue;
+        const float4 g = acc[u], up = acc[u + 1];
+        st_bf16x4(args.y + (tok0 + tl[u]) * args.ldy + blk * 64 + c, sw(g.x, up.x), sw(g.y, up.y), sw(g.z, up.z),
+                  sw(g.w, up.w));
+      }
     }
   } else {
-    // kFinRopeKv: units (owned token, 4 consecutive rotation pairs of one head)
+    // kFinRopeKv: units (owned token, 4 consecutive rotation pairs of one head);
+    // thread e takes units e + 128 k, all with the same pairs
     const int D = args.D, half = D >> 1;
-    const int slots = args.H + 2 * args.KVH;
-    for (int u = e; u < ntok * 16; u += 128) {
-      const int tl = u >> 4, p = (u & 15) * 4;  // first pair index within the block
-      const int hd = p / half, i = p - hd * half;
-      const int c0 = hd * D + i;               // row of the first element, within the block
-      const int slot = (row0 + hd * D) / D;
-      if (slot >= slots) continue;
-      const int t = tok0 + tl;
-      float4 a0 = gather(tl, c0), a1 = gather(tl, c0 + half);
-      const int f0 = row0 + c0;
-      if (args.bias) {
-        add4(a0, ld_bf16x4(args.bias + f0));
-        add4(a1, ld_bf16x4(args.bias + f0 + half));
-      }
-      const float x0[4] = {rbf(a0.x), rbf(a0.y), rbf(a0.z), rbf(a0.w)};
-      const float x1[4] = {rbf(a1.x), rbf(a1.y), rbf(a1.z), rbf(a1.w)};
-      __nv_bfloat16* dst;
-      if (slot < args.H)
-        dst = args.q_out + ((int64_t)t * args.H + slot) * D;
-      else if (slot < args.H + args.KVH)
-        dst = args.k_cache + (((int64_t)t * args.KVH + (slot - args.H)) * args.smax + args.pos) * D;
-      else
-        dst = args.v_cache + (((int64_t)t * args.KVH + (slot - args.H - args.KVH)) * args.smax + args.pos) * D;
-      float o0[4], o1[4];
-      if (slot >= args.H + args.KVH || !args.cos_t) {
+    const int p = (e & 15) * 4;  // first pair index within the block
+    const int hd = p / half, i = p - hd * half;
+    const int c0 = hd * D + i;   // row of the first element, within the block
+    const int slot = (row0 + hd * D) / D;
+    if (slot < args.H + 2 * args.KVH) {
+      for (int u0 = e; u0 < ntok * 16; u0 += 2 * 128) {
+        int tl[4], cc[4];
+        bool ok[4];
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          o0[jj] = x0[jj];
-          o1[jj] = x1[jj];
+        for (int u = 0; u < 4; ++u) {  // (first, second half) of two units
+          tl[u] = (u0 + 128 * (u >> 1)) >> 4;
+          cc[u] = c0 + half * (u & 1);
+          ok[u] = u0 + 128 * (u >> 1) < ntok * 16;
         }
-      } else {
-        const float* cr = args.cos_t + (int64_t)args.pos * D;
-        const float* sr = args.sin_t + (int64_t)args.pos * D;
+        float4 acc[4];
+        gather4(tl, cc, ok, acc);
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          o0[jj] = __fadd_rn(__fmul_rn(x0[jj], cr[i + jj]), __fmul_rn(-x1[jj], sr[i + jj]));
-          o1[jj] = __fadd_rn(__fmul_rn(x1[jj], cr[i + jj + half]), __fmul_rn(x0[jj], sr[i + jj + half]));
+        for (int u = 0; u < 4; u += 2) {
+          if (!ok[u]) continue;
+          const int t = tok0 + tl[u];
+          float4 a0 = acc[u], a1 = acc[u + 1];
+          add4(a0, pb0);
+          add4(a1, pb1);
+          const float x0[4] = {rbf(a0.x), rbf(a0.y), rbf(a0.z), rbf(a0.w)};
+          const float x1[4] = {rbf(a1.x), rbf(a1.y), rbf(a1.z), rbf(a1.w)};
+          __nv_bfloat16* dst;
+          if (slot < args.H)
+            dst = args.q_out + ((int64_t)t * args.H + slot) * D;
+          else if (slot < args.H + args.KVH)
+            dst = args.k_cache + (((int64_t)t * args.KVH + (slot - args.H)) * args.smax + args.pos) * D;
+          else
+            dst = args.v_cache + (((int64_t)t * args.KVH + (slot - args.H - args.KVH)) * args.smax + args.pos) * D;
+          float o0[4], o1[4];
+          if (slot >= args.H + args.KVH || !args.cos_t) {
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              o0[jj] = x0[jj];
+              o1[jj] = x1[jj];
+            }
+          } else {
+            const float c0v[4] = {pc0.x, pc0.y, pc0.z, pc0.w}, c1v[4] = {pc1.x, pc1.y, pc1.z, pc1.w};
+            const float s0v[4] = {ps0.x, ps0.y, ps0.z, ps0.w}, s1v[4] = {ps1.x, ps1.y, ps1.z, ps1.w};
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              o0[jj] = __fadd_rn(__fmul_rn(x0[jj], c0v[jj]), __fmul_rn(-x1[jj], s0v[jj]));
+              o1[jj] = __fadd_rn(__fmul_rn(x1[jj], c1v[jj]), __fmul_rn(x0[jj], s1v[jj]));
+            }
+          }
+          st_bf16x4(dst + i, o0[0], o0[1], o0[2], o0[3]);
+          st_bf16x4(dst + i + half, o1[0], o1[1], o1[2], o1[3]);
         }
       }
-      st_bf16x4(dst + i, o0[0], o0[1], o0[2], o0[3]);
-      st_bf16x4(dst + i + half, o1[0], o1[1], o1[2], o1[3]);
     }
   }
 }
@@ -2420,7 +2530,8 @@ extern "C" int xb_linear_small_rope_kv_bf16(const void* X, const void* W, const 
   }
   const int64_t N = (n_head + 2 * n_kv_head) * head_dim;
   if (decode_cluster_enabled() && decode_fits(X, W, batch, N, K, ldx, ldw) && head_dim % 8 == 0 &&
-      kDecBM % head_dim == 0 && al8(q_out) && al8(k_cache) && al8(v_cache) && (!bias || al8(bias))) {
+      kDecBM % head_dim == 0 && al8(q_out) && al8(k_cache) && al8(v_cache) && (!bias || al8(bias)) &&
+      (!cos_t || (al16(cos_t) && al16(sin_t)))) {
     DecArgs a;
     memset(&a, 0, sizeof(a));
     a.bias = static_cast<const __nv_bfloat16*>(bias);
@@ -2670,8 +2781,8 @@ extern "C" int xb_decode_linear_rope_kv_bf16(const void* X, int64_t M, int64_t l
   const int64_t N = (n_head + 2 * n_kv_head) * head_dim;
   XB_DECODE_INPUT
   if (!q_out || !k_cache || !v_cache || (!cos_t) != (!sin_t) || !al8(q_out) || !al8(k_cache) || !al8(v_cache) ||
-      (bias && !al8(bias))) {
-    set_err(err, errlen, "%s: null or unaligned (8-byte) output / bias", what);
+      (bias && !al8(bias)) || (cos_t && (!al16(cos_t) || !al16(sin_t)))) {
+    set_err(err, errlen, "%s: null or unaligned output / bias (8-byte) or RoPE tables (16-byte)", what);
     return XB_ERR_INVALID;
   }
   DecArgs a;
