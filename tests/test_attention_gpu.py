@@ -54,6 +54,23 @@ def test_attention_matches_oracle(B, S, H, KVH, pos, smax):
     assert float((got - exact).abs().max()) < 3e-2
 
 
+@pytest.mark.parametrize("B,H,KVH,pos,smax", [(48, 14, 2, 575, 640), (48, 14, 2, 0, 8), (32, 12, 4, 40, 64),
+                                              (100, 8, 1, 255, 300), (24, 20, 4, 1000, 1024), (96, 5, 1, 33, 40)])
+def test_decode_attention_one_cta_per_kv_head(B, H, KVH, pos, smax):
+    """Many sequences (>= 96 (batch, KV head) pairs) take the kernel in which
+    one CTA walks a KV head's whole context; ragged and single-key contexts."""
+    q = _rand((B, H, 1, 64), 11, 2.0)
+    kc = _rand((B, KVH, smax, 64), 12, 2.0)
+    vc = _rand((B, KVH, smax, 64), 13)
+    got = _run(q, kc, vc, B, 1, H, KVH, pos).float()
+    T = pos + 1
+    ref = OQ.attention(q, kc[:, :, :T], vc[:, :, :T], pos, 1 / 8).float()
+    torch.testing.assert_close(got, ref, atol=2e-2, rtol=2e-2)
+    exact = _exact(q, kc[:, :, :T], vc[:, :, :T], pos, 1 / 8).float()
+    assert float((got - exact).abs().max()) < 3e-2
+    assert torch.equal(got, _run(q, kc, vc, B, 1, H, KVH, pos).float())  # fixed merge order
+
+
 def test_prefill_rows_equal_decode_steps():
     B, H, KVH, smax = 2, 14, 2, 256
     q = _rand((B, H, 80, 64), 4, 2.0)

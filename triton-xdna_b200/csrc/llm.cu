@@ -575,6 +575,199 @@ __global__ void __launch_bounds__(128) attn_decode_split_kernel(const bf16* __re
   }
 }
 
+// Many sequences, one token each: a CTA per (batch, KV head).  The NREP query
+// heads sharing the KV head are the rows of one mma.sync tile; warp w walks
+// the 32-key tiles w, w + 8, w + 16, ... of the context with an online
+// softmax (P = exp2(S - running max) rounded to bf16 for P V, fp32 l and O
+// rescaled when the max grows), double-buffering its own tiles in shared
+// memory with cp.async (rows past the context zero-filled), and the eight
+// warps' (O, m, l) merge in shared memory in warp order at the end.  The
+// context is read once and no cross-CTA merge or second kernel is needed;
+// with >= 96 (batch, KV head) pairs the CTAs alone cover the SMs.
+constexpr int kHeadWarps = 8;
+constexpr int kTileK = 32;
+constexpr int kHeadTileElems = kTileK * kPad;  // one K or V tile (bf16 elements)
+constexpr int kHeadSmem = kHeadWarps * 2 * 2 * kHeadTileElems * (int)sizeof(bf16);
+
+template <int NREP>
+__global__ void __launch_bounds__(kHeadWarps * 32, 1) attn_decode_head_kernel(
+    const bf16* __restrict__ q, const bf16* __restrict__ kc, const bf16* __restrict__ vc, int H, int KVH, int smax,
+    int total, float scale_log2, bf16* __restrict__ out) {
+  static_assert(NREP >= 1 && NREP <= 16, "query heads per KV head fill one 16-row tile");
+  static_assert(kHeadWarps * 16 * kHD * (int)sizeof(float) <= kHeadSmem, "merge buffer fits the tiles");
+  extern __shared__ __align__(16) uint8_t head_smem[];
+  __shared__ float wm[kHeadWarps][16], wl[kHeadWarps][16];
+  const int b = blockIdx.x, kvh = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  bf16* wb = reinterpret_cast<bf16*>(head_smem) + warp * (2 * 2 * kHeadTileElems);
+  const bf16* kp = kc + (int64_t)(b * KVH + kvh) * smax * kHD;
+  const bf16* vp = vc + (int64_t)(b * KVH + kvh) * smax * kHD;
+  const bf16* qp = q + ((int64_t)b * H + kvh * NREP) * kHD;
+  const int ntiles = (total + kTileK - 1) / kTileK;
+  pdl_wait();
+  pdl_trigger();
+  // tile `tile` -> buffer `buf` of this warp: 32 keys x 128 bytes of K and of V,
+  // 16 bytes per lane per copy, rows past the context zero-filled
+  auto issue = [&](int tile, int buf) {
+    bf16* sk = wb + (buf * 2) * kHeadTileElems;
+    bf16* sv = sk + kHeadTileElems;
+#pragma unroll
+    for (int j = 0; j < kTileK * kHD / 8 / 32; ++j) {
+      const int i = lane + 32 * j;
+      const int r = i >> 3, c8 = (i & 7) * 8;
+      const int key = tile * kTileK + r;
+      const int src = key < total ? key : 0;
+      const uint32_t bytes = key < total ? 16u : 0u;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                       (uint32_t)__cvta_generic_to_shared(sk + r * kPad + c8)),
+                   "l"(kp + (int64_t)src * kHD + c8), "r"(bytes)
+                   : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                       (uint32_t)__cvta_generic_to_shared(sv + r * kPad + c8)),
+                   "l"(vp + (int64_t)src * kHD + c8), "r"(bytes)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (warp < ntiles) issue(warp, 0);
+  if (warp + kHeadWarps < ntiles) issue(warp + kHeadWarps, 1);
+  uint32_t qa[4][4];
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    const int c = kk * 16 + 2 * t;
+    qa[kk][0] = g < NREP ? *reinterpret_cast<const uint32_t*>(qp + g * kHD + c) : 0u;
+    qa[kk][1] = g + 8 < NREP ? *reinterpret_cast<const uint32_t*>(qp + (g + 8) * kHD + c) : 0u;
+    qa[kk][2] = g < NREP ? *reinterpret_cast<const uint32_t*>(qp + g * kHD + c + 8) : 0u;
+    qa[kk][3] = g + 8 < NREP ? *reinterpret_cast<const uint32_t*>(qp + (g + 8) * kHD + c + 8) : 0u;
+  }
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  for (int it = 0, tile = warp; tile < ntiles; ++it, tile += kHeadWarps) {
+    const int buf = it & 1;
+    if (tile + kHeadWarps < ntiles) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncwarp();
+    const bf16* sk = wb + (buf * 2) * kHeadTileElems;
+    const bf16* sv = sk + kHeadTileElems;
+    float s[4][4];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(sk + (nt * 8 + g) * kPad + kk * 16 + 2 * t);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(sk + (nt * 8 + g) * kPad + kk * 16 + 8 + 2 * t);
+        mma_bf16_16816(s[nt], qa[kk], b0, b1);
+      }
+    }
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const bool ok = tile * kTileK + nt * 8 + 2 * t + (e & 1) < total;
+        s[nt][e] = ok ? s[nt][e] * scale_log2 : -INFINITY;
+        if (e < 2) mx0 = fmaxf(mx0, s[nt][e]);
+        else mx1 = fmaxf(mx1, s[nt][e]);
+      }
+#pragma unroll
+    for (int o_ = 1; o_ <= 2; o_ <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o_));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o_));
+    }
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float base0 = mn0 == -INFINITY ? 0.0f : mn0, base1 = mn1 == -INFINITY ? 0.0f : mn1;
+    const float al0 = ex2_approx(m0 - base0), al1 = ex2_approx(m1 - base1);
+    m0 = mn0;
+    m1 = mn1;
+    float rs0 = 0.0f, rs1 = 0.0f;
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      s[nt][0] = ex2_approx(s[nt][0] - base0);
+      s[nt][1] = ex2_approx(s[nt][1] - base0);
+      s[nt][2] = ex2_approx(s[nt][2] - base1);
+      s[nt][3] = ex2_approx(s[nt][3] - base1);
+      rs0 += s[nt][0] + s[nt][1];
+      rs1 += s[nt][2] + s[nt][3];
+    }
+    l0 = l0 * al0 + rs0;
+    l1 = l1 * al1 + rs1;
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) {
+      o[dt][0] *= al0;
+      o[dt][1] *= al0;
+      o[dt][2] *= al1;
+      o[dt][3] *= al1;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {  // keys kk*16 .. kk*16+15 of the tile
+      uint32_t pa[4];
+      pa[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      pa[1] = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+      pa[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pa[3] = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dt = 0; dt < 8; dt += 2) {
+        const int mi = lane >> 3, r = lane & 7;
+        uint32_t vb[4];
+        ldmatrix_x4_trans(vb, sv + (kk * 16 + (mi & 1) * 8 + r) * kPad + dt * 8 + (mi >> 1) * 8);
+        mma_bf16_16816(o[dt], pa, vb[0], vb[1]);
+        mma_bf16_16816(o[dt + 1], pa, vb[2], vb[3]);
+      }
+    }
+    __syncwarp();  // the buffer is free for the tile two steps ahead
+    if (tile + 2 * kHeadWarps < ntiles) issue(tile + 2 * kHeadWarps, buf);
+  }
+#pragma unroll
+  for (int o_ = 1; o_ <= 2; o_ <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, o_);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, o_);
+  }
+  if (t == 0) {
+    wm[warp][g] = m0;
+    wm[warp][g + 8] = m1;
+    wl[warp][g] = l0;
+    wl[warp][g + 8] = l1;
+  }
+  __syncthreads();  // every warp is past its tiles: the buffers hold the merge
+  float* red = reinterpret_cast<float*>(head_smem);  // [warp][16][64] fp32
+  {
+    float M0 = -INFINITY, M1 = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kHeadWarps; ++w) {
+      M0 = fmaxf(M0, wm[w][g]);
+      M1 = fmaxf(M1, wm[w][g + 8]);
+    }
+    const float f0 = m0 == -INFINITY ? 0.0f : ex2_approx(m0 - M0);
+    const float f1 = m1 == -INFINITY ? 0.0f : ex2_approx(m1 - M1);
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) {
+      const int d = dt * 8 + 2 * t;
+      red[(warp * 16 + g) * kHD + d] = o[dt][0] * f0;
+      red[(warp * 16 + g) * kHD + d + 1] = o[dt][1] * f0;
+      red[(warp * 16 + g + 8) * kHD + d] = o[dt][2] * f1;
+      red[(warp * 16 + g + 8) * kHD + d + 1] = o[dt][3] * f1;
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < NREP * kHD; i += kHeadWarps * 32) {
+    const int r = i / kHD, d = i % kHD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kHeadWarps; ++w) M = fmaxf(M, wm[w][r]);
+    float acc = 0.0f, l = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kHeadWarps; ++w) {
+      acc += red[(w * 16 + r) * kHD + d];
+      l += wm[w][r] == -INFINITY ? 0.0f : wl[w][r] * ex2_approx(wm[w][r] - M);
+    }
+    out[((int64_t)b * H + kvh * NREP + r) * kHD + d] = __float2bfloat16_rn(acc / l);
+  }
+}
+
 // The same partials computed on the CUDA cores, for one or two query heads
 // per KV head (GPT-2's multi-head attention), where a 16-row mma tile would
 // be mostly padding: thread t scores key t of the chunk (K rows staged in
@@ -962,6 +1155,32 @@ extern "C" int xb_rope_kv_bf16(const void* qkv, const float* cos_t, const float*
   return check_launch("xb_rope_kv_bf16", err, errlen);
 }
 
+// Launch attn_decode_head_kernel<R> (its shared-memory limit raised once).
+template <int R>
+static cudaError_t launch_head(dim3 grid, cudaStream_t s, const bf16* q, const bf16* k, const bf16* v, int H, int KVH,
+                               int smax, int total, float scale_log2, bf16* out) {
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_decode_head_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  return launch_k(attn_decode_head_kernel<R>, grid, kHeadWarps * 32, kHeadSmem, s, q, k, v, H, KVH, smax, total,
+                  scale_log2, out);
+}
+
+// XB_HEAD_ATTN=0 in the environment keeps many-sequence decode attention on
+// the chunked kernels (A/B timing).
+static bool head_attn_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("XB_HEAD_ATTN");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 extern "C" int xb_attention_workspace_size(int64_t batch, int64_t seq, int64_t n_head, int64_t n_kv_head,
                                            int64_t pos_offset, size_t* bytes, char* err, size_t errlen) {
   if (!bytes || batch < 0 || seq < 0 || n_head <= 0 || n_kv_head <= 0 || pos_offset < 0) {
@@ -1021,6 +1240,24 @@ extern "C" int xb_attention_bf16(const void* q, const void* k_cache, const void*
     const bf16* vv = static_cast<const bf16*>(v_cache);
     const int Hh = (int)n_head, KV = (int)n_kv_head, SM = (int)max_seq;
     bf16* ob = static_cast<bf16*>(out);
+    // many (batch, KV head) pairs: one CTA each walks the whole context
+    if (n_rep >= 3 && n_rep <= 8 && batch * n_kv_head >= 96 && head_attn_enabled()) {
+      const dim3 hg((unsigned)batch, (unsigned)n_kv_head);
+      cudaError_t ce;
+      switch (n_rep) {
+        case 3: ce = launch_head<3>(hg, s, qq, kk, vv, Hh, KV, SM, total, scale_log2, ob); break;
+        case 4: ce = launch_head<4>(hg, s, qq, kk, vv, Hh, KV, SM, total, scale_log2, ob); break;
+        case 5: ce = launch_head<5>(hg, s, qq, kk, vv, Hh, KV, SM, total, scale_log2, ob); break;
+        case 6: ce = launch_head<6>(hg, s, qq, kk, vv, Hh, KV, SM, total, scale_log2, ob); break;
+        case 7: ce = launch_head<7>(hg, s, qq, kk, vv, Hh, KV, SM, total, scale_log2, ob); break;
+        default: ce = launch_head<8>(hg, s, qq, kk, vv, Hh, KV, SM, total, scale_log2, ob); break;
+      }
+      if (ce != cudaSuccess) {
+        set_err(err, errlen, "%s: %s", what, cudaGetErrorString(ce));
+        return XB_ERR_CUDA;
+      }
+      return check_launch(what, err, errlen);
+    }
     // contexts of up to 8 chunks merge inside a cluster (no combine launch)
     const bool clustered = n_rep >= 3 && nchunks <= 8;
     auto launch_cluster = [&](auto kernel) -> cudaError_t {
