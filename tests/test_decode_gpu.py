@@ -154,3 +154,12 @@ def test_decode_linear_rejects_what_it_cannot_take():
     with pytest.raises(XbError):
         ops.decode_linear(x64[:, :892], w[:, :892], b, xnorm=(st, nw, None, 1e-6, "rms"))  # K % 8 != 0
     _status_ok()
+
+
+def test_reserved_workspace_is_shared_by_device_spellings():
+    """A reservation made for "cuda" is the buffer an operator on cuda:N uses,
+    so decode graphs captured after it never see the scratch buffer move."""
+    ops.reserve_workspace("cuda", 8 << 20)
+    a = ops._workspace(torch.device("cuda", torch.cuda.current_device()), 1 << 20)
+    b = ops._workspace("cuda", 2 << 20)
+    assert a.data_ptr() == b.data_ptr() and a.numel() * 4 >= 8 << 20

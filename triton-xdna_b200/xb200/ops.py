@@ -409,6 +409,9 @@ def _workspace(device, nbytes: int) -> torch.Tensor:
     """A per-device fp32 scratch buffer that only grows (kept alive so its
     address is stable, e.g. across CUDA-graph replays).  One buffer per
     device: operators that use it must not run concurrently on two streams."""
+    device = torch.device(device)
+    if device.index is None:  # "cuda" and "cuda:<current>" name the same buffer
+        device = torch.device(device.type, torch.cuda.current_device())
     ws = _workspaces.get(device)
     if ws is None or ws.numel() * 4 < nbytes:
         ws = torch.empty(max(nbytes // 4, 1 << 20), dtype=torch.float32, device=device)
