@@ -400,6 +400,23 @@ XB_API int xb_linear_small_residual_norm_bf16(
  * The statistics are summed in block order, so every result is bit-
  * repeatable.  Pitches are in elements; outputs and bf16 vectors 8-byte
  * aligned with pitches % 4 == 0; N % 4 == 0. */
+/* The LM head and the greedy next token in one pass (examples/qwen2_5/
+ * model.py:1134-1179 and examples/gpt2/model.py:1144-1206 take the argmax of
+ * the last position's logits): idx[m] = argmax_n (X W^T)[m, n] (int64, first
+ * index of the maximum, NaN largest, as torch.argmax) with X [M, K] and
+ * W [N, K] bf16, fp32 accumulation -- the same values a fp32-output linear
+ * writes, but the logits never leave the chip: each 128-row tile of W keeps
+ * its best row per token ({float, int32} per (tile, token) in `workspace`,
+ * xb_linear_argmax_workspace_size bytes) and a second kernel reduces the
+ * tiles. */
+XB_API int xb_linear_argmax_workspace_size(int64_t M, int64_t N, size_t* bytes,
+                                           char* err, size_t errlen);
+XB_API int xb_linear_argmax_bf16(const void* X, const void* W, int64_t M,
+                                 int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                                 int64_t* idx, void* workspace,
+                                 size_t workspace_bytes, void* stream,
+                                 char* err, size_t errlen);
+
 XB_API int xb_decode_linear_bf16(const void* X, int64_t M, int64_t ldx,
                                  const float* x_stats, const void* x_norm_w,
                                  const void* x_norm_b, float x_eps,

@@ -163,3 +163,28 @@ def test_reserved_workspace_is_shared_by_device_spellings():
     a = ops._workspace(torch.device("cuda", torch.cuda.current_device()), 1 << 20)
     b = ops._workspace("cuda", 2 << 20)
     assert a.data_ptr() == b.data_ptr() and a.numel() * 4 >= 8 << 20
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 151936, 896), (1, 50257, 768), (7, 1000, 64), (33, 128, 200)])
+def test_linear_argmax_equals_argmax_of_logits(M, N, K):
+    x, w, _, _ = _data(M, N, K, N + M)
+    got = ops.linear_argmax(x, w)
+    logits = ops.linear(x, w, out_dtype=torch.float32)
+    assert torch.equal(got, torch.argmax(logits, -1))
+    assert torch.equal(got, ops.argmax(logits))
+    _status_ok()
+
+
+def test_linear_argmax_ties_take_the_first_row():
+    """Equal logits in different 128-row tiles and within one tile: the first
+    index wins, as torch.argmax."""
+    M, N, K = 5, 3000, 128
+    x, w, _, _ = _data(M, N, K, 9)
+    big = (torch.ones(K) * 0.5).to(torch.bfloat16).cuda()
+    x = x.abs()  # every logit of the `big` rows is the same positive maximum
+    for r in (2900, 1700, 1701, 130):
+        w[r] = big
+    got = ops.linear_argmax(x, w)
+    assert torch.equal(got.cpu(), torch.full((M,), 130, dtype=torch.int64))
+    assert torch.equal(got, torch.argmax(ops.linear(x, w, out_dtype=torch.float32), -1))
+    _status_ok()

@@ -116,6 +116,18 @@ __device__ __forceinline__ float gelu_tanh_bf16path(float x) {
   return __fmul_rn(x, rcp_approx(1.0f + ex2_approx(__fmul_rn(2.0f, inner) * -1.4426950408889634f)));
 }
 
+// Is (v2, i2) a better argmax candidate than (v1, i1)?  Larger value wins,
+// then the smaller index; NaN is larger than every number (torch.argmax);
+// an index >= cols is "no candidate".  A total order, so any reduction tree
+// gives the first index of the maximum.
+__device__ __forceinline__ bool argmax_better(float v1, int64_t i1, float v2, int64_t i2, int64_t cols) {
+  if (i2 >= cols) return false;
+  if (i1 >= cols) return true;
+  const bool n1 = v1 != v1, n2 = v2 != v2;
+  if (n1 || n2) return n1 && n2 ? i2 < i1 : n2;
+  return v2 > v1 || (v2 == v1 && i2 < i1);
+}
+
 // ---- programmatic dependent launch ----------------------------------------
 // Every kernel waits for its predecessor on the stream with pdl_wait() before
 // touching global memory, then lets its own successor begin launching

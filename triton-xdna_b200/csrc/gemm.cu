@@ -53,7 +53,10 @@ enum Kind { kBf16 = 0, kInt8 = 1, kInt16Limbs = 2 };
 // the decode kernel's unit, those of 64); the epilogue writes
 // bf16(silu(bf16(g)) * bf16(u)) into C [M, N/2] -- the roundings of two bf16
 // linears followed by the silu*up kernel.
-enum Out { kOutF32 = 0, kOutBf16 = 1, kOutI32 = 2, kOutSwiglu = 3 };
+// kOutArgmax (swap-AB only): no logits; per 128-row tile of W and token the
+// best (value, row) goes to C as {float, int32} [row tiles][tokens], and
+// xb_linear_argmax_bf16 reduces the tiles (the greedy next token).
+enum Out { kOutF32 = 0, kOutBf16 = 1, kOutI32 = 2, kOutSwiglu = 3, kOutArgmax = 4 };
 
 constexpr int tmem_cols_for(int cols) { return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512; }
 
@@ -371,7 +374,13 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       const uint32_t tph = (local / C::ACC_BUFS) & 1;
       const bool got = PAIR ? mbar_wait_cl(&tfull_bar[buf], tph, kWaitLimit, &abort_flag)
                             : mbar_wait(&tfull_bar[buf], tph, kWaitLimit, &abort_flag);
-      if (!got) { fail(); break; }
+      if (!got) {
+        fail();
+        // the argmax epilogue's warps meet at named barriers every tile: after a
+        // timeout they keep stepping through the tiles (garbage, flagged) so
+        // none waits for a warp that left
+        if constexpr (OUT != kOutArgmax) break;
+      }
       tc_fence_after();
       int tm, tn;
       tile_coords<GM>(t / args.splits, args.tiles_m, args.tiles_n, tm, tn);
@@ -426,6 +435,56 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
           tmem_ld_wait();
         }
         const int col0 = tn * C::BN + cc * 32;
+        if constexpr (OUT == kOutArgmax) {
+          static_assert(TRANS && !PAIR && !PEERS && C::BN == 64, "argmax epilogue: swap-AB, 64 tokens per tile");
+          // Warp q transposes its 32 rows x 32 tokens through shared memory so
+          // lane j scans token col0 + j down the rows in order; the four
+          // warps' candidates meet in shared memory after the last chunk.
+          float* stg = reinterpret_cast<float*>(smem + C::STAGES * C::STAGE_BYTES);
+          float* cv = stg + 4 * 32 * 33;                // [warp quarter][64 tokens]
+          int* ci = reinterpret_cast<int*>(cv + 4 * 64);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) stg[(q * 32 + lane) * 33 + j] = __uint_as_float(v[j]);
+          __syncwarp();
+          // rows in increasing order: a later row replaces the best only if
+          // strictly larger, or the first NaN (argmax_better's order)
+          float best = 0.0f;
+          int bi = args.m;  // no candidate
+          const int rmax = min(32, args.m - (row - lane));
+#pragma unroll 8
+          for (int r = 0; r < rmax; ++r) {
+            const float val = stg[(q * 32 + r) * 33 + lane];
+            if (bi == args.m || val > best || (val != val && best == best)) {
+              best = val;
+              bi = row - lane + r;
+            }
+          }
+          cv[q * 64 + cc * 32 + lane] = best;
+          ci[q * 64 + cc * 32 + lane] = bi;
+          __syncwarp();
+          if (cc == C::BN / 32 - 1) {
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the four epilogue warps
+            if (q == 0) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int tk = h * 32 + lane;
+                float b = cv[tk];
+                int i = ci[tk];
+#pragma unroll
+                for (int w = 1; w < 4; ++w)
+                  if (argmax_better(b, i, cv[w * 64 + tk], ci[w * 64 + tk], args.m)) {
+                    b = cv[w * 64 + tk];
+                    i = ci[w * 64 + tk];
+                  }
+                const int token = tn * C::BN + tk;
+                if (token < args.n)
+                  static_cast<uint2*>(args.c)[(int64_t)tm * args.n + token] = make_uint2(__float_as_uint(b), (uint32_t)i);
+              }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // candidates read: free for the next tile
+          }
+          continue;
+        }
         if constexpr (OUT != kOutBf16 && !TRANS && !PEERS) {
           if (args.c_tma) {
             // Coalesced store: each thread writes its row's 128 bytes into a
@@ -1226,9 +1285,10 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   // 4-byte outputs of whole-tile GEMMs leave through the TMA-store epilogue
   // when C meets the TMA alignment rules.
   // Transposed (small-M) outputs too, through [tokens][features] staging tiles.
-  constexpr bool kStaged = !PEERS && OUT != kOutSwiglu && (TRANS || OUT != kOutBf16);
+  constexpr bool kStaged = !PEERS && OUT != kOutSwiglu && OUT != kOutArgmax && (TRANS || OUT != kOutBf16);
   constexpr bool kLines = !TRANS && (PEERS || OUT == kOutBf16);  // whole-line staged stores
-  constexpr int kSmem = Cf::SMEM + ((kStaged || kLines) ? kEpiStageBytes : 0);
+  constexpr int kSmem = Cf::SMEM + ((kStaged || kLines || OUT == kOutArgmax) ? kEpiStageBytes : 0);
+  static_assert(4 * 32 * 33 * 4 + 4 * 64 * 8 <= kEpiStageBytes, "argmax staging fits");
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
   args.c_tma = 0;
   if constexpr (kStaged && !TRANS) {
@@ -2848,6 +2908,88 @@ extern "C" int xb_decode_linear_residual_bf16(const void* X, int64_t M, int64_t 
   return launch_decode<kFinResidual>(in, W, N, K, ldw, a, (cudaStream_t)stream, what, err, errlen);
 }
 #undef XB_DECODE_INPUT
+
+// ---- LM head + greedy next token --------------------------------------------
+
+// idx[m] = argmax_n (X W^T)[m, n] per tile, then over the tiles.
+namespace xb {
+namespace gemm {
+__global__ void __launch_bounds__(256) argmax_tiles_kernel(const uint2* __restrict__ cand, int tiles, int M,
+                                                           int64_t cols, int64_t* __restrict__ idx) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float sv[8];
+  __shared__ int64_t si[8];
+  const int m = blockIdx.x;
+  float best = 0.0f;
+  int64_t bi = cols;
+  for (int t = threadIdx.x; t < tiles; t += 256) {
+    const uint2 c = cand[(int64_t)t * M + m];
+    if (argmax_better(best, bi, __uint_as_float(c.x), (int64_t)(int)c.y, cols)) {
+      best = __uint_as_float(c.x);
+      bi = (int)c.y;
+    }
+  }
+#pragma unroll
+  for (int o_ = 16; o_ > 0; o_ >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o_);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, o_);
+    if (argmax_better(best, bi, ov, oi, cols)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = best;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; ++w)
+      if (argmax_better(best, bi, sv[w], si[w], cols)) {
+        best = sv[w];
+        bi = si[w];
+      }
+    idx[m] = bi;
+  }
+}
+}  // namespace gemm
+}  // namespace xb
+
+extern "C" int xb_linear_argmax_workspace_size(int64_t M, int64_t N, size_t* bytes, char* err, size_t errlen) {
+  if (!bytes || M < 0 || N < 0) {
+    set_err(err, errlen, "xb_linear_argmax_workspace_size: bad arguments");
+    return XB_ERR_INVALID;
+  }
+  *bytes = (size_t)((N + 127) / 128) * (size_t)M * 8u;
+  return XB_OK;
+}
+
+extern "C" int xb_linear_argmax_bf16(const void* X, const void* W, int64_t M, int64_t N, int64_t K, int64_t ldx,
+                                     int64_t ldw, int64_t* idx, void* workspace, size_t workspace_bytes,
+                                     void* stream, char* err, size_t errlen) {
+  const char* what = "xb_linear_argmax_bf16";
+  cudaStream_t s = (cudaStream_t)stream;
+  if (M <= 0 || M > 65535 || N <= 0 || N > ((int64_t)1 << 30) || K <= 0 || ldx < K || ldw < K || !X || !W || !idx) {
+    set_err(err, errlen, "%s: bad shape or null pointer", what);
+    return XB_ERR_INVALID;
+  }
+  if (!tma_ok(X, ldx, 2) || !tma_ok(W, ldw, 2)) {
+    set_err(err, errlen, "%s: X/W must be 16-byte aligned with row pitches a multiple of 16 bytes", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  const int tiles = (int)((N + 127) / 128);
+  const size_t need = (size_t)tiles * (size_t)M * 8u;
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 7)) {
+    set_err(err, errlen, "%s: 8-byte aligned workspace of %zu bytes needed (%zu given)", what, need, workspace_bytes);
+    return XB_ERR_INVALID;
+  }
+  Operands op{{W, nullptr}, {X, nullptr}, ldw, ldx};  // swap-AB: vocabulary rows x tokens
+  int rc = launch<kBf16, true, kOutArgmax, 64, true>(op, workspace, nullptr, N, M, K, M, s, what, err, errlen);
+  if (rc) return rc;
+  launch_k(argmax_tiles_kernel, dim3((unsigned)M), 256, 0, s, (const uint2*)workspace, tiles, (int)M, (int64_t)N, idx);
+  return check_launch(what, err, errlen);
+}
 
 extern "C" int xb_matmul_sharded(const void* A, const void* B_shard, void* const* C_ranks, void* const* signal_ranks,
                                  int world, int rank, int64_t M, int64_t N_shard, int64_t K, int64_t lda, int64_t ldb,

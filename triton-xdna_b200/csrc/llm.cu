@@ -933,15 +933,8 @@ __global__ void __launch_bounds__(kHD) attn_decode_combine_kernel(const float* _
 
 // ----------------------------------------------------------------------------- argmax
 
-// Is (v2, i2) a better argmax candidate than (v1, i1)?  Larger value wins,
-// ties go to the smaller index, NaN counts as the maximum (torch.argmax);
-// an index >= cols marks "no candidate yet".
 __device__ __forceinline__ bool better(float v1, int64_t i1, float v2, int64_t i2, int64_t cols) {
-  if (i2 >= cols) return false;
-  if (i1 >= cols) return true;
-  const bool n1 = v1 != v1, n2 = v2 != v2;
-  if (n1 || n2) return n1 && n2 ? i2 < i1 : n2;
-  return v2 > v1 || (v2 == v1 && i2 < i1);
+  return xb::argmax_better(v1, i1, v2, i2, cols);
 }
 
 // idx[r] = first index of the maximum of logits[r, :].

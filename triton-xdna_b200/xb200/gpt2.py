@@ -156,9 +156,13 @@ class GPT2Model:
         return KVCache(self.cfg, batch, max_seq, self.device)
 
     @torch.no_grad()
-    def forward(self, ids: torch.Tensor, cache: KVCache, last_only: bool = False) -> torch.Tensor:
+    def forward(self, ids: torch.Tensor, cache: KVCache, last_only: bool = False,
+                next_token: torch.Tensor | None = None) -> torch.Tensor | None:
         """ids [B, S] int64 on the device; appends S positions to `cache`.
-        Returns fp32 logits [B, S, vocab], or [B, vocab] of the last position."""
+        Returns fp32 logits [B, S, vocab], or [B, vocab] of the last position;
+        with `next_token` (int64 [B]) it writes the greedy token of the last
+        position there instead (LM head and argmax in one pass, no logits)
+        and returns None."""
         c = self.cfg
         B, S = ids.shape
         if cache.batch != B:
@@ -206,6 +210,11 @@ class GPT2Model:
             x = x.reshape(B, S, D)[:, -1, :]  # strided rows: the norm kernel gathers them
         x = ops.layernorm(x, self.lnf_w, self.lnf_b, c.ln_eps,
                           out=torch.empty((x.shape[0], D), dtype=torch.bfloat16, device=self.device))
+        if next_token is not None:
+            if not last_only:
+                raise ValueError("next_token needs last_only=True")
+            ops.linear_argmax(x, self.wte, out=next_token)
+            return None
         logits = ops.linear(x, self.wte, out_dtype=torch.float32)
         return logits if last_only else logits.reshape(B, S, c.vocab_size)
 
@@ -227,15 +236,13 @@ class GPT2Model:
         cache.length = 0
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
-        logits = self.forward(ids, cache, last_only=True)
-        ops.argmax(logits, out=toks[0])
+        self.forward(ids, cache, last_only=True, next_token=toks[0])
         e1.record()
         if graphs is not None:
             graphs.replay()
         else:
             for step in range(1, max_new_tokens):
-                logits = self.forward(toks[step - 1].view(B, 1), cache, last_only=True)
-                ops.argmax(logits, out=toks[step])
+                self.forward(toks[step - 1].view(B, 1), cache, last_only=True, next_token=toks[step])
         e2.record()
         torch.cuda.synchronize()
         return toks.t(), {"prefill_ms": e0.elapsed_time(e1), "decode_ms": e1.elapsed_time(e2)}

@@ -760,6 +760,31 @@ def attention(q, k_cache, v_cache, out, batch, seq, n_head, n_kv_head, head_dim,
     return out
 
 
+def linear_argmax_workspace_bytes(M: int, N: int) -> int:
+    need = ctypes.c_size_t(0)
+    _lib.call("xb_linear_argmax_workspace_size", M, N, ctypes.byref(need))
+    return need.value
+
+
+def linear_argmax(x, weight, out=None):
+    """argmax_n (x @ weight^T)[m, n] per row (int64, torch.argmax semantics on
+    the fp32 logits) without writing the logits: the LM head and the greedy
+    next token of a decode step in one GEMM plus a small reduction."""
+    _cuda(x, weight, out)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("linear_argmax takes bf16 x and weight")
+    M, K = x.shape
+    N = weight.shape[0]
+    if weight.shape[1] != K:
+        raise ValueError("shape mismatch")
+    if out is None:
+        out = torch.empty(M, dtype=torch.int64, device=x.device)
+    ws = _workspace(x.device, linear_argmax_workspace_bytes(M, N))
+    _lib.call("xb_linear_argmax_bf16", x.data_ptr(), weight.data_ptr(), M, N, K, _mat(x, "x"),
+              _mat(weight, "weight"), out.data_ptr(), ws.data_ptr(), ws.numel() * 4, _stream())
+    return out
+
+
 def argmax(x, out=None):
     """First index of the row maximum of a 2-D fp32 tensor (torch.argmax(-1))."""
     _cuda(x, out)

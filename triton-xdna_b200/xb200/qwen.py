@@ -145,9 +145,13 @@ class Qwen2Model:
         return KVCache(self.cfg, batch, max_seq, self.device)
 
     @torch.no_grad()
-    def forward(self, ids: torch.Tensor, cache: KVCache, last_only: bool = False) -> torch.Tensor:
+    def forward(self, ids: torch.Tensor, cache: KVCache, last_only: bool = False,
+                next_token: torch.Tensor | None = None) -> torch.Tensor | None:
         """ids [B, S] int64 on the device; appends S positions to `cache`.
-        Returns fp32 logits [B, S, vocab], or [B, vocab] of the last position."""
+        Returns fp32 logits [B, S, vocab], or [B, vocab] of the last position;
+        with `next_token` (int64 [B]) it writes the greedy token of the last
+        position there instead (LM head and argmax in one pass, no logits)
+        and returns None."""
         c = self.cfg
         B, S = ids.shape
         if cache.batch != B:
@@ -192,6 +196,11 @@ class Qwen2Model:
             x = x.reshape(B, S, D)[:, -1, :]  # strided rows: the norm kernel gathers them
         x = ops.rms_norm(x, self.norm_w, c.rms_eps, out=torch.empty((x.shape[0], D), dtype=torch.bfloat16,
                                                                      device=self.device))
+        if next_token is not None:
+            if not last_only:
+                raise ValueError("next_token needs last_only=True")
+            ops.linear_argmax(x, self.embed, out=next_token)
+            return None
         logits = ops.linear(x, self.embed, out_dtype=torch.float32)
         return logits if last_only else logits.reshape(B, S, c.vocab_size)
 
@@ -217,15 +226,13 @@ class Qwen2Model:
         cache.length = 0
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
-        logits = self.forward(ids, cache, last_only=True)
-        ops.argmax(logits, out=toks[0])
+        self.forward(ids, cache, last_only=True, next_token=toks[0])
         e1.record()
         if graphs is not None:
             graphs.replay()
         else:
             for step in range(1, max_new_tokens):
-                logits = self.forward(toks[step - 1].view(B, 1), cache, last_only=True)
-                ops.argmax(logits, out=toks[step])
+                self.forward(toks[step - 1].view(B, 1), cache, last_only=True, next_token=toks[step])
         e2.record()
         torch.cuda.synchronize()
         return toks.t(), {"prefill_ms": e0.elapsed_time(e1), "decode_ms": e1.elapsed_time(e2)}
@@ -244,14 +251,16 @@ class DecodeGraphs:
         self.batch, self.prompt, self.new = batch, prompt, new
         self.cache = model.new_cache(batch, prompt + new)
         self.toks = torch.zeros((new, batch), dtype=torch.int64, device=model.device)
-        # the scratch buffer the last step's attention needs is reserved
-        # before any capture (graphs record its address), then one eager step
+        # the scratch buffer the last step's attention (or the LM-head argmax)
+        # needs is reserved before any capture (graphs record its address), then one eager step
         # sets up per-kernel attributes and the small-M workspace
         c = model.cfg
-        ops.reserve_workspace(model.device, ops.attention_workspace_bytes(batch, 1, c.n_head, c.n_kv_head,
-                                                                          prompt + new - 1))
+        vocab = model.cfg.vocab_size
+        ops.reserve_workspace(model.device, max(ops.attention_workspace_bytes(batch, 1, c.n_head, c.n_kv_head,
+                                                                              prompt + new - 1),
+                                                ops.linear_argmax_workspace_bytes(batch, vocab)))
         self.cache.length = prompt
-        model.forward(self.toks[0].view(batch, 1), self.cache, last_only=True)
+        model.forward(self.toks[0].view(batch, 1), self.cache, last_only=True, next_token=torch.empty_like(self.toks[0]))
         torch.cuda.synchronize()
         pool = torch.cuda.graph_pool_handle()
         self.graphs = []
@@ -259,8 +268,8 @@ class DecodeGraphs:
             self.cache.length = prompt + step - 1
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, pool=pool):
-                logits = model.forward(self.toks[step - 1].view(batch, 1), self.cache, last_only=True)
-                ops.argmax(logits, out=self.toks[step])
+                model.forward(self.toks[step - 1].view(batch, 1), self.cache, last_only=True,
+                              next_token=self.toks[step])
             self.graphs.append(g)
         self.cache.length = 0
 
