@@ -294,6 +294,28 @@ XB_API int xb_linear_small_swiglu_bf16(const void* X, const void* W, void* Y,
                                        void* workspace, size_t workspace_bytes,
                                        void* stream, char* err, size_t errlen);
 
+/* The fused QKV projection of a prefill (any number of tokens), finished in
+ * the GEMM epilogue: qkv = bf16(X @ W^T + bias) with X [batch * seq, K] and
+ * W [(H + 2 KVH) * 64, K], then the rotate-half RoPE of the query and key
+ * heads at positions pos_offset + s (cos/sin fp32 [>= pos_offset + seq, 64];
+ * both NULL: no rotation, learned positions; rope_dup = 1 promises that
+ * every table row's second half repeats its first, as rotate-half RoPE
+ * tables do, and only the first half is read) -- the roundings of
+ * xb_linear_bf16 followed by xb_rope_kv_bf16 -- written straight to q
+ * [batch, H, seq, 64] and the K / V caches [batch, KVH, max_seq, 64] (16-byte
+ * aligned).  The qkv activations never reach memory.  Replaces
+ * examples/qwen2_5/model.py:836-867 (q/k/v projections + rope) and
+ * examples/gpt2/model.py:757-775 (c_attn + head split). */
+XB_API int xb_linear_rope_kv_bf16(const void* X, const void* W, const void* bias,
+                                  const float* cos_t, const float* sin_t,
+                                  int rope_dup, void* q_out, void* k_cache,
+                                  void* v_cache,
+                                  int64_t batch, int64_t seq, int64_t n_head,
+                                  int64_t n_kv_head, int64_t head_dim,
+                                  int64_t max_seq, int64_t pos_offset,
+                                  int64_t K, int64_t ldx, int64_t ldw,
+                                  void* stream, char* err, size_t errlen);
+
 /* Y = residual + bf16(X @ W^T + bias) (bf16, any M): the linear with the
  * residual add fused into the GEMM epilogue (o_proj / down_proj of a
  * prefill; examples/qwen2_5/model.py:1045-1046, 1060-1061). */

@@ -132,3 +132,35 @@ def test_rope_kv_many_tokens_matches_oracle(rope):
     assert torch.equal(kc.cpu()[:, :, pos:pos + S], rk)
     assert torch.equal(vc.cpu()[:, :, pos:pos + S], vv.reshape(B, S, KVH, 64).transpose(1, 2))
     assert torch.all(kc.cpu()[:, :, :pos] == 0) and torch.all(kc.cpu()[:, :, pos + S:] == 0)
+
+
+@pytest.mark.parametrize("B,S,H,KVH,pos,rope", [(2, 100, 14, 2, 0, True), (3, 70, 14, 2, 30, True),
+                                                (2, 130, 12, 12, 0, False), (4, 128, 14, 2, 0, True),
+                                                (1, 1, 14, 2, 5, True), (4, 96, 14, 2, 3, "random")])
+def test_prefill_qkv_gemm_with_rope_epilogue_equals_linear_then_rope(B, S, H, KVH, pos, rope):
+    """linear_qkv_rope (RoPE + KV write in the GEMM epilogue) = linear then
+    rope_kv, bit for bit, including the CTA-pair GEMM (B*S >= 256)."""
+    g = torch.Generator().manual_seed(B * S + H)
+    K, smax = 896, pos + S + 3
+    x = (torch.randn(B * S, K, generator=g) / 4).to(torch.bfloat16).cuda()
+    w = (torch.randn((H + 2 * KVH) * 64, K, generator=g) / 16).to(torch.bfloat16).cuda()
+    b = (torch.randn((H + 2 * KVH) * 64, generator=g) / 4).to(torch.bfloat16).cuda()
+    cos, sin = (t.cuda() for t in OQ.rope_tables(64, smax, 1e6)) if rope else (None, None)
+    if rope == "random":  # rows whose halves differ: both halves are read
+        cos, sin = torch.rand(smax, 64, generator=g).cuda(), torch.rand(smax, 64, generator=g).cuda()
+        assert not ops.rope_tables_repeat_halves(cos, sin)
+    elif rope:
+        assert ops.rope_tables_repeat_halves(cos, sin)
+    outs = []
+    for fused in (True, False):
+        q = torch.full((B, H, S, 64), 7.0, dtype=torch.bfloat16, device="cuda")
+        kc = torch.zeros((B, KVH, smax, 64), dtype=torch.bfloat16, device="cuda")
+        vc = torch.zeros_like(kc)
+        if fused:
+            ops.linear_qkv_rope(x, w, b, cos, sin, q, kc, vc, B, S, H, KVH, 64, pos)
+        else:
+            ops.rope_kv(ops.linear(x, w, b), cos, sin, q, kc, vc, B, S, H, KVH, 64, pos)
+        outs.append((q.cpu(), kc.cpu(), vc.cpu()))
+    for a, c in zip(*outs):
+        assert torch.equal(a, c)
+    assert ops.device_status() == 0

@@ -56,7 +56,11 @@ enum Kind { kBf16 = 0, kInt8 = 1, kInt16Limbs = 2 };
 // kOutArgmax (swap-AB only): no logits; per 128-row tile of W and token the
 // best (value, row) goes to C as {float, int32} [row tiles][tokens], and
 // xb_linear_argmax_bf16 reduces the tiles (the greedy next token).
-enum Out { kOutF32 = 0, kOutBf16 = 1, kOutI32 = 2, kOutSwiglu = 3, kOutArgmax = 4 };
+// kOutQkv: the fused QKV projection of a prefill, finished in the epilogue:
+// bf16(acc + bias) per 64-column head slot, RoPE of the query / key heads
+// (none without tables), written to q [B, H, S, 64] and the K / V caches at
+// pos_offset + s -- the roundings of a linear followed by the RoPE kernel.
+enum Out { kOutF32 = 0, kOutBf16 = 1, kOutI32 = 2, kOutSwiglu = 3, kOutArgmax = 4, kOutQkv = 5 };
 
 constexpr int tmem_cols_for(int cols) { return cols <= 32 ? 32 : cols <= 64 ? 64 : cols <= 128 ? 128 : cols <= 256 ? 256 : 512; }
 
@@ -122,6 +126,14 @@ struct Args {
   // into each rank's C (peer pointers, this rank's column block), and the
   // grid's last CTA signals every peer.
   int c_tma;  // 1: C is written through maps.c (TMA stores from shared memory)
+  // kOutQkv: destinations, head layout and RoPE tables (rows are the B*S tokens)
+  void* q_out;
+  void* k_cache;
+  void* v_cache;
+  const float* cos_t;
+  const float* sin_t;
+  int H, KVH, S, smax, pos;
+  int rope_dup;  // 1: every table row's second half repeats its first (read the first only)
   int world, rank;
   void* peers[8];
   uint64_t* signals[8];  // each rank's signal buffer (uint64 [world + 1])
@@ -389,6 +401,69 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * C::ACCS * C::BN;
 #pragma unroll 1
       for (int cc = 0; cc < C::BN / 32; ++cc) {
+        if constexpr (OUT == kOutQkv) {
+          static_assert(!TRANS && !PEERS && C::BN % 64 == 0, "fused QKV epilogue: row-major tiles of whole heads");
+          if (cc & 1) continue;  // the even chunk takes the whole 64-column head slot
+          uint32_t v0[32], v1[32];
+          tmem_ld_32x32b_x32(tbase + cc * 32, v0);
+          tmem_ld_32x32b_x32(tbase + cc * 32 + 32, v1);
+          tmem_ld_wait();
+          const int c0 = tn * C::BN + cc * 32;  // first column of the head slot
+          if (row >= args.m || c0 >= args.n) continue;
+          const int slot = c0 >> 6;
+          const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(args.bias);
+          float x0[32], x1[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float b0 = bp ? __bfloat162float(bp[c0 + j]) : 0.0f;
+            const float b1 = bp ? __bfloat162float(bp[c0 + 32 + j]) : 0.0f;
+            x0[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[j]) + b0));
+            x1[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[j]) + b1));
+          }
+          const int bq = row / args.S, sq = row - bq * args.S, pos = args.pos + sq;
+          __nv_bfloat16* dst;
+          if (slot < args.H)
+            dst = static_cast<__nv_bfloat16*>(args.q_out) + (((int64_t)bq * args.H + slot) * args.S + sq) * 64;
+          else if (slot < args.H + args.KVH)
+            dst = static_cast<__nv_bfloat16*>(args.k_cache) +
+                  (((int64_t)bq * args.KVH + (slot - args.H)) * args.smax + pos) * 64;
+          else
+            dst = static_cast<__nv_bfloat16*>(args.v_cache) +
+                  (((int64_t)bq * args.KVH + (slot - args.H - args.KVH)) * args.smax + pos) * 64;
+          if (args.cos_t && slot < args.H + args.KVH) {
+            // each lane reads its own token's table rows (16-byte loads: a
+            // warp's 32 tokens touch 32 rows per instruction)
+            const float4* cr = reinterpret_cast<const float4*>(args.cos_t + (int64_t)pos * 64);
+            const float4* sr = reinterpret_cast<const float4*>(args.sin_t + (int64_t)pos * 64);
+#pragma unroll
+            for (int j4 = 0; j4 < 8; ++j4) {
+              const float4 ca = __ldg(cr + j4), sa = __ldg(sr + j4);
+              const float4 cb = args.rope_dup ? ca : __ldg(cr + 8 + j4), sb = args.rope_dup ? sa : __ldg(sr + 8 + j4);
+              const float c0v[4] = {ca.x, ca.y, ca.z, ca.w}, c1v[4] = {cb.x, cb.y, cb.z, cb.w};
+              const float s0v[4] = {sa.x, sa.y, sa.z, sa.w}, s1v[4] = {sb.x, sb.y, sb.z, sb.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int j = 4 * j4 + e;
+                const float y0 = __fadd_rn(__fmul_rn(x0[j], c0v[e]), __fmul_rn(-x1[j], s0v[e]));
+                const float y1 = __fadd_rn(__fmul_rn(x1[j], c1v[e]), __fmul_rn(x0[j], s1v[e]));
+                x0[j] = y0;
+                x1[j] = y1;
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 32; j += 8) {
+            __nv_bfloat162 h0[4], h1[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              h0[e] = __floats2bfloat162_rn(x0[j + 2 * e], x0[j + 2 * e + 1]);
+              h1[e] = __floats2bfloat162_rn(x1[j + 2 * e], x1[j + 2 * e + 1]);
+            }
+            *reinterpret_cast<int4*>(dst + j) = *reinterpret_cast<int4*>(h0);
+            *reinterpret_cast<int4*>(dst + 32 + j) = *reinterpret_cast<int4*>(h1);
+          }
+          continue;
+        }
         if constexpr (OUT == kOutSwiglu) {
           if (cc >= C::BN / 64) continue;
           uint32_t gv[32], uv[32];
@@ -1245,7 +1320,8 @@ bool lines_enabled();
 template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false>
 int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
            cudaStream_t s, const char* what, char* err, size_t errlen, int splits = 1, int64_t split_stride = 0,
-           const PeerArgs* pa = nullptr, const void* residual = nullptr, int64_t ldr = 0, int act = 0) {
+           const PeerArgs* pa = nullptr, const void* residual = nullptr, int64_t ldr = 0, int act = 0,
+           const Args* qkv = nullptr) {
   using Cf = Cfg<KIND, B_KMAJOR, BN_, PAIR>;
   const CUtensorMapDataType dt = KIND == kBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   Maps maps;
@@ -1258,6 +1334,8 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
     if (rc) return rc;
   }
   Args args;
+  memset(&args, 0, sizeof(args));
+  if (qkv) args = *qkv;  // kOutQkv destinations
   args.c = c;
   args.bias = bias;
   args.residual = residual;
@@ -1285,8 +1363,10 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   // 4-byte outputs of whole-tile GEMMs leave through the TMA-store epilogue
   // when C meets the TMA alignment rules.
   // Transposed (small-M) outputs too, through [tokens][features] staging tiles.
-  constexpr bool kStaged = !PEERS && OUT != kOutSwiglu && OUT != kOutArgmax && (TRANS || OUT != kOutBf16);
+  constexpr bool kStaged =
+      !PEERS && OUT != kOutSwiglu && OUT != kOutArgmax && OUT != kOutQkv && (TRANS || OUT != kOutBf16);
   constexpr bool kLines = !TRANS && (PEERS || OUT == kOutBf16);  // whole-line staged stores
+  static_assert(OUT != kOutQkv || !TRANS, "the fused QKV epilogue takes row-major tiles");
   constexpr int kSmem = Cf::SMEM + ((kStaged || kLines || OUT == kOutArgmax) ? kEpiStageBytes : 0);
   static_assert(4 * 32 * 33 * 4 + 4 * 64 * 8 <= kEpiStageBytes, "argmax staging fits");
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
@@ -2675,6 +2755,56 @@ extern "C" int xb_linear_small_residual_norm_bf16(const void* X, const void* W, 
              static_cast<const bf*>(bias), static_cast<const bf*>(residual), ldr, static_cast<bf*>(Y), ldy,
              static_cast<bf*>(Yn), ldn, static_cast<const bf*>(norm_w), static_cast<const bf*>(norm_b), eps);
   return check_launch(what, err, errlen);
+}
+
+extern "C" int xb_linear_rope_kv_bf16(const void* X, const void* W, const void* bias, const float* cos_t,
+                                      const float* sin_t, int rope_dup, void* q_out, void* k_cache, void* v_cache,
+                                      int64_t batch, int64_t seq, int64_t n_head, int64_t n_kv_head,
+                                      int64_t head_dim, int64_t max_seq, int64_t pos_offset, int64_t K, int64_t ldx,
+                                      int64_t ldw, void* stream, char* err, size_t errlen) {
+  const char* what = "xb_linear_rope_kv_bf16";
+  if (head_dim != 64 || n_head <= 0 || n_kv_head <= 0 || n_head % n_kv_head || batch < 0 || seq <= 0 ||
+      pos_offset < 0 || pos_offset + seq > max_seq || max_seq > INT32_MAX) {
+    set_err(err, errlen, "%s: bad head layout (head_dim 64) or positions", what);
+    return XB_ERR_INVALID;
+  }
+  const int64_t M = batch * seq, N = (n_head + 2 * n_kv_head) * head_dim;
+  if (M == 0) return XB_OK;
+  if (!X || !W || !q_out || !k_cache || !v_cache || (!cos_t) != (!sin_t) || K <= 0 || ldx < K || ldw < K ||
+      M > INT32_MAX) {
+    set_err(err, errlen, "%s: null pointer or bad shape", what);
+    return XB_ERR_INVALID;
+  }
+  const void* outs[5] = {q_out, k_cache, v_cache, cos_t, sin_t};
+  for (const void* p : outs)
+    if (reinterpret_cast<uintptr_t>(p) & 15) {
+      set_err(err, errlen, "%s: q / K / V buffers and RoPE tables must be 16-byte aligned", what);
+      return XB_ERR_UNSUPPORTED;
+    }
+  if (!tma_ok(X, ldx, 2) || !tma_ok(W, ldw, 2)) {
+    set_err(err, errlen, "%s: X/W must be 16-byte aligned with row pitches a multiple of 16 bytes", what);
+    return XB_ERR_UNSUPPORTED;
+  }
+  Args a;
+  memset(&a, 0, sizeof(a));
+  a.q_out = q_out;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.cos_t = cos_t;
+  a.sin_t = sin_t;
+  a.H = (int)n_head;
+  a.KVH = (int)n_kv_head;
+  a.S = (int)seq;
+  a.smax = (int)max_seq;
+  a.pos = (int)pos_offset;
+  a.rope_dup = rope_dup ? 1 : 0;
+  Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
+  cudaStream_t s = (cudaStream_t)stream;
+  if (use_pairs(M))
+    return launch<kBf16, true, kOutQkv, 0, false, false, true>(op, nullptr, bias, M, N, K, N, s, what, err, errlen, 1,
+                                                               0, nullptr, nullptr, 0, 0, &a);
+  return launch<kBf16, true, kOutQkv>(op, nullptr, bias, M, N, K, N, s, what, err, errlen, 1, 0, nullptr, nullptr, 0, 0,
+                                      &a);
 }
 
 extern "C" int xb_linear_residual_bf16(const void* X, const void* W, const void* bias, const void* residual, void* Y,

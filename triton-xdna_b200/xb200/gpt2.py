@@ -187,8 +187,9 @@ class GPT2Model:
                                           H, H, HD, pos, xnorm=xnorm)
             else:
                 xn = ops.layernorm(x, L["ln1_w"], L["ln1_b"], c.ln_eps)
-                qkv = ops.linear(xn, L["qkv_w"], L["qkv_b"])
-                ops.rope_kv(qkv, None, None, q_buf, cache.k[i], cache.v[i], B, S, H, H, HD, pos)
+                # c_attn GEMM with the head split + KV write in its epilogue
+                ops.linear_qkv_rope(xn, L["qkv_w"], L["qkv_b"], None, None, q_buf, cache.k[i], cache.v[i],
+                                    B, S, H, H, HD, pos)
             ops.attention(q_buf, cache.k[i], cache.v[i], attn, B, S, H, H, HD, pos, self.scale)
             if decode:
                 y, st = ops.decode_linear_residual(attn, L["proj_w"], L["proj_b"], x, stats_kind="layer")

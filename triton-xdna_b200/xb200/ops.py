@@ -734,6 +734,41 @@ def token_status() -> int:
     return st.value
 
 
+_rope_halves: dict = {}
+
+
+def rope_tables_repeat_halves(cos_t, sin_t) -> bool:
+    """Whether every row of both RoPE tables repeats its first half in its
+    second (rotate-half tables built from duplicated frequencies); checked
+    once per pair of tables (keyed by their storage and version)."""
+    key = (cos_t.data_ptr(), sin_t.data_ptr(), cos_t.shape, cos_t._version, sin_t._version)
+    v = _rope_halves.get(key)
+    if v is None:
+        h = cos_t.shape[-1] // 2
+        v = bool(torch.equal(cos_t[..., :h], cos_t[..., h:]) and torch.equal(sin_t[..., :h], sin_t[..., h:]))
+        _rope_halves[key] = v
+    return v
+
+
+def linear_qkv_rope(x, w_qkv, b_qkv, cos_t, sin_t, q_out, k_cache, v_cache, batch, seq, n_head, n_kv_head, head_dim,
+                    pos_offset):
+    """Prefill QKV projection + RoPE (none when the tables are None) + KV-cache
+    write in one GEMM (the epilogue finishes each head slot): the results of
+    linear() followed by rope_kv(), without the qkv activations in memory."""
+    _cuda(x, w_qkv, b_qkv, cos_t, sin_t, q_out, k_cache, v_cache)
+    if (cos_t is None) != (sin_t is None):
+        raise ValueError("give both RoPE tables or neither")
+    if cos_t is not None and cos_t.shape[0] < pos_offset + seq:
+        raise ValueError("RoPE tables are shorter than the positions")
+    x2 = x.reshape(-1, x.shape[-1])
+    K = x2.shape[1]
+    _lib.call("xb_linear_rope_kv_bf16", x2.data_ptr(), w_qkv.data_ptr(),
+              b_qkv.data_ptr() if b_qkv is not None else None,
+              cos_t.data_ptr() if cos_t is not None else None, sin_t.data_ptr() if sin_t is not None else None,
+              int(cos_t is not None and rope_tables_repeat_halves(cos_t, sin_t)), q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), batch, seq, n_head, n_kv_head, head_dim,
+              k_cache.shape[2], pos_offset, K, _mat(x2, "x"), _mat(w_qkv, "w"), _stream())
+
+
 def rope_kv(qkv, cos_t, sin_t, q_out, k_cache, v_cache, batch, seq, n_head, n_kv_head, head_dim, pos_offset):
     """RoPE on the fused QKV projection + KV-cache write (model.py:851-867).
     cos_t = sin_t = None: heads are split and written unrotated (GPT-2)."""

@@ -176,8 +176,9 @@ class Qwen2Model:
                                           cache.v[i], H, KVH, HD, pos, xnorm=xnorm)
             else:
                 xn = ops.rms_norm(x, L["input_ln"], c.rms_eps)
-                qkv = ops.linear(xn, L["qkv_w"], L["qkv_b"])
-                ops.rope_kv(qkv, self.cos, self.sin, q_buf, cache.k[i], cache.v[i], B, S, H, KVH, HD, pos)
+                # QKV GEMM with RoPE + KV write in its epilogue
+                ops.linear_qkv_rope(xn, L["qkv_w"], L["qkv_b"], self.cos, self.sin, q_buf, cache.k[i], cache.v[i],
+                                    B, S, H, KVH, HD, pos)
             ops.attention(q_buf, cache.k[i], cache.v[i], attn, B, S, H, KVH, HD, pos, self.scale)
             if decode:
                 y, st = ops.decode_linear_residual(attn, L["o_w"], None, x, stats_kind="rms")
