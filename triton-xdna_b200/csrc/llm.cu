@@ -221,8 +221,8 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const bf16* __restric
                                                            float scale_log2) {
   pdl_wait();
   pdl_trigger();
-  __shared__ __align__(16) bf16 sK[kBK][kPad];
-  __shared__ __align__(16) bf16 sV[kBK][kPad];
+  __shared__ __align__(16) bf16 sK[2][kBK][kPad];  // double-buffered key / value tiles
+  __shared__ __align__(16) bf16 sV[2][kBK][kPad];
   const int bh = blockIdx.y;
   const int b = bh / H, h = bh % H;
   const int kvh = h / (H / KVH);
@@ -253,19 +253,35 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const bf16* __restric
   const int kmax = min(total, pos_offset + last_q + 1);
   const int qa0 = pos_offset + qw + g, qa1 = qa0 + 8;  // absolute positions of this thread's rows
 
-  for (int k0 = 0; k0 < kmax; k0 += kBK) {
-    __syncthreads();  // previous tile fully consumed
+  // Tiles stream through two buffers with cp.async: tile i + 2 is requested
+  // as soon as tile i has been consumed, so the copies overlap the math
+  // (rows past the context are zero-filled, nothing read).
+  const int ntiles = (kmax + kBK - 1) / kBK;
+  auto issue = [&](int tile, int buf) {
+    const int t0 = tile * kBK;
     for (int v = threadIdx.x; v < kBK * kHD / 8; v += 128) {
       const int row = v / (kHD / 8), c8 = (v % (kHD / 8)) * 8;
-      int4 kv = make_int4(0, 0, 0, 0), vv = make_int4(0, 0, 0, 0);
-      if (k0 + row < total) {
-        kv = *reinterpret_cast<const int4*>(kp + (int64_t)(k0 + row) * kHD + c8);
-        vv = *reinterpret_cast<const int4*>(vp + (int64_t)(k0 + row) * kHD + c8);
-      }
-      *reinterpret_cast<int4*>(&sK[row][c8]) = kv;
-      *reinterpret_cast<int4*>(&sV[row][c8]) = vv;
+      const bool ok = t0 + row < total;
+      const int64_t src = (int64_t)(ok ? t0 + row : 0) * kHD + c8;
+      const uint32_t bytes = ok ? 16u : 0u;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                       (uint32_t)__cvta_generic_to_shared(&sK[buf][row][c8])),
+                   "l"(kp + src), "r"(bytes)
+                   : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                       (uint32_t)__cvta_generic_to_shared(&sV[buf][row][c8])),
+                   "l"(vp + src), "r"(bytes)
+                   : "memory");
     }
-    __syncthreads();
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (ntiles > 0) issue(0, 0);
+  if (ntiles > 1) issue(1, 1);
+  for (int it = 0; it < ntiles; ++it) {
+    const int buf = it & 1, k0 = it * kBK;
+    if (it + 1 < ntiles) asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // every thread's copies of tile `it` have landed
 
     float s[8][4];
 #pragma unroll
@@ -273,23 +289,38 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const bf16* __restric
       s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&sK[nt * 8 + g][kk * 16 + 2 * t]);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&sK[nt * 8 + g][kk * 16 + 8 + 2 * t]);
+        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(&sK[buf][nt * 8 + g][kk * 16 + 2 * t]);
+        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(&sK[buf][nt * 8 + g][kk * 16 + 8 + 2 * t]);
         mma_bf16_16816(s[nt], qa[kk], b0, b1);
       }
     }
     float mx0 = -INFINITY, mx1 = -INFINITY;
+    // a tile wholly inside the context and at or below the warp's first
+    // query row needs no mask (every tile but the diagonal ones)
+    const bool unmasked = k0 + kBK <= total && k0 + kBK - 1 <= pos_offset + qw;
+    if (unmasked) {
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = k0 + nt * 8 + 2 * t + (e & 1);
-        const int qpos = e < 2 ? qa0 : qa1;
-        const bool ok = key < total && key <= qpos;
-        s[nt][e] = ok ? s[nt][e] * scale_log2 : -INFINITY;
-        if (e < 2) mx0 = fmaxf(mx0, s[nt][e]);
-        else mx1 = fmaxf(mx1, s[nt][e]);
+      for (int nt = 0; nt < 8; ++nt) {
+        s[nt][0] *= scale_log2;
+        s[nt][1] *= scale_log2;
+        s[nt][2] *= scale_log2;
+        s[nt][3] *= scale_log2;
+        mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+        mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
       }
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = k0 + nt * 8 + 2 * t + (e & 1);
+          const int qpos = e < 2 ? qa0 : qa1;
+          const bool ok = key < total && key <= qpos;
+          s[nt][e] = ok ? s[nt][e] * scale_log2 : -INFINITY;
+          if (e < 2) mx0 = fmaxf(mx0, s[nt][e]);
+          else mx1 = fmaxf(mx1, s[nt][e]);
+        }
+    }
 #pragma unroll
     for (int o_ = 1; o_ <= 2; o_ <<= 1) {
       mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o_));
@@ -330,11 +361,13 @@ __global__ void __launch_bounds__(128) attn_prefill_kernel(const bf16* __restric
       for (int dt = 0; dt < 8; dt += 2) {
         const int mi = lane >> 3, r = lane & 7;
         uint32_t vb[4];
-        ldmatrix_x4_trans(vb, &sV[kk * 16 + (mi & 1) * 8 + r][dt * 8 + (mi >> 1) * 8]);
+        ldmatrix_x4_trans(vb, &sV[buf][kk * 16 + (mi & 1) * 8 + r][dt * 8 + (mi >> 1) * 8]);
         mma_bf16_16816(o[dt], pa, vb[0], vb[1]);
         mma_bf16_16816(o[dt + 1], pa, vb[2], vb[3]);
       }
     }
+    __syncthreads();  // tile `it` consumed: its buffer takes tile it + 2
+    if (it + 2 < ntiles) issue(it + 2, buf);
   }
 #pragma unroll
   for (int o_ = 1; o_ <= 2; o_ <<= 1) {
