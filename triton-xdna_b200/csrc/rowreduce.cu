@@ -282,12 +282,11 @@ bool dispatch_vec(const RowArgs& a, int64_t nvec, cudaStream_t s) {
   constexpr int MAXV = sizeof(T) == 2 ? 4 : 8;  // at most 32 fp32 values per thread
   // The configuration depends on the row length only, never on the row
   // count, so a row is reduced in the same order whatever the batch (batch
-  // invariance).  Rows of 33..256 vectors (e.g. the 896-wide hidden state of
-  // Qwen2.5-0.5B) get one row per CTA, which also spreads the few rows of a
-  // decode step over the SMs.
-  if (nvec > 32 && nvec <= 256) {
-    if (nvec <= 64) { launch_vec<T, 64, 1, OP>(a, s); return true; }
-    if (nvec <= 128) { launch_vec<T, 128, 1, OP>(a, s); return true; }
+  // invariance).  Rows of up to 32 * MAXV vectors (the 768- and 896-wide
+  // hidden states of GPT-2 and Qwen2.5-0.5B included) take a warp (or less)
+  // each, several 16-byte loads in flight per lane; rows of 129..256 vectors
+  // get one row per CTA.
+  if (nvec > 32 * MAXV && nvec <= 256) {
     launch_vec<T, 128, 2, OP>(a, s);
     return true;
   }
