@@ -72,6 +72,36 @@ def test_decode_attention_one_cta_per_kv_head(B, H, KVH, pos, smax):
     assert torch.equal(got, _run(q, kc, vc, B, 1, H, KVH, pos).float())  # fixed merge order
 
 
+@pytest.mark.parametrize("B,S,H,KVH,pos,smax", [(2, 512, 14, 2, 0, 640), (3, 300, 12, 12, 37, 400),
+                                                (1, 128, 4, 1, 0, 128), (2, 200, 14, 2, 100, 320),
+                                                (1, 257, 14, 2, 5, 300)])
+def test_prefill_attention_long_chunks_match_oracle(B, S, H, KVH, pos, smax):
+    """Prefill chunks of 128 tokens or more: ragged tails, a position offset
+    and key tiles that cross the end of the context."""
+    q = _rand((B, H, S, 64), 21, 2.0)
+    kc = _rand((B, KVH, smax, 64), 22, 2.0)
+    vc = _rand((B, KVH, smax, 64), 23)
+    got = _run(q, kc, vc, B, S, H, KVH, pos).float()
+    T = pos + S
+    ref = OQ.attention(q, kc[:, :, :T], vc[:, :, :T], pos, 1 / 8).float()
+    torch.testing.assert_close(got, ref, atol=2e-2, rtol=2e-2)
+    exact = _exact(q, kc[:, :, :T], vc[:, :, :T], pos, 1 / 8).float()
+    assert float((got - exact).abs().max()) < 3e-2
+    assert torch.equal(got, _run(q, kc, vc, B, S, H, KVH, pos).float())  # deterministic
+    assert ops.device_status() == 0
+
+
+def test_prefill_rows_equal_decode_steps_long_chunk():
+    B, H, KVH, smax = 2, 14, 2, 256
+    q = _rand((B, H, 160, 64), 24, 2.0)
+    kc = _rand((B, KVH, smax, 64), 25, 2.0)
+    vc = _rand((B, KVH, smax, 64), 26)
+    pre = _run(q, kc, vc, B, 160, H, KVH, 0).float()
+    for s in (0, 63, 64, 127, 128, 159):
+        dec = _run(q[:, :, s:s + 1].contiguous(), kc, vc, B, 1, H, KVH, s).float()
+        torch.testing.assert_close(dec[:, :, 0], pre[:, :, s], atol=1.6e-2, rtol=1e-2)
+
+
 def test_prefill_rows_equal_decode_steps():
     B, H, KVH, smax = 2, 14, 2, 256
     q = _rand((B, H, 80, 64), 4, 2.0)
