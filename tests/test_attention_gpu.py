@@ -56,7 +56,7 @@ def test_attention_matches_oracle(B, S, H, KVH, pos, smax):
 
 @pytest.mark.parametrize("B,H,KVH,pos,smax", [(48, 14, 2, 575, 640), (48, 14, 2, 0, 8), (32, 12, 4, 40, 64),
                                               (100, 8, 1, 255, 300), (24, 20, 4, 1000, 1024), (96, 5, 1, 33, 40),
-                                              (24, 14, 2, 300, 320)])
+                                              (24, 14, 2, 300, 320), (8, 12, 12, 575, 640), (16, 8, 4, 100, 128)])
 def test_decode_attention_one_cta_per_kv_head(B, H, KVH, pos, smax):
     """Many sequences (>= 48 (batch, KV head) pairs) take the kernel in which
     one CTA walks a KV head's whole context; ragged and single-key contexts."""
