@@ -140,12 +140,28 @@ def elementwise_workload(dev, n: int, seed: int, host: bool):
                   lambda: kernels.avg_pool2d_kernel[(planes,)](hpin, hpout, planes, H, W, BLOCK=1),
                   h2d=(nin + nout) * 4, d2h=nout * 4))
     config = {
-        "workload": f"elementwise/activation suite: 8 ops x {{bf16,f32}} on {n} elements "
-                    f"(swiglu {half}+{half}) + avg_pool2d 2x2/s2 on [{planes // 256},256,224,224] f32",
+        "workload": suite_workload("elementwise", n),
         "n_elements": n,
         "l2": "every input > 126 MB L2 (no flush needed)" if n * 2 > 126e6 else "inputs may fit in L2",
     }
-    return out, config, "elementwise/activation suite algorithmic HBM throughput", "bf16+f32"
+    return out, config, SUITE_METRICS["elementwise"], "bf16+f32"
+
+
+SUITE_METRICS = {"elementwise": "elementwise/activation suite algorithmic HBM throughput",
+                 "rowreduce": "row-reduction suite algorithmic HBM throughput"}
+
+
+def suite_workload(kind: str, n: int = None) -> str:
+    """The workload description both arms print for the elementwise and
+    row-reduction suites (n: flat length of the elementwise tensors)."""
+    n = N28 if n is None else n
+    if kind == "elementwise":
+        half = n // 2
+        planes = max(1, POOL_SHAPE[0] * n // N28) * POOL_SHAPE[1]
+        return (f"elementwise/activation suite: 8 ops x {{bf16,f32}} on {n} elements "
+                f"(swiglu {half}+{half}) + avg_pool2d 2x2/s2 on [{planes // 256},256,224,224] f32")
+    rows = max(1, ROWS * n // N28)
+    return f"row reductions on [{rows} x {COLS}] bf16 and f32, x~N(0,1)*3"
 
 
 def rowreduce_workload(dev, n: int, seed: int, host: bool):
@@ -168,9 +184,9 @@ def rowreduce_workload(dev, n: int, seed: int, host: bool):
             Op(f"rms_norm_{t}", nb, lambda x=x, y=y: X.rms_norm(x, None, 1e-6, out=y)),
             Op(f"weighted_rms_norm_{t}", nb + COLS * eb, lambda x=x, y=y, gm=gm: X.rms_norm(x, gm, 1e-6, out=y)),
         ]
-    config = {"workload": f"row reductions on [{rows} x {COLS}] bf16 and f32, x~N(0,1)*3", "rows": rows,
+    config = {"workload": suite_workload("rowreduce", n), "rows": rows,
               "cols": COLS, "l2": "every input > 126 MB L2 (no flush needed)"}
-    return out, config, "row-reduction suite algorithmic HBM throughput", "bf16+f32"
+    return out, config, SUITE_METRICS["rowreduce"], "bf16+f32"
 
 
 GEMM_SIZES = [(256, 256, 256), (1024, 1024, 1024), (4096, 4096, 4096), (8192, 8192, 8192), (16384, 16384, 16384),
@@ -815,11 +831,11 @@ def main():
         _, threads, desc = cpu_baseline(args.workload, sample)
         value = statistics.median(vals)
         print(json.dumps({
-            "impl": "reference", "metric": f"{args.workload} suite algorithmic HBM throughput",
+            "impl": "reference", "metric": SUITE_METRICS[args.workload],
             "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16+f32",
             "data": "synthetic N(0,1), seed 0",
-            "config": {"workload": f"{args.workload} suite, CPU sample", "sample": desc},
+            "config": {"workload": suite_workload(args.workload, args.elements), "cpu_sample": desc},
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": desc},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
