@@ -20,6 +20,16 @@ Launch semantics mirror the reference's NPU launcher
 * CUDA tensors are used in place (no copies);
 * errors raise ``RuntimeError`` (driver.py:1553-1556) -- here ``XbError``.
 
+Kernels whose programs cover independent units along one leading dimension
+(elements, rows, planes, GEMM rows of A and C) carry a ``Split``.  When every
+pointer argument is a contiguous host tensor, such a launch copies only what
+the kernel reads and brings back only the region of the output it writes, so
+the output's other elements stay as they were, as under the copy-everything
+path.  With pinned host tensors the launch is cut into pieces of a few tens of
+MB: pieces' uploads, kernels and downloads run on three streams, so the
+host-to-device and device-to-host copies overlap each other and the kernels.
+The call still returns only after the last byte is back in the host tensor.
+
 The returned object carries ``.asm["ttsharedir"]`` because the examples write
 that field to ``tt.shared.mlir`` after each launch; xb200 compiles no MLIR,
 so it holds a one-line description of the CUDA entry point that ran.
@@ -47,14 +57,47 @@ class LaunchResult:
         return f"LaunchResult({self.name})"
 
 
+class Split:
+    """How a launch divides into independent pieces along its leading dimension.
+
+    ``units(b, g)`` is the number of units the launch covers (elements, rows,
+    planes); a piece is a whole number of ``align(b)`` units except the last.
+    ``pitch(b)`` maps each pointer that divides to its elements per unit; the
+    other pointers are read whole by every piece.  ``span(b)`` is the elements
+    of one unit the output is written over: the written region is one
+    contiguous range only when it equals the output's pitch.  ``piece(b, g, n)``
+    gives the scalar arguments and grid that make a launch cover ``n`` units.
+    """
+
+    def __init__(self, units, pitch, span, piece, align=lambda b: 1):
+        self.units, self.pitch, self.span, self.piece, self.align = units, pitch, span, piece, align
+
+
+_PIECE_BYTES = 32 << 20  # bytes crossing PCIe per piece (uploads + download)
+_MAX_PIECES = 256
+_SIDE_STREAMS: dict = {}
+
+
+def _side_streams(dev: torch.device):
+    if dev.index not in _SIDE_STREAMS:
+        _SIDE_STREAMS[dev.index] = (torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev))
+    return _SIDE_STREAMS[dev.index]
+
+
+def _span_bytes(t: torch.Tensor):
+    lo = t.data_ptr()
+    return lo, lo + t.numel() * t.element_size()
+
+
 class XbKernel:
     """A reference kernel signature bound to an xb200 CUDA implementation."""
 
-    def __init__(self, name: str, entry: str, run: Callable):
+    def __init__(self, name: str, entry: str, run: Callable, split: Split | None = None):
         self.__name__ = name
         self.name = name
         self.entry = entry
         self.run = run
+        self.split = split
         sig = inspect.signature(run)
         self.params = [p for p in sig.parameters if p != "grid"]
 
@@ -89,15 +132,106 @@ class XbKernel:
             if not torch.cuda.is_available():
                 raise RuntimeError(f"{self.name}: no CUDA device available (xb200 has no CPU fallback)")
             dev = torch.device("cuda", torch.cuda.current_device())
-            dbound = dict(bound)
-            for k in ptr_names:
-                dbound[k] = bound[k].to(dev)
-            self.run(grid=g, **dbound)
-            last = ptr_names[-1]
-            bound[last].copy_(dbound[last])  # blocking device->host copy
+            plan = self._plan(bound, g, ptr_names, host)
+            if plan is not None:
+                self._launch_pieces(bound, g, ptr_names, dev, *plan)
+            else:
+                dbound = dict(bound)
+                for k in ptr_names:
+                    dbound[k] = bound[k].to(dev)
+                self.run(grid=g, **dbound)
+                last = ptr_names[-1]
+                bound[last].copy_(dbound[last])  # blocking device->host copy
         else:
             self.run(grid=g, **bound)
         return LaunchResult(self.name, self.entry)
+
+    def _plan(self, bound, g, ptr_names, host):
+        """(units, pitch, units per piece, pinned) when the launch may copy
+        only what it reads and writes; None keeps the copy-everything path
+        (which also raises the runner's own errors for malformed arguments)."""
+        sp = self.split
+        if sp is None or len(host) != len(ptr_names) or len(ptr_names) < 2:
+            return None
+        tensors = [bound[k] for k in ptr_names]
+        if not all(t.is_contiguous() for t in tensors):
+            return None
+        try:
+            units, pitch = int(sp.units(bound, g)), sp.pitch(bound)
+            span, align = int(sp.span(bound)), int(sp.align(bound))
+        except (TypeError, ValueError, ZeroDivisionError):
+            return None
+        out = ptr_names[-1]
+        if units <= 0 or align <= 0 or out not in pitch or span != pitch[out] or span <= 0:
+            return None
+        for k, p in pitch.items():
+            if k not in ptr_names or p <= 0 or bound[k].numel() < units * p:
+                return None
+        # the output may be one of the inputs exactly (an in-place launch), but
+        # must not partly overlap any other pointer's memory
+        olo, ohi = _span_bytes(bound[out])
+        for k in ptr_names[:-1]:
+            lo, hi = _span_bytes(bound[k])
+            if lo < ohi and olo < hi:
+                same = lo == olo and bound[k].dtype == bound[out].dtype and pitch.get(k) == pitch[out]
+                if not same:
+                    return None
+        unit_bytes = sum(pitch[k] * bound[k].element_size() for k in pitch)
+        pinned = all(t.is_pinned() for t in tensors)
+        if pinned:
+            per = max(align, (_PIECE_BYTES // max(1, unit_bytes)) // align * align)
+            fewest = -(-units // _MAX_PIECES)
+            per = max(per, -(-fewest // align) * align)
+        else:
+            per = units  # pageable memory: the copies are synchronous, one piece
+        return units, pitch, per, pinned
+
+    def _launch_pieces(self, bound, g, ptr_names, dev, units, pitch, per, nb):
+        out = ptr_names[-1]
+        cur = torch.cuda.current_stream(dev)
+        up, down = _side_streams(dev)
+        start = torch.cuda.Event()
+        start.record(cur)
+        flat = {k: bound[k].reshape(-1) for k in ptr_names}
+        dbuf = {k: torch.empty(units * pitch[k] if k in pitch else flat[k].numel(), dtype=flat[k].dtype, device=dev)
+                for k in ptr_names}
+        up.wait_event(start)
+        try:
+            with torch.cuda.stream(up):
+                for k in ptr_names:
+                    if k not in pitch:
+                        dbuf[k].copy_(flat[k], non_blocking=nb)
+            for lo in range(0, units, per):
+                n = min(per, units - lo)
+                with torch.cuda.stream(up):
+                    for k in ptr_names:
+                        if k in pitch and k != out:
+                            a, b = lo * pitch[k], (lo + n) * pitch[k]
+                            dbuf[k][a:b].copy_(flat[k][a:b], non_blocking=nb)
+                    ready = torch.cuda.Event()
+                    ready.record(up)
+                cur.wait_event(ready)
+                args = dict(bound)
+                args.update({k: dbuf[k][lo * pitch[k]:] if k in pitch else dbuf[k] for k in ptr_names})
+                scal, pg = self.split.piece(bound, g, n)
+                args.update(scal)
+                self.run(grid=pg, **args)
+                computed = torch.cuda.Event()
+                computed.record(cur)
+                down.wait_event(computed)
+                with torch.cuda.stream(down):
+                    a, b = lo * pitch[out], (lo + n) * pitch[out]
+                    flat[out][a:b].copy_(dbuf[out][a:b], non_blocking=nb)
+        finally:
+            # every copy into or out of the device buffers ends before they are freed
+            done = torch.cuda.Event()
+            done.record(down)
+            up_done = torch.cuda.Event()
+            up_done.record(up)
+            cur.wait_event(up_done)
+            cur.wait_event(done)
+            up_done.synchronize()
+            done.synchronize()  # the output is complete in host memory on return
 
 
 def _n(t: torch.Tensor, n: int) -> torch.Tensor:
@@ -143,15 +277,22 @@ def _swiglu(GATE, UP, OUT, n_elements, BLOCK_SIZE, grid):
     ops.swiglu(_n(GATE, n_elements), _n(UP, n_elements), out=_n(OUT, n_elements))
 
 
-vecadd = XbKernel("vecadd", "xb_vecadd", _vecadd)
-axpy_kernel = XbKernel("axpy_kernel", "xb_axpy", _axpy)
-relu_kernel = XbKernel("relu_kernel", "xb_relu", _unary(ops.relu))
-leaky_relu_kernel = XbKernel("leaky_relu_kernel", "xb_leaky_relu", _leaky)
-gelu_kernel = XbKernel("gelu_kernel", "xb_gelu", _unary(ops.gelu))
-gelu_kernel_gpu = XbKernel("gelu_kernel_gpu", "xb_gelu_tanh", _unary(ops.gelu_tanh))
-sigmoid_kernel = XbKernel("sigmoid_kernel", "xb_sigmoid", _unary(ops.sigmoid))
-silu_kernel = XbKernel("silu_kernel", "xb_silu", _unary(ops.silu))
-swiglu_kernel = XbKernel("swiglu_kernel", "xb_swiglu", _swiglu)
+def _flat(*ptrs):
+    # one unit per element; pieces start on 4096-element boundaries, so each
+    # piece's pointers keep the alignment of the vectorised loads
+    return Split(units=lambda b, g: b["n_elements"], pitch=lambda b: {k: 1 for k in ptrs}, span=lambda b: 1,
+                 piece=lambda b, g, n: ({"n_elements": n}, g), align=lambda b: 4096)
+
+
+vecadd = XbKernel("vecadd", "xb_vecadd", _vecadd, _flat("A", "B", "C"))
+axpy_kernel = XbKernel("axpy_kernel", "xb_axpy", _axpy, _flat("X", "Y", "OUT"))
+relu_kernel = XbKernel("relu_kernel", "xb_relu", _unary(ops.relu), _flat("X", "Y"))
+leaky_relu_kernel = XbKernel("leaky_relu_kernel", "xb_leaky_relu", _leaky, _flat("X", "Y"))
+gelu_kernel = XbKernel("gelu_kernel", "xb_gelu", _unary(ops.gelu), _flat("X", "Y"))
+gelu_kernel_gpu = XbKernel("gelu_kernel_gpu", "xb_gelu_tanh", _unary(ops.gelu_tanh), _flat("X", "Y"))
+sigmoid_kernel = XbKernel("sigmoid_kernel", "xb_sigmoid", _unary(ops.sigmoid), _flat("X", "Y"))
+silu_kernel = XbKernel("silu_kernel", "xb_silu", _unary(ops.silu), _flat("X", "Y"))
+swiglu_kernel = XbKernel("swiglu_kernel", "xb_swiglu", _swiglu, _flat("GATE", "UP", "OUT"))
 
 
 # ----------------------------------------------------------------------------- row reductions
@@ -191,14 +332,40 @@ def _avg_pool2d(X, Y, planes, H, W, BLOCK, grid):
     ops.avg_pool2d_2x2(x, out=Y.reshape(-1)[: planes * (H // 2) * (W // 2)].view(planes, H // 2, W // 2))
 
 
-avg_pool_kernel = XbKernel("avg_pool_kernel", "xb_row_center", _avg_pool)
+def _unit_cols(b, name):
+    if b[name] != 1:
+        raise ValueError("unit column stride")
+    return 1
+
+
+def _rows(block, pitch, span):
+    # one unit per row; a piece is a whole number of the kernel's row blocks,
+    # launched over that many programs
+    return Split(units=lambda b, g: g[0] * b[block], pitch=pitch, span=span,
+                 piece=lambda b, g, n: ({}, (n // b[block], g[1], g[2])), align=lambda b: b[block])
+
+
+_POOL2D = Split(units=lambda b, g: b["planes"],
+                pitch=lambda b: {"X": b["H"] * b["W"], "Y": (b["H"] // 2) * (b["W"] // 2)},
+                span=lambda b: (b["H"] // 2) * (b["W"] // 2), piece=lambda b, g, n: ({"planes": n}, (n, 1, 1)))
+_STRIDED_ROWS = dict(
+    pitch=lambda b: {"input_ptr": b["input_stride_row"] * _unit_cols(b, "input_stride_col"),
+                     "output_ptr": b["output_stride_row"] * _unit_cols(b, "output_stride_col")},
+    span=lambda b: b["n_cols"])
+
+avg_pool_kernel = XbKernel("avg_pool_kernel", "xb_row_center", _avg_pool,
+                           _rows("BLOCK_M", lambda b: {"X": b["N"], "Y": b["N"]}, lambda b: b["BLOCK_N"]))
 # The 2-D (NCHW, 2x2 / stride 2) pooling form has no reference kernel; this
 # launcher gives it the same calling convention as the others.
-avg_pool2d_kernel = XbKernel("avg_pool2d_kernel", "xb_avg_pool2d_2x2", _avg_pool2d)
-softmax_kernel = XbKernel("softmax_kernel", "xb_softmax", _softmax)
-_layer_norm_fwd_fused = XbKernel("_layer_norm_fwd_fused", "xb_layernorm", _layernorm)
-rms_norm_kernel = XbKernel("rms_norm_kernel", "xb_rms_norm", _rms)
-weighted_rms_norm_kernel = XbKernel("weighted_rms_norm_kernel", "xb_rms_norm", _wrms)
+avg_pool2d_kernel = XbKernel("avg_pool2d_kernel", "xb_avg_pool2d_2x2", _avg_pool2d, _POOL2D)
+softmax_kernel = XbKernel("softmax_kernel", "xb_softmax", _softmax, _rows("BLOCK_SIZE", **_STRIDED_ROWS))
+_layer_norm_fwd_fused = XbKernel("_layer_norm_fwd_fused", "xb_layernorm", _layernorm,
+                                 _rows("BLOCK_SIZE", **_STRIDED_ROWS))
+rms_norm_kernel = XbKernel("rms_norm_kernel", "xb_rms_norm", _rms,
+                           _rows("BLOCK_M", lambda b: {"X": b["N"], "Y": b["N"]}, lambda b: b["BLOCK_N"]))
+# the weight vector is read whole by every piece
+weighted_rms_norm_kernel = XbKernel("weighted_rms_norm_kernel", "xb_rms_norm", _wrms,
+                                    _rows("BLOCK_M", lambda b: {"X": b["N"], "Y": b["N"]}, lambda b: b["BLOCK_N"]))
 
 
 # ----------------------------------------------------------------------------- GEMMs
@@ -231,8 +398,8 @@ class _Autotuned(XbKernel):
     from its first config (examples/autotune-matmul/matmul.py:16-19), the way
     Triton's autotuner fills META before calling the grid."""
 
-    def __init__(self, name, entry, run, defaults):
-        super().__init__(name, entry, run)
+    def __init__(self, name, entry, run, defaults, split=None):
+        super().__init__(name, entry, run, split)
         self.defaults = defaults
 
     def _bind(self, args, kwargs):
@@ -272,11 +439,18 @@ def _load_2d(x_ptr, y_ptr, z_ptr, n_rows, n_cols, stride_0, stride_1, VEC_REG_SI
     ops.mul_2d(views[0], views[1], views[2])
 
 
-bare_matmul_i8 = XbKernel("bare_matmul_i8", "xb_matmul_i8", _matmul)
+# rows of A and C divide into pieces of whole 128-row tiles; B is read whole
+# by every piece
+_GEMM_ROWS = Split(units=lambda b, g: b["M"],
+                   pitch=lambda b: {"A": b["stride_am"] * _unit_cols(b, "stride_ak"),
+                                    "C": b["stride_cm"] * _unit_cols(b, "stride_cn")},
+                   span=lambda b: b["N"], piece=lambda b, g, n: ({"M": n}, g), align=lambda b: 128)
+
+bare_matmul_i8 = XbKernel("bare_matmul_i8", "xb_matmul_i8", _matmul, _GEMM_ROWS)
 padded_matmul_kernel = XbKernel("padded_matmul_kernel", "xb_matmul_f32_bf16emu", _padded_matmul)
 load_2d_block_kernel = XbKernel("kernel", "xb_mul_2d", _load_2d)
-bare_matmul = XbKernel("bare_matmul", "xb_matmul_bf16", _matmul)
-bare_matmul_autotuned = _Autotuned("bare_matmul", "xb_matmul_bf16", _matmul, {"BLOCK_SIZE_M": 256})
+bare_matmul = XbKernel("bare_matmul", "xb_matmul_bf16", _matmul, _GEMM_ROWS)
+bare_matmul_autotuned = _Autotuned("bare_matmul", "xb_matmul_bf16", _matmul, {"BLOCK_SIZE_M": 256}, _GEMM_ROWS)
 
 
 REGISTRY = {
