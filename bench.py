@@ -168,22 +168,45 @@ def suite_workload(kind: str, n: int = None) -> str:
 def rowreduce_workload(dev, n: int, seed: int, host: bool):
     from xb200 import ops as X
 
+    from xb200 import kernels
+
     rows = max(1, ROWS * n // N28)
     g = torch.Generator(device=dev).manual_seed(seed)
+    gh = torch.Generator().manual_seed(seed)
     out = []
+    blk = 16  # rows per program of the reference-signature launches
+    grid = (max(1, rows // blk),)
     for dt in (torch.bfloat16, torch.float32):
         eb = 2 if dt == torch.bfloat16 else 4
         x = (torch.randn(rows, COLS, generator=g, device=dev) * 3).to(dt)
         gm = (1 + 0.1 * torch.randn(COLS, generator=g, device=dev)).to(dt)
         bt = (0.1 * torch.randn(COLS, generator=g, device=dev)).to(dt)
         y = torch.empty_like(x)
+        hx = hg = hy = None
+        if host:
+            hx = (torch.randn(rows, COLS, generator=gh) * 3).to(dt).pin_memory()
+            hg = (1 + 0.1 * torch.randn(COLS, generator=gh)).to(dt).pin_memory()
+            hy = torch.empty_like(hx).pin_memory()
         t = _tag(dt)
         nb = 2 * rows * COLS * eb
+        io = {"h2d": rows * COLS * eb, "d2h": rows * COLS * eb}
         out += [
-            Op(f"softmax_{t}", nb, lambda x=x, y=y: X.softmax(x, out=y)),
-            Op(f"layernorm_{t}", nb + 2 * COLS * eb, lambda x=x, y=y, gm=gm, bt=bt: X.layernorm(x, gm, bt, 1e-5, out=y)),
-            Op(f"rms_norm_{t}", nb, lambda x=x, y=y: X.rms_norm(x, None, 1e-6, out=y)),
-            Op(f"weighted_rms_norm_{t}", nb + COLS * eb, lambda x=x, y=y, gm=gm: X.rms_norm(x, gm, 1e-6, out=y)),
+            Op(f"softmax_{t}", nb, lambda x=x, y=y: X.softmax(x, out=y),
+               lambda hx=hx, hy=hy: kernels.softmax_kernel[grid](hx, hy, COLS, 1, COLS, 1, COLS, BLOCK_SIZE=blk),
+               **io),
+            # the reference's fused layernorm kernel fixes gamma = 1, beta = 0
+            # (examples/test_layernorm/test_layernorm.py:46-47), so its launch
+            # moves 2 x 4096 fewer parameter bytes than the device line
+            Op(f"layernorm_{t}", nb + 2 * COLS * eb, lambda x=x, y=y, gm=gm, bt=bt: X.layernorm(x, gm, bt, 1e-5, out=y),
+               lambda hx=hx, hy=hy: kernels._layer_norm_fwd_fused[grid](hx, hy, COLS, 1, COLS, 1, COLS, 1e-5,
+                                                                        BLOCK_SIZE=blk), **io),
+            Op(f"rms_norm_{t}", nb, lambda x=x, y=y: X.rms_norm(x, None, 1e-6, out=y),
+               lambda hx=hx, hy=hy: kernels.rms_norm_kernel[grid](hx, hy, COLS, 1e-6, BLOCK_M=blk, BLOCK_N=COLS),
+               **io),
+            Op(f"weighted_rms_norm_{t}", nb + COLS * eb, lambda x=x, y=y, gm=gm: X.rms_norm(x, gm, 1e-6, out=y),
+               lambda hx=hx, hg=hg, hy=hy: kernels.weighted_rms_norm_kernel[grid](hx, hg, hy, COLS, 1e-6, BLOCK_M=blk,
+                                                                                  BLOCK_N=COLS),
+               h2d=rows * COLS * eb + COLS * eb, d2h=rows * COLS * eb),
         ]
     config = {"workload": suite_workload("rowreduce", n), "rows": rows,
               "cols": COLS, "l2": "every input > 126 MB L2 (no flush needed)"}
@@ -844,7 +867,7 @@ def main():
 
     _lib.load()
     dev = torch.device("cuda", torch.cuda.current_device())
-    want_e2e = rank == 0 and args.e2e_steps > 0 and args.workload == "elementwise"
+    want_e2e = rank == 0 and args.e2e_steps > 0 and args.workload in ("elementwise", "rowreduce")
     if args.workload in LLM_WORKLOADS:
         run_llm_bench(args, world, rank, local, dev, args.workload)
         if world > 1:
