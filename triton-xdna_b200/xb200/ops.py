@@ -740,21 +740,28 @@ _rope_halves: dict = {}
 def rope_tables_repeat_halves(cos_t, sin_t) -> bool:
     """Whether every row of both RoPE tables repeats its first half in its
     second (rotate-half tables built from duplicated frequencies); checked
-    once per pair of tables (keyed by their storage and version)."""
-    key = (cos_t.data_ptr(), sin_t.data_ptr(), cos_t.shape, cos_t._version, sin_t._version)
-    v = _rope_halves.get(key)
-    if v is None:
+    once per pair of tables (keyed by their address, shape, strides and
+    version; the entry keeps the tables alive, so no other tensor can take
+    their address while the answer is cached)."""
+    key = (cos_t.data_ptr(), sin_t.data_ptr(), cos_t.shape, cos_t.stride(), sin_t.stride(), cos_t._version,
+           sin_t._version)
+    hit = _rope_halves.get(key)
+    if hit is None:
         h = cos_t.shape[-1] // 2
         v = bool(torch.equal(cos_t[..., :h], cos_t[..., h:]) and torch.equal(sin_t[..., :h], sin_t[..., h:]))
-        _rope_halves[key] = v
-    return v
+        hit = _rope_halves[key] = (v, cos_t, sin_t)
+    return hit[0]
 
 
 def linear_qkv_rope(x, w_qkv, b_qkv, cos_t, sin_t, q_out, k_cache, v_cache, batch, seq, n_head, n_kv_head, head_dim,
-                    pos_offset):
+                    pos_offset, rope_dup: bool | None = None):
     """Prefill QKV projection + RoPE (none when the tables are None) + KV-cache
     write in one GEMM (the epilogue finishes each head slot): the results of
-    linear() followed by rope_kv(), without the qkv activations in memory."""
+    linear() followed by rope_kv(), without the qkv activations in memory.
+
+    ``rope_dup`` says that every table row repeats its first half in its
+    second (the epilogue then reads half rows); None checks the tables once
+    (a device comparison and a host read, cached per table pair)."""
     _cuda(x, w_qkv, b_qkv, cos_t, sin_t, q_out, k_cache, v_cache)
     if (cos_t is None) != (sin_t is None):
         raise ValueError("give both RoPE tables or neither")
@@ -762,11 +769,15 @@ def linear_qkv_rope(x, w_qkv, b_qkv, cos_t, sin_t, q_out, k_cache, v_cache, batc
         raise ValueError("RoPE tables are shorter than the positions")
     x2 = x.reshape(-1, x.shape[-1])
     K = x2.shape[1]
+    if cos_t is None:
+        dup = False
+    else:
+        dup = rope_tables_repeat_halves(cos_t, sin_t) if rope_dup is None else bool(rope_dup)
     _lib.call("xb_linear_rope_kv_bf16", x2.data_ptr(), w_qkv.data_ptr(),
               b_qkv.data_ptr() if b_qkv is not None else None,
               cos_t.data_ptr() if cos_t is not None else None, sin_t.data_ptr() if sin_t is not None else None,
-              int(cos_t is not None and rope_tables_repeat_halves(cos_t, sin_t)), q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), batch, seq, n_head, n_kv_head, head_dim,
-              k_cache.shape[2], pos_offset, K, _mat(x2, "x"), _mat(w_qkv, "w"), _stream())
+              int(dup), q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), batch, seq, n_head, n_kv_head,
+              head_dim, k_cache.shape[2], pos_offset, K, _mat(x2, "x"), _mat(w_qkv, "w"), _stream())
 
 
 def rope_kv(qkv, cos_t, sin_t, q_out, k_cache, v_cache, batch, seq, n_head, n_kv_head, head_dim, pos_offset):

@@ -177,8 +177,9 @@ class Qwen2Model:
             else:
                 xn = ops.rms_norm(x, L["input_ln"], c.rms_eps)
                 # QKV GEMM with RoPE + KV write in its epilogue
+                # rope_tables() concatenates the frequencies with themselves
                 ops.linear_qkv_rope(xn, L["qkv_w"], L["qkv_b"], self.cos, self.sin, q_buf, cache.k[i], cache.v[i],
-                                    B, S, H, KVH, HD, pos)
+                                    B, S, H, KVH, HD, pos, rope_dup=True)
             ops.attention(q_buf, cache.k[i], cache.v[i], attn, B, S, H, KVH, HD, pos, self.scale)
             if decode:
                 y, st = ops.decode_linear_residual(attn, L["o_w"], None, x, stats_kind="rms")
