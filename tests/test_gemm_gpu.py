@@ -311,6 +311,23 @@ def test_linear_residual_epilogue_equals_linear_then_add(M):
     _status_ok()
 
 
+@pytest.mark.parametrize("M", [300, 1000])
+def test_linear_residual_epilogue_unaligned_residual(M):
+    """A residual whose base is 2 bytes past a 16-byte boundary: the
+    whole-line epilogue (16-byte residual pieces) must not take it; the
+    per-row path gives the same bits as linear then add."""
+    g = torch.Generator().manual_seed(43)
+    x = (torch.randn(M, 896, generator=g) / 4).to(torch.bfloat16).cuda()
+    w = (torch.randn(896, 896, generator=g) / 16).to(torch.bfloat16).cuda()
+    rbig = torch.randn(M * 896 + 8, generator=g).to(torch.bfloat16).cuda()
+    r = rbig[1:1 + M * 896].view(M, 896)
+    assert r.data_ptr() % 16 == 2
+    fused = ops.linear(x, w, None, residual=r)
+    unfused = ops.vecadd(ops.linear(x, w, None), r.contiguous())
+    assert torch.equal(fused.cpu(), unfused.cpu())
+    _status_ok()
+
+
 @pytest.mark.parametrize("M", [1, 16, 64, 100, 300, 700])
 def test_interleaved_swiglu_linear_equals_unfused(M):
     """One GEMM with the SwiGLU in its epilogue (or the small-M split-K form)
