@@ -318,7 +318,9 @@ XB_API int xb_linear_rope_kv_bf16(const void* X, const void* W, const void* bias
 
 /* Y = residual + bf16(X @ W^T + bias) (bf16, any M): the linear with the
  * residual add fused into the GEMM epilogue (o_proj / down_proj of a
- * prefill; examples/qwen2_5/model.py:1045-1046, 1060-1061). */
+ * prefill; examples/qwen2_5/model.py:1045-1046, 1060-1061).  The residual
+ * may have any alignment; a 16-byte aligned base and row pitch take the
+ * faster whole-line epilogue. */
 XB_API int xb_linear_residual_bf16(const void* X, const void* W, const void* bias,
                                    const void* residual, void* Y, int64_t M,
                                    int64_t N, int64_t K, int64_t ldx,
