@@ -381,38 +381,9 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int local = 0;
-    // Whole-line residual epilogue: each lane's residual segments are fetched
-    // ahead of use -- chunks 0-2 of a tile while its main loop still runs,
-    // then chunk cc + 2 while chunk cc is finished -- so the chunks do not
-    // each wait out a global-load latency.  res[0..2] hold chunks cc..cc+2.
-    constexpr bool kResAhead = OUT == kOutBf16 && !TRANS && !PEERS;
-    constexpr int kChunks = C::BN / 32;
-    int4 res0[4], res1[4], res2[4];
-    const __nv_bfloat16* res_row = nullptr;  // this lane's residual row at the tile's first column
-    int res_cols = 0;                        // columns of the tile inside N
-    auto res_fetch = [&](int cc, int4* dst) {
-      if (res_row && cc < kChunks && cc * 32 + 32 <= res_cols) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) dst[j] = __ldg(reinterpret_cast<const int4*>(res_row + cc * 32) + j);
-      }
-    };
     for (int t = tile0; t < args.num_tiles; t += tstep, ++local) {
       const int buf = local % C::ACC_BUFS;
       const uint32_t tph = (local / C::ACC_BUFS) & 1;
-      if constexpr (kResAhead) {
-        res_row = nullptr;
-        if (args.c_tma && args.residual) {
-          int ptm, ptn;
-          tile_coords<GM>(t / args.splits, args.tiles_m, args.tiles_n, ptm, ptn);
-          const int prow = ptm * C::TILE_M + (int)crank * C::BM + q * 32 + lane;
-          res_cols = args.n - ptn * C::BN;
-          if (prow < args.m)
-            res_row = static_cast<const __nv_bfloat16*>(args.residual) + (int64_t)prow * args.ldr + ptn * C::BN;
-          res_fetch(0, res0);
-          res_fetch(1, res1);
-          res_fetch(2, res2);
-        }
-      }
       const bool got = PAIR ? mbar_wait_cl(&tfull_bar[buf], tph, kWaitLimit, &abort_flag)
                             : mbar_wait(&tfull_bar[buf], tph, kWaitLimit, &abort_flag);
       if (!got) {
@@ -430,16 +401,6 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * C::ACCS * C::BN;
 #pragma unroll 1
       for (int cc = 0; cc < C::BN / 32; ++cc) {
-        if constexpr (kResAhead) {
-          if (cc > 0) {  // shift the window: res0 = chunk cc, res2 = chunk cc + 2
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              res0[j] = res1[j];
-              res1[j] = res2[j];
-            }
-            res_fetch(cc + 2, res2);
-          }
-        }
         if constexpr (OUT == kOutQkv) {
           static_assert(!TRANS && !PEERS && C::BN % 64 == 0, "fused QKV epilogue: row-major tiles of whole heads");
           if (cc & 1) continue;  // the even chunk takes the whole 64-column head slot
@@ -701,10 +662,12 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
                     v[j] = __float_as_uint(gelu_tanh_bf16path(
                         __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[j])))));
                 }
-                if (args.residual && row < args.m) {  // residual + bf16(x W^T + b), fetched ahead
+                if (args.residual && row < args.m) {  // residual + bf16(x W^T + b)
+                  const __nv_bfloat16* rp =
+                      static_cast<const __nv_bfloat16*>(args.residual) + (int64_t)row * args.ldr + col0;
 #pragma unroll
                   for (int j = 0; j < 32; j += 8) {
-                    const int4 raw = res0[j / 8];
+                    const int4 raw = __ldg(reinterpret_cast<const int4*>(rp + j));
                     const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
                     for (int e = 0; e < 8; ++e)
