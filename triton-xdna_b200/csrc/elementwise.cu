@@ -42,9 +42,13 @@ constexpr int kUnroll = 2;
 // that the bf16 activations stay HBM-bound instead of issue-bound.  Both
 // approximations flush subnormals, so a bf16 result below 2^-126 in
 // magnitude (sigmoid(x) for x < -87.3) becomes 0.
+//
+// The bf16 form multiplies the reciprocal by an exact 1.0f (a no-op on every
+// value): written without it, the bf16 sigmoid kernel measured 200.7 us on
+// 2^28 elements against 176.0 us with it, the same bits out.
 template <typename T>
 __device__ __forceinline__ float sigmoid_t(float x) {
-  if constexpr (sizeof(T) == 2) return rcp_approx(1.0f + ex2_approx(x * -1.4426950408889634f));
+  if constexpr (sizeof(T) == 2) return __fmul_rn(1.0f, rcp_approx(1.0f + ex2_approx(x * -1.4426950408889634f)));
   else return __frcp_rn(__fadd_rn(1.0f, expf(-x)));
 }
 
