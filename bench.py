@@ -82,12 +82,20 @@ class Op:
         self.flops, self.peak_key = flops, peak_key
 
 
+def _pinned_copy(t):
+    """A pinned host copy of a device tensor: the end-to-end leg's inputs
+    (filled over PCIe, not by CPU random generation, so that every rank sets
+    up its host tensors in a second or two)."""
+    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    h.copy_(t)
+    return h
+
+
 def elementwise_workload(dev, n: int, seed: int, host: bool):
     from xb200 import kernels
     from xb200 import ops as X
 
     g = torch.Generator(device=dev).manual_seed(seed)
-    gh = torch.Generator().manual_seed(seed)
     half = n // 2
     out = []
     for dt in (torch.bfloat16, torch.float32):
@@ -97,9 +105,8 @@ def elementwise_workload(dev, n: int, seed: int, host: bool):
         o = torch.empty_like(x)
         hx = hy = ho = None
         if host:
-            hx = torch.randn(n, generator=gh).to(dt).pin_memory()
-            hy = torch.randn(n, generator=gh).to(dt).pin_memory()
-            ho = torch.empty_like(hx).pin_memory()
+            hx, hy = _pinned_copy(x), _pinned_copy(y)
+            ho = torch.empty(hx.shape, dtype=hx.dtype, pin_memory=True)
         t = _tag(dt)
         B = {"BLOCK_SIZE": 1024}
         grid = (max(1, n // 1024),)
@@ -134,8 +141,8 @@ def elementwise_workload(dev, n: int, seed: int, host: bool):
     pout = torch.empty((planes, H // 2, W // 2), device=dev)
     hpin = hpout = None
     if host:
-        hpin = torch.randn((planes, H, W), generator=gh).pin_memory()
-        hpout = torch.empty((planes, H // 2, W // 2)).pin_memory()
+        hpin = _pinned_copy(pin)
+        hpout = torch.empty((planes, H // 2, W // 2), pin_memory=True)
     nin, nout = planes * H * W, planes * (H // 2) * (W // 2)
     out.append(Op("avg_pool2d_2x2_f32", (nin + nout) * 4, lambda: X.avg_pool2d_2x2(pin, out=pout),
                   lambda: kernels.avg_pool2d_kernel[(planes,)](hpin, hpout, planes, H, W, BLOCK=1),
@@ -172,7 +179,6 @@ def rowreduce_workload(dev, n: int, seed: int, host: bool):
 
     rows = max(1, ROWS * n // N28)
     g = torch.Generator(device=dev).manual_seed(seed)
-    gh = torch.Generator().manual_seed(seed)
     out = []
     blk = 16  # rows per program of the reference-signature launches
     grid = (max(1, rows // blk),)
@@ -184,9 +190,8 @@ def rowreduce_workload(dev, n: int, seed: int, host: bool):
         y = torch.empty_like(x)
         hx = hg = hy = None
         if host:
-            hx = (torch.randn(rows, COLS, generator=gh) * 3).to(dt).pin_memory()
-            hg = (1 + 0.1 * torch.randn(COLS, generator=gh)).to(dt).pin_memory()
-            hy = torch.empty_like(hx).pin_memory()
+            hx, hg = _pinned_copy(x), _pinned_copy(gm)
+            hy = torch.empty(hx.shape, dtype=hx.dtype, pin_memory=True)
         t = _tag(dt)
         nb = 2 * rows * COLS * eb
         io = {"h2d": rows * COLS * eb, "d2h": rows * COLS * eb}
@@ -867,7 +872,9 @@ def main():
 
     _lib.load()
     dev = torch.device("cuda", torch.cuda.current_device())
-    want_e2e = rank == 0 and args.e2e_steps > 0 and args.workload in ("elementwise", "rowreduce")
+    # every rank runs the end-to-end leg (its own pinned host tensors and PCIe
+    # link); the job's figure is all ranks' bytes over the slowest rank's time
+    want_e2e = args.e2e_steps > 0 and args.workload in ("elementwise", "rowreduce")
     if args.workload in LLM_WORKLOADS:
         run_llm_bench(args, world, rank, local, dev, args.workload)
         if world > 1:
@@ -932,16 +939,18 @@ def main():
         for o in ops_list:
             o.e2e()
         torch.cuda.synchronize()
+        _barrier(world)
         t0 = time.perf_counter()
         for _ in range(args.e2e_steps):
             for o in ops_list:
                 o.e2e()
         torch.cuda.synchronize()
-        secs = (time.perf_counter() - t0) / args.e2e_steps
-        e2e = {"value": round(step_bytes / secs / 1e9, 3), "unit": "GB/s",
-               "h2d_bytes_per_step": sum(o.h2d for o in ops_list), "d2h_bytes_per_step": sum(o.d2h for o in ops_list),
+        secs = _max_over_ranks((time.perf_counter() - t0) / args.e2e_steps, world)
+        e2e = {"value": round(world * step_bytes / secs / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": world * sum(o.h2d for o in ops_list),
+               "d2h_bytes_per_step": world * sum(o.d2h for o in ops_list),
                "ms_per_step": round(secs * 1e3, 2),
-               "api": "xb200.kernels.<reference kernel>[grid](pinned host tensors...)"}
+               "api": "xb200.kernels.<reference kernel>[grid](pinned host tensors...), every rank"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
