@@ -222,10 +222,11 @@ XB_API int xb_matmul_i16(const void* A, const void* B, void* C, int64_t M,
  * (held on every GPU that loads the library until the process exits). */
 #define XB_I16_NOALLOC_SCRATCH_BYTES (32u * 1024u * 1024u)
 
-/* xb_matmul_i16 for callers that cannot allocate device memory (a stream
- * being captured into a CUDA graph, a host framework that owns every device
- * allocation, a path where an allocation could stall).  No counterpart in the
- * reference.  The int8 limb planes go to a fixed XB_I16_NOALLOC_SCRATCH_BYTES
+/* xb_matmul_i16 for callers that cannot allocate device memory: plugins
+ * whose host framework owns every device allocation through its own pool
+ * (memory taken behind its back breaks its accounting and limits), and
+ * latency-bound paths where a cudaMalloc may synchronise the device and
+ * stall.  No counterpart in the reference.  The int8 limb planes go to a fixed XB_I16_NOALLOC_SCRATCH_BYTES
  * array inside the library instead of a caller workspace; a product needing
  * more than that (xb_matmul_i16_workspace_size) is rejected with
  * XB_ERR_UNSUPPORTED.  Nothing is allocated.  The first call on a device looks
@@ -489,16 +490,29 @@ XB_API int xb_peer_free(void* ptr, char* err, size_t errlen);
  * B_shard[K,N_shard] (int8 -> int32, or bf16 -> bf16 with fp32
  * accumulation) and stores every output tile into the C of EVERY rank
  * (C_ranks[r]: rank r's C [M, ldc] as mapped in this process) with plain
- * stores over NVLink; when its grid is done it adds 1 to slot `rank` of every
- * peer's signal buffer (signal_ranks[r]: uint64 [world + 1], zero-initialised
- * peer memory).  Wait for the peers with xb_peer_wait.  The caller must make
- * sure no rank still reads the previous contents of C.  world <= 8. */
+ * stores over NVLink.  Signal buffers (signal_ranks[r]: rank r's uint64
+ * [2 * world + 1], zero-initialised peer memory, one per C) hold in slot p
+ * the calls whose block from rank p has landed, in slot `world` a CTA
+ * counter, in slot world + 1 + p the calls rank p has started.
+ *
+ * `epoch` is the 1-based number of this call on these buffers (every rank
+ * passes the same value).  At its start the kernel adds 1 to slot
+ * world + 1 + rank of every peer (this rank's C may be overwritten: every
+ * earlier kernel on `stream`, including readers of the previous C, has
+ * completed); before its first store into peer p's C it waits, for at most
+ * timeout_ns, until p has done the same for this epoch.  So back-to-back
+ * calls never overwrite a C that a peer still reads on its stream.  When its
+ * grid is done it adds 1 to slot `rank` of every peer; wait for the peers with
+ * xb_peer_wait.  A wait that runs out records XB_ERR_TIMEOUT
+ * (xb_device_status), skips every store and withholds the completion
+ * signal, so the peers' xb_peer_wait times out too; the buffers must then be
+ * re-created.  world <= 8. */
 XB_API int xb_matmul_sharded(const void* A, const void* B_shard,
                              void* const* C_ranks, void* const* signal_ranks,
                              int world, int rank, int64_t M, int64_t N_shard,
                              int64_t K, int64_t lda, int64_t ldb, int64_t ldc,
-                             int dtype, void* stream, char* err,
-                             size_t errlen);
+                             uint64_t epoch, uint64_t timeout_ns, int dtype,
+                             void* stream, char* err, size_t errlen);
 
 /* Enqueue a wait until every other rank's slot in this rank's signal buffer
  * reaches `epoch` (the number of sharded GEMMs issued so far); gives up

@@ -3,6 +3,7 @@ processes) exercise the column sharding and the re-layout of all-gathered
 blocks that the NCCL baseline of the N-sharded GEMM uses, and the batch
 sharding of the LLM."""
 
+import ctypes
 import os
 import socket
 
@@ -59,8 +60,13 @@ def test_sharded_gemm_layout_with_two_gloo_ranks():
 def test_sharded_entry_rejects_bad_world_without_a_gpu():
     from xb200 import _lib
 
-    with pytest.raises(_lib.XbError) as e:
-        _lib.call("xb_matmul_sharded", 16, 16, None, None, 9, 0, 8, 8, 8, 8, 8, 64, 0, None)
+    with pytest.raises(_lib.XbError) as e:  # world 9 > 8
+        _lib.call("xb_matmul_sharded", 16, 16, None, None, 9, 0, 8, 8, 8, 8, 8, 64, 1, 10**9, 0, None)
     assert e.value.code == _lib.XB_ERR_INVALID
+    cp = (ctypes.c_void_p * 2)(16, 16)
+    with pytest.raises(_lib.XbError) as e:  # epoch 0: the first call on a signal buffer is epoch 1
+        _lib.call("xb_matmul_sharded", 16, 16, ctypes.cast(cp, ctypes.c_void_p), ctypes.cast(cp, ctypes.c_void_p),
+                  2, 0, 8, 8, 8, 8, 8, 16, 0, 10**9, 0, None)
+    assert e.value.code == _lib.XB_ERR_INVALID and "epoch" in e.value.message
     with pytest.raises(_lib.XbError):
         _lib.call("xb_peer_wait", None, 2, 0, 1, 1000, None)

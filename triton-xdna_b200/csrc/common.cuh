@@ -45,11 +45,14 @@ inline int check_launch(const char* what, char* err, size_t errlen) {
 inline int sm_count(int* out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return -1;
-  static int cached[64] = {0};
-  if (dev >= 0 && dev < 64 && cached[dev] > 0) { *out = cached[dev]; return 0; }
+  static std::atomic<int> cached[64];  // zero-initialised (static storage)
+  if (dev >= 0 && dev < 64) {
+    const int c = cached[dev].load(std::memory_order_relaxed);
+    if (c > 0) { *out = c; return 0; }
+  }
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
-  if (dev >= 0 && dev < 64) cached[dev] = n;
+  if (dev >= 0 && dev < 64) cached[dev].store(n, std::memory_order_relaxed);
   *out = n;
   return 0;
 }
@@ -157,17 +160,60 @@ inline std::atomic<unsigned long long>& launch_counter() {
   return n;
 }
 
+constexpr int kMaxDevices = 64;
+
+// Set-up done once per (kernel, what, device).  Kernel attributes set with
+// cudaFuncSetAttribute belong to the device that was current at the call, so
+// a process that drives several GPUs must set them on each one.  The registry
+// is shared by every translation unit of the library and guarded by a mutex
+// (host threads may launch concurrently).
+struct OnceEntry {
+  const void* key;
+  int what, dev, value;
+};
+struct OnceRegistry {
+  std::mutex mu;
+  std::vector<OnceEntry> done;
+};
+inline OnceRegistry& once_registry() {
+  static OnceRegistry r;
+  return r;
+}
+enum : int { kOnceCarveout = 0, kOnceSmem = 1 };
+
+// Runs setup(&value) the first time (key, what) is seen on the current device
+// and stores `value`; later calls on that device return the stored value
+// through *value.  A failed set-up is not recorded (the next call retries).
+template <typename F>
+inline cudaError_t once_per_device(const void* key, int what, F&& setup, int* value = nullptr) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  OnceRegistry& r = once_registry();
+  std::lock_guard<std::mutex> lock(r.mu);
+  for (const OnceEntry& o : r.done)
+    if (o.key == key && o.what == what && o.dev == dev) {
+      if (value) *value = o.value;
+      return cudaSuccess;
+    }
+  int v = 0;
+  e = setup(&v);
+  if (e != cudaSuccess) return e;
+  r.done.push_back({key, what, dev, v});
+  if (value) *value = v;
+  return cudaSuccess;
+}
+
 // Every kernel of the library prefers the largest shared-memory carveout, so
 // consecutive kernels never force an SM to drain and reconfigure its L1 /
 // shared split (which would serialise them despite programmatic launch).
 inline void prefer_max_smem(const void* fn) {
-  static std::mutex mu;
-  static std::vector<const void*> done;
-  std::lock_guard<std::mutex> lock(mu);
-  for (const void* f : done)
-    if (f == fn) return;
-  cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
-  done.push_back(fn);
+  once_per_device(fn, kOnceCarveout, [fn](int*) {
+    cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+    cudaGetLastError();  // a preference only: a refusal is not an error of the launch
+    return cudaSuccess;
+  });
 }
 
 // kMaxSmem = false keeps the default carveout: the streaming elementwise and

@@ -7,7 +7,7 @@
 // their grids in multiples of it).
 #include "common.cuh"
 
-extern "C" int xb_abi_version(void) { return 1; }
+extern "C" int xb_abi_version(void) { return 2; }
 
 extern "C" int xb_device_name(int device, char* buf, size_t buf_len, int* sm_count, char* err, size_t errlen) {
   if (!buf || buf_len == 0) {

@@ -136,7 +136,9 @@ struct Args {
   int rope_dup;  // 1: every table row's second half repeats its first (read the first only)
   int world, rank;
   void* peers[8];
-  uint64_t* signals[8];  // each rank's signal buffer (uint64 [world + 1])
+  uint64_t* signals[8];  // each rank's signal buffer (uint64 [2 * world + 1], layout in peer.cu)
+  uint64_t epoch;        // 1-based number of this sharded call on this rank
+  uint64_t peer_timeout_ns;  // limit of the wait for a peer's release of its C
 };
 
 constexpr int kGroupM = 16;  // tile raster: groups of 16 M-tiles sweep N (L2 reuse)
@@ -156,6 +158,30 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 // c * ldc + r); with A = W and B = X this computes Y = X W^T for few tokens.
 __device__ __forceinline__ void red_release_sys_add(uint64_t* p, uint64_t v) {
   asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Sharded GEMM: before this rank's first store into peer pe's C, peer pe
+// must have released the previous call's C, i.e. its own stream must have
+// reached this call's GEMM (which releases at its start, after every earlier
+// kernel on that stream -- the readers of the previous C -- completed).
+// Polls this rank's own signal buffer (peers write their release counts into
+// it); false when a peer has not released within the call's time limit.
+__device__ __forceinline__ bool wait_peer_releases(const Args& args) {
+  const uint64_t* rel = args.signals[args.rank] + args.world + 1;
+  const uint64_t t0 = globaltimer_ns();
+  for (int pe = 0; pe < args.world; ++pe) {
+    if (pe == args.rank) continue;
+    while (ld_acquire_sys_u64(rel + pe) < args.epoch) {
+      if (globaltimer_ns() - t0 > args.peer_timeout_ns) return false;
+      __nanosleep(256);
+    }
+  }
+  return true;
 }
 
 template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false>
@@ -289,9 +315,11 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
         }
       }
       if (leader) {
-        // Drain: every load issued into a stage must have landed before exit.
+        // Drain: every load issued into a stage must have landed before exit
+        // (also after an abort; one time limit for all stages).
+        const uint64_t deadline = globaltimer_ns() + kWaitLimit;
         for (int s = 0; s < C::STAGES; ++s)
-          if (issued[s] && !mbar_wait(&full_bar[s], (issued[s] - 1) & 1, kWaitLimit, &abort_flag)) fail();
+          if (issued[s] && !mbar_wait_deadline(&full_bar[s], (issued[s] - 1) & 1, deadline)) fail();
       } else if (!ok) {
         // The odd CTA's loads complete on the leader's barriers: after a
         // failure give any load still in flight time to land (loads take
@@ -374,14 +402,30 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       if (any) {
         if constexpr (PAIR) tc_commit2(smem_u32(&drain_bar));
         else tc_commit(&drain_bar);
-        if (!mbar_wait(&drain_bar, 0, kWaitLimit, &abort_flag)) fail();
+        // every issued MMA has completed before TMEM is released (also after an abort)
+        if (!mbar_wait_deadline(&drain_bar, 0, globaltimer_ns() + kWaitLimit)) fail();
       }
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     int local = 0;
-    for (int t = tile0; t < args.num_tiles; t += tstep, ++local) {
+    int first_tile = tile0;
+    if constexpr (PEERS) {
+      // CTA 0 tells every peer that this rank's C is free for this call
+      // (everything before this kernel on the stream has completed).
+      if (blockIdx.x == 0 && warp == 2 && lane == 0)
+        for (int pe = 0; pe < args.world; ++pe)
+          if (pe != args.rank) red_release_sys_add(args.signals[pe] + args.world + 1 + args.rank, 1ull);
+      bool ok = true;
+      if (lane == 0) ok = wait_peer_releases(args);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) {
+        fail();
+        first_tile = args.num_tiles;  // no tile of this warp is stored anywhere
+      }
+    }
+    for (int t = first_tile; t < args.num_tiles; t += tstep, ++local) {
       const int buf = local % C::ACC_BUFS;
       const uint32_t tph = (local / C::ACC_BUFS) & 1;
       const bool got = PAIR ? mbar_wait_cl(&tfull_bar[buf], tph, kWaitLimit, &abort_flag)
@@ -821,13 +865,21 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
   if constexpr (PEERS) __threadfence_system();  // this thread's peer stores, before the CTA is counted done
   __syncthreads();
   if constexpr (PEERS) {
-    if (threadIdx.x == 0 && !abort_flag) {
+    // Every CTA counts itself once, aborted or not, so the counter always
+    // returns to zero at the end of a call; an aborted CTA also adds 2^32.
+    // The last CTA signals the peers only when no CTA aborted: a peer then
+    // times out in its wait (an error status) instead of reading a C whose
+    // tiles were partly skipped.
+    if (threadIdx.x == 0) {
       uint64_t* done = args.signals[args.rank] + args.world;
-      const unsigned long long prev = atomicAdd(reinterpret_cast<unsigned long long*>(done), 1ull);
-      if (prev == gridDim.x - 1) {  // last CTA of the grid: every tile of this rank has landed everywhere
-        __threadfence_system();
-        for (int pe = 0; pe < args.world; ++pe)
-          if (pe != args.rank) red_release_sys_add(args.signals[pe] + args.rank, 1ull);
+      const unsigned long long add = abort_flag ? (1ull << 32) + 1ull : 1ull;
+      const unsigned long long prev = atomicAdd(reinterpret_cast<unsigned long long*>(done), add);
+      if ((prev & 0xffffffffull) == gridDim.x - 1) {  // last CTA of the grid
+        if ((prev >> 32) == 0 && !abort_flag) {  // every tile of this rank has landed everywhere
+          __threadfence_system();
+          for (int pe = 0; pe < args.world; ++pe)
+            if (pe != args.rank) red_release_sys_add(args.signals[pe] + args.rank, 1ull);
+        }
         *done = 0;  // no CTA of this grid touches it again; ready for the next call
       }
     }
@@ -1290,6 +1342,7 @@ struct PeerArgs {
   int world = 1, rank = 0;
   void* peers[8] = {nullptr};
   uint64_t* signals[8] = {nullptr};
+  uint64_t epoch = 0, timeout_ns = 0;
 };
 
 // Launch with clusters of two CTAs (and programmatic dependent launch when enabled).
@@ -1360,6 +1413,8 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
     args.peers[i] = pa ? pa->peers[i] : nullptr;
     args.signals[i] = pa ? pa->signals[i] : nullptr;
   }
+  args.epoch = pa ? pa->epoch : 0;
+  args.peer_timeout_ns = pa ? pa->timeout_ns : 0;
   // 4-byte outputs of whole-tile GEMMs leave through the TMA-store epilogue
   // when C meets the TMA alignment rules.
   // Transposed (small-M) outputs too, through [tokens][features] staging tiles.
@@ -1404,31 +1459,33 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
     args.c_tma = ok ? 1 : 0;
   }
   auto kernel = gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS, PEERS, PAIR>;
-  static bool attr_set = false;
-  static int max_clusters = 0;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    if (e == cudaSuccess && PAIR) {
-      // resident pairs: the persistent grid is sized to what runs at once
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(2);
-      cfg.blockDim = dim3(192);
-      cfg.dynamicSmemBytes = kSmem;
-      cudaLaunchAttribute attr;
-      attr.id = cudaLaunchAttributeClusterDimension;
-      attr.val.clusterDim.x = 2;
-      attr.val.clusterDim.y = 1;
-      attr.val.clusterDim.z = 1;
-      cfg.attrs = &attr;
-      cfg.numAttrs = 1;
-      e = cudaOccupancyMaxActiveClusters(&max_clusters, kernel, &cfg);
-      if (e == cudaSuccess && max_clusters < 1) e = cudaErrorInvalidConfiguration;
-    }
+  // shared-memory limit and (pairs) the resident cluster count, once per device
+  int max_clusters = 0;
+  {
+    cudaError_t e = once_per_device(reinterpret_cast<const void*>(kernel), kOnceSmem, [&](int* v) {
+      cudaError_t r = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+      if (r == cudaSuccess && PAIR) {
+        // resident pairs: the persistent grid is sized to what runs at once
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2);
+        cfg.blockDim = dim3(192);
+        cfg.dynamicSmemBytes = kSmem;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        r = cudaOccupancyMaxActiveClusters(v, kernel, &cfg);
+        if (r == cudaSuccess && *v < 1) r = cudaErrorInvalidConfiguration;
+      }
+      return r;
+    }, &max_clusters);
     if (e != cudaSuccess) {
       set_err(err, errlen, "%s: kernel setup: %s", what, cudaGetErrorString(e));
       return XB_ERR_CUDA;
     }
-    attr_set = true;
   }
   int sms = 148;
   sm_count(&sms);
@@ -1620,10 +1677,11 @@ extern "C" int xb_matmul_i16(const void* A, const void* B, void* C, int64_t M, i
 // ---------------------------------------------------------------------------
 // int16 GEMM for callers that cannot allocate device memory.
 //
-// Some callers cannot call cudaMalloc at all: code running while a CUDA graph
-// is being captured, plugins whose host framework owns every device
-// allocation through its own pool, or real-time paths where an allocation
-// could stall.  xb_matmul_i16 needs a caller-provided workspace for its int8
+// Some callers cannot call cudaMalloc at all: plugins whose host framework
+// owns every device allocation through its own pool (memory taken behind its
+// back breaks its accounting and limits), and latency-bound paths where a
+// cudaMalloc may synchronise the device and stall.  xb_matmul_i16 needs a
+// caller-provided workspace for its int8
 // limb planes; this variant instead keeps them in a fixed-size array compiled
 // into the library (XB_I16_NOALLOC_SCRATCH_BYTES per GPU, resident on every
 // GPU that loads this module until the process exits).  The caller still
@@ -1946,9 +2004,11 @@ __global__ void __launch_bounds__(192, 1) decode_linear_kernel(const __grid_cons
         tma_load_2d(smem + s * kDecStage + kDecA, &maps.x, &full_bar[s], (kb0 + i) * kDecBK, 0);
         issued = i + 1;
       }
-      // every load issued must have landed before the ring is reused or the CTA exits
+      // every load issued must have landed before the ring is reused or the CTA
+      // exits (also after an abort; one time limit for all of them)
+      const uint64_t deadline = globaltimer_ns() + kWaitLimit;
       for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i)
-        if (!mbar_wait(&full_bar[i % STAGES], (i / STAGES) & 1, kWaitLimit, &abort_flag)) fail();
+        if (!mbar_wait_deadline(&full_bar[i % STAGES], (i / STAGES) & 1, deadline)) fail();
     } else {
       pdl_wait();
       pdl_trigger();
@@ -2427,14 +2487,14 @@ int launch_decode(const DecInput& in, const void* W, int64_t N, int64_t K, int64
       xn ? (deep ? decode_linear_kernel<FIN, 7, true> : decode_linear_kernel<FIN, 3, true>)
          : (deep ? decode_linear_kernel<FIN, 7, false> : decode_linear_kernel<FIN, 3, false>);
   const int smem = (deep ? 7 : 3) * kDecStage + kDecRecvBytes + 1024;
-  static bool attr_set[2][2] = {{false, false}, {false, false}};
-  if (!attr_set[xn][deep]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  {
+    cudaError_t e = once_per_device(reinterpret_cast<const void*>(kernel), kOnceSmem, [&](int*) {
+      return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    });
     if (e != cudaSuccess) {
       set_err(err, errlen, "%s: kernel setup: %s", what, cudaGetErrorString(e));
       return XB_ERR_CUDA;
     }
-    attr_set[xn][deep] = true;
   }
   cudaError_t e = launch_clusters(kernel, (unsigned)(blocks * args.splits), (unsigned)args.splits, 192, smem, s, maps,
                                   args);
@@ -3127,11 +3187,16 @@ extern "C" int xb_linear_argmax_bf16(const void* X, const void* W, int64_t M, in
 
 extern "C" int xb_matmul_sharded(const void* A, const void* B_shard, void* const* C_ranks, void* const* signal_ranks,
                                  int world, int rank, int64_t M, int64_t N_shard, int64_t K, int64_t lda, int64_t ldb,
-                                 int64_t ldc, int dtype, void* stream, char* err, size_t errlen) {
+                                 int64_t ldc, uint64_t epoch, uint64_t timeout_ns, int dtype, void* stream, char* err,
+                                 size_t errlen) {
   const char* what = "xb_matmul_sharded";
   cudaStream_t s = (cudaStream_t)stream;
   if (world < 1 || world > 8 || rank < 0 || rank >= world || !C_ranks || !signal_ranks) {
     set_err(err, errlen, "%s: world must be 1..8 with a C and a signal pointer per rank", what);
+    return XB_ERR_INVALID;
+  }
+  if (epoch == 0 || timeout_ns == 0) {
+    set_err(err, errlen, "%s: epoch (1 for the first call on a signal buffer) and timeout_ns must be positive", what);
     return XB_ERR_INVALID;
   }
   if (ldc < (int64_t)world * N_shard) {
@@ -3157,6 +3222,8 @@ extern "C" int xb_matmul_sharded(const void* A, const void* B_shard, void* const
   PeerArgs pa;
   pa.world = world;
   pa.rank = rank;
+  pa.epoch = epoch;
+  pa.timeout_ns = timeout_ns;
   for (int r = 0; r < world; ++r) {
     if (!C_ranks[r] || !signal_ranks[r]) {
       set_err(err, errlen, "%s: null peer pointer for rank %d", what, r);

@@ -1186,13 +1186,10 @@ extern "C" int xb_rope_kv_bf16(const void* qkv, const float* cos_t, const float*
 template <int R>
 static cudaError_t launch_head(dim3 grid, cudaStream_t s, const bf16* q, const bf16* k, const bf16* v, int H, int KVH,
                                int smax, int total, float scale_log2, bf16* out) {
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(attn_decode_head_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  cudaError_t e = xb::once_per_device(reinterpret_cast<const void*>(attn_decode_head_kernel<R>), xb::kOnceSmem, [](int*) {
+    return cudaFuncSetAttribute(attn_decode_head_kernel<R>, cudaFuncAttributeMaxDynamicSharedMemorySize, kHeadSmem);
+  });
+  if (e != cudaSuccess) return e;
   return launch_k(attn_decode_head_kernel<R>, grid, kHeadWarps * 32, kHeadSmem, s, q, k, v, H, KVH, smax, total,
                   scale_log2, out);
 }

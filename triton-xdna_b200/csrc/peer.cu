@@ -8,9 +8,12 @@
 // buffer.  A peer then waits -- bounded -- until every rank's counter reaches
 // the epoch of the call.
 //
-// Signal buffer of a rank: uint64 [world + 1]; slot r counts the calls whose
-// shard from rank r has fully landed here; slot `world` is the rank's own
-// CTA-completion counter (the last CTA of the GEMM grid sends the signals).
+// Signal buffer of a rank: uint64 [2 * world + 1]; slot r counts the calls
+// whose shard from rank r has fully landed here; slot `world` is the rank's
+// own CTA-completion counter (the last CTA of the GEMM grid sends the
+// signals); slot world + 1 + r counts the calls rank r has started, i.e. how
+// many times rank r has released its C for overwriting (the GEMM waits on
+// these before its first store into rank r's C).
 #include "common.cuh"
 
 namespace xb {

@@ -52,6 +52,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
   }
 }
 
+// Exit drain: wait for a phase regardless of any abort (asynchronous copies
+// or MMAs still in flight must finish before the CTA leaves), until the
+// globaltimer reaches `deadline_ns`.  Returns false at the deadline.
+__device__ __forceinline__ bool mbar_wait_deadline(uint64_t* bar, uint32_t parity, uint64_t deadline_ns) {
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255) == 255 && globaltimer_ns() > deadline_ns) return false;
+  }
+}
+
 // ---- CTA pairs (clusters of two CTAs sharing one MMA) ------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

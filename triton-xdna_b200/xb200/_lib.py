@@ -32,6 +32,8 @@ XB_ERR_CUDA = -2
 XB_ERR_UNSUPPORTED = -3
 XB_ERR_TIMEOUT = -4
 
+XB_DT_BF16, XB_DT_F32, XB_DT_I8, XB_DT_I16, XB_DT_I32 = 0, 1, 2, 3, 4
+
 _ERR_NAMES = {
     XB_ERR_INVALID: "XB_ERR_INVALID",
     XB_ERR_CUDA: "XB_ERR_CUDA",

@@ -102,9 +102,18 @@ class ShardedMatmul:
     every rank ending with the full C.
 
     `run` issues one fused kernel per rank (GEMM tiles stored into every
-    rank's C over NVLink, then a release signal to each peer) and a bounded
-    wait for the peers' signals.  Successive calls reuse C: run them in
-    lockstep (all ranks call `run` the same number of times)."""
+    rank's C over NVLink, then a completion signal to each peer) and a
+    bounded wait for the peers' signals; it returns `out`, this rank's C.
+    All ranks call `run` the same number of times.
+
+    Successive calls reuse C and are stream-ordered: a call's kernel first
+    tells every peer that this rank's C may be overwritten (every earlier
+    kernel on the current stream, e.g. a reader of the previous `out`, has
+    completed) and stores into a peer's C only after that peer has done the
+    same for this call.  So work that reads `out` before the next `run` must
+    be enqueued on the same stream (or ordered before it with an event).
+    A wait that runs out is reported by `status()`; the plan must then be
+    closed and rebuilt."""
 
     def __init__(self, m: int, n: int, k: int, dtype=torch.bfloat16, group=None, timeout_s: float = 10.0):
         if dtype not in (torch.bfloat16, torch.int8):
@@ -118,7 +127,7 @@ class ShardedMatmul:
         self.out_dtype = torch.int32 if dtype == torch.int8 else torch.bfloat16
         osz = 4 if dtype == torch.int8 else 2
         self.c = PeerBuffer(m * n * osz, group)
-        self.sig = PeerBuffer(8 * (self.world + 1), group)
+        self.sig = PeerBuffer(8 * (2 * self.world + 1), group)
         self.epoch = 0
         self.timeout_ns = int(timeout_s * 1e9)
         self._c_ptrs = (ctypes.c_void_p * self.world)(*self.c.ptrs)
@@ -134,15 +143,21 @@ class ShardedMatmul:
         self.epoch += 1
         _lib.call("xb_matmul_sharded", a.data_ptr(), b_shard.data_ptr(), ctypes.cast(self._c_ptrs, ctypes.c_void_p),
                   ctypes.cast(self._s_ptrs, ctypes.c_void_p), self.world, self.rank, self.m, self.n_shard, self.k,
-                  a.stride(0), b_shard.stride(0), self.n, dt, _stream())
+                  a.stride(0), b_shard.stride(0), self.n, self.epoch, self.timeout_ns, dt, _stream())
         _lib.call("xb_peer_wait", self.sig.ptrs[self.rank], self.world, self.rank, self.epoch, self.timeout_ns,
                   _stream())
         return self.out
 
     def status(self) -> int:
+        """0, or the first error recorded since the last call (synchronises the
+        stream and clears the status words): XB_ERR_TIMEOUT when a peer's
+        completion signal (xb_peer_wait) or its release of C (the GEMM
+        kernel) did not come in time."""
         st = ctypes.c_int(0)
         _lib.call("xb_peer_status", _stream(), ctypes.byref(st))
-        return st.value
+        dev = ctypes.c_int(0)
+        _lib.call("xb_device_status", _stream(), ctypes.byref(dev))
+        return st.value or dev.value
 
     def close(self):
         torch.cuda.synchronize()
