@@ -1,29 +1,34 @@
 """Benchmark of the xb200 operator set on B200.
 
-Default workload (N=1): the elementwise / activation suite on flat tensors of
-2^28 elements, x, y ~ N(0, 1) from a seed -- vec-add, axpy (alpha 2.5), relu,
-leaky_relu (0.01), gelu (tanh form), sigmoid, silu in bf16 and fp32, swiglu
-on 2^27 + 2^27, and 2x2 / stride-2 average pooling of a [64, 256, 224, 224]
-fp32 tensor.  One step = one pass of every operator over its inputs
-(17 kernel launches).  Every input is larger than L2 (126 MB), so no flush is
-needed between steps.
+Headline (the default, ``--workload gemm``): the int8 GEMM, int32
+accumulate / output, at M = N = K = 16384 with A, B uniform over
+[-128, 127] from a seed.  One step = 16 products C_j = A_j B_j, cycling over
+4 resident operand sets (every operand is larger than L2, so no flush is
+needed).  N = 1 runs the single-GPU tcgen05 kernel; N > 1 runs the N-sharded
+kernel (rank r computes columns [r N/P, (r+1) N/P) and its epilogue stores
+them into every rank's C over NVLink), so every rank ends with every full C
+and the total work is the same at every N (strong scaling).  Before timing,
+every rank checks its full C of every operand set: exact int64 row / column
+checksums, sampled rows against an fp64 product, and (N > 1) equality with
+the single-GPU product; a mismatch exits non-zero.
 
-Other workloads (``--workload``) measure the remaining operator rows with the
-same machinery: ``rowreduce`` (softmax, layernorm, rms_norm,
-weighted_rms_norm on [32768, 4096] bf16 and fp32), ``gemm`` (the int8 /
-int16 / bf16 GEMM sweep; N-sharded over the ranks when N > 1), ``qwen`` and
-``gpt2`` (batch 64 x 512-token prefill + 128 greedy decode steps of the
-Qwen2.5-0.5B and GPT-2 124M architectures with random-init weights,
-batch-sharded over the ranks; metric tokens/s).
+The same process then measures the metric's other rows as extra keys
+(``--no-extras`` skips them): the GEMM sweep (int8 / int8 linear / int16 /
+bf16 at 4096^3 .. 16384^3 and the 16 x 8192 x 8192 decode shape; N > 1: the
+fused sharded kernel against the NCCL all-gather baseline), the row
+reductions (softmax, layernorm, rms_norm, weighted_rms_norm on
+[32768, 4096] bf16 + f32), the elementwise / activation suite (2^28
+elements) and the Qwen2.5-0.5B forward (batch 64 x 512-token prefill + 128
+greedy decode steps, batch-sharded over the ranks).
 
-Metric: algorithmic HBM bytes (each input read once, each output written
-once) per second, aggregated over the step and over all ranks.
+Other workloads (``--workload``): ``elementwise``, ``rowreduce``,
+``gemm-sweep``, ``qwen``, ``gpt2`` print their own line.
 
 Contract:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl xb200|reference]
-Multi-GPU (torchrun, one rank per GPU): every rank runs its own full suite
-(weak scaling, no data-path collective); the time is the max over ranks.
-``--impl reference`` times the examples' PyTorch CPU expressions (the oracle
-port of the reference's CPU path) on the host cores.
+Multi-GPU: torchrun, one rank per GPU over NCCL; times are CUDA events on
+each rank, max over ranks.  ``--impl reference`` times the reference's CPU
+path (the examples' own CPU expressions, restated in the oracle) on the host
+cores on the same sample the xb200 line's ``cpu_baseline`` uses.
 """
 
 from __future__ import annotations
@@ -45,19 +50,36 @@ N28 = 1 << 28
 POOL_SHAPE = (64, 256, 224, 224)
 ROWS, COLS = 32768, 4096
 
+# headline GEMM
+HEAD_MNK = 16384
+HEAD_SETS = 4  # resident operand sets (A, B, C), cycled
+HEAD_PRODUCTS = 16  # products per step
+CPU_SAMPLE_ROWS = 512  # CPU legs: these rows of A times the full B (same N, K as the headline)
+METRIC = "GEMM TOPS (i8/bf16) % of TC peak; norm/softmax GB/s % HBM; LLM tokens/s"
+
 
 def _peaks() -> dict:
+    """Roofline denominators: the measured copy bandwidth and bf16 GEMM rate
+    of this pool's B200s.  Dense int8 runs at twice the bf16 rate on sm_100
+    (4.5 vs 2.25 POPS nominal); no int8 rate is measured, so the int8
+    denominator is twice the measured bf16 burst rate (the nominal 4.5 POPS
+    fraction is reported beside it)."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        pk = {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    else:
+        pk = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+    pk["i8_tops"] = 2.0 * pk["bf16_tflops"]
+    pk["i8_tops_source"] = f"2 x {pk['source']} bf16 TFLOP/s"
+    pk["i8_tops_nominal"] = 4500.0
+    return pk
 
 
 # DRAM traffic per launch / algorithmic bytes, from one ncu capture of the
-# kernel on a smaller case of the same workload (traffic scales with the
-# units processed); see the named summary under profiles/.
+# kernel (traffic scales with the units processed); see the named summary
+# under profiles/.
 MEASURED_TRAFFIC_RATIO = {
     "avg_pool2d_2x2_f32": (1000.5 / 1027.6, "profiles/avg_pool2d_f32_16x256x224x224.md"),
 }
@@ -69,10 +91,10 @@ def _tag(dt):
 
 # ----------------------------------------------------------------------------- workloads
 #
-# A workload is a list of ops.  Each op has a name, its algorithmic bytes, a
-# device launch (closure over device-resident tensors) and, for the headline
-# workload, a launch through the public reference-signature API on pinned
-# host tensors (for the end-to-end number).
+# A suite workload is a list of ops.  Each op has a name, its algorithmic
+# bytes, a device launch (closure over device-resident tensors) and a launch
+# through the public reference-signature API on pinned host tensors (for the
+# end-to-end number).
 
 
 class Op:
@@ -89,7 +111,6 @@ def _pinned_copy(t):
     h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
     h.copy_(t)
     return h
-
 
 def elementwise_workload(dev, n: int, seed: int, host: bool):
     from xb200 import kernels
@@ -267,15 +288,6 @@ def gemm_workload(dev, n: int, seed: int, host: bool):
     return out, config, "GEMM TOPS", "i8/i16/bf16"
 
 
-def qwen_workload(dev, n: int, seed: int, host: bool):
-    return [], {"workload": "Qwen2.5-0.5B architecture, random-init bf16 weights (seed 0): batch 64 x 512-token "
-                            "random-id prefill + 128 greedy decode steps, batch-sharded over ranks"}, \
-        "LLM tokens/s", "bf16"
-
-
-WORKLOADS = {"elementwise": elementwise_workload, "rowreduce": rowreduce_workload, "gemm": gemm_workload,
-             "qwen": qwen_workload, "gpt2": qwen_workload}
-
 
 def llm_flops_bytes(kind, cfg, B, S, ctx_end):
     """Algorithmic work of an LLM forward: prefill FLOPs (linears over all
@@ -309,7 +321,11 @@ def _llm_model(kind, dev):
     return cfg, GPT2Model(random_weights(cfg, seed=0), cfg, device=dev)
 
 
-def run_llm_bench(args, world, rank, local, dev, kind):
+def llm_bench(args, world, rank, local, dev, kind, steps, warmup, cpu_leg):
+    """Batch B x S prompt prefill + `new` greedy decode steps (CUDA-graph
+    replays), batch-sharded over the ranks (replicated weights, no
+    collective).  Returns the line (tokens/s over all ranks, max-over-ranks
+    times)."""
     from xb200 import ops as X
 
     B_total, S, new = args.qwen_batch, args.qwen_prompt, args.qwen_new
@@ -332,14 +348,14 @@ def run_llm_bench(args, world, rank, local, dev, kind):
     def step():
         return model.generate(ids, new, cache=cache, graphs=graphs)
 
-    for _ in range(max(1, args.warmup)):
+    for _ in range(max(1, warmup)):
         step()
     peaks = _peaks()
     pre, dec = [], []
     _barrier(world)
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
-        for _ in range(args.steps):
+        for _ in range(steps):
             _, t = step()
             pre.append(t["prefill_ms"])
             dec.append(t["decode_ms"])
@@ -366,34 +382,35 @@ def run_llm_bench(args, world, rank, local, dev, kind):
     total_tps = B_total * (S + new) / ((pre_ms + dec_ms) * 1e-3)
     tflops = flops / (pre_ms * 1e-3) / 1e12
     dec_gbs = dec_bytes * (new - 1) / (dec_ms * 1e-3) / 1e9
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = llm_cpu_baseline(kind, cfg)
-    if rank == 0:
-        print(json.dumps({
-            "metric": "LLM tokens/s (prefill + decode)", "value": round(total_tps, 1), "unit": "tokens/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(pre_ms + dec_ms, 2), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic random ids, random-init weights (seed 0)",
-            "config": {"workload": f"{LLM_WORKLOADS[kind]}: batch {B_total} x {S} prefill + {new} greedy decode",
-                       "global_batch": B_total, "seq_len": S, "new_tokens": new,
-                       "parallelism": f"batch-sharded x{world} (replicated weights, no collective)",
-                       "l2": "weights re-read every step; decode steps replay CUDA graphs"},
-            "prefill_tokens_per_s": round(prefill_tps, 1), "decode_tokens_per_s": round(decode_tps, 1),
-            "prefill_ms": round(pre_ms, 2), "decode_ms": round(dec_ms, 2),
-            "roofline": {"bound": "tensor (prefill) / hbm (decode)",
-                         "prefill": {"achieved": round(tflops, 1), "unit": "TFLOP/s", "peak": peaks["bf16_tflops"],
-                                     "frac": round(tflops / peaks["bf16_tflops"], 4)},
-                         "decode": {"achieved": round(dec_gbs, 1), "unit": "GB/s", "peak": peaks["hbm_gbs"],
-                                    "frac": round(dec_gbs / peaks["hbm_gbs"], 4)},
-                         "peak_source": peaks["source"]},
-            "e2e": {"value": round(B_total * (S + new) / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
-                    "h2d_bytes_per_step": ids_host.numel() * 8 * world,
-                    "d2h_bytes_per_step": toks_host.numel() * 8 * world, "ms_per_step": round(e2e_ms, 2),
-                    "api": f"{type(model).__name__}.generate(ids copied from pinned host memory) -> tokens to host"},
-            "gpu_launches": launches_per_step * args.steps,
-            "cpu_baseline": cpu, "clocks": clk.summary(),
-        }))
+    cpu = llm_cpu_baseline(kind, cfg) if cpu_leg else None
+    del graphs, model, cache
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return {
+        "metric": "LLM tokens/s (prefill + decode)", "value": round(total_tps, 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": steps, "warmup": warmup,
+        "ms_per_step": round(pre_ms + dec_ms, 2), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic random ids, random-init weights (seed 0)",
+        "config": {"workload": f"{LLM_WORKLOADS[kind]}: batch {B_total} x {S} prefill + {new} greedy decode",
+                   "global_batch": B_total, "seq_len": S, "new_tokens": new,
+                   "parallelism": f"batch-sharded x{world} (replicated weights, no collective)",
+                   "l2": "weights re-read every step; decode steps replay CUDA graphs"},
+        "prefill_tokens_per_s": round(prefill_tps, 1), "decode_tokens_per_s": round(decode_tps, 1),
+        "prefill_ms": round(pre_ms, 2), "decode_ms": round(dec_ms, 2),
+        "roofline": {"bound": "tensor (prefill) / hbm (decode)",
+                     "prefill": {"achieved": round(tflops, 1), "unit": "TFLOP/s", "peak": peaks["bf16_tflops"],
+                                 "frac": round(tflops / peaks["bf16_tflops"], 4)},
+                     "decode": {"achieved": round(dec_gbs, 1), "unit": "GB/s", "peak": peaks["hbm_gbs"],
+                                "frac": round(dec_gbs / peaks["hbm_gbs"], 4)},
+                     "peak_source": peaks["source"]},
+        "e2e": {"value": round(B_total * (S + new) / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": ids_host.numel() * 8 * world,
+                "d2h_bytes_per_step": toks_host.numel() * 8 * world, "ms_per_step": round(e2e_ms, 2),
+                "api": f"{LLM_WORKLOADS[kind].split(' (')[0]} generate(ids copied from pinned host memory) -> tokens "
+                       "to host"},
+        "gpu_launches": launches_per_step * steps,
+        "cpu_baseline": cpu, "clocks": clk.summary(),
+    }
 
 
 def llm_cpu_baseline(kind, cfg):
@@ -421,196 +438,459 @@ def llm_cpu_baseline(kind, cfg):
             "sample": "1 sequence: 128-token prefill + 4 greedy decode steps through the oracle forward"}
 
 
-def run_gemm_sharded_bench(args, world, rank, local, dev):
-    """N-sharded GEMMs over `world` GPUs: the fused kernel (GEMM epilogue
-    stores into every rank's C over NVLink) and the NCCL all-gather baseline,
-    each timed with CUDA events on every rank (max over ranks); TOPS counts
-    the whole M x N x K product."""
+
+WORKLOADS = {"elementwise": elementwise_workload, "rowreduce": rowreduce_workload, "gemm-sweep": gemm_workload,
+             "qwen": None, "gpt2": None}
+
+
+
+# ----------------------------------------------------------------------------- headline: int8 GEMM
+
+
+def headline_config() -> dict:
+    """The headline workload as both arms describe it (identical at every N)."""
+    return {"workload": f"int8 GEMM C = A @ B, M = N = K = {HEAD_MNK}, int32 accumulate and output, "
+                        f"A and B uniform over [-128, 127]; one step = {HEAD_PRODUCTS} products cycling over "
+                        f"{HEAD_SETS} resident operand sets",
+            "M": HEAD_MNK, "N": HEAD_MNK, "K": HEAD_MNK, "dtype": "int8 -> int32",
+            "products_per_step": HEAD_PRODUCTS, "operand_sets": HEAD_SETS,
+            "l2": "every operand > 126 MB L2 (A, B 256 MiB, C 1 GiB): no flush needed"}
+
+
+def _int_checksums_ok(c, a, b) -> bool:
+    """Exact check of every element of C = A B (int8 operands, so |C| < 2^28
+    and int64 sums are exact): row sums C 1 = A (B 1) and column sums
+    1^T C = (1^T A) B, in 2048-row bands to bound the int64 temporaries."""
+    M = c.shape[0]
+    b_rowsum = b.to(torch.int64).sum(1)
+    col_want = torch.zeros(c.shape[1], dtype=torch.int64, device=c.device)
+    col_got = torch.zeros_like(col_want)
+    a_colsum = a.to(torch.int64).sum(0)
+    for r0 in range(0, M, 2048):
+        cb = c[r0:r0 + 2048].to(torch.int64)
+        if not torch.equal(cb.sum(1), (a[r0:r0 + 2048].to(torch.int64) * b_rowsum).sum(1)):
+            return False
+        col_got += cb.sum(0)
+    for k0 in range(0, a.shape[1], 2048):
+        col_want += (a_colsum[k0:k0 + 2048, None] * b[k0:k0 + 2048].to(torch.int64)).sum(0)
+    return torch.equal(col_got, col_want)
+
+
+def _sampled_rows_ok(c, a, b, seed) -> bool:
+    """Eight rows against an fp64 product (exact: |partial sums| < 2^28)."""
+    rows = torch.randint(0, a.shape[0], (8,), generator=torch.Generator().manual_seed(seed)).to(c.device)
+    want = (a[rows].double() @ b.double()).to(torch.int64)
+    return torch.equal(c[rows].to(torch.int64), want)
+
+
+def _gen_set(j, dev, M, N, K):
+    g = torch.Generator(device=dev).manual_seed(100 + j)
+    a = torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=torch.int8)
+    b = torch.randint(-128, 128, (K, N), generator=g, device=dev, dtype=torch.int8)
+    return a, b
+
+
+def gemm_headline(args, world, rank, local, dev) -> dict:
+    from xb200 import ops as X
+
+    M = N = K = HEAD_MNK
+    P = args.products
+    nsets = min(HEAD_SETS, P)
+    stream = torch.cuda.current_stream()
+    peaks = _peaks()
+    plans = []
+    sets = []
+    if world == 1:
+        for j in range(nsets):
+            a, b = _gen_set(j, dev, M, N, K)
+            c = torch.empty((M, N), dtype=torch.int32, device=dev)
+            sets.append((a, b, c))
+
+        def run(j):
+            a, b, c = sets[j]
+            X.matmul_i8(a, b, out=c)
+            return c
+        parallelism = "single GPU"
+    else:
+        from xb200.dist import ShardedMatmul, shard_columns
+
+        s0, ns = shard_columns(N, world)[rank]
+        for j in range(nsets):
+            a, b = _gen_set(j, dev, M, N, K)
+            sets.append((a, b[:, s0:s0 + ns].contiguous(), None))
+            del b
+            plans.append(ShardedMatmul(M, N, K, torch.int8))
+
+        def run(j):
+            return plans[j].run(sets[j][0], sets[j][1])
+        parallelism = (f"N-sharded x{world}: each rank computes {N // world} columns and its GEMM epilogue stores "
+                       f"them into every rank's C over NVLink (all-gather fused, no NCCL on the data path)")
+
+    # ---- parity: every rank's full C of every operand set, before timing
+    checks = []
+    for j in range(nsets):
+        c = run(j)
+        torch.cuda.synchronize()
+        a = sets[j][0]
+        _, b_full = _gen_set(j, dev, M, N, K)
+        ok = _int_checksums_ok(c, a, b_full) and _sampled_rows_ok(c, a, b_full, j)
+        if world > 1:
+            ok = ok and torch.equal(c, X.matmul_i8(a, b_full))
+            ok = ok and plans[j].status() == 0
+        ok = ok and X.device_status() == 0
+        checks.append(bool(ok))
+        del b_full
+        torch.cuda.empty_cache()
+    if not all(checks):
+        print(json.dumps({"error": "headline GEMM parity check failed", "rank": rank, "checks": checks}),
+              file=sys.stderr)
+        raise SystemExit(3)
+
+    for i in range(max(3, args.warmup)):
+        run(i % nsets)
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps x P products, per-launch CUDA events on the launching stream
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps * P)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = X.launch_count()
+    _barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for i in range(args.steps * P):
+            evs[i][0].record(stream)
+            run(i % nsets)
+            evs[i][1].record(stream)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    launches = X.launch_count() - n0
+    _barrier(world)
+    total_ms = _max_over_ranks(start.elapsed_time(stop), world)
+    launch_ms = _max_over_ranks(statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs), world)
+    status = [p.status() for p in plans] + [X.device_status()]
+    if any(status):
+        print(json.dumps({"error": "device status after timing", "rank": rank, "status": status}), file=sys.stderr)
+        raise SystemExit(3)
+    ms_per_step = total_ms / args.steps
+    ops_per_step = P * 2 * M * N * K
+    value = ops_per_step / (ms_per_step * 1e-3) / 1e12
+    rank_ops = 2 * M * (N // world) * K  # this rank's share of one product
+    achieved = rank_ops / (launch_ms * 1e-3) / 1e12
+    alg_bytes = M * K + K * (N // world) + 4 * M * N  # A, B shard read once; full C written once per rank
+
+    e2e = None
+    if args.e2e_steps > 0:
+        e2e = gemm_headline_e2e(args, world, rank, dev, sets, plans)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, threads, desc = gemm_cpu_sample()
+        cpu = {"value": round(v, 4), "unit": "TOPS", "cores": threads, "kind": "port", "sample": desc}
+    for p in plans:
+        p.close()
+    del sets, plans
+    torch.cuda.empty_cache()
+    traffic = HEADLINE_TRAFFIC.get(world)
+    return {
+        "metric": METRIC, "value": round(value, 1), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+        "warmup": max(3, args.warmup), "ms_per_step": round(ms_per_step, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic, uniform int8, seeds 100..103",
+        "config": headline_config(), "parallelism": parallelism,
+        "parity": {"checked_before_timing": True, "operand_sets": nsets,
+                   "checks": "int64 row+column checksums of every element, 8 rows vs fp64"
+                             + (", equality with the single-GPU product" if world > 1 else ""),
+                   "ok": True},
+        "roofline": {"bound": "tensor", "kernel": "gemm_kernel<int8, CTA pairs" + (", peer stores>" if world > 1
+                                                                                    else ">"),
+                     "achieved": round(achieved, 1), "peak": peaks["i8_tops"], "peak_source": peaks["i8_tops_source"],
+                     "unit": "TOPS", "frac": round(achieved / peaks["i8_tops"], 4),
+                     "frac_of_nominal_4500": round(achieved / peaks["i8_tops_nominal"], 4),
+                     "launch_ms": round(launch_ms, 4), "ops_per_launch": rank_ops,
+                     "traffic": traffic[0] if traffic else None,
+                     "traffic_source": traffic[1] if traffic else None, "algorithmic_bytes": alg_bytes},
+        "e2e": e2e, "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
+    }
+
+
+# ncu dram__bytes_read.sum + dram__bytes_write.sum of one headline launch (per
+# rank), keyed by world size; see the named summary under profiles/.
+HEADLINE_TRAFFIC = {}
+
+
+def gemm_headline_e2e(args, world, rank, dev, sets, plans) -> dict:
+    """The headline through the public API with host buffers, every product
+    copying its inputs from pinned host memory and its result back.
+    N = 1: `bare_matmul_i8[grid](A, B, C)` on pinned host tensors (the
+    launcher uploads B, then pieces of A's rows, and brings C's rows back,
+    the copies of consecutive pieces overlapping).  N > 1: every rank uploads
+    A and its B shard, runs the sharded GEMM, and brings back its 1/N band of
+    C's rows (each rank holds the full C; the bands together are C), so the
+    host-side result is spread over the N PCIe links."""
+    from xb200 import kernels
+
+    M = N = K = HEAD_MNK
+    P = args.products
+    a_dev, b_dev, c_dev = sets[0]
+    ha = _pinned_copy(a_dev)
+    hb = _pinned_copy(b_dev)
+    if world == 1:
+        hc = torch.empty((M, N), dtype=torch.int32, pin_memory=True)
+        grid = (M // 128, N // 64)
+
+        def product(j):
+            kernels.bare_matmul_i8[grid](ha, hb, hc, M, N, K, K, 1, N, 1, N, 1, BLOCK_SIZE_M=128, BLOCK_SIZE_N=64,
+                                         BLOCK_SIZE_K=K)
+        h2d, d2h = P * (M * K + K * N), P * M * N * 4
+        api = "xb200.kernels.bare_matmul_i8[grid](pinned host A, B, C, ...)"
+    else:
+        rows = M // world
+        hc = torch.empty((rows, N), dtype=torch.int32, pin_memory=True)
+
+        def product(j):
+            a, bs, _ = sets[j]
+            a.copy_(ha, non_blocking=True)
+            bs.copy_(hb, non_blocking=True)
+            c = plans[j].run(a, bs)
+            hc.copy_(c[rank * rows:(rank + 1) * rows], non_blocking=True)
+        h2d, d2h = world * P * (M * K + K * (N // world)), P * M * N * 4
+        api = ("xb200.dist.ShardedMatmul.run with A and the B shard copied from pinned host memory and each "
+               "rank's band of C's rows copied back, every rank")
+    nsets = len(sets)
+    for j in range(2):
+        product(j % nsets)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.e2e_steps):
+        _barrier(world)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for i in range(P):
+            product(i % nsets)
+        torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+    secs = _max_over_ranks(statistics.mean(times), world)
+    return {"value": round(P * 2 * M * N * K / secs / 1e12, 1), "unit": "TOPS", "ms_per_step": round(secs * 1e3, 2),
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "api": api}
+
+
+_CPU_SAMPLE = {}  # seed -> (A rows, B): generated once per process
+
+
+def gemm_cpu_sample(rows: int = CPU_SAMPLE_ROWS, seed: int = 100):
+    """The reference's CPU path for the headline: the example's int32 GEMM
+    (restated in plain C, OpenMP over every host thread) on `rows` rows of A
+    times a full B of the headline's N and K; TOPS = 2 rows N K / time.
+    Inputs from a CPU generator (the same sample in both arms)."""
+    from oracle import cgemm
+
+    threads = os.cpu_count() or 1
+    if seed not in _CPU_SAMPLE:
+        g = torch.Generator().manual_seed(seed)
+        b = torch.randint(-128, 128, (HEAD_MNK, HEAD_MNK), generator=g, dtype=torch.int8)
+        a = torch.randint(-128, 128, (CPU_SAMPLE_ROWS, HEAD_MNK), generator=g, dtype=torch.int8)
+        _CPU_SAMPLE[seed] = (a, b)
+    a, b = _CPU_SAMPLE[seed]
+    a = a[:rows]
+    cgemm.gemm_int(a[:8], b)  # warm-up (and build check)
+    t0 = time.perf_counter()
+    cgemm.gemm_int(a, b)
+    secs = time.perf_counter() - t0
+    return (2 * rows * HEAD_MNK * HEAD_MNK / secs / 1e12, threads,
+            f"int8 {rows} x {HEAD_MNK} x {HEAD_MNK} (rows of A times the full B of the headline shape) through "
+            f"the oracle's C GEMM, {threads} threads")
+
+
+# ----------------------------------------------------------------------------- GEMM sweep (extras)
+
+SWEEP_EXTRA = [(4096, 4096, 4096), (8192, 8192, 8192), (16384, 16384, 16384), (16, 8192, 8192)]
+
+
+def gemm_sweep_single(args, dev, sizes, kinds, library: bool) -> dict:
+    """Per-GEMM timing on one GPU: L2 flushed (256 MB write) before each
+    launch, CUDA events around it, median of the repetitions; cuBLAS bf16 /
+    int8 GEMMs timed the same way as reference lines."""
+    from xb200 import ops as X
+
+    peaks = _peaks()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    ops_list = [o for o in gemm_workload(dev, N28, 0, False)[0]
+                if (o.name.split("_")[1] in kinds) and tuple(map(int, o.name.split("_")[2].split("x"))) in sizes]
+    if args.only:
+        ops_list = [o for o in ops_list if args.only in o.name]
+    reps = max(3, min(10, args.steps // 2))
+    res = {}
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        times = []
+        for _ in range(reps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            times.append(e0.elapsed_time(e1))
+        return statistics.median(times)
+
+    for op in ops_list:
+        fn, keep = op.make()
+        ms = timed(fn)
+        tops = op.flops / (ms * 1e-3) / 1e12
+        res[op.name] = {"ms": round(ms, 4), "tops": round(tops, 1), "frac": round(tops / peaks[op.peak_key], 3),
+                        "peak_key": op.peak_key}
+        del fn, keep
+        torch.cuda.empty_cache()
+    if library:  # cuBLAS reference lines (library GEMMs, not the product)
+        for n in (8192, 16384):
+            a = torch.randn((n, n), device=dev).to(torch.bfloat16)
+            b = torch.randn((n, n), device=dev).to(torch.bfloat16)
+            ai = torch.randint(-128, 128, (n, n), device=dev, dtype=torch.int8)
+            bi = torch.randint(-128, 128, (n, n), device=dev, dtype=torch.int8)
+            for name, fn in ((f"cublas_bf16_{n}", lambda: a @ b), (f"cublas_int8_{n}", lambda: torch._int_mm(ai, bi))):
+                ms = timed(fn)
+                res[name] = {"ms": round(ms, 4), "tops": round(2 * n ** 3 / (ms * 1e-3) / 1e12, 1), "library": True}
+            del a, b, ai, bi
+            torch.cuda.empty_cache()
+    X.device_status()
+    return {"unit": "TOPS", "l2": "flushed before every launch", "peaks": {k: peaks[k] for k in
+                                                                          ("bf16_tflops", "i8_tops")}, "ops": res}
+
+
+def gemm_sweep_sharded(args, world, rank, dev, sizes) -> dict:
+    """N-sharded GEMMs over the ranks: the fused kernel (epilogue stores into
+    every rank's C over NVLink) against the NCCL all-gather baseline, CUDA
+    events on every rank, max over ranks; TOPS counts the whole product."""
     from xb200.dist import ShardedMatmul, nccl_sharded_matmul, shard_columns
 
     peaks = _peaks()
-    peaks["i8_tops"] = 4500.0
     stream = torch.cuda.current_stream()
-    sizes = [(4096, 4096, 4096), (8192, 8192, 8192), (16384, 16384, 16384), (16, 8192, 8192)]
+    reps = max(3, min(10, args.steps // 2))
     res = {}
-    with ClockSampler(local) as clk:
-        for dt in (torch.int8, torch.bfloat16):
-            for (M, N, K) in sizes:
-                if args.only and args.only not in f"{M}":
-                    continue
-                g = torch.Generator(device=dev).manual_seed(0)
-                if dt == torch.int8:
-                    a = torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=dt)
-                    b = torch.randint(-128, 128, (K, N), generator=g, device=dev, dtype=dt)
-                else:
-                    a = torch.randn((M, K), generator=g, device=dev).to(dt)
-                    b = torch.randn((K, N), generator=g, device=dev).to(dt)
-                s0, ns = shard_columns(N, world)[rank]
-                bs = b[:, s0:s0 + ns].contiguous()
-                del b
-                sm = ShardedMatmul(M, N, K, dt)
-                tag = "i8" if dt == torch.int8 else "bf16"
-                for name, fn in ((f"sharded_fused_{tag}_{M}x{N}x{K}", lambda: sm.run(a, bs)),
-                                 (f"sharded_nccl_{tag}_{M}x{N}x{K}", lambda: nccl_sharded_matmul(a, bs))):
-                    for _ in range(max(3, args.warmup)):
-                        fn()
-                    times = []
-                    for _ in range(max(3, args.steps // 3)):
-                        _barrier(world)
-                        torch.cuda.synchronize()
-                        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                        e0.record(stream)
-                        fn()
-                        e1.record(stream)
-                        torch.cuda.synchronize()
-                        times.append(_max_over_ranks(e0.elapsed_time(e1), world))
-                    ms = statistics.median(times)
-                    tops = 2 * M * N * K / (ms * 1e-3) / 1e12
-                    pk = peaks["i8_tops"] if tag == "i8" else peaks["bf16_tflops"]
-                    res[name] = {"ms": round(ms, 4), "tops": round(tops, 1), "frac_of_world_peak":
-                                 round(tops / (pk * world), 3)}
-                st = sm.status()
-                if st != 0:
-                    raise RuntimeError(f"peer wait timed out (status {st})")
-                sm.close()
-                del a, bs
-                torch.cuda.empty_cache()
-    big = "sharded_fused_bf16_16384x16384x16384"
-    if rank == 0:
-        print(json.dumps({
-            "metric": "GEMM TOPS (N-sharded, all-gather of C fused into the epilogue)",
-            "value": res.get(big, {}).get("tops"), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "i8/bf16", "data": "synthetic, seed 0",
-            "config": {"workload": "GEMM M=N=K in {4096, 8192, 16384} + 16x8192x8192, N-sharded, full C on every rank",
-                       "parallelism": f"N-shard x{world}, peer-store all-gather over NVLink (NCCL path timed beside)"},
-            "ops": res, "clocks": clk.summary(),
-        }))
-
-
-def run_gemm_bench(args, ops_list, config, world, rank, local, dev):
-    """Per-GEMM timing: L2 flush, then CUDA events around each launch; the
-    cuBLAS bf16 / int8 GEMMs are timed the same way as reference lines."""
-    peaks = _peaks()
-    peaks["i8_tops"] = 4500.0  # nominal dense int8 (no measured value in MEASURED_PEAKS.json)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream()
-    res = {}
-    if args.only:
-        ops_list = [o for o in ops_list if args.only in o.name]
-    from xb200 import ops as X
-
-    launches = 0
-    with ClockSampler(local) as clk:
-        for op in ops_list:
-            fn, keep = op.make()
-            for _ in range(max(3, args.warmup)):
-                fn()
-            times = []
-            n0 = X.launch_count()
-            for _ in range(max(3, args.steps // 3)):
-                flush.zero_()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                fn()
-                e1.record(stream)
-                torch.cuda.synchronize()
-                times.append(e0.elapsed_time(e1))
-            launches += X.launch_count() - n0
-            ms = statistics.median(times)
-            tops = op.flops / (ms * 1e-3) / 1e12
-            res[op.name] = {"ms": round(ms, 4), "tops": round(tops, 1),
-                            "frac": round(tops / peaks[op.peak_key], 3), "peak_key": op.peak_key}
-            del fn, keep
-            torch.cuda.empty_cache()
-        # cuBLAS reference lines (library GEMMs, not the product)
-        ref = {}
-        for n in (() if args.no_library else (4096, 8192, 16384)):
-            a = torch.randn((n, n), device=dev).to(torch.bfloat16)
-            b = torch.randn((n, n), device=dev).to(torch.bfloat16)
-            ref[f"torch.matmul_bf16_{n}"] = a @ b
-            ai = torch.randint(-128, 128, (n, n), device=dev, dtype=torch.int8)
-            bi = torch.randint(-128, 128, (n, n), device=dev, dtype=torch.int8)
-            for name, fn, fl in ((f"cublas_bf16_{n}", lambda: a @ b, 2 * n ** 3),
-                                 (f"cublas_int8_{n}", lambda: torch._int_mm(ai, bi), 2 * n ** 3)):
+    for dt in (torch.int8, torch.bfloat16):
+        for (M, N, K) in sizes:
+            g = torch.Generator(device=dev).manual_seed(0)
+            if dt == torch.int8:
+                a = torch.randint(-128, 128, (M, K), generator=g, device=dev, dtype=dt)
+                b = torch.randint(-128, 128, (K, N), generator=g, device=dev, dtype=dt)
+            else:
+                a = torch.randn((M, K), generator=g, device=dev).to(dt)
+                b = torch.randn((K, N), generator=g, device=dev).to(dt)
+            s0, ns = shard_columns(N, world)[rank]
+            bs = b[:, s0:s0 + ns].contiguous()
+            del b
+            sm = ShardedMatmul(M, N, K, dt)
+            tag = "i8" if dt == torch.int8 else "bf16"
+            for name, fn in ((f"sharded_fused_{tag}_{M}x{N}x{K}", lambda: sm.run(a, bs)),
+                             (f"sharded_nccl_{tag}_{M}x{N}x{K}", lambda: nccl_sharded_matmul(a, bs))):
                 for _ in range(3):
                     fn()
                 times = []
-                for _ in range(5):
-                    flush.zero_()
+                for _ in range(reps):
+                    _barrier(world)
+                    torch.cuda.synchronize()
                     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     e0.record(stream)
                     fn()
                     e1.record(stream)
                     torch.cuda.synchronize()
-                    times.append(e0.elapsed_time(e1))
+                    times.append(_max_over_ranks(e0.elapsed_time(e1), world))
                 ms = statistics.median(times)
-                res[name] = {"ms": round(ms, 4), "tops": round(fl / (ms * 1e-3) / 1e12, 1), "library": True}
-            del a, b, ai, bi
-            ref.clear()
+                tops = 2 * M * N * K / (ms * 1e-3) / 1e12
+                pk = peaks["i8_tops"] if tag == "i8" else peaks["bf16_tflops"]
+                res[name] = {"ms": round(ms, 4), "tops": round(tops, 1), "frac_of_world_peak":
+                             round(tops / (pk * world), 3)}
+            st = sm.status()
+            if st != 0:
+                raise RuntimeError(f"sharded GEMM status {st}")
+            sm.close()
+            del a, bs
             torch.cuda.empty_cache()
-    clocks = clk.summary()
-    big = "gemm_bf16_8192x8192x8192"
-    e2e = gemm_e2e(dev, args.e2e_steps) if (big in res and args.e2e_steps > 0) else None
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        v, threads, desc = gemm_cpu_baseline()
-        cpu = {"value": round(v, 4), "unit": "TOPS", "cores": threads, "kind": "port", "sample": desc}
-    line = {
-        "metric": "GEMM TOPS", "value": res[big]["tops"] if big in res else None, "unit": "TOPS", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "i8/i16/bf16", "data": "synthetic, seed 0", "config": config,
-        "roofline": {"bound": "tensor", "kernel": big, "achieved": res.get(big, {}).get("tops"),
-                     "peak": peaks["bf16_tflops"], "peak_source": peaks["source"], "unit": "TFLOP/s",
-                     "frac": res.get(big, {}).get("frac"), "traffic": None},
-        "ops": res, "clocks": clocks, "gpu_launches": launches, "e2e": e2e, "cpu_baseline": cpu,
-    }
-    if rank == 0:
-        print(json.dumps(line))
+    return {"unit": "TOPS", "parallelism": f"N-shard x{world}", "ops": res}
 
 
-def gemm_e2e(dev, steps):
-    """bf16 8192^3 through the reference-signature launcher with pinned host
-    operands, every step: B uploaded whole, then row pieces of A uploaded,
-    multiplied and their rows of C brought back, the copies of consecutive
-    pieces overlapping; wall clock around each call (it returns with C in host
-    memory)."""
-    from xb200 import kernels
+# ----------------------------------------------------------------------------- suites (elementwise, rows)
 
-    n = 8192
-    g = torch.Generator().manual_seed(0)
-    ha = torch.randn((n, n), generator=g).to(torch.bfloat16).pin_memory()
-    hb = torch.randn((n, n), generator=g).to(torch.bfloat16).pin_memory()
-    hc = torch.empty((n, n), dtype=torch.bfloat16).pin_memory()
-    grid = (n // 256, n // 256)
-    times = []
-    for i in range(steps + 1):
+
+def time_suite(kind, args, world, rank, local, dev, steps, warmup, with_e2e: bool, cpu_leg: bool) -> dict:
+    """Every operator of a suite once per step (weak scaling: every rank runs
+    the whole suite on its own data), per-launch CUDA events; the line's
+    value is all ranks' algorithmic bytes over the slowest rank's time."""
+    ops_list, config, metric, dtype = WORKLOADS[kind](dev, args.elements, rank, with_e2e)
+    config["launches_per_step"] = len(ops_list)
+    config["parallelism"] = f"weak x{world} (independent replicas, no collective)"
+    step_bytes = sum(o.nbytes for o in ops_list)
+    config["bytes_per_step"] = step_bytes
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        for o in ops_list:
+            o.run()
+    torch.cuda.synchronize()
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in ops_list]
+           for _ in range(steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for s in range(steps):
+            for i, o in enumerate(ops_list):
+                evs[s][i][0].record(stream)
+                o.run()
+                evs[s][i][1].record(stream)
+        stop.record(stream)
         torch.cuda.synchronize()
+    _barrier(world)
+    total_ms = _max_over_ranks(start.elapsed_time(stop), world)
+    per_op_ms = {o.name: statistics.mean(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(steps))
+                 for i, o in enumerate(ops_list)}
+    ms_per_step = total_ms / steps
+    value = step_bytes * world / (ms_per_step * 1e-3) / 1e9
+    peaks = _peaks()
+    hbm = peaks["hbm_gbs"]
+    dom = max(ops_list, key=lambda o: per_op_ms[o.name])
+    dom_gbs = dom.nbytes / (per_op_ms[dom.name] * 1e-3) / 1e9
+    detail = {o.name: {"ms": round(per_op_ms[o.name], 4), "gbs": round(o.nbytes / (per_op_ms[o.name] * 1e-3) / 1e9, 1),
+                       "frac": round(o.nbytes / (per_op_ms[o.name] * 1e-3) / 1e9 / hbm, 3)} for o in ops_list}
+    e2e = None
+    if with_e2e:
+        for o in ops_list:
+            o.e2e()
+        torch.cuda.synchronize()
+        _barrier(world)
         t0 = time.perf_counter()
-        kernels.bare_matmul[grid](ha, hb, hc, n, n, n, n, 1, n, 1, n, 1, 256, 256, 64)
-        if i:
-            times.append((time.perf_counter() - t0) * 1e3)
-    ms = statistics.mean(times)
-    return {"value": round(2 * n ** 3 / (ms * 1e-3) / 1e12, 1), "unit": "TOPS", "ms_per_step": round(ms, 3),
-            "h2d_bytes_per_step": 2 * n * n * 2, "d2h_bytes_per_step": n * n * 2,
-            "api": "xb200.kernels.bare_matmul[grid](pinned host A, B, C, ...) (bf16 8192^3)"}
-
-
-def gemm_cpu_baseline():
-    """The int8 GEMM of the oracle (plain-C int32 accumulation, OpenMP over
-    every host thread) on a 2048^3 sample; TOPS = 2 M N K / time."""
-    from oracle import cgemm
-
-    threads = os.cpu_count() or 1
-    n = 2048
-    g = torch.Generator().manual_seed(0)
-    a = torch.randint(-128, 128, (n, n), generator=g, dtype=torch.int8)
-    b = torch.randint(-128, 128, (n, n), generator=g, dtype=torch.int8)
-    cgemm.gemm_int(a[:256], b)  # warm-up (and build check)
-    t0 = time.perf_counter()
-    cgemm.gemm_int(a, b)
-    secs = time.perf_counter() - t0
-    return 2 * n ** 3 / secs / 1e12, threads, f"int8 {n}x{n}x{n} through the oracle's C GEMM ({threads} threads)"
+        for _ in range(args.e2e_steps):
+            for o in ops_list:
+                o.e2e()
+        torch.cuda.synchronize()
+        secs = _max_over_ranks((time.perf_counter() - t0) / args.e2e_steps, world)
+        e2e = {"value": round(world * step_bytes / secs / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": world * sum(o.h2d for o in ops_list),
+               "d2h_bytes_per_step": world * sum(o.d2h for o in ops_list),
+               "ms_per_step": round(secs * 1e3, 2),
+               "api": "xb200.kernels.<reference kernel>[grid](pinned host tensors...), every rank"}
+    cpu = None
+    if cpu_leg:
+        gbs, threads, desc = cpu_baseline(kind, 1 << 24)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc}
+    del ops_list
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return {
+        "metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": dtype, "data": "synthetic N(0,1), seed = rank", "config": config,
+        "roofline": {"bound": "hbm", "kernel": dom.name, "achieved": round(dom_gbs, 1), "peak": hbm,
+                     "peak_source": peaks["source"], "unit": "GB/s", "frac": round(dom_gbs / hbm, 4),
+                     "traffic": (round(MEASURED_TRAFFIC_RATIO[dom.name][0] * dom.nbytes)
+                                 if dom.name in MEASURED_TRAFFIC_RATIO else None),
+                     "traffic_source": MEASURED_TRAFFIC_RATIO.get(dom.name, (None, None))[1],
+                     "algorithmic_bytes": dom.nbytes},
+        "ops": detail, "e2e": e2e, "cpu_baseline": cpu, "clocks": clk.summary(),
+        "gpu_launches": len(detail) * steps,
+    }
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -732,6 +1012,10 @@ def _max_over_ranks(v: float, world: int) -> float:
 # ----------------------------------------------------------------------------- CPU baseline
 
 
+
+# ----------------------------------------------------------------------------- CPU baseline
+
+
 def cpu_baseline(workload: str, sample: int, reps: int = 1):
     """Time the oracle (the examples' torch CPU expressions) on a bounded sample
     of the workload with every host thread; returns (GB/s, threads, description)."""
@@ -776,18 +1060,20 @@ def cpu_baseline(workload: str, sample: int, reps: int = 1):
     return total_b / total_s / 1e9, threads, desc
 
 
-def reference_arm_other(args, world, warmup):
-    """--impl reference for the GEMM and LLM workloads: the oracle's CPU path
-    (the examples' torch expressions / the C int GEMM) on bounded samples."""
+
+def reference_arm(args, world, warmup):
+    """--impl reference: the reference's CPU path of the workload on the host
+    cores, with every host thread, printed on the xb200 line's metric, unit
+    and config.  The examples' own CPU expressions run in the oracle (the
+    reference itself cannot run here: its launch path needs an XDNA NPU)."""
     vals = []
     if args.workload == "gemm":
-        for i in range(warmup + args.steps):
-            v, threads, desc = gemm_cpu_baseline()
-            if i >= warmup:
-                vals.append(v)
-        metric, unit, dtype = "GEMM TOPS", "TOPS", "i8"
-        cfg = {"workload": "GEMM sweep (CPU sample)", "sample": desc}
-    else:
+        gemm_cpu_sample(rows=8)  # warm-up (builds the oracle's C GEMM)
+        for _ in range(args.steps):
+            v, threads, desc = gemm_cpu_sample()
+            vals.append(v)
+        metric, unit, dtype, cfg = METRIC, "TOPS", "int8", headline_config()
+    elif args.workload in LLM_WORKLOADS:
         if args.workload == "qwen":
             from xb200.qwen import QwenConfig
             cfg_m = QwenConfig()
@@ -801,12 +1087,25 @@ def reference_arm_other(args, world, warmup):
                 vals.append(r["value"])
         threads, desc = r["cores"], r["sample"]
         metric, unit, dtype = "LLM tokens/s (prefill + decode)", "tokens/s", "bf16"
-        cfg = {"workload": f"{LLM_WORKLOADS[args.workload]} (CPU sample)", "sample": desc}
+        cfg = {"workload": f"{LLM_WORKLOADS[args.workload]}: batch {args.qwen_batch} x {args.qwen_prompt} prefill "
+                           f"+ {args.qwen_new} greedy decode"}
+    elif args.workload in SUITE_METRICS:
+        sample = 1 << 24
+        for _ in range(warmup):
+            cpu_baseline(args.workload, 1 << 16)
+        vals = [cpu_baseline(args.workload, sample)[0] for _ in range(args.steps)]
+        _, threads, desc = cpu_baseline(args.workload, sample)
+        metric, unit, dtype = SUITE_METRICS[args.workload], "GB/s", "bf16+f32"
+        cfg = {"workload": suite_workload(args.workload, args.elements)}
+    else:
+        print(json.dumps({"impl": "reference", "unavailable": f"no CPU arm for workload {args.workload}"}))
+        return
     value = statistics.median(vals)
     print(json.dumps({
         "impl": "reference", "metric": metric, "value": round(value, 4), "unit": unit, "n_gpus": world,
-        "steps": len(vals), "warmup": warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": dtype, "data": "synthetic, seed 0", "config": cfg,
+        "steps": len(vals), "warmup": warmup, "higher_is_better": True,
+        "scaling": "strong" if args.workload == "gemm" else "weak", "vs_baseline": None,
+        "dtype": dtype, "data": "synthetic, seeded", "config": cfg,
         "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
@@ -821,21 +1120,45 @@ def _timeit(fn):
 # ----------------------------------------------------------------------------- main
 
 
+def run_extras(args, world, rank, local, dev) -> dict:
+    """The metric's other rows, measured in the same process after the headline."""
+    extras = {}
+    steps = max(3, min(args.steps, 20))
+    warm = 3
+    t0 = time.perf_counter()
+    if world == 1:
+        extras["gemm_sweep"] = gemm_sweep_single(args, dev, SWEEP_EXTRA, ("i8", "i8nt", "i16", "bf16"),
+                                                 library=not args.no_library)
+    else:
+        extras["gemm_sweep_sharded"] = gemm_sweep_sharded(args, world, rank, dev,
+                                                          [(8192, 8192, 8192), (16384, 16384, 16384)])
+    cpu_leg = rank == 0 and world == 1 and not args.no_cpu_baseline
+    extras["rowreduce"] = time_suite("rowreduce", args, world, rank, local, dev, steps, warm, args.e2e_steps > 0,
+                                     cpu_leg)
+    extras["elementwise"] = time_suite("elementwise", args, world, rank, local, dev, steps, warm, False, cpu_leg)
+    extras["qwen"] = llm_bench(args, world, rank, local, dev, "qwen", steps, warm, cpu_leg)
+    extras["wall_s"] = round(time.perf_counter() - t0, 1)
+    return extras
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="xb200", choices=["xb200", "reference"])
-    ap.add_argument("--workload", default="elementwise", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="gemm", choices=["gemm"] + sorted(WORKLOADS))
+    ap.add_argument("--products", type=int, default=HEAD_PRODUCTS,
+                    help="gemm: products per step (default 16; fewer only for profiling)")
+    ap.add_argument("--no-extras", action="store_true", help="gemm: only the headline line's own measurements")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--qwen-batch", type=int, default=64)
     ap.add_argument("--qwen-prompt", type=int, default=512)
     ap.add_argument("--qwen-new", type=int, default=128)
     ap.add_argument("--qwen-eager", action="store_true", help="qwen: launch decode steps directly (no CUDA graphs)")
-    ap.add_argument("--only", default=None, help="gemm workload: run only ops whose name contains this string")
-    ap.add_argument("--no-library", action="store_true", help="gemm workload: skip the cuBLAS reference lines")
+    ap.add_argument("--only", default=None, help="gemm-sweep: run only ops whose name contains this string")
+    ap.add_argument("--no-library", action="store_true", help="gemm sweeps: skip the cuBLAS reference lines")
     ap.add_argument("--elements", type=int, default=N28,
                     help="flat tensor length (default 2^28, the workload); smaller values are for profiling only")
     args = ap.parse_args()
@@ -844,27 +1167,9 @@ def main():
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))
-        if rank != 0:
-            return
-        if args.workload in LLM_WORKLOADS or args.workload == "gemm":
-            reference_arm_other(args, world, warmup)
-            return
-        sample = 1 << 22
-        for _ in range(warmup):
-            cpu_baseline(args.workload, 1 << 16)
-        vals = [cpu_baseline(args.workload, sample)[0] for _ in range(args.steps)]
-        _, threads, desc = cpu_baseline(args.workload, sample)
-        value = statistics.median(vals)
-        print(json.dumps({
-            "impl": "reference", "metric": SUITE_METRICS[args.workload],
-            "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16+f32",
-            "data": "synthetic N(0,1), seed 0",
-            "config": {"workload": suite_workload(args.workload, args.elements), "cpu_sample": desc},
-            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": desc},
-            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }))
+        if rank == 0:
+            torch.set_num_threads(os.cpu_count() or 1)
+            reference_arm(args, world, warmup)
         return
 
     world, rank, local = _dist_init()
@@ -872,109 +1177,32 @@ def main():
 
     _lib.load()
     dev = torch.device("cuda", torch.cuda.current_device())
-    # every rank runs the end-to-end leg (its own pinned host tensors and PCIe
-    # link); the job's figure is all ranks' bytes over the slowest rank's time
-    want_e2e = args.e2e_steps > 0 and args.workload in ("elementwise", "rowreduce")
-    if args.workload in LLM_WORKLOADS:
-        run_llm_bench(args, world, rank, local, dev, args.workload)
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.destroy_process_group()
-        return
-    ops_list, config, metric, dtype = WORKLOADS[args.workload](dev, args.elements, rank, want_e2e)
-    if args.workload == "gemm":
-        if world > 1:
-            run_gemm_sharded_bench(args, world, rank, local, dev)
+    try:
+        if args.workload == "gemm":
+            line = gemm_headline(args, world, rank, local, dev)
+            if not args.no_extras:
+                line["extras"] = run_extras(args, world, rank, local, dev)
+        elif args.workload in LLM_WORKLOADS:
+            line = llm_bench(args, world, rank, local, dev, args.workload, args.steps, warmup,
+                             rank == 0 and world == 1 and not args.no_cpu_baseline)
+        elif args.workload == "gemm-sweep":
+            if world == 1:
+                res = gemm_sweep_single(args, dev, GEMM_SIZES, ("i8", "i8nt", "i16", "bf16"),
+                                        library=not args.no_library)
+            else:
+                res = gemm_sweep_sharded(args, world, rank, dev, [(4096, 4096, 4096), (8192, 8192, 8192),
+                                                                  (16384, 16384, 16384), (16, 8192, 8192)])
+            line = {"metric": "GEMM sweep TOPS", "n_gpus": world, "steps": args.steps, "warmup": warmup, **res}
         else:
-            run_gemm_bench(args, ops_list, config, world, rank, local, dev)
+            line = time_suite(args.workload, args, world, rank, local, dev, args.steps, warmup,
+                              args.e2e_steps > 0, rank == 0 and world == 1 and not args.no_cpu_baseline)
+        if rank == 0:
+            print(json.dumps(line))
+    finally:
         if world > 1:
             import torch.distributed as dist
 
             dist.destroy_process_group()
-        return
-    config["launches_per_step"] = len(ops_list)
-    config["parallelism"] = f"weak x{world} (independent replicas, no collective)"
-    step_bytes = sum(o.nbytes for o in ops_list)
-    config["bytes_per_step"] = step_bytes
-    stream = torch.cuda.current_stream()
-
-    for _ in range(warmup):
-        for o in ops_list:
-            o.run()
-    torch.cuda.synchronize()
-
-    # ---- timed region: K steps, per-launch CUDA events on the launching stream
-    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in ops_list]
-           for _ in range(args.steps)]
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    _barrier(world)
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
-        start.record(stream)
-        for s in range(args.steps):
-            for i, o in enumerate(ops_list):
-                evs[s][i][0].record(stream)
-                o.run()
-                evs[s][i][1].record(stream)
-        stop.record(stream)
-        torch.cuda.synchronize()
-    _barrier(world)
-    total_ms = _max_over_ranks(start.elapsed_time(stop), world)
-    clocks = clk.summary()
-
-    per_op_ms = {o.name: statistics.mean(evs[s][i][0].elapsed_time(evs[s][i][1]) for s in range(args.steps))
-                 for i, o in enumerate(ops_list)}
-    ms_per_step = total_ms / args.steps
-    value = step_bytes * world / (ms_per_step * 1e-3) / 1e9
-    peaks = _peaks()
-    hbm = peaks["hbm_gbs"]
-    dom = max(ops_list, key=lambda o: per_op_ms[o.name])
-    dom_gbs = dom.nbytes / (per_op_ms[dom.name] * 1e-3) / 1e9
-    detail = {o.name: {"ms": round(per_op_ms[o.name], 4), "gbs": round(o.nbytes / (per_op_ms[o.name] * 1e-3) / 1e9, 1),
-                       "frac": round(o.nbytes / (per_op_ms[o.name] * 1e-3) / 1e9 / hbm, 3)} for o in ops_list}
-
-    e2e = None
-    if want_e2e:
-        for o in ops_list:
-            o.e2e()
-        torch.cuda.synchronize()
-        _barrier(world)
-        t0 = time.perf_counter()
-        for _ in range(args.e2e_steps):
-            for o in ops_list:
-                o.e2e()
-        torch.cuda.synchronize()
-        secs = _max_over_ranks((time.perf_counter() - t0) / args.e2e_steps, world)
-        e2e = {"value": round(world * step_bytes / secs / 1e9, 3), "unit": "GB/s",
-               "h2d_bytes_per_step": world * sum(o.h2d for o in ops_list),
-               "d2h_bytes_per_step": world * sum(o.d2h for o in ops_list),
-               "ms_per_step": round(secs * 1e3, 2),
-               "api": "xb200.kernels.<reference kernel>[grid](pinned host tensors...), every rank"}
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        gbs, threads, desc = cpu_baseline(args.workload, 1 << 24)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc}
-
-    if rank == 0:
-        print(json.dumps({
-            "metric": metric, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-            "warmup": warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": dtype, "data": "synthetic N(0,1), seed = rank", "config": config,
-            "roofline": {"bound": "hbm", "kernel": dom.name, "achieved": round(dom_gbs, 1), "peak": hbm,
-                         "peak_source": peaks["source"], "unit": "GB/s", "frac": round(dom_gbs / hbm, 4),
-                         "traffic": (round(MEASURED_TRAFFIC_RATIO[dom.name][0] * dom.nbytes)
-                                     if dom.name in MEASURED_TRAFFIC_RATIO else None),
-                         "traffic_source": MEASURED_TRAFFIC_RATIO.get(dom.name, (None, None))[1],
-                         "algorithmic_bytes": dom.nbytes},
-            "ops": detail, "e2e": e2e, "cpu_baseline": cpu, "clocks": clocks,
-            "gpu_launches": len(ops_list) * args.steps,
-        }))
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.destroy_process_group()
 
 
 if __name__ == "__main__":

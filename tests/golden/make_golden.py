@@ -2,7 +2,7 @@
 
 Run here (where the reference source tree is mounted), not on the GPU box:
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference   (or XB_REFERENCE_ROOT=/path/to/reference)
 
 For each example, the script imports ``examples/<name>/<name>.py`` from the
 reference with a stub ``benchmark`` module (the real one imports the NPU
@@ -255,4 +255,8 @@ def make(ref: str) -> dict:
 
 
 if __name__ == "__main__":
-    make(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    # the reference source tree: first argument, else $XB_REFERENCE_ROOT
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("XB_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_golden.py <reference source tree>  (or set XB_REFERENCE_ROOT)")
+    make(root)
