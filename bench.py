@@ -68,11 +68,16 @@ def _peaks() -> dict:
     if os.path.exists(p):
         with open(p) as f:
             d = json.load(f)
-        pk = {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+        pk = {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+              "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "source": "measured"}
     else:
-        pk = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        pk = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+    # burst: a kernel timed alone; sustained: back-to-back for about a second
+    # under the 1 kW power cap (the headline's timed region)
     pk["i8_tops"] = 2.0 * pk["bf16_tflops"]
-    pk["i8_tops_source"] = f"2 x {pk['source']} bf16 TFLOP/s"
+    pk["i8_tops_sustained"] = 2.0 * pk["bf16_tflops_sustained"]
+    pk["i8_tops_source"] = f"2 x {pk['source']} bf16 TFLOP/s (burst)"
+    pk["i8_tops_sustained_source"] = f"2 x {pk['source']} bf16 TFLOP/s (sustained)"
     pk["i8_tops_nominal"] = 4500.0
     return pk
 
@@ -602,8 +607,11 @@ def gemm_headline(args, world, rank, local, dev) -> dict:
                    "ok": True},
         "roofline": {"bound": "tensor", "kernel": "gemm_kernel<int8, CTA pairs" + (", peer stores>" if world > 1
                                                                                     else ">"),
-                     "achieved": round(achieved, 1), "peak": peaks["i8_tops"], "peak_source": peaks["i8_tops_source"],
-                     "unit": "TOPS", "frac": round(achieved / peaks["i8_tops"], 4),
+                     "achieved": round(achieved, 1), "peak": peaks["i8_tops_sustained"],
+                     "peak_source": peaks["i8_tops_sustained_source"] + ": the timed region runs the kernel back "
+                                    "to back for about a second",
+                     "unit": "TOPS", "frac": round(achieved / peaks["i8_tops_sustained"], 4),
+                     "frac_of_burst": round(achieved / peaks["i8_tops"], 4),
                      "frac_of_nominal_4500": round(achieved / peaks["i8_tops_nominal"], 4),
                      "launch_ms": round(launch_ms, 4), "ops_per_launch": rank_ops,
                      "traffic": traffic[0] if traffic else None,

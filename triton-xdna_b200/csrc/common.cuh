@@ -179,7 +179,7 @@ inline OnceRegistry& once_registry() {
   static OnceRegistry r;
   return r;
 }
-enum : int { kOnceCarveout = 0, kOnceSmem = 1 };
+enum : int { kOnceCarveout = 0, kOnceSmem = 1, kOnceClusters = 16 };  // kOnceClusters + cluster size
 
 // Runs setup(&value) the first time (key, what) is seen on the current device
 // and stores `value`; later calls on that device return the stored value

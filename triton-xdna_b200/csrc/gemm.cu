@@ -46,6 +46,15 @@ using namespace tc;
 __device__ int g_gemm_status = 0;
 constexpr uint64_t kWaitLimit = 2000000000ull;  // 2 s per wait: far above any legitimate wait
 
+// CTA-pair raster group (in 256-row tiles) and int8 pair ring depth; build-time
+// tuning knobs (nvcc -D...), defaults measured best on B200
+#ifndef XB_PAIR_GROUP_M
+#define XB_PAIR_GROUP_M 8
+#endif
+#ifndef XB_I8_PAIR_STAGES
+#define XB_I8_PAIR_STAGES 6
+#endif
+
 enum Kind { kBf16 = 0, kInt8 = 1, kInt16Limbs = 2 };
 // kOutSwiglu: W interleaves 64-row blocks of gate and up rows (block 2b =
 // gate rows 64b.., block 2b+1 = up rows 64b..), so a 256-column tile holds
@@ -86,7 +95,8 @@ struct Cfg {
   static constexpr int STAGE_BYTES = PLANES * (A_BYTES + B_BYTES);
   // BN <= 64 (small-M, swap-AB): 6 slots leave room on the SM for the small
   // kernel before it, so the weight prefetch can overlap that kernel
-  static constexpr int STAGES = PAIR ? (KIND == kInt16Limbs ? 4 : 6) : KIND == kInt16Limbs ? 3 : (BN <= 64 ? 6 : 4);
+  static constexpr int STAGES = PAIR ? (KIND == kInt16Limbs ? 4 : KIND == kInt8 ? XB_I8_PAIR_STAGES : 6)
+                                     : KIND == kInt16Limbs ? 3 : (BN <= 64 ? 6 : 4);
   static constexpr int UMMA_K = 32 / ESZ;  // 32 bytes of K per MMA
   static constexpr int KSTEPS = BK / UMMA_K;
   static constexpr int ACCS = KIND == kInt16Limbs ? 3 : 1;
@@ -187,7 +197,7 @@ __device__ __forceinline__ bool wait_peer_releases(const Args& args) {
 template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false>
 __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Maps maps, const Args args) {
   using C = Cfg<KIND, B_KMAJOR, BN_, PAIR>;
-  constexpr int GM = PAIR ? 8 : kGroupM;  // raster group (in tiles)
+  constexpr int GM = PAIR ? XB_PAIR_GROUP_M : kGroupM;  // raster group (in tiles)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
   __shared__ __align__(8) uint64_t empty_bar[C::STAGES];
@@ -1841,7 +1851,7 @@ constexpr int kDecBK = 64;                    // K elements per ring slot (128 b
 constexpr int kDecA = kDecBM * 128;           // weight tile bytes per slot
 constexpr int kDecStage = kDecA + kDecBN * 128;
 constexpr int kDecRedBytes = kDecBN * kDecBM * 4;  // this CTA's fp32 partial [token][row], over the ring
-constexpr int kDecMaxCluster = 8;             // CTAs per cluster (the portable cluster size)
+constexpr int kDecMaxCluster = 16;            // CTAs per cluster at most (above 8: non-portable cluster size)
 // receive buffer [source rank][owned token][row] fp32: S * ceil(64 / S) <= 72 token rows
 constexpr int kDecRecvBytes = 72 * kDecBM * 4;
 
@@ -2425,15 +2435,32 @@ bool decode_cluster_enabled() {
 // Cluster size for a decode linear of `blocks` 128-row weight blocks and
 // `kblocks` 64-wide K blocks: about two CTAs per SM, at most 8 (portable
 // cluster size), every CTA with at least one K block.
-void decode_split(int blocks, int kblocks, int* splits, int* kps) {
+// Largest split-K cluster the decode linears may use: the portable 8, or up
+// to 16 with XB_DECODE_CLUSTER_MAX=16 in the environment (non-portable
+// cluster size; used only where every cluster of the grid is resident at once).
+int decode_cluster_max() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("XB_DECODE_CLUSTER_MAX");
+    int x = e ? atoi(e) : 8;
+    v = x < 1 ? 1 : (x > kDecMaxCluster ? kDecMaxCluster : x);
+  }
+  return v;
+}
+
+void decode_split(int blocks, int kblocks, int max_s, int* splits, int* kps) {
   int sms = 148;
   sm_count(&sms);
   int s = (2 * sms) / blocks;
-  if (s > kDecMaxCluster) s = kDecMaxCluster;
+  if (s > max_s) s = max_s;
   if (s > kblocks) s = kblocks;
   if (s < 1) s = 1;
-  *kps = (kblocks + s - 1) / s;
-  *splits = (kblocks + *kps - 1) / *kps;
+  for (;; --s) {
+    *kps = (kblocks + s - 1) / s;
+    *splits = (kblocks + *kps - 1) / *kps;
+    // the receive buffer holds splits * ceil(64 / splits) token rows (<= 72)
+    if (*splits * ((kDecBN + *splits - 1) / *splits) <= kDecRecvBytes / (kDecBM * 4) || s == 1) break;
+  }
 }
 
 bool al8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7) == 0; }
@@ -2477,24 +2504,57 @@ int launch_decode(const DecInput& in, const void* W, int64_t N, int64_t K, int64
   args.xnb = static_cast<const __nv_bfloat16*>(in.nb);
   args.xeps = in.eps;
   args.xkind = in.kind;
-  decode_split(blocks, args.kblocks, &args.splits, &args.kps);
   int sms = 148;
   sm_count(&sms);
-  // one CTA per SM with a deep ring when the grid is small, two with a short one
-  const bool deep = blocks * args.splits <= sms;
   const bool xn = in.stats != nullptr;
-  void (*kernel)(DecMaps, DecArgs) =
-      xn ? (deep ? decode_linear_kernel<FIN, 7, true> : decode_linear_kernel<FIN, 3, true>)
-         : (deep ? decode_linear_kernel<FIN, 7, false> : decode_linear_kernel<FIN, 3, false>);
-  const int smem = (deep ? 7 : 3) * kDecStage + kDecRecvBytes + 1024;
-  {
+  void (*kernel)(DecMaps, DecArgs) = nullptr;
+  int smem = 0;
+  for (int max_s = decode_cluster_max();;) {
+    decode_split(blocks, args.kblocks, max_s, &args.splits, &args.kps);
+    // one CTA per SM with a deep ring when the grid is small, two with a short one
+    const bool deep = blocks * args.splits <= sms;
+    kernel = xn ? (deep ? decode_linear_kernel<FIN, 7, true> : decode_linear_kernel<FIN, 3, true>)
+                : (deep ? decode_linear_kernel<FIN, 7, false> : decode_linear_kernel<FIN, 3, false>);
+    smem = (deep ? 7 : 3) * kDecStage + kDecRecvBytes + 1024;
     cudaError_t e = once_per_device(reinterpret_cast<const void*>(kernel), kOnceSmem, [&](int*) {
-      return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      cudaError_t r = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      if (r == cudaSuccess) r = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      return r;
     });
     if (e != cudaSuccess) {
       set_err(err, errlen, "%s: kernel setup: %s", what, cudaGetErrorString(e));
       return XB_ERR_CUDA;
     }
+    if (args.splits <= 8) break;
+    // a cluster above the portable size: keep it only if all `blocks` clusters
+    // are resident at once (one wave), else fall back to the portable size
+    int fits = 0;
+    const int sp = args.splits;
+    e = once_per_device(reinterpret_cast<const void*>(kernel), kOnceClusters + sp, [&](int* v) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)sp);
+      cfg.blockDim = dim3(192);
+      cfg.dynamicSmemBytes = smem;
+      cudaLaunchAttribute attr;
+      attr.id = cudaLaunchAttributeClusterDimension;
+      attr.val.clusterDim.x = (unsigned)sp;
+      attr.val.clusterDim.y = 1;
+      attr.val.clusterDim.z = 1;
+      cfg.attrs = &attr;
+      cfg.numAttrs = 1;
+      cudaError_t r = cudaOccupancyMaxActiveClusters(v, kernel, &cfg);
+      if (r != cudaSuccess) {  // not schedulable at this size: record zero resident clusters
+        cudaGetLastError();
+        *v = 0;
+      }
+      return cudaSuccess;
+    }, &fits);
+    if (e != cudaSuccess) {
+      set_err(err, errlen, "%s: kernel setup: %s", what, cudaGetErrorString(e));
+      return XB_ERR_CUDA;
+    }
+    if (fits >= blocks) break;
+    max_s = 8;
   }
   cudaError_t e = launch_clusters(kernel, (unsigned)(blocks * args.splits), (unsigned)args.splits, 192, smem, s, maps,
                                   args);
