@@ -18,8 +18,8 @@ bf16 at 4096^3 .. 16384^3 and the 16 x 8192 x 8192 decode shape; N > 1: the
 fused sharded kernel against the NCCL all-gather baseline), the row
 reductions (softmax, layernorm, rms_norm, weighted_rms_norm on
 [32768, 4096] bf16 + f32), the elementwise / activation suite (2^28
-elements) and the Qwen2.5-0.5B forward (batch 64 x 512-token prefill + 128
-greedy decode steps, batch-sharded over the ranks).
+elements), and the Qwen2.5-0.5B and GPT-2 124M forwards (batch 64 x
+512-token prefill + 128 greedy decode steps, batch-sharded over the ranks).
 
 Other workloads (``--workload``): ``elementwise``, ``rowreduce``,
 ``gemm-sweep``, ``qwen``, ``gpt2`` print their own line.
@@ -1145,6 +1145,7 @@ def run_extras(args, world, rank, local, dev) -> dict:
                                      cpu_leg)
     extras["elementwise"] = time_suite("elementwise", args, world, rank, local, dev, steps, warm, False, cpu_leg)
     extras["qwen"] = llm_bench(args, world, rank, local, dev, "qwen", steps, warm, cpu_leg)
+    extras["gpt2"] = llm_bench(args, world, rank, local, dev, "gpt2", steps, warm, cpu_leg)
     extras["wall_s"] = round(time.perf_counter() - t0, 1)
     return extras
 

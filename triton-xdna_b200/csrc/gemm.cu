@@ -194,9 +194,17 @@ __device__ __forceinline__ bool wait_peer_releases(const Args& args) {
   return true;
 }
 
-template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false>
-__global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Maps maps, const Args args) {
+// EPI: epilogue warps (4, or 8 for bf16-output and fused-QKV tiles: two warps
+// per TMEM lane quarter, each finishing half of the tile's 32-column chunks,
+// so that a short-K tile's epilogue hides behind the next tile's main loop).
+template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false,
+          int EPI = 4>
+__global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_constant__ Maps maps, const Args args) {
   using C = Cfg<KIND, B_KMAJOR, BN_, PAIR>;
+  static_assert(EPI == 4 || (EPI == 8 && (OUT == kOutBf16 || OUT == kOutQkv) && !TRANS && !PEERS),
+                "eight epilogue warps: bf16-output or fused-QKV row-major tiles only");
+  constexpr int kEpiThreads = 32 * EPI;
+  constexpr int kHalves = EPI / 4;  // warps per TMEM lane quarter
   constexpr int GM = PAIR ? XB_PAIR_GROUP_M : kGroupM;  // raster group (in tiles)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[C::STAGES];
@@ -225,7 +233,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
     }
     for (int b = 0; b < C::ACC_BUFS; ++b) {
       mbar_init(&tfull_bar[b], 1);
-      mbar_init(&tempty_bar[b], PAIR ? 256 : 128);
+      mbar_init(&tempty_bar[b], PAIR ? 2 * kEpiThreads : kEpiThreads);
     }
     mbar_init(&drain_bar, 1);
     abort_flag = 0;
@@ -419,6 +427,8 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;  // epilogue warp 0 .. EPI - 1
+    const int half = ew >> 2;  // which of the quarter's warps (EPI = 8)
     int local = 0;
     int first_tile = tile0;
     if constexpr (PEERS) {
@@ -455,6 +465,9 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + buf * C::ACCS * C::BN;
 #pragma unroll 1
       for (int cc = 0; cc < C::BN / 32; ++cc) {
+        if constexpr (kHalves > 1) {  // chunks (QKV: 64-column head slots) alternate between the quarter's warps
+          if ((((OUT == kOutQkv) ? (cc >> 1) : cc) % kHalves) != half) continue;
+        }
         if constexpr (OUT == kOutQkv) {
           static_assert(!TRANS && !PEERS && C::BN % 64 == 0, "fused QKV epilogue: row-major tiles of whole heads");
           if (cc & 1) continue;  // the even chunk takes the whole 64-column head slot
@@ -730,7 +743,7 @@ __global__ void __launch_bounds__(192, 1) gemm_kernel(const __grid_constant__ Ma
                   }
                 }
               }
-              uint8_t* stg = smem + C::STAGES * C::STAGE_BYTES + q * 2 * (32 * 128);
+              uint8_t* stg = smem + C::STAGES * C::STAGE_BYTES + (EPI == 4 ? q * 2 : ew) * (32 * 128);
               if constexpr (OUT == kOutBf16) {
 #pragma unroll
                 for (int p = 0; p < 4; ++p) {
@@ -1379,8 +1392,10 @@ cudaError_t launch_pairs(void (*kernel)(KArgs...), unsigned grid, unsigned block
 }
 
 bool lines_enabled();
+bool epi8_enabled();
 
-template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false>
+template <int KIND, bool B_KMAJOR, int OUT, int BN_ = 0, bool TRANS = false, bool PEERS = false, bool PAIR = false,
+          int EPI = 4>
 int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, int64_t K, int64_t ldc,
            cudaStream_t s, const char* what, char* err, size_t errlen, int splits = 1, int64_t split_stride = 0,
            const PeerArgs* pa = nullptr, const void* residual = nullptr, int64_t ldr = 0, int act = 0,
@@ -1468,7 +1483,8 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
     if (residual) ok = ok && (reinterpret_cast<uintptr_t>(residual) & 15) == 0 && (ldr * 2) % 16 == 0;
     args.c_tma = ok ? 1 : 0;
   }
-  auto kernel = gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS, PEERS, PAIR>;
+  auto kernel = gemm_kernel<KIND, B_KMAJOR, OUT, BN_, TRANS, PEERS, PAIR, EPI>;
+  constexpr unsigned kBlock = 64 + 32 * EPI;
   // shared-memory limit and (pairs) the resident cluster count, once per device
   int max_clusters = 0;
   {
@@ -1478,7 +1494,7 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
         // resident pairs: the persistent grid is sized to what runs at once
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2);
-        cfg.blockDim = dim3(192);
+        cfg.blockDim = dim3(kBlock);
         cfg.dynamicSmemBytes = kSmem;
         cudaLaunchAttribute attr;
         attr.id = cudaLaunchAttributeClusterDimension;
@@ -1501,14 +1517,14 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
   sm_count(&sms);
   if constexpr (PAIR) {
     const int clusters = args.num_tiles < max_clusters ? args.num_tiles : max_clusters;
-    cudaError_t e = launch_pairs(kernel, 2 * clusters, 192, kSmem, s, maps, args);
+    cudaError_t e = launch_pairs(kernel, 2 * clusters, kBlock, kSmem, s, maps, args);
     if (e != cudaSuccess) {
       set_err(err, errlen, "%s: %s", what, cudaGetErrorString(e));
       return XB_ERR_CUDA;
     }
   } else {
     const int grid = args.num_tiles < sms ? args.num_tiles : sms;
-    launch_k(kernel, grid, 192, kSmem, s, maps, args);
+    launch_k(kernel, grid, kBlock, kSmem, s, maps, args);
   }
   return check_launch(what, err, errlen);
 }
@@ -1521,6 +1537,17 @@ bool lines_enabled() {
   if (on < 0) {
     const char* v = getenv("XB_GEMM_LINES");
     on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+// Epilogue warps of bf16-output / fused-QKV CTA-pair tiles: XB_GEMM_EPI=8 in
+// the environment selects eight (two per TMEM lane quarter), else four.
+bool epi8_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("XB_GEMM_EPI");
+    on = (v && atoi(v) == 8) ? 1 : 0;
   }
   return on == 1;
 }
@@ -1772,6 +1799,9 @@ extern "C" int xb_matmul_bf16(const void* A, const void* B, void* C, int64_t M, 
   if (use_pairs(M)) {
     if (out_dtype == XB_DT_F32)
       return launch<kBf16, false, kOutF32, 0, false, false, true>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
+    if (epi8_enabled())
+      return launch<kBf16, false, kOutBf16, 0, false, false, true, 8>(op, C, nullptr, M, N, K, ldc, s, what, err,
+                                                                      errlen);
     return launch<kBf16, false, kOutBf16, 0, false, false, true>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
   }
   if (out_dtype == XB_DT_F32) return launch<kBf16, false, kOutF32>(op, C, nullptr, M, N, K, ldc, s, what, err, errlen);
@@ -1801,6 +1831,8 @@ extern "C" int xb_linear_bf16(const void* X, const void* W, const void* bias, vo
   if (use_pairs(M)) {
     if (out_dtype == XB_DT_F32)
       return launch<kBf16, true, kOutF32, 0, false, false, true>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
+    if (epi8_enabled())
+      return launch<kBf16, true, kOutBf16, 0, false, false, true, 8>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
     return launch<kBf16, true, kOutBf16, 0, false, false, true>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
   }
   if (out_dtype == XB_DT_F32) return launch<kBf16, true, kOutF32>(op, Y, bias, M, N, K, ldy, s, what, err, errlen);
@@ -2925,8 +2957,11 @@ extern "C" int xb_linear_rope_kv_bf16(const void* X, const void* W, const void* 
   Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
   cudaStream_t s = (cudaStream_t)stream;
   if (use_pairs(M))
-    return launch<kBf16, true, kOutQkv, 0, false, false, true>(op, nullptr, bias, M, N, K, N, s, what, err, errlen, 1,
-                                                               0, nullptr, nullptr, 0, 0, &a);
+    return epi8_enabled()
+               ? launch<kBf16, true, kOutQkv, 0, false, false, true, 8>(op, nullptr, bias, M, N, K, N, s, what, err,
+                                                                        errlen, 1, 0, nullptr, nullptr, 0, 0, &a)
+               : launch<kBf16, true, kOutQkv, 0, false, false, true>(op, nullptr, bias, M, N, K, N, s, what, err,
+                                                                     errlen, 1, 0, nullptr, nullptr, 0, 0, &a);
   return launch<kBf16, true, kOutQkv>(op, nullptr, bias, M, N, K, N, s, what, err, errlen, 1, 0, nullptr, nullptr, 0, 0,
                                       &a);
 }
@@ -2948,8 +2983,11 @@ extern "C" int xb_linear_residual_bf16(const void* X, const void* W, const void*
   }
   Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
   if (use_pairs(M))
-    return launch<kBf16, true, kOutBf16, 0, false, false, true>(op, Y, bias, M, N, K, ldy, s, what, err, errlen, 1, 0,
-                                                                nullptr, residual, ldr);
+    return epi8_enabled()
+               ? launch<kBf16, true, kOutBf16, 0, false, false, true, 8>(op, Y, bias, M, N, K, ldy, s, what, err,
+                                                                         errlen, 1, 0, nullptr, residual, ldr)
+               : launch<kBf16, true, kOutBf16, 0, false, false, true>(op, Y, bias, M, N, K, ldy, s, what, err, errlen,
+                                                                      1, 0, nullptr, residual, ldr);
   return launch<kBf16, true, kOutBf16>(op, Y, bias, M, N, K, ldy, s, what, err, errlen, 1, 0, nullptr, residual,
                                       ldr);
 }
@@ -2968,8 +3006,11 @@ extern "C" int xb_linear_gelu_bf16(const void* X, const void* W, const void* bia
   if (M > 64) {
     Operands op{{X, nullptr}, {W, nullptr}, ldx, ldw};
     if (use_pairs(M))
-      return launch<kBf16, true, kOutBf16, 0, false, false, true>(op, Y, bias, M, N, K, ldy, s, what, err, errlen, 1,
-                                                                  0, nullptr, nullptr, 0, 1);
+      return epi8_enabled()
+                 ? launch<kBf16, true, kOutBf16, 0, false, false, true, 8>(op, Y, bias, M, N, K, ldy, s, what, err,
+                                                                           errlen, 1, 0, nullptr, nullptr, 0, 1)
+                 : launch<kBf16, true, kOutBf16, 0, false, false, true>(op, Y, bias, M, N, K, ldy, s, what, err,
+                                                                        errlen, 1, 0, nullptr, nullptr, 0, 1);
     return launch<kBf16, true, kOutBf16>(op, Y, bias, M, N, K, ldy, s, what, err, errlen, 1, 0, nullptr, nullptr, 0,
                                         1);
   }

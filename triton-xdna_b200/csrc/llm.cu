@@ -618,7 +618,12 @@ __global__ void __launch_bounds__(128) attn_decode_split_kernel(const bf16* __re
 // context is read once and no cross-CTA merge or second kernel is needed;
 // from 48 (batch, KV head) pairs up it beats the chunked kernels (measured:
 // 64 pairs 5.3 vs 6.4 us at a 576-key context; 16 pairs 5.3 vs 4.5 us).
-constexpr int kHeadWarps = 8;
+// warps per CTA (build-time knob): 8 keeps two of a warp's 32-key tiles in
+// flight; 12 puts every tile of a context of up to 768 keys in flight at once
+#ifndef XB_HEAD_WARPS
+#define XB_HEAD_WARPS 8
+#endif
+constexpr int kHeadWarps = XB_HEAD_WARPS;
 constexpr int kTileK = 32;
 constexpr int kHeadTileElems = kTileK * kPad;  // one K or V tile (bf16 elements)
 constexpr int kHeadSmem = kHeadWarps * 2 * 2 * kHeadTileElems * (int)sizeof(bf16);
