@@ -3364,3 +3364,339 @@ extern "C" int xb_device_status(void* stream, int* status, char* err, size_t err
   }
   return XB_OK;
 }
+
+// ---- causal prefill attention on tcgen05 ----------------------------------------
+//
+// FlashAttention-style causal GQA attention (head_dim 64) for a prefill chunk,
+// the numerics of examples/qwen2_5/kernels/attention.py:27-122: per key tile
+// S = (Q K^T) * scale with the bounds and causal masks, m_new = max(m,
+// rowmax S), alpha = exp(m - m_new), P = exp(S - m_new),
+// acc = alpha * acc + bf16(P) @ V, l = alpha * l + rowsum(P), out = acc / l
+// (exponentials in base 2 on the pre-scaled S).
+//
+// One CTA owns 128 query rows of one (sequence, head); key tiles of 64 keys.
+// Warp 0 streams Q once and K / V tiles through a two-slot ring with TMA
+// (3-D tensor maps whose key extent is the context length, so keys past it
+// arrive as zeros); warp 1 issues the tcgen05 MMAs: S = Q K^T into 64 TMEM
+// columns, then, once P is in shared memory, the tile's P V into 64 more
+// (a fresh accumulator per tile).  Warps 2-5 own one query row per thread:
+// they read the row's S straight from TMEM (no cross-thread reductions),
+// write bf16(P) into a 128-byte-swizzled K-major tile for the P V MMA, and
+// fold the tile's P V into the row's fp32 accumulator held in registers
+// (acc = alpha * acc + PV).  Two CTAs share an SM (65 KB shared memory, 128
+// TMEM columns each), so one CTA's softmax overlaps the other's MMAs.  CTAs
+// take the query tiles with the most key tiles first.  Every wait is bounded
+// (XB_ERR_TIMEOUT through the GEMM status word).
+namespace xb {
+namespace gemm {
+
+constexpr int kAtBQ = 128;                 // query rows per CTA (TMEM lanes)
+constexpr int kAtBK = 64;                  // keys per tile
+constexpr int kAtQBytes = kAtBQ * 128;     // Q tile: 128 rows x 64 bf16
+constexpr int kAtKVBytes = kAtBK * 128;    // K or V tile: 64 keys x 64 bf16
+constexpr int kAtStages = 2;               // K / V ring slots
+constexpr int kAtPBytes = kAtBQ * 128;     // P tile: 128 rows x 64 keys bf16
+constexpr int kAtSmem = kAtQBytes + kAtStages * 2 * kAtKVBytes + kAtPBytes + 1024;
+
+// two floats -> packed bf16 pair, the first in the low half (lower address)
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+struct alignas(64) AtMaps {
+  CUtensorMap q;  // [B * H][S][64]
+  CUtensorMap k;  // [B * KVH][total][64] (cache rows, extent = keys in context)
+  CUtensorMap v;
+};
+
+struct AtArgs {
+  __nv_bfloat16* out;  // [B * S][H * 64]
+  int H, KVH, S, total, pos, nqt, nbh;
+  float scale_log2;
+};
+
+__global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_constant__ AtMaps maps,
+                                                                  const AtArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t q_full, s_full, p_full, o_full, drain_bar;
+  __shared__ __align__(8) uint64_t kv_full[kAtStages], kv_empty[kAtStages];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ volatile int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base_u32 - smem_u32(smem_raw));
+  const uint32_t sQ = base_u32, sKV = base_u32 + kAtQBytes, sP = sKV + kAtStages * 2 * kAtKVBytes;
+  uint8_t* sPg = smem + kAtQBytes + kAtStages * 2 * kAtKVBytes;
+
+  // unit -> (query tile, sequence * head): the query tiles with the most key tiles first
+  const int u = (int)blockIdx.x;
+  const int qt = args.nqt - 1 - u / args.nbh;
+  const int bh = u % args.nbh;
+  const int b = bh / args.H, h = bh - b * args.H;
+  const int kvh = h / (args.H / args.KVH);
+  const int qs = qt * kAtBQ;
+  const int rows = min(kAtBQ, args.S - qs);
+  const int kmax = min(args.total, args.pos + qs + rows);  // keys the last row sees
+  const int nkt = (kmax + kAtBK - 1) / kAtBK;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    mbar_init(&s_full, 1);
+    mbar_init(&p_full, 128);
+    mbar_init(&o_full, 1);
+    mbar_init(&drain_bar, 1);
+    for (int s = 0; s < kAtStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&maps.q);
+    prefetch_tmap(&maps.k);
+    prefetch_tmap(&maps.v);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_sh, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+  const uint32_t tS = tmem_base, tO = tmem_base + 64;  // S and the tile's P V, 64 columns each
+  pdl_wait();  // Q and the caches are written by the previous kernel
+  pdl_trigger();
+
+  auto fail = [&]() {
+    atomicExch(&g_gemm_status, XB_ERR_TIMEOUT);
+    abort_flag = 1;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      uint32_t issued[kAtStages] = {0, 0};
+      mbar_arrive_expect_tx(&q_full, kAtQBytes);
+      tma_load_3d(smem, &maps.q, &q_full, 0, qs, bh);
+      const int kvrow = b * args.KVH + kvh;
+      for (int j = 0; j < nkt; ++j) {
+        const int st = j % kAtStages;
+        const uint32_t ph = (j / kAtStages) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1, kWaitLimit, &abort_flag)) {
+          fail();
+          break;
+        }
+        uint8_t* dst = smem + kAtQBytes + st * 2 * kAtKVBytes;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kAtKVBytes);
+        tma_load_3d(dst, &maps.k, &kv_full[st], 0, j * kAtBK, kvrow);
+        tma_load_3d(dst + kAtKVBytes, &maps.v, &kv_full[st], 0, j * kAtBK, kvrow);
+        issued[st] = j / kAtStages + 1;
+      }
+      // every load issued must have landed before the CTA exits (also after an abort)
+      const uint64_t deadline = globaltimer_ns() + kWaitLimit;
+      if (!mbar_wait_deadline(&q_full, 0, deadline)) fail();
+      for (int st = 0; st < kAtStages; ++st)
+        if (issued[st] && !mbar_wait_deadline(&kv_full[st], (issued[st] - 1) & 1, deadline)) fail();
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t kIdS = umma_idesc(1, 1, 1, 0, 0, kAtBQ, kAtBK);  // Q (K-major) x K tile (K-major)
+      constexpr uint32_t kIdO = umma_idesc(1, 1, 1, 0, 1, kAtBQ, 64);     // P (K-major) x V tile (MN-major)
+      bool any = false;
+      if (!mbar_wait(&q_full, 0, kWaitLimit, &abort_flag)) fail();
+      for (int j = 0; j < nkt && !abort_flag; ++j) {
+        const int st = j % kAtStages;
+        if (!mbar_wait(&kv_full[st], (j / kAtStages) & 1, kWaitLimit, &abort_flag)) {
+          fail();
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sk = sKV + st * 2 * kAtKVBytes, sv = sk + kAtKVBytes;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)  // head dim in steps of 16
+          mma_f16(tS, umma_desc_sw128(sQ + ks * 32, 16, 1024), umma_desc_sw128(sk + ks * 32, 16, 1024), kIdS,
+                  ks > 0 ? 1u : 0u);
+        any = true;
+        tc_commit(&s_full);
+        if (!mbar_wait(&p_full, j & 1, kWaitLimit, &abort_flag)) {
+          fail();
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)  // keys in steps of 16
+          mma_f16(tO, umma_desc_sw128(sP + ks * 32, 16, 1024),
+                  umma_desc_sw128(sv + ks * 16 * 128, kAtKVBytes, 1024), kIdO, ks > 0 ? 1u : 0u);
+        tc_commit(&o_full);
+        tc_commit(&kv_empty[st]);
+      }
+      if (any) {  // every issued MMA completes before TMEM is released (also after an abort)
+        tc_commit(&drain_bar);
+        if (!mbar_wait_deadline(&drain_bar, 0, globaltimer_ns() + kWaitLimit)) fail();
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax: one query row per thread
+    const int q4 = warp & 3;  // TMEM lane quarter
+    const int r = q4 * 32 + lane;
+    const int qpos = args.pos + qs + r;  // absolute position of this row
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    float o[64];
+#pragma unroll
+    for (int c = 0; c < 64; ++c) o[c] = 0.0f;
+    float m = -INFINITY, l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nkt; ++j) {
+      if (!mbar_wait(&s_full, j & 1, kWaitLimit, &abort_flag)) {
+        fail();
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[64];
+      tmem_ld_32x32b_x32(tS + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+      tmem_ld_32x32b_x32(tS + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      tmem_ld_wait();
+      const int k0 = j * kAtBK;
+      const bool whole = k0 + kAtBK <= args.total && k0 + kAtBK - 1 <= qpos;  // no key of the tile masked
+      float s[64];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const int key = k0 + c;
+        const bool keep = whole || (key < args.total && key <= qpos);
+        s[c] = keep ? __uint_as_float(sv[c]) * args.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, s[c]);
+      }
+      const float mn = fmaxf(m, mx);
+      const float base = mn == -INFINITY ? 0.0f : mn;
+      const float alpha = ex2_approx(m - base);
+      m = mn;
+      float rs = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        s[c] = ex2_approx(s[c] - base);
+        rs += s[c];
+      }
+      l = l * alpha + rs;
+      // bf16(P) row r -> the K-major swizzled tile (16-byte chunk c8 at c8 ^ (r & 7))
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        uint4 w;
+        w.x = pack_bf16x2(s[c8 * 8 + 0], s[c8 * 8 + 1]);
+        w.y = pack_bf16x2(s[c8 * 8 + 2], s[c8 * 8 + 3]);
+        w.z = pack_bf16x2(s[c8 * 8 + 4], s[c8 * 8 + 5]);
+        w.w = pack_bf16x2(s[c8 * 8 + 6], s[c8 * 8 + 7]);
+        *reinterpret_cast<uint4*>(sPg + r * 128 + ((c8 ^ (r & 7)) << 4)) = w;
+      }
+      fence_proxy_async_smem();  // P, before the MMA (async proxy) reads it
+      tc_fence_before();         // S read, before the next S MMA overwrites it
+      mbar_arrive(&p_full);
+      if (!mbar_wait(&o_full, j & 1, kWaitLimit, &abort_flag)) {
+        fail();
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t ov[64];
+      tmem_ld_32x32b_x32(tO + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+      tmem_ld_32x32b_x32(tO + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+      tmem_ld_wait();
+#pragma unroll
+      for (int c = 0; c < 64; ++c) o[c] = fmaf(o[c], alpha, __uint_as_float(ov[c]));
+      tc_fence_before();  // this tile's P V read, before the next tile's P V overwrites it
+    }
+    if (ok && r < rows) {
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+      __nv_bfloat16* op = args.out + ((int64_t)b * args.S + qs + r) * ((int64_t)args.H * 64) + h * 64;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        uint4 w;
+        w.x = pack_bf16x2(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
+        w.y = pack_bf16x2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
+        w.z = pack_bf16x2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
+        w.w = pack_bf16x2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
+        *reinterpret_cast<uint4*>(op + c8 * 8) = w;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 128);
+  }
+}
+
+// 3-D map [outer2][outer1][64 bf16] with 128-byte swizzle, box {64, box1, 1}.
+int make_map_3d_sw128(CUtensorMap* map, const void* ptr, uint64_t outer1, uint64_t outer2, uint64_t ld1,
+                      uint64_t ld2, uint32_t box1, char* err, size_t errlen) {
+  EncodeTiledFn enc = encoder(err, errlen);
+  if (!enc) return XB_ERR_CUDA;
+  cuuint64_t dims[3] = {64, outer1, outer2};
+  cuuint64_t strides[2] = {ld1 * 2, ld2 * 2};
+  cuuint32_t box[3] = {64, box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_err(err, errlen, "cuTensorMapEncodeTiled failed (%d) for a [%llu][%llu][64] attention operand", (int)r,
+            (unsigned long long)outer2, (unsigned long long)outer1);
+    return XB_ERR_CUDA;
+  }
+  return XB_OK;
+}
+
+}  // namespace gemm
+
+// Host side of the tcgen05 prefill attention (called by xb_attention_bf16 for
+// seq > 1).  Returns XB_ERR_UNSUPPORTED when an operand breaks the TMA rules
+// (the caller then uses the mma.sync kernel).
+int attention_prefill_tc(const void* q, const void* k_cache, const void* v_cache, void* out, int64_t batch,
+                         int64_t seq, int64_t n_head, int64_t n_kv_head, int64_t max_seq, int64_t pos_offset,
+                         float scale_log2, cudaStream_t s, const char* what, char* err, size_t errlen) {
+  using namespace gemm;
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (!al16(q) || !al16(k_cache) || !al16(v_cache) || !al16(out)) return XB_ERR_UNSUPPORTED;
+  const int64_t total = pos_offset + seq;
+  const int64_t nqt = (seq + kAtBQ - 1) / kAtBQ;
+  const int64_t nbh = batch * n_head;
+  if (nqt * nbh > 0x7fffffffLL || total > 0x7fffffffLL) return XB_ERR_UNSUPPORTED;
+  AtMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  int rc = make_map_3d_sw128(&maps.q, q, (uint64_t)seq, (uint64_t)nbh, 64, (uint64_t)(seq * 64), kAtBQ, err, errlen);
+  if (rc) return rc;
+  rc = make_map_3d_sw128(&maps.k, k_cache, (uint64_t)total, (uint64_t)(batch * n_kv_head), 64,
+                         (uint64_t)(max_seq * 64), kAtBK, err, errlen);
+  if (rc) return rc;
+  rc = make_map_3d_sw128(&maps.v, v_cache, (uint64_t)total, (uint64_t)(batch * n_kv_head), 64,
+                         (uint64_t)(max_seq * 64), kAtBK, err, errlen);
+  if (rc) return rc;
+  AtArgs args;
+  args.out = static_cast<__nv_bfloat16*>(out);
+  args.H = (int)n_head;
+  args.KVH = (int)n_kv_head;
+  args.S = (int)seq;
+  args.total = (int)total;
+  args.pos = (int)pos_offset;
+  args.nqt = (int)nqt;
+  args.nbh = (int)nbh;
+  args.scale_log2 = scale_log2;
+  cudaError_t e = once_per_device(reinterpret_cast<const void*>(attn_prefill_tc_kernel), kOnceSmem, [](int*) {
+    return cudaFuncSetAttribute(attn_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtSmem);
+  });
+  if (e != cudaSuccess) {
+    set_err(err, errlen, "%s: kernel setup: %s", what, cudaGetErrorString(e));
+    return XB_ERR_CUDA;
+  }
+  launch_k(attn_prefill_tc_kernel, dim3((unsigned)(nqt * nbh)), 192, kAtSmem, s, maps, args);
+  return check_launch(what, err, errlen);
+}
+
+}  // namespace xb

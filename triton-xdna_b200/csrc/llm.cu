@@ -1210,6 +1210,23 @@ static bool head_attn_enabled() {
   return on == 1;
 }
 
+namespace xb {
+int attention_prefill_tc(const void* q, const void* k_cache, const void* v_cache, void* out, int64_t batch,
+                         int64_t seq, int64_t n_head, int64_t n_kv_head, int64_t max_seq, int64_t pos_offset,
+                         float scale_log2, cudaStream_t s, const char* what, char* err, size_t errlen);
+}  // namespace xb
+
+// Prefill attention on tcgen05 (csrc/gemm.cu) when XB_ATTN_TC=1 in the
+// environment, else the mma.sync kernel above.
+static bool attn_tc_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("XB_ATTN_TC");
+    on = (v && v[0] == '1') ? 1 : 0;
+  }
+  return on == 1;
+}
+
 extern "C" int xb_attention_workspace_size(int64_t batch, int64_t seq, int64_t n_head, int64_t n_kv_head,
                                            int64_t pos_offset, size_t* bytes, char* err, size_t errlen) {
   if (!bytes || batch < 0 || seq < 0 || n_head <= 0 || n_kv_head <= 0 || pos_offset < 0) {
@@ -1332,6 +1349,11 @@ extern "C" int xb_attention_bf16(const void* q, const void* k_cache, const void*
       launch_k(attn_decode_combine_kernel, dim3((unsigned)batch, (unsigned)n_head), kHD, 0, s, (const float*)ws,
                static_cast<bf16*>(out), Hh, KV, nchunks);
   } else {
+    if (attn_tc_enabled()) {  // tcgen05 kernel; operands that break its TMA rules take the mma.sync kernel
+      const int rc = xb::attention_prefill_tc(q, k_cache, v_cache, out, batch, seq, n_head, n_kv_head, max_seq,
+                                              pos_offset, scale_log2, s, what, err, errlen);
+      if (rc != XB_ERR_UNSUPPORTED) return rc;
+    }
     dim3 grid((unsigned)((seq + kBQ - 1) / kBQ), (unsigned)(batch * n_head));
     launch_k(attn_prefill_kernel, grid, 128, 0, s, static_cast<const bf16*>(q), static_cast<const bf16*>(k_cache),
                                              static_cast<const bf16*>(v_cache), static_cast<bf16*>(out),
