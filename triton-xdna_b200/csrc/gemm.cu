@@ -54,6 +54,12 @@ constexpr uint64_t kWaitLimit = 2000000000ull;  // 2 s per wait: far above any l
 #ifndef XB_I8_PAIR_STAGES
 #define XB_I8_PAIR_STAGES 6
 #endif
+// L2 cache policies of the tiled GEMMs: bit 0 = C stores evict-first (C is
+// written once), bit 1 = A loads evict-last (an A panel is reused by every
+// column tile of its raster group)
+#ifndef XB_L2_HINTS
+#define XB_L2_HINTS 0
+#endif
 
 enum Kind { kBf16 = 0, kInt8 = 1, kInt16Limbs = 2 };
 // kOutSwiglu: W interleaves 64-row blocks of gate and up rows (block 2b =
@@ -318,9 +324,17 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
             if constexpr (PAIR) tma_load_2d_pair(dst, map, fb, c0, c1);
             else tma_load_2d(dst, map, &full_bar[s], c0, c1);
           };
+          auto load_a = [&](void* dst, const CUtensorMap* map, int32_t c0, int32_t c1) {
+            if constexpr ((XB_L2_HINTS & 2) != 0 && !TRANS) {
+              if constexpr (PAIR) tma_load_2d_pair_hint(dst, map, fb, c0, c1, l2_policy_evict_last());
+              else tma_load_2d_hint(dst, map, &full_bar[s], c0, c1, l2_policy_evict_last());
+            } else {
+              load(dst, map, c0, c1);
+            }
+          };
           uint8_t* st = smem + s * C::STAGE_BYTES;
           for (int p = 0; p < C::PLANES; ++p) {
-            if (!pre) load(st + p * C::A_BYTES, &maps.a[p], kb * C::BK, arow);
+            if (!pre) load_a(st + p * C::A_BYTES, &maps.a[p], kb * C::BK, arow);
             uint8_t* sb = st + C::PLANES * C::A_BYTES + p * C::B_BYTES;
             if (B_KMAJOR) {
               load(sb, &maps.b[p], kb * C::BK, bcol);
@@ -657,7 +671,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) {
-              tma_store_2d(&maps.c, stg, col0, row);
+              if constexpr ((XB_L2_HINTS & 1) != 0) tma_store_2d_hint(&maps.c, stg, col0, row, l2_policy_evict_first());
+              else tma_store_2d(&maps.c, stg, col0, row);
               bulk_commit();
             }
             continue;
@@ -774,8 +789,11 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
                   const int r = k * kRowsPer + lane / kPieces, p = lane % kPieces;
                   const int phys = OUT == kOutBf16 ? (p ^ ((r >> 1) & 3)) : (p ^ (r & 7));
                   const int4 val = *reinterpret_cast<const int4*>(stg + r * (kPieces * 16) + phys * 16);
-                  if (row0 + r < args.m)
-                    *reinterpret_cast<int4*>(cb + ((int64_t)r * args.ldc) * kEsz + p * 16) = val;
+                  if (row0 + r < args.m) {
+                    int4* dst = reinterpret_cast<int4*>(cb + ((int64_t)r * args.ldc) * kEsz + p * 16);
+                    if constexpr ((XB_L2_HINTS & 1) != 0 && !PEERS) __stcs(dst, val);
+                    else *dst = val;
+                  }
                 }
               }
               __syncwarp();  // staging free for the next chunk
