@@ -349,9 +349,9 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
       if (leader) {
         // Drain: every load issued into a stage must have landed before exit
         // (also after an abort; one time limit for all stages).
-        const uint64_t deadline = globaltimer_ns() + kWaitLimit;
+        uint64_t deadline = 0;
         for (int s = 0; s < C::STAGES; ++s)
-          if (issued[s] && !mbar_wait_deadline(&full_bar[s], (issued[s] - 1) & 1, deadline)) fail();
+          if (issued[s] && !mbar_wait_deadline(&full_bar[s], (issued[s] - 1) & 1, &deadline, kWaitLimit)) fail();
       } else if (!ok) {
         // The odd CTA's loads complete on the leader's barriers: after a
         // failure give any load still in flight time to land (loads take
@@ -435,7 +435,8 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
         if constexpr (PAIR) tc_commit2(smem_u32(&drain_bar));
         else tc_commit(&drain_bar);
         // every issued MMA has completed before TMEM is released (also after an abort)
-        if (!mbar_wait_deadline(&drain_bar, 0, globaltimer_ns() + kWaitLimit)) fail();
+        uint64_t deadline = 0;
+        if (!mbar_wait_deadline(&drain_bar, 0, &deadline, kWaitLimit)) fail();
       }
     }
   } else {
@@ -2066,9 +2067,9 @@ __global__ void __launch_bounds__(192, 1) decode_linear_kernel(const __grid_cons
       }
       // every load issued must have landed before the ring is reused or the CTA
       // exits (also after an abort; one time limit for all of them)
-      const uint64_t deadline = globaltimer_ns() + kWaitLimit;
+      uint64_t deadline = 0;
       for (int i = issued > STAGES ? issued - STAGES : 0; i < issued; ++i)
-        if (!mbar_wait_deadline(&full_bar[i % STAGES], (i / STAGES) & 1, deadline)) fail();
+        if (!mbar_wait_deadline(&full_bar[i % STAGES], (i / STAGES) & 1, &deadline, kWaitLimit)) fail();
     } else {
       pdl_wait();
       pdl_trigger();
@@ -2568,7 +2569,9 @@ int launch_decode(const DecInput& in, const void* W, int64_t N, int64_t K, int64
     smem = (deep ? 7 : 3) * kDecStage + kDecRecvBytes + 1024;
     cudaError_t e = once_per_device(reinterpret_cast<const void*>(kernel), kOnceSmem, [&](int*) {
       cudaError_t r = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-      if (r == cudaSuccess) r = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      // clusters above the portable 8 only when asked for (XB_DECODE_CLUSTER_MAX)
+      if (r == cudaSuccess && decode_cluster_max() > 8)
+        r = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       return r;
     });
     if (e != cudaSuccess) {
@@ -3515,10 +3518,10 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
         issued[st] = j / kAtStages + 1;
       }
       // every load issued must have landed before the CTA exits (also after an abort)
-      const uint64_t deadline = globaltimer_ns() + kWaitLimit;
-      if (!mbar_wait_deadline(&q_full, 0, deadline)) fail();
+      uint64_t deadline = 0;
+      if (!mbar_wait_deadline(&q_full, 0, &deadline, kWaitLimit)) fail();
       for (int st = 0; st < kAtStages; ++st)
-        if (issued[st] && !mbar_wait_deadline(&kv_full[st], (issued[st] - 1) & 1, deadline)) fail();
+        if (issued[st] && !mbar_wait_deadline(&kv_full[st], (issued[st] - 1) & 1, &deadline, kWaitLimit)) fail();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -3555,7 +3558,8 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
       }
       if (any) {  // every issued MMA completes before TMEM is released (also after an abort)
         tc_commit(&drain_bar);
-        if (!mbar_wait_deadline(&drain_bar, 0, globaltimer_ns() + kWaitLimit)) fail();
+        uint64_t deadline = 0;
+        if (!mbar_wait_deadline(&drain_bar, 0, &deadline, kWaitLimit)) fail();
       }
     }
   } else {

@@ -53,12 +53,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
 }
 
 // Exit drain: wait for a phase regardless of any abort (asynchronous copies
-// or MMAs still in flight must finish before the CTA leaves), until the
-// globaltimer reaches `deadline_ns`.  Returns false at the deadline.
-__device__ __forceinline__ bool mbar_wait_deadline(uint64_t* bar, uint32_t parity, uint64_t deadline_ns) {
-  for (uint32_t i = 0;; ++i) {
+// or MMAs still in flight must finish before the CTA leaves).  The waits of
+// one drain share one time limit: *deadline is 0 until a wait first has to
+// spin, then the globaltimer value at which every later wait gives up too.
+// Returns false at the deadline.
+__device__ __forceinline__ bool mbar_wait_deadline(uint64_t* bar, uint32_t parity, uint64_t* deadline,
+                                                   uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  if (*deadline == 0) *deadline = globaltimer_ns() + limit_ns;
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255) == 255 && globaltimer_ns() > deadline_ns) return false;
+    if ((i & 255) == 0 && globaltimer_ns() > *deadline) return false;
   }
 }
 
