@@ -1560,13 +1560,13 @@ bool lines_enabled() {
   return on == 1;
 }
 
-// Epilogue warps of bf16-output / fused-QKV CTA-pair tiles: XB_GEMM_EPI=8 in
-// the environment selects eight (two per TMEM lane quarter), else four.
+// Epilogue warps of bf16-output / fused-QKV CTA-pair tiles: eight (two per
+// TMEM lane quarter); XB_GEMM_EPI=4 in the environment selects four.
 bool epi8_enabled() {
   static int on = -1;
   if (on < 0) {
     const char* v = getenv("XB_GEMM_EPI");
-    on = (v && atoi(v) == 8) ? 1 : 0;
+    on = (v && atoi(v) == 4) ? 0 : 1;
   }
   return on == 1;
 }
@@ -3396,18 +3396,20 @@ extern "C" int xb_device_status(void* stream, int* status, char* err, size_t err
 // (exponentials in base 2 on the pre-scaled S).
 //
 // One CTA owns 128 query rows of one (sequence, head); key tiles of 64 keys.
-// Warp 0 streams Q once and K / V tiles through a two-slot ring with TMA
-// (3-D tensor maps whose key extent is the context length, so keys past it
-// arrive as zeros); warp 1 issues the tcgen05 MMAs: S = Q K^T into 64 TMEM
-// columns, then, once P is in shared memory, the tile's P V into 64 more
-// (a fresh accumulator per tile).  Warps 2-5 own one query row per thread:
-// they read the row's S straight from TMEM (no cross-thread reductions),
-// write bf16(P) into a 128-byte-swizzled K-major tile for the P V MMA, and
-// fold the tile's P V into the row's fp32 accumulator held in registers
-// (acc = alpha * acc + PV).  Two CTAs share an SM (65 KB shared memory, 128
-// TMEM columns each), so one CTA's softmax overlaps the other's MMAs.  CTAs
-// take the query tiles with the most key tiles first.  Every wait is bounded
-// (XB_ERR_TIMEOUT through the GEMM status word).
+// Warp 0 loads Q once and K / V tiles into a three-slot ring with TMA (3-D
+// tensor maps whose key extent is the context length, so keys past it arrive
+// as zeros).  Warp 1 issues the tcgen05 MMAs: S_j = Q K_j^T into one of two
+// 64-column TMEM buffers, then, once P_j is in shared memory, P_j V_j into one
+// of two more (a fresh accumulator per tile).  Warps 2-5 own one query row per
+// thread: the row's scores come straight from TMEM (no cross-thread
+// reductions), bf16(P) goes into one of two 128-byte-swizzled K-major tiles,
+// and the tile's P V is folded into the row's fp32 accumulator in registers.
+// Everything is double-buffered, so the MMAs of S_{j+1} and P_j V_j run while
+// the softmax works on tile j and folds tile j - 1: the softmax warps stream
+// through the tiles instead of waiting on each hand-off.  Two CTAs share an
+// SM (97 KB shared memory, 256 TMEM columns each).  CTAs take the query tiles
+// with the most key tiles first.  Every wait is bounded (XB_ERR_TIMEOUT
+// through the GEMM status word).
 namespace xb {
 namespace gemm {
 
@@ -3415,9 +3417,9 @@ constexpr int kAtBQ = 128;                 // query rows per CTA (TMEM lanes)
 constexpr int kAtBK = 64;                  // keys per tile
 constexpr int kAtQBytes = kAtBQ * 128;     // Q tile: 128 rows x 64 bf16
 constexpr int kAtKVBytes = kAtBK * 128;    // K or V tile: 64 keys x 64 bf16
-constexpr int kAtStages = 2;               // K / V ring slots
+constexpr int kAtStages = 3;               // K / V ring slots
 constexpr int kAtPBytes = kAtBQ * 128;     // P tile: 128 rows x 64 keys bf16
-constexpr int kAtSmem = kAtQBytes + kAtStages * 2 * kAtKVBytes + kAtPBytes + 1024;
+constexpr int kAtSmem = kAtQBytes + kAtStages * 2 * kAtKVBytes + 2 * kAtPBytes + 1024;
 
 // two floats -> packed bf16 pair, the first in the low half (lower address)
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -3440,7 +3442,8 @@ struct AtArgs {
 __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_constant__ AtMaps maps,
                                                                   const AtArgs args) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full, s_full, p_full, o_full, drain_bar;
+  __shared__ __align__(8) uint64_t q_full, drain_bar;
+  __shared__ __align__(8) uint64_t s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2];
   __shared__ __align__(8) uint64_t kv_full[kAtStages], kv_empty[kAtStages];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
@@ -3464,13 +3467,17 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
-    mbar_init(&s_full, 1);
-    mbar_init(&p_full, 128);
-    mbar_init(&o_full, 1);
     mbar_init(&drain_bar, 1);
-    for (int s = 0; s < kAtStages; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_empty[i], 128);
+    }
+    for (int i = 0; i < kAtStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
     }
     abort_flag = 0;
     mbar_fence_init();
@@ -3481,14 +3488,14 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
     prefetch_tmap(&maps.v);
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_base_sh, 128);
+    tmem_alloc(&tmem_base_sh, 256);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
-  const uint32_t tS = tmem_base, tO = tmem_base + 64;  // S and the tile's P V, 64 columns each
+  // TMEM columns: S buffers [0, 64) and [64, 128), P V buffers [128, 192) and [192, 256)
   pdl_wait();  // Q and the caches are written by the previous kernel
   pdl_trigger();
 
@@ -3500,7 +3507,9 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      uint32_t issued[kAtStages] = {0, 0};
+      uint32_t issued[kAtStages];
+#pragma unroll
+      for (int i = 0; i < kAtStages; ++i) issued[i] = 0;
       mbar_arrive_expect_tx(&q_full, kAtQBytes);
       tma_load_3d(smem, &maps.q, &q_full, 0, qs, bh);
       const int kvrow = b * args.KVH + kvh;
@@ -3528,34 +3537,50 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
     if (lane == 0) {
       constexpr uint32_t kIdS = umma_idesc(1, 1, 1, 0, 0, kAtBQ, kAtBK);  // Q (K-major) x K tile (K-major)
       constexpr uint32_t kIdO = umma_idesc(1, 1, 1, 0, 1, kAtBQ, 64);     // P (K-major) x V tile (MN-major)
-      bool any = false;
-      if (!mbar_wait(&q_full, 0, kWaitLimit, &abort_flag)) fail();
-      for (int j = 0; j < nkt && !abort_flag; ++j) {
-        const int st = j % kAtStages;
-        if (!mbar_wait(&kv_full[st], (j / kAtStages) & 1, kWaitLimit, &abort_flag)) {
-          fail();
-          break;
-        }
+      bool any = false, ok = true;
+      // P_i V_i into P V buffer i & 1, once P_i is written and that buffer's previous result was read
+      auto pv = [&](int i) -> bool {
+        const int ob = i & 1;
+        if (!mbar_wait(&p_full[ob], (i >> 1) & 1, kWaitLimit, &abort_flag)) return false;
+        if (i >= 2 && !mbar_wait(&o_empty[ob], ((i - 2) >> 1) & 1, kWaitLimit, &abort_flag)) return false;
         tc_fence_after();
-        const uint32_t sk = sKV + st * 2 * kAtKVBytes, sv = sk + kAtKVBytes;
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks)  // head dim in steps of 16
-          mma_f16(tS, umma_desc_sw128(sQ + ks * 32, 16, 1024), umma_desc_sw128(sk + ks * 32, 16, 1024), kIdS,
-                  ks > 0 ? 1u : 0u);
-        any = true;
-        tc_commit(&s_full);
-        if (!mbar_wait(&p_full, j & 1, kWaitLimit, &abort_flag)) {
-          fail();
-          break;
-        }
-        tc_fence_after();
+        const uint32_t sv = sKV + (i % kAtStages) * 2 * kAtKVBytes + kAtKVBytes;
+        const uint32_t pb = sP + ob * kAtPBytes;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)  // keys in steps of 16
-          mma_f16(tO, umma_desc_sw128(sP + ks * 32, 16, 1024),
+          mma_f16(tmem_base + 128 + ob * 64, umma_desc_sw128(pb + ks * 32, 16, 1024),
                   umma_desc_sw128(sv + ks * 16 * 128, kAtKVBytes, 1024), kIdO, ks > 0 ? 1u : 0u);
-        tc_commit(&o_full);
-        tc_commit(&kv_empty[st]);
+        tc_commit(&o_full[ob]);
+        tc_commit(&kv_empty[i % kAtStages]);
+        return true;
+      };
+      if (!mbar_wait(&q_full, 0, kWaitLimit, &abort_flag)) {
+        fail();
+        ok = false;
       }
+      for (int j = 0; j < nkt && ok; ++j) {
+        // S_j into S buffer j & 1 (its previous scores, S_{j-2}, read by the softmax)
+        const int st = j % kAtStages, sb = j & 1;
+        if (!mbar_wait(&kv_full[st], (j / kAtStages) & 1, kWaitLimit, &abort_flag) ||
+            (j >= 2 && !mbar_wait(&s_empty[sb], ((j - 2) >> 1) & 1, kWaitLimit, &abort_flag))) {
+          fail();
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sk = sKV + st * 2 * kAtKVBytes;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)  // head dim in steps of 16
+          mma_f16(tmem_base + sb * 64, umma_desc_sw128(sQ + ks * 32, 16, 1024),
+                  umma_desc_sw128(sk + ks * 32, 16, 1024), kIdS, ks > 0 ? 1u : 0u);
+        any = true;
+        tc_commit(&s_full[sb]);
+        if (j >= 1 && !pv(j - 1)) {
+          fail();
+          ok = false;
+        }
+      }
+      if (ok && nkt > 0 && !pv(nkt - 1)) fail();
       if (any) {  // every issued MMA completes before TMEM is released (also after an abort)
         tc_commit(&drain_bar);
         uint64_t deadline = 0;
@@ -3571,19 +3596,37 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
     float o[64];
 #pragma unroll
     for (int c = 0; c < 64; ++c) o[c] = 0.0f;
-    float m = -INFINITY, l = 0.0f;
+    float m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
     bool ok = true;
+    // acc = alpha_i * acc + P_i V_i, once P_i V_i is in TMEM
+    auto fold = [&](int i, float alpha) -> bool {
+      const int ob = i & 1;
+      if (!mbar_wait(&o_full[ob], (i >> 1) & 1, kWaitLimit, &abort_flag)) return false;
+      tc_fence_after();
+      uint32_t ov[64];
+      tmem_ld_32x32b_x32(tmem_base + 128 + ob * 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+      tmem_ld_32x32b_x32(tmem_base + 128 + ob * 64 + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&o_empty[ob]);
+#pragma unroll
+      for (int c = 0; c < 64; ++c) o[c] = fmaf(o[c], alpha, __uint_as_float(ov[c]));
+      return true;
+    };
     for (int j = 0; j < nkt; ++j) {
-      if (!mbar_wait(&s_full, j & 1, kWaitLimit, &abort_flag)) {
+      const int sb = j & 1;
+      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, kWaitLimit, &abort_flag)) {
         fail();
         ok = false;
         break;
       }
       tc_fence_after();
       uint32_t sv[64];
-      tmem_ld_32x32b_x32(tS + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tmem_ld_32x32b_x32(tS + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      tmem_ld_32x32b_x32(tmem_base + sb * 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+      tmem_ld_32x32b_x32(tmem_base + sb * 64 + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
       tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);  // S buffer free for S_{j+2}
       const int k0 = j * kAtBK;
       const bool whole = k0 + kAtBK <= args.total && k0 + kAtBK - 1 <= qpos;  // no key of the tile masked
       float s[64];
@@ -3606,7 +3649,9 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
         rs += s[c];
       }
       l = l * alpha + rs;
-      // bf16(P) row r -> the K-major swizzled tile (16-byte chunk c8 at c8 ^ (r & 7))
+      // bf16(P_j) row r -> P buffer j & 1 (read last by P_{j-2} V, folded in the previous
+      // iteration); 16-byte chunk c8 at c8 ^ (r & 7) of the 128-byte-swizzled K-major tile
+      uint8_t* pt = sPg + sb * kAtPBytes + r * 128;
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         uint4 w;
@@ -3614,24 +3659,20 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
         w.y = pack_bf16x2(s[c8 * 8 + 2], s[c8 * 8 + 3]);
         w.z = pack_bf16x2(s[c8 * 8 + 4], s[c8 * 8 + 5]);
         w.w = pack_bf16x2(s[c8 * 8 + 6], s[c8 * 8 + 7]);
-        *reinterpret_cast<uint4*>(sPg + r * 128 + ((c8 ^ (r & 7)) << 4)) = w;
+        *reinterpret_cast<uint4*>(pt + ((c8 ^ (r & 7)) << 4)) = w;
       }
       fence_proxy_async_smem();  // P, before the MMA (async proxy) reads it
-      tc_fence_before();         // S read, before the next S MMA overwrites it
-      mbar_arrive(&p_full);
-      if (!mbar_wait(&o_full, j & 1, kWaitLimit, &abort_flag)) {
+      mbar_arrive(&p_full[sb]);
+      if (j >= 1 && !fold(j - 1, alpha_prev)) {
         fail();
         ok = false;
         break;
       }
-      tc_fence_after();
-      uint32_t ov[64];
-      tmem_ld_32x32b_x32(tO + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
-      tmem_ld_32x32b_x32(tO + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
-      tmem_ld_wait();
-#pragma unroll
-      for (int c = 0; c < 64; ++c) o[c] = fmaf(o[c], alpha, __uint_as_float(ov[c]));
-      tc_fence_before();  // this tile's P V read, before the next tile's P V overwrites it
+      alpha_prev = alpha;
+    }
+    if (ok && !fold(nkt - 1, alpha_prev)) {
+      fail();
+      ok = false;
     }
     if (ok && r < rows) {
       const float inv = l > 0.0f ? 1.0f / l : 0.0f;
@@ -3651,7 +3692,7 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 128);
+    tmem_dealloc(tmem_base, 256);
   }
 }
 
