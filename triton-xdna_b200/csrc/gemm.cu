@@ -3395,8 +3395,9 @@ extern "C" int xb_device_status(void* stream, int* status, char* err, size_t err
 // acc = alpha * acc + bf16(P) @ V, l = alpha * l + rowsum(P), out = acc / l
 // (exponentials in base 2 on the pre-scaled S).
 //
-// One CTA owns 128 query rows of one (sequence, head); key tiles of 64 keys.
-// Warp 0 loads Q once and K / V tiles into a three-slot ring with TMA (3-D
+// A unit is 128 query rows of one (sequence, head); key tiles of 64 keys.
+// Two persistent CTAs per SM walk the units.  Warp 0 loads each unit's Q and
+// its K / V tiles into a three-slot ring with TMA (3-D
 // tensor maps whose key extent is the context length, so keys past it arrive
 // as zeros).  Warp 1 issues the tcgen05 MMAs: S_j = Q K_j^T into one of two
 // 64-column TMEM buffers, then, once P_j is in shared memory, P_j V_j into one
@@ -3407,9 +3408,9 @@ extern "C" int xb_device_status(void* stream, int* status, char* err, size_t err
 // Everything is double-buffered, so the MMAs of S_{j+1} and P_j V_j run while
 // the softmax works on tile j and folds tile j - 1: the softmax warps stream
 // through the tiles instead of waiting on each hand-off.  Two CTAs share an
-// SM (97 KB shared memory, 256 TMEM columns each).  CTAs take the query tiles
-// with the most key tiles first.  Every wait is bounded (XB_ERR_TIMEOUT
-// through the GEMM status word).
+// SM (97 KB shared memory, 256 TMEM columns each), and the units with the
+// most key tiles come first.  Every wait is bounded (XB_ERR_TIMEOUT through
+// the GEMM status word).
 namespace xb {
 namespace gemm {
 
@@ -3439,10 +3440,33 @@ struct AtArgs {
   float scale_log2;
 };
 
+// Unit u (query tile, sequence * head) of the causal prefill: the query tiles
+// with the most key tiles come first.
+struct AtUnit {
+  int b, h, kvh, bh, qs, rows, nkt;
+};
+__device__ __forceinline__ AtUnit at_unit(const AtArgs& a, int u) {
+  AtUnit t;
+  const int qt = a.nqt - 1 - u / a.nbh;
+  t.bh = u % a.nbh;
+  t.b = t.bh / a.H;
+  t.h = t.bh - t.b * a.H;
+  t.kvh = t.h / (a.H / a.KVH);
+  t.qs = qt * kAtBQ;
+  t.rows = min(kAtBQ, a.S - t.qs);
+  const int kmax = min(a.total, a.pos + t.qs + t.rows);  // keys the last row sees
+  t.nkt = (kmax + kAtBK - 1) / kAtBK;
+  return t;
+}
+
+// Persistent: each CTA walks units blockIdx.x, blockIdx.x + gridDim.x, ...;
+// barrier phases, ring slots and TMEM buffers continue across units (tile
+// counters are global to the CTA), so the next unit's Q and K / V loads and
+// its first scores overlap the current unit's last tiles.
 __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_constant__ AtMaps maps,
                                                                   const AtArgs args) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full, drain_bar;
+  __shared__ __align__(8) uint64_t q_full, q_empty, drain_bar;
   __shared__ __align__(8) uint64_t s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2];
   __shared__ __align__(8) uint64_t kv_full[kAtStages], kv_empty[kAtStages];
   __shared__ uint32_t tmem_base_sh;
@@ -3453,20 +3477,11 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
   uint8_t* smem = smem_raw + (base_u32 - smem_u32(smem_raw));
   const uint32_t sQ = base_u32, sKV = base_u32 + kAtQBytes, sP = sKV + kAtStages * 2 * kAtKVBytes;
   uint8_t* sPg = smem + kAtQBytes + kAtStages * 2 * kAtKVBytes;
-
-  // unit -> (query tile, sequence * head): the query tiles with the most key tiles first
-  const int u = (int)blockIdx.x;
-  const int qt = args.nqt - 1 - u / args.nbh;
-  const int bh = u % args.nbh;
-  const int b = bh / args.H, h = bh - b * args.H;
-  const int kvh = h / (args.H / args.KVH);
-  const int qs = qt * kAtBQ;
-  const int rows = min(kAtBQ, args.S - qs);
-  const int kmax = min(args.total, args.pos + qs + rows);  // keys the last row sees
-  const int nkt = (kmax + kAtBK - 1) / kAtBK;
+  const int units = args.nqt * args.nbh;
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
+    mbar_init(&q_empty, 1);
     mbar_init(&drain_bar, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -3510,25 +3525,36 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
       uint32_t issued[kAtStages];
 #pragma unroll
       for (int i = 0; i < kAtStages; ++i) issued[i] = 0;
-      mbar_arrive_expect_tx(&q_full, kAtQBytes);
-      tma_load_3d(smem, &maps.q, &q_full, 0, qs, bh);
-      const int kvrow = b * args.KVH + kvh;
-      for (int j = 0; j < nkt; ++j) {
-        const int st = j % kAtStages;
-        const uint32_t ph = (j / kAtStages) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, kWaitLimit, &abort_flag)) {
+      int g = 0, lu = 0;  // tiles and units of this CTA so far
+      bool ok = true, q_issued = false;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++lu) {
+        const AtUnit t = at_unit(args, u);
+        // Q of this unit once the previous unit's last S MMA has read the old one
+        if (lu > 0 && !mbar_wait(&q_empty, (lu - 1) & 1, kWaitLimit, &abort_flag)) {
           fail();
           break;
         }
-        uint8_t* dst = smem + kAtQBytes + st * 2 * kAtKVBytes;
-        mbar_arrive_expect_tx(&kv_full[st], 2 * kAtKVBytes);
-        tma_load_3d(dst, &maps.k, &kv_full[st], 0, j * kAtBK, kvrow);
-        tma_load_3d(dst + kAtKVBytes, &maps.v, &kv_full[st], 0, j * kAtBK, kvrow);
-        issued[st] = j / kAtStages + 1;
+        mbar_arrive_expect_tx(&q_full, kAtQBytes);
+        tma_load_3d(smem, &maps.q, &q_full, 0, t.qs, t.bh);
+        q_issued = true;
+        const int kvrow = t.b * args.KVH + t.kvh;
+        for (int j = 0; j < t.nkt; ++j, ++g) {
+          const int st = g % kAtStages;
+          if (!mbar_wait(&kv_empty[st], ((g / kAtStages) & 1) ^ 1, kWaitLimit, &abort_flag)) {
+            fail();
+            ok = false;
+            break;
+          }
+          uint8_t* dst = smem + kAtQBytes + st * 2 * kAtKVBytes;
+          mbar_arrive_expect_tx(&kv_full[st], 2 * kAtKVBytes);
+          tma_load_3d(dst, &maps.k, &kv_full[st], 0, j * kAtBK, kvrow);
+          tma_load_3d(dst + kAtKVBytes, &maps.v, &kv_full[st], 0, j * kAtBK, kvrow);
+          issued[st] = g / kAtStages + 1;
+        }
       }
       // every load issued must have landed before the CTA exits (also after an abort)
       uint64_t deadline = 0;
-      if (!mbar_wait_deadline(&q_full, 0, &deadline, kWaitLimit)) fail();
+      if (q_issued && !mbar_wait_deadline(&q_full, (lu - 1) & 1, &deadline, kWaitLimit)) fail();
       for (int st = 0; st < kAtStages; ++st)
         if (issued[st] && !mbar_wait_deadline(&kv_full[st], (issued[st] - 1) & 1, &deadline, kWaitLimit)) fail();
     }
@@ -3538,49 +3564,55 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
       constexpr uint32_t kIdS = umma_idesc(1, 1, 1, 0, 0, kAtBQ, kAtBK);  // Q (K-major) x K tile (K-major)
       constexpr uint32_t kIdO = umma_idesc(1, 1, 1, 0, 1, kAtBQ, 64);     // P (K-major) x V tile (MN-major)
       bool any = false, ok = true;
-      // P_i V_i into P V buffer i & 1, once P_i is written and that buffer's previous result was read
-      auto pv = [&](int i) -> bool {
-        const int ob = i & 1;
-        if (!mbar_wait(&p_full[ob], (i >> 1) & 1, kWaitLimit, &abort_flag)) return false;
-        if (i >= 2 && !mbar_wait(&o_empty[ob], ((i - 2) >> 1) & 1, kWaitLimit, &abort_flag)) return false;
+      // P_g V_g into P V buffer g & 1, once P_g is written and that buffer's previous result was read
+      auto pv = [&](int gi) -> bool {
+        const int ob = gi & 1;
+        if (!mbar_wait(&p_full[ob], (gi >> 1) & 1, kWaitLimit, &abort_flag)) return false;
+        if (gi >= 2 && !mbar_wait(&o_empty[ob], ((gi - 2) >> 1) & 1, kWaitLimit, &abort_flag)) return false;
         tc_fence_after();
-        const uint32_t sv = sKV + (i % kAtStages) * 2 * kAtKVBytes + kAtKVBytes;
+        const uint32_t sv = sKV + (gi % kAtStages) * 2 * kAtKVBytes + kAtKVBytes;
         const uint32_t pb = sP + ob * kAtPBytes;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)  // keys in steps of 16
           mma_f16(tmem_base + 128 + ob * 64, umma_desc_sw128(pb + ks * 32, 16, 1024),
                   umma_desc_sw128(sv + ks * 16 * 128, kAtKVBytes, 1024), kIdO, ks > 0 ? 1u : 0u);
         tc_commit(&o_full[ob]);
-        tc_commit(&kv_empty[i % kAtStages]);
+        tc_commit(&kv_empty[gi % kAtStages]);
         return true;
       };
-      if (!mbar_wait(&q_full, 0, kWaitLimit, &abort_flag)) {
-        fail();
-        ok = false;
-      }
-      for (int j = 0; j < nkt && ok; ++j) {
-        // S_j into S buffer j & 1 (its previous scores, S_{j-2}, read by the softmax)
-        const int st = j % kAtStages, sb = j & 1;
-        if (!mbar_wait(&kv_full[st], (j / kAtStages) & 1, kWaitLimit, &abort_flag) ||
-            (j >= 2 && !mbar_wait(&s_empty[sb], ((j - 2) >> 1) & 1, kWaitLimit, &abort_flag))) {
+      int g = 0, lu = 0;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++lu) {
+        const AtUnit t = at_unit(args, u);
+        if (!mbar_wait(&q_full, lu & 1, kWaitLimit, &abort_flag)) {
           fail();
-          ok = false;
           break;
         }
-        tc_fence_after();
-        const uint32_t sk = sKV + st * 2 * kAtKVBytes;
+        for (int j = 0; j < t.nkt; ++j, ++g) {
+          // S_g into S buffer g & 1 (its previous scores, S_{g-2}, read by the softmax)
+          const int st = g % kAtStages, sb = g & 1;
+          if (!mbar_wait(&kv_full[st], (g / kAtStages) & 1, kWaitLimit, &abort_flag) ||
+              (g >= 2 && !mbar_wait(&s_empty[sb], ((g - 2) >> 1) & 1, kWaitLimit, &abort_flag))) {
+            fail();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sk = sKV + st * 2 * kAtKVBytes;
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)  // head dim in steps of 16
-          mma_f16(tmem_base + sb * 64, umma_desc_sw128(sQ + ks * 32, 16, 1024),
-                  umma_desc_sw128(sk + ks * 32, 16, 1024), kIdS, ks > 0 ? 1u : 0u);
-        any = true;
-        tc_commit(&s_full[sb]);
-        if (j >= 1 && !pv(j - 1)) {
-          fail();
-          ok = false;
+          for (int ks = 0; ks < 4; ++ks)  // head dim in steps of 16
+            mma_f16(tmem_base + sb * 64, umma_desc_sw128(sQ + ks * 32, 16, 1024),
+                    umma_desc_sw128(sk + ks * 32, 16, 1024), kIdS, ks > 0 ? 1u : 0u);
+          any = true;
+          tc_commit(&s_full[sb]);
+          if (j == t.nkt - 1) tc_commit(&q_empty);  // the unit's last S: Q may be replaced
+          if (g >= 1 && !pv(g - 1)) {
+            fail();
+            ok = false;
+            break;
+          }
         }
       }
-      if (ok && nkt > 0 && !pv(nkt - 1)) fail();
+      if (ok && g > 0 && !pv(g - 1)) fail();
       if (any) {  // every issued MMA completes before TMEM is released (also after an abort)
         tc_commit(&drain_bar);
         uint64_t deadline = 0;
@@ -3591,17 +3623,13 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
     // ------------------------------------------------------------ softmax: one query row per thread
     const int q4 = warp & 3;  // TMEM lane quarter
     const int r = q4 * 32 + lane;
-    const int qpos = args.pos + qs + r;  // absolute position of this row
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     float o[64];
-#pragma unroll
-    for (int c = 0; c < 64; ++c) o[c] = 0.0f;
-    float m = -INFINITY, l = 0.0f, alpha_prev = 1.0f;
-    bool ok = true;
-    // acc = alpha_i * acc + P_i V_i, once P_i V_i is in TMEM
-    auto fold = [&](int i, float alpha) -> bool {
-      const int ob = i & 1;
-      if (!mbar_wait(&o_full[ob], (i >> 1) & 1, kWaitLimit, &abort_flag)) return false;
+    float alpha_prev = 1.0f;
+    // acc = alpha_g * acc + P_g V_g, once P_g V_g is in TMEM
+    auto fold = [&](int gi, float alpha) -> bool {
+      const int ob = gi & 1;
+      if (!mbar_wait(&o_full[ob], (gi >> 1) & 1, kWaitLimit, &abort_flag)) return false;
       tc_fence_after();
       uint32_t ov[64];
       tmem_ld_32x32b_x32(tmem_base + 128 + ob * 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
@@ -3613,78 +3641,105 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
       for (int c = 0; c < 64; ++c) o[c] = fmaf(o[c], alpha, __uint_as_float(ov[c]));
       return true;
     };
-    for (int j = 0; j < nkt; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, kWaitLimit, &abort_flag)) {
+    bool ok = true;
+    int g = 0;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+      const AtUnit t = at_unit(args, u);
+      const int qpos = args.pos + t.qs + r;  // absolute position of this row
+#pragma unroll
+      for (int c = 0; c < 64; ++c) o[c] = 0.0f;
+      float m = -INFINITY, l = 0.0f;
+      const int g0 = g;
+      for (int j = 0; j < t.nkt; ++j, ++g) {
+        const int sb = g & 1;
+        if (!mbar_wait(&s_full[sb], (g >> 1) & 1, kWaitLimit, &abort_flag)) {
+          fail();
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sv[64];
+        tmem_ld_32x32b_x32(tmem_base + sb * 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld_32x32b_x32(tmem_base + sb * 64 + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&s_empty[sb]);  // S buffer free for S_{g+2}
+        const int k0 = j * kAtBK;
+        const bool whole = k0 + kAtBK <= args.total && k0 + kAtBK - 1 <= qpos;  // no key of the tile masked
+        // Raw scores (the scale is positive, so the max of the raw scores
+        // scales to the max of the scaled ones); masked keys become -inf.  Row
+        // max and row sum run as eight interleaved partial chains.
+        float s[64];
+        float mx8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
+        if (whole) {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            s[c] = __uint_as_float(sv[c]);
+            mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            const int key = k0 + c;
+            s[c] = (key < args.total && key <= qpos) ? __uint_as_float(sv[c]) : -INFINITY;
+            mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
+          }
+        }
+        const float mxr = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float mn = fmaxf(m, mxr * args.scale_log2);
+        const float base = mn == -INFINITY ? 0.0f : mn;
+        const float alpha = ex2_approx(m - base);
+        m = mn;
+        float rs8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) rs8[i] = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {  // P = exp2(S * scale - max): one FMA and one exponential
+          s[c] = ex2_approx(fmaf(s[c], args.scale_log2, -base));
+          rs8[c & 7] += s[c];
+        }
+        l = l * alpha + (((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7])));
+        // bf16(P_g) row r -> P buffer g & 1 (read last by P_{g-2} V, folded in the previous
+        // tile); 16-byte chunk c8 at c8 ^ (r & 7) of the 128-byte-swizzled K-major tile
+        uint8_t* pt = sPg + sb * kAtPBytes + r * 128;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint4 w;
+          w.x = pack_bf16x2(s[c8 * 8 + 0], s[c8 * 8 + 1]);
+          w.y = pack_bf16x2(s[c8 * 8 + 2], s[c8 * 8 + 3]);
+          w.z = pack_bf16x2(s[c8 * 8 + 4], s[c8 * 8 + 5]);
+          w.w = pack_bf16x2(s[c8 * 8 + 6], s[c8 * 8 + 7]);
+          *reinterpret_cast<uint4*>(pt + ((c8 ^ (r & 7)) << 4)) = w;
+        }
+        fence_proxy_async_smem();  // P, before the MMA (async proxy) reads it
+        mbar_arrive(&p_full[sb]);
+        if (g > g0 && !fold(g - 1, alpha_prev)) {  // the previous tile of this unit
+          fail();
+          ok = false;
+          break;
+        }
+        alpha_prev = alpha;
+      }
+      if (!ok || !fold(g - 1, alpha_prev)) {  // the unit's last tile
         fail();
         ok = false;
         break;
       }
-      tc_fence_after();
-      uint32_t sv[64];
-      tmem_ld_32x32b_x32(tmem_base + sb * 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tmem_ld_32x32b_x32(tmem_base + sb * 64 + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);  // S buffer free for S_{j+2}
-      const int k0 = j * kAtBK;
-      const bool whole = k0 + kAtBK <= args.total && k0 + kAtBK - 1 <= qpos;  // no key of the tile masked
-      float s[64];
-      float mx = -INFINITY;
+      if (r < t.rows) {
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        __nv_bfloat16* op = args.out + ((int64_t)t.b * args.S + t.qs + r) * ((int64_t)args.H * 64) + t.h * 64;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const int key = k0 + c;
-        const bool keep = whole || (key < args.total && key <= qpos);
-        s[c] = keep ? __uint_as_float(sv[c]) * args.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, s[c]);
-      }
-      const float mn = fmaxf(m, mx);
-      const float base = mn == -INFINITY ? 0.0f : mn;
-      const float alpha = ex2_approx(m - base);
-      m = mn;
-      float rs = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        s[c] = ex2_approx(s[c] - base);
-        rs += s[c];
-      }
-      l = l * alpha + rs;
-      // bf16(P_j) row r -> P buffer j & 1 (read last by P_{j-2} V, folded in the previous
-      // iteration); 16-byte chunk c8 at c8 ^ (r & 7) of the 128-byte-swizzled K-major tile
-      uint8_t* pt = sPg + sb * kAtPBytes + r * 128;
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        uint4 w;
-        w.x = pack_bf16x2(s[c8 * 8 + 0], s[c8 * 8 + 1]);
-        w.y = pack_bf16x2(s[c8 * 8 + 2], s[c8 * 8 + 3]);
-        w.z = pack_bf16x2(s[c8 * 8 + 4], s[c8 * 8 + 5]);
-        w.w = pack_bf16x2(s[c8 * 8 + 6], s[c8 * 8 + 7]);
-        *reinterpret_cast<uint4*>(pt + ((c8 ^ (r & 7)) << 4)) = w;
-      }
-      fence_proxy_async_smem();  // P, before the MMA (async proxy) reads it
-      mbar_arrive(&p_full[sb]);
-      if (j >= 1 && !fold(j - 1, alpha_prev)) {
-        fail();
-        ok = false;
-        break;
-      }
-      alpha_prev = alpha;
-    }
-    if (ok && !fold(nkt - 1, alpha_prev)) {
-      fail();
-      ok = false;
-    }
-    if (ok && r < rows) {
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-      __nv_bfloat16* op = args.out + ((int64_t)b * args.S + qs + r) * ((int64_t)args.H * 64) + h * 64;
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        uint4 w;
-        w.x = pack_bf16x2(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
-        w.y = pack_bf16x2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
-        w.z = pack_bf16x2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
-        w.w = pack_bf16x2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
-        *reinterpret_cast<uint4*>(op + c8 * 8) = w;
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint4 w;
+          w.x = pack_bf16x2(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
+          w.y = pack_bf16x2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
+          w.z = pack_bf16x2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
+          w.w = pack_bf16x2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
+          *reinterpret_cast<uint4*>(op + c8 * 8) = w;
+        }
       }
     }
   }
@@ -3758,7 +3813,11 @@ int attention_prefill_tc(const void* q, const void* k_cache, const void* v_cache
     set_err(err, errlen, "%s: kernel setup: %s", what, cudaGetErrorString(e));
     return XB_ERR_CUDA;
   }
-  launch_k(attn_prefill_tc_kernel, dim3((unsigned)(nqt * nbh)), 192, kAtSmem, s, maps, args);
+  int sms = 148;
+  sm_count(&sms);
+  const int64_t units = nqt * nbh;
+  const int64_t grid = units < 2 * (int64_t)sms ? units : 2 * (int64_t)sms;  // two resident CTAs per SM
+  launch_k(attn_prefill_tc_kernel, dim3((unsigned)grid), 192, kAtSmem, s, maps, args);
   return check_launch(what, err, errlen);
 }
 
