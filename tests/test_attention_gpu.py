@@ -8,6 +8,9 @@ same cache must agree.
 """
 
 import math
+import os
+import subprocess
+import sys
 
 import pytest
 import torch
@@ -195,3 +198,15 @@ def test_prefill_qkv_gemm_with_rope_epilogue_equals_linear_then_rope(B, S, H, KV
     for a, c in zip(*outs):
         assert torch.equal(a, c)
     assert ops.device_status() == 0
+
+
+def test_mma_sync_prefill_fallback_matches_oracle():
+    """The mma.sync prefill kernel (selected with XB_ATTN_TC=0, and taken for
+    operands that break the TMA rules) through the same parity tests, in a
+    child process (the selection is read once per process)."""
+    env = dict(os.environ, XB_ATTN_TC="0")
+    res = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-p", "no:cacheprovider", "-k",
+                          "(matches_oracle or long_chunks) and not fallback and not decode"],
+                         env=env, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-2000:]
+    assert " passed" in res.stdout

@@ -210,7 +210,8 @@ constexpr int kBQ = 64;        // query rows per CTA (16 per warp)
 constexpr int kBK = 64;        // keys per tile
 constexpr int kPad = kHD + 8;  // smem row pitch (elements): conflict-free fragment loads
 
-// Causal GQA attention, FlashAttention-style: a CTA of 4 warps owns 64 query
+// Causal GQA attention on mma.sync (the fallback of the tcgen05 kernel in
+// csrc/gemm.cu), FlashAttention-style: a CTA of 4 warps owns 64 query
 // rows of one (batch, head); K/V tiles of 64 keys go through shared memory;
 // S = Q K^T and O += P V run on mma.sync m16n8k16 (bf16 in, fp32 accumulate);
 // the softmax is online in fp32 with exp2.  Query row s (absolute position
@@ -1216,13 +1217,14 @@ int attention_prefill_tc(const void* q, const void* k_cache, const void* v_cache
                          float scale_log2, cudaStream_t s, const char* what, char* err, size_t errlen);
 }  // namespace xb
 
-// Prefill attention on tcgen05 (csrc/gemm.cu) when XB_ATTN_TC=1 in the
-// environment, else the mma.sync kernel above.
+// Prefill attention on tcgen05 (csrc/gemm.cu); XB_ATTN_TC=0 in the
+// environment selects the mma.sync kernel above (also taken when an operand
+// breaks the TMA alignment rules).
 static bool attn_tc_enabled() {
   static int on = -1;
   if (on < 0) {
     const char* v = getenv("XB_ATTN_TC");
-    on = (v && v[0] == '1') ? 1 : 0;
+    on = (v && v[0] == '0') ? 0 : 1;
   }
   return on == 1;
 }
