@@ -2499,6 +2499,15 @@ int decode_cluster_max() {
   return v;
 }
 
+bool decode_deep_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("XB_DECODE_DEEP");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 void decode_split(int blocks, int kblocks, int max_s, int* splits, int* kps) {
   int sms = 148;
   sm_count(&sms);
@@ -2562,8 +2571,9 @@ int launch_decode(const DecInput& in, const void* W, int64_t N, int64_t K, int64
   int smem = 0;
   for (int max_s = decode_cluster_max();;) {
     decode_split(blocks, args.kblocks, max_s, &args.splits, &args.kps);
-    // one CTA per SM with a deep ring when the grid is small, two with a short one
-    const bool deep = blocks * args.splits <= sms;
+    // one CTA per SM with a deep ring when the grid is small, two with a short
+    // one (XB_DECODE_DEEP=0 in the environment: always the short ring)
+    const bool deep = blocks * args.splits <= sms && decode_deep_enabled();
     kernel = xn ? (deep ? decode_linear_kernel<FIN, 7, true> : decode_linear_kernel<FIN, 3, true>)
                 : (deep ? decode_linear_kernel<FIN, 7, false> : decode_linear_kernel<FIN, 3, false>);
     smem = (deep ? 7 : 3) * kDecStage + kDecRecvBytes + 1024;
