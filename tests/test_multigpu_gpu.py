@@ -101,10 +101,12 @@ def _rank_main(rank, world, port):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        # ragged rows (300), ragged shard columns (partial 32-column chunks
-        # take the per-thread store path), pairs (M >= 256) and single CTAs
+        # ragged rows (300), ragged shard columns (176 int8 / 200 bf16: partial
+        # 32-column chunks take the per-thread store path; shard row pitches
+        # stay multiples of 16 bytes, as the TMA loads of B require), pairs
+        # (M >= 256) and single CTAs
         for dtype, (m, n, k) in ((torch.bfloat16, (512, 1024, 768)), (torch.int8, (300, 64 * world, 256)),
-                                 (torch.int8, (300, 88 * world, 128)), (torch.bfloat16, (200, 50 * world, 64)),
+                                 (torch.int8, (300, 176 * world, 128)), (torch.bfloat16, (200, 200 * world, 64)),
                                  (torch.bfloat16, (4096, 4096, 4096)), (torch.int8, (2048, 8192, 2048))):
             s0, ns = shard_columns(n, world)[rank]
             sm = ShardedMatmul(m, n, k, dtype)
