@@ -44,6 +44,40 @@ def test_peer_wait_times_out_and_reports_status():
                        torch.full((8,), 2.0))  # context still healthy
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_kernels_on_two_devices_in_one_process():
+    """Kernel set-up (shared-memory limits, resident cluster counts) is per
+    device: one process runs the same GEMMs and attention on device 0, then
+    device 1, then device 0 again, each checked exactly against the first."""
+    from oracle import cgemm
+    from xb200 import ops
+
+    g = torch.Generator().manual_seed(4)
+    a = torch.randint(-128, 128, (512, 384), generator=g, dtype=torch.int8)
+    b = torch.randint(-128, 128, (384, 640), generator=g, dtype=torch.int8)
+    x = torch.randn((300, 896), generator=g).to(torch.bfloat16)
+    w = (torch.randn((1152, 896), generator=g) * 0.05).to(torch.bfloat16)
+    q = torch.randn((2, 14, 100, 64), generator=g).to(torch.bfloat16)
+    kc = torch.randn((2, 2, 128, 64), generator=g).to(torch.bfloat16)
+    vc = torch.randn((2, 2, 128, 64), generator=g).to(torch.bfloat16)
+    want = cgemm.gemm_int(a, b)
+    results = []
+    for dev in (0, 1, 0):
+        with torch.cuda.device(dev):
+            d = torch.device("cuda", dev)
+            c = ops.matmul_i8(a.to(d), b.to(d))  # CTA pairs (M >= 256)
+            y = ops.linear(x.to(d), w.to(d))
+            o = torch.empty((2, 100, 14 * 64), dtype=torch.bfloat16, device=d)
+            ops.attention(q.to(d), kc.to(d), vc.to(d), o, 2, 100, 14, 2, 64, 0, 0.125)
+            torch.cuda.synchronize(d)
+            assert ops.device_status() == 0
+            results.append((c.cpu(), y.cpu(), o.cpu()))
+    assert torch.equal(results[0][0], want)
+    for r in results[1:]:
+        for got, ref in zip(r, results[0]):
+            assert torch.equal(got, ref)
+
+
 @pytest.mark.parametrize("m", [512, 200])  # CTA pairs, single CTAs
 def test_sharded_gemm_release_wait_times_out_then_proceeds(m):
     from xb200 import _lib, ops
