@@ -3411,16 +3411,14 @@ extern "C" int xb_device_status(void* stream, int* status, char* err, size_t err
 // tensor maps whose key extent is the context length, so keys past it arrive
 // as zeros).  Warp 1 issues the tcgen05 MMAs: S_j = Q K_j^T into one of two
 // 64-column TMEM buffers, then, once P_j is in shared memory, P_j V_j into one
-// of two more (a fresh accumulator per tile).  Warps 2-9 take two threads per
-// query row, each with 32 of the tile's 64 keys and 32 of the 64 output
-// columns: the scores come straight from TMEM, the two halves swap their
-// partial row maxima through shared memory, bf16(P) goes into one of two
-// 128-byte-swizzled K-major tiles, and the tile's P V is folded into the
-// row's fp32 accumulator in registers.
+// of two more (a fresh accumulator per tile).  Warps 2-5 own one query row per
+// thread: the row's scores come straight from TMEM (no cross-thread
+// reductions), bf16(P) goes into one of two 128-byte-swizzled K-major tiles,
+// and the tile's P V is folded into the row's fp32 accumulator in registers.
 // Everything is double-buffered, so the MMAs of S_{j+1} and P_j V_j run while
 // the softmax works on tile j and folds tile j - 1: the softmax warps stream
 // through the tiles instead of waiting on each hand-off.  Two CTAs share an
-// SM (100 KB shared memory, 256 TMEM columns, 320 threads each), and the units with the
+// SM (97 KB shared memory, 256 TMEM columns each), and the units with the
 // most key tiles come first.  Every wait is bounded (XB_ERR_TIMEOUT through
 // the GEMM status word).
 namespace xb {
@@ -3433,8 +3431,6 @@ constexpr int kAtKVBytes = kAtBK * 128;    // K or V tile: 64 keys x 64 bf16
 constexpr int kAtStages = 3;               // K / V ring slots
 constexpr int kAtPBytes = kAtBQ * 128;     // P tile: 128 rows x 64 keys bf16
 constexpr int kAtSmem = kAtQBytes + kAtStages * 2 * kAtKVBytes + 2 * kAtPBytes + 1024;
-constexpr int kAtSoftThreads = 256;            // softmax: two threads per query row
-constexpr int kAtThreads = 64 + kAtSoftThreads;
 
 // two floats -> packed bf16 pair, the first in the low half (lower address)
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -3477,15 +3473,12 @@ __device__ __forceinline__ AtUnit at_unit(const AtArgs& a, int u) {
 // barrier phases, ring slots and TMEM buffers continue across units (tile
 // counters are global to the CTA), so the next unit's Q and K / V loads and
 // its first scores overlap the current unit's last tiles.
-__global__ void __launch_bounds__(kAtThreads, 2) attn_prefill_tc_kernel(const __grid_constant__ AtMaps maps,
+__global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_constant__ AtMaps maps,
                                                                   const AtArgs args) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full, q_empty, drain_bar;
   __shared__ __align__(8) uint64_t s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2];
   __shared__ __align__(8) uint64_t kv_full[kAtStages], kv_empty[kAtStages];
-  __shared__ __align__(8) uint64_t xbar[2][4], lbar[4];  // row-max / row-sum exchange per lane quarter
-  __shared__ float xmax[2][2][kAtBQ];                    // [tile parity][half][row]
-  __shared__ float lsum[2][kAtBQ];                       // [half][row]
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
 
@@ -3502,13 +3495,11 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_prefill_tc_kernel(const __
     mbar_init(&drain_bar, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], kAtSoftThreads);
-      mbar_init(&p_full[i], kAtSoftThreads);
+      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
       mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], kAtSoftThreads);
-      for (int q = 0; q < 4; ++q) mbar_init(&xbar[i][q], 64);
+      mbar_init(&o_empty[i], 128);
     }
-    for (int q = 0; q < 4; ++q) mbar_init(&lbar[q], 64);
     for (int i = 0; i < kAtStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
@@ -3639,41 +3630,34 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_prefill_tc_kernel(const __
       }
     }
   } else {
-    // ------------------------------------------------------------ softmax: two threads per query row
-    // Warps 2-9: warp w reads TMEM lane quarter w & 3 (rows 32 (w & 3) ..),
-    // columns 32 hf .. 32 hf + 31 of each 64-column tile, hf = (w - 2) >> 2.
-    // The two threads of a row swap their partial row maxima every tile
-    // through shared memory (double-buffered by tile parity; an mbarrier of 64
-    // arrivals per lane quarter orders it, with a bounded wait) and their
-    // partial row sums once per unit.
-    const int q4 = warp & 3;
-    const int hf = (warp - 2) >> 2;
+    // ------------------------------------------------------------ softmax: one query row per thread
+    const int q4 = warp & 3;  // TMEM lane quarter
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    const int col0 = hf * 32;
-    float o[32];
+    float o[64];
     float alpha_prev = 1.0f;
-    // acc = alpha_g * acc + P_g V_g (this thread's 32 columns), once P_g V_g is in TMEM
+    // acc = alpha_g * acc + P_g V_g, once P_g V_g is in TMEM
     auto fold = [&](int gi, float alpha) -> bool {
       const int ob = gi & 1;
       if (!mbar_wait(&o_full[ob], (gi >> 1) & 1, kWaitLimit, &abort_flag)) return false;
       tc_fence_after();
-      uint32_t ov[32];
-      tmem_ld_32x32b_x32(tmem_base + 128 + ob * 64 + col0 + lane_off, ov);
+      uint32_t ov[64];
+      tmem_ld_32x32b_x32(tmem_base + 128 + ob * 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+      tmem_ld_32x32b_x32(tmem_base + 128 + ob * 64 + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(&o_empty[ob]);
 #pragma unroll
-      for (int c = 0; c < 32; ++c) o[c] = fmaf(o[c], alpha, __uint_as_float(ov[c]));
+      for (int c = 0; c < 64; ++c) o[c] = fmaf(o[c], alpha, __uint_as_float(ov[c]));
       return true;
     };
     bool ok = true;
-    int g = 0, lu = 0;
-    for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++lu) {
+    int g = 0;
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       const AtUnit t = at_unit(args, u);
       const int qpos = args.pos + t.qs + r;  // absolute position of this row
 #pragma unroll
-      for (int c = 0; c < 32; ++c) o[c] = 0.0f;
+      for (int c = 0; c < 64; ++c) o[c] = 0.0f;
       float m = -INFINITY, l = 0.0f;
       const int g0 = g;
       for (int j = 0; j < t.nkt; ++j, ++g) {
@@ -3684,66 +3668,60 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_prefill_tc_kernel(const __
           break;
         }
         tc_fence_after();
-        uint32_t sv[32];
-        tmem_ld_32x32b_x32(tmem_base + sb * 64 + col0 + lane_off, sv);
+        uint32_t sv[64];
+        tmem_ld_32x32b_x32(tmem_base + sb * 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld_32x32b_x32(tmem_base + sb * 64 + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive(&s_empty[sb]);  // S buffer free for S_{g+2}
-        const int k0 = j * kAtBK + col0;  // first key of this thread's half
-        const bool whole = k0 + 32 <= args.total && k0 + 31 <= qpos;  // no key of the half masked
+        const int k0 = j * kAtBK;
+        const bool whole = k0 + kAtBK <= args.total && k0 + kAtBK - 1 <= qpos;  // no key of the tile masked
         // Raw scores (the scale is positive, so the max of the raw scores
-        // scales to the max of the scaled ones); masked keys become -inf.
-        float s[32];
-        float mx4[4];
+        // scales to the max of the scaled ones); masked keys become -inf.  Row
+        // max and row sum run as eight interleaved partial chains.
+        float s[64];
+        float mx8[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) mx4[i] = -INFINITY;
+        for (int i = 0; i < 8; ++i) mx8[i] = -INFINITY;
         if (whole) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
+          for (int c = 0; c < 64; ++c) {
             s[c] = __uint_as_float(sv[c]);
-            mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+            mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
           }
         } else {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
+          for (int c = 0; c < 64; ++c) {
             const int key = k0 + c;
             s[c] = (key < args.total && key <= qpos) ? __uint_as_float(sv[c]) : -INFINITY;
-            mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+            mx8[c & 7] = fmaxf(mx8[c & 7], s[c]);
           }
         }
-        const float mine = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-        xmax[sb][hf][r] = mine;  // the partner reads it after the exchange barrier
-        mbar_arrive(&xbar[sb][q4]);
-        if (!mbar_wait(&xbar[sb][q4], (g >> 1) & 1, kWaitLimit, &abort_flag)) {
-          fail();
-          ok = false;
-          break;
-        }
-        const float mxr = fmaxf(mine, xmax[sb][hf ^ 1][r]);
+        const float mxr = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float mn = fmaxf(m, mxr * args.scale_log2);
         const float base = mn == -INFINITY ? 0.0f : mn;
         const float alpha = ex2_approx(m - base);
         m = mn;
-        float rs4[4];
+        float rs8[8];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) rs4[i] = 0.0f;
+        for (int i = 0; i < 8; ++i) rs8[i] = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) {  // P = exp2(S * scale - max): one FMA and one exponential
+        for (int c = 0; c < 64; ++c) {  // P = exp2(S * scale - max): one FMA and one exponential
           s[c] = ex2_approx(fmaf(s[c], args.scale_log2, -base));
-          rs4[c & 3] += s[c];
+          rs8[c & 7] += s[c];
         }
-        l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));  // this thread's part of the row sum
-        // bf16(P_g) row r, keys col0 .. col0 + 31 -> P buffer g & 1 (read last by P_{g-2} V,
-        // folded in the previous tile); 16-byte chunk c8 at c8 ^ (r & 7) of the 128-byte-swizzled tile
+        l = l * alpha + (((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7])));
+        // bf16(P_g) row r -> P buffer g & 1 (read last by P_{g-2} V, folded in the previous
+        // tile); 16-byte chunk c8 at c8 ^ (r & 7) of the 128-byte-swizzled K-major tile
         uint8_t* pt = sPg + sb * kAtPBytes + r * 128;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int c8 = hf * 4 + q;
+        for (int c8 = 0; c8 < 8; ++c8) {
           uint4 w;
-          w.x = pack_bf16x2(s[q * 8 + 0], s[q * 8 + 1]);
-          w.y = pack_bf16x2(s[q * 8 + 2], s[q * 8 + 3]);
-          w.z = pack_bf16x2(s[q * 8 + 4], s[q * 8 + 5]);
-          w.w = pack_bf16x2(s[q * 8 + 6], s[q * 8 + 7]);
+          w.x = pack_bf16x2(s[c8 * 8 + 0], s[c8 * 8 + 1]);
+          w.y = pack_bf16x2(s[c8 * 8 + 2], s[c8 * 8 + 3]);
+          w.z = pack_bf16x2(s[c8 * 8 + 4], s[c8 * 8 + 5]);
+          w.w = pack_bf16x2(s[c8 * 8 + 6], s[c8 * 8 + 7]);
           *reinterpret_cast<uint4*>(pt + ((c8 ^ (r & 7)) << 4)) = w;
         }
         fence_proxy_async_smem();  // P, before the MMA (async proxy) reads it
@@ -3760,27 +3738,17 @@ __global__ void __launch_bounds__(kAtThreads, 2) attn_prefill_tc_kernel(const __
         ok = false;
         break;
       }
-      // row sum = both halves' parts (one exchange per unit)
-      lsum[hf][r] = l;
-      mbar_arrive(&lbar[q4]);
-      if (!mbar_wait(&lbar[q4], lu & 1, kWaitLimit, &abort_flag)) {
-        fail();
-        ok = false;
-        break;
-      }
-      const float lt = l + lsum[hf ^ 1][r];
       if (r < t.rows) {
-        const float inv = lt > 0.0f ? 1.0f / lt : 0.0f;
-        __nv_bfloat16* op =
-            args.out + ((int64_t)t.b * args.S + t.qs + r) * ((int64_t)args.H * 64) + t.h * 64 + col0;
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        __nv_bfloat16* op = args.out + ((int64_t)t.b * args.S + t.qs + r) * ((int64_t)args.H * 64) + t.h * 64;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int c8 = 0; c8 < 8; ++c8) {
           uint4 w;
-          w.x = pack_bf16x2(o[q * 8 + 0] * inv, o[q * 8 + 1] * inv);
-          w.y = pack_bf16x2(o[q * 8 + 2] * inv, o[q * 8 + 3] * inv);
-          w.z = pack_bf16x2(o[q * 8 + 4] * inv, o[q * 8 + 5] * inv);
-          w.w = pack_bf16x2(o[q * 8 + 6] * inv, o[q * 8 + 7] * inv);
-          *reinterpret_cast<uint4*>(op + q * 8) = w;
+          w.x = pack_bf16x2(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
+          w.y = pack_bf16x2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
+          w.z = pack_bf16x2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
+          w.w = pack_bf16x2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
+          *reinterpret_cast<uint4*>(op + c8 * 8) = w;
         }
       }
     }
@@ -3859,7 +3827,7 @@ int attention_prefill_tc(const void* q, const void* k_cache, const void* v_cache
   sm_count(&sms);
   const int64_t units = nqt * nbh;
   const int64_t grid = units < 2 * (int64_t)sms ? units : 2 * (int64_t)sms;  // two resident CTAs per SM
-  launch_k(attn_prefill_tc_kernel, dim3((unsigned)grid), kAtThreads, kAtSmem, s, maps, args);
+  launch_k(attn_prefill_tc_kernel, dim3((unsigned)grid), 192, kAtSmem, s, maps, args);
   return check_launch(what, err, errlen);
 }
 
