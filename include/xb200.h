@@ -471,6 +471,65 @@ XB_API int xb_decode_linear_residual_bf16(
     float* stats_out, int stats_kind, int64_t N, int64_t K, int64_t ldw,
     int64_t ldr, int64_t ldy, void* stream, char* err, size_t errlen);
 
+/* A chain of decode-step linears in ONE persistent launch: up to four
+ * phases, each one of the four linears above (kind XB_DECODE_*), where a
+ * phase may read what an earlier phase of the chain wrote (its X, the
+ * statistics of a pending norm, a residual).  The decoder layer's o_proj +
+ * residual, gate/up + SwiGLU, down_proj + residual and the next layer's QKV +
+ * RoPE + KV write are one call instead of four launches
+ * (examples/qwen2_5/model.py:1045-1061 and 836-867, per decode step).
+ *
+ * The grid is persistent: clusters of 8 CTAs split K (eight slices of
+ * ceil(K / 512) 64-wide blocks, summed over distributed shared memory in rank
+ * order) and take the 128-row blocks of each phase in turn; the phases are
+ * separated by grid-wide barriers on the counters in `sync`, and the weights
+ * of every phase stream in from the start of the launch.  The roundings are
+ * those of the single-launch entry points; only the K split can differ from
+ * theirs (they pick it per shape), which changes the fp32 sums in their last
+ * bits.
+ *
+ * Field meanings follow the single-launch entry points; n is the number of W
+ * rows for every kind (XB_DECODE_SWIGLU: 2 n_out, interleaved 64-row blocks;
+ * XB_DECODE_ROPE_KV: (n_head + 2 n_kv_head) * head_dim).  Limits: M <= 64,
+ * K <= 5120.  `sync`: 16 bytes of device memory, zeroed once before the first
+ * call; every launch leaves it zero when it ends, also after a timeout.  One
+ * sync buffer serves one stream at a time.  Returns XB_ERR_UNSUPPORTED when a
+ * phase is outside the limits or no 8-CTA cluster fits on the device. */
+#define XB_DECODE_STORE 0
+#define XB_DECODE_ROPE_KV 1
+#define XB_DECODE_SWIGLU 2
+#define XB_DECODE_RESIDUAL 3
+typedef struct xb_decode_phase {
+  int32_t kind;             /* XB_DECODE_* */
+  int32_t act;              /* XB_DECODE_STORE: 1 = tanh GELU */
+  const void* x;            /* X [m, k] bf16 */
+  int64_t m, ldx;
+  const float* x_stats;     /* pending norm of X, or NULL */
+  const void* x_norm_w;
+  const void* x_norm_b;
+  float x_eps;
+  int32_t x_norm_kind;
+  const void* w;            /* W [n, k] bf16 */
+  int64_t n, k, ldw;
+  const void* bias;         /* STORE / ROPE_KV / RESIDUAL, or NULL */
+  void* y;                  /* STORE / SWIGLU / RESIDUAL output */
+  int64_t ldy;
+  const void* residual;     /* RESIDUAL */
+  int64_t ldr;
+  float* stats_out;         /* RESIDUAL: statistics of Y for the next norm, or NULL */
+  int32_t stats_kind;
+  int32_t reserved;
+  const float* cos_t;       /* ROPE_KV: RoPE tables, or NULL */
+  const float* sin_t;
+  void* q_out;
+  void* k_cache;
+  void* v_cache;
+  int64_t n_head, n_kv_head, head_dim, max_seq, pos_offset;
+} xb_decode_phase;
+XB_API int xb_decode_chain_bf16(const xb_decode_phase* phases, int n_phases,
+                                void* sync, void* stream, char* err,
+                                size_t errlen);
+
 /* ---------------------------------------------------------------------------
  * N-sharded GEMM across the GPUs of one node (one process per GPU).  The
  * reference runs on one device; this is the multi-GPU form of its GEMM

@@ -1950,6 +1950,272 @@ __device__ __forceinline__ void st_dsmem_f4(uint32_t addr, float4 v) {
                : "memory");
 }
 
+// ---- decode finishers, shared by the one-launch decode linear and the decode chain
+//
+// After the split-K reduction, CTA `rank` of a cluster owns tokens [tok0,
+// tok0 + ntok) of a 128-row weight block (row0 = 128 * blk); its receive
+// buffer rv holds, per source rank jr < S, the partial rows [jr * pt + tl][128]
+// as float4.  The four epilogue warps (warps 2..5) finish the block.
+
+constexpr int kDecPre = 4;  // residual rows requested ahead, per epilogue thread
+
+__device__ __forceinline__ float4 ld_bf16x4_cg(const __nv_bfloat16* p) {
+  // L2 load: residual rows may have been written earlier in the same launch
+  const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(p));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  return make_float4(__low2float(h[0]), __high2float(h[0]), __low2float(h[1]), __high2float(h[1]));
+}
+
+// Bias and RoPE rows an epilogue thread uses for every unit of one block.
+struct DecConsts {
+  float4 pb0, pb1, pc0, pc1, ps0, ps1;
+};
+
+template <int FIN>
+__device__ __forceinline__ DecConsts dec_consts(const DecArgs& args, int row0, int lane) {
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  DecConsts k{z4, z4, z4, z4, z4, z4};
+  if constexpr (FIN == kFinStore || FIN == kFinResidual) {
+    const int n = row0 + lane * 4;
+    if (args.bias && n < args.n) k.pb0 = ld_bf16x4(args.bias + n);
+  } else if constexpr (FIN == kFinRopeKv) {
+    const int half = args.D >> 1, p = (lane & 15) * 4, hd = p / half, i = p - hd * half;
+    const int f0 = row0 + hd * args.D + i, slot = (row0 + hd * args.D) / args.D;
+    if (slot < args.H + 2 * args.KVH) {
+      if (args.bias) {
+        k.pb0 = ld_bf16x4(args.bias + f0);
+        k.pb1 = ld_bf16x4(args.bias + f0 + half);
+      }
+      if (args.cos_t && slot < args.H + args.KVH) {
+        const float* cr = args.cos_t + (int64_t)args.pos * args.D;
+        const float* sr = args.sin_t + (int64_t)args.pos * args.D;
+        k.pc0 = __ldg(reinterpret_cast<const float4*>(cr + i));
+        k.pc1 = __ldg(reinterpret_cast<const float4*>(cr + i + half));
+        k.ps0 = __ldg(reinterpret_cast<const float4*>(sr + i));
+        k.ps1 = __ldg(reinterpret_cast<const float4*>(sr + i + half));
+      }
+    }
+  }
+  return k;
+}
+
+// Residual rows of the first kDecPre owned tokens of this epilogue warp.
+template <int FIN>
+__device__ __forceinline__ void dec_rpre(const DecArgs& args, int ntok, int tok0, int row0, int warp, int lane,
+                                         float4 (&rpre)[kDecPre]) {
+  if constexpr (FIN == kFinResidual) {
+#pragma unroll
+    for (int u = 0; u < kDecPre; ++u) {
+      const int tl = (warp - 2) + 4 * u, n = row0 + lane * 4;
+      rpre[u] = tl < ntok && n < args.n ? ld_bf16x4_cg(args.residual + (tok0 + tl) * args.ldr + n)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+}
+
+template <int FIN>
+__device__ __forceinline__ void dec_finish(const DecArgs& args, const float4* rv, int S, int pt, int ntok, int tok0,
+                                           int row0, int blk, int warp, int lane, const DecConsts& kc,
+                                           const float4 (&rpre)[kDecPre]) {
+  const int e = (warp - 2) * 32 + lane;  // 0 .. 127
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  constexpr int kSlot = kDecBM / 4;  // float4 per token row of the receive buffer
+  // acc[u] = sum of the S partials of (owned token tl[u], rows c[u]..c[u]+3), rank
+  // order; the loads of up to four units are issued together
+  auto gather4 = [&](const int (&tl)[4], const int (&c)[4], const bool (&ok)[4], float4 (&acc)[4]) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) acc[u] = ok[u] ? rv[tl[u] * kSlot + (c[u] >> 2)] : z4;
+#pragma unroll
+    for (int jr = 1; jr < kDecMaxCluster; ++jr) {
+      if (jr < S) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = ok[u] ? rv[(jr * pt + tl[u]) * kSlot + (c[u] >> 2)] : z4;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (ok[u]) add4(acc[u], v[u]);
+      }
+    }
+  };
+  if constexpr (FIN == kFinStore) {
+    // units (owned token, 4-row group): thread e takes units e + 128 k, all with rows c
+    const int c = (e & 31) * 4, n = row0 + c;
+    for (int u0 = e; u0 < ntok * 32; u0 += 4 * 128) {
+      int tl[4], cc[4];
+      bool ok[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        tl[u] = (u0 + 128 * u) >> 5;
+        cc[u] = c;
+        ok[u] = u0 + 128 * u < ntok * 32 && n < args.n;
+      }
+      float4 acc[4];
+      gather4(tl, cc, ok, acc);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (!ok[u]) continue;
+        add4(acc[u], kc.pb0);
+        float4 o = make_float4(rbf(acc[u].x), rbf(acc[u].y), rbf(acc[u].z), rbf(acc[u].w));
+        if (args.act == 1)
+          o = make_float4(gelu_tanh_bf16path(o.x), gelu_tanh_bf16path(o.y), gelu_tanh_bf16path(o.z),
+                          gelu_tanh_bf16path(o.w));
+        st_bf16x4(args.y + (tok0 + tl[u]) * args.ldy + n, o.x, o.y, o.z, o.w);
+      }
+    }
+  } else if constexpr (FIN == kFinResidual) {
+    // warp per owned token (tokens w, w + 4, ... of the epilogue warp w), lane =
+    // 4-row group: the block statistics of a token row reduce within the warp;
+    // four tokens at a time, their loads and reductions interleaved
+    const int c = lane * 4, n = row0 + c;
+    const bool valid = n < args.n;
+    const float cnt = (float)min(kDecBM, args.n - row0);
+    for (int ub = 0; (warp - 2) + 16 * ub < ntok; ++ub) {
+      int tl[4], cc[4];
+      bool ok[4], live[4];
+      float4 r[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        tl[u] = (warp - 2) + 4 * (4 * ub + u);
+        cc[u] = c;
+        live[u] = tl[u] < ntok;  // warp-uniform
+        ok[u] = live[u] && valid;
+        r[u] = ub == 0 ? rpre[u]
+                       : (ok[u] ? ld_bf16x4_cg(args.residual + (tok0 + tl[u]) * args.ldr + n) : z4);
+      }
+      float4 acc[4], o[4];
+      gather4(tl, cc, ok, acc);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        o[u] = z4;
+        if (!ok[u]) continue;
+        add4(acc[u], kc.pb0);
+        o[u] = make_float4(rbf(r[u].x + rbf(acc[u].x)), rbf(r[u].y + rbf(acc[u].y)), rbf(r[u].z + rbf(acc[u].z)),
+                           rbf(r[u].w + rbf(acc[u].w)));
+        st_bf16x4(args.y + (tok0 + tl[u]) * args.ldy + n, o[u].x, o[u].y, o[u].z, o[u].w);
+      }
+      if (args.stats) {
+        float s1[4], s2[4], sh[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float4 v = o[u];
+          if (args.stats_kind == 0) {
+            sh[u] = 0.0f;
+            s1[u] = (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
+            s2[u] = 0.0f;
+          } else {
+            // shifted sums (shift: the block's first value) give the block mean
+            // and the sum of squared deviations in one pass
+            sh[u] = __shfl_sync(0xffffffffu, v.x, 0);
+            const float a = v.x - sh[u], b = v.y - sh[u], cz = v.z - sh[u], d = v.w - sh[u];
+            s1[u] = valid ? (a + b) + (cz + d) : 0.0f;
+            s2[u] = valid ? (a * a + b * b) + (cz * cz + d * d) : 0.0f;
+          }
+        }
+#pragma unroll
+        for (int o_ = 16; o_ > 0; o_ >>= 1) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            s1[u] += __shfl_xor_sync(0xffffffffu, s1[u], o_);
+            s2[u] += __shfl_xor_sync(0xffffffffu, s2[u], o_);
+          }
+        }
+        if (lane == 0) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (!live[u]) continue;
+            args.stats[blk * kDecBN + tok0 + tl[u]] =
+                args.stats_kind == 0 ? make_float2(s1[u], 0.0f)
+                                     : make_float2(sh[u] + s1[u] / cnt, fmaxf(s2[u] - s1[u] * s1[u] / cnt, 0.0f));
+          }
+        }
+      }
+    }
+  } else if constexpr (FIN == kFinSwiglu) {
+    // rows [0, 64) gate and [64, 128) up of features blk*64 .. blk*64+63;
+    // units (owned token, 4 features): thread e takes units e + 128 k
+    const int c = (e & 15) * 4;
+    for (int u0 = e; u0 < ntok * 16; u0 += 2 * 128) {
+      int tl[4], cc[4];
+      bool ok[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {  // (gate, up) of two units
+        tl[u] = (u0 + 128 * (u >> 1)) >> 4;
+        cc[u] = c + 64 * (u & 1);
+        ok[u] = u0 + 128 * (u >> 1) < ntok * 16;
+      }
+      float4 acc[4];
+      gather4(tl, cc, ok, acc);
+      auto sw = [](float gg, float uu) { return __fmul_rn(silu_bf16path(rbf(gg)), rbf(uu)); };
+#pragma unroll
+      for (int u = 0; u < 4; u += 2) {
+        if (!ok[u]) continue;
+        const float4 g = acc[u], up = acc[u + 1];
+        st_bf16x4(args.y + (tok0 + tl[u]) * args.ldy + blk * 64 + c, sw(g.x, up.x), sw(g.y, up.y), sw(g.z, up.z),
+                  sw(g.w, up.w));
+      }
+    }
+  } else {
+    // kFinRopeKv: units (owned token, 4 consecutive rotation pairs of one head);
+    // thread e takes units e + 128 k, all with the same pairs
+    const int D = args.D, half = D >> 1;
+    const int p = (e & 15) * 4;  // first pair index within the block
+    const int hd = p / half, i = p - hd * half;
+    const int c0 = hd * D + i;   // row of the first element, within the block
+    const int slot = (row0 + hd * D) / D;
+    if (slot < args.H + 2 * args.KVH) {
+      for (int u0 = e; u0 < ntok * 16; u0 += 2 * 128) {
+        int tl[4], cc[4];
+        bool ok[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {  // (first, second half) of two units
+          tl[u] = (u0 + 128 * (u >> 1)) >> 4;
+          cc[u] = c0 + half * (u & 1);
+          ok[u] = u0 + 128 * (u >> 1) < ntok * 16;
+        }
+        float4 acc[4];
+        gather4(tl, cc, ok, acc);
+#pragma unroll
+        for (int u = 0; u < 4; u += 2) {
+          if (!ok[u]) continue;
+          const int t = tok0 + tl[u];
+          float4 a0 = acc[u], a1 = acc[u + 1];
+          add4(a0, kc.pb0);
+          add4(a1, kc.pb1);
+          const float x0[4] = {rbf(a0.x), rbf(a0.y), rbf(a0.z), rbf(a0.w)};
+          const float x1[4] = {rbf(a1.x), rbf(a1.y), rbf(a1.z), rbf(a1.w)};
+          __nv_bfloat16* dst;
+          if (slot < args.H)
+            dst = args.q_out + ((int64_t)t * args.H + slot) * D;
+          else if (slot < args.H + args.KVH)
+            dst = args.k_cache + (((int64_t)t * args.KVH + (slot - args.H)) * args.smax + args.pos) * D;
+          else
+            dst = args.v_cache + (((int64_t)t * args.KVH + (slot - args.H - args.KVH)) * args.smax + args.pos) * D;
+          float o0[4], o1[4];
+          if (slot >= args.H + args.KVH || !args.cos_t) {
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              o0[jj] = x0[jj];
+              o1[jj] = x1[jj];
+            }
+          } else {
+            const float c0v[4] = {kc.pc0.x, kc.pc0.y, kc.pc0.z, kc.pc0.w};
+            const float c1v[4] = {kc.pc1.x, kc.pc1.y, kc.pc1.z, kc.pc1.w};
+            const float s0v[4] = {kc.ps0.x, kc.ps0.y, kc.ps0.z, kc.ps0.w};
+            const float s1v[4] = {kc.ps1.x, kc.ps1.y, kc.ps1.z, kc.ps1.w};
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              o0[jj] = __fadd_rn(__fmul_rn(x0[jj], c0v[jj]), __fmul_rn(-x1[jj], s0v[jj]));
+              o1[jj] = __fadd_rn(__fmul_rn(x1[jj], c1v[jj]), __fmul_rn(x0[jj], s1v[jj]));
+            }
+          }
+          st_bf16x4(dst + i, o0[0], o0[1], o0[2], o0[3]);
+          st_bf16x4(dst + i + half, o1[0], o1[1], o1[2], o1[3]);
+        }
+      }
+    }
+  }
+}
+
 template <int FIN, int STAGES, bool XNORM>
 __global__ void __launch_bounds__(192, 1) decode_linear_kernel(const __grid_constant__ DecMaps maps,
                                                                const DecArgs args) {
@@ -2010,36 +2276,11 @@ __global__ void __launch_bounds__(192, 1) decode_linear_kernel(const __grid_cons
 
   // Residual finisher: warp w of the epilogue takes owned tokens w, w + 4, ...;
   // their residual rows are requested while the MMAs run.
-  constexpr int kPre = 4;
-  float4 rpre[kPre];
+  float4 rpre[kDecPre];
   // Finisher constants (bias, RoPE table rows), requested before the
   // programmatic-launch wait: every finisher unit of a thread uses the same rows.
-  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 pb0 = z4, pb1 = z4, pc0 = z4, pc1 = z4, ps0 = z4, ps1 = z4;
-  if (warp >= 2) {
-    const int e = threadIdx.x - 64;
-    if constexpr (FIN == kFinStore || FIN == kFinResidual) {
-      const int n = row0 + (FIN == kFinStore ? (e & 31) : lane) * 4;
-      if (args.bias && n < args.n) pb0 = ld_bf16x4(args.bias + n);
-    } else if constexpr (FIN == kFinRopeKv) {
-      const int half = args.D >> 1, p = (e & 15) * 4, hd = p / half, i = p - hd * half;
-      const int f0 = row0 + hd * args.D + i, slot = (row0 + hd * args.D) / args.D;
-      if (slot < args.H + 2 * args.KVH) {
-        if (args.bias) {
-          pb0 = ld_bf16x4(args.bias + f0);
-          pb1 = ld_bf16x4(args.bias + f0 + half);
-        }
-        if (args.cos_t && slot < args.H + args.KVH) {
-          const float* cr = args.cos_t + (int64_t)args.pos * args.D;
-          const float* sr = args.sin_t + (int64_t)args.pos * args.D;
-          pc0 = __ldg(reinterpret_cast<const float4*>(cr + i));
-          pc1 = __ldg(reinterpret_cast<const float4*>(cr + i + half));
-          ps0 = __ldg(reinterpret_cast<const float4*>(sr + i));
-          ps1 = __ldg(reinterpret_cast<const float4*>(sr + i + half));
-        }
-      }
-    }
-  }
+  DecConsts kc = {};
+  if (warp >= 2) kc = dec_consts<FIN>(args, row0, lane);
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -2197,14 +2438,7 @@ __global__ void __launch_bounds__(192, 1) decode_linear_kernel(const __grid_cons
       pdl_wait();
       pdl_trigger();
     }
-    if constexpr (FIN == kFinResidual) {
-#pragma unroll
-      for (int u = 0; u < kPre; ++u) {
-        const int tl = (warp - 2) + 4 * u, n = row0 + lane * 4;
-        rpre[u] = tl < ntok && n < args.n ? ld_bf16x4(args.residual + (tok0 + tl) * args.ldr + n)
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-    }
+    dec_rpre<FIN>(args, ntok, tok0, row0, warp, lane, rpre);
     // ------------------------------------------------------------ accumulator -> owners
     const int q = warp & 3;  // TMEM lane quarter this warp may read
     const bool got = mbar_wait(&tfull_bar, 0, kWaitLimit, &abort_flag);
@@ -2252,201 +2486,7 @@ __global__ void __launch_bounds__(192, 1) decode_linear_kernel(const __grid_cons
   if (warp < 2) return;
 
   // ------------------------------------------------------------ finisher (own shared memory only)
-  const int e = threadIdx.x - 64;  // 0 .. 127
-  constexpr int kSlot = kDecBM / 4;  // float4 per token row of the receive buffer
-  const float4* rv = reinterpret_cast<const float4*>(recv);
-  // acc[u] = sum of the S partials of (owned token tl[u], rows c[u]..c[u]+3), rank
-  // order; the loads of up to four units are issued together
-  auto gather4 = [&](const int (&tl)[4], const int (&c)[4], const bool (&ok)[4], float4 (&acc)[4]) {
-#pragma unroll
-    for (int u = 0; u < 4; ++u) acc[u] = ok[u] ? rv[tl[u] * kSlot + (c[u] >> 2)] : z4;
-#pragma unroll
-    for (int jr = 1; jr < kDecMaxCluster; ++jr) {
-      if (jr < S) {
-        float4 v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = ok[u] ? rv[(jr * pt + tl[u]) * kSlot + (c[u] >> 2)] : z4;
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (ok[u]) add4(acc[u], v[u]);
-      }
-    }
-  };
-  if constexpr (FIN == kFinStore) {
-    // units (owned token, 4-row group): thread e takes units e + 128 k, all with rows c
-    const int c = (e & 31) * 4, n = row0 + c;
-    for (int u0 = e; u0 < ntok * 32; u0 += 4 * 128) {
-      int tl[4], cc[4];
-      bool ok[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        tl[u] = (u0 + 128 * u) >> 5;
-        cc[u] = c;
-        ok[u] = u0 + 128 * u < ntok * 32 && n < args.n;
-      }
-      float4 acc[4];
-      gather4(tl, cc, ok, acc);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (!ok[u]) continue;
-        add4(acc[u], pb0);
-        float4 o = make_float4(rbf(acc[u].x), rbf(acc[u].y), rbf(acc[u].z), rbf(acc[u].w));
-        if (args.act == 1)
-          o = make_float4(gelu_tanh_bf16path(o.x), gelu_tanh_bf16path(o.y), gelu_tanh_bf16path(o.z),
-                          gelu_tanh_bf16path(o.w));
-        st_bf16x4(args.y + (tok0 + tl[u]) * args.ldy + n, o.x, o.y, o.z, o.w);
-      }
-    }
-  } else if constexpr (FIN == kFinResidual) {
-    // warp per owned token (tokens w, w + 4, ... of the epilogue warp w), lane =
-    // 4-row group: the block statistics of a token row reduce within the warp;
-    // four tokens at a time, their loads and reductions interleaved
-    const int c = lane * 4, n = row0 + c;
-    const bool valid = n < args.n;
-    const float cnt = (float)min(kDecBM, args.n - row0);
-    for (int ub = 0; (warp - 2) + 16 * ub < ntok; ++ub) {
-      int tl[4], cc[4];
-      bool ok[4], live[4];
-      float4 r[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        tl[u] = (warp - 2) + 4 * (4 * ub + u);
-        cc[u] = c;
-        live[u] = tl[u] < ntok;  // warp-uniform
-        ok[u] = live[u] && valid;
-        r[u] = ub == 0 ? rpre[u]
-                       : (ok[u] ? ld_bf16x4(args.residual + (tok0 + tl[u]) * args.ldr + n) : z4);
-      }
-      float4 acc[4], o[4];
-      gather4(tl, cc, ok, acc);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        o[u] = z4;
-        if (!ok[u]) continue;
-        add4(acc[u], pb0);
-        o[u] = make_float4(rbf(r[u].x + rbf(acc[u].x)), rbf(r[u].y + rbf(acc[u].y)), rbf(r[u].z + rbf(acc[u].z)),
-                           rbf(r[u].w + rbf(acc[u].w)));
-        st_bf16x4(args.y + (tok0 + tl[u]) * args.ldy + n, o[u].x, o[u].y, o[u].z, o[u].w);
-      }
-      if (args.stats) {
-        float s1[4], s2[4], sh[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float4 v = o[u];
-          if (args.stats_kind == 0) {
-            sh[u] = 0.0f;
-            s1[u] = (v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w);
-            s2[u] = 0.0f;
-          } else {
-            // shifted sums (shift: the block's first value) give the block mean
-            // and the sum of squared deviations in one pass
-            sh[u] = __shfl_sync(0xffffffffu, v.x, 0);
-            const float a = v.x - sh[u], b = v.y - sh[u], cz = v.z - sh[u], d = v.w - sh[u];
-            s1[u] = valid ? (a + b) + (cz + d) : 0.0f;
-            s2[u] = valid ? (a * a + b * b) + (cz * cz + d * d) : 0.0f;
-          }
-        }
-#pragma unroll
-        for (int o_ = 16; o_ > 0; o_ >>= 1) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            s1[u] += __shfl_xor_sync(0xffffffffu, s1[u], o_);
-            s2[u] += __shfl_xor_sync(0xffffffffu, s2[u], o_);
-          }
-        }
-        if (lane == 0) {
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (!live[u]) continue;
-            args.stats[blk * kDecBN + tok0 + tl[u]] =
-                args.stats_kind == 0 ? make_float2(s1[u], 0.0f)
-                                     : make_float2(sh[u] + s1[u] / cnt, fmaxf(s2[u] - s1[u] * s1[u] / cnt, 0.0f));
-          }
-        }
-      }
-    }
-  } else if constexpr (FIN == kFinSwiglu) {
-    // rows [0, 64) gate and [64, 128) up of features blk*64 .. blk*64+63;
-    // units (owned token, 4 features): thread e takes units e + 128 k
-    const int c = (e & 15) * 4;
-    for (int u0 = e; u0 < ntok * 16; u0 += 2 * 128) {
-      int tl[4], cc[4];
-      bool ok[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {  // (gate, up) of two units
-        tl[u] = (u0 + 128 * (u >> 1)) >> 4;
-        cc[u] = c + 64 * (u & 1);
-        ok[u] = u0 + 128 * (u >> 1) < ntok * 16;
-      }
-      float4 acc[4];
-      gather4(tl, cc, ok, acc);
-      auto sw = [](float gg, float uu) { return __fmul_rn(silu_bf16path(rbf(gg)), rbf(uu)); };
-#pragma unroll
-      for (int u = 0; u < 4; u += 2) {
-        if (!ok[u]) continue;
-        const float4 g = acc[u], up = acc[u + 1];
-        st_bf16x4(args.y + (tok0 + tl[u]) * args.ldy + blk * 64 + c, sw(g.x, up.x), sw(g.y, up.y), sw(g.z, up.z),
-                  sw(g.w, up.w));
-      }
-    }
-  } else {
-    // kFinRopeKv: units (owned token, 4 consecutive rotation pairs of one head);
-    // thread e takes units e + 128 k, all with the same pairs
-    const int D = args.D, half = D >> 1;
-    const int p = (e & 15) * 4;  // first pair index within the block
-    const int hd = p / half, i = p - hd * half;
-    const int c0 = hd * D + i;   // row of the first element, within the block
-    const int slot = (row0 + hd * D) / D;
-    if (slot < args.H + 2 * args.KVH) {
-      for (int u0 = e; u0 < ntok * 16; u0 += 2 * 128) {
-        int tl[4], cc[4];
-        bool ok[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {  // (first, second half) of two units
-          tl[u] = (u0 + 128 * (u >> 1)) >> 4;
-          cc[u] = c0 + half * (u & 1);
-          ok[u] = u0 + 128 * (u >> 1) < ntok * 16;
-        }
-        float4 acc[4];
-        gather4(tl, cc, ok, acc);
-#pragma unroll
-        for (int u = 0; u < 4; u += 2) {
-          if (!ok[u]) continue;
-          const int t = tok0 + tl[u];
-          float4 a0 = acc[u], a1 = acc[u + 1];
-          add4(a0, pb0);
-          add4(a1, pb1);
-          const float x0[4] = {rbf(a0.x), rbf(a0.y), rbf(a0.z), rbf(a0.w)};
-          const float x1[4] = {rbf(a1.x), rbf(a1.y), rbf(a1.z), rbf(a1.w)};
-          __nv_bfloat16* dst;
-          if (slot < args.H)
-            dst = args.q_out + ((int64_t)t * args.H + slot) * D;
-          else if (slot < args.H + args.KVH)
-            dst = args.k_cache + (((int64_t)t * args.KVH + (slot - args.H)) * args.smax + args.pos) * D;
-          else
-            dst = args.v_cache + (((int64_t)t * args.KVH + (slot - args.H - args.KVH)) * args.smax + args.pos) * D;
-          float o0[4], o1[4];
-          if (slot >= args.H + args.KVH || !args.cos_t) {
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              o0[jj] = x0[jj];
-              o1[jj] = x1[jj];
-            }
-          } else {
-            const float c0v[4] = {pc0.x, pc0.y, pc0.z, pc0.w}, c1v[4] = {pc1.x, pc1.y, pc1.z, pc1.w};
-            const float s0v[4] = {ps0.x, ps0.y, ps0.z, ps0.w}, s1v[4] = {ps1.x, ps1.y, ps1.z, ps1.w};
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              o0[jj] = __fadd_rn(__fmul_rn(x0[jj], c0v[jj]), __fmul_rn(-x1[jj], s0v[jj]));
-              o1[jj] = __fadd_rn(__fmul_rn(x1[jj], c1v[jj]), __fmul_rn(x0[jj], s1v[jj]));
-            }
-          }
-          st_bf16x4(dst + i, o0[0], o0[1], o0[2], o0[3]);
-          st_bf16x4(dst + i + half, o1[0], o1[1], o1[2], o1[3]);
-        }
-      }
-    }
-  }
+  dec_finish<FIN>(args, reinterpret_cast<const float4*>(recv), S, pt, ntok, tok0, row0, blk, warp, lane, kc, rpre);
 }
 
 // Launch with clusters of `cx` CTAs along x (and programmatic dependent launch when enabled).
@@ -3234,6 +3274,8 @@ extern "C" int xb_decode_linear_residual_bf16(const void* X, int64_t M, int64_t 
   return launch_decode<kFinResidual>(in, W, N, K, ldw, a, (cudaStream_t)stream, what, err, errlen);
 }
 #undef XB_DECODE_INPUT
+
+#include "decode_chain.cuh"
 
 // ---- LM head + greedy next token --------------------------------------------
 

@@ -64,6 +64,8 @@ _CTYPES = {
     "const char*": ctypes.c_char_p,
     "uint64_t": ctypes.c_uint64,
     "uint32_t": ctypes.c_uint32,
+    # an array of DecodePhase (ops.py), passed by address
+    "const xb_decode_phase*": ctypes.c_void_p,
 }
 
 

@@ -30,6 +30,7 @@ sequence runs the requested number of steps).
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -149,11 +150,65 @@ class GPT2Model:
         self.lnf_w = t("transformer.ln_f.weight")
         self.lnf_b = t("transformer.ln_f.bias")
         self.scale = 1.0 / math.sqrt(c.head_dim)
+        self._chain = None  # decided at the first decode step
+        self._chain_sync = None
 
     def new_cache(self, batch: int, max_seq: int) -> KVCache:
         if max_seq > self.cfg.n_positions:
             raise ValueError(f"cache length {max_seq} exceeds the position table ({self.cfg.n_positions})")
         return KVCache(self.cfg, batch, max_seq, self.device)
+
+    def _chain_ok(self) -> bool:
+        """Decode steps run as decode chains (one launch per layer besides its
+        attention) unless XB_DECODE_CHAIN=0 or a linear is too deep for one
+        (gpt2-xl's mlp c_proj, K = 6400)."""
+        if self._chain is None:
+            self._chain = os.environ.get("XB_DECODE_CHAIN", "1") != "0" and self.cfg.mlp <= ops.CHAIN_MAX_K
+            if self._chain:
+                self._chain_sync = ops.decode_chain_sync(self.device)
+        return self._chain
+
+    def _decode_chain_layers(self, x, xin, cache, pos: int, q_buf, attn):
+        """The blocks of one decode step: per block, the attention kernel and
+        one decode chain -- attn c_proj + residual (with the statistics of
+        ln_2), c_fc + GELU (ln_2 applied as its input is loaded), mlp c_proj
+        + residual, and the next block's c_attn + head split + KV write (its
+        ln_1 applied the same way).  The first block's c_attn is a chain of
+        its own (examples/gpt2/model.py:1032-1059 per block)."""
+        c = self.cfg
+        M, D = x.shape
+        H, HD, eps = c.n_head, c.head_dim, c.ln_eps
+        dev = self.device
+        y = torch.empty((M, D), dtype=torch.bfloat16, device=dev)
+        h = torch.empty((M, c.mlp), dtype=torch.bfloat16, device=dev)
+        xs = [x, torch.empty((M, D), dtype=torch.bfloat16, device=dev)]  # residual stream, ping-pong
+        st_post = ops.decode_stats(D, dev)
+        st_in = ops.decode_stats(D, dev)
+        sync = self._chain_sync
+
+        def qkv(i, xsrc, xnorm):
+            L = self.layers[i]
+            return ops.chain_rope_kv(xsrc, L["qkv_w"], L["qkv_b"], None, None, q_buf, cache.k[i], cache.v[i],
+                                     H, H, HD, pos, xnorm=xnorm)
+
+        phases = [qkv(0, xin, None)]
+        for i, L in enumerate(self.layers):
+            ops.decode_chain(phases, sync)
+            ops.attention(q_buf, cache.k[i], cache.v[i], attn, M, 1, H, H, HD, pos, self.scale)
+            last = i + 1 == len(self.layers)
+            xr, xo = xs[i % 2], xs[(i + 1) % 2]
+            phases = [
+                ops.chain_residual(attn, L["proj_w"], L["proj_b"], xr, y, st_post, "layer"),
+                ops.chain_store(y, L["fc_w"], L["fc_b"], h, act="gelu_tanh",
+                                xnorm=(st_post, L["ln2_w"], L["ln2_b"], eps, "layer")),
+                ops.chain_residual(h, L["mproj_w"], L["mproj_b"], y, xo, None if last else st_in,
+                                   None if last else "layer"),
+            ]
+            if not last:
+                nxt = self.layers[i + 1]
+                phases.append(qkv(i + 1, xo, (st_in, nxt["ln1_w"], nxt["ln1_b"], eps, "layer")))
+        ops.decode_chain(phases, sync)
+        return xs[len(self.layers) % 2]
 
     @torch.no_grad()
     def forward(self, ids: torch.Tensor, cache: KVCache, last_only: bool = False,
@@ -181,7 +236,10 @@ class GPT2Model:
         decode = S == 1 and M <= ops.SMALL_M
         if decode:
             xin, xnorm = ops.layernorm(x, self.layers[0]["ln1_w"], self.layers[0]["ln1_b"], c.ln_eps), None
-        for i, L in enumerate(self.layers):
+        chain = decode and self._chain_ok()
+        if chain:
+            x = self._decode_chain_layers(x, xin, cache, pos, q_buf, attn)
+        for i, L in enumerate(self.layers if not chain else ()):
             if decode:
                 ops.decode_linear_rope_kv(xin, L["qkv_w"], L["qkv_b"], None, None, q_buf, cache.k[i], cache.v[i],
                                           H, H, HD, pos, xnorm=xnorm)

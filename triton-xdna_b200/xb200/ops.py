@@ -677,6 +677,135 @@ def decode_linear_residual(x, weight, bias, residual, stats_kind=None, xnorm=Non
     return y, st
 
 
+# --------------------------------------------------------------------------- decode chain
+#
+# Up to four decode linears in one persistent launch (xb_decode_chain_bf16):
+# each phase is built like the single-launch call of the same kind, and a
+# phase may read what an earlier one wrote.  The structures hold raw device
+# addresses: the caller keeps the tensors alive until the launch has run.
+
+CHAIN_MAX_PHASES = 4
+CHAIN_MAX_K = 5120  # ten 64-wide K blocks per CTA of an 8-CTA cluster
+
+
+class DecodePhase(ctypes.Structure):
+    """Mirror of the C ``xb_decode_phase`` (include/xb200.h)."""
+
+    _fields_ = [
+        ("kind", ctypes.c_int32), ("act", ctypes.c_int32),
+        ("x", ctypes.c_void_p), ("m", ctypes.c_int64), ("ldx", ctypes.c_int64),
+        ("x_stats", ctypes.c_void_p), ("x_norm_w", ctypes.c_void_p), ("x_norm_b", ctypes.c_void_p),
+        ("x_eps", ctypes.c_float), ("x_norm_kind", ctypes.c_int32),
+        ("w", ctypes.c_void_p), ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("ldw", ctypes.c_int64),
+        ("bias", ctypes.c_void_p), ("y", ctypes.c_void_p), ("ldy", ctypes.c_int64),
+        ("residual", ctypes.c_void_p), ("ldr", ctypes.c_int64),
+        ("stats_out", ctypes.c_void_p), ("stats_kind", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("cos_t", ctypes.c_void_p), ("sin_t", ctypes.c_void_p),
+        ("q_out", ctypes.c_void_p), ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+        ("n_head", ctypes.c_int64), ("n_kv_head", ctypes.c_int64), ("head_dim", ctypes.c_int64),
+        ("max_seq", ctypes.c_int64), ("pos_offset", ctypes.c_int64),
+    ]
+
+
+XB_DECODE_STORE, XB_DECODE_ROPE_KV, XB_DECODE_SWIGLU, XB_DECODE_RESIDUAL = 0, 1, 2, 3
+
+
+def _phase(kind, x, weight, xnorm) -> DecodePhase:
+    _cuda(x, weight)
+    if x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16:
+        raise TypeError("decode chain phases take bf16 x and weight")
+    M = x.shape[0]
+    if not 0 < M <= SMALL_M:
+        raise ValueError(f"decode chain phases take 1..{SMALL_M} tokens, got {M}")
+    N, K = weight.shape
+    if x.shape[1] != K:
+        raise ValueError("shape mismatch")
+    ph = DecodePhase()
+    ph.kind = kind
+    ph.x, ph.m, ph.ldx = x.data_ptr(), M, _mat(x, "x")
+    ph.w, ph.n, ph.k, ph.ldw = weight.data_ptr(), N, K, _mat(weight, "weight")
+    if xnorm is not None:
+        stats, w, b, eps, nk = xnorm
+        _cuda(stats, w, b)
+        if stats.dtype != torch.float32 or stats.numel() < ((K + 127) // 128) * 128:
+            raise ValueError("xnorm statistics must be a float32 decode_stats buffer for x's width")
+        ph.x_stats, ph.x_norm_w = stats.data_ptr(), w.data_ptr()
+        ph.x_norm_b = b.data_ptr() if b is not None else None
+        ph.x_eps, ph.x_norm_kind = float(eps), _NORM_KIND[nk]
+    return ph
+
+
+def chain_store(x, weight, bias, y, act=None, xnorm=None) -> DecodePhase:
+    """Phase: y = bf16(norm?(x) @ weight^T + bias) [tanh GELU] (decode_linear)."""
+    ph = _phase(XB_DECODE_STORE, x, weight, xnorm)
+    _cuda(bias, y)
+    if act not in (None, "gelu_tanh"):
+        raise ValueError("act must be None or 'gelu_tanh'")
+    ph.act = 1 if act else 0
+    ph.bias = bias.data_ptr() if bias is not None else None
+    ph.y, ph.ldy = y.data_ptr(), _mat(y, "y")
+    return ph
+
+
+def chain_rope_kv(x, w_qkv, b_qkv, cos_t, sin_t, q_out, k_cache, v_cache, n_head, n_kv_head, head_dim,
+                  pos_offset, xnorm=None) -> DecodePhase:
+    """Phase: QKV projection + RoPE + KV-cache write at pos_offset (decode_linear_rope_kv)."""
+    ph = _phase(XB_DECODE_ROPE_KV, x, w_qkv, xnorm)
+    _cuda(b_qkv, cos_t, sin_t, q_out, k_cache, v_cache)
+    if cos_t is not None and cos_t.shape[0] <= pos_offset:
+        raise ValueError("RoPE tables are shorter than the position")
+    ph.bias = b_qkv.data_ptr() if b_qkv is not None else None
+    ph.cos_t = cos_t.data_ptr() if cos_t is not None else None
+    ph.sin_t = sin_t.data_ptr() if sin_t is not None else None
+    ph.q_out, ph.k_cache, ph.v_cache = q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr()
+    ph.n_head, ph.n_kv_head, ph.head_dim = n_head, n_kv_head, head_dim
+    ph.max_seq, ph.pos_offset = k_cache.shape[2], pos_offset
+    return ph
+
+
+def chain_swiglu(x, w_gate_up, y, xnorm=None) -> DecodePhase:
+    """Phase: y = silu(norm?(x) Wg^T) * (norm?(x) Wu^T), W from interleave_gate_up (decode_linear_swiglu)."""
+    ph = _phase(XB_DECODE_SWIGLU, x, w_gate_up, xnorm)
+    _cuda(y)
+    if tuple(y.shape) != (x.shape[0], w_gate_up.shape[0] // 2):
+        raise ValueError("y must be [M, n_out]")
+    ph.y, ph.ldy = y.data_ptr(), _mat(y, "y")
+    return ph
+
+
+def chain_residual(x, weight, bias, residual, y, stats=None, stats_kind=None, xnorm=None) -> DecodePhase:
+    """Phase: y = residual + bf16(norm?(x) @ weight^T + bias), with the row
+    statistics of y in `stats` (a decode_stats buffer) for the next norm
+    (decode_linear_residual)."""
+    ph = _phase(XB_DECODE_RESIDUAL, x, weight, xnorm)
+    _cuda(bias, residual, y, stats)
+    M, N = x.shape[0], weight.shape[0]
+    if tuple(residual.shape) != (M, N) or tuple(y.shape) != (M, N):
+        raise ValueError("residual and y must be [M, N]")
+    ph.bias = bias.data_ptr() if bias is not None else None
+    ph.residual, ph.ldr = residual.data_ptr(), _mat(residual, "residual")
+    ph.y, ph.ldy = y.data_ptr(), _mat(y, "y")
+    if stats is not None:
+        if stats.dtype != torch.float32 or stats.numel() < ((N + 127) // 128) * 128:
+            raise ValueError("stats must be a float32 decode_stats buffer for N")
+        ph.stats_out, ph.stats_kind = stats.data_ptr(), _NORM_KIND[stats_kind]
+    return ph
+
+
+def decode_chain_sync(device) -> torch.Tensor:
+    """The chain's grid-barrier counters: 16 zeroed bytes, one buffer per stream."""
+    return torch.zeros(4, dtype=torch.int32, device=device)
+
+
+def decode_chain(phases, sync) -> None:
+    """Run 1..4 decode-chain phases in one launch (xb_decode_chain_bf16)."""
+    if not 0 < len(phases) <= CHAIN_MAX_PHASES:
+        raise ValueError(f"a decode chain has 1..{CHAIN_MAX_PHASES} phases")
+    _cuda(sync)
+    arr = (DecodePhase * len(phases))(*phases)
+    _lib.call("xb_decode_chain_bf16", ctypes.addressof(arr), len(phases), sync.data_ptr(), _stream())
+
+
 def device_status() -> int:
     """Read and clear the device status word (0 = fine, -4 = a kernel timed out)."""
     st = ctypes.c_int(0)

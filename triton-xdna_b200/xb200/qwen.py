@@ -23,6 +23,7 @@ and may return last-position logits only (all a greedy step needs).
 from __future__ import annotations
 
 import math
+import os
 import time
 from dataclasses import dataclass
 
@@ -138,6 +139,59 @@ class Qwen2Model:
         self.cos = cos.to(dev).contiguous()
         self.sin = sin.to(dev).contiguous()
         self.scale = 1.0 / math.sqrt(c.head_dim)
+        self._chain = None  # decided at the first decode step
+        self._chain_sync = None
+
+    def _chain_ok(self) -> bool:
+        """Decode steps run as decode chains (one launch per layer besides its
+        attention) unless XB_DECODE_CHAIN=0 or a linear is too deep for one."""
+        if self._chain is None:
+            c = self.cfg
+            self._chain = (os.environ.get("XB_DECODE_CHAIN", "1") != "0"
+                           and max(c.n_embd, c.intermediate) <= ops.CHAIN_MAX_K)
+            if self._chain:
+                self._chain_sync = ops.decode_chain_sync(self.device)
+        return self._chain
+
+    def _decode_chain_layers(self, x, xin, cache: KVCache, pos: int, q_buf, attn):
+        """The decoder layers of one decode step: per layer, the attention
+        kernel and one decode chain -- o_proj + residual (with the statistics
+        of the post-attention RMSNorm), gate/up + SwiGLU (that norm applied as
+        its input is loaded), down_proj + residual, and the next layer's QKV +
+        RoPE + KV write (its input norm applied the same way).  The first
+        layer's QKV is a chain of its own.  Returns the residual stream after
+        the last layer (examples/qwen2_5/model.py:1045-1061 per layer)."""
+        c = self.cfg
+        M, D = x.shape
+        H, KVH, HD, eps = c.n_head, c.n_kv_head, c.head_dim, c.rms_eps
+        dev = self.device
+        y = torch.empty((M, D), dtype=torch.bfloat16, device=dev)
+        h = torch.empty((M, c.intermediate), dtype=torch.bfloat16, device=dev)
+        xs = [x, torch.empty((M, D), dtype=torch.bfloat16, device=dev)]  # residual stream, ping-pong
+        st_post = ops.decode_stats(D, dev)
+        st_in = ops.decode_stats(D, dev)
+        sync = self._chain_sync
+
+        def qkv(i, xsrc, xnorm):
+            L = self.layers[i]
+            return ops.chain_rope_kv(xsrc, L["qkv_w"], L["qkv_b"], self.cos, self.sin, q_buf, cache.k[i],
+                                     cache.v[i], H, KVH, HD, pos, xnorm=xnorm)
+
+        phases = [qkv(0, xin, None)]
+        for i, L in enumerate(self.layers):
+            ops.decode_chain(phases, sync)
+            ops.attention(q_buf, cache.k[i], cache.v[i], attn, M, 1, H, KVH, HD, pos, self.scale)
+            last = i + 1 == len(self.layers)
+            xr, xo = xs[i % 2], xs[(i + 1) % 2]
+            phases = [
+                ops.chain_residual(attn, L["o_w"], None, xr, y, st_post, "rms"),
+                ops.chain_swiglu(y, L["gate_up_w"], h, xnorm=(st_post, L["post_ln"], None, eps, "rms")),
+                ops.chain_residual(h, L["down_w"], None, y, xo, None if last else st_in, None if last else "rms"),
+            ]
+            if not last:
+                phases.append(qkv(i + 1, xo, (st_in, self.layers[i + 1]["input_ln"], None, eps, "rms")))
+        ops.decode_chain(phases, sync)
+        return xs[len(self.layers) % 2]
 
     def new_cache(self, batch: int, max_seq: int) -> KVCache:
         if max_seq > self.cos.shape[0]:
@@ -170,7 +224,10 @@ class Qwen2Model:
         decode = S == 1 and M <= ops.SMALL_M
         if decode:
             xin, xnorm = ops.rms_norm(x, self.layers[0]["input_ln"], c.rms_eps), None
-        for i, L in enumerate(self.layers):
+        chain = decode and self._chain_ok()
+        if chain:
+            x = self._decode_chain_layers(x, xin, cache, pos, q_buf, attn)
+        for i, L in enumerate(self.layers if not chain else ()):
             if decode:
                 ops.decode_linear_rope_kv(xin, L["qkv_w"], L["qkv_b"], self.cos, self.sin, q_buf, cache.k[i],
                                           cache.v[i], H, KVH, HD, pos, xnorm=xnorm)
