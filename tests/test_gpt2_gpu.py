@@ -138,22 +138,22 @@ def test_workload_shape_runs_finite():
 
 @pytest.mark.parametrize("name", ["gpt2", "gpt2-medium"])
 def test_decode_chain_equals_single_launch_decode(name):
-    """Decode steps through the decode chain (the default) against the
+    """Decode steps through the decode chain (opt-in) against the
     single-launch decode linears, teacher-forced, batch 8.  At the GPT-2
     widths the single launches split every K exactly as the chain does
     (ceil(K / 512) 64-wide blocks per rank), so the logits are bit-identical."""
     cfg = GPT2Config.variant(name)
     model = GPT2Model(random_weights(cfg, seed=24), cfg)
-    assert model._chain_ok()
+    assert model.use_decode_chain(True)
     B, S = 8, 40
     ids = _ids(B, S + 3, cfg.vocab_size, 12).cuda()
     outs = {}
     for chain in (True, False):
-        model._chain = chain
+        model.use_decode_chain(chain)
         cache = model.new_cache(B, S + 3)
         model.forward(ids[:, :S], cache, last_only=True)
         outs[chain] = [model.forward(ids[:, t:t + 1], cache, last_only=True) for t in range(S, S + 3)]
-    model._chain = True
+    model.use_decode_chain(True)
     for a, b in zip(outs[True], outs[False]):
         assert torch.equal(a, b)
     assert ops.device_status() == 0

@@ -150,8 +150,9 @@ def test_workload_shape_runs_finite():
 
 
 def test_decode_chain_equals_single_launch_decode():
-    """Decode steps through the decode chain (the default) against the
-    single-launch decode linears, teacher-forced, 24 layers, batch 8.  The
+    """Decode steps through the decode chain (opt-in) against the
+    single-launch decode linears (the default), teacher-forced, 24 layers,
+    batch 8.  The
     chain splits the gate/up K eight ways where the single launch splits it
     three ways; the different fp32 roundings compound over 24 bf16 layers, so
     the logits agree to the level of the 24-layer oracle bounds, not bit for
@@ -159,16 +160,16 @@ def test_decode_chain_equals_single_launch_decode():
     cfg = QwenConfig()
     sd = random_weights(cfg, seed=16)
     model = Qwen2Model(sd, cfg, rope_len=1024)
-    assert model._chain_ok()
+    assert model.use_decode_chain(True)
     B, S = 8, 40
     ids = _ids(B, S + 3, cfg.vocab_size, 11).cuda()
     outs = {}
     for chain in (True, False):
-        model._chain = chain
+        model.use_decode_chain(chain)
         cache = model.new_cache(B, S + 3)
         model.forward(ids[:, :S], cache, last_only=True)
         outs[chain] = [model.forward(ids[:, t:t + 1], cache, last_only=True) for t in range(S, S + 3)]
-    model._chain = True
+    model.use_decode_chain(True)
     for a, b in zip(outs[True], outs[False]):  # measured: cosine >= 0.99986, max diff 1.7 % of the range
         _cmp(a, b.cpu(), cos_min=0.9995, rel=0.03)
     assert ops.device_status() == 0

@@ -32,25 +32,35 @@ namespace xb {
 namespace gemm {
 
 constexpr int kChS = 8;                                  // CTAs per cluster (K split)
-constexpr int kChPt = kDecBN / kChS;                     // tokens each CTA finishes
-constexpr int kChStages = 4;                             // weight ring slots
+constexpr int kChStages = 3;                             // weight ring slots
 constexpr int kChXMax = 10;                              // resident X tiles: K <= kChXMax * 64 * kChS
 constexpr int kChMaxPhases = 4;
 constexpr int kChWBytes = kDecBM * 128;                  // weight tile: 128 rows x 64 bf16
 constexpr int kChXBytes = kDecBN * 128;                  // X tile: 64 tokens x 64 bf16
-constexpr int kChRecvFloats = kChS * kChPt * kDecBM;     // one receive buffer
-constexpr int kChSmem = kChStages * kChWBytes + kChXMax * kChXBytes + 2 * kChRecvFloats * 4 + 1024;
-static_assert(kChPt * kChS == kDecBN, "every token has one owner");
+constexpr int kChRecvFloats = kDecBN * kDecBM;           // one receive buffer: [group token slot][row]
+constexpr int kChRedBytes = kDecBN * kDecBM * 4;              // this CTA's partial [token][row]
+constexpr int kChSmem =
+    kChStages * kChWBytes + kChXMax * kChXBytes + 2 * kChRecvFloats * 4 + kChRedBytes + 1024;
+
+// What a phase needs besides its tensor maps; copied into shared memory at
+// the start of the launch (parameter reads at a run-time phase index go
+// through the constant cache, whose first-touch misses cost ~0.5 us each on
+// the finisher's critical path).
+struct ChMeta {
+  DecArgs a;   // finisher arguments (as the one-launch decode linear takes them)
+  int fin;     // Fin
+  int xnorm;   // X carries a pending norm (a.xstats ...)
+  int units;   // 128-row weight blocks
+  int split;   // CTAs of a cluster sharing a unit (8, 4, 2 or 1)
+  int kps;     // K blocks per CTA of the group
+  int nsplit;  // CTAs of the group that hold K blocks: ceil(kblocks / kps)
+};
+static_assert(sizeof(ChMeta) % 4 == 0, "copied as 32-bit words");
 
 struct ChPhase {
   CUtensorMap w;  // W [N, K] K-major, 64 x 128 boxes
   CUtensorMap x;  // X [M, K] K-major, 64 x 64 boxes (rows past M read as zero)
-  DecArgs a;      // finisher arguments (as the one-launch decode linear takes them)
-  int fin;        // Fin
-  int xnorm;      // X carries a pending norm (a.xstats ...)
-  int units;      // 128-row weight blocks
-  int kps;        // K blocks per rank
-  int nsplit;     // ranks that hold K blocks: ceil(kblocks / kps)
+  ChMeta m;
 };
 
 struct ChParams {
@@ -82,6 +92,18 @@ __device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int32
                : "memory");
 }
 
+// Arrivals (weight n) on an mbarrier of any CTA of the cluster.  The relaxed
+// form is for signals that order only earlier reads: a release would also
+// wait for this CTA's earlier global stores to be acknowledged.
+__device__ __forceinline__ void mbar_arrive_cluster_n(uint32_t bar_cluster, uint32_t n) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar_cluster), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed_n(uint32_t bar_cluster, uint32_t n) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(bar_cluster), "r"(n)
+               : "memory");
+}
+
 // Bounded mbarrier wait that also gives up when this CTA (la) or any CTA of
 // the grid (ga) has aborted.  CL: the phase is completed by arrivals from
 // other CTAs of the cluster (acquire at cluster scope).
@@ -108,28 +130,27 @@ __device__ __forceinline__ DecConsts ch_consts(int fin, const DecArgs& a, int ro
     default: return dec_consts<kFinResidual>(a, row0, lane);
   }
 }
-__device__ __forceinline__ void ch_finish(int fin, const DecArgs& a, const float4* rv, int S, int ntok, int tok0,
-                                          int row0, int blk, int warp, int lane, const DecConsts& kc,
+__device__ __forceinline__ void ch_finish(int fin, const DecArgs& a, const float4* rv, int S, int pt, int ntok,
+                                          int tok0, int row0, int blk, int warp, int lane, const DecConsts& kc,
                                           const float4 (&rpre)[kDecPre]) {
   switch (fin) {
-    case kFinStore: dec_finish<kFinStore>(a, rv, S, kChPt, ntok, tok0, row0, blk, warp, lane, kc, rpre); break;
-    case kFinRopeKv: dec_finish<kFinRopeKv>(a, rv, S, kChPt, ntok, tok0, row0, blk, warp, lane, kc, rpre); break;
-    case kFinSwiglu: dec_finish<kFinSwiglu>(a, rv, S, kChPt, ntok, tok0, row0, blk, warp, lane, kc, rpre); break;
-    default: dec_finish<kFinResidual>(a, rv, S, kChPt, ntok, tok0, row0, blk, warp, lane, kc, rpre); break;
+    case kFinStore: dec_finish<kFinStore>(a, rv, S, pt, ntok, tok0, row0, blk, warp, lane, kc, rpre); break;
+    case kFinRopeKv: dec_finish<kFinRopeKv>(a, rv, S, pt, ntok, tok0, row0, blk, warp, lane, kc, rpre); break;
+    case kFinSwiglu: dec_finish<kFinSwiglu>(a, rv, S, pt, ntok, tok0, row0, blk, warp, lane, kc, rpre); break;
+    default: dec_finish<kFinResidual>(a, rv, S, pt, ntok, tok0, row0, blk, warp, lane, kc, rpre); break;
   }
-}
-
-// v[base + i] for a runtime i in 0..3 (selects, no local-memory indexing)
-__device__ __forceinline__ float sel4(const uint32_t (&v)[32], int base, int i) {
-  const float a = __uint_as_float(v[base]), b = __uint_as_float(v[base + 1]);
-  const float c = __uint_as_float(v[base + 2]), d = __uint_as_float(v[base + 3]);
-  return i == 0 ? a : (i == 1 ? b : (i == 2 ? c : d));
 }
 
 // One CTA: warp 0 streams weight tiles, warp 1 issues the MMAs, warps 2..5
 // (the epilogue) load and normalise X, exchange partials and finish.  The
 // epilogue never leaves its loops early: after an abort it runs on with every
 // wait and every piece of work skipped, so its named barriers stay matched.
+//
+// K split per phase: s = split CTAs of a cluster share a unit (their K
+// slices summed by the group's owners), so a cluster works on 8 / s units at
+// once.  Every CTA of the grid runs the same number of unit slots in a phase
+// (slots past the last unit exchange empty partials), which keeps the
+// exchange barriers of all CTAs in step when the groups change between phases.
 __global__ void __launch_bounds__(192, 1) decode_chain_kernel(const __grid_constant__ ChParams P) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t wfull[kChStages];
@@ -143,13 +164,15 @@ __global__ void __launch_bounds__(192, 1) decode_chain_kernel(const __grid_const
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
   __shared__ float s_mean[kDecBN], s_rstd[kDecBN];
+  __shared__ ChMeta s_ph[kChMaxPhases];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t base_u32 = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base_u32 - smem_u32(smem_raw));
   uint8_t* xs = smem + kChStages * kChWBytes;                         // resident X tiles
-  float* recv = reinterpret_cast<float*>(xs + kChXMax * kChXBytes);  // [2][kChS * kChPt][128]
+  float* recv = reinterpret_cast<float*>(xs + kChXMax * kChXBytes);  // [2][64 tokens of the group][128]
+  float* red = recv + 2 * kChRecvFloats;                            // [64 tokens][128 rows]
   const uint32_t x_u32 = base_u32 + kChStages * kChWBytes;
   const int rank = (int)cluster_ctarank();
   const int cl = (int)blockIdx.x / kChS, ncl = (int)gridDim.x / kChS;
@@ -167,11 +190,18 @@ __global__ void __launch_bounds__(192, 1) decode_chain_kernel(const __grid_const
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 128);
-      mbar_init(&rfull[a], kChS * 4);  // every rank's four epilogue warps
-      mbar_init(&rfree[a], kChS);      // every owner, once its finisher is done
+      // arrivals are weighted by 8 / split, so these counts hold for every split:
+      mbar_init(&rfull[a], kChS * 4);  // each source of the group, once per epilogue warp
+      mbar_init(&rfree[a], kChS);      // each owner of the group, once its finisher is done
     }
     abort_flag = 0;
     mbar_fence_init();
+  }
+  {
+    constexpr int kWords = (int)(sizeof(ChMeta) / 4);
+    for (int i = threadIdx.x; i < nph * kWords; i += blockDim.x)
+      reinterpret_cast<uint32_t*>(s_ph)[i] =
+          reinterpret_cast<const uint32_t*>(&P.ph[i / kWords].m)[i % kWords];
   }
   if (warp == 1) {
     tmem_alloc(&tmem_base_sh, 2 * kDecBN);
@@ -188,10 +218,24 @@ __global__ void __launch_bounds__(192, 1) decode_chain_kernel(const __grid_const
     abort_flag = 1;
     atomicExch(sync + 2, 1u);
   };
-  // this rank's K blocks of a phase: [kb0, kb0 + nkb)
-  auto kslice = [&](const ChPhase& ph, int& kb0, int& nkb) {
-    kb0 = rank * ph.kps;
-    nkb = max(0, min(kb0 + ph.kps, ph.a.kblocks) - kb0);
+  // Geometry of a phase for this CTA: its group (split CTAs sharing a unit),
+  // its K blocks [kb0, kb0 + nkb), its first unit and the unit stride, and
+  // the number of unit slots every CTA runs.
+  struct Geo {
+    int s, r, g0, kb0, nkb, u0, ustep, slots;
+  };
+  auto geo = [&](const ChMeta& m) {
+    Geo q;
+    q.s = m.split;
+    q.r = rank % q.s;  // rank within the group
+    q.g0 = rank - q.r;  // the group's first rank
+    q.kb0 = q.r * m.kps;
+    q.nkb = max(0, min(q.kb0 + m.kps, m.a.kblocks) - q.kb0);
+    const int ng = kChS / q.s;
+    q.u0 = cl * ng + rank / q.s;
+    q.ustep = ncl * ng;
+    q.slots = (m.units + q.ustep - 1) / q.ustep;
+    return q;
   };
 
   if (warp == 0) {
@@ -201,33 +245,37 @@ __global__ void __launch_bounds__(192, 1) decode_chain_kernel(const __grid_const
         prefetch_tmap(&P.ph[p].w);
         prefetch_tmap(&P.ph[p].x);
       }
-      // every tile past the ring's first fill goes to L2 now: the chain's
-      // weight traffic runs at full DRAM rate under its latency-bound steps
+      // the ring's first fill, then every later tile of the launch into L2:
+      // the chain's weight traffic runs at full DRAM rate under its
+      // latency-bound steps (requested right after the first ring loads, so
+      // those do not queue behind the prefetches)
       int it = 0;
-      for (int p = 0; p < nph; ++p) {
-        const ChPhase& ph = P.ph[p];
-        int kb0, nkb;
-        kslice(ph, kb0, nkb);
-        for (int u = cl; u < ph.units; u += ncl)
-          for (int i = 0; i < nkb; ++i, ++it)
-            if (it >= kChStages) tma_prefetch_l2_2d(&ph.w, (kb0 + i) * kDecBK, u * kDecBM);
-      }
-      it = 0;
-      bool ok = true;
+      bool ok = true, prefetched = false;
+      auto prefetch_rest = [&]() {
+        int k = 0;
+        for (int p = 0; p < nph; ++p) {
+          const ChMeta& m = s_ph[p];
+          const Geo q = geo(m);
+          for (int u = q.u0; u < m.units; u += q.ustep)
+            for (int i = 0; i < q.nkb; ++i, ++k)
+              if (k >= kChStages) tma_prefetch_l2_2d(&P.ph[p].w, (q.kb0 + i) * kDecBK, u * kDecBM);
+        }
+        prefetched = true;
+      };
       for (int p = 0; p < nph && ok; ++p) {
-        const ChPhase& ph = P.ph[p];
-        int kb0, nkb;
-        kslice(ph, kb0, nkb);
-        for (int u = cl; u < ph.units && ok; u += ncl)
-          for (int i = 0; i < nkb; ++i, ++it) {
+        const ChMeta& m = s_ph[p];
+        const Geo q = geo(m);
+        for (int u = q.u0; u < m.units && ok; u += q.ustep)
+          for (int i = 0; i < q.nkb; ++i, ++it) {
             const int s = it % kChStages;
+            if (it == kChStages && !prefetched) prefetch_rest();
             if (!ch_wait<false>(&wempty[s], ((it / kChStages) & 1) ^ 1, &abort_flag, sync + 2)) {
               fail();
               ok = false;
               break;
             }
             mbar_arrive_expect_tx(&wfull[s], kChWBytes);
-            tma_load_2d(smem + s * kChWBytes, &ph.w, &wfull[s], (kb0 + i) * kDecBK, u * kDecBM);
+            tma_load_2d(smem + s * kChWBytes, &P.ph[p].w, &wfull[s], (q.kb0 + i) * kDecBK, u * kDecBM);
           }
       }
       // the loads still in flight land before the CTA leaves (one time limit)
@@ -243,25 +291,26 @@ __global__ void __launch_bounds__(192, 1) decode_chain_kernel(const __grid_const
       int it = 0, ul = 0, xc = 0;
       bool ok = true, pending = false;
       for (int p = 0; p < nph && ok; ++p) {
-        const ChPhase& ph = P.ph[p];
-        if (cl >= ph.units) continue;
-        int kb0, nkb;
-        kslice(ph, kb0, nkb);
-        if (!ch_wait<false>(&xready, xc & 1, &abort_flag, sync + 2)) {
-          fail();
-          break;
+        const ChMeta& m = s_ph[p];
+        const Geo q = geo(m);
+        if (q.u0 < m.units) {  // X is loaded only where the CTA has a unit
+          if (!ch_wait<false>(&xready, xc & 1, &abort_flag, sync + 2)) {
+            fail();
+            break;
+          }
+          ++xc;
         }
-        ++xc;
         tc_fence_after();
-        for (int u = cl; u < ph.units; u += ncl, ++ul) {
+        for (int j = 0; j < q.slots; ++j, ++ul) {
           const int a = ul & 1;
+          const bool live = q.u0 + j * q.ustep < m.units;
           if (!ch_wait<false>(&tempty[a], ((ul >> 1) & 1) ^ 1, &abort_flag, sync + 2)) {
             fail();
             ok = false;
             break;
           }
           tc_fence_after();
-          for (int i = 0; i < nkb; ++i, ++it) {
+          for (int i = 0; live && i < q.nkb; ++i, ++it) {
             const int s = it % kChStages;
             if (!ch_wait<false>(&wfull[s], (it / kChStages) & 1, &abort_flag, sync + 2)) {
               fail();
@@ -278,7 +327,7 @@ __global__ void __launch_bounds__(192, 1) decode_chain_kernel(const __grid_const
             tc_commit(&wempty[s]);
           }
           if (!ok) break;
-          tc_commit(&tfull[a]);  // no MMAs (empty K slice): completes at once
+          tc_commit(&tfull[a]);  // no MMAs (empty slot or K slice): completes at once
           pending = false;
         }
       }
@@ -295,14 +344,17 @@ __global__ void __launch_bounds__(192, 1) decode_chain_kernel(const __grid_const
   } else {
     // ------------------------------------------------------------ epilogue (128 threads)
     const int e = threadIdx.x - 64;  // 0 .. 127
-    const int q = warp & 3;          // TMEM lane quarter this warp may read
-    const int l4 = lane & 3, g4 = lane >> 2;
-    const int tok0 = rank * kChPt;
+    const int q4 = warp & 3;         // TMEM lane quarter this warp may read
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
     int ul = 0, xf = 0, xissued = 0;
     for (int p = 0; p < nph; ++p) {
-      const ChPhase& ph = P.ph[p];
-      const DecArgs& A = ph.a;
+      const ChMeta& m = s_ph[p];
+      const DecArgs& A = m.a;
+      const Geo q = geo(m);
+      const int pt = kDecBN / q.s;  // tokens each CTA of the group finishes
+      const int tok0 = q.r * pt;
+      const int ntok = max(0, min(A.m, tok0 + pt) - tok0);
+      const unsigned weight = (unsigned)(kChS / q.s);  // exchange arrivals count 8 / split
       // ---- what phase p reads is complete: the previous kernel (phase 0) or
       // every CTA of this grid (the barrier counter reaches p * G)
       if (p == 0) {
@@ -330,15 +382,15 @@ __global__ void __launch_bounds__(192, 1) decode_chain_kernel(const __grid_const
         }
         epi_bar();
       }
-      if (cl < ph.units) {
-        int kb0, nkb;
-        kslice(ph, kb0, nkb);
-        if (e == 0 && nkb > 0 && !abort_flag) {
-          mbar_arrive_expect_tx(&xfull, nkb * kChXBytes);
-          for (int i = 0; i < nkb; ++i) tma_load_2d(xs + i * kChXBytes, &ph.x, &xfull, (kb0 + i) * kDecBK, 0);
+      if (q.u0 < m.units) {
+        // ---- this rank's K slice of X, all tokens, resident for the phase
+        if (e == 0 && q.nkb > 0 && !abort_flag) {
+          mbar_arrive_expect_tx(&xfull, q.nkb * kChXBytes);
+          for (int i = 0; i < q.nkb; ++i)
+            tma_load_2d(xs + i * kChXBytes, &P.ph[p].x, &xfull, (q.kb0 + i) * kDecBK, 0);
           ++xissued;
         }
-        if (ph.xnorm) {
+        if (m.xnorm) {
           // per-token mean / rstd from the producer's block statistics, in block order
           if (e < kDecBN && !abort_flag) {
             const int t = e;
@@ -373,15 +425,16 @@ __global__ void __launch_bounds__(192, 1) decode_chain_kernel(const __grid_const
           }
           epi_bar();
         }
-        if (nkb > 0) {
-          if (!abort_flag && !ch_wait<false>(&xfull, xf & 1, &abort_flag, sync + 2)) fail();
+        if (q.nkb > 0) {
+          if (e == 0 && !abort_flag && !ch_wait<false>(&xfull, xf & 1, &abort_flag, sync + 2)) fail();
           ++xf;
-          if (ph.xnorm && !abort_flag) {
+          epi_bar();
+          if (m.xnorm && !abort_flag) {
             // thread e rewrites the 16-byte chunks (token (e >> 3) + 16 jj, K
             // elements 8 (e & 7) .. + 7) of every tile as bf16(norm(x))
             const int j = e & 7;
-            for (int i = 0; i < nkb; ++i) {
-              const int k0 = (kb0 + i) * kDecBK + j * 8;
+            for (int i = 0; i < q.nkb; ++i) {
+              const int k0 = (q.kb0 + i) * kDecBK + j * 8;
               if (k0 >= A.k) continue;  // past K: zero-filled, stays zero
               const uint4 wraw = __ldg(reinterpret_cast<const uint4*>(A.xnw + k0));
               const uint4 braw = (A.xkind == 1 && A.xnb) ? __ldg(reinterpret_cast<const uint4*>(A.xnb + k0))
@@ -416,69 +469,95 @@ __global__ void __launch_bounds__(192, 1) decode_chain_kernel(const __grid_const
           fence_proxy_async_smem();  // these writes, before the MMAs' (async-proxy) reads
         }
         mbar_arrive(&xready);
-        // ---- the cluster's units of this phase
-        for (int u = cl; u < ph.units; u += ncl, ++ul) {
-          const int a = ul & 1;
-          const int row0 = u * kDecBM;
-          const int ntok = max(0, min(A.m, tok0 + kChPt) - tok0);
-          const DecConsts kc = ch_consts(ph.fin, A, row0, lane);
-          float4 rpre[kDecPre];
+      }
+      // ---- the unit slots of this phase, software-pipelined: slot j's
+      // partial is pushed before slot j - 1 is finished, so the wait for the
+      // slowest group member's push overlaps this CTA's own push.  Slot ul
+      // (counted over the launch) uses accumulator and receive buffer ul & 1.
+      int pj = -1, pa = 0, pul = 0, pu = 0;
+      bool plive = false;
+      DecConsts pkc = {};
+      float4 prpre[kDecPre];
+      auto finish_pending = [&]() {
+        if (e == 0 && !abort_flag && !ch_wait<true>(&rfull[pa], (pul >> 1) & 1, &abort_flag, sync + 2)) fail();
+        epi_bar();
+        if (plive && !abort_flag)
+          ch_finish(m.fin, A, reinterpret_cast<const float4*>(recv + pa * kChRecvFloats), m.nsplit, pt, ntok, tok0,
+                    pu * kDecBM, pu, warp, lane, pkc, prpre);
+        // every epilogue thread has read receive buffer pa (the named barrier
+        // orders those reads); the sources are told so without waiting for the
+        // finisher's global stores
+        epi_bar();
+        if (e < q.s) mbar_arrive_cluster_relaxed_n(mapa_u32(smem_u32(&rfree[pa]), (uint32_t)(q.g0 + e)), weight);
+      };
+      for (int j = 0; j < q.slots; ++j, ++ul) {
+        const int a = ul & 1;
+        const int u = q.u0 + j * q.ustep;
+        const bool live = u < m.units;
+        DecConsts kc = {};
+        float4 rpre[kDecPre];
 #pragma unroll
-          for (int v4 = 0; v4 < kDecPre; ++v4) rpre[v4] = z4;
-          if (ph.fin == kFinResidual) dec_rpre<kFinResidual>(A, ntok, tok0, row0, warp, lane, rpre);
-          // receive buffers a of every owner are free (unit ul - 2 finished) and
-          // this CTA's accumulator a is final
-          if (!abort_flag && !ch_wait<true>(&rfree[a], ((ul >> 1) & 1) ^ 1, &abort_flag, sync + 2)) fail();
-          if (!abort_flag && !ch_wait<false>(&tfull[a], (ul >> 1) & 1, &abort_flag, sync + 2)) fail();
-          tc_fence_after();
-          if (nkb > 0 && !abort_flag) {
-            // rows q*32 + lane of the accumulator, 32 tokens at a time; 4x4
-            // transposes within lane quads give each lane four consecutive rows
-            // of one token, pushed as one 16-byte store into the owner's buffer
-            const uint32_t recv_a = smem_u32(recv + a * kChRecvFloats);
+        for (int v4 = 0; v4 < kDecPre; ++v4) rpre[v4] = z4;
+        if (live) {
+          kc = ch_consts(m.fin, A, u * kDecBM, lane);
+          if (m.fin == kFinResidual) dec_rpre<kFinResidual>(A, ntok, tok0, u * kDecBM, warp, lane, rpre);
+        }
+        // receive buffers a of the group are free (slot ul - 2 finished) and
+        // this CTA's accumulator a is final (one thread polls each barrier;
+        // the named barrier passes the result on)
+        if (e == 0 && !abort_flag) {
+          if (!ch_wait<true>(&rfree[a], ((ul >> 1) & 1) ^ 1, &abort_flag, sync + 2) ||
+              !ch_wait<false>(&tfull[a], (ul >> 1) & 1, &abort_flag, sync + 2))
+            fail();
+        }
+        epi_bar();
+        tc_fence_after();
+        const bool push = live && q.nkb > 0 && !abort_flag;
+        if (push) {
+          // accumulator -> red [token][row] (thread = row), the TMEM
+          // accumulator is then free for the next slot's MMAs
+          const int row = q4 * 32 + lane;
 #pragma unroll
-            for (int h = 0; h < kDecBN / 32; ++h) {
-              uint32_t v[32];
-              tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + a * kDecBN + h * 32, v);
-              tmem_ld_wait();
+          for (int h = 0; h < kDecBN / 32; ++h) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q4 * 32) << 16) + a * kDecBN + h * 32, v);
+            tmem_ld_wait();
 #pragma unroll
-              for (int jb = 0; jb < 8; ++jb) {
-                float y[4] = {0.f, 0.f, 0.f, 0.f};
-                const float own = sel4(v, 4 * jb, l4);
-#pragma unroll
-                for (int jj = 0; jj < 4; ++jj)
-                  if (jj == l4) y[jj] = own;
-#pragma unroll
-                for (int k = 1; k < 4; ++k) {
-                  const float rcv = __shfl_xor_sync(0xffffffffu, sel4(v, 4 * jb, l4 ^ k), k);
-#pragma unroll
-                  for (int jj = 0; jj < 4; ++jj)
-                    if (jj == (l4 ^ k)) y[jj] = rcv;
-                }
-                const int t = h * 32 + 4 * jb + l4;  // token of this lane's four rows
-                const uint32_t off = (uint32_t)(((rank * kChPt + (t % kChPt)) * kDecBM + q * 32 + 4 * g4) * 4);
-                st_dsmem_f4(mapa_u32(recv_a + off, (uint32_t)(t / kChPt)), make_float4(y[0], y[1], y[2], y[3]));
-              }
-            }
-          }
-          tc_fence_before();
-          mbar_arrive(&tempty[a]);
-          __syncwarp();
-          if (lane == 0) {  // this warp's pushes, released to every owner
-            const uint32_t rf = smem_u32(&rfull[a]);
-            for (int o = 0; o < kChS; ++o) mbar_arrive_cluster(mapa_u32(rf, (uint32_t)o));
-          }
-          if (!abort_flag && !ch_wait<true>(&rfull[a], (ul >> 1) & 1, &abort_flag, sync + 2)) fail();
-          if (!abort_flag)
-            ch_finish(ph.fin, A, reinterpret_cast<const float4*>(recv + a * kChRecvFloats), ph.nsplit, ntok, tok0,
-                      row0, u, warp, lane, kc, rpre);
-          epi_bar();  // every epilogue thread is done with receive buffer a
-          if (e == 0) {
-            const uint32_t rf = smem_u32(&rfree[a]);
-            for (int o = 0; o < kChS; ++o) mbar_arrive_cluster(mapa_u32(rf, (uint32_t)o));
+            for (int jj = 0; jj < 32; ++jj) red[(h * 32 + jj) * kDecBM + row] = __uint_as_float(v[jj]);
           }
         }
+        tc_fence_before();
+        mbar_arrive(&tempty[a]);
+        epi_bar();
+        if (push) {
+          // token t's row of the partial -> slot (q.r, t % pt) of its owner's
+          // receive buffer: thread e sends rows (e & 31) * 4 .. + 3 of tokens
+          // e / 32 + 4 k, one 16-byte store each (a warp: one 512-byte row).
+          // Staged through shared memory: stores of register values straight
+          // after the TMEM load ran ~0.5 us each (measured).
+          const uint32_t recv_a = smem_u32(recv + a * kChRecvFloats);
+          const float4* red4 = reinterpret_cast<const float4*>(red);
+#pragma unroll 4
+          for (int t = e >> 5; t < kDecBN; t += 4)
+            st_dsmem_f4(mapa_u32(recv_a + (uint32_t)(((q.r * pt + t % pt) * kDecBM + (e & 31) * 4) * 4),
+                                 (uint32_t)(q.g0 + t / pt)),
+                        red4[t * (kDecBM / 4) + (e & 31)]);
+        }
+        // this warp's pushes, released to every owner of the group (lane o
+        // arrives at owner o)
+        __syncwarp();
+        if (lane < q.s) mbar_arrive_cluster_n(mapa_u32(smem_u32(&rfull[a]), (uint32_t)(q.g0 + lane)), weight);
+        if (pj >= 0) finish_pending();
+        pj = j;
+        pa = a;
+        pul = ul;
+        pu = u;
+        plive = live;
+        pkc = kc;
+#pragma unroll
+        for (int v4 = 0; v4 < kDecPre; ++v4) prpre[v4] = rpre[v4];
       }
+      if (pj >= 0) finish_pending();
       // ---- this CTA's part of phase p is written: one arrival on the grid counter
       if (p + 1 < nph) {
         epi_bar();
@@ -525,7 +604,7 @@ int chain_phase(const xb_decode_phase& d, ChPhase& ph, const char* what, char* e
   const int64_t N = d.n, K = d.k;
   int rc = decode_check(in, d.w, N, K, d.ldw, what, err, errlen);
   if (rc) return rc;
-  DecArgs& a = ph.a;
+  DecArgs& a = ph.m.a;
   memset(&a, 0, sizeof(a));
   switch (d.kind) {
     case XB_DECODE_STORE:
@@ -594,18 +673,14 @@ int chain_phase(const xb_decode_phase& d, ChPhase& ph, const char* what, char* e
   a.xnb = static_cast<const __nv_bfloat16*>(d.x_norm_b);
   a.xeps = d.x_eps;
   a.xkind = d.x_norm_kind;
-  ph.kps = (a.kblocks + kChS - 1) / kChS;
-  if (ph.kps > kChXMax) {
+  if ((a.kblocks + kChS - 1) / kChS > kChXMax) {
     set_err(err, errlen, "%s: K = %lld exceeds the chain's %d resident K blocks per CTA (K <= %d)", what,
             (long long)K, kChXMax, kChXMax * kDecBK * kChS);
     return XB_ERR_UNSUPPORTED;
   }
-  ph.nsplit = (a.kblocks + ph.kps - 1) / ph.kps;
-  a.kps = ph.kps;
-  a.splits = ph.nsplit;
-  ph.fin = d.kind;  // XB_DECODE_* match the Fin values
-  ph.xnorm = d.x_stats != nullptr;
-  ph.units = (int)((N + kDecBM - 1) / kDecBM);
+  ph.m.fin = d.kind;  // XB_DECODE_* match the Fin values
+  ph.m.xnorm = d.x_stats != nullptr;
+  ph.m.units = (int)((N + kDecBM - 1) / kDecBM);
   return XB_OK;
 }
 
@@ -634,11 +709,9 @@ extern "C" int xb_decode_chain_bf16(const xb_decode_phase* phases, int n_phases,
   }
   ChParams P;
   memset(&P, 0, sizeof(P));
-  int max_units = 1;
   for (int i = 0; i < n_phases; ++i) {
     const int rc = chain_phase(phases[i], P.ph[i], what, err, errlen);
     if (rc) return rc;
-    max_units = std::max(max_units, P.ph[i].units);
   }
   for (int i = 0; i < n_phases; ++i) {
     const int rc = chain_maps(phases[i], P.ph[i], err, errlen);
@@ -679,7 +752,20 @@ extern "C" int xb_decode_chain_bf16(const xb_decode_phase* phases, int n_phases,
     set_err(err, errlen, "%s: no %d-CTA cluster of the chain kernel fits on this device", what, kChS);
     return XB_ERR_UNSUPPORTED;
   }
-  const int ncl = std::min(fits, max_units);
+  // every resident cluster takes part; each phase then splits K as little as
+  // keeps all of them busy: halve the split while the units times the halved
+  // split still cover the grid and the slices still fit the resident X tiles
+  const int ncl = fits;
+  for (int i = 0; i < n_phases; ++i) {
+    ChMeta& m = P.ph[i].m;
+    int sp = kChS;
+    while (sp > 1 && (m.a.kblocks + sp / 2 - 1) / (sp / 2) <= kChXMax && m.units * (sp / 2) >= ncl * kChS) sp /= 2;
+    m.split = sp;
+    m.kps = (m.a.kblocks + sp - 1) / sp;
+    m.nsplit = (m.a.kblocks + m.kps - 1) / m.kps;
+    m.a.kps = m.kps;
+    m.a.splits = m.nsplit;
+  }
   e = launch_clusters(kernel, (unsigned)(ncl * kChS), (unsigned)kChS, 192, kChSmem, (cudaStream_t)stream, P);
   if (e != cudaSuccess) {
     set_err(err, errlen, "%s: %s", what, cudaGetErrorString(e));

@@ -1959,12 +1959,24 @@ __device__ __forceinline__ void st_dsmem_f4(uint32_t addr, float4 v) {
 
 constexpr int kDecPre = 4;  // residual rows requested ahead, per epilogue thread
 
-__device__ __forceinline__ float4 ld_bf16x4_cg(const __nv_bfloat16* p) {
-  // L2 load: residual rows may have been written earlier in the same launch
-  const uint2 raw = __ldcg(reinterpret_cast<const uint2*>(p));
+// Loads a finisher requests long before it uses them.  Volatile asm keeps
+// them where they are written (ahead of the barrier waits) instead of letting
+// the compiler sink them next to their use on the critical path.
+__device__ __forceinline__ uint2 ld_early_cg_u2(const void* p) {
+  uint2 v;  // L2 load: residual rows may have been written earlier in the same launch
+  asm volatile("ld.global.cg.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 ld_early_nc_f4(const float* p) {
+  float4 v;  // read-only tables
+  asm volatile("ld.global.nc.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ float4 bf16x4_to_f4(uint2 raw) {
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
   return make_float4(__low2float(h[0]), __high2float(h[0]), __low2float(h[1]), __high2float(h[1]));
 }
+__device__ __forceinline__ float4 ld_bf16x4_cg(const __nv_bfloat16* p) { return bf16x4_to_f4(ld_early_cg_u2(p)); }
 
 // Bias and RoPE rows an epilogue thread uses for every unit of one block.
 struct DecConsts {
@@ -1977,22 +1989,22 @@ __device__ __forceinline__ DecConsts dec_consts(const DecArgs& args, int row0, i
   DecConsts k{z4, z4, z4, z4, z4, z4};
   if constexpr (FIN == kFinStore || FIN == kFinResidual) {
     const int n = row0 + lane * 4;
-    if (args.bias && n < args.n) k.pb0 = ld_bf16x4(args.bias + n);
+    if (args.bias && n < args.n) k.pb0 = ld_bf16x4_cg(args.bias + n);
   } else if constexpr (FIN == kFinRopeKv) {
     const int half = args.D >> 1, p = (lane & 15) * 4, hd = p / half, i = p - hd * half;
     const int f0 = row0 + hd * args.D + i, slot = (row0 + hd * args.D) / args.D;
     if (slot < args.H + 2 * args.KVH) {
       if (args.bias) {
-        k.pb0 = ld_bf16x4(args.bias + f0);
-        k.pb1 = ld_bf16x4(args.bias + f0 + half);
+        k.pb0 = ld_bf16x4_cg(args.bias + f0);
+        k.pb1 = ld_bf16x4_cg(args.bias + f0 + half);
       }
       if (args.cos_t && slot < args.H + args.KVH) {
         const float* cr = args.cos_t + (int64_t)args.pos * args.D;
         const float* sr = args.sin_t + (int64_t)args.pos * args.D;
-        k.pc0 = __ldg(reinterpret_cast<const float4*>(cr + i));
-        k.pc1 = __ldg(reinterpret_cast<const float4*>(cr + i + half));
-        k.ps0 = __ldg(reinterpret_cast<const float4*>(sr + i));
-        k.ps1 = __ldg(reinterpret_cast<const float4*>(sr + i + half));
+        k.pc0 = ld_early_nc_f4(cr + i);
+        k.pc1 = ld_early_nc_f4(cr + i + half);
+        k.ps0 = ld_early_nc_f4(sr + i);
+        k.ps1 = ld_early_nc_f4(sr + i + half);
       }
     }
   }

@@ -144,13 +144,19 @@ class Qwen2Model:
 
     def _chain_ok(self) -> bool:
         """Decode steps run as decode chains (one launch per layer besides its
-        attention) unless XB_DECODE_CHAIN=0 or a linear is too deep for one."""
+        attention) when XB_DECODE_CHAIN=1 (or use_decode_chain(True)) and every
+        linear fits one; otherwise as single-launch decode linears."""
         if self._chain is None:
-            c = self.cfg
-            self._chain = (os.environ.get("XB_DECODE_CHAIN", "1") != "0"
-                           and max(c.n_embd, c.intermediate) <= ops.CHAIN_MAX_K)
-            if self._chain:
-                self._chain_sync = ops.decode_chain_sync(self.device)
+            self.use_decode_chain(os.environ.get("XB_DECODE_CHAIN", "0") == "1")
+        return self._chain
+
+    def use_decode_chain(self, on: bool) -> bool:
+        """Choose the decode-chain path for later decode steps (if the shapes
+        allow it); returns whether it is used."""
+        c = self.cfg
+        self._chain = bool(on) and max(c.n_embd, c.intermediate) <= ops.CHAIN_MAX_K
+        if self._chain and self._chain_sync is None:
+            self._chain_sync = ops.decode_chain_sync(self.device)
         return self._chain
 
     def _decode_chain_layers(self, x, xin, cache: KVCache, pos: int, q_buf, attn):
