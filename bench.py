@@ -347,7 +347,9 @@ def llm_bench(args, world, rank, local, dev, kind, steps, warmup, cpu_leg):
     n0 = X.launch_count()
     model.generate(ids, new)
     launches_per_step = X.launch_count() - n0
-    graphs = None if args.qwen_eager else model.decode_graphs(B, S, new)  # decode steps replay CUDA graphs
+    groups = args.decode_groups if B % args.decode_groups == 0 else 1
+    # decode steps replay CUDA graphs, `groups` groups of sequences on their own streams
+    graphs = None if args.qwen_eager else model.decode_graphs(B, S, new, groups=groups)
     cache = model.new_cache(B, S + new) if graphs is None else None
 
     def step():
@@ -388,6 +390,7 @@ def llm_bench(args, world, rank, local, dev, kind, steps, warmup, cpu_leg):
     tflops = flops / (pre_ms * 1e-3) / 1e12
     dec_gbs = dec_bytes * (new - 1) / (dec_ms * 1e-3) / 1e9
     cpu = llm_cpu_baseline(kind, cfg) if cpu_leg else None
+    groups = 1 if graphs is None else groups
     del graphs, model, cache
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
@@ -399,7 +402,8 @@ def llm_bench(args, world, rank, local, dev, kind, steps, warmup, cpu_leg):
         "config": {"workload": f"{LLM_WORKLOADS[kind]}: batch {B_total} x {S} prefill + {new} greedy decode",
                    "global_batch": B_total, "seq_len": S, "new_tokens": new,
                    "parallelism": f"batch-sharded x{world} (replicated weights, no collective)",
-                   "l2": "weights re-read every step; decode steps replay CUDA graphs"},
+                   "l2": "weights re-read every step; decode steps replay CUDA graphs",
+                   "decode_groups": groups},
         "prefill_tokens_per_s": round(prefill_tps, 1), "decode_tokens_per_s": round(decode_tps, 1),
         "prefill_ms": round(pre_ms, 2), "decode_ms": round(dec_ms, 2),
         "roofline": {"bound": "tensor (prefill) / hbm (decode)",
@@ -1166,6 +1170,8 @@ def main():
     ap.add_argument("--qwen-prompt", type=int, default=512)
     ap.add_argument("--qwen-new", type=int, default=128)
     ap.add_argument("--qwen-eager", action="store_true", help="qwen: launch decode steps directly (no CUDA graphs)")
+    ap.add_argument("--decode-groups", type=int, default=1,
+                    help="LLM decode: sequence groups replaying their graphs concurrently on their own streams")
     ap.add_argument("--only", default=None, help="gemm-sweep: run only ops whose name contains this string")
     ap.add_argument("--no-library", action="store_true", help="gemm sweeps: skip the cuBLAS reference lines")
     ap.add_argument("--elements", type=int, default=N28,

@@ -136,12 +136,14 @@ def test_workload_shape_runs_finite():
     assert ops.device_status() == 0 and ops.token_status() == 0
 
 
-@pytest.mark.parametrize("name", ["gpt2", "gpt2-medium"])
-def test_decode_chain_equals_single_launch_decode(name):
+@pytest.mark.parametrize("name,exact", [("gpt2", True), ("gpt2-medium", False)])
+def test_decode_chain_equals_single_launch_decode(name, exact):
     """Decode steps through the decode chain (opt-in) against the
-    single-launch decode linears, teacher-forced, batch 8.  At the GPT-2
-    widths the single launches split every K exactly as the chain does
-    (ceil(K / 512) 64-wide blocks per rank), so the logits are bit-identical."""
+    single-launch decode linears (the default), teacher-forced, batch 8.  At
+    GPT-2 small the chain splits every K as the single launches do, so the
+    logits are bit-identical; at gpt2-medium it splits c_fc's K four ways
+    (32 row blocks keep the grid busy at that split) where the single launch
+    splits it eight ways, so the logits agree to bf16-rounding level."""
     cfg = GPT2Config.variant(name)
     model = GPT2Model(random_weights(cfg, seed=24), cfg)
     assert model.use_decode_chain(True)
@@ -155,6 +157,20 @@ def test_decode_chain_equals_single_launch_decode(name):
         outs[chain] = [model.forward(ids[:, t:t + 1], cache, last_only=True) for t in range(S, S + 3)]
     model.use_decode_chain(True)
     for a, b in zip(outs[True], outs[False]):
-        assert torch.equal(a, b)
+        if exact:
+            assert torch.equal(a, b)
+        else:
+            _cmp(a, b.cpu(), cos_min=0.9999, rel=0.02)
     assert ops.device_status() == 0
-    assert int(model._chain_sync.abs().sum()) == 0
+    assert int(ops.decode_chain_sync(model.device).abs().sum()) == 0
+
+
+def test_decode_groups_replay_equals_one_group():
+    cfg = GPT2Config.variant("gpt2")
+    cfg.n_layer = 4
+    model = GPT2Model(random_weights(cfg, seed=25), cfg)
+    ids = _ids(8, 32, cfg.vocab_size, 14).cuda()
+    one, _ = model.generate(ids, 6, graphs=model.decode_graphs(8, 32, 6))
+    two, _ = model.generate(ids, 6, graphs=model.decode_graphs(8, 32, 6, groups=2))
+    assert torch.equal(one, two)
+    assert ops.device_status() == 0

@@ -152,11 +152,9 @@ def test_workload_shape_runs_finite():
 def test_decode_chain_equals_single_launch_decode():
     """Decode steps through the decode chain (opt-in) against the
     single-launch decode linears (the default), teacher-forced, 24 layers,
-    batch 8.  The
-    chain splits the gate/up K eight ways where the single launch splits it
-    three ways; the different fp32 roundings compound over 24 bf16 layers, so
-    the logits agree to the level of the 24-layer oracle bounds, not bit for
-    bit."""
+    batch 8.  The two split the gate/up K differently; the different fp32
+    roundings compound over 24 bf16 layers, so the logits agree to the level
+    of the 24-layer oracle bounds, not bit for bit."""
     cfg = QwenConfig()
     sd = random_weights(cfg, seed=16)
     model = Qwen2Model(sd, cfg, rope_len=1024)
@@ -173,4 +171,19 @@ def test_decode_chain_equals_single_launch_decode():
     for a, b in zip(outs[True], outs[False]):  # measured: cosine >= 0.99986, max diff 1.7 % of the range
         _cmp(a, b.cpu(), cos_min=0.9995, rel=0.03)
     assert ops.device_status() == 0
-    assert int(model._chain_sync.abs().sum()) == 0
+    assert int(ops.decode_chain_sync(model.device).abs().sum()) == 0
+
+
+def test_decode_groups_replay_equals_one_group():
+    """Two sequence groups replaying their decode graphs concurrently on two
+    streams produce the tokens of one group (a sequence's arithmetic does not
+    depend on its batch neighbours), on views of one KV cache."""
+    cfg = QwenConfig(n_layer=4)
+    model = Qwen2Model(random_weights(cfg, seed=17), cfg, rope_len=1024)
+    ids = _ids(8, 32, cfg.vocab_size, 13).cuda()
+    one, _ = model.generate(ids, 6, graphs=model.decode_graphs(8, 32, 6))
+    two_graphs = model.decode_graphs(8, 32, 6, groups=2)
+    two, t = model.generate(ids, 6, graphs=two_graphs)
+    again, _ = model.generate(ids, 6, graphs=two_graphs)
+    assert torch.equal(one, two) and torch.equal(two, again)
+    assert t["decode_ms"] > 0 and ops.device_status() == 0

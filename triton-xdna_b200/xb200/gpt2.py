@@ -151,7 +151,6 @@ class GPT2Model:
         self.lnf_b = t("transformer.ln_f.bias")
         self.scale = 1.0 / math.sqrt(c.head_dim)
         self._chain = None  # decided at the first decode step
-        self._chain_sync = None
 
     def new_cache(self, batch: int, max_seq: int) -> KVCache:
         if max_seq > self.cfg.n_positions:
@@ -171,8 +170,6 @@ class GPT2Model:
         """Choose the decode-chain path for later decode steps (if the shapes
         allow it); returns whether it is used."""
         self._chain = bool(on) and self.cfg.mlp <= ops.CHAIN_MAX_K
-        if self._chain and self._chain_sync is None:
-            self._chain_sync = ops.decode_chain_sync(self.device)
         return self._chain
 
     def _decode_chain_layers(self, x, xin, cache, pos: int, q_buf, attn):
@@ -191,7 +188,7 @@ class GPT2Model:
         xs = [x, torch.empty((M, D), dtype=torch.bfloat16, device=dev)]  # residual stream, ping-pong
         st_post = ops.decode_stats(D, dev)
         st_in = ops.decode_stats(D, dev)
-        sync = self._chain_sync
+        sync = ops.decode_chain_sync(dev)  # this workspace slot's counters
 
         def qkv(i, xsrc, xnorm):
             L = self.layers[i]
@@ -314,5 +311,5 @@ class GPT2Model:
         return toks.t(), {"prefill_ms": e0.elapsed_time(e1), "decode_ms": e1.elapsed_time(e2)}
 
     @torch.no_grad()
-    def decode_graphs(self, batch: int, prompt: int, new: int) -> DecodeGraphs:
-        return DecodeGraphs(self, batch, prompt, new)
+    def decode_graphs(self, batch: int, prompt: int, new: int, groups: int = 1) -> DecodeGraphs:
+        return DecodeGraphs(self, batch, prompt, new, groups)

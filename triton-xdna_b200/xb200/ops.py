@@ -389,6 +389,27 @@ def matmul_bf16(a, b, out_dtype=torch.float32, out=None):
 
 SMALL_M = 64  # token counts at or below this take the swap-AB split-K path
 _workspaces: dict = {}
+_slot = [0]  # workspace slot of the operators being issued (see workspace_slot)
+
+
+class workspace_slot:
+    """Operators issued inside ``with workspace_slot(i):`` use scratch slot i:
+    work issued on different streams at the same time (e.g. two decode
+    groups replaying their CUDA graphs concurrently) must use different
+    slots, because each slot's buffers are reused by every operator issued
+    under it."""
+
+    def __init__(self, slot: int):
+        self.slot = int(slot)
+
+    def __enter__(self):
+        self.prev = _slot[0]
+        _slot[0] = self.slot
+        return self
+
+    def __exit__(self, *exc):
+        _slot[0] = self.prev
+        return False
 
 
 def reserve_workspace(device, nbytes: int) -> None:
@@ -406,16 +427,17 @@ def attention_workspace_bytes(batch, seq, n_head, n_kv_head, pos_offset) -> int:
 
 
 def _workspace(device, nbytes: int) -> torch.Tensor:
-    """A per-device fp32 scratch buffer that only grows (kept alive so its
-    address is stable, e.g. across CUDA-graph replays).  One buffer per
-    device: operators that use it must not run concurrently on two streams."""
+    """A per-(device, workspace slot) fp32 scratch buffer that only grows
+    (kept alive so its address is stable, e.g. across CUDA-graph replays).
+    Operators issued under one slot must not run concurrently on two streams."""
     device = torch.device(device)
     if device.index is None:  # "cuda" and "cuda:<current>" name the same buffer
         device = torch.device(device.type, torch.cuda.current_device())
-    ws = _workspaces.get(device)
+    key = (device, _slot[0])
+    ws = _workspaces.get(key)
     if ws is None or ws.numel() * 4 < nbytes:
         ws = torch.empty(max(nbytes // 4, 1 << 20), dtype=torch.float32, device=device)
-        _workspaces[device] = ws
+        _workspaces[key] = ws
     return ws
 
 
@@ -792,9 +814,19 @@ def chain_residual(x, weight, bias, residual, y, stats=None, stats_kind=None, xn
     return ph
 
 
+_chain_syncs: dict = {}
+
+
 def decode_chain_sync(device) -> torch.Tensor:
-    """The chain's grid-barrier counters: 16 zeroed bytes, one buffer per stream."""
-    return torch.zeros(4, dtype=torch.int32, device=device)
+    """The chain's grid-barrier counters for the current workspace slot: 16
+    bytes, zero between launches, one buffer per (device, slot)."""
+    device = torch.device(device)
+    if device.index is None:
+        device = torch.device(device.type, torch.cuda.current_device())
+    key = (device, _slot[0])
+    if key not in _chain_syncs:
+        _chain_syncs[key] = torch.zeros(4, dtype=torch.int32, device=device)
+    return _chain_syncs[key]
 
 
 def decode_chain(phases, sync) -> None:

@@ -22,6 +22,7 @@ and may return last-position logits only (all a greedy step needs).
 
 from __future__ import annotations
 
+import copy
 import math
 import os
 import time
@@ -140,7 +141,6 @@ class Qwen2Model:
         self.sin = sin.to(dev).contiguous()
         self.scale = 1.0 / math.sqrt(c.head_dim)
         self._chain = None  # decided at the first decode step
-        self._chain_sync = None
 
     def _chain_ok(self) -> bool:
         """Decode steps run as decode chains (one launch per layer besides its
@@ -155,8 +155,6 @@ class Qwen2Model:
         allow it); returns whether it is used."""
         c = self.cfg
         self._chain = bool(on) and max(c.n_embd, c.intermediate) <= ops.CHAIN_MAX_K
-        if self._chain and self._chain_sync is None:
-            self._chain_sync = ops.decode_chain_sync(self.device)
         return self._chain
 
     def _decode_chain_layers(self, x, xin, cache: KVCache, pos: int, q_buf, attn):
@@ -176,7 +174,7 @@ class Qwen2Model:
         xs = [x, torch.empty((M, D), dtype=torch.bfloat16, device=dev)]  # residual stream, ping-pong
         st_post = ops.decode_stats(D, dev)
         st_in = ops.decode_stats(D, dev)
-        sync = self._chain_sync
+        sync = ops.decode_chain_sync(dev)  # this workspace slot's counters
 
         def qkv(i, xsrc, xnorm):
             L = self.layers[i]
@@ -303,42 +301,84 @@ class Qwen2Model:
         return toks.t(), {"prefill_ms": e0.elapsed_time(e1), "decode_ms": e1.elapsed_time(e2)}
 
     @torch.no_grad()
-    def decode_graphs(self, batch: int, prompt: int, new: int) -> "DecodeGraphs":
-        return DecodeGraphs(self, batch, prompt, new)
+    def decode_graphs(self, batch: int, prompt: int, new: int, groups: int = 1) -> "DecodeGraphs":
+        return DecodeGraphs(self, batch, prompt, new, groups)
+
+
+def batch_view(cache, start: int, size: int):
+    """The KV cache of sequences [start, start + size) of `cache`: views of its
+    per-layer K / V tensors (the batch is the leading, outermost dimension)."""
+    view = copy.copy(cache)
+    view.k = [t[start:start + size] for t in cache.k]
+    view.v = [t[start:start + size] for t in cache.v]
+    view.batch = size
+    return view
 
 
 class DecodeGraphs:
     """One captured CUDA graph per decode step (positions are baked into the
-    kernel arguments), sharing one memory pool and replayed in capture order.
-    Owns the KV cache and the token buffer the graphs read and write."""
+    kernel arguments), replayed in capture order.  Owns the KV cache and the
+    token buffer the graphs read and write.
 
-    def __init__(self, model: Qwen2Model, batch: int, prompt: int, new: int):
-        self.batch, self.prompt, self.new = batch, prompt, new
+    With `groups` > 1 the batch is split into that many equal groups of
+    sequences; each group replays its own graphs on its own stream, with its
+    own graph memory pool and scratch slot.  A decode step is a chain of
+    latency-bound launches that leaves most SMs idle, so the groups' chains
+    overlap on the GPU.  Every kernel computes a sequence's row with the same
+    arithmetic whatever the batch, so the tokens are the same as with one
+    group."""
+
+    def __init__(self, model, batch: int, prompt: int, new: int, groups: int = 1):
+        if groups < 1 or batch % groups:
+            raise ValueError("groups must divide the batch")
+        self.batch, self.prompt, self.new, self.groups = batch, prompt, new, groups
         self.cache = model.new_cache(batch, prompt + new)
         self.toks = torch.zeros((new, batch), dtype=torch.int64, device=model.device)
+        bg = batch // groups
+        self.views = [self.cache] if groups == 1 else [batch_view(self.cache, g * bg, bg) for g in range(groups)]
+        self.streams = [None] if groups == 1 else [torch.cuda.Stream(device=model.device) for _ in range(groups)]
+        c = model.cfg
         # the scratch buffer the last step's attention (or the LM-head argmax)
         # needs is reserved before any capture (graphs record its address), then one eager step
         # sets up per-kernel attributes and the small-M workspace
-        c = model.cfg
-        vocab = model.cfg.vocab_size
-        ops.reserve_workspace(model.device, max(ops.attention_workspace_bytes(batch, 1, c.n_head, c.n_kv_head,
-                                                                              prompt + new - 1),
-                                                ops.linear_argmax_workspace_bytes(batch, vocab)))
-        self.cache.length = prompt
-        model.forward(self.toks[0].view(batch, 1), self.cache, last_only=True, next_token=torch.empty_like(self.toks[0]))
-        torch.cuda.synchronize()
-        pool = torch.cuda.graph_pool_handle()
+        need = max(ops.attention_workspace_bytes(bg, 1, c.n_head, c.n_kv_head, prompt + new - 1),
+                   ops.linear_argmax_workspace_bytes(bg, c.vocab_size))
         self.graphs = []
-        for step in range(1, new):
-            self.cache.length = prompt + step - 1
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, pool=pool):
-                model.forward(self.toks[step - 1].view(batch, 1), self.cache, last_only=True,
-                              next_token=self.toks[step])
-            self.graphs.append(g)
+        for g, (view, stream) in enumerate(zip(self.views, self.streams)):
+            lo = g * bg
+            with ops.workspace_slot(g):
+                ops.reserve_workspace(model.device, need)
+                view.length = prompt
+                model.forward(self.toks[0, lo:lo + bg].view(bg, 1), view, last_only=True,
+                              next_token=torch.empty_like(self.toks[0, lo:lo + bg]))
+                torch.cuda.synchronize()
+                pool = torch.cuda.graph_pool_handle()  # one pool per group: groups replay concurrently
+                graphs = []
+                for step in range(1, new):
+                    view.length = prompt + step - 1
+                    gr = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(gr, pool=pool, stream=stream):
+                        model.forward(self.toks[step - 1, lo:lo + bg].view(bg, 1), view, last_only=True,
+                                      next_token=self.toks[step, lo:lo + bg])
+                    graphs.append(gr)
+                self.graphs.append(graphs)
+                view.length = 0
         self.cache.length = 0
 
     def replay(self):
-        for g in self.graphs:
-            g.replay()
+        if self.groups == 1:
+            for gr in self.graphs[0]:
+                gr.replay()
+        else:
+            cur = torch.cuda.current_stream()
+            for st in self.streams:
+                st.wait_stream(cur)
+            for step in range(self.new - 1):  # interleaved, so both groups start at once
+                for graphs, st in zip(self.graphs, self.streams):
+                    with torch.cuda.stream(st):
+                        graphs[step].replay()
+            for st in self.streams:
+                cur.wait_stream(st)
         self.cache.length = self.prompt + self.new - 1
+        for view in self.views:
+            view.length = self.cache.length
