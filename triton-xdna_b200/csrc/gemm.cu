@@ -3531,7 +3531,7 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
                                                                   const AtArgs args) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full, q_empty, drain_bar;
-  __shared__ __align__(8) uint64_t s_full[2], s_empty[2], p_full[2], o_full[2], o_empty[2];
+  __shared__ __align__(8) uint64_t s_full[2], s_empty[2], p_full[2], o_full, o_empty;
   __shared__ __align__(8) uint64_t kv_full[kAtStages], kv_empty[kAtStages];
   __shared__ uint32_t tmem_base_sh;
   __shared__ volatile int abort_flag;
@@ -3551,9 +3551,9 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
       mbar_init(&s_full[i], 1);
       mbar_init(&s_empty[i], 128);
       mbar_init(&p_full[i], 128);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 128);
     }
+    mbar_init(&o_full, 1);    // one P V accumulated into O
+    mbar_init(&o_empty, 128);  // a unit's O read by the softmax warps
     for (int i = 0; i < kAtStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
@@ -3574,7 +3574,7 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
-  // TMEM columns: S buffers [0, 64) and [64, 128), P V buffers [128, 192) and [192, 256)
+  // TMEM columns: S buffers [0, 64) and [64, 128), the output accumulator O [128, 192)
   pdl_wait();  // Q and the caches are written by the previous kernel
   pdl_trigger();
 
@@ -3628,23 +3628,27 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
       constexpr uint32_t kIdS = umma_idesc(1, 1, 1, 0, 0, kAtBQ, kAtBK);  // Q (K-major) x K tile (K-major)
       constexpr uint32_t kIdO = umma_idesc(1, 1, 1, 0, 1, kAtBQ, 64);     // P (K-major) x V tile (MN-major)
       bool any = false, ok = true;
-      // P_g V_g into P V buffer g & 1, once P_g is written and that buffer's previous result was read
-      auto pv = [&](int gi) -> bool {
-        const int ob = gi & 1;
-        if (!mbar_wait(&p_full[ob], (gi >> 1) & 1, kWaitLimit, &abort_flag)) return false;
-        if (gi >= 2 && !mbar_wait(&o_empty[ob], ((gi - 2) >> 1) & 1, kWaitLimit, &abort_flag)) return false;
+      // P_g V_g accumulated into O once P_g is written (and O rescaled where
+      // the softmax moved its base); the first tile of a unit starts O afresh,
+      // after the softmax has read the previous unit's O
+      auto pv = [&](int gi, bool first, int ulu) -> bool {
+        const int pb_i = gi & 1;
+        if (!mbar_wait(&p_full[pb_i], (gi >> 1) & 1, kWaitLimit, &abort_flag)) return false;
+        if (first && ulu > 0 && !mbar_wait(&o_empty, (ulu - 1) & 1, kWaitLimit, &abort_flag)) return false;
         tc_fence_after();
         const uint32_t sv = sKV + (gi % kAtStages) * 2 * kAtKVBytes + kAtKVBytes;
-        const uint32_t pb = sP + ob * kAtPBytes;
+        const uint32_t pb = sP + pb_i * kAtPBytes;
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)  // keys in steps of 16
-          mma_f16(tmem_base + 128 + ob * 64, umma_desc_sw128(pb + ks * 32, 16, 1024),
-                  umma_desc_sw128(sv + ks * 16 * 128, kAtKVBytes, 1024), kIdO, ks > 0 ? 1u : 0u);
-        tc_commit(&o_full[ob]);
+          mma_f16(tmem_base + 128, umma_desc_sw128(pb + ks * 32, 16, 1024),
+                  umma_desc_sw128(sv + ks * 16 * 128, kAtKVBytes, 1024), kIdO, (!first || ks > 0) ? 1u : 0u);
+        tc_commit(&o_full);
         tc_commit(&kv_empty[gi % kAtStages]);
         return true;
       };
       int g = 0, lu = 0;
+      int pend_g = -1, pend_lu = 0;  // the tile whose P V is still to issue
+      bool pend_first = false;
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++lu) {
         const AtUnit t = at_unit(args, u);
         if (!mbar_wait(&q_full, lu & 1, kWaitLimit, &abort_flag)) {
@@ -3669,14 +3673,17 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
           any = true;
           tc_commit(&s_full[sb]);
           if (j == t.nkt - 1) tc_commit(&q_empty);  // the unit's last S: Q may be replaced
-          if (g >= 1 && !pv(g - 1)) {
+          if (pend_g >= 0 && !pv(pend_g, pend_first, pend_lu)) {
             fail();
             ok = false;
             break;
           }
+          pend_g = g;
+          pend_first = j == 0;
+          pend_lu = lu;
         }
       }
-      if (ok && g > 0 && !pv(g - 1)) fail();
+      if (ok && pend_g >= 0 && !pv(pend_g, pend_first, pend_lu)) fail();
       if (any) {  // every issued MMA completes before TMEM is released (also after an abort)
         tc_commit(&drain_bar);
         uint64_t deadline = 0;
@@ -3685,35 +3692,20 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
     }
   } else {
     // ------------------------------------------------------------ softmax: one query row per thread
+    // O accumulates in TMEM across the unit's key tiles.  P is taken relative
+    // to a per-row base that moves only when the tile's max exceeds it by more
+    // than 2^8 (P <= 256 otherwise, exact in bf16's range); a warp with such a
+    // row rescales its rows of O in TMEM before the tile's P V is issued.
     const int q4 = warp & 3;  // TMEM lane quarter
     const int r = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
-    float o[64];
-    float alpha_prev = 1.0f;
-    // acc = alpha_g * acc + P_g V_g, once P_g V_g is in TMEM
-    auto fold = [&](int gi, float alpha) -> bool {
-      const int ob = gi & 1;
-      if (!mbar_wait(&o_full[ob], (gi >> 1) & 1, kWaitLimit, &abort_flag)) return false;
-      tc_fence_after();
-      uint32_t ov[64];
-      tmem_ld_32x32b_x32(tmem_base + 128 + ob * 64 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
-      tmem_ld_32x32b_x32(tmem_base + 128 + ob * 64 + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&o_empty[ob]);
-#pragma unroll
-      for (int c = 0; c < 64; ++c) o[c] = fmaf(o[c], alpha, __uint_as_float(ov[c]));
-      return true;
-    };
+    constexpr float kRebase = 8.0f;  // log2 of the largest P kept without rescaling
     bool ok = true;
     int g = 0;
     for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       const AtUnit t = at_unit(args, u);
       const int qpos = args.pos + t.qs + r;  // absolute position of this row
-#pragma unroll
-      for (int c = 0; c < 64; ++c) o[c] = 0.0f;
-      float m = -INFINITY, l = 0.0f;
-      const int g0 = g;
+      float m = -INFINITY, l = 0.0f;  // m: the base of P (log2 units)
       for (int j = 0; j < t.nkt; ++j, ++g) {
         const int sb = g & 1;
         if (!mbar_wait(&s_full[sb], (g >> 1) & 1, kWaitLimit, &abort_flag)) {
@@ -3754,20 +3746,27 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
         const float mxr = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                 fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
         const float mn = fmaxf(m, mxr * args.scale_log2);
-        const float base = mn == -INFINITY ? 0.0f : mn;
-        const float alpha = ex2_approx(m - base);
-        m = mn;
+        // first tile: the base is the row max; later tiles: a warp moves the
+        // bases of its rows only when one of them outgrew its base by 2^8
+        const bool rebase = j == 0 || __any_sync(0xffffffffu, mn > m + kRebase);
+        float alpha = 1.0f;
+        if (rebase) {
+          alpha = (j == 0 || m == -INFINITY) ? 0.0f : ex2_approx(m - mn);
+          m = mn;
+        }
+        const float base = m == -INFINITY ? 0.0f : m;
         float rs8[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) rs8[i] = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {  // P = exp2(S * scale - max): one FMA and one exponential
+        for (int c = 0; c < 64; ++c) {  // P = exp2(S * scale - base): one FMA and one exponential
           s[c] = ex2_approx(fmaf(s[c], args.scale_log2, -base));
           rs8[c & 7] += s[c];
         }
         l = l * alpha + (((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7])));
-        // bf16(P_g) row r -> P buffer g & 1 (read last by P_{g-2} V, folded in the previous
-        // tile); 16-byte chunk c8 at c8 ^ (r & 7) of the 128-byte-swizzled K-major tile
+        // bf16(P_g) row r -> P buffer g & 1 (read last by P_{g-2} V, complete:
+        // waited in the previous tile); 16-byte chunk c8 at c8 ^ (r & 7) of the
+        // 128-byte-swizzled K-major tile
         uint8_t* pt = sPg + sb * kAtPBytes + r * 128;
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
@@ -3779,29 +3778,54 @@ __global__ void __launch_bounds__(192, 2) attn_prefill_tc_kernel(const __grid_co
           *reinterpret_cast<uint4*>(pt + ((c8 ^ (r & 7)) << 4)) = w;
         }
         fence_proxy_async_smem();  // P, before the MMA (async proxy) reads it
-        mbar_arrive(&p_full[sb]);
-        if (g > g0 && !fold(g - 1, alpha_prev)) {  // the previous tile of this unit
-          fail();
-          ok = false;
-          break;
+        if (j > 0) {
+          // P_{g-1} V is in O; rescale O's rows to the new bases before P_g V adds to it
+          if (!mbar_wait(&o_full, (g - 1) & 1, kWaitLimit, &abort_flag)) {
+            fail();
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (rebase) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint32_t ov[32];
+              tmem_ld_32x32b_x32(tmem_base + 128 + h * 32 + lane_off, ov);
+              tmem_ld_wait();
+#pragma unroll
+              for (int c = 0; c < 32; ++c) ov[c] = __float_as_uint(__uint_as_float(ov[c]) * alpha);
+              tmem_st_32x32b_x32(tmem_base + 128 + h * 32 + lane_off, ov);
+            }
+            tmem_st_wait();
+          }
+          tc_fence_before();
         }
-        alpha_prev = alpha;
+        mbar_arrive(&p_full[sb]);
       }
-      if (!ok || !fold(g - 1, alpha_prev)) {  // the unit's last tile
+      if (!ok) break;
+      // the unit's last P V, then O: read, released for the next unit, normalised
+      if (!mbar_wait(&o_full, (g - 1) & 1, kWaitLimit, &abort_flag)) {
         fail();
         ok = false;
         break;
       }
+      tc_fence_after();
+      uint32_t ov[64];
+      tmem_ld_32x32b_x32(tmem_base + 128 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&ov[0]));
+      tmem_ld_32x32b_x32(tmem_base + 128 + 32 + lane_off, *reinterpret_cast<uint32_t(*)[32]>(&ov[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&o_empty);
       if (r < t.rows) {
         const float inv = l > 0.0f ? 1.0f / l : 0.0f;
         __nv_bfloat16* op = args.out + ((int64_t)t.b * args.S + t.qs + r) * ((int64_t)args.H * 64) + t.h * 64;
 #pragma unroll
         for (int c8 = 0; c8 < 8; ++c8) {
           uint4 w;
-          w.x = pack_bf16x2(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
-          w.y = pack_bf16x2(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
-          w.z = pack_bf16x2(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
-          w.w = pack_bf16x2(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
+          w.x = pack_bf16x2(__uint_as_float(ov[c8 * 8 + 0]) * inv, __uint_as_float(ov[c8 * 8 + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(ov[c8 * 8 + 2]) * inv, __uint_as_float(ov[c8 * 8 + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(ov[c8 * 8 + 4]) * inv, __uint_as_float(ov[c8 * 8 + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(ov[c8 * 8 + 6]) * inv, __uint_as_float(ov[c8 * 8 + 7]) * inv);
           *reinterpret_cast<uint4*>(op + c8 * 8) = w;
         }
       }
