@@ -491,27 +491,48 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
           tmem_ld_32x32b_x32(tbase + cc * 32 + 32, v1);
           tmem_ld_wait();
           const int c0 = tn * C::BN + cc * 32;  // first column of the head slot
-          if (row >= args.m || c0 >= args.n) continue;
+          const int row0 = row - lane;
+          if (row0 >= args.m || c0 >= args.n) continue;  // warp-uniform
           const int slot = c0 >> 6;
           const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(args.bias);
           float x0[32], x1[32];
+          if (bp && (reinterpret_cast<uintptr_t>(bp + c0) & 15) == 0) {
+            // the head slot's 64 bias values as eight 16-byte loads (the same
+            // address in every lane)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float b0 = bp ? __bfloat162float(bp[c0 + j]) : 0.0f;
-            const float b1 = bp ? __bfloat162float(bp[c0 + 32 + j]) : 0.0f;
-            x0[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[j]) + b0));
-            x1[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[j]) + b1));
+            for (int j = 0; j < 32; j += 8) {
+              const uint4 r0 = __ldg(reinterpret_cast<const uint4*>(bp + c0 + j));
+              const uint4 r1 = __ldg(reinterpret_cast<const uint4*>(bp + c0 + 32 + j));
+              const __nv_bfloat16* b0 = reinterpret_cast<const __nv_bfloat16*>(&r0);
+              const __nv_bfloat16* b1 = reinterpret_cast<const __nv_bfloat16*>(&r1);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                x0[j + e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[j + e]) + __bfloat162float(b0[e])));
+                x1[j + e] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[j + e]) + __bfloat162float(b1[e])));
+              }
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float b0 = bp ? __bfloat162float(bp[c0 + j]) : 0.0f;
+              const float b1 = bp ? __bfloat162float(bp[c0 + 32 + j]) : 0.0f;
+              x0[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v0[j]) + b0));
+              x1[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v1[j]) + b1));
+            }
           }
-          const int bq = row / args.S, sq = row - bq * args.S, pos = args.pos + sq;
-          __nv_bfloat16* dst;
-          if (slot < args.H)
-            dst = static_cast<__nv_bfloat16*>(args.q_out) + (((int64_t)bq * args.H + slot) * args.S + sq) * 64;
-          else if (slot < args.H + args.KVH)
-            dst = static_cast<__nv_bfloat16*>(args.k_cache) +
-                  (((int64_t)bq * args.KVH + (slot - args.H)) * args.smax + pos) * 64;
-          else
-            dst = static_cast<__nv_bfloat16*>(args.v_cache) +
-                  (((int64_t)bq * args.KVH + (slot - args.H - args.KVH)) * args.smax + pos) * 64;
+          // destination row of token `rw` (its head slot: the query output or
+          // the K / V cache at the token's position)
+          auto dst_of = [&](int rw) -> __nv_bfloat16* {
+            const int bq = rw / args.S, sq = rw - bq * args.S;
+            if (slot < args.H)
+              return static_cast<__nv_bfloat16*>(args.q_out) + (((int64_t)bq * args.H + slot) * args.S + sq) * 64;
+            if (slot < args.H + args.KVH)
+              return static_cast<__nv_bfloat16*>(args.k_cache) +
+                     (((int64_t)bq * args.KVH + (slot - args.H)) * args.smax + args.pos + sq) * 64;
+            return static_cast<__nv_bfloat16*>(args.v_cache) +
+                   (((int64_t)bq * args.KVH + (slot - args.H - args.KVH)) * args.smax + args.pos + sq) * 64;
+          };
+          const int pos = args.pos + (row - (row / args.S) * args.S);
           if (args.cos_t && slot < args.H + args.KVH) {
             // each lane reads its own token's table rows (16-byte loads: a
             // warp's 32 tokens touch 32 rows per instruction)
@@ -533,6 +554,10 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
               }
             }
           }
+          // the warp's 32 rows x 128 bytes through its swizzled staging tile,
+          // then each store instruction writes four whole 128-byte rows (a
+          // token's head slot), consecutive tokens at consecutive addresses
+          uint8_t* stg = smem + C::STAGES * C::STAGE_BYTES + (EPI == 4 ? q * 2 : ew) * (32 * 128);
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
             __nv_bfloat162 h0[4], h1[4];
@@ -541,9 +566,18 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
               h0[e] = __floats2bfloat162_rn(x0[j + 2 * e], x0[j + 2 * e + 1]);
               h1[e] = __floats2bfloat162_rn(x1[j + 2 * e], x1[j + 2 * e + 1]);
             }
-            *reinterpret_cast<int4*>(dst + j) = *reinterpret_cast<int4*>(h0);
-            *reinterpret_cast<int4*>(dst + 32 + j) = *reinterpret_cast<int4*>(h1);
+            const int p0 = j / 8, p1 = 4 + j / 8;  // 16-byte pieces of the row
+            *reinterpret_cast<int4*>(stg + lane * 128 + ((p0 ^ (lane & 7)) * 16)) = *reinterpret_cast<int4*>(h0);
+            *reinterpret_cast<int4*>(stg + lane * 128 + ((p1 ^ (lane & 7)) * 16)) = *reinterpret_cast<int4*>(h1);
           }
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int r = k * 4 + lane / 8, pc = lane % 8;
+            const int4 val = *reinterpret_cast<const int4*>(stg + r * 128 + ((pc ^ (r & 7)) * 16));
+            if (row0 + r < args.m) *reinterpret_cast<int4*>(dst_of(row0 + r) + pc * 8) = val;
+          }
+          __syncwarp();  // staging free for the next head slot
           continue;
         }
         if constexpr (OUT == kOutSwiglu) {
@@ -1466,7 +1500,7 @@ int launch(const Operands& op, void* c, const void* bias, int64_t M, int64_t N, 
       !PEERS && OUT != kOutSwiglu && OUT != kOutArgmax && OUT != kOutQkv && (TRANS || OUT != kOutBf16);
   constexpr bool kLines = !TRANS && (PEERS || OUT == kOutBf16);  // whole-line staged stores
   static_assert(OUT != kOutQkv || !TRANS, "the fused QKV epilogue takes row-major tiles");
-  constexpr int kSmem = Cf::SMEM + ((kStaged || kLines || OUT == kOutArgmax) ? kEpiStageBytes : 0);
+  constexpr int kSmem = Cf::SMEM + ((kStaged || kLines || OUT == kOutArgmax || OUT == kOutQkv) ? kEpiStageBytes : 0);
   static_assert(4 * 32 * 33 * 4 + 4 * 64 * 8 <= kEpiStageBytes, "argmax staging fits");
   static_assert(kSmem <= 227 * 1024, "shared memory budget");
   args.c_tma = 0;
