@@ -532,31 +532,12 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
             return static_cast<__nv_bfloat16*>(args.v_cache) +
                    (((int64_t)bq * args.KVH + (slot - args.H - args.KVH)) * args.smax + args.pos + sq) * 64;
           };
-          const int pos = args.pos + (row - (row / args.S) * args.S);
-          if (args.cos_t && slot < args.H + args.KVH) {
-            // each lane reads its own token's table rows (16-byte loads: a
-            // warp's 32 tokens touch 32 rows per instruction)
-            const float4* cr = reinterpret_cast<const float4*>(args.cos_t + (int64_t)pos * 64);
-            const float4* sr = reinterpret_cast<const float4*>(args.sin_t + (int64_t)pos * 64);
-#pragma unroll
-            for (int j4 = 0; j4 < 8; ++j4) {
-              const float4 ca = __ldg(cr + j4), sa = __ldg(sr + j4);
-              const float4 cb = args.rope_dup ? ca : __ldg(cr + 8 + j4), sb = args.rope_dup ? sa : __ldg(sr + 8 + j4);
-              const float c0v[4] = {ca.x, ca.y, ca.z, ca.w}, c1v[4] = {cb.x, cb.y, cb.z, cb.w};
-              const float s0v[4] = {sa.x, sa.y, sa.z, sa.w}, s1v[4] = {sb.x, sb.y, sb.z, sb.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int j = 4 * j4 + e;
-                const float y0 = __fadd_rn(__fmul_rn(x0[j], c0v[e]), __fmul_rn(-x1[j], s0v[e]));
-                const float y1 = __fadd_rn(__fmul_rn(x1[j], c1v[e]), __fmul_rn(x0[j], s1v[e]));
-                x0[j] = y0;
-                x1[j] = y1;
-              }
-            }
-          }
-          // the warp's 32 rows x 128 bytes through its swizzled staging tile,
-          // then each store instruction writes four whole 128-byte rows (a
-          // token's head slot), consecutive tokens at consecutive addresses
+          // the warp's 32 rows x 128 bytes (bf16(x W^T + b), exact in bf16)
+          // through its swizzled staging tile; RoPE is applied on the way out,
+          // where four lanes share a token: lane (r, pc) rotates the pairs
+          // (8 pc + e, 32 + 8 pc + e) of row r and stores both 16-byte pieces,
+          // so the table rows are read in 32-byte runs and every store
+          // instruction writes eight tokens' half rows
           uint8_t* stg = smem + C::STAGES * C::STAGE_BYTES + (EPI == 4 ? q * 2 : ew) * (32 * 128);
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
@@ -571,11 +552,39 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
             *reinterpret_cast<int4*>(stg + lane * 128 + ((p1 ^ (lane & 7)) * 16)) = *reinterpret_cast<int4*>(h1);
           }
           __syncwarp();
+          const bool rope = args.cos_t && slot < args.H + args.KVH;
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const int r = k * 4 + lane / 8, pc = lane % 8;
-            const int4 val = *reinterpret_cast<const int4*>(stg + r * 128 + ((pc ^ (r & 7)) * 16));
-            if (row0 + r < args.m) *reinterpret_cast<int4*>(dst_of(row0 + r) + pc * 8) = val;
+          for (int k = 0; k < 4; ++k) {
+            const int r = k * 8 + lane / 4, pc = lane % 4;
+            const int rw = row0 + r;
+            int4 a0 = *reinterpret_cast<const int4*>(stg + r * 128 + ((pc ^ (r & 7)) * 16));
+            int4 a1 = *reinterpret_cast<const int4*>(stg + r * 128 + (((pc + 4) ^ (r & 7)) * 16));
+            if (rw >= args.m) continue;
+            if (rope) {
+              const int pos = args.pos + (rw - (rw / args.S) * args.S);
+              const float4* cr = reinterpret_cast<const float4*>(args.cos_t + (int64_t)pos * 64 + pc * 8);
+              const float4* sr = reinterpret_cast<const float4*>(args.sin_t + (int64_t)pos * 64 + pc * 8);
+              const float4 ca0 = __ldg(cr), ca1 = __ldg(cr + 1), sa0 = __ldg(sr), sa1 = __ldg(sr + 1);
+              const float4 cb0 = args.rope_dup ? ca0 : __ldg(cr + 8), cb1 = args.rope_dup ? ca1 : __ldg(cr + 9);
+              const float4 sb0 = args.rope_dup ? sa0 : __ldg(sr + 8), sb1 = args.rope_dup ? sa1 : __ldg(sr + 9);
+              const float c0v[8] = {ca0.x, ca0.y, ca0.z, ca0.w, ca1.x, ca1.y, ca1.z, ca1.w};
+              const float c1v[8] = {cb0.x, cb0.y, cb0.z, cb0.w, cb1.x, cb1.y, cb1.z, cb1.w};
+              const float s0v[8] = {sa0.x, sa0.y, sa0.z, sa0.w, sa1.x, sa1.y, sa1.z, sa1.w};
+              const float s1v[8] = {sb0.x, sb0.y, sb0.z, sb0.w, sb1.x, sb1.y, sb1.z, sb1.w};
+              __nv_bfloat16* h0 = reinterpret_cast<__nv_bfloat16*>(&a0);
+              __nv_bfloat16* h1 = reinterpret_cast<__nv_bfloat16*>(&a1);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float u0 = __bfloat162float(h0[e]), u1 = __bfloat162float(h1[e]);
+                const float y0 = __fadd_rn(__fmul_rn(u0, c0v[e]), __fmul_rn(-u1, s0v[e]));
+                const float y1 = __fadd_rn(__fmul_rn(u1, c1v[e]), __fmul_rn(u0, s1v[e]));
+                h0[e] = __float2bfloat16_rn(y0);
+                h1[e] = __float2bfloat16_rn(y1);
+              }
+            }
+            __nv_bfloat16* d = dst_of(rw);
+            *reinterpret_cast<int4*>(d + pc * 8) = a0;
+            *reinterpret_cast<int4*>(d + 32 + pc * 8) = a1;
           }
           __syncwarp();  // staging free for the next head slot
           continue;
