@@ -775,6 +775,23 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
             const int row0 = row - lane;
             if (col0 >= args.n || row0 >= args.m) continue;  // warp-uniform
             if (col0 + 32 <= args.n) {
+              // residual pieces this lane adds on the way out (row k * 8 + lane / 4,
+              // 16-byte piece lane % 4): requested now, eight rows' 64-byte
+              // segments per load instruction, used after the staging
+              int4 rres[4];
+              if constexpr (OUT == kOutBf16 && !PEERS) {
+                if (args.residual) {
+#pragma unroll
+                  for (int k = 0; k < 4; ++k) {
+                    const int r = k * 8 + lane / 4;
+                    rres[k] = row0 + r < args.m
+                                  ? __ldg(reinterpret_cast<const int4*>(static_cast<const __nv_bfloat16*>(args.residual) +
+                                                                        (int64_t)(row0 + r) * args.ldr + col0 +
+                                                                        (lane % 4) * 8))
+                                  : make_int4(0, 0, 0, 0);
+                  }
+                }
+              }
               if constexpr (OUT == kOutBf16 && !PEERS) {
                 if (args.bias) {
                   const __nv_bfloat16* bp = static_cast<const __nv_bfloat16*>(args.bias);
@@ -788,19 +805,7 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
                     v[j] = __float_as_uint(gelu_tanh_bf16path(
                         __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[j])))));
                 }
-                if (args.residual && row < args.m) {  // residual + bf16(x W^T + b)
-                  const __nv_bfloat16* rp =
-                      static_cast<const __nv_bfloat16*>(args.residual) + (int64_t)row * args.ldr + col0;
-#pragma unroll
-                  for (int j = 0; j < 32; j += 8) {
-                    const int4 raw = __ldg(reinterpret_cast<const int4*>(rp + j));
-                    const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&raw);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                      v[j + e] = __float_as_uint(__bfloat162float(re[e]) +
-                                                 __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[j + e]))));
-                  }
-                }
+                // (a residual is added on the way out, below: residual + bf16(x W^T + b))
               }
               uint8_t* stg = smem + C::STAGES * C::STAGE_BYTES + (EPI == 4 ? q * 2 : ew) * (32 * 128);
               if constexpr (OUT == kOutBf16) {
@@ -832,7 +837,17 @@ __global__ void __launch_bounds__(64 + 32 * EPI, 1) gemm_kernel(const __grid_con
                 for (int k = 0; k < 32 / kRowsPer; ++k) {
                   const int r = k * kRowsPer + lane / kPieces, p = lane % kPieces;
                   const int phys = OUT == kOutBf16 ? (p ^ ((r >> 1) & 3)) : (p ^ (r & 7));
-                  const int4 val = *reinterpret_cast<const int4*>(stg + r * (kPieces * 16) + phys * 16);
+                  int4 val = *reinterpret_cast<const int4*>(stg + r * (kPieces * 16) + phys * 16);
+                  if constexpr (OUT == kOutBf16 && !PEERS) {
+                    // residual + bf16(x W^T + b), the residual piece of the same (row, piece)
+                    if (args.residual && row0 + r < args.m) {
+                      const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rres[k]);
+                      __nv_bfloat16* vb = reinterpret_cast<__nv_bfloat16*>(&val);
+#pragma unroll
+                      for (int e = 0; e < 8; ++e)
+                        vb[e] = __float2bfloat16_rn(__bfloat162float(re[e]) + __bfloat162float(vb[e]));
+                    }
+                  }
                   if (row0 + r < args.m) {
                     int4* dst = reinterpret_cast<int4*>(cb + ((int64_t)r * args.ldc) * kEsz + p * 16);
                     if constexpr ((XB_L2_HINTS & 1) != 0 && !PEERS) __stcs(dst, val);
