@@ -1,12 +1,14 @@
 """Decode chain host side without a GPU: the ctypes mirror of xb_decode_phase
-has the C layout (checked against gcc on the header), and the library
-rejects bad chains before any CUDA call."""
+has the C layout (checked against gcc on the header), the library rejects
+bad chains before any CUDA call, and the per-slot scratch buffers and chain
+counters stay apart."""
 
 import ctypes
 import os
 import subprocess
 
 import pytest
+import torch
 
 from xb200 import _lib, ops
 from xb200._lib import XbError
@@ -81,3 +83,24 @@ def test_bad_kind_and_shapes_are_rejected():
     with pytest.raises(XbError) as e:
         _call([sw])
     assert e.value.code == _lib.XB_ERR_INVALID
+
+
+def test_workspace_slots_keep_separate_buffers():
+    """Each (device, slot) has its own scratch buffer and chain counters;
+    nested slots restore the outer one, and growth stays within its slot."""
+    dev = torch.device("cpu", 0)  # an explicit index: no CUDA call needed
+    base = ops._workspace(dev, 1024)
+    with ops.workspace_slot(7):
+        a = ops._workspace(dev, 1024)
+        sync_a = ops.decode_chain_sync(dev)
+        with ops.workspace_slot(8):
+            b = ops._workspace(dev, 1024)
+            assert b.data_ptr() != a.data_ptr()
+            assert ops.decode_chain_sync(dev).data_ptr() != sync_a.data_ptr()
+        assert ops._workspace(dev, 1024).data_ptr() == a.data_ptr()  # slot 7 again
+        assert ops.decode_chain_sync(dev) is sync_a
+        big = ops._workspace(dev, 8 << 20)  # grows slot 7 only
+        assert big.numel() * 4 >= 8 << 20 and big.data_ptr() != a.data_ptr()
+    assert a.data_ptr() != base.data_ptr()
+    assert ops._workspace(dev, 1024).data_ptr() == base.data_ptr()  # slot 0 untouched
+    assert sync_a.dtype == torch.int32 and sync_a.numel() * 4 == 16 and int(sync_a.abs().sum()) == 0
